@@ -1,0 +1,351 @@
+#!/usr/bin/env python
+"""Benchmark of the Foveal Pattention MLP forward (token-routed) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 8b]
+
+One step = one token-routed forward (router + selection + block CSR + gated contraction + additive
+stream) over one batch of the configuration's synthetic input (Llama-3-8B MLP shape by default:
+x [8, 2048, 4096] bf16, 224 blocks, base 4, top-p 0.8, K in [8, 56]).  With N > 1 (torchrun, one
+process per GPU) every rank processes its own batch with replicated weights: tokens are independent,
+so there is no collective and the scaling is weak.
+
+Prints one JSON line (rank 0): ``value`` = tokens/s over all ranks with inputs resident in HBM,
+timed with CUDA events around exactly K steps (max over ranks); ``e2e`` = the same through the public
+``FovealPattentionMLP.forward`` with the input copied from pinned host memory and the output copied
+back every step; ``roofline`` = the dominant kernel's algorithmic FLOP rate against the measured bf16
+peak; ``cpu_baseline`` = the CPU oracle on a token sample (rank 0, N = 1).
+
+``--impl reference`` times the CPU restatement of the reference path (oracle/, all host threads) on a
+bounded token sample per step, on rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+import torch  # noqa: E402
+
+fsi = importlib.import_module("foveal-sparse-indexer_b200")
+configs = fsi.configs
+
+METRIC = "Pattention-MLP fwd tokens/s & % bf16 tensor peak (8B shape), 1/2/4/8 B200 vs host CPU"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+KERNELS_PER_STEP = 8  # router_scores, convert_keys, select, csr_count, csr_scan, csr_fill, gateup, down
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", default="8b")
+    ap.add_argument("--e2e-steps", type=int, default=0)
+    ap.add_argument("--cpu-sample", type=int, default=256)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+def load_traffic():
+    path = os.path.join(REPO, "profiles", "traffic.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f)
+    return {}
+
+
+def config_block(wl, world):
+    return {"workload": f"{wl.name}: token-routed Pattention MLP fwd", "model": "Llama-3-8B MLP shape"
+            if wl.name == "8b" else wl.name, "tokens_per_rank": wl.tokens, "batch": wl.batch,
+            "seq_len": wl.seq_len, "d_model": wl.hidden_dim, "param_tokens": wl.intermediate_dim,
+            "blocks": wl.num_blocks, "base_blocks": wl.base_blocks, "top_p": wl.top_p,
+            "k_min": wl.min_remote_blocks, "k_max": wl.max_remote_blocks, "routing": "token",
+            "global_batch_tokens": wl.tokens * world, "parallelism": f"token-split x{world} (no collective)",
+            "l2": "inputs larger than L2: x 134 MB + weights 352 MB + activations 470 MB per step vs 126 MB L2"}
+
+
+# ------------------------------------------------------------------ clocks
+def gpu_smi_id(dev, local: int) -> str:
+    """nvidia-smi -i selector for this CUDA device (its UUID; the local index if unavailable)."""
+    try:
+        u = str(torch.cuda.get_device_properties(dev).uuid)
+        return u if u.startswith("GPU-") else f"GPU-{u}"
+    except Exception:
+        return str(local)
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [c.strip() for c in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        load = [s for s in sm if s > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(load), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ CPU baseline (oracle)
+def cpu_oracle_rate(wl, w_cpu, x_cpu, sample: int, reps: int = 3):
+    import oracle  # CPU baseline leg only
+    torch.set_num_threads(os.cpu_count() or 1)
+    xs = x_cpu[:sample].float().contiguous()
+    kw = dict(base_blocks=wl.base_blocks, top_p=wl.top_p, min_remote_blocks=wl.min_remote_blocks,
+              max_remote_blocks=wl.max_remote_blocks, temperature=wl.temperature)
+    oracle.token_forward(xs[:16], w_cpu, **kw)  # warm-up
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        oracle.token_forward(xs, w_cpu, **kw)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {"value": sample / med, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{sample} tokens of the {wl.name} workload, oracle token_forward (fp32 torch CPU), "
+                      f"median of {reps} after 1 warm-up; {med:.2f} s per call"}
+
+
+# ------------------------------------------------------------------ reference arm
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    if rank != 0:
+        return
+    import oracle  # reference arm: the CPU restatement of the reference path
+    wl = configs.CONFIGS[args.config]
+    torch.set_num_threads(os.cpu_count() or 1)
+    w = configs.make_weights(wl)
+    x2d = configs.make_x(wl).reshape(-1, wl.hidden_dim)
+    kw = dict(base_blocks=wl.base_blocks, top_p=wl.top_p, min_remote_blocks=wl.min_remote_blocks,
+              max_remote_blocks=wl.max_remote_blocks, temperature=wl.temperature)
+    # size the per-step sample so that warm-up + steps stay within ~3 minutes
+    sample = 64
+    t0 = time.perf_counter()
+    oracle.token_forward(x2d[:sample].contiguous(), w, **kw)
+    per_tok = (time.perf_counter() - t0) / sample
+    budget = 150.0 / max(1, args.steps + args.warmup)
+    sample = int(max(16, min(1024, budget / max(per_tok, 1e-6))))
+    xs = x2d[:sample].contiguous()
+    for _ in range(args.warmup):
+        oracle.token_forward(xs, w, **kw)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.token_forward(xs, w, **kw)
+    dt = time.perf_counter() - t0
+    value = sample * args.steps / dt
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) x, N(0,0.02) weights)",
+        "impl": "reference", "config": config_block(wl, 1),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": f"{sample} tokens per step of the {wl.name} workload (oracle token_forward, "
+                                   f"fp32 torch CPU restatement of the reference path)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ our arm
+def run_ours(args):
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    wl = configs.CONFIGS[args.config]
+    w = configs.make_weights(wl)
+    m = fsi.FovealPattentionMLP(hidden_dim=wl.hidden_dim, intermediate_dim=wl.intermediate_dim,
+                                base_blocks=wl.base_blocks, remote_blocks=wl.max_remote_blocks,
+                                temperature=wl.temperature, dtype=torch.bfloat16, routing="token", top_p=wl.top_p,
+                                min_remote_blocks=wl.min_remote_blocks, max_remote_blocks=wl.max_remote_blocks)
+    m.load_state_dict({k: t.to(torch.bfloat16) for k, t in w.state_dict().items()}, strict=False)
+    m = m.to(dev).eval()
+    x_cpu = configs.make_x(wl, seed=rank).reshape(-1, wl.hidden_dim)
+    x = x_cpu.to(dev, torch.bfloat16)
+    M, D = x.shape
+    kg, ku, v, vt, wq, k16, wout = m._weights()
+    kw = dict(base_blocks=wl.base_blocks, top_p=wl.top_p, min_remote=wl.min_remote_blocks,
+              max_remote=wl.max_remote_blocks, temperature=wl.temperature, additive=True)
+
+    def step(y_out):
+        fsi.kernels.token_forward(x, kg, ku, v, vt, wq, k16, wout, y=y_out, **kw)
+
+    y = torch.empty(M, D, dtype=torch.bfloat16, device=dev)
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            step(y)
+        # mean active blocks per token of this workload (for the algorithmic FLOP count)
+        _, _, cnt, _ = fsi.kernels.token_forward(x, kg, ku, v, vt, wq, k16, wout, want_routes=True, **kw)
+        a_mean = wl.base_blocks + float(cnt.float().mean())
+        torch.cuda.synchronize()
+
+        K = args.steps
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(K)]
+        for row in ev:
+            for e in row:
+                e.record()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clocks = ClockSampler(gpu_smi_id(dev, local))
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        clocks.start()
+        time.sleep(0.3)  # let the sampler attach before the timed region
+        start.record()
+        for k in range(K):
+            fsi._lib.set_stage_events(ev[k])
+            step(y)
+        end.record()
+        torch.cuda.synchronize()
+        fsi._lib.set_stage_events(None)
+        clk = clocks.stop()
+        t_ms = start.elapsed_time(end)
+        if world > 1:
+            t = torch.tensor([t_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            t_ms = float(t.item())
+        stage = [statistics.mean(ev[k][i].elapsed_time(ev[k][i + 1]) for k in range(K)) for i in range(4)]
+
+        err = fsi._lib.device_error(fsi._lib.workspace(dev, 0))
+
+        # e2e through the public API: pinned host input -> forward -> pinned host output, every step
+        E = args.e2e_steps or max(10, K // 10)
+        x_host = x_cpu.to(torch.bfloat16).pin_memory()
+        y_host = torch.empty(M, D, dtype=torch.bfloat16).pin_memory()
+        x_dev = torch.empty(M, D, dtype=torch.bfloat16, device=dev)
+
+        def e2e_step():
+            x_dev.copy_(x_host, non_blocking=True)
+            out = m(x_dev)
+            y_host.copy_(out, non_blocking=True)
+
+        for _ in range(3):
+            e2e_step()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s2.record()
+        for _ in range(E):
+            e2e_step()
+        e2.record()
+        torch.cuda.synchronize()
+        e2_ms = s2.elapsed_time(e2)
+        if world > 1:
+            t = torch.tensor([e2_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2_ms = float(t.item())
+
+    value = world * M * K / (t_ms / 1e3)
+    ms_step = t_ms / K
+    peaks, src = load_peaks()
+    peak_sus = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
+    gu_flops = 4.0 * D * 64 * a_mean * M
+    dn_flops = 2.0 * D * 64 * a_mean * M
+    names = ["route", "csr", "gateup", "down"]
+    dom = 2 if stage[2] >= stage[3] else 3
+    dom_flops = gu_flops if dom == 2 else dn_flops
+    achieved = dom_flops / (stage[dom] / 1e3) / 1e12
+    traffic = load_traffic().get(f"{wl.name}_{names[dom]}")
+    total_flops = gu_flops + dn_flops
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) x, N(0,0.02) weights)",
+        "config": config_block(wl, world),
+        "tensor_peak_frac": total_flops / (ms_step / 1e3) / 1e12 / peak_sus,
+        "active_blocks_per_token": a_mean,
+        "stages_ms": {n: s for n, s in zip(names, stage)},
+        "roofline": {"bound": "tensor", "kernel": names[dom], "achieved": achieved, "peak": peak_sus,
+                     "unit": "TFLOP/s", "frac": achieved / peak_sus, "traffic": traffic,
+                     "peak_source": f"{src} bf16 sustained (MEASURED_PEAKS.json)" if src == "measured"
+                     else "fallback 1.4 PFLOP/s sustained",
+                     "algorithmic_flops_per_launch": dom_flops},
+        "e2e": {"value": world * M * E / (e2_ms / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": M * D * 2, "d2h_bytes_per_step": M * D * 2,
+                "path": "FovealPattentionMLP.forward, pinned host x -> device -> pinned host y"},
+        "gpu_launches": KERNELS_PER_STEP * K,
+        "clocks": clk,
+        "device_error": err,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_oracle_rate(wl, w, x_cpu, args.cpu_sample)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,153 @@
+"""Workload configurations and seeded synthetic inputs for the Foveal Pattention MLP forward.
+
+The five configurations are the ones the reference's hot path is measured on (Llama-3-8B / 70B MLP
+shapes, a decode step, a CPU-runnable case and a sparsity sweep).  No public dataset is involved:
+every tensor is drawn from a seeded normal distribution.
+
+Draw order (fixed, so that a CPU oracle on another machine regenerates identical tensors):
+    weights: generator seeded with ``seed``      -> k_gate, k_up, v, q_proj_16d, block_keys_16d, out_proj_16d
+    inputs : generator seeded with ``seed + 1``  -> x of shape [B, L, D]
+All tensors are drawn in fp32 (x ~ N(0, 1), weights ~ N(0, 0.02)) and, for bf16 configurations,
+rounded to bf16 after drawing.  Weights and x use separate generators so that a token subsample of x
+does not change the weights.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field, replace
+from typing import Dict, List, Optional
+
+import torch
+
+BLOCK_SIZE = 64
+INDEX_DIM = 16
+WEIGHT_STD = 0.02
+
+
+@dataclass(frozen=True)
+class Workload:
+    """One Pattention-MLP forward configuration.
+
+    Field names follow the reference module (``FovealPattentionMLP`` / ``select_blocks``):
+    ``hidden_dim`` = d_model, ``intermediate_dim`` = N_p parameter tokens, ``base_blocks`` = the
+    always-active leading blocks, ``top_p`` / ``min_remote_blocks`` / ``max_remote_blocks`` = the
+    router's mass target and [K_min, K_max] guardrails.
+    """
+
+    name: str
+    dtype: str  # "fp32" | "bf16"
+    batch: int
+    seq_len: int
+    hidden_dim: int
+    intermediate_dim: int
+    base_blocks: int
+    top_p: float
+    min_remote_blocks: int
+    max_remote_blocks: int
+    temperature: float = 1.0
+    # pooled (reference default) mode active remote-block count; reuses K_max
+    note: str = ""
+
+    @property
+    def tokens(self) -> int:
+        return self.batch * self.seq_len
+
+    @property
+    def num_blocks(self) -> int:
+        return self.intermediate_dim // BLOCK_SIZE
+
+    @property
+    def torch_dtype(self) -> torch.dtype:
+        return torch.float32 if self.dtype == "fp32" else torch.bfloat16
+
+    def active_blocks_per_token(self) -> int:
+        """A = base + K_max: at the BASELINE weight scale every token selects exactly K_max remote
+        blocks (the block softmax is near-uniform, so top-p never binds)."""
+        return self.base_blocks + min(self.max_remote_blocks, self.num_blocks - self.base_blocks)
+
+    def flops_per_token(self, active: Optional[int] = None) -> float:
+        """Algorithmic FLOPs of the gated contraction per token: 6 * D * 64 * A."""
+        a = self.active_blocks_per_token() if active is None else active
+        return 6.0 * self.hidden_dim * BLOCK_SIZE * a
+
+    def with_(self, **kw) -> "Workload":
+        return replace(self, **kw)
+
+
+CONFIGS: Dict[str, Workload] = {
+    "pr1": Workload("pr1", "fp32", 4, 128, 512, 2048, 1, 0.9, 2, 8,
+                    note="CPU-runnable reference case"),
+    "8b": Workload("8b", "bf16", 8, 2048, 4096, 14336, 4, 0.8, 8, 56,
+                   note="Llama-3-8B MLP shape, 1 GPU"),
+    "decode": Workload("decode", "bf16", 64, 1, 4096, 14336, 4, 0.9, 8, 16,
+                       note="decode step; K_max swept over 8/16/32"),
+    "70b": Workload("70b", "bf16", 4, 4096, 8192, 28672, 8, 0.8, 16, 112,
+                    note="Llama-3-70B MLP shape, blocks sharded over GPUs"),
+    "sweep": Workload("sweep", "bf16", 4, 4096, 4096, 14336, 4, 0.9, 8, 56,
+                      note="sparsity sweep; top_p x K_max grid"),
+}
+
+DECODE_KMAX = (8, 16, 32)
+SWEEP_TOP_P = (1.0, 0.9, 0.7, 0.5, 0.3)
+SWEEP_KMAX = (224, 56, 28, 14)
+
+
+def sweep_points() -> List[Workload]:
+    base = CONFIGS["sweep"]
+    pts = []
+    for p in SWEEP_TOP_P:
+        for k in SWEEP_KMAX:
+            pts.append(base.with_(name=f"sweep_p{p}_k{k}", top_p=p, max_remote_blocks=k,
+                                  min_remote_blocks=min(8, k)))
+    return pts
+
+
+def decode_points() -> List[Workload]:
+    base = CONFIGS["decode"]
+    return [base.with_(name=f"decode_k{k}", max_remote_blocks=k, min_remote_blocks=min(8, k))
+            for k in DECODE_KMAX]
+
+
+@dataclass
+class Weights:
+    """Parameter tensors with the reference module's names and shapes (fp32 storage, values already
+    rounded to the configuration's dtype)."""
+
+    k_gate: torch.Tensor        # [N_p, D]
+    k_up: torch.Tensor          # [N_p, D]
+    v: torch.Tensor             # [N_p, D]  (= W_down^T)
+    q_proj_16d: torch.Tensor    # [16, D]
+    block_keys_16d: torch.Tensor  # [NB, 16]
+    out_proj_16d: torch.Tensor  # [D, 16]
+
+    def to(self, device=None, dtype=None) -> "Weights":
+        f = lambda t: t.to(device=device, dtype=dtype)
+        return Weights(f(self.k_gate), f(self.k_up), f(self.v), f(self.q_proj_16d),
+                       f(self.block_keys_16d), f(self.out_proj_16d))
+
+    def state_dict(self) -> Dict[str, torch.Tensor]:
+        return {
+            "k_gate": self.k_gate, "k_up": self.k_up, "v": self.v,
+            "q_proj_16d.weight": self.q_proj_16d, "block_keys_16d": self.block_keys_16d,
+            "out_proj_16d.weight": self.out_proj_16d,
+        }
+
+
+def _round(t: torch.Tensor, dtype: str) -> torch.Tensor:
+    return t if dtype == "fp32" else t.to(torch.bfloat16).to(torch.float32)
+
+
+def make_weights(w: Workload, seed: int = 0) -> Weights:
+    g = torch.Generator().manual_seed(seed)
+    D, Np, NB = w.hidden_dim, w.intermediate_dim, w.num_blocks
+
+    def draw(*shape):
+        return _round(torch.randn(*shape, generator=g) * WEIGHT_STD, w.dtype)
+
+    return Weights(draw(Np, D), draw(Np, D), draw(Np, D), draw(INDEX_DIM, D),
+                   draw(NB, INDEX_DIM), draw(D, INDEX_DIM))
+
+
+def make_x(w: Workload, seed: int = 0) -> torch.Tensor:
+    g = torch.Generator().manual_seed(seed + 1)
+    return _round(torch.randn(w.batch, w.seq_len, w.hidden_dim, generator=g), w.dtype)

@@ -1,0 +1,386 @@
+// extern "C" entry points of libfovealpatt.so: argument validation, workspace layout and the launch
+// sequence of each forward.  Declarations and contracts: include/foveal_pattention.h.
+#include "fp_internal.cuh"
+
+#include <algorithm>
+#include <mutex>
+
+namespace fp {
+namespace {
+
+constexpr size_t kAlign = 1024;
+
+size_t align_up(size_t v, size_t a = kAlign) { return (v + a - 1) / a * a; }
+
+struct Carve {
+  size_t off = 0;
+  size_t take(size_t bytes) {
+    const size_t o = off;
+    off = align_up(off + bytes);
+    return o;
+  }
+};
+
+// Token-chunk length of the block CSR: one chunk of x (bf16) is ~32 MB, so that the gate/up tiles of
+// one chunk gather their token rows from L2.
+int csr_chunk(int D) { return std::max(1024, (1 << 24) / std::max(D, 1)); }
+
+int local_blocks(int NB, int stride, int offset) {
+  return offset >= NB ? 0 : (NB - offset + stride - 1) / stride;
+}
+
+bool tensor_path(int dtype, int D) { return dtype == FP_DTYPE_BF16 && D % 64 == 0 && D >= 64; }
+
+struct TokenLayout {
+  size_t err, meta, k16f, scores, ridx, rcnt, ctx, key_cnt, key_off, key_fill, pair_tok, tiles, h, total;
+  int nbl, chunk, nkey, max_tiles;
+};
+
+TokenLayout token_layout(int dtype, int64_t M, int D, int NB, int base, int kmax, int stride, int offset) {
+  TokenLayout L{};
+  Carve c;
+  L.err = c.take(256);
+  L.meta = c.take(64);
+  L.k16f = c.take((size_t)NB * 16 * 4);
+  L.scores = c.take((size_t)M * NB * 4);
+  L.ridx = c.take((size_t)M * std::max(kmax, 1) * 4);
+  L.rcnt = c.take((size_t)M * 4);
+  L.ctx = c.take((size_t)M * 16 * 4);
+  L.nbl = local_blocks(NB, stride, offset);
+  L.chunk = csr_chunk(D);
+  const int64_t nchunks = (M + L.chunk - 1) / L.chunk;
+  L.nkey = (int)(nchunks * std::max(L.nbl, 1));
+  const int64_t pairs = M * (int64_t)(base + kmax);
+  L.max_tiles = (int)(pairs / kTileN + L.nkey + 1);
+  if (tensor_path(dtype, D)) {
+    L.key_cnt = c.take((size_t)L.nkey * 4);
+    L.key_off = c.take(((size_t)L.nkey + 1) * 4);
+    L.key_fill = c.take((size_t)L.nkey * 4);
+    L.pair_tok = c.take((size_t)pairs * 4);
+    L.tiles = c.take((size_t)L.max_tiles * 8);
+    L.h = c.take((size_t)M * L.nbl * kBlock * 2);
+  }
+  L.total = c.off;
+  return L;
+}
+
+struct PooledLayout {
+  size_t err, part, mean, h, total;
+};
+
+PooledLayout pooled_layout(int dtype, int64_t M, int D, int NB, int n_active) {
+  PooledLayout L{};
+  Carve c;
+  L.err = c.take(256);
+  const int64_t nchunk = (M + 255) / 256;
+  const int width = std::max(D, NB);
+  L.part = c.take((size_t)nchunk * width * 4);
+  L.mean = c.take((size_t)width * 4);
+  if (tensor_path(dtype, D)) L.h = c.take((size_t)M * std::max(n_active, 1) * kBlock * 2);
+  L.total = c.off;
+  return L;
+}
+
+template <typename T>
+T* at(void* ws, size_t off) { return reinterpret_cast<T*>(reinterpret_cast<char*>(ws) + off); }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int device_info(int& num_sms) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return FP_ERR_CUDA;
+  static int cache_sms[64] = {0};
+  static int cache_major[64] = {0};
+  if (dev < 64 && cache_sms[dev] > 0) {
+    num_sms = cache_sms[dev];
+    return cache_major[dev] == 10 ? FP_OK : FP_ERR_DEVICE;
+  }
+  int major = 0, sms = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return FP_ERR_CUDA;
+  if (dev < 64) {
+    cache_sms[dev] = sms;
+    cache_major[dev] = major;
+  }
+  num_sms = sms;
+  return major == 10 ? FP_OK : FP_ERR_DEVICE;
+}
+
+int check_common(int dtype, int64_t M, int D, int NB) {
+  if (dtype != FP_DTYPE_F32 && dtype != FP_DTYPE_BF16) return FP_ERR_UNSUPPORTED;
+  if (M < 0 || D <= 0 || NB <= 0) return FP_ERR_INVALID_ARG;
+  if (D % 8 != 0 || NB > 1024) return FP_ERR_UNSUPPORTED;
+  if (M > (int64_t)INT32_MAX / 8) return FP_ERR_UNSUPPORTED;
+  return FP_OK;
+}
+
+template <typename T>
+__global__ void transpose_kernel(const T* __restrict__ in, int rows, int cols, T* __restrict__ out) {
+  __shared__ T tile[32][33];
+  const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int r = r0 + i, c = c0 + threadIdx.x;
+    if (r < rows && c < cols) tile[i][threadIdx.x] = in[(int64_t)r * cols + c];
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int c = c0 + i, r = r0 + threadIdx.x;
+    if (r < rows && c < cols) out[(int64_t)c * rows + r] = tile[threadIdx.x][i];
+  }
+}
+
+thread_local cudaEvent_t g_stage_events[8];
+thread_local int g_n_stage = 0;
+
+inline void stage_mark(int i, cudaStream_t st) {
+  if (i < g_n_stage && g_stage_events[i]) cudaEventRecord(g_stage_events[i], st);
+}
+
+#define FP_TRY(expr)              \
+  do {                            \
+    const int _s = (expr);        \
+    if (_s != FP_OK) return _s;   \
+  } while (0)
+
+}  // namespace
+}  // namespace fp
+
+using namespace fp;
+
+extern "C" {
+
+int fp_abi_version(void) { return FP_ABI_VERSION; }
+
+const char* fp_status_string(int status) {
+  switch (status) {
+    case FP_OK: return "ok";
+    case FP_ERR_INVALID_ARG: return "invalid argument (null pointer, shape, parameter or alignment)";
+    case FP_ERR_UNSUPPORTED: return "unsupported dtype or shape";
+    case FP_ERR_WORKSPACE: return "workspace too small";
+    case FP_ERR_CUDA: return "CUDA runtime error or launch failure";
+    case FP_ERR_DEVICE: return "current device is not an sm_100 GPU";
+    case FP_ERR_TIMEOUT: return "a kernel's bounded wait ran out";
+    default: return "unknown status";
+  }
+}
+
+int fp_router_scores(const void* x, const void* q_proj, const void* block_keys, int dtype, int64_t M, int D,
+                     int NB, float* scores, float* q16, void* stream) {
+  FP_TRY(check_common(dtype, M, D, NB));
+  if (!x || !q_proj || !block_keys || !scores) return FP_ERR_INVALID_ARG;
+  if (!aligned16(x) || !aligned16(q_proj)) return FP_ERR_INVALID_ARG;
+  int sms;
+  FP_TRY(device_info(sms));
+  return launch_router_scores(x, q_proj, block_keys, dtype, M, D, NB, 1.0f, scores, q16,
+                              (cudaStream_t)stream);
+}
+
+int fp_select_blocks(const float* scores, int64_t M, int NB, int base_blocks, float top_p, int min_remote,
+                     int max_remote, int capacity, float temperature, int32_t* remote_indices,
+                     int32_t* remote_counts, const float* block_keys_f32, float* ctx16, float* stats,
+                     void* stream) {
+  if (M < 0 || NB <= 0 || NB > 1024 || base_blocks < 0 || capacity < 0 || min_remote < 0 || max_remote < 0)
+    return FP_ERR_INVALID_ARG;
+  if (!scores || !(temperature > 0.f)) return FP_ERR_INVALID_ARG;
+  if ((block_keys_f32 == nullptr) != (ctx16 == nullptr)) return FP_ERR_INVALID_ARG;
+  if (remote_indices == nullptr && ctx16 == nullptr) return FP_ERR_INVALID_ARG;
+  if (remote_indices && (!remote_counts || capacity <= 0)) return FP_ERR_INVALID_ARG;
+  int sms;
+  FP_TRY(device_info(sms));
+  return launch_select(scores, M, NB, base_blocks, top_p, min_remote, max_remote, capacity, temperature,
+                       remote_indices, remote_counts, block_keys_f32, ctx16, stats, (cudaStream_t)stream);
+}
+
+size_t fp_pooled_workspace_size(int dtype, int64_t M, int D, int NB, int n_active) {
+  return pooled_layout(dtype, M, D, NB, n_active).total;
+}
+
+size_t fp_token_workspace_size(int dtype, int64_t M, int D, int NB, int base_blocks, int max_remote,
+                               int block_stride) {
+  return token_layout(dtype, M, D, NB, base_blocks, max_remote, std::max(block_stride, 1), 0).total;
+}
+
+int fp_pooled_route(const void* x, const void* q_proj, const void* block_keys, int dtype, int64_t M, int D,
+                    int NB, int base_blocks, int remote_blocks, int mode, const float* token_scores,
+                    int32_t* active, float* mean_scores, void* workspace, size_t workspace_bytes,
+                    void* stream) {
+  FP_TRY(check_common(dtype, M, D, NB));
+  if (!q_proj || !block_keys || !active || !workspace || M <= 0) return FP_ERR_INVALID_ARG;
+  if (base_blocks < 0 || remote_blocks < 0 || base_blocks + remote_blocks > NB) return FP_ERR_INVALID_ARG;
+  if (NB > 4096) return FP_ERR_UNSUPPORTED;
+  if (mode == 0 && !x) return FP_ERR_INVALID_ARG;
+  if (mode == 1 && !token_scores) return FP_ERR_INVALID_ARG;
+  if (mode != 0 && mode != 1) return FP_ERR_INVALID_ARG;
+  const PooledLayout L = pooled_layout(dtype, M, D, NB, 0);
+  if (workspace_bytes < L.total) return FP_ERR_WORKSPACE;
+  int sms;
+  FP_TRY(device_info(sms));
+  cudaStream_t st = (cudaStream_t)stream;
+  float* part = at<float>(workspace, L.part);
+  float* mean = at<float>(workspace, L.mean);
+  if (mode == 0) FP_TRY(launch_colmean(x, dtype, M, D, part, mean, st));
+  else FP_TRY(launch_colmean(token_scores, FP_DTYPE_F32, M, NB, part, mean, st));
+  return launch_pooled_topk(mean, q_proj, block_keys, dtype, D, NB, base_blocks, remote_blocks, mode, active,
+                            mean_scores, st);
+}
+
+int fp_pack_v(const void* v, int dtype, int Np, int D, void* v_t, void* stream) {
+  if (!v || !v_t || Np <= 0 || D <= 0) return FP_ERR_INVALID_ARG;
+  if (dtype != FP_DTYPE_BF16 && dtype != FP_DTYPE_F32) return FP_ERR_UNSUPPORTED;
+  int sms;
+  FP_TRY(device_info(sms));
+  dim3 grid((D + 31) / 32, (Np + 31) / 32), block(32, 8);
+  if (dtype == FP_DTYPE_BF16)
+    transpose_kernel<__nv_bfloat16><<<grid, block, 0, (cudaStream_t)stream>>>(
+        (const __nv_bfloat16*)v, Np, D, (__nv_bfloat16*)v_t);
+  else
+    transpose_kernel<float><<<grid, block, 0, (cudaStream_t)stream>>>((const float*)v, Np, D, (float*)v_t);
+  return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+}
+
+int fp_pattention_token_fwd(const void* x, int64_t M, int D, int NB, int dtype, const void* k_gate,
+                            const void* k_up, const void* v, const void* v_t, const void* q_proj,
+                            const void* block_keys, const void* out_proj, int base_blocks, float top_p,
+                            int min_remote, int max_remote, float temperature, int additive,
+                            int block_stride, int block_offset, void* y, int y_f32,
+                            int32_t* remote_indices, int32_t* remote_counts, float* scores,
+                            void* workspace, size_t workspace_bytes, void* stream) {
+  FP_TRY(check_common(dtype, M, D, NB));
+  if (!x || !k_gate || !k_up || !v || !q_proj || !block_keys || !y || !workspace) return FP_ERR_INVALID_ARG;
+  if (additive && !out_proj) return FP_ERR_INVALID_ARG;
+  if (base_blocks < 0 || base_blocks > NB || min_remote < 0 || max_remote < 0) return FP_ERR_INVALID_ARG;
+  if (block_stride < 1 || block_offset < 0 || block_offset >= block_stride) return FP_ERR_INVALID_ARG;
+  if (!(temperature > 0.f)) return FP_ERR_INVALID_ARG;
+  const bool tc = tensor_path(dtype, D);
+  if (tc && (!v_t || !aligned16(v_t) || !aligned16(x) || !aligned16(k_gate) || !aligned16(k_up)))
+    return FP_ERR_INVALID_ARG;
+  if (!tc && D > 32 * 256) return FP_ERR_UNSUPPORTED;
+  const int cap = std::max(max_remote, 1);
+  const TokenLayout L = token_layout(dtype, M, D, NB, base_blocks, max_remote, block_stride, block_offset);
+  if (workspace_bytes < L.total) return FP_ERR_WORKSPACE;
+  int sms;
+  FP_TRY(device_info(sms));
+  cudaStream_t st = (cudaStream_t)stream;
+  int* err = at<int>(workspace, L.err);
+  if (cudaMemsetAsync(err, 0, 256, st) != cudaSuccess) return FP_ERR_CUDA;
+  if (M == 0) return FP_OK;
+
+  float* S = scores ? scores : at<float>(workspace, L.scores);
+  int32_t* ridx = remote_indices ? remote_indices : at<int32_t>(workspace, L.ridx);
+  int32_t* rcnt = remote_counts ? remote_counts : at<int32_t>(workspace, L.rcnt);
+  float* k16f = at<float>(workspace, L.k16f);
+  float* ctx = additive ? at<float>(workspace, L.ctx) : nullptr;
+
+  stage_mark(0, st);
+  FP_TRY(launch_router_scores(x, q_proj, block_keys, dtype, M, D, NB, 1.0f, S, nullptr, st));
+  FP_TRY(launch_convert_keys(block_keys, dtype, NB * 16, k16f, st));
+  FP_TRY(launch_select(S, M, NB, base_blocks, top_p, min_remote, max_remote, cap, temperature, ridx, rcnt,
+                       additive ? k16f : nullptr, ctx, nullptr, st));
+  stage_mark(1, st);
+
+  if (!tc || L.nbl == 0) {
+    // CUDA-core path; a shard that owns no block contributes only the additive stream (or zeros).
+    SimtArgs a{};
+    a.x = x; a.k_gate = k_gate; a.k_up = k_up; a.v = v; a.dtype = dtype; a.M = M; a.D = D; a.NB = NB;
+    a.base = base_blocks; a.ridx = ridx; a.rcnt = rcnt; a.cap = cap;
+    a.active = L.nbl == 0 ? ridx : nullptr; a.n_active = 0;
+    a.stride = block_stride; a.offset = block_offset; a.ctx16 = ctx; a.out_proj = out_proj; a.y = y;
+    a.y_f32 = y_f32;
+    return launch_simt(a, st);
+  }
+  int32_t* key_cnt = at<int32_t>(workspace, L.key_cnt);
+  int32_t* key_off = at<int32_t>(workspace, L.key_off);
+  int32_t* key_fill = at<int32_t>(workspace, L.key_fill);
+  int32_t* pair_tok = at<int32_t>(workspace, L.pair_tok);
+  int2* tiles = at<int2>(workspace, L.tiles);
+  int32_t* meta = at<int32_t>(workspace, L.meta);
+  void* h = at<void>(workspace, L.h);
+  const int nbl = L.nbl;
+  FP_TRY(launch_build_csr(ridx, rcnt, M, base_blocks, cap, block_stride, block_offset, nbl, L.chunk, L.nkey,
+                          kTileN, key_cnt, key_off, key_fill, pair_tok, tiles, L.max_tiles, meta, err, st));
+  // H is "dense masked": every (token, block) pair the token did not select must read as zero.
+  if (cudaMemsetAsync(h, 0, (size_t)M * nbl * kBlock * 2, st) != cudaSuccess) return FP_ERR_CUDA;
+  stage_mark(2, st);
+  GateUpArgs g{};
+  g.x = x; g.k_gate = k_gate; g.k_up = k_up; g.M = M; g.D = D; g.Np = NB * kBlock;
+  g.tiles = tiles; g.meta = meta; g.key_off = key_off; g.pair_tok = pair_tok;
+  g.nbl = nbl; g.stride = block_stride; g.offset = block_offset; g.active = nullptr; g.n_keys = 0;
+  g.h = h; g.ldh = (int64_t)nbl * kBlock; g.err = err; g.num_sms = sms;
+  FP_TRY(launch_gateup(g, st));
+  stage_mark(3, st);
+  DownArgs d{};
+  d.h = h; d.v_t = v_t; d.M = M; d.D = D; d.Np = NB * kBlock; d.K = nbl * kBlock; d.bmap = nullptr;
+  d.stride = block_stride; d.offset = block_offset; d.ctx16 = ctx; d.out_proj = out_proj;
+  d.out_proj_f32 = dtype == FP_DTYPE_F32; d.y = y; d.y_f32 = y_f32; d.err = err; d.num_sms = sms;
+  FP_TRY(launch_down(d, st));
+  stage_mark(4, st);
+  return FP_OK;
+}
+
+int fp_pattention_pooled_fwd(const void* x, int64_t M, int D, int NB, int dtype, const void* k_gate,
+                             const void* k_up, const void* v, const void* v_t, const int32_t* active,
+                             int n_active, const float* ctx16, const void* out_proj, void* y, int y_f32,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+  FP_TRY(check_common(dtype, M, D, NB));
+  if (!x || !k_gate || !k_up || !v || !active || !y || !workspace || n_active < 0 || n_active > NB)
+    return FP_ERR_INVALID_ARG;
+  if (ctx16 && !out_proj) return FP_ERR_INVALID_ARG;
+  const bool tc = tensor_path(dtype, D);
+  if (tc && (!v_t || !aligned16(v_t) || !aligned16(x) || !aligned16(k_gate) || !aligned16(k_up)))
+    return FP_ERR_INVALID_ARG;
+  if (!tc && D > 32 * 256) return FP_ERR_UNSUPPORTED;
+  const PooledLayout L = pooled_layout(dtype, M, D, NB, n_active);
+  if (workspace_bytes < L.total) return FP_ERR_WORKSPACE;
+  int sms;
+  FP_TRY(device_info(sms));
+  cudaStream_t st = (cudaStream_t)stream;
+  int* err = at<int>(workspace, L.err);
+  if (cudaMemsetAsync(err, 0, 256, st) != cudaSuccess) return FP_ERR_CUDA;
+  if (M == 0) return FP_OK;
+  if (!tc || n_active == 0) {
+    // CUDA-core path (fp32 or untiled shapes); with no active block only the additive stream remains.
+    SimtArgs a{};
+    a.x = x; a.k_gate = k_gate; a.k_up = k_up; a.v = v; a.dtype = dtype; a.M = M; a.D = D; a.NB = NB;
+    a.active = active; a.n_active = n_active; a.stride = 1; a.offset = 0; a.ctx16 = ctx16;
+    a.out_proj = out_proj; a.y = y; a.y_f32 = y_f32;
+    return launch_simt(a, st);
+  }
+  void* h = at<void>(workspace, L.h);
+  GateUpArgs g{};
+  g.x = x; g.k_gate = k_gate; g.k_up = k_up; g.M = M; g.D = D; g.Np = NB * kBlock;
+  g.tiles = nullptr; g.meta = nullptr; g.key_off = nullptr; g.pair_tok = nullptr;
+  g.nbl = n_active; g.stride = 1; g.offset = 0; g.active = active; g.n_keys = n_active;
+  g.h = h; g.ldh = (int64_t)n_active * kBlock; g.err = err; g.num_sms = sms;
+  stage_mark(0, st);
+  FP_TRY(launch_gateup(g, st));
+  stage_mark(1, st);
+  DownArgs d{};
+  d.h = h; d.v_t = v_t; d.M = M; d.D = D; d.Np = NB * kBlock; d.K = n_active * kBlock; d.bmap = active;
+  d.stride = 1; d.offset = 0; d.ctx16 = ctx16; d.out_proj = out_proj; d.out_proj_f32 = dtype == FP_DTYPE_F32;
+  d.y = y; d.y_f32 = y_f32; d.err = err; d.num_sms = sms;
+  FP_TRY(launch_down(d, st));
+  stage_mark(2, st);
+  return FP_OK;
+}
+
+int fp_set_stage_events(void* const* events, int n_events) {
+  if (n_events < 0 || n_events > 8 || (n_events > 0 && !events)) return FP_ERR_INVALID_ARG;
+  for (int i = 0; i < 8; ++i) g_stage_events[i] = i < n_events ? (cudaEvent_t)events[i] : nullptr;
+  g_n_stage = n_events;
+  return FP_OK;
+}
+
+int fp_device_error(void* workspace, void* stream, int* code) {
+  if (!workspace) return FP_ERR_INVALID_ARG;
+  int host = 0;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (cudaMemcpyAsync(&host, workspace, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return FP_ERR_CUDA;
+  if (code) *code = host;
+  if (host != 0 && cudaMemsetAsync(workspace, 0, sizeof(int), st) != cudaSuccess) return FP_ERR_CUDA;
+  return host == 0 ? FP_OK : FP_ERR_TIMEOUT;
+}
+
+}  // extern "C"

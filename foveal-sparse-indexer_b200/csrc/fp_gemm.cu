@@ -1,0 +1,523 @@
+// Tensor-core (tcgen05 / TMEM / TMA) kernels of the gated Pattention contraction, bf16 in, fp32 accumulate.
+//
+//   gate/up:  for each work tile (parameter block b, up to 256 tokens that selected b):
+//             D[128 x n] = [K_gate,b ; K_up,b] (128 x D) . X[tokens]^T (D x n)   (A = weights, B = tokens)
+//             h[t, c] = silu(D[gate c, t]) * D[up c, t]  ->  H[t, slot(b)*64 + c]  (bf16)
+//   down:     Y[128 tokens x 256 cols] = sum over k-blocks j of H[:, j*64:+64] . V_b(j)^T ; + ctx16 . W_out^T
+//
+// Reference semantics: foveal_indexer/foveal_pattention.py:329-335 (two projections, SwiGLU, V
+// projection over the active blocks), per-token form foveal_indexer/pattention_triton.py:280-311,
+// additive stream foveal_pattention.py:338-342.
+//
+// Both kernels are persistent (one CTA per SM), warp-specialised: warp 0 issues TMA loads into a
+// 4-stage shared-memory ring, warp 1 (one thread) issues tcgen05.mma into one of two TMEM
+// accumulators (2 x 256 fp32 columns), warps 2-5 drain the other accumulator (epilogue overlaps the
+// next tile's MMAs).  Operand tiles are K-major with the 128-byte swizzle: one 64-element k-block is
+// exactly one parameter block's worth of the contraction dimension of the down projection.
+#include "fp_internal.cuh"
+
+#include <cudaTypedefs.h>
+#include <mutex>
+
+namespace fp {
+
+constexpr uint32_t kABytes = kTileM * kTileK * 2;  // 16 KB
+constexpr uint32_t kBBytes = kTileN * kTileK * 2;  // 32 KB
+constexpr uint32_t kStageBytes = kABytes + kBBytes;
+constexpr uint32_t kTmemCols = 512;
+
+struct __align__(8) PipeBars {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t accf[2];
+  uint64_t acce[2];
+  uint64_t done;
+  uint32_t tmem;
+  int32_t consumed;
+};
+
+constexpr size_t kGemmSmem = 1024 + kStages * kStageBytes + sizeof(PipeBars) + 256 * sizeof(int32_t) + 64;
+
+__device__ __forceinline__ uint8_t* aligned_smem(uint8_t* raw) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+}
+
+// Lane 0 waits, the warp follows its verdict (keeps warp-collective instructions uniform).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, err, code);
+  ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+  __syncwarp();
+  return ok;
+}
+
+__device__ __forceinline__ void pipe_init(PipeBars* bars, int epi_warps) {
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&bars->accf[a], 1);
+      mbar_init(&bars->acce[a], epi_warps);
+    }
+    mbar_init(&bars->done, 1);
+    bars->consumed = 0;
+    fence_mbar_init();
+  }
+  if ((threadIdx.x >> 5) == 0) {
+    tmem_alloc(&bars->tmem, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+}
+
+// After every role has left its loop: make sure no TMA copy or MMA is still in flight, then free TMEM.
+__device__ __forceinline__ void pipe_teardown(PipeBars* bars, uint32_t issued, int* err) {
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && aborted(err)) {
+    for (uint32_t i = (uint32_t)bars->consumed; i < issued; ++i)
+      if (!mbar_wait(&bars->full[i % kStages], (i / kStages) & 1u, nullptr, 0)) {
+        record_error(err, kErrDrain);
+        break;
+      }
+  }
+  __syncthreads();
+  if ((threadIdx.x >> 5) == 0) {
+    tc_fence_after();
+    tmem_dealloc(bars->tmem, kTmemCols);
+  }
+}
+
+// MMA issuer tail: wait until every tcgen05.mma issued by this thread has completed.
+__device__ __forceinline__ void mma_quiesce(PipeBars* bars, uint32_t consumed, int* err) {
+  bars->consumed = (int32_t)consumed;
+  umma_commit(&bars->done);
+  if (!mbar_wait(&bars->done, 0, nullptr, 0)) record_error(err, kErrDrain);
+}
+
+// ============================================================================================
+// Gate/up grouped GEMM with SwiGLU epilogue
+// ============================================================================================
+struct GuTile {
+  int b;               // global parameter block
+  int slot;            // column slot in H (x64)
+  const int32_t* list; // token ids (nullptr: identity r0 + i)
+  int64_t r0;
+  int n;               // valid tokens in this tile (0: skip)
+};
+
+__device__ __forceinline__ GuTile gu_decode(const GateUpArgs& a, int tile) {
+  GuTile t;
+  if (a.tiles) {
+    const int2 d = a.tiles[tile];
+    const int key = d.x;
+    t.slot = key % a.nbl;
+    t.b = t.slot * a.stride + a.offset;
+    const int start = a.key_off[key];
+    const int cnt = a.key_off[key + 1] - start;
+    t.list = a.pair_tok + start + d.y;
+    t.r0 = d.y;
+    t.n = min(kTileN, cnt - d.y);
+  } else {
+    const int key = tile % a.n_keys;  // token-tile-major order: concurrent tiles share rows of x
+    const int64_t rt = tile / a.n_keys;
+    t.slot = key;
+    t.b = a.active[key];
+    t.list = nullptr;
+    t.r0 = rt * kTileN;
+    t.n = (int)((a.M - t.r0) < (int64_t)kTileN ? (a.M - t.r0) : (int64_t)kTileN);
+  }
+  if (t.b < 0 || (int64_t)(t.b + 1) * kBlock > a.Np) {
+    record_error(a.err, kErrBadTile);
+    t.n = 0;
+  }
+  return t;
+}
+
+__device__ __forceinline__ int gu_token(const GuTile& t, int i) {
+  return t.list ? t.list[i] : (int)(t.r0 + i);
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_kg,
+              const __grid_constant__ CUtensorMap tm_ku, const GateUpArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = aligned_smem(smem_raw);
+  PipeBars* bars = reinterpret_cast<PipeBars*>(smem + kStages * kStageBytes);
+  int32_t* tok_ids = reinterpret_cast<int32_t*>(bars + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tm_x);
+    tma_prefetch_desc(&tm_kg);
+    tma_prefetch_desc(&tm_ku);
+  }
+  pipe_init(bars, 4);
+  const uint32_t tmem_base = bars->tmem;
+  const int ntiles = a.tiles ? a.meta[0] : a.n_keys * (int)((a.M + kTileN - 1) / kTileN);
+  const int nkb = a.D / kTileK;
+  uint32_t issued = 0;
+
+  if (warp == 0) {
+    // ---------------- TMA producer
+    uint32_t it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+      const GuTile t = gu_decode(a, tile);
+      if (t.n <= 0) continue;
+      const int npad = (t.n + 15) & ~15;
+      __syncwarp();
+      for (int i = lane; i < npad; i += 32) tok_ids[i] = gu_token(t, i < t.n ? i : t.n - 1);
+      __syncwarp();
+      if (lane == 0) {
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1u;
+          if (!mbar_wait(&bars->empty[s], ph ^ 1u, a.err, kErrWaitEmpty)) { ok = false; break; }
+          uint8_t* As = smem + s * kStageBytes;
+          uint8_t* Bs = As + kABytes;
+          mbar_arrive_expect_tx(&bars->full[s], kABytes + (uint32_t)npad * 128u);
+          const int kc = kb * kTileK;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {  // rows [32q, 32q+16) gate, [32q+16, 32q+32) up: channels 16q..16q+15
+            tma_load_2d(As + (32 * q) * 128, &tm_kg, &bars->full[s], kc, t.b * kBlock + 16 * q);
+            tma_load_2d(As + (32 * q + 16) * 128, &tm_ku, &bars->full[s], kc, t.b * kBlock + 16 * q);
+          }
+          for (int g = 0; g < npad / 4; ++g)
+            tma_gather4(Bs + 4 * g * 128, &tm_x, &bars->full[s], kc, tok_ids[4 * g], tok_ids[4 * g + 1],
+                        tok_ids[4 * g + 2], tok_ids[4 * g + 3]);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      it = __shfl_sync(0xffffffffu, it, 0);
+    }
+    issued = it;
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (one thread)
+    if (lane == 0) {
+      uint32_t it = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        const GuTile t = gu_decode(a, tile);
+        if (t.n <= 0) continue;
+        const int npad = (t.n + 15) & ~15;
+        const int acc = local & 1;
+        const uint32_t aph = (local >> 1) & 1;
+        if (!mbar_wait(&bars->acce[acc], aph ^ 1u, a.err, kErrWaitAccEmpty)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kTileN;
+        const uint32_t idesc = umma_idesc_bf16(kTileM, npad);
+        for (int kb = 0; kb < nkb; ++kb) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1u;
+          if (!mbar_wait(&bars->full[s], ph, a.err, kErrWaitFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t ad = umma_desc_sw128(smem_u32(smem + s * kStageBytes));
+          const uint64_t bd = umma_desc_sw128(smem_u32(smem + s * kStageBytes + kABytes));
+#pragma unroll
+          for (int k = 0; k < kTileK / 16; ++k)
+            umma_bf16(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+          umma_commit(&bars->empty[s]);
+          ++it;
+        }
+        if (!ok) break;
+        umma_commit(&bars->accf[acc]);
+        ++local;
+      }
+      mma_quiesce(bars, it, a.err);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue: warps 2..5; warp w reads TMEM lanes [32*(w%4), +32)
+    const int q = warp & 3;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+      const GuTile t = gu_decode(a, tile);
+      if (t.n <= 0) continue;
+      const int npad = (t.n + 15) & ~15;
+      const int acc = local & 1;
+      const uint32_t aph = (local >> 1) & 1;
+      if (!warp_wait(&bars->accf[acc], aph, a.err, kErrWaitAccFull)) break;
+      tc_fence_after();
+      __nv_bfloat16* hbase = reinterpret_cast<__nv_bfloat16*>(a.h) + (int64_t)t.slot * kBlock + 16 * q + (lane & 15);
+      for (int c = 0; c * 32 < npad; ++c) {
+        uint32_t v[32];
+        __syncwarp();
+        tmem_ld32(tmem_base + acc * kTileN + c * 32 + ((uint32_t)(32 * q) << 16), v);
+        tmem_ld_wait();
+        const int ni = c * 32 + lane;
+        const int tok_l = ni < t.n ? gu_token(t, ni) : -1;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          // lane L<16 holds gate(channel 16q+L), lane L+16 holds up(channel 16q+L), columns = tokens
+          const uint32_t send = lane < 16 ? v[16 + j] : v[j];
+          const float recv = __uint_as_float(__shfl_xor_sync(0xffffffffu, send, 16));
+          const float g = lane < 16 ? __uint_as_float(v[j]) : recv;
+          const float u = lane < 16 ? recv : __uint_as_float(v[16 + j]);
+          const float h = g / (1.0f + expf(-g)) * u;
+          const int tok = __shfl_sync(0xffffffffu, tok_l, lane < 16 ? j : 16 + j);
+          if (tok >= 0) hbase[(int64_t)tok * a.ldh] = __float2bfloat16_rn(h);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->acce[acc]);
+      ++local;
+    }
+  }
+  pipe_teardown(bars, issued, a.err);
+}
+
+// ============================================================================================
+// Down projection: Y = H . V_sel + additive stream
+// ============================================================================================
+constexpr int kGroupM = 16;
+
+__device__ __forceinline__ void down_tile(int tile, int m_tiles, int n_tiles, int& m, int& n) {
+  const int per_group = kGroupM * n_tiles;
+  const int group = tile / per_group;
+  const int first_m = group * kGroupM;
+  const int gsz = min(m_tiles - first_m, kGroupM);
+  const int r = tile % per_group;
+  m = first_m + r % gsz;
+  n = r / gsz;
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CUtensorMap tm_vt,
+            const DownArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = aligned_smem(smem_raw);
+  PipeBars* bars = reinterpret_cast<PipeBars*>(smem + kStages * kStageBytes);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tm_h);
+    tma_prefetch_desc(&tm_vt);
+  }
+  pipe_init(bars, 4);
+  const uint32_t tmem_base = bars->tmem;
+  const int m_tiles = (int)((a.M + kTileM - 1) / kTileM);
+  const int n_tiles = (a.D + kTileN - 1) / kTileN;
+  const int ntiles = m_tiles * n_tiles;
+  const int nkb = a.K / kTileK;
+  uint32_t issued = 0;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        int m, n;
+        down_tile(tile, m_tiles, n_tiles, m, n);
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1u;
+          if (!mbar_wait(&bars->empty[s], ph ^ 1u, a.err, kErrWaitEmpty)) { ok = false; break; }
+          uint8_t* As = smem + s * kStageBytes;
+          uint8_t* Bs = As + kABytes;
+          const int gb = a.bmap ? a.bmap[kb] : kb * a.stride + a.offset;
+          mbar_arrive_expect_tx(&bars->full[s], kStageBytes);
+          tma_load_2d(As, &tm_h, &bars->full[s], kb * kTileK, m * kTileM);
+          tma_load_2d(Bs, &tm_vt, &bars->full[s], gb * kBlock, n * kTileN);
+        }
+      }
+      issued = it;
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      int local = 0;
+      bool ok = true;
+      const uint32_t idesc = umma_idesc_bf16(kTileM, kTileN);
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        const int acc = local & 1;
+        const uint32_t aph = (local >> 1) & 1;
+        if (!mbar_wait(&bars->acce[acc], aph ^ 1u, a.err, kErrWaitAccEmpty)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kTileN;
+        for (int kb = 0; kb < nkb; ++kb) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1u;
+          if (!mbar_wait(&bars->full[s], ph, a.err, kErrWaitFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t ad = umma_desc_sw128(smem_u32(smem + s * kStageBytes));
+          const uint64_t bd = umma_desc_sw128(smem_u32(smem + s * kStageBytes + kABytes));
+#pragma unroll
+          for (int k = 0; k < kTileK / 16; ++k)
+            umma_bf16(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+          umma_commit(&bars->empty[s]);
+          ++it;
+        }
+        if (!ok) break;
+        umma_commit(&bars->accf[acc]);
+        ++local;
+      }
+      mma_quiesce(bars, it, a.err);
+    }
+    __syncwarp();
+  } else {
+    const int q = warp & 3;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+      int m, n;
+      down_tile(tile, m_tiles, n_tiles, m, n);
+      const int acc = local & 1;
+      const uint32_t aph = (local >> 1) & 1;
+      if (!warp_wait(&bars->accf[acc], aph, a.err, kErrWaitAccFull)) break;
+      tc_fence_after();
+      const int64_t row = (int64_t)m * kTileM + 32 * q + lane;
+      const bool row_ok = row < a.M;
+      float ctx[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) ctx[k] = 0.f;
+      if (a.ctx16 && row_ok) {
+        const float4* cp = reinterpret_cast<const float4*>(a.ctx16 + row * 16);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 f = __ldg(cp + i);
+          ctx[4 * i] = f.x; ctx[4 * i + 1] = f.y; ctx[4 * i + 2] = f.z; ctx[4 * i + 3] = f.w;
+        }
+      }
+      for (int c = 0; c < kTileN / 32; ++c) {
+        const int col0 = n * kTileN + c * 32;
+        uint32_t v[32];
+        __syncwarp();
+        tmem_ld32(tmem_base + acc * kTileN + c * 32 + ((uint32_t)(32 * q) << 16), v);
+        tmem_ld_wait();
+        // additive stream: o[i] += sum_k ctx[k] * W_out[col0 + i][k]; lane L loads row col0 + L of
+        // W_out and the warp broadcasts it (all lanes of a chunk share the same 32 columns)
+        float o[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = __uint_as_float(v[i]);
+        if (a.ctx16 && col0 < a.D) {
+          float w[16];
+          const int64_t wrow = (int64_t)(col0 + lane) * 16;
+          if (a.out_proj_f32) {
+            const float4* wp = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.out_proj) + wrow);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float4 f = __ldg(wp + k);
+              w[4 * k] = f.x; w[4 * k + 1] = f.y; w[4 * k + 2] = f.z; w[4 * k + 3] = f.w;
+            }
+          } else {
+            const uint4* wp = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.out_proj) + wrow);
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+              const uint4 u = __ldg(wp + k);
+              const uint32_t ww[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                w[8 * k + 2 * e] = __uint_as_float(ww[e] << 16);
+                w[8 * k + 2 * e + 1] = __uint_as_float(ww[e] & 0xFFFF0000u);
+              }
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            float s = 0.f;
+#pragma unroll
+            for (int k = 0; k < 16; ++k) s = fmaf(ctx[k], __shfl_sync(0xffffffffu, w[k], i), s);
+            o[i] += s;
+          }
+        }
+        if (row_ok && col0 < a.D) {
+        if (a.y_f32) {
+          float4* yp = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.y) + row * a.D + col0);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) yp[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+        } else {
+          uint4* yp = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.y) + row * a.D + col0);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint32_t p[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const __nv_bfloat162 b2 = __floats2bfloat162_rn(o[8 * i + 2 * e], o[8 * i + 2 * e + 1]);
+              p[e] = *reinterpret_cast<const uint32_t*>(&b2);
+            }
+            yp[i] = make_uint4(p[0], p[1], p[2], p[3]);
+          }
+        }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->acce[acc]);
+      ++local;
+    }
+  }
+  pipe_teardown(bars, issued, a.err);
+}
+
+// ============================================================================================
+// Host side
+// ============================================================================================
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+bool encode_map_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                   uint32_t box_inner, uint32_t box_outer) {
+  auto fn = get_encode();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+static int set_smem(const void* fn) {
+  return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem) == cudaSuccess
+             ? FP_OK : FP_ERR_CUDA;
+}
+
+int launch_gateup(const GateUpArgs& a, cudaStream_t st) {
+  CUtensorMap tx, tg, tu;
+  if (!encode_map_2d(&tx, a.x, a.D, a.M, (uint64_t)a.D * 2, kTileK, 1) ||
+      !encode_map_2d(&tg, a.k_gate, a.D, a.Np, (uint64_t)a.D * 2, kTileK, 16) ||
+      !encode_map_2d(&tu, a.k_up, a.D, a.Np, (uint64_t)a.D * 2, kTileK, 16))
+    return FP_ERR_CUDA;
+  static std::once_flag once;
+  static int attr = FP_OK;
+  std::call_once(once, [] { attr = set_smem((const void*)gateup_kernel); });
+  if (attr != FP_OK) return attr;
+  gateup_kernel<<<a.num_sms, kGemmThreads, kGemmSmem, st>>>(tx, tg, tu, a);
+  return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+}
+
+int launch_down(const DownArgs& a, cudaStream_t st) {
+  CUtensorMap th, tv;
+  if (!encode_map_2d(&th, a.h, a.K, a.M, (uint64_t)a.K * 2, kTileK, kTileM) ||
+      !encode_map_2d(&tv, a.v_t, a.Np, a.D, (uint64_t)a.Np * 2, kTileK, kTileN))
+    return FP_ERR_CUDA;
+  static std::once_flag once;
+  static int attr = FP_OK;
+  std::call_once(once, [] { attr = set_smem((const void*)down_kernel); });
+  if (attr != FP_OK) return attr;
+  const int64_t tiles = ((a.M + kTileM - 1) / kTileM) * ((a.D + kTileN - 1) / kTileN);
+  const int grid = (int)std::min<int64_t>(tiles, a.num_sms);
+  if (grid <= 0) return FP_OK;
+  down_kernel<<<grid, kGemmThreads, kGemmSmem, st>>>(th, tv, a);
+  return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+}
+
+}  // namespace fp

@@ -1,0 +1,108 @@
+// Internal declarations shared by the CUDA translation units of libfovealpatt.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "../../include/foveal_pattention.h"
+#include "fp_ptx.cuh"
+
+namespace fp {
+
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+// Tile shapes of the tensor-core path.
+constexpr int kTileM = 128;       // UMMA M: weight rows (gate/up) or tokens (down)
+constexpr int kTileN = 256;       // UMMA N: tokens (gate/up) or output columns (down)
+constexpr int kTileK = 64;        // one 128-byte swizzle row of bf16 = one parameter block
+constexpr int kStages = 4;
+constexpr int kBlock = 64;        // parameter tokens per block
+constexpr int kGemmThreads = 192; // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+
+// ---- router.cu
+int launch_router_scores(const void* x, const void* wq, const void* k16, int dtype, int64_t M, int D,
+                         int NB, float temperature, float* scores, float* q16, cudaStream_t st);
+int launch_select(const float* scores, int64_t M, int NB, int base, float top_p, int k_min, int k_max,
+                  int capacity, float temperature, int32_t* idx, int32_t* cnt, const float* k16f,
+                  float* ctx16, float* stats, cudaStream_t st);
+int launch_convert_keys(const void* k16, int dtype, int n, float* out, cudaStream_t st);
+int launch_build_csr(const int32_t* ridx, const int32_t* rcnt, int64_t M, int base, int cap, int stride,
+                     int offset, int nbl, int chunk, int nkey, int tile_rows, int32_t* key_cnt,
+                     int32_t* key_off, int32_t* key_fill, int32_t* pair_tok, int2* tiles, int max_tiles,
+                     int32_t* meta, int* err, cudaStream_t st);
+int launch_colmean(const void* a, int dtype, int64_t M, int D, float* part, float* mean, cudaStream_t st);
+int launch_pooled_topk(const float* mean_vec, const void* wq, const void* k16, int dtype, int D, int NB,
+                       int base, int remote, int mode, int32_t* active, float* mean_scores_out,
+                       cudaStream_t st);
+
+// ---- gemm.cu (tensor-core path, bf16)
+struct GateUpArgs {
+  const void* x;        // [M, D] bf16
+  const void* k_gate;   // [Np, D] bf16
+  const void* k_up;     // [Np, D] bf16
+  int64_t M;
+  int D, Np;
+  // work list: explicit (tiles/meta from the CSR builder) or implicit (pooled: n_keys x ceil(M/256))
+  const int2* tiles;
+  const int32_t* meta;      // meta[0] = number of tiles (explicit mode)
+  const int32_t* key_off;   // [nkey + 1] (explicit mode)
+  const int32_t* pair_tok;  // token ids grouped by key (explicit mode)
+  int nbl, stride, offset;  // explicit mode: slot = key % nbl, block = slot * stride + offset
+  const int32_t* active;    // implicit mode: block id of key j
+  int n_keys;               // implicit mode: number of active blocks
+  void* h;                  // [M, ldh] bf16 activations
+  int64_t ldh;
+  int* err;
+  int num_sms;
+};
+int launch_gateup(const GateUpArgs& a, cudaStream_t st);
+
+struct DownArgs {
+  const void* h;        // [M, K] bf16
+  const void* v_t;      // [D, Np] bf16 (V transposed)
+  int64_t M;
+  int D, Np, K;         // K = number of k-blocks * 64 read from h
+  const int32_t* bmap;  // optional: global block of k-block j (pooled); else j*stride+offset
+  int stride, offset;
+  const float* ctx16;   // optional additive stream context [M, 16]
+  const void* out_proj; // [D, 16] (bf16 or fp32 per out_proj_f32)
+  int out_proj_f32;
+  void* y;              // [M, D]
+  int y_f32;
+  int* err;
+  int num_sms;
+};
+int launch_down(const DownArgs& a, cudaStream_t st);
+
+// ---- simt.cu (CUDA-core path: fp32 models and shapes the tensor-core path does not tile)
+struct SimtArgs {
+  const void* x;
+  const void* k_gate;
+  const void* k_up;
+  const void* v;        // [Np, D] reference layout
+  int dtype;
+  int64_t M;
+  int D, NB;
+  // per-token lists (token mode) or a shared list (pooled mode)
+  int base;
+  const int32_t* ridx;  // [M, cap]
+  const int32_t* rcnt;  // [M]
+  int cap;
+  const int32_t* active;
+  int n_active;
+  int stride, offset;   // local block filter (token mode)
+  const float* ctx16;
+  const void* out_proj;
+  void* y;
+  int y_f32;
+};
+int launch_simt(const SimtArgs& a, cudaStream_t st);
+
+// ---- tensor maps
+bool encode_map_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                   uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer);
+
+}  // namespace fp

@@ -1,0 +1,544 @@
+// 16-D foveal router, top-p block selection, block-CSR construction and pooled routing.
+//
+// Reference semantics (kreasof-ai/foveal-sparse-indexer):
+//   compute_router_scores   foveal_indexer/foveal_pattention.py:257-262
+//   masked_softmax          foveal_indexer/core.py:36-43
+//   select_blocks           foveal_indexer/core.py:46-160 (non-causal branch :90-99)
+//   pooled routing          foveal_indexer/foveal_pattention.py:292-303 (train), :310-321 (eval)
+//   additive-stream context foveal_indexer/foveal_pattention.py:338-340
+//
+// All router arithmetic is fp32 (the cumulative sum accumulates in fp64 and rounds every prefix to
+// fp32, as PyTorch's CPU cumsum does).  Ties in probability are broken toward the lower block id.
+#include "fp_internal.cuh"
+
+namespace fp {
+
+// --------------------------------------------------------------------------------------------
+// Scores: S[m, b] = (rms_norm(x[m] . Wq^T) . K16[b]) / sqrt(16)  [/ temperature]
+// One warp handles TPW tokens at a time; lanes split the hidden dimension in 8-element vectors.
+// --------------------------------------------------------------------------------------------
+constexpr int kScoreTPW = 4;
+constexpr int kScoreWarps = 8;
+
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&v)[8]);
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float (&v)[8]) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
+  const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kScoreWarps * 32)
+router_scores_kernel(const T* __restrict__ x, const T* __restrict__ wq, const T* __restrict__ k16,
+                     int64_t M, int D, int NB, float inv_scale_div, float temperature,
+                     float* __restrict__ scores, float* __restrict__ q16_out) {
+  extern __shared__ float sk[];  // [NB][16] fp32 block keys
+  for (int i = threadIdx.x; i < NB * 16; i += blockDim.x) sk[i] = to_f32(k16[i]);
+  __syncthreads();
+
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int64_t tok0 = ((int64_t)blockIdx.x * kScoreWarps + warp) * kScoreTPW;
+  if (tok0 >= M) return;
+
+  float acc[kScoreTPW][16];
+#pragma unroll
+  for (int t = 0; t < kScoreTPW; ++t)
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc[t][j] = 0.f;
+
+  for (int c = lane * 8; c < D; c += 256) {
+    float xv[kScoreTPW][8];
+#pragma unroll
+    for (int t = 0; t < kScoreTPW; ++t) {
+      const int64_t tok = tok0 + t < M ? tok0 + t : M - 1;
+      load8<T>(x + tok * D + c, xv[t]);
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      float wv[8];
+      load8<T>(wq + (int64_t)j * D + c, wv);
+#pragma unroll
+      for (int t = 0; t < kScoreTPW; ++t)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[t][j] = fmaf(xv[t][e], wv[e], acc[t][j]);
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < kScoreTPW; ++t)
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      float v = acc[t][j];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      acc[t][j] = v;
+    }
+
+  const float eps = 1.1920928955078125e-07f;  // torch.finfo(float32).eps: F.rms_norm's default
+#pragma unroll
+  for (int t = 0; t < kScoreTPW; ++t) {
+    const int64_t tok = tok0 + t;
+    if (tok >= M) break;
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) ss = fmaf(acc[t][j], acc[t][j], ss);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(ss * (1.0f / 16.0f) + eps));
+    float q[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) q[j] = acc[t][j] * inv;
+    if (q16_out && lane < 16) {
+      float qv = q[0];
+#pragma unroll
+      for (int j = 1; j < 16; ++j) qv = (lane == j) ? q[j] : qv;
+      q16_out[tok * 16 + lane] = qv;
+    }
+    for (int b = lane; b < NB; b += 32) {
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) s = fmaf(q[j], sk[b * 16 + j], s);
+      s = s * inv_scale_div;            // / sqrt(16): exact power-of-two scaling
+      if (temperature != 1.0f) s = __fdiv_rn(s, temperature);
+      scores[tok * NB + b] = s;
+    }
+  }
+}
+
+// --------------------------------------------------------------------------------------------
+// Selection: one warp per token row of scores.  Softmax over all blocks, base mass credit, stable
+// descending order of remote probabilities (bitonic sort of 64-bit keys in per-warp shared memory),
+// fp64-accumulated cumulative sum, count clamped to [K_min, min(available, K_max)].  Optionally the
+// additive-stream context ctx16 = softmax(S/T) . K16.
+// --------------------------------------------------------------------------------------------
+constexpr int kSelWarps = 4;
+
+__device__ __forceinline__ unsigned long long sel_key(float p, int b, bool remote) {
+  // remote: (bits(p)+1, ~b) so that higher p first, then lower id; base: below every remote key.
+  const uint32_t lo = 0xFFFFFFFFu - (uint32_t)b;
+  return remote ? (((unsigned long long)(__float_as_uint(p) + 1u)) << 32) | lo : (unsigned long long)lo;
+}
+
+__global__ void __launch_bounds__(kSelWarps * 32)
+select_blocks_kernel(const float* __restrict__ scores, int64_t M, int NB, int nb_pad, int base,
+                     float top_p, int k_min, int k_max, int capacity, float temperature,
+                     int32_t* __restrict__ out_idx, int32_t* __restrict__ out_cnt,
+                     const float* __restrict__ k16f, float* __restrict__ ctx16,
+                     float* __restrict__ stats) {
+  extern __shared__ unsigned long long skeys[];  // [kSelWarps][nb_pad]
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int64_t tok = (int64_t)blockIdx.x * kSelWarps + warp;
+  if (tok >= M) return;
+  unsigned long long* keys = skeys + (size_t)warp * nb_pad;
+  float* pbuf = reinterpret_cast<float*>(skeys + (size_t)kSelWarps * nb_pad) + (size_t)warp * nb_pad;
+  const float* srow = scores + tok * NB;
+
+  // softmax (core.py:36-43): max, exp(s - max), sum, divide
+  float mx = -INFINITY;
+  for (int b = lane; b < NB; b += 32) {
+    float s = srow[b];
+    if (temperature != 1.0f) s = __fdiv_rn(s, temperature);
+    pbuf[b] = s;
+    mx = fmaxf(mx, s);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (!isfinite(mx)) mx = 0.f;
+  float sum = 0.f;
+  for (int b = lane; b < NB; b += 32) {
+    const float e = expf(pbuf[b] - mx);
+    pbuf[b] = e;
+    sum += e;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float denom = fmaxf(sum, 1e-20f);
+  __syncwarp();
+  for (int b = lane; b < nb_pad; b += 32) {
+    if (b < NB) {
+      const float p = __fdiv_rn(pbuf[b], denom);
+      pbuf[b] = p;
+      keys[b] = sel_key(p, b, b >= base);
+    } else {
+      keys[b] = 0ull;
+    }
+  }
+  __syncwarp();
+
+  // additive-stream context (foveal_pattention.py:339-340): ctx[j] = sum_b p[b] K16[b][j]
+  if (ctx16) {
+    float c[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) c[j] = 0.f;
+    for (int b = lane; b < NB; b += 32) {
+      const float p = pbuf[b];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) c[j] = fmaf(p, k16f[b * 16 + j], c[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      float v = c[j];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      c[j] = v;
+    }
+    if (lane < 16) {
+      float v = c[0];
+#pragma unroll
+      for (int j = 1; j < 16; ++j) v = (lane == j) ? c[j] : v;
+      ctx16[tok * 16 + lane] = v;
+    }
+  }
+  if (out_idx == nullptr) return;  // context-only mode
+
+  // bitonic sort, descending by key
+  for (int k = 2; k <= nb_pad; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int idx = lane; idx < (nb_pad >> 1); idx += 32) {
+        const int i = 2 * j * (idx / j) + (idx % j);
+        const int l = i + j;
+        const unsigned long long a = keys[i], bkey = keys[l];
+        const bool desc = (i & k) == 0;
+        if (desc ? (a < bkey) : (a > bkey)) {
+          keys[i] = bkey;
+          keys[l] = a;
+        }
+      }
+      __syncwarp();
+    }
+  }
+
+  // remote_indices = sorted ids (core.py:121-123); entries past NB are zero padding
+  int32_t* orow = out_idx + tok * capacity;
+  for (int i = lane; i < capacity; i += 32) {
+    orow[i] = i < NB ? (int32_t)(0xFFFFFFFFu - (uint32_t)(keys[i] & 0xFFFFFFFFull)) : 0;
+  }
+
+  if (lane == 0) {
+    // base (local) mass (core.py:104), target (:111), needed/count (:115-119)
+    float local_mass = 0.f;
+    for (int b = 0; b < base && b < NB; ++b) local_mass += pbuf[b];
+    float target = top_p - local_mass;
+    target = target > 0.f ? target : 0.f;
+    const int available = NB - base;
+    int counts = 0;
+    if (available > 0) {
+      const int X = available < k_max ? available : k_max;
+      int needed;
+      if (target > 0.f) {
+        double acc = 0.0;
+        int n = 0;
+        for (; n < X; ++n) {
+          const uint32_t hi = (uint32_t)(keys[n] >> 32);
+          const float p = hi ? __uint_as_float(hi - 1u) : 0.f;  // base/pad entries clamp to 0
+          acc += (double)p;
+          if ((float)acc >= target) break;
+        }
+        needed = n + 1;  // #(cum < target) + 1; saturates at X + 1 when never reached within X
+      } else {
+        needed = 0;
+      }
+      needed = needed > k_min ? needed : k_min;
+      counts = needed < available ? needed : available;
+      counts = counts < k_max ? counts : k_max;
+      if (counts < 0) counts = 0;
+    }
+    out_cnt[tok] = counts;
+    if (stats) {
+      atomicAdd(&stats[0], (k_max > 0 && counts >= k_max) ? 1.f : 0.f);
+      atomicAdd(&stats[1], (float)counts);
+      atomicAdd(&stats[2], counts == 0 ? 1.f : 0.f);
+    }
+  }
+}
+
+// --------------------------------------------------------------------------------------------
+// Block CSR (block-major token lists) in token chunks: key = chunk(t) * NBL + slot(b), where only
+// blocks with b % stride == offset are local and slot(b) = b / stride.
+// --------------------------------------------------------------------------------------------
+__device__ __forceinline__ int token_block(int s, int base, const int32_t* ridx, int cap, int cnt) {
+  // slot s < base: base block s; otherwise the (s-base)-th selected remote block, or -1
+  if (s < base) return s;
+  const int r = s - base;
+  return r < cnt ? ridx[r] : -1;
+}
+
+__global__ void csr_count_kernel(const int32_t* __restrict__ ridx, const int32_t* __restrict__ rcnt,
+                                 int64_t M, int base, int cap, int stride, int offset, int nbl,
+                                 int chunk, int32_t* __restrict__ key_cnt) {
+  const int slots = base + cap;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= M * slots) return;
+  const int64_t t = i / slots;
+  const int s = (int)(i % slots);
+  const int b = token_block(s, base, ridx + t * cap, cap, rcnt[t]);
+  if (b < 0 || (b % stride) != offset) return;
+  const int key = (int)(t / chunk) * nbl + b / stride;
+  atomicAdd(&key_cnt[key], 1);
+}
+
+// Single CTA: exclusive scan of key counts, tile list (key, first row) with <= tile_rows rows each.
+__global__ void __launch_bounds__(1024)
+csr_scan_kernel(const int32_t* __restrict__ key_cnt, int nkey, int tile_rows,
+                int32_t* __restrict__ key_off, int32_t* __restrict__ key_fill,
+                int2* __restrict__ tiles, int max_tiles, int32_t* __restrict__ meta, int* err) {
+  __shared__ int s_pairs[1024], s_tiles[1024];
+  const int tid = threadIdx.x;
+  const int per = (nkey + 1023) / 1024;
+  const int k0 = tid * per, k1 = min(nkey, k0 + per);
+  int pairs = 0, ntile = 0;
+  for (int k = k0; k < k1; ++k) {
+    pairs += key_cnt[k];
+    ntile += (key_cnt[k] + tile_rows - 1) / tile_rows;
+  }
+  s_pairs[tid] = pairs;
+  s_tiles[tid] = ntile;
+  __syncthreads();
+  for (int o = 1; o < 1024; o <<= 1) {  // Hillis-Steele inclusive scan
+    const int a = tid >= o ? s_pairs[tid - o] : 0;
+    const int b = tid >= o ? s_tiles[tid - o] : 0;
+    __syncthreads();
+    s_pairs[tid] += a;
+    s_tiles[tid] += b;
+    __syncthreads();
+  }
+  int poff = s_pairs[tid] - pairs, toff = s_tiles[tid] - ntile;
+  for (int k = k0; k < k1; ++k) {
+    const int c = key_cnt[k];
+    key_off[k] = poff;
+    key_fill[k] = 0;
+    for (int r = 0; r < c; r += tile_rows) {
+      if (toff < max_tiles) tiles[toff] = make_int2(k, r);
+      ++toff;
+    }
+    poff += c;
+  }
+  if (tid == 1023) {
+    key_off[nkey] = s_pairs[1023];
+    const int nt = s_tiles[1023];
+    meta[0] = nt < max_tiles ? nt : max_tiles;
+    meta[1] = s_pairs[1023];
+    if (nt > max_tiles) record_error(err, kErrBadTile);
+  }
+}
+
+__global__ void csr_fill_kernel(const int32_t* __restrict__ ridx, const int32_t* __restrict__ rcnt,
+                                int64_t M, int base, int cap, int stride, int offset, int nbl, int chunk,
+                                const int32_t* __restrict__ key_off, int32_t* __restrict__ key_fill,
+                                int32_t* __restrict__ pair_tok) {
+  const int slots = base + cap;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= M * slots) return;
+  const int64_t t = i / slots;
+  const int s = (int)(i % slots);
+  const int b = token_block(s, base, ridx + t * cap, cap, rcnt[t]);
+  if (b < 0 || (b % stride) != offset) return;
+  const int key = (int)(t / chunk) * nbl + b / stride;
+  const int pos = atomicAdd(&key_fill[key], 1);
+  pair_tok[key_off[key] + pos] = (int32_t)t;
+}
+
+// --------------------------------------------------------------------------------------------
+// Pooled routing.
+// --------------------------------------------------------------------------------------------
+constexpr int kColRows = 256;
+
+// partial column sums over kColRows-row chunks: part[chunk][d]
+template <typename T>
+__global__ void colsum_partial_kernel(const T* __restrict__ a, int64_t M, int D, float* __restrict__ part) {
+  const int d = blockIdx.x * blockDim.x + threadIdx.x;
+  if (d >= D) return;
+  const int64_t r0 = (int64_t)blockIdx.y * kColRows;
+  const int64_t r1 = min(M, r0 + kColRows);
+  float s = 0.f;
+  for (int64_t r = r0; r < r1; ++r) s += to_f32(a[r * D + d]);
+  part[(int64_t)blockIdx.y * D + d] = s;
+}
+__global__ void colsum_final_kernel(const float* __restrict__ part, int nchunk, int64_t M, int D,
+                                    float* __restrict__ mean) {
+  const int d = blockIdx.x * blockDim.x + threadIdx.x;
+  if (d >= D) return;
+  float s = 0.f;
+  for (int c = 0; c < nchunk; ++c) s += part[(int64_t)c * D + d];
+  mean[d] = __fdiv_rn(s, (float)M);
+}
+
+__device__ __forceinline__ uint32_t orderable(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Single CTA of 512 threads.  mode 0 (eval): mean_vec is the token-mean of x [D]; the pooled query
+// q = rms_norm(W_q mean), scores = q . K16^T (no 1/sqrt(16), foveal_pattention.py:312-313).
+// mode 1 (train): mean_vec is the token-mean of the per-token scores [NB].  Then top-k over the
+// remote blocks, ordered by descending score (ties: lower id), base ids first.
+template <typename T>
+__global__ void __launch_bounds__(512)
+pooled_topk_kernel(const float* __restrict__ mean_vec, const T* __restrict__ wq, const T* __restrict__ k16,
+                   int D, int NB, int nb_pad, int base, int remote, int mode, int32_t* __restrict__ active,
+                   float* __restrict__ mean_scores_out) {
+  extern __shared__ unsigned long long pk[];  // [nb_pad]
+  __shared__ float sq[16];
+  __shared__ float sscore[4096];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (mode == 0) {
+    if (warp < 16) {
+      float acc = 0.f;
+      for (int d = lane; d < D; d += 32) acc = fmaf(mean_vec[d], to_f32(wq[(int64_t)warp * D + d]), acc);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane == 0) sq[warp] = acc;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      float ss = 0.f;
+      for (int j = 0; j < 16; ++j) ss = fmaf(sq[j], sq[j], ss);
+      const float inv = __fdiv_rn(1.0f, __fsqrt_rn(ss * (1.0f / 16.0f) + 1.1920928955078125e-07f));
+      for (int j = 0; j < 16; ++j) sq[j] = sq[j] * inv;
+    }
+    __syncthreads();
+    for (int b = tid; b < NB; b += blockDim.x) {
+      float s = 0.f;
+      for (int j = 0; j < 16; ++j) s = fmaf(sq[j], to_f32(k16[b * 16 + j]), s);
+      sscore[b] = s;
+    }
+  } else {
+    for (int b = tid; b < NB; b += blockDim.x) sscore[b] = mean_vec[b];
+  }
+  __syncthreads();
+  for (int b = tid; b < nb_pad; b += blockDim.x) {
+    unsigned long long key = 0ull;
+    if (b < NB && b >= base)
+      key = ((unsigned long long)orderable(sscore[b]) << 32) | (0xFFFFFFFFu - (uint32_t)b);
+    pk[b] = key;
+    if (mean_scores_out && b < NB) mean_scores_out[b] = sscore[b];
+  }
+  __syncthreads();
+  for (int k = 2; k <= nb_pad; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int idx = tid; idx < (nb_pad >> 1); idx += blockDim.x) {
+        const int i = 2 * j * (idx / j) + (idx % j);
+        const int l = i + j;
+        const unsigned long long a = pk[i], bb = pk[l];
+        const bool desc = (i & k) == 0;
+        if (desc ? (a < bb) : (a > bb)) { pk[i] = bb; pk[l] = a; }
+      }
+      __syncthreads();
+    }
+  }
+  for (int i = tid; i < base + remote; i += blockDim.x) {
+    active[i] = i < base ? i : (int32_t)(0xFFFFFFFFu - (uint32_t)(pk[i - base] & 0xFFFFFFFFull));
+  }
+}
+
+// ============================================================================================
+// Host launchers
+// ============================================================================================
+int launch_router_scores(const void* x, const void* wq, const void* k16, int dtype, int64_t M, int D,
+                         int NB, float temperature, float* scores, float* q16, cudaStream_t st) {
+  if (M <= 0) return FP_OK;
+  const int blocks = (int)((M + kScoreWarps * kScoreTPW - 1) / (kScoreWarps * kScoreTPW));
+  const size_t smem = (size_t)NB * 16 * sizeof(float);
+  if (smem > 48 * 1024) {
+    cudaError_t e = dtype == FP_DTYPE_BF16
+        ? cudaFuncSetAttribute(router_scores_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
+        : cudaFuncSetAttribute(router_scores_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return FP_ERR_CUDA;
+  }
+  if (dtype == FP_DTYPE_BF16)
+    router_scores_kernel<__nv_bfloat16><<<blocks, kScoreWarps * 32, smem, st>>>(
+        (const __nv_bfloat16*)x, (const __nv_bfloat16*)wq, (const __nv_bfloat16*)k16, M, D, NB, 0.25f,
+        temperature, scores, q16);
+  else
+    router_scores_kernel<float><<<blocks, kScoreWarps * 32, smem, st>>>(
+        (const float*)x, (const float*)wq, (const float*)k16, M, D, NB, 0.25f, temperature, scores, q16);
+  return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+}
+
+static int pow2_at_least(int n) {
+  int p = 32;
+  while (p < n) p <<= 1;
+  return p;
+}
+
+__global__ void convert_keys_kernel(const void* k16, int dtype, int n, float* out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  out[i] = dtype == FP_DTYPE_BF16 ? __bfloat162float(((const __nv_bfloat16*)k16)[i]) : ((const float*)k16)[i];
+}
+
+int launch_select(const float* scores, int64_t M, int NB, int base, float top_p, int k_min, int k_max,
+                  int capacity, float temperature, int32_t* idx, int32_t* cnt, const float* k16f,
+                  float* ctx16, float* stats, cudaStream_t st) {
+  if (M <= 0) return FP_OK;
+  const int nb_pad = pow2_at_least(NB);
+  const size_t smem = (size_t)kSelWarps * nb_pad * (sizeof(unsigned long long) + sizeof(float));
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(select_blocks_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return FP_ERR_CUDA;
+  const int blocks = (int)((M + kSelWarps - 1) / kSelWarps);
+  select_blocks_kernel<<<blocks, kSelWarps * 32, smem, st>>>(scores, M, NB, nb_pad, base, top_p, k_min,
+                                                              k_max, capacity, temperature, idx, cnt,
+                                                              k16f, ctx16, stats);
+  return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+}
+
+int launch_convert_keys(const void* k16, int dtype, int n, float* out, cudaStream_t st) {
+  convert_keys_kernel<<<(n + 255) / 256, 256, 0, st>>>(k16, dtype, n, out);
+  return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+}
+
+int launch_build_csr(const int32_t* ridx, const int32_t* rcnt, int64_t M, int base, int cap, int stride,
+                     int offset, int nbl, int chunk, int nkey, int tile_rows, int32_t* key_cnt,
+                     int32_t* key_off, int32_t* key_fill, int32_t* pair_tok, int2* tiles, int max_tiles,
+                     int32_t* meta, int* err, cudaStream_t st) {
+  if (cudaMemsetAsync(key_cnt, 0, sizeof(int32_t) * nkey, st) != cudaSuccess) return FP_ERR_CUDA;
+  const int64_t n = M * (int64_t)(base + cap);
+  const int blocks = (int)((n + 255) / 256);
+  if (n > 0)
+    csr_count_kernel<<<blocks, 256, 0, st>>>(ridx, rcnt, M, base, cap, stride, offset, nbl, chunk, key_cnt);
+  csr_scan_kernel<<<1, 1024, 0, st>>>(key_cnt, nkey, tile_rows, key_off, key_fill, tiles, max_tiles, meta, err);
+  if (n > 0)
+    csr_fill_kernel<<<blocks, 256, 0, st>>>(ridx, rcnt, M, base, cap, stride, offset, nbl, chunk, key_off,
+                                            key_fill, pair_tok);
+  return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+}
+
+int launch_colmean(const void* a, int dtype, int64_t M, int D, float* part, float* mean, cudaStream_t st) {
+  const int nchunk = (int)((M + kColRows - 1) / kColRows);
+  dim3 g((D + 255) / 256, nchunk);
+  if (dtype == FP_DTYPE_BF16)
+    colsum_partial_kernel<__nv_bfloat16><<<g, 256, 0, st>>>((const __nv_bfloat16*)a, M, D, part);
+  else
+    colsum_partial_kernel<float><<<g, 256, 0, st>>>((const float*)a, M, D, part);
+  colsum_final_kernel<<<(D + 255) / 256, 256, 0, st>>>(part, nchunk, M, D, mean);
+  return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+}
+
+int launch_pooled_topk(const float* mean_vec, const void* wq, const void* k16, int dtype, int D, int NB,
+                       int base, int remote, int mode, int32_t* active, float* mean_scores_out,
+                       cudaStream_t st) {
+  const int nb_pad = pow2_at_least(NB);
+  const size_t smem = (size_t)nb_pad * sizeof(unsigned long long);
+  if (dtype == FP_DTYPE_BF16)
+    pooled_topk_kernel<__nv_bfloat16><<<1, 512, smem, st>>>(mean_vec, (const __nv_bfloat16*)wq,
+                                                            (const __nv_bfloat16*)k16, D, NB, nb_pad, base,
+                                                            remote, mode, active, mean_scores_out);
+  else
+    pooled_topk_kernel<float><<<1, 512, smem, st>>>(mean_vec, (const float*)wq, (const float*)k16, D, NB,
+                                                    nb_pad, base, remote, mode, active, mean_scores_out);
+  return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+}
+
+}  // namespace fp

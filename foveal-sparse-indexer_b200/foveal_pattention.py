@@ -1,0 +1,275 @@
+"""``FovealPattentionMLP``: drop-in replacement of the reference module, forward on B200 kernels.
+
+Mirrors ``foveal_indexer/foveal_pattention.py`` of the reference: same constructor arguments,
+parameter names / shapes / ``state_dict`` keys (k_gate, k_up, v, q_proj_16d.weight, block_keys_16d,
+out_proj_16d.weight, offsets), ``forward(x, return_router_info)``, ``from_dense_mlp``,
+``set_active_blocks``, ``clear_cache`` and ``sparsify_model_with_foveal_pattention``.
+
+Routing modes:
+
+* ``routing="pooled"`` (default) reproduces the reference forward (foveal_pattention.py:264-352):
+  eval routes once on the pooled query and caches the active set (decode reuses it); training routes
+  on the token-mean of per-token scores and adds the 16-D additive stream.
+* ``routing="token"`` is per-token adaptive routing: ``select_blocks`` (core.py:46-160, non-causal,
+  base blocks reserved) with ``top_p`` / ``min_remote_blocks`` / ``max_remote_blocks``, the gated
+  contraction over each token's own blocks (pattention_triton.py:280-311) and the additive stream.
+
+All arithmetic runs in ``libfovealpatt.so``; CPU tensors raise (no fallback).  The forward is not
+differentiable: calling ``backward`` through it raises ``NotImplementedError``.
+"""
+
+from __future__ import annotations
+
+from typing import Any, Dict, List, Optional, Tuple
+
+import torch
+import torch.nn.functional as F
+from torch import Tensor, nn
+
+from . import kernels
+
+
+class _ForwardOnly(torch.autograd.Function):
+    """Attaches a backward that raises, so a training graph through the kernels fails loudly."""
+
+    @staticmethod
+    def forward(ctx, y, *inputs):
+        return y
+
+    @staticmethod
+    def backward(ctx, *grads):
+        raise NotImplementedError("the B200 Foveal Pattention forward has no backward kernels yet")
+
+
+class FovealPattentionMLP(nn.Module):
+    """Foveal block-sparse SwiGLU token-parameter attention (Pattention) layer."""
+
+    def __init__(
+        self,
+        hidden_dim: int = 2048,
+        intermediate_dim: int = 6144,
+        block_size: int = 64,
+        base_blocks: int = 4,
+        remote_blocks: int = 20,
+        index_dim: int = 16,
+        temperature: float = 1.0,
+        dtype: torch.dtype = torch.bfloat16,
+        use_fused_kernel: bool = True,
+        *,
+        routing: str = "pooled",
+        top_p: float = 0.9,
+        min_remote_blocks: int = 0,
+        max_remote_blocks: Optional[int] = None,
+        device=None,
+    ):
+        super().__init__()
+        if block_size != 64:
+            raise ValueError("the kernels use 64-token parameter blocks (block_size=64)")
+        if index_dim != 16:
+            raise ValueError("the router is specialised for index_dim=16")
+        if intermediate_dim % block_size:
+            raise ValueError("intermediate_dim must be a multiple of block_size")
+        if routing not in ("pooled", "token"):
+            raise ValueError("routing must be 'pooled' or 'token'")
+        self.hidden_dim = hidden_dim
+        self.intermediate_dim = intermediate_dim
+        self.block_size = block_size
+        self.num_blocks = intermediate_dim // block_size
+        self.base_blocks = base_blocks
+        self.remote_blocks = remote_blocks
+        self.total_active_blocks = base_blocks + remote_blocks
+        self.active_channels = self.total_active_blocks * block_size
+        self.index_dim = index_dim
+        self.temperature = temperature
+        self.dtype = dtype
+        self.use_fused_kernel = use_fused_kernel
+        self.routing = routing
+        self.top_p = top_p
+        self.min_remote_blocks = min_remote_blocks
+        self.max_remote_blocks = remote_blocks if max_remote_blocks is None else max_remote_blocks
+
+        fk = dict(dtype=dtype, device=device)
+        self.k_gate = nn.Parameter(torch.empty(intermediate_dim, hidden_dim, **fk))
+        self.k_up = nn.Parameter(torch.empty(intermediate_dim, hidden_dim, **fk))
+        self.v = nn.Parameter(torch.empty(intermediate_dim, hidden_dim, **fk))
+        self.q_proj_16d = nn.Linear(hidden_dim, index_dim, bias=False, **fk)
+        self.block_keys_16d = nn.Parameter(torch.empty(self.num_blocks, index_dim, **fk))
+        self.out_proj_16d = nn.Linear(index_dim, hidden_dim, bias=False, **fk)
+        self.register_buffer("offsets", torch.arange(block_size, dtype=torch.int64, device=device))
+
+        # Eval-mode routing cache (foveal_pattention.py:100-104).  The kernels read the active blocks in
+        # place, so the cache holds the active block ids only; the gathered-weight attributes of the
+        # reference are kept for compatibility and stay None.
+        self._cached_kg = None
+        self._cached_ku = None
+        self._cached_v = None
+        self._cached_active_blocks: Optional[Tensor] = None
+        self._vt = None
+        self._vt_key = None
+        self._shard = None  # (rank, world, group) when parameter blocks are sharded
+        self.reset_parameters()
+
+    # ------------------------------------------------------------------ reference API
+    def clear_cache(self) -> None:
+        """Clears the cached active set (foveal_pattention.py:108-113)."""
+        self._cached_kg = self._cached_ku = self._cached_v = None
+        self._cached_active_blocks = None
+
+    def set_active_blocks(self, active_blocks: Tensor) -> None:
+        """Fixes the active block set used by eval/decode calls (foveal_pattention.py:115-122)."""
+        self._cached_active_blocks = active_blocks.to(device=self.k_gate.device, dtype=torch.int32).contiguous()
+
+    def reset_parameters(self) -> None:
+        """Reference initialisation (foveal_pattention.py:124-131)."""
+        std = self.hidden_dim ** -0.5
+        nn.init.normal_(self.k_gate, std=std)
+        nn.init.normal_(self.k_up, std=std)
+        nn.init.normal_(self.v, std=std)
+        nn.init.normal_(self.q_proj_16d.weight, std=std)
+        nn.init.normal_(self.block_keys_16d, std=self.index_dim ** -0.5)
+        nn.init.normal_(self.out_proj_16d.weight, std=1e-3)
+
+    @classmethod
+    def from_dense_mlp(cls, dense_mlp: nn.Module, block_size: int = 64, base_blocks: int = 4,
+                       remote_blocks: int = 20, index_dim: int = 16, temperature: float = 1.0,
+                       use_fused_kernel: bool = True, **kwargs) -> "FovealPattentionMLP":
+        """Exact reparameterisation of a dense SwiGLU MLP (foveal_pattention.py:133-173):
+        K_gate = W_gate, K_up = W_up, V = W_down^T, additive stream initialised to zero."""
+        hidden_dim = dense_mlp.gate_proj.in_features
+        intermediate_dim = dense_mlp.gate_proj.out_features
+        dtype = dense_mlp.gate_proj.weight.dtype
+        device = dense_mlp.gate_proj.weight.device
+        m = cls(hidden_dim=hidden_dim, intermediate_dim=intermediate_dim, block_size=block_size,
+                base_blocks=base_blocks, remote_blocks=remote_blocks, index_dim=index_dim,
+                temperature=temperature, dtype=dtype, use_fused_kernel=use_fused_kernel, **kwargs).to(device)
+        with torch.no_grad():
+            m.k_gate = nn.Parameter(dense_mlp.gate_proj.weight.data)
+            m.k_up = nn.Parameter(dense_mlp.up_proj.weight.data)
+            m.v = nn.Parameter(dense_mlp.down_proj.weight.data.t().contiguous())
+            nn.init.zeros_(m.out_proj_16d.weight)
+        return m
+
+    def calibrate_offline_svd(self, features: Tensor, ridge_lambda: float = 1e-2) -> Dict[str, float]:
+        raise NotImplementedError("offline SVD router calibration (foveal_pattention.py:175-255) is not "
+                                  "part of the forward library yet")
+
+    def compute_router_scores(self, x: Tensor) -> Tensor:
+        """Per-token 16-D router scores (foveal_pattention.py:257-262), computed in fp32."""
+        shape = x.shape
+        x2d = x.reshape(-1, shape[-1]).to(self.k_gate.dtype)
+        s, _ = kernels.router_scores(x2d, self.q_proj_16d.weight.detach(), self.block_keys_16d.detach())
+        return s.reshape(*shape[:-1], self.num_blocks)
+
+    # ------------------------------------------------------------------ helpers
+    def _packed_v(self) -> Optional[Tensor]:
+        """V^T for the tensor-core path, rebuilt whenever ``v`` is replaced or modified in place."""
+        if self.v.dtype != torch.bfloat16 or self.hidden_dim % 64:
+            return None
+        key = (self.v.data_ptr(), self.v._version, self.v.device)
+        if self._vt is None or self._vt_key != key:
+            self._vt = kernels.pack_v(self.v.detach())
+            self._vt_key = key
+        return self._vt
+
+    def _weights(self):
+        return (self.k_gate.detach(), self.k_up.detach(), self.v.detach(), self._packed_v(),
+                self.q_proj_16d.weight.detach(), self.block_keys_16d.detach(), self.out_proj_16d.weight.detach())
+
+    def _attach_no_grad(self, y: Tensor, x: Tensor) -> Tensor:
+        if torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in self.parameters())):
+            params = [p for p in self.parameters() if p.requires_grad]
+            return _ForwardOnly.apply(y, x, *params)
+        return y
+
+    # ------------------------------------------------------------------ forward
+    def forward(self, x: Tensor, return_router_info: bool = False) -> Tensor | Tuple[Tensor, Dict[str, Any]]:
+        orig_shape = x.shape
+        D = orig_shape[-1]
+        x_in = x
+        x2d = x.reshape(-1, D)
+        if x2d.dtype != self.k_gate.dtype:
+            x2d = x2d.to(self.k_gate.dtype)
+        x2d = x2d.detach()
+        if self.routing == "token":
+            y, info = self._forward_token(x2d, return_router_info)
+        else:
+            y, info = self._forward_pooled(x2d, orig_shape, return_router_info)
+        y = self._attach_no_grad(y.reshape(*orig_shape[:-1], y.shape[-1]), x_in)
+        if return_router_info:
+            return y, info
+        return y
+
+    def _forward_pooled(self, x2d: Tensor, orig_shape, return_router_info: bool):
+        kg, ku, v, vt, wq, k16, wout = self._weights()
+        is_prefill = (len(orig_shape) >= 3 and orig_shape[-2] > 1) or (
+            len(orig_shape) == 2 and orig_shape[0] > 1 and self.training)
+        if not self.training and self._cached_active_blocks is not None and not is_prefill:
+            y = kernels.pooled_forward(x2d, kg, ku, v, vt, self._cached_active_blocks)
+            return y, {"active_blocks": self._cached_active_blocks}
+        scores = None
+        ctx = None
+        if self.training:
+            scores, _ = kernels.router_scores(x2d, wq, k16)
+            active, _ = kernels.pooled_route(None, wq, k16, base_blocks=self.base_blocks,
+                                             remote_blocks=self.remote_blocks, mode=1, token_scores=scores,
+                                             dtype=x2d.dtype, D=x2d.shape[1])
+            _, _, ctx, _ = kernels.select(scores, base_blocks=self.base_blocks, top_p=1.0, min_remote=0,
+                                          max_remote=0, capacity=0, temperature=self.temperature,
+                                          block_keys=k16, want_routes=False)
+        else:
+            if self._cached_active_blocks is None:
+                active, _ = kernels.pooled_route(x2d, wq, k16, base_blocks=self.base_blocks,
+                                                 remote_blocks=self.remote_blocks, mode=0)
+                self.set_active_blocks(active)
+            active = self._cached_active_blocks
+        y = kernels.pooled_forward(x2d, kg, ku, v, vt, active, ctx16=ctx, out_proj=wout if ctx is not None else None)
+        info = {}
+        if return_router_info:
+            if scores is None:
+                scores, _ = kernels.router_scores(x2d, wq, k16)
+            info = {"scores": scores, "active_blocks": active,
+                    "sparsity": (1.0 - self.total_active_blocks / self.num_blocks) * 100.0}
+        return y, info
+
+    def _forward_token(self, x2d: Tensor, return_router_info: bool):
+        kg, ku, v, vt, wq, k16, wout = self._weights()
+        if self._shard is not None:
+            from .sharding import sharded_token_forward
+            y, ridx, cnt, S = sharded_token_forward(self, x2d, want_routes=return_router_info)
+        else:
+            y, ridx, cnt, S = kernels.token_forward(
+                x2d, kg, ku, v, vt, wq, k16, wout, base_blocks=self.base_blocks, top_p=self.top_p,
+                min_remote=self.min_remote_blocks, max_remote=self.max_remote_blocks,
+                temperature=self.temperature, additive=True, want_routes=return_router_info)
+        info = {}
+        if return_router_info:
+            info = {"scores": S, "remote_indices": ridx, "remote_counts": cnt,
+                    "active_blocks": None,
+                    "sparsity": (1.0 - (self.base_blocks + cnt.float().mean()) / self.num_blocks) * 100.0}
+        return y, info
+
+
+def sparsify_model_with_foveal_pattention(
+    model: nn.Module,
+    layers_to_sparsify: Optional[List[int]] = None,
+    block_size: int = 64,
+    base_blocks: int = 4,
+    remote_blocks: int = 20,
+    index_dim: int = 16,
+    temperature: float = 1.0,
+    use_fused_kernel: bool = True,
+    **kwargs,
+) -> nn.Module:
+    """Replaces the MLPs of a causal LM's decoder layers (foveal_pattention.py:355-387)."""
+    layers = getattr(model, "model", model).layers
+    targets = layers_to_sparsify if layers_to_sparsify is not None else list(range(len(layers)))
+    for idx in targets:
+        if hasattr(layers[idx], "mlp"):
+            dense_mlp = layers[idx].mlp
+            layers[idx].mlp = FovealPattentionMLP.from_dense_mlp(
+                dense_mlp, block_size=block_size, base_blocks=base_blocks, remote_blocks=remote_blocks,
+                index_dim=index_dim, temperature=temperature, use_fused_kernel=use_fused_kernel, **kwargs)
+            del dense_mlp
+    if torch.cuda.is_available():
+        torch.cuda.empty_cache()
+    return model

@@ -1,0 +1,156 @@
+"""Functional wrappers of the C-ABI entry points (one call = one ``fp_*`` entry point).
+
+These are the operator layer the module classes are built on.  Each function validates its tensors
+(CUDA, dtype, contiguity), allocates its outputs with torch, passes the current stream and raises
+``FovealKernelError`` on a non-zero status.
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+from ._lib import check, contig, dtype_code, ptr, require_cuda, stream_handle
+
+
+def router_scores(x2d: torch.Tensor, q_proj: torch.Tensor, block_keys: torch.Tensor,
+                  want_q16: bool = False) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """``rms_norm(x W_q^T) K_16^T / 4`` per token (foveal_pattention.py:257-262); fp32 [M, NB]."""
+    dev = require_cuda(x2d, q_proj, block_keys)
+    dt = dtype_code(x2d.dtype)
+    x2d, q_proj, block_keys = contig(x2d), contig(q_proj.to(x2d.dtype)), contig(block_keys.to(x2d.dtype))
+    M, D = x2d.shape
+    NB = block_keys.shape[0]
+    scores = torch.empty(M, NB, dtype=torch.float32, device=dev)
+    q16 = torch.empty(M, 16, dtype=torch.float32, device=dev) if want_q16 else None
+    rc = _lib.load().fp_router_scores(ptr(x2d), ptr(q_proj), ptr(block_keys), dt, M, D, NB, ptr(scores),
+                                      ptr(q16), stream_handle(dev))
+    check(rc, "fp_router_scores")
+    return scores, q16
+
+
+def select(scores: torch.Tensor, *, base_blocks: int, top_p: float, min_remote: int, max_remote: int,
+           capacity: int, temperature: float = 1.0, block_keys: Optional[torch.Tensor] = None,
+           want_stats: bool = False, want_routes: bool = True):
+    """Top-p block selection (core.py:46-160, non-causal) and optionally the additive-stream context.
+
+    Returns (remote_indices [M, capacity] int32, remote_counts [M] int32, ctx16 [M, 16] fp32 or None,
+    stats [3] fp32 or None)."""
+    dev = require_cuda(scores)
+    scores = contig(scores.float())
+    M, NB = scores.shape
+    idx = cnt = None
+    if want_routes:
+        idx = torch.empty(M, capacity, dtype=torch.int32, device=dev)
+        cnt = torch.empty(M, dtype=torch.int32, device=dev)
+    k16f = ctx = None
+    if block_keys is not None:
+        k16f = contig(block_keys.detach().float())
+        ctx = torch.empty(M, 16, dtype=torch.float32, device=dev)
+    stats = torch.zeros(3, dtype=torch.float32, device=dev) if want_stats else None
+    rc = _lib.load().fp_select_blocks(ptr(scores), M, NB, int(base_blocks), float(top_p), int(min_remote),
+                                      int(max_remote), int(capacity) if want_routes else 0, float(temperature),
+                                      ptr(idx), ptr(cnt), ptr(k16f), ptr(ctx), ptr(stats), stream_handle(dev))
+    check(rc, "fp_select_blocks")
+    return idx, cnt, ctx, stats
+
+
+def pooled_route(x2d: Optional[torch.Tensor], q_proj: torch.Tensor, block_keys: torch.Tensor, *,
+                 base_blocks: int, remote_blocks: int, mode: int,
+                 token_scores: Optional[torch.Tensor] = None, dtype: Optional[torch.dtype] = None,
+                 M: Optional[int] = None, D: Optional[int] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Pooled routing (foveal_pattention.py:292-303 train / :310-321 eval): (active int32, pooled scores)."""
+    dev = require_cuda(q_proj, block_keys, x2d, token_scores)
+    dt_t = dtype or (x2d.dtype if x2d is not None else q_proj.dtype)
+    dt = dtype_code(dt_t)
+    q_proj, block_keys = contig(q_proj.to(dt_t)), contig(block_keys.to(dt_t))
+    NB = block_keys.shape[0]
+    if x2d is not None:
+        x2d = contig(x2d)
+        M, D = x2d.shape
+    if token_scores is not None:
+        token_scores = contig(token_scores.float())
+        M = token_scores.shape[0]
+    D = D if D is not None else q_proj.shape[1]
+    active = torch.empty(base_blocks + remote_blocks, dtype=torch.int32, device=dev)
+    mean_scores = torch.empty(NB, dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    nbytes = lib.fp_pooled_workspace_size(dt, M, D, NB, 0)
+    ws = _lib.workspace(dev, nbytes)
+    rc = lib.fp_pooled_route(ptr(x2d), ptr(q_proj), ptr(block_keys), dt, M, D, NB, int(base_blocks),
+                             int(remote_blocks), int(mode), ptr(token_scores), ptr(active), ptr(mean_scores),
+                             ptr(ws), ws.numel(), stream_handle(dev))
+    check(rc, "fp_pooled_route")
+    return active, mean_scores
+
+
+def pack_v(v: torch.Tensor) -> torch.Tensor:
+    """V^T [D, Np] for the tensor-core path (derived layout of FovealPattentionMLP.v)."""
+    dev = require_cuda(v)
+    v = contig(v.detach())
+    Np, D = v.shape
+    vt = torch.empty(D, Np, dtype=v.dtype, device=dev)
+    rc = _lib.load().fp_pack_v(ptr(v), dtype_code(v.dtype), Np, D, ptr(vt), stream_handle(dev))
+    check(rc, "fp_pack_v")
+    return vt
+
+
+def token_forward(x2d, k_gate, k_up, v, v_t, q_proj, block_keys, out_proj, *, base_blocks: int,
+                  top_p: float, min_remote: int, max_remote: int, temperature: float = 1.0,
+                  additive: bool = True, block_stride: int = 1, block_offset: int = 0,
+                  out_f32: bool = False, want_routes: bool = False, y: Optional[torch.Tensor] = None):
+    """Per-token routed forward, one ``fp_pattention_token_fwd`` call.
+
+    Returns (y [M, D], remote_indices or None, remote_counts or None, scores or None)."""
+    dev = require_cuda(x2d, k_gate, k_up, v, q_proj, block_keys)
+    dtt = x2d.dtype
+    dt = dtype_code(dtt)
+    x2d = contig(x2d)
+    M, D = x2d.shape
+    NB = block_keys.shape[0]
+    k_gate, k_up, v = contig(k_gate.detach()), contig(k_up.detach()), contig(v.detach())
+    q_proj, block_keys = contig(q_proj.detach().to(dtt)), contig(block_keys.detach().to(dtt))
+    out_proj = contig(out_proj.detach().to(dtt)) if out_proj is not None else None
+    if y is None:
+        y = torch.empty(M, D, dtype=torch.float32 if out_f32 else dtt, device=dev)
+    cap = max(int(max_remote), 1)
+    ridx = cnt = S = None
+    if want_routes:
+        ridx = torch.empty(M, cap, dtype=torch.int32, device=dev)
+        cnt = torch.empty(M, dtype=torch.int32, device=dev)
+        S = torch.empty(M, NB, dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    nbytes = lib.fp_token_workspace_size(dt, M, D, NB, int(base_blocks), int(max_remote), int(block_stride))
+    ws = _lib.workspace(dev, nbytes)
+    rc = lib.fp_pattention_token_fwd(
+        ptr(x2d), M, D, NB, dt, ptr(k_gate), ptr(k_up), ptr(v), ptr(v_t), ptr(q_proj), ptr(block_keys),
+        ptr(out_proj), int(base_blocks), float(top_p), int(min_remote), int(max_remote), float(temperature),
+        1 if additive else 0, int(block_stride), int(block_offset), ptr(y), 1 if out_f32 else 0, ptr(ridx),
+        ptr(cnt), ptr(S), ptr(ws), ws.numel(), stream_handle(dev))
+    check(rc, "fp_pattention_token_fwd")
+    return y, ridx, cnt, S
+
+
+def pooled_forward(x2d, k_gate, k_up, v, v_t, active, *, ctx16=None, out_proj=None, out_f32: bool = False):
+    """Forward over one shared active set (``fp_pattention_pooled_fwd``); y [M, D]."""
+    dev = require_cuda(x2d, k_gate, k_up, v, active)
+    dtt = x2d.dtype
+    dt = dtype_code(dtt)
+    x2d = contig(x2d)
+    M, D = x2d.shape
+    NB = k_gate.shape[0] // 64
+    k_gate, k_up, v = contig(k_gate.detach()), contig(k_up.detach()), contig(v.detach())
+    active = contig(active.to(torch.int32))
+    out_proj = contig(out_proj.detach().to(dtt)) if out_proj is not None else None
+    y = torch.empty(M, D, dtype=torch.float32 if out_f32 else dtt, device=dev)
+    lib = _lib.load()
+    n_active = active.numel()
+    nbytes = lib.fp_pooled_workspace_size(dt, M, D, NB, n_active)
+    ws = _lib.workspace(dev, nbytes)
+    rc = lib.fp_pattention_pooled_fwd(ptr(x2d), M, D, NB, dt, ptr(k_gate), ptr(k_up), ptr(v), ptr(v_t),
+                                      ptr(active), n_active, ptr(ctx16), ptr(out_proj), ptr(y),
+                                      1 if out_f32 else 0, ptr(ws), ws.numel(), stream_handle(dev))
+    check(rc, "fp_pattention_pooled_fwd")
+    return y

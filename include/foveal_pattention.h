@@ -1,0 +1,164 @@
+/*
+ * foveal_pattention.h — C ABI of libfovealpatt.so, the B200 (sm_100a) implementation of the Foveal
+ * Pattention MLP forward: 16-D router, top-p block selection and the gated block-sparse SwiGLU
+ * contraction with the 16-D additive stream.
+ *
+ * The reference (kreasof-ai/foveal-sparse-indexer) has no native interface: its hot path is the
+ * Python module FovealPattentionMLP and the functions it calls.  Each entry point below names the
+ * reference function it replaces (paths relative to that project).
+ *
+ * Conventions (all entry points):
+ *   - All tensor pointers are DEVICE pointers, row-major and contiguous, 16-byte aligned.
+ *   - dtype: FP_DTYPE_F32 or FP_DTYPE_BF16 for x and all weights of one call.
+ *   - The caller allocates every output and the workspace (size from the *_workspace_size queries).
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Work is only enqueued: no entry
+ *     point synchronizes the host except fp_device_error.
+ *   - Return value: FP_OK (0) or an fp_status code.  No exception crosses the ABI.
+ *   - Thread-safe as long as concurrent calls use different workspaces.
+ *   - Kernels never wait unboundedly: a wait that runs out records a code that fp_device_error
+ *     returns as FP_ERR_TIMEOUT.
+ */
+#ifndef FOVEAL_PATTENTION_H_
+#define FOVEAL_PATTENTION_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FP_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define FP_API __attribute__((visibility("default")))
+#else
+#define FP_API
+#endif
+
+typedef enum fp_status {
+  FP_OK = 0,
+  FP_ERR_INVALID_ARG = 1,  /* null pointer, bad shape or parameter, misaligned pointer */
+  FP_ERR_UNSUPPORTED = 2,  /* dtype / shape combination not implemented */
+  FP_ERR_WORKSPACE = 3,    /* workspace too small */
+  FP_ERR_CUDA = 4,         /* a CUDA runtime call or kernel launch failed */
+  FP_ERR_DEVICE = 5,       /* current device is not an sm_100 GPU */
+  FP_ERR_TIMEOUT = 6       /* a kernel's bounded wait ran out (reported by fp_device_error) */
+} fp_status;
+
+typedef enum fp_dtype { FP_DTYPE_F32 = 0, FP_DTYPE_BF16 = 1 } fp_dtype;
+
+/* ABI version (FP_ABI_VERSION of the built library). */
+FP_API int fp_abi_version(void);
+
+/* Static description of a status code. */
+FP_API const char* fp_status_string(int status);
+
+/*
+ * Router scores.  Replaces FovealPattentionMLP.compute_router_scores
+ * (foveal_indexer/foveal_pattention.py:257-262):
+ *   scores[m, b] = (rms_norm(x[m] . q_proj^T) . block_keys[b]) / sqrt(16)        (fp32 out)
+ * x [M, D], q_proj [16, D], block_keys [NB, 16] in `dtype`; q16 (optional) [M, 16] fp32 receives the
+ * normalised 16-D queries (FovealIndexer.compute_query_16d, foveal_indexer/core.py:214-223).
+ * D must be a multiple of 8; NB <= 1024.
+ */
+FP_API int fp_router_scores(const void* x, const void* q_proj, const void* block_keys, int dtype, int64_t M,
+                     int D, int NB, float* scores, float* q16, void* stream);
+
+/*
+ * Adaptive top-p block selection, non-causal, with `base_blocks` always-on leading blocks.  Replaces
+ * select_blocks(block_scores, causal=False, local_window_blocks=base_blocks, top_p, min_remote_blocks,
+ * max_remote_blocks, remote_capacity) (foveal_indexer/core.py:46-160, branch :90-99) and, when ctx16
+ * is given, the additive-stream context softmax(S / T) . K_16 (foveal_pattention.py:339-340).
+ *   scores         [M, NB] fp32 pre-softmax scores S (divided by `temperature` before the softmax)
+ *   remote_indices [M, capacity] int32: block ids by descending probability, ties to the lower id
+ *   remote_counts  [M] int32: number of selected remote blocks
+ *   block_keys_f32 [NB, 16] fp32 and ctx16 [M, 16] fp32: both NULL or both set
+ *   stats          optional float[3] accumulated in place: sum of (count >= K_max), sum of counts,
+ *                  sum of (count == 0); divide by M for cap_rate, mean_remote_blocks, base_only_rate
+ */
+FP_API int fp_select_blocks(const float* scores, int64_t M, int NB, int base_blocks, float top_p, int min_remote,
+                     int max_remote, int capacity, float temperature, int32_t* remote_indices,
+                     int32_t* remote_counts, const float* block_keys_f32, float* ctx16, float* stats,
+                     void* stream);
+
+/*
+ * Pooled routing: one active set for the whole call (foveal_pattention.py:292-303 training,
+ * :310-321 eval).  active[0..base) = 0..base-1, then `remote_blocks` ids by descending pooled score.
+ *   mode 0 (eval):  pooled query rms_norm(q_proj . mean_t(x)), scores = q . K_16^T (no 1/sqrt(16))
+ *   mode 1 (train): token-mean of `token_scores` [M, NB] (fp32, from fp_router_scores)
+ * mean_scores (optional) [NB] fp32 receives the pooled scores.  Workspace: fp_pooled_workspace_size.
+ */
+FP_API int fp_pooled_route(const void* x, const void* q_proj, const void* block_keys, int dtype, int64_t M, int D,
+                    int NB, int base_blocks, int remote_blocks, int mode, const float* token_scores,
+                    int32_t* active, float* mean_scores, void* workspace, size_t workspace_bytes,
+                    void* stream);
+
+/*
+ * V layout for the tensor-core path: v_t[D, Np] = v[Np, D]^T (FovealPattentionMLP.v, which stores
+ * W_down^T, foveal_pattention.py:88 and :169).  Call once per weight update; bf16 only.
+ */
+FP_API int fp_pack_v(const void* v, int dtype, int Np, int D, void* v_t, void* stream);
+
+/* Workspace bytes of fp_pattention_token_fwd (block_stride = 1 unless blocks are sharded). */
+FP_API size_t fp_token_workspace_size(int dtype, int64_t M, int D, int NB, int base_blocks, int max_remote,
+                               int block_stride);
+
+/* Workspace bytes of fp_pattention_pooled_fwd and fp_pooled_route. */
+FP_API size_t fp_pooled_workspace_size(int dtype, int64_t M, int D, int NB, int n_active);
+
+/*
+ * Per-token routed forward (router + selection + gated contraction + additive stream), the
+ * composition compute_router_scores -> select_blocks(non-causal, base) -> per-token Pattention over
+ * base ∪ selected (pattention_triton.py:280-311, "swiglu", block_n = 64) -> + out_proj_16d(softmax(S/T) K_16)
+ * (foveal_pattention.py:257-262, core.py:46-160, foveal_pattention.py:338-342).
+ *   x [M, D]; k_gate, k_up, v [Np, D] (Np = NB * 64); v_t [D, Np] from fp_pack_v (bf16 path, may be
+ *   NULL for fp32); q_proj [16, D]; block_keys [NB, 16]; out_proj [D, 16]; all in `dtype`.
+ *   additive: 1 adds the additive stream.
+ *   block_stride / block_offset: this call computes only blocks b with b % block_stride == block_offset
+ *   (parameter-block sharding across GPUs; 1 / 0 = all blocks).  Routing still covers all blocks.
+ *   y [M, D]: `dtype`, or fp32 when y_f32 = 1 (partial sums of a block shard).
+ *   remote_indices [M, max_remote] int32, remote_counts [M] int32, scores [M, NB] fp32: optional
+ *   outputs (NULL = keep inside the workspace).
+ */
+FP_API int fp_pattention_token_fwd(const void* x, int64_t M, int D, int NB, int dtype, const void* k_gate,
+                            const void* k_up, const void* v, const void* v_t, const void* q_proj,
+                            const void* block_keys, const void* out_proj, int base_blocks, float top_p,
+                            int min_remote, int max_remote, float temperature, int additive,
+                            int block_stride, int block_offset, void* y, int y_f32,
+                            int32_t* remote_indices, int32_t* remote_counts, float* scores,
+                            void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Pooled forward over one shared active set.  Replaces the active-block execution of
+ * FovealPattentionMLP.forward (foveal_pattention.py:115-122 gather, :329-335 SwiGLU) and the
+ * training-mode additive stream (:338-342) when ctx16 is given.
+ *   active [n_active] int32 device ids; ctx16 [M, 16] fp32 (softmax(S/T) K_16, from fp_select_blocks
+ *   with capacity 0) or NULL; other tensors as in fp_pattention_token_fwd.
+ */
+FP_API int fp_pattention_pooled_fwd(const void* x, int64_t M, int D, int NB, int dtype, const void* k_gate,
+                             const void* k_up, const void* v, const void* v_t, const int32_t* active,
+                             int n_active, const float* ctx16, const void* out_proj, void* y, int y_f32,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Measurement hook (no counterpart in the reference): for the calling host thread, the forward entry
+ * points record events[i] (cudaEvent_t handles) on their stream at stage boundaries:
+ *   fp_pattention_token_fwd:  0 start, 1 routed (scores + selection), 2 block CSR built and H cleared,
+ *                             3 gate/up kernel done, 4 down kernel done
+ *   fp_pattention_pooled_fwd: 0 start, 1 gate/up kernel done, 2 down kernel done
+ * Boundaries past n_events are not recorded.  events = NULL or n_events = 0 turns the hook off.
+ */
+FP_API int fp_set_stage_events(void* const* events, int n_events);
+
+/*
+ * Reads (and clears) the device error word of a workspace after synchronizing `stream`.  Returns
+ * FP_OK, FP_ERR_TIMEOUT (a bounded wait ran out) or FP_ERR_CUDA; *code receives the raw device code.
+ */
+FP_API int fp_device_error(void* workspace, void* stream, int* code);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FOVEAL_PATTENTION_H_ */

@@ -1,0 +1,294 @@
+"""CPU restatement of the reference's Foveal Pattention MLP forward (test infrastructure only).
+
+Every function cites the reference file:line it restates.  All arithmetic is fp32 PyTorch on the CPU,
+with the same operator sequence as the reference, so that on the same inputs the results match the
+reference bit for bit where the reference is deterministic.  Two deliberate differences:
+
+* ``select_blocks`` sorts with ``stable=True``.  The reference calls ``Tensor.sort`` with the default
+  ``stable=False`` (core.py:107); a stable descending sort breaks probability ties toward the lower
+  block id, which is the documented tie rule of the CUDA router.
+* ``token_pattention`` accumulates the per-token output block by block (grouping tokens that share a
+  block) instead of one gathered matmul per token (pattention_triton.py:280-311).  The sum is the same
+  and only the fp32 summation order differs (relative differences ~1e-7).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Dict, Optional, Tuple
+
+import torch
+import torch.nn.functional as F
+
+__all__ = [
+    "masked_softmax",
+    "select_blocks_noncausal",
+    "OracleRoute",
+    "router_scores",
+    "additive_stream",
+    "token_pattention",
+    "token_pattention_per_token",
+    "token_forward",
+    "pooled_eval_active",
+    "pooled_train_active",
+    "pooled_pattention",
+    "pooled_forward",
+    "boundary_margins",
+    "dense_swiglu",
+]
+
+
+def masked_softmax(scores: torch.Tensor, mask: torch.Tensor) -> torch.Tensor:
+    """core.py:36-43 — fp32 softmax that zeroes masked entries; denominator clamped at 1e-20."""
+    safe = scores.float().masked_fill(~mask, -float("inf"))
+    row_max = safe.amax(dim=-1, keepdim=True)
+    row_max = torch.where(torch.isfinite(row_max), row_max, torch.zeros_like(row_max))
+    numer = torch.exp(safe - row_max) * mask
+    denom = numer.sum(dim=-1, keepdim=True).clamp_min(1e-20)
+    return (numer / denom).to(scores.dtype)
+
+
+@dataclass
+class OracleRoute:
+    """Fields of the reference ``Route`` (core.py:23-33) for the non-causal branch."""
+
+    remote_indices: torch.Tensor   # [B, Q, capacity] int32, sorted by descending probability
+    remote_counts: torch.Tensor    # [B, Q] int32
+    base_indices: Optional[torch.Tensor]
+    base_counts: Optional[torch.Tensor]
+    block_scores: torch.Tensor
+    cap_rate: torch.Tensor
+    mean_remote_blocks: torch.Tensor
+    base_only_rate: torch.Tensor
+    remote_probs_sorted: torch.Tensor  # [B, Q, NB] fp32, the sorted probabilities (for margins)
+
+
+def select_blocks_noncausal(
+    block_scores: torch.Tensor,
+    *,
+    local_window_blocks: int = 0,
+    top_p: float = 0.95,
+    min_remote_blocks: int = 0,
+    max_remote_blocks: int = 16,
+    remote_capacity: int = 16,
+    stable: bool = True,
+) -> OracleRoute:
+    """core.py:46-160, non-causal branch (core.py:90-99), with base blocks [0, local_window_blocks).
+
+    Steps (reference line numbers): softmax over all blocks (:101-102), base ("local") mass (:104),
+    remote probabilities with base entries set to -1 (:105), descending sort (:107), clamp and
+    fp32 cumulative sum (:108-109; torch's CPU cumsum accumulates in fp64 and rounds each prefix to
+    fp32), ``needed = #(cum < target) + (target > 0)`` (:111-115), clamp to [K_min, min(avail, K_max)]
+    (:116-119), first ``capacity`` sorted ids (:121-123), base ids (:137-140) and statistics
+    (:145-159).
+    """
+    batch, query_blocks, total_blocks = block_scores.shape
+    device = block_scores.device
+    top_p_t = torch.as_tensor(top_p, device=device, dtype=torch.float32)
+    min_remote_t = torch.as_tensor(min_remote_blocks, device=device, dtype=torch.int64)
+    max_remote_t = torch.as_tensor(max_remote_blocks, device=device, dtype=torch.int64)
+    pb = torch.arange(total_blocks, device=device)
+
+    complete = torch.ones((query_blocks, total_blocks), dtype=torch.bool, device=device)
+    if local_window_blocks > 0:
+        local_complete = (pb.view(1, total_blocks) < local_window_blocks).expand(query_blocks, -1)
+        remote = (pb.view(1, total_blocks) >= local_window_blocks).expand(query_blocks, -1)
+    else:
+        local_complete = torch.zeros_like(complete)
+        remote = complete
+
+    probs = masked_softmax(block_scores, complete[None].expand(batch, -1, -1))
+    local_mass = (probs * local_complete[None]).sum(dim=-1)
+    remote_probs = probs.masked_fill(~remote[None], -1.0)
+    sorted_prob, sorted_idx = remote_probs.sort(dim=-1, descending=True, stable=stable)
+    sorted_prob = sorted_prob.clamp_min(0.0)
+    cumulative = sorted_prob.cumsum(dim=-1)
+
+    target = (top_p_t - local_mass).clamp_min(0.0)
+    available = remote.sum(dim=-1).view(1, query_blocks).expand(batch, -1)
+    needed = (cumulative < target[..., None]).sum(dim=-1) + (target > 0).long()
+    needed = torch.where(available > 0, needed, torch.zeros_like(needed))
+    needed = torch.where(available > 0, torch.maximum(needed, min_remote_t), needed)
+    counts = torch.minimum(needed, available)
+    counts = torch.minimum(counts, max_remote_t)
+
+    indices = sorted_idx[..., :remote_capacity].to(torch.int32)
+    if indices.shape[-1] < remote_capacity:
+        indices = F.pad(indices, (0, remote_capacity - indices.shape[-1]))
+
+    if local_window_blocks > 0:
+        base_indices = torch.arange(local_window_blocks, device=device, dtype=torch.int32)
+        base_indices = base_indices[None, None, :].expand(batch, query_blocks, -1)
+        base_counts = torch.full((batch, query_blocks), local_window_blocks, device=device,
+                                 dtype=torch.int32)
+    else:
+        base_indices = None
+        base_counts = None
+
+    cap_rate = torch.where(
+        max_remote_t > 0,
+        (counts >= max_remote_t).float().mean(),
+        counts.new_zeros((), dtype=torch.float32),
+    )
+    return OracleRoute(
+        remote_indices=indices,
+        remote_counts=counts.to(torch.int32),
+        base_indices=base_indices,
+        base_counts=base_counts,
+        block_scores=block_scores,
+        cap_rate=cap_rate,
+        mean_remote_blocks=counts.float().mean(),
+        base_only_rate=(counts == 0).float().mean(),
+        remote_probs_sorted=sorted_prob,
+    )
+
+
+def router_scores(x2d: torch.Tensor, q_proj_16d: torch.Tensor, block_keys_16d: torch.Tensor) -> torch.Tensor:
+    """foveal_pattention.py:257-262 — ``rms_norm(x W_q^T) K_16^T / sqrt(16)`` (block keys not normalised)."""
+    index_dim = q_proj_16d.shape[0]
+    q_16 = F.rms_norm(F.linear(x2d, q_proj_16d), (index_dim,))
+    return torch.matmul(q_16, block_keys_16d.t()) / math.sqrt(index_dim)
+
+
+def additive_stream(scores_over_t: torch.Tensor, block_keys_16d: torch.Tensor,
+                    out_proj_16d: torch.Tensor) -> torch.Tensor:
+    """foveal_pattention.py:338-342 — ``out_proj_16d(softmax(S / T) K_16)``; the argument is S / T."""
+    soft = F.softmax(scores_over_t, dim=-1)
+    context_16d = torch.matmul(soft, block_keys_16d)
+    return F.linear(context_16d, out_proj_16d)
+
+
+def _active_lists(base: int, remote_indices: torch.Tensor, remote_counts: torch.Tensor):
+    M = remote_indices.shape[0]
+    out = []
+    for t in range(M):
+        c = int(remote_counts[t])
+        rem = remote_indices[t, :c].to(torch.int64)
+        out.append(torch.cat([torch.arange(base, dtype=torch.int64), rem]))
+    return out
+
+
+def token_pattention_per_token(x2d, k_gate, k_up, v, base, remote_indices, remote_counts,
+                               block_size: int = 64) -> torch.Tensor:
+    """pattention_triton.py:280-311 applied token by token (``activation="swiglu"``): gather the
+    active rows, ``silu(x K_g^T) * (x K_u^T)``, then ``@ V``.  Slow; used on small token counts."""
+    offsets = torch.arange(block_size)
+    y = torch.empty(x2d.shape[0], v.shape[1], dtype=torch.float32)
+    for t, active in enumerate(_active_lists(base, remote_indices, remote_counts)):
+        idx = (active.view(-1, 1) * block_size + offsets).flatten()
+        g = torch.matmul(x2d[t:t + 1], k_gate[idx].t())
+        u = torch.matmul(x2d[t:t + 1], k_up[idx].t())
+        y[t] = torch.matmul(F.silu(g) * u, v[idx])[0]
+    return y
+
+
+def token_pattention(x2d, k_gate, k_up, v, base, remote_indices, remote_counts,
+                     block_size: int = 64) -> torch.Tensor:
+    """Same sum as :func:`token_pattention_per_token`, grouped by block (each block's weights are
+    read once for all tokens that selected it)."""
+    M, D = x2d.shape
+    NB = k_gate.shape[0] // block_size
+    sel = torch.zeros(M, NB, dtype=torch.bool)
+    sel[:, :base] = True
+    for t in range(M):
+        c = int(remote_counts[t])
+        if c:
+            sel[t, remote_indices[t, :c].long()] = True
+    y = torch.zeros(M, v.shape[1], dtype=torch.float32)
+    for b in range(NB):
+        toks = sel[:, b].nonzero().flatten()
+        if toks.numel() == 0:
+            continue
+        rows = slice(b * block_size, (b + 1) * block_size)
+        xb = x2d[toks]
+        h = F.silu(xb @ k_gate[rows].t()) * (xb @ k_up[rows].t())
+        y.index_add_(0, toks, h @ v[rows])
+    return y
+
+
+def token_forward(x, w, *, base_blocks, top_p, min_remote_blocks, max_remote_blocks,
+                  temperature: float = 1.0, additive: bool = True, per_token: bool = False,
+                  stable: bool = True) -> Dict[str, torch.Tensor]:
+    """Per-token routed forward (the north-star composition of reference functions):
+    ``S = compute_router_scores(x) / T`` -> ``select_blocks(S, causal=False, base)`` -> gated
+    Pattention over base ∪ selected (pattention_triton.py:280-311) -> ``+ additive_stream(S)``."""
+    D = x.shape[-1]
+    x2d = x.reshape(-1, D).float()
+    S = router_scores(x2d, w.q_proj_16d, w.block_keys_16d) / temperature
+    r = select_blocks_noncausal(S[None], local_window_blocks=base_blocks, top_p=top_p,
+                                min_remote_blocks=min_remote_blocks,
+                                max_remote_blocks=max_remote_blocks,
+                                remote_capacity=max_remote_blocks, stable=stable)
+    idx, cnt = r.remote_indices[0], r.remote_counts[0]
+    fn = token_pattention_per_token if per_token else token_pattention
+    y = fn(x2d, w.k_gate, w.k_up, w.v, base_blocks, idx, cnt)
+    if additive:
+        y = y + additive_stream(S, w.block_keys_16d, w.out_proj_16d)
+    return {"y": y.reshape(x.shape), "scores": S, "remote_indices": idx, "remote_counts": cnt,
+            "sorted_probs": r.remote_probs_sorted[0]}
+
+
+def _pooled_active(mean_scores: torch.Tensor, base: int, remote: int) -> torch.Tensor:
+    """foveal_pattention.py:296-303 / :314-321 — top-k over the remote part, base ids first."""
+    _, top_remote = torch.topk(mean_scores[base:], k=remote)
+    if base > 0:
+        return torch.cat([torch.arange(base, dtype=torch.int32), (top_remote + base).to(torch.int32)])
+    return top_remote.to(torch.int32)
+
+
+def pooled_eval_active(x2d, w, base, remote) -> torch.Tensor:
+    """foveal_pattention.py:310-321 — pooled query ``rms_norm(W_q mean_t(x))``, scores without the
+    1/sqrt(16) scale, top-k."""
+    index_dim = w.q_proj_16d.shape[0]
+    q_16 = F.rms_norm(F.linear(x2d.mean(dim=0, keepdim=True), w.q_proj_16d), (index_dim,))
+    mean_scores = torch.matmul(q_16, w.block_keys_16d.t()).squeeze(0)
+    return _pooled_active(mean_scores, base, remote)
+
+
+def pooled_train_active(scores: torch.Tensor, base, remote) -> torch.Tensor:
+    """foveal_pattention.py:294-303 — top-k over the token-mean of per-token scores."""
+    return _pooled_active(scores.mean(dim=0), base, remote)
+
+
+def pooled_pattention(x2d, w, active: torch.Tensor, block_size: int = 64) -> torch.Tensor:
+    """foveal_pattention.py:115-122 and :329-335 — gather the active rows, then
+    ``F.linear(silu(F.linear(x, kg)) * F.linear(x, ku), v^T)``."""
+    offs = torch.arange(block_size, dtype=torch.int64)
+    idx = (active.view(-1, 1).to(torch.int64) * block_size + offs).flatten()
+    kg, ku, v = w.k_gate[idx], w.k_up[idx], w.v[idx]
+    act = F.silu(F.linear(x2d, kg)) * F.linear(x2d, ku)
+    return F.linear(act, v.t())
+
+
+def pooled_forward(x, w, *, base_blocks, remote_blocks, training: bool = False,
+                   temperature: float = 1.0) -> Dict[str, torch.Tensor]:
+    """foveal_pattention.py:264-352 for a fresh module (no cached active set): eval routes on the
+    pooled query; training routes on the token-mean of per-token scores and adds the additive
+    stream."""
+    D = x.shape[-1]
+    x2d = x.reshape(-1, D).float()
+    scores = router_scores(x2d, w.q_proj_16d, w.block_keys_16d)
+    if training:
+        active = pooled_train_active(scores, base_blocks, remote_blocks)
+    else:
+        active = pooled_eval_active(x2d, w, base_blocks, remote_blocks)
+    y = pooled_pattention(x2d, w, active)
+    if training:
+        y = y + additive_stream(scores / temperature, w.block_keys_16d, w.out_proj_16d)
+    return {"y": y.reshape(x.shape), "active_blocks": active, "scores": scores}
+
+
+def boundary_margins(sorted_probs: torch.Tensor, counts: torch.Tensor) -> torch.Tensor:
+    """Per token, the fp32 gap between the last selected and the first unselected remote probability
+    (``p[count-1] - p[count]``); a tiny gap marks a near tie whose order depends on rounding."""
+    M, n = sorted_probs.shape
+    c = counts.long().clamp(1, n - 1)
+    ar = torch.arange(M)
+    return sorted_probs[ar, c - 1] - sorted_probs[ar, c]
+
+
+def dense_swiglu(x2d, w) -> torch.Tensor:
+    """Dense SwiGLU with the reparameterised weights (foveal_pattention.py:162-169):
+    ``(silu(x W_gate^T) * (x W_up^T)) W_down^T`` with ``W_down^T = v``."""
+    return torch.matmul(F.silu(x2d @ w.k_gate.t()) * (x2d @ w.k_up.t()), w.v)

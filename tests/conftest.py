@@ -1,0 +1,90 @@
+"""Shared test setup.
+
+* ``gpu`` marker: tests that need a B200 (``pytest -m gpu``); everything else runs on the CPU.
+* ``fsi``: the package under test (directory ``foveal-sparse-indexer_b200``, imported by path).
+* ``golden(name)``: loads a fixture from ``tests/golden`` (written by ``tests/golden/make_golden.py``
+  from the reference implementation itself).
+"""
+
+from __future__ import annotations
+
+import importlib
+import json
+import os
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(HERE)
+if REPO not in sys.path:
+    sys.path.insert(0, REPO)
+
+fsi = importlib.import_module("foveal-sparse-indexer_b200")
+configs = fsi.configs
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs an sm_100 GPU (B200) and the built CUDA library")
+
+
+def pytest_collection_modifyitems(config, items):
+    if torch.cuda.is_available():
+        return
+    skip = pytest.mark.skip(reason="no CUDA device")
+    for it in items:
+        if "gpu" in it.keywords:
+            it.add_marker(skip)
+
+
+class Golden(dict):
+    meta: dict
+
+
+def golden(name: str) -> Golden:
+    path = os.path.join(HERE, "golden", f"{name}.npz")
+    z = np.load(path, allow_pickle=False)
+    g = Golden({k: z[k] for k in z.files if k != "meta"})
+    g.meta = json.loads(str(z["meta"]))
+    return g
+
+
+def rel_err(a: torch.Tensor, b: torch.Tensor) -> float:
+    """||a - b|| / ||b|| in fp64."""
+    a, b = a.double().cpu(), b.double().cpu()
+    return float((a - b).norm() / b.norm().clamp_min(1e-30))
+
+
+def max_rel(a: torch.Tensor, b: torch.Tensor) -> float:
+    """max|a - b| / max|b|."""
+    a, b = a.double().cpu(), b.double().cpu()
+    return float((a - b).abs().max() / b.abs().max().clamp_min(1e-30))
+
+
+def route_sets(idx, cnt):
+    idx = np.asarray(idx)
+    cnt = np.asarray(cnt)
+    return [frozenset(idx[t, :int(cnt[t])].tolist()) for t in range(len(cnt))]
+
+
+# Probabilities closer than this (fp32, absolute) at the selection boundary are rounding-level ties:
+# their order may legitimately differ between two correct fp32 implementations.
+TIE_EPS = 2e-8
+
+
+def compare_routes(idx, cnt, ref_idx, ref_cnt, margins=None, tie_eps: float = TIE_EPS):
+    """Counts must match exactly; selected sets must match exactly except on tokens whose reference
+    boundary margin is below ``tie_eps``.  Returns (n_mismatch_outside_ties, n_near_ties)."""
+    cnt = np.asarray(cnt)
+    ref_cnt = np.asarray(ref_cnt)
+    a, b = route_sets(idx, cnt), route_sets(ref_idx, ref_cnt)
+    bad = 0
+    ties = 0
+    for t in range(len(a)):
+        near = margins is not None and float(margins[t]) < tie_eps
+        ties += int(near)
+        if (a[t] != b[t] or cnt[t] != ref_cnt[t]) and not near:
+            bad += 1
+    return bad, ties

@@ -1,0 +1,210 @@
+"""Generate golden vectors by running the reference implementation itself.
+
+Run in a container that has the reference checkout (``--ref`` points at the directory holding the
+reference's ``foveal_indexer`` package):
+
+    python tests/golden/make_golden.py --ref <path-to-reference-checkout>
+
+It imports the reference's own functions (``FovealPattentionMLP``, ``select_blocks``,
+``_pytorch_pattention_fallback``), runs them in fp32 on the seeded synthetic inputs of each
+configuration (bf16 configurations use bf16-rounded values in an fp32 module) and writes small
+``.npz`` fixtures next to this script.  Weights and inputs are NOT stored: they are regenerated from
+the seed by ``configs.make_weights`` / ``configs.make_x``.  The fixtures hold routes, outputs for a
+few tokens and the per-token near-tie margins.
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, REPO)
+cfgmod = importlib.import_module("foveal-sparse-indexer_b200.configs")
+
+
+def load_reference(ref_root: str):
+    sys.path.insert(0, ref_root)
+    from foveal_indexer.foveal_pattention import FovealPattentionMLP
+    from foveal_indexer.core import select_blocks, masked_softmax
+    from foveal_indexer.pattention_triton import _pytorch_pattention_fallback
+    return FovealPattentionMLP, select_blocks, masked_softmax, _pytorch_pattention_fallback
+
+
+def build_module(FovealPattentionMLP, wl, w, remote_blocks):
+    m = FovealPattentionMLP(hidden_dim=wl.hidden_dim, intermediate_dim=wl.intermediate_dim,
+                            block_size=64, base_blocks=wl.base_blocks, remote_blocks=remote_blocks,
+                            index_dim=16, temperature=wl.temperature, dtype=torch.float32,
+                            use_fused_kernel=False)
+    with torch.no_grad():
+        sd = m.state_dict()
+        for k, t in w.state_dict().items():
+            sd[k].copy_(t)
+    return m
+
+
+def margins_from_scores(S, base, counts):
+    p = torch.softmax(S.float(), dim=-1)[:, base:]
+    sp = p.sort(dim=-1, descending=True, stable=True).values
+    c = counts.long().clamp(1, sp.shape[1] - 1)
+    ar = torch.arange(S.shape[0])
+    return (sp[ar, c - 1] - sp[ar, c]).numpy()
+
+
+def token_case(ref, wl, x2d, w, n_out):
+    FovealPattentionMLP, select_blocks, _, fallback = ref
+    m = build_module(FovealPattentionMLP, wl, w, wl.max_remote_blocks)
+    with torch.no_grad():
+        S = m.compute_router_scores(x2d) / wl.temperature
+        r = select_blocks(S[None], causal=False, block_size=64, local_window_blocks=wl.base_blocks,
+                          top_p=wl.top_p, min_remote_blocks=wl.min_remote_blocks,
+                          max_remote_blocks=wl.max_remote_blocks,
+                          remote_capacity=wl.max_remote_blocks)
+        idx, cnt = r.remote_indices[0], r.remote_counts[0]
+        ys = []
+        for t in range(n_out):
+            act = torch.cat([torch.arange(wl.base_blocks, dtype=torch.int64),
+                             idx[t, :int(cnt[t])].long()])
+            y = fallback(x2d[t:t + 1], m.k_gate, m.v, m.k_up, act, "swiglu", 64)
+            soft = F.softmax(S[t:t + 1], dim=-1)  # foveal_pattention.py:339 (S already / T)
+            y = y + m.out_proj_16d(torch.matmul(soft, m.block_keys_16d))
+            ys.append(y[0])
+        y = torch.stack(ys) if ys else torch.zeros(0, wl.hidden_dim)
+    return {
+        "scores": S.numpy().astype(np.float32),
+        "remote_indices": idx.numpy().astype(np.int32),
+        "remote_counts": cnt.numpy().astype(np.int32),
+        "margins": margins_from_scores(S, wl.base_blocks, cnt),
+        "cap_rate": np.float32(r.cap_rate), "mean_remote_blocks": np.float32(r.mean_remote_blocks),
+        "y": y.numpy().astype(np.float32),
+    }
+
+
+def pooled_case(ref, wl, x, w, remote_blocks, training, n_out):
+    FovealPattentionMLP = ref[0]
+    m = build_module(FovealPattentionMLP, wl, w, remote_blocks)
+    m.train(training)
+    with torch.no_grad():
+        y, info = m(x, return_router_info=True)
+    D = wl.hidden_dim
+    y2 = y.reshape(-1, D)[:n_out]
+    x2d = x.reshape(-1, D)
+    if training:
+        ms = info["scores"].mean(dim=0)
+    else:
+        q = F.rms_norm(m.q_proj_16d(x2d.mean(dim=0, keepdim=True)), (16,))
+        ms = torch.matmul(q, m.block_keys_16d.t()).squeeze(0)
+    rem = ms[wl.base_blocks:].sort(descending=True).values
+    gap = (rem[remote_blocks - 1] - rem[remote_blocks]).item() if remote_blocks < rem.numel() else 1.0
+    return {"active_blocks": info["active_blocks"].numpy().astype(np.int32),
+            "y": y2.numpy().astype(np.float32), "topk_gap": np.float32(gap)}
+
+
+def save(name, meta, arrays):
+    arrays = {k: np.asarray(v) for k, v in arrays.items()}
+    arrays["meta"] = np.array(json.dumps(meta))
+    path = os.path.join(HERE, f"{name}.npz")
+    np.savez_compressed(path, **arrays)
+    print(f"wrote {path} ({os.path.getsize(path) / 1024:.0f} KB)")
+
+
+def flat(prefix, d):
+    return {f"{prefix}{k}": v for k, v in d.items()}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", required=True)
+    ap.add_argument("--seed", type=int, default=0)
+    args = ap.parse_args()
+    ref = load_reference(args.ref)
+    torch.set_num_threads(os.cpu_count())
+    C = cfgmod.CONFIGS
+    meta_common = {"seed": args.seed, "torch": torch.__version__}
+
+    # 1. PR1 (fp32, full size): token mode, pooled eval and pooled train.
+    wl = C["pr1"]
+    w, x = cfgmod.make_weights(wl, args.seed), cfgmod.make_x(wl, args.seed)
+    x2d = x.reshape(-1, wl.hidden_dim)
+    arr = flat("tok_", token_case(ref, wl, x2d, w, n_out=x2d.shape[0]))
+    arr.update(flat("peval_", pooled_case(ref, wl, x, w, wl.max_remote_blocks, False, 512)))
+    arr.update(flat("ptrain_", pooled_case(ref, wl, x, w, wl.max_remote_blocks, True, 512)))
+    save("pr1", {**meta_common, "config": "pr1"}, arr)
+
+    # 2. Decode (bf16 values, fp32 math): K_max in {8, 16, 32}, all 64 tokens.
+    arr = {}
+    for wl in cfgmod.decode_points():
+        w, x = cfgmod.make_weights(wl, args.seed), cfgmod.make_x(wl, args.seed)
+        x2d = x.reshape(-1, wl.hidden_dim)
+        arr.update(flat(f"k{wl.max_remote_blocks}_", token_case(ref, wl, x2d, w, n_out=64)))
+        if wl.max_remote_blocks == 16:
+            arr.update(flat("peval_", pooled_case(ref, wl, x, w, 16, False, 64)))
+    save("decode", {**meta_common, "config": "decode", "kmax": list(cfgmod.DECODE_KMAX)}, arr)
+
+    # 3. 8B slice: first 128 tokens; outputs for 16 of them.
+    wl = C["8b"]
+    w, x = cfgmod.make_weights(wl, args.seed), cfgmod.make_x(wl, args.seed)
+    xs = x.reshape(-1, wl.hidden_dim)[:128].contiguous()
+    arr = flat("tok_", token_case(ref, wl, xs, w, n_out=16))
+    arr.update(flat("peval_", pooled_case(ref, wl, xs.view(1, 128, -1), w, 20, False, 16)))
+    save("8b_slice", {**meta_common, "config": "8b", "tokens": 128}, arr)
+    del w, x
+
+    # 4. 70B slice: first 64 tokens; outputs for 4 of them.
+    wl = C["70b"]
+    w, x = cfgmod.make_weights(wl, args.seed), cfgmod.make_x(wl, args.seed)
+    xs = x.reshape(-1, wl.hidden_dim)[:64].contiguous()
+    save("70b_slice", {**meta_common, "config": "70b", "tokens": 64},
+         flat("tok_", token_case(ref, wl, xs, w, n_out=4)))
+    del w, x
+
+    # 5. Sweep: routes for the first 64 tokens at all 20 points, outputs for 4 tokens at two.
+    arr = {}
+    pts = cfgmod.sweep_points()
+    w = cfgmod.make_weights(pts[0], args.seed)
+    x = cfgmod.make_x(pts[0], args.seed)
+    xs = x.reshape(-1, pts[0].hidden_dim)[:64].contiguous()
+    for i, wl in enumerate(pts):
+        n_out = 4 if (wl.top_p, wl.max_remote_blocks) in ((0.3, 14), (1.0, 224)) else 0
+        d = token_case(ref, wl, xs, w, n_out=n_out)
+        d.pop("scores")
+        arr.update(flat(f"p{i}_", d))
+    save("sweep_slice", {**meta_common, "config": "sweep",
+                         "points": [[p.top_p, p.max_remote_blocks, p.min_remote_blocks] for p in pts]},
+         arr)
+
+    # 6. Router known-answer cases from the reference's own tests plus a peaked case where top-p
+    #    binds (counts vary between K_min and K_max).
+    FovealPattentionMLP, select_blocks, masked_softmax, _ = ref
+    scores = torch.tensor([[1.0, 2.0, 3.0], [4.0, 5.0, 6.0]])
+    mask = torch.tensor([[True, True, False], [False, True, True]])
+    arr = {"ms_scores": scores.numpy(), "ms_mask": mask.numpy(),
+           "ms_probs": masked_softmax(scores, mask).numpy()}
+    g = torch.Generator().manual_seed(1234)
+    for name, (B, Q, NB, base, tp, kmin, kmax, cap, scale) in {
+        "guard": (2, 8, 8, 2, 0.99, 1, 3, 4, 1.0),      # tests/test_indexer.py:42-61
+        "peaked": (1, 256, 32, 1, 0.9, 2, 8, 8, 6.0),
+        "wide": (1, 128, 224, 4, 0.5, 0, 56, 56, 20.0),
+        "nobase": (1, 64, 40, 0, 0.7, 3, 12, 16, 8.0),
+    }.items():
+        s = torch.randn(B, Q, NB, generator=g) * scale
+        r = select_blocks(s, causal=False, local_window_blocks=base, top_p=tp,
+                          min_remote_blocks=kmin, max_remote_blocks=kmax, remote_capacity=cap)
+        arr[f"{name}_scores"] = s.numpy()
+        arr[f"{name}_params"] = np.array([base, tp, kmin, kmax, cap], dtype=np.float64)
+        arr[f"{name}_indices"] = r.remote_indices.numpy()
+        arr[f"{name}_counts"] = r.remote_counts.numpy()
+        arr[f"{name}_cap_rate"] = np.float32(r.cap_rate)
+    save("router_kat", {**meta_common, "config": "router"}, arr)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,330 @@
+"""GPU parity: the CUDA path (through the C ABI) against the golden vectors and the CPU oracle.
+
+Bars: active-block sets and counts bit-exact (tokens whose reference boundary margin is below
+TIE_EPS are rounding-level ties and are counted, not failed); outputs within 1e-4 relative (fp32
+configuration) or 2e-2 relative (bf16 configurations) of the fp32 reference, measured as
+||y - ref|| / ||ref|| and as max|y - ref| / max|ref|.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import compare_routes, configs, fsi, golden, max_rel, rel_err
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"fp32": 1e-4, "bf16": 2e-2}
+DEV = "cuda"
+
+
+def module_for(wl, w, routing="token", remote_blocks=None):
+    m = fsi.FovealPattentionMLP(
+        hidden_dim=wl.hidden_dim, intermediate_dim=wl.intermediate_dim, base_blocks=wl.base_blocks,
+        remote_blocks=remote_blocks if remote_blocks is not None else wl.max_remote_blocks,
+        temperature=wl.temperature, dtype=wl.torch_dtype, routing=routing, top_p=wl.top_p,
+        min_remote_blocks=wl.min_remote_blocks, max_remote_blocks=wl.max_remote_blocks)
+    sd = {k: t.to(wl.torch_dtype) for k, t in w.state_dict().items()}
+    m.load_state_dict(sd, strict=False)
+    return m.to(DEV).eval()
+
+
+def check_y(y, ref, dtype, factor=1.0):
+    tol = TOL[dtype] * factor
+    e1, e2 = rel_err(y.float(), ref), max_rel(y.float(), ref)
+    assert e1 < tol and e2 < tol, f"rel_l2 {e1:.3e}, max_rel {e2:.3e}, tol {tol}"
+    return e1
+
+
+def run_token(m, x2d):
+    with torch.no_grad():
+        y, info = m(x2d.to(DEV), return_router_info=True)
+    torch.cuda.synchronize()
+    return y, info
+
+
+def device_error_is_clear():
+    ws = fsi._lib._ws
+    for buf in ws.values():
+        assert fsi._lib.device_error(buf) == 0
+
+
+# ------------------------------------------------------------------ router
+@pytest.mark.parametrize("case", ["guard", "peaked", "wide", "nobase"])
+def test_select_blocks_known_answer(case):
+    g = golden("router_kat")
+    base, tp, kmin, kmax, cap = g[f"{case}_params"]
+    s = torch.from_numpy(g[f"{case}_scores"]).to(DEV)
+    r = fsi.select_blocks(s, causal=False, local_window_blocks=int(base), top_p=float(tp),
+                          min_remote_blocks=int(kmin), max_remote_blocks=int(kmax), remote_capacity=int(cap))
+    B, Q, _ = s.shape
+    bad, _ = compare_routes(r.remote_indices.reshape(B * Q, -1).cpu(), r.remote_counts.reshape(-1).cpu(),
+                            g[f"{case}_indices"].reshape(B * Q, -1), g[f"{case}_counts"].reshape(-1))
+    assert bad == 0
+    assert np.array_equal(r.remote_counts.cpu().numpy(), g[f"{case}_counts"])
+    assert abs(float(r.cap_rate) - float(g[f"{case}_cap_rate"])) < 1e-6
+    # full capacity array, including the tail past the counts (base ids / padding), matches the oracle
+    o = oracle.select_blocks_noncausal(s.cpu(), local_window_blocks=int(base), top_p=float(tp),
+                                       min_remote_blocks=int(kmin), max_remote_blocks=int(kmax),
+                                       remote_capacity=int(cap))
+    assert torch.equal(r.remote_indices.cpu(), o.remote_indices)
+
+
+def test_router_scores_match_oracle():
+    for name, n in (("pr1", 512), ("8b", 256), ("70b", 128)):
+        wl = configs.CONFIGS[name]
+        w = configs.make_weights(wl)
+        x2d = configs.make_x(wl).reshape(-1, wl.hidden_dim)[:n].contiguous()
+        ref = oracle.router_scores(x2d, w.q_proj_16d, w.block_keys_16d)
+        s, q16 = fsi.kernels.router_scores(x2d.to(DEV, wl.torch_dtype), w.q_proj_16d.to(DEV, wl.torch_dtype),
+                                           w.block_keys_16d.to(DEV, wl.torch_dtype), want_q16=True)
+        assert rel_err(s, ref) < 1e-5, name
+        qref = torch.nn.functional.rms_norm(x2d @ w.q_proj_16d.t(), (16,))
+        assert rel_err(q16, qref) < 1e-5, name
+
+
+# ------------------------------------------------------------------ token mode vs golden
+def token_vs_golden(wl, w, x2d, g, prefix, n_out):
+    m = module_for(wl, w)
+    y, info = run_token(m, x2d)
+    bad, ties = compare_routes(info["remote_indices"].cpu(), info["remote_counts"].cpu(),
+                               g[f"{prefix}remote_indices"], g[f"{prefix}remote_counts"], g[f"{prefix}margins"])
+    assert bad == 0, f"{bad} routes differ outside near ties ({ties} ties)"
+    if n_out:
+        check_y(y[:n_out].cpu(), torch.from_numpy(g[f"{prefix}y"]), wl.dtype)
+    device_error_is_clear()
+    return y, info
+
+
+def test_token_pr1_fp32():
+    wl = configs.CONFIGS["pr1"]
+    w, x = configs.make_weights(wl), configs.make_x(wl)
+    token_vs_golden(wl, w, x.reshape(-1, wl.hidden_dim), golden("pr1"), "tok_", 512)
+
+
+@pytest.mark.parametrize("k", [8, 16, 32])
+def test_token_decode(k):
+    wl = [p for p in configs.decode_points() if p.max_remote_blocks == k][0]
+    w, x = configs.make_weights(wl), configs.make_x(wl)
+    token_vs_golden(wl, w, x.reshape(-1, wl.hidden_dim), golden("decode"), f"k{k}_", 64)
+
+
+def test_token_8b_slice():
+    wl = configs.CONFIGS["8b"]
+    w = configs.make_weights(wl)
+    xs = configs.make_x(wl).reshape(-1, wl.hidden_dim)[:128].contiguous()
+    token_vs_golden(wl, w, xs, golden("8b_slice"), "tok_", 16)
+
+
+def test_token_70b_slice():
+    wl = configs.CONFIGS["70b"]
+    w = configs.make_weights(wl)
+    xs = configs.make_x(wl).reshape(-1, wl.hidden_dim)[:64].contiguous()
+    token_vs_golden(wl, w, xs, golden("70b_slice"), "tok_", 4)
+
+
+def test_token_sweep_slice():
+    g = golden("sweep_slice")
+    pts = configs.sweep_points()
+    w = configs.make_weights(pts[0])
+    xs = configs.make_x(pts[0]).reshape(-1, pts[0].hidden_dim)[:64].contiguous()
+    for i, wl in enumerate(pts):
+        n_out = g[f"p{i}_y"].shape[0] if f"p{i}_y" in g else 0
+        token_vs_golden(wl, w, xs, g, f"p{i}_", n_out)
+
+
+# ------------------------------------------------------------------ pooled mode vs golden
+@pytest.mark.parametrize("training", [False, True])
+def test_pooled_pr1(training):
+    wl = configs.CONFIGS["pr1"]
+    g = golden("pr1")
+    w, x = configs.make_weights(wl), configs.make_x(wl)
+    m = module_for(wl, w, routing="pooled")
+    m.train(training)
+    with torch.no_grad():
+        y, info = m(x.to(DEV), return_router_info=True)
+    p = "ptrain_" if training else "peval_"
+    assert set(info["active_blocks"].cpu().tolist()) == set(g[f"{p}active_blocks"].tolist())
+    check_y(y.reshape(-1, wl.hidden_dim).cpu(), torch.from_numpy(g[f"{p}y"]), "fp32")
+
+
+def test_pooled_decode_and_cache():
+    wl = configs.decode_points()[1]
+    g = golden("decode")
+    w, x = configs.make_weights(wl), configs.make_x(wl)
+    m = module_for(wl, w, routing="pooled", remote_blocks=16)
+    with torch.no_grad():
+        y, info = m(x.to(DEV), return_router_info=True)
+        assert set(info["active_blocks"].cpu().tolist()) == set(g["peval_active_blocks"].tolist())
+        check_y(y.reshape(-1, wl.hidden_dim).cpu(), torch.from_numpy(g["peval_y"]), "bf16")
+        y2 = m(x.to(DEV))  # cache hit (decode fast path): same active set, same result
+    assert torch.equal(y, y2)
+
+
+def test_pooled_8b_slice():
+    wl = configs.CONFIGS["8b"]
+    g = golden("8b_slice")
+    w = configs.make_weights(wl)
+    xs = configs.make_x(wl).reshape(-1, wl.hidden_dim)[:128].contiguous()
+    m = module_for(wl, w, routing="pooled", remote_blocks=20)
+    with torch.no_grad():
+        y, info = m(xs.view(1, 128, -1).to(DEV), return_router_info=True)
+    assert set(info["active_blocks"].cpu().tolist()) == set(g["peval_active_blocks"].tolist())
+    check_y(y.reshape(-1, wl.hidden_dim)[:16].cpu(), torch.from_numpy(g["peval_y"]), "bf16")
+
+
+# ------------------------------------------------------------------ full-size configurations
+def full_size_check(name, n_out):
+    """All tokens: routes vs the oracle; a token subsample: outputs vs the oracle."""
+    wl = configs.CONFIGS[name]
+    w = configs.make_weights(wl)
+    x2d = configs.make_x(wl).reshape(-1, wl.hidden_dim)
+    m = module_for(wl, w)
+    y, info = run_token(m, x2d)
+    S = oracle.router_scores(x2d, w.q_proj_16d, w.block_keys_16d) / wl.temperature
+    r = oracle.select_blocks_noncausal(S[None], local_window_blocks=wl.base_blocks, top_p=wl.top_p,
+                                       min_remote_blocks=wl.min_remote_blocks,
+                                       max_remote_blocks=wl.max_remote_blocks,
+                                       remote_capacity=wl.max_remote_blocks)
+    idx, cnt = r.remote_indices[0], r.remote_counts[0]
+    margins = oracle.boundary_margins(r.remote_probs_sorted[0], cnt)
+    bad, ties = compare_routes(info["remote_indices"].cpu(), info["remote_counts"].cpu(), idx, cnt, margins)
+    assert bad == 0, f"{bad} of {x2d.shape[0]} routes differ outside near ties ({ties} ties)"
+    sel = torch.randperm(x2d.shape[0], generator=torch.Generator().manual_seed(7))[:n_out].sort().values
+    ref = oracle.token_pattention(x2d[sel], w.k_gate, w.k_up, w.v, wl.base_blocks, idx[sel], cnt[sel])
+    ref = ref + oracle.additive_stream(S[sel], w.block_keys_16d, w.out_proj_16d)
+    check_y(y[sel.to(DEV)].cpu(), ref, wl.dtype)
+    device_error_is_clear()
+    return y
+
+
+def test_full_8b_config():
+    y = full_size_check("8b", 128)
+    assert torch.isfinite(y).all()
+
+
+def test_full_70b_config():
+    full_size_check("70b", 32)
+
+
+def test_block_shards_sum_to_full():
+    """Parameter-block sharding arithmetic on one GPU: the fp32 partials of stride-2 shards (additive
+    stream on shard 0 only) sum to the unsharded forward."""
+    wl = configs.CONFIGS["8b"]
+    w = configs.make_weights(wl)
+    x2d = configs.make_x(wl).reshape(-1, wl.hidden_dim)[:1000].contiguous().to(DEV, torch.bfloat16)
+    m = module_for(wl, w)
+    kg, ku, v, vt, wq, k16, wout = m._weights()
+    kw = dict(base_blocks=wl.base_blocks, top_p=wl.top_p, min_remote=wl.min_remote_blocks,
+              max_remote=wl.max_remote_blocks)
+    full, _, _, _ = fsi.kernels.token_forward(x2d, kg, ku, v, vt, wq, k16, wout, out_f32=True, **kw)
+    parts = [fsi.kernels.token_forward(x2d, kg, ku, v, vt, wq, k16, wout, out_f32=True, block_stride=4,
+                                       block_offset=r, additive=(r == 0), **kw)[0] for r in range(4)]
+    assert rel_err(sum(parts).cpu(), full.cpu()) < 1e-5
+
+
+def test_all_blocks_active_equals_dense():
+    wl = configs.CONFIGS["8b"].with_(hidden_dim=1024, intermediate_dim=2048)
+    w = configs.make_weights(wl)
+    x2d = configs.make_x(wl).reshape(-1, wl.hidden_dim)[:300].contiguous()
+    m = module_for(wl, w, routing="pooled", remote_blocks=wl.num_blocks - wl.base_blocks)
+    active = torch.arange(wl.num_blocks, dtype=torch.int32, device=DEV)
+    kg, ku, v, vt, *_ = m._weights()
+    y = fsi.kernels.pooled_forward(x2d.to(DEV, torch.bfloat16), kg, ku, v, vt, active)
+    check_y(y.cpu(), oracle.dense_swiglu(x2d, w), "bf16")
+
+
+# ------------------------------------------------------------------ edge cases
+@pytest.mark.parametrize("M", [1, 7, 129, 300])
+def test_ragged_token_counts(M):
+    wl = configs.CONFIGS["8b"].with_(hidden_dim=512, intermediate_dim=1024, base_blocks=2,
+                                     max_remote_blocks=5, min_remote_blocks=2)
+    w = configs.make_weights(wl)
+    x2d = configs.make_x(wl).reshape(-1, wl.hidden_dim)[:M].contiguous()
+    m = module_for(wl, w)
+    y, info = run_token(m, x2d)
+    ref = oracle.token_forward(x2d, w, base_blocks=wl.base_blocks, top_p=wl.top_p,
+                               min_remote_blocks=wl.min_remote_blocks, max_remote_blocks=wl.max_remote_blocks)
+    bad, _ = compare_routes(info["remote_indices"].cpu(), info["remote_counts"].cpu(), ref["remote_indices"],
+                            ref["remote_counts"], oracle.boundary_margins(ref["sorted_probs"], ref["remote_counts"]))
+    assert bad == 0
+    check_y(y.cpu(), ref["y"].reshape(M, -1), "bf16")
+
+
+def test_no_base_blocks_and_capacity_past_available():
+    """base=0, and K_max larger than the number of remote blocks (counts clamp to `available`)."""
+    for base, kmax in ((0, 6), (3, 40)):
+        wl = configs.CONFIGS["8b"].with_(hidden_dim=256, intermediate_dim=2048, base_blocks=base,
+                                         max_remote_blocks=kmax, min_remote_blocks=2, top_p=0.95)
+        w = configs.make_weights(wl)
+        x2d = configs.make_x(wl).reshape(-1, wl.hidden_dim)[:200].contiguous()
+        m = module_for(wl, w)
+        y, info = run_token(m, x2d)
+        ref = oracle.token_forward(x2d, w, base_blocks=base, top_p=wl.top_p, min_remote_blocks=2,
+                                   max_remote_blocks=kmax)
+        mg = oracle.boundary_margins(ref["sorted_probs"], ref["remote_counts"])
+        bad, _ = compare_routes(info["remote_indices"].cpu(), info["remote_counts"].cpu(), ref["remote_indices"],
+                                ref["remote_counts"], mg)
+        assert bad == 0
+        assert int(info["remote_counts"].max()) <= min(kmax, wl.num_blocks - base)
+        check_y(y.cpu(), ref["y"].reshape(200, -1), "bf16")
+
+
+def test_empty_input():
+    wl = configs.CONFIGS["pr1"]
+    w = configs.make_weights(wl)
+    m = module_for(wl, w)
+    with torch.no_grad():
+        y = m(torch.zeros(0, wl.hidden_dim, device=DEV))
+    assert y.shape == (0, wl.hidden_dim)
+
+
+# ------------------------------------------------------------------ reference API behaviour
+class _DenseMLP(torch.nn.Module):
+    def __init__(self, hidden_dim=256, intermediate_dim=512):
+        super().__init__()
+        self.gate_proj = torch.nn.Linear(hidden_dim, intermediate_dim, bias=False)
+        self.up_proj = torch.nn.Linear(hidden_dim, intermediate_dim, bias=False)
+        self.down_proj = torch.nn.Linear(intermediate_dim, hidden_dim, bias=False)
+
+
+def test_reference_module_tests_on_gpu():
+    """tests/test_foveal_pattention.py:27-44, :69-96 and :99-124 of the reference, on the GPU."""
+    torch.manual_seed(0)
+    dense = _DenseMLP().to(DEV)
+    patt = fsi.FovealPattentionMLP.from_dense_mlp(dense, block_size=64, base_blocks=2, remote_blocks=4)
+    assert patt.num_blocks == 8 and patt.total_active_blocks == 6
+    x = torch.randn(2, 16, 256, device=DEV)
+    patt.train()
+    out, info = patt(x, return_router_info=True)
+    assert out.shape == (2, 16, 256) and "scores" in info and "active_blocks" in info
+    with pytest.raises(NotImplementedError):
+        out.sum().backward()
+    patt0 = fsi.FovealPattentionMLP.from_dense_mlp(dense, block_size=64, base_blocks=0, remote_blocks=4).eval()
+    with torch.no_grad():
+        out, info = patt0(x, return_router_info=True)
+        assert out.shape == (2, 16, 256) and len(info["active_blocks"]) == 4
+        patt0.clear_cache()
+        assert patt0(torch.randn(2, 1, 256, device=DEV)).shape == (2, 1, 256)
+    # dense equivalence when every block is active (fp32, CUDA-core path)
+    full = fsi.FovealPattentionMLP.from_dense_mlp(dense, block_size=64, base_blocks=8, remote_blocks=0).eval()
+    with torch.no_grad():
+        y = full(x)
+        ref = dense.down_proj(torch.nn.functional.silu(dense.gate_proj(x)) * dense.up_proj(x))
+    assert rel_err(y.cpu(), ref.cpu()) < 1e-5
+
+
+def test_errors_are_loud():
+    wl = configs.CONFIGS["pr1"]
+    w = configs.make_weights(wl)
+    m = module_for(wl, w)
+    with pytest.raises(RuntimeError):
+        m(torch.zeros(4, wl.hidden_dim))  # CPU input: no fallback
+    with pytest.raises(fsi.FovealKernelError):
+        fsi.kernels.select(torch.zeros(4, 2000, device=DEV), base_blocks=0, top_p=0.5, min_remote=0,
+                           max_remote=4, capacity=4)  # NB > 1024 unsupported
+    with pytest.raises(NotImplementedError):
+        fsi.select_blocks(torch.zeros(1, 4, 8, device=DEV), causal=True)
