@@ -247,6 +247,7 @@ int fp_pattention_token_fwd(const void* x, int64_t M, int D, int NB, int dtype, 
                             int32_t* remote_indices, int32_t* remote_counts, float* scores,
                             void* workspace, size_t workspace_bytes, void* stream) {
   FP_TRY(check_common(dtype, M, D, NB));
+  if (M == 0) return FP_OK;  // empty batch: nothing to do (empty tensors may carry null pointers)
   if (!x || !k_gate || !k_up || !v || !q_proj || !block_keys || !y || !workspace) return FP_ERR_INVALID_ARG;
   if (additive && !out_proj) return FP_ERR_INVALID_ARG;
   if (base_blocks < 0 || base_blocks > NB || min_remote < 0 || max_remote < 0) return FP_ERR_INVALID_ARG;
@@ -323,6 +324,7 @@ int fp_pattention_pooled_fwd(const void* x, int64_t M, int D, int NB, int dtype,
                              int n_active, const float* ctx16, const void* out_proj, void* y, int y_f32,
                              void* workspace, size_t workspace_bytes, void* stream) {
   FP_TRY(check_common(dtype, M, D, NB));
+  if (M == 0) return FP_OK;  // empty batch
   if (!x || !k_gate || !k_up || !v || !active || !y || !workspace || n_active < 0 || n_active > NB)
     return FP_ERR_INVALID_ARG;
   if (ctx16 && !out_proj) return FP_ERR_INVALID_ARG;

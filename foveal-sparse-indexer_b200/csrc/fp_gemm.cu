@@ -36,7 +36,7 @@ struct __align__(8) PipeBars {
   int32_t consumed;
 };
 
-constexpr size_t kGemmSmem = 1024 + kStages * kStageBytes + sizeof(PipeBars) + 256 * sizeof(int32_t) + 64;
+constexpr size_t kGemmSmem = 1024 + kStages * kStageBytes + sizeof(PipeBars) + 64;
 
 __device__ __forceinline__ uint8_t* aligned_smem(uint8_t* raw) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
@@ -148,7 +148,6 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = aligned_smem(smem_raw);
   PipeBars* bars = reinterpret_cast<PipeBars*>(smem + kStages * kStageBytes);
-  int32_t* tok_ids = reinterpret_cast<int32_t*>(bars + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -163,37 +162,44 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
   uint32_t issued = 0;
 
   if (warp == 0) {
-    // ---------------- TMA producer
+    // ---------------- TMA producer: the whole warp issues.  Lane 0 arms the stage barrier, lanes 0-7
+    // load the eight 16-row weight boxes, and every lane issues the row gathers g = lane, lane + 32.
     uint32_t it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
       const GuTile t = gu_decode(a, tile);
       if (t.n <= 0) continue;
       const int npad = (t.n + 15) & ~15;
-      __syncwarp();
-      for (int i = lane; i < npad; i += 32) tok_ids[i] = gu_token(t, i < t.n ? i : t.n - 1);
-      __syncwarp();
-      if (lane == 0) {
-        for (int kb = 0; kb < nkb; ++kb, ++it) {
-          const int s = it % kStages;
-          const uint32_t ph = (it / kStages) & 1u;
-          if (!mbar_wait(&bars->empty[s], ph ^ 1u, a.err, kErrWaitEmpty)) { ok = false; break; }
-          uint8_t* As = smem + s * kStageBytes;
-          uint8_t* Bs = As + kABytes;
-          mbar_arrive_expect_tx(&bars->full[s], kABytes + (uint32_t)npad * 128u);
-          const int kc = kb * kTileK;
+      int ids[8];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {  // rows [32q, 32q+16) gate, [32q+16, 32q+32) up: channels 16q..16q+15
-            tma_load_2d(As + (32 * q) * 128, &tm_kg, &bars->full[s], kc, t.b * kBlock + 16 * q);
-            tma_load_2d(As + (32 * q + 16) * 128, &tm_ku, &bars->full[s], kc, t.b * kBlock + 16 * q);
-          }
-          for (int g = 0; g < npad / 4; ++g)
-            tma_gather4(Bs + 4 * g * 128, &tm_x, &bars->full[s], kc, tok_ids[4 * g], tok_ids[4 * g + 1],
-                        tok_ids[4 * g + 2], tok_ids[4 * g + 3]);
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int row = 4 * (lane + 32 * j) + r;
+          ids[4 * j + r] = row < npad ? gu_token(t, row < t.n ? row : t.n - 1) : 0;
+        }
+      const int wq = lane >> 1;
+      const void* wmap = (lane & 1) ? (const void*)&tm_ku : (const void*)&tm_kg;
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % kStages;
+        const uint32_t ph = (it / kStages) & 1u;
+        if (!warp_wait(&bars->empty[s], ph ^ 1u, a.err, kErrWaitEmpty)) { ok = false; break; }
+        uint8_t* As = smem + s * kStageBytes;
+        uint8_t* Bs = As + kABytes;
+        if (lane == 0) mbar_arrive_expect_tx(&bars->full[s], kABytes + (uint32_t)npad * 128u);
+        __syncwarp();
+        const int kc = kb * kTileK;
+        // rows [32q, 32q+16) gate, [32q+16, 32q+32) up of channels 16q..16q+15
+        if (lane < 8)
+          tma_load_2d(As + (32 * wq + 16 * (lane & 1)) * 128, wmap, &bars->full[s], kc, t.b * kBlock + 16 * wq);
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int g = lane + 32 * j;
+          if (4 * g < npad)
+            tma_gather4(Bs + 4 * g * 128, &tm_x, &bars->full[s], kc, ids[4 * j], ids[4 * j + 1], ids[4 * j + 2],
+                        ids[4 * j + 3]);
         }
       }
-      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-      it = __shfl_sync(0xffffffffu, it, 0);
     }
     issued = it;
   } else if (warp == 1) {

@@ -1,0 +1,166 @@
+"""Multi-rank host logic on CPU (gloo, world_size 2).
+
+* Parameter-block sharding: every rank routes all tokens, computes the partial output of the blocks it
+  owns (b % world == rank; the additive stream only on rank 0), and one all-reduce (or reduce-scatter)
+  sums the partials.  The partials here come from the CPU oracle restricted to the owned blocks, so the
+  test checks the decomposition and the collective wiring of ``sharding.sharded_token_forward``.
+* Failure detection: a rank that leaves before the collective makes the other rank's collective end
+  with an error within the process-group timeout instead of hanging.
+"""
+
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+import sys
+import tempfile
+import time
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(HERE)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _setup(rank, world, port, timeout_s=60):
+    sys.path.insert(0, REPO)
+    sys.path.insert(0, HERE)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=timeout_s))
+
+
+def _oracle_partial(module, x2d, world, rank, additive, want_routes):
+    import oracle
+    from conftest import configs
+
+    w = configs.Weights(module.k_gate.detach(), module.k_up.detach(), module.v.detach(),
+                        module.q_proj_16d.weight.detach(), module.block_keys_16d.detach(),
+                        module.out_proj_16d.weight.detach())
+    S = oracle.router_scores(x2d, w.q_proj_16d, w.block_keys_16d) / module.temperature
+    r = oracle.select_blocks_noncausal(S[None], local_window_blocks=module.base_blocks, top_p=module.top_p,
+                                       min_remote_blocks=module.min_remote_blocks,
+                                       max_remote_blocks=module.max_remote_blocks,
+                                       remote_capacity=module.max_remote_blocks)
+    idx, cnt = r.remote_indices[0], r.remote_counts[0]
+    M = x2d.shape[0]
+    sel = torch.zeros(M, module.num_blocks, dtype=torch.bool)
+    sel[:, :module.base_blocks] = True
+    for t in range(M):
+        sel[t, idx[t, :int(cnt[t])].long()] = True
+    y = torch.zeros(M, x2d.shape[1])
+    for b in range(rank, module.num_blocks, world):  # owned blocks
+        toks = sel[:, b].nonzero().flatten()
+        if toks.numel():
+            rows = slice(b * 64, (b + 1) * 64)
+            xb = x2d[toks]
+            h = torch.nn.functional.silu(xb @ w.k_gate[rows].t()) * (xb @ w.k_up[rows].t())
+            y.index_add_(0, toks, h @ w.v[rows])
+    if additive:
+        y = y + oracle.additive_stream(S, w.block_keys_16d, w.out_proj_16d)
+    return y, idx, cnt, S
+
+
+def _shard_worker(rank, world, port, out_dir):
+    _setup(rank, world, port)
+    from conftest import fsi
+    import oracle
+
+    torch.manual_seed(0)
+    m = fsi.FovealPattentionMLP(hidden_dim=64, intermediate_dim=640, base_blocks=2, remote_blocks=3,
+                                dtype=torch.float32, routing="token", top_p=0.7, min_remote_blocks=1,
+                                max_remote_blocks=3)
+    with torch.no_grad():
+        m.out_proj_16d.weight.normal_(std=0.05)
+    x2d = torch.randn(32, 64)
+    fsi.sharding.shard_parameter_blocks(m)
+    assert fsi.sharding.owned_blocks(10, rank, world) == list(range(rank, 10, world))
+    y, _, _, _ = fsi.sharding.sharded_token_forward(m, x2d, compute_partial=_oracle_partial)
+    ys, _, _, _ = fsi.sharding.sharded_token_forward(m, x2d, compute_partial=_oracle_partial, reduce="scatter")
+    ref = oracle.token_forward(x2d, m_weights(m), base_blocks=2, top_p=0.7, min_remote_blocks=1,
+                               max_remote_blocks=3)["y"]
+    err = float((y - ref).norm() / ref.norm())
+    errs = float((ys - ref[rank * 16:(rank + 1) * 16]).norm() / ref[rank * 16:(rank + 1) * 16].norm())
+    with open(os.path.join(out_dir, f"r{rank}.txt"), "w") as f:
+        f.write(f"{err} {errs}")
+    dist.destroy_process_group()
+
+
+def m_weights(m):
+    from conftest import configs
+    return configs.Weights(m.k_gate.detach(), m.k_up.detach(), m.v.detach(), m.q_proj_16d.weight.detach(),
+                           m.block_keys_16d.detach(), m.out_proj_16d.weight.detach())
+
+
+def test_block_sharded_forward_matches_full():
+    port = _free_port()
+    with tempfile.TemporaryDirectory() as d:
+        mp.spawn(_shard_worker, args=(2, port, d), nprocs=2, join=True)
+        for r in range(2):
+            err, errs = map(float, open(os.path.join(d, f"r{r}.txt")).read().split())
+            assert err < 1e-5 and errs < 1e-5, (r, err, errs)
+
+
+def _token_split_worker(rank, world, port, out_dir):
+    _setup(rank, world, port)
+    from conftest import fsi
+
+    x = torch.arange(37 * 3, dtype=torch.float32).view(37, 3)
+    part = fsi.sharding.split_tokens(x, rank, world)
+    sizes = [torch.zeros(1, dtype=torch.int64) for _ in range(world)]
+    dist.all_gather(sizes, torch.tensor([part.shape[0]]))
+    with open(os.path.join(out_dir, f"r{rank}.txt"), "w") as f:
+        f.write(f"{int(part[0, 0]) // 3} {part.shape[0]} {sum(int(s) for s in sizes)}")
+    dist.destroy_process_group()
+
+
+def test_token_split_covers_all_rows():
+    port = _free_port()
+    with tempfile.TemporaryDirectory() as d:
+        mp.spawn(_token_split_worker, args=(2, port, d), nprocs=2, join=True)
+        r0 = list(map(int, open(os.path.join(d, "r0.txt")).read().split()))
+        r1 = list(map(int, open(os.path.join(d, "r1.txt")).read().split()))
+        assert r0 == [0, 19, 37] and r1 == [19, 18, 37]
+
+
+def _failure_worker(rank, world, port, out_dir):
+    _setup(rank, world, port, timeout_s=5)
+    if rank == 1:
+        # leaves between steps, before the collective, with nothing in flight
+        with open(os.path.join(out_dir, "r1.txt"), "w") as f:
+            f.write("left")
+        os._exit(0)
+    t = torch.ones(4)
+    try:
+        dist.all_reduce(t)
+        outcome = "completed"
+    except Exception as e:  # noqa: BLE001 - any collective error is the expected outcome
+        outcome = f"error:{type(e).__name__}"
+    with open(os.path.join(out_dir, "r0.txt"), "w") as f:
+        f.write(outcome)
+    os._exit(0)
+
+
+def test_lost_rank_surfaces_as_error_not_hang():
+    port = _free_port()
+    with tempfile.TemporaryDirectory() as d:
+        ctx = mp.spawn(_failure_worker, args=(2, port, d), nprocs=2, join=False)
+        deadline = time.time() + 120
+        while not ctx.join(timeout=2):
+            if time.time() > deadline:
+                for p in ctx.processes:
+                    if p.is_alive():
+                        p.kill()
+                pytest.fail("a rank hung instead of failing")
+        assert open(os.path.join(d, "r0.txt")).read().startswith("error:")
