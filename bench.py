@@ -225,19 +225,19 @@ def run_ours(args):
     x_cpu = configs.make_x(wl, seed=rank).reshape(-1, wl.hidden_dim)
     x = x_cpu.to(dev, torch.bfloat16)
     M, D = x.shape
-    kg, ku, v, vt, wq, k16, wout = m._weights()
+    kg, ku, v, packed, wq, k16, wout = m._weights()
     kw = dict(base_blocks=wl.base_blocks, top_p=wl.top_p, min_remote=wl.min_remote_blocks,
               max_remote=wl.max_remote_blocks, temperature=wl.temperature, additive=True)
 
     def step(y_out):
-        fsi.kernels.token_forward(x, kg, ku, v, vt, wq, k16, wout, y=y_out, **kw)
+        fsi.kernels.token_forward(x, kg, ku, v, packed, wq, k16, wout, y=y_out, **kw)
 
     y = torch.empty(M, D, dtype=torch.bfloat16, device=dev)
     with torch.no_grad():
         for _ in range(args.warmup):
             step(y)
         # mean active blocks per token of this workload (for the algorithmic FLOP count)
-        _, _, cnt, _ = fsi.kernels.token_forward(x, kg, ku, v, vt, wq, k16, wout, want_routes=True, **kw)
+        _, _, cnt, _ = fsi.kernels.token_forward(x, kg, ku, v, packed, wq, k16, wout, want_routes=True, **kw)
         a_mean = wl.base_blocks + float(cnt.float().mean())
         torch.cuda.synchronize()
 

@@ -31,13 +31,13 @@ SIGNATURES = {
                                   _c_p, _c_p, _c_p, _c_p]),
     "fp_pooled_route": (_c_int, [_c_p, _c_p, _c_p, _c_int, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int, _c_p,
                                  _c_p, _c_p, _c_p, _c_sz, _c_p]),
-    "fp_pack_v": (_c_int, [_c_p, _c_int, _c_int, _c_int, _c_p, _c_p]),
+    "fp_pack_weights": (_c_int, [_c_p, _c_p, _c_p, _c_int, _c_int, _c_int, _c_p, _c_p, _c_p]),
     "fp_token_workspace_size": (_c_sz, [_c_int, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int]),
     "fp_pooled_workspace_size": (_c_sz, [_c_int, _c_i64, _c_int, _c_int, _c_int]),
-    "fp_pattention_token_fwd": (_c_int, [_c_p, _c_i64, _c_int, _c_int, _c_int, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
+    "fp_pattention_token_fwd": (_c_int, [_c_p, _c_i64, _c_int, _c_int, _c_int, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
                                          _c_p, _c_int, _c_f, _c_int, _c_int, _c_f, _c_int, _c_int, _c_int, _c_p,
                                          _c_int, _c_p, _c_p, _c_p, _c_p, _c_sz, _c_p]),
-    "fp_pattention_pooled_fwd": (_c_int, [_c_p, _c_i64, _c_int, _c_int, _c_int, _c_p, _c_p, _c_p, _c_p, _c_p,
+    "fp_pattention_pooled_fwd": (_c_int, [_c_p, _c_i64, _c_int, _c_int, _c_int, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
                                           _c_int, _c_p, _c_p, _c_p, _c_int, _c_p, _c_sz, _c_p]),
     "fp_set_stage_events": (_c_int, [ctypes.POINTER(_c_p), _c_int]),
     "fp_device_error": (_c_int, [_c_p, _c_p, _c_p]),

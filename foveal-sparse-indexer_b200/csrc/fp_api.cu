@@ -23,7 +23,7 @@ struct Carve {
 
 // Token-chunk length of the block CSR: one chunk of x (bf16) is ~32 MB, so that the gate/up tiles of
 // one chunk gather their token rows from L2.
-int csr_chunk(int D) { return std::max(1024, (1 << 24) / std::max(D, 1)); }
+int csr_chunk(int D) { return std::max(1024, (1 << 24) / std::max(D, 1)) / 128 * 128; }
 
 int local_blocks(int NB, int stride, int offset) {
   return offset >= NB ? 0 : (NB - offset + stride - 1) / stride;
@@ -225,22 +225,23 @@ int fp_pooled_route(const void* x, const void* q_proj, const void* block_keys, i
                             mean_scores, st);
 }
 
-int fp_pack_v(const void* v, int dtype, int Np, int D, void* v_t, void* stream) {
-  if (!v || !v_t || Np <= 0 || D <= 0) return FP_ERR_INVALID_ARG;
-  if (dtype != FP_DTYPE_BF16 && dtype != FP_DTYPE_F32) return FP_ERR_UNSUPPORTED;
+int fp_pack_weights(const void* k_gate, const void* k_up, const void* v, int dtype, int Np, int D, void* w_gu,
+                    void* v_t, void* stream) {
+  if (!k_gate || !k_up || !v || !w_gu || !v_t || Np <= 0 || D <= 0) return FP_ERR_INVALID_ARG;
+  if (dtype != FP_DTYPE_BF16) return FP_ERR_UNSUPPORTED;
+  if (Np % kBlock || D % 64) return FP_ERR_UNSUPPORTED;
+  if (!aligned16(k_gate) || !aligned16(k_up) || !aligned16(w_gu)) return FP_ERR_INVALID_ARG;
   int sms;
   FP_TRY(device_info(sms));
+  cudaStream_t st = (cudaStream_t)stream;
+  FP_TRY(launch_pack_gate_up(k_gate, k_up, Np, D, w_gu, st));
   dim3 grid((D + 31) / 32, (Np + 31) / 32), block(32, 8);
-  if (dtype == FP_DTYPE_BF16)
-    transpose_kernel<__nv_bfloat16><<<grid, block, 0, (cudaStream_t)stream>>>(
-        (const __nv_bfloat16*)v, Np, D, (__nv_bfloat16*)v_t);
-  else
-    transpose_kernel<float><<<grid, block, 0, (cudaStream_t)stream>>>((const float*)v, Np, D, (float*)v_t);
+  transpose_kernel<__nv_bfloat16><<<grid, block, 0, st>>>((const __nv_bfloat16*)v, Np, D, (__nv_bfloat16*)v_t);
   return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
 }
 
 int fp_pattention_token_fwd(const void* x, int64_t M, int D, int NB, int dtype, const void* k_gate,
-                            const void* k_up, const void* v, const void* v_t, const void* q_proj,
+                            const void* k_up, const void* v, const void* w_gu, const void* v_t, const void* q_proj,
                             const void* block_keys, const void* out_proj, int base_blocks, float top_p,
                             int min_remote, int max_remote, float temperature, int additive,
                             int block_stride, int block_offset, void* y, int y_f32,
@@ -254,8 +255,7 @@ int fp_pattention_token_fwd(const void* x, int64_t M, int D, int NB, int dtype, 
   if (block_stride < 1 || block_offset < 0 || block_offset >= block_stride) return FP_ERR_INVALID_ARG;
   if (!(temperature > 0.f)) return FP_ERR_INVALID_ARG;
   const bool tc = tensor_path(dtype, D);
-  if (tc && (!v_t || !aligned16(v_t) || !aligned16(x) || !aligned16(k_gate) || !aligned16(k_up)))
-    return FP_ERR_INVALID_ARG;
+  if (tc && (!v_t || !w_gu || !aligned16(v_t) || !aligned16(w_gu) || !aligned16(x))) return FP_ERR_INVALID_ARG;
   if (!tc && D > 32 * 256) return FP_ERR_UNSUPPORTED;
   const int cap = std::max(max_remote, 1);
   const TokenLayout L = token_layout(dtype, M, D, NB, base_blocks, max_remote, block_stride, block_offset);
@@ -299,12 +299,12 @@ int fp_pattention_token_fwd(const void* x, int64_t M, int D, int NB, int dtype, 
   void* h = at<void>(workspace, L.h);
   const int nbl = L.nbl;
   FP_TRY(launch_build_csr(ridx, rcnt, M, base_blocks, cap, block_stride, block_offset, nbl, L.chunk, L.nkey,
-                          kTileN, key_cnt, key_off, key_fill, pair_tok, tiles, L.max_tiles, meta, err, st));
+                          key_cnt, key_off, key_fill, pair_tok, tiles, L.max_tiles, meta, err, st));
   // H is "dense masked": every (token, block) pair the token did not select must read as zero.
   if (cudaMemsetAsync(h, 0, (size_t)M * nbl * kBlock * 2, st) != cudaSuccess) return FP_ERR_CUDA;
   stage_mark(2, st);
   GateUpArgs g{};
-  g.x = x; g.k_gate = k_gate; g.k_up = k_up; g.M = M; g.D = D; g.Np = NB * kBlock;
+  g.x = x; g.w_gu = w_gu; g.M = M; g.D = D; g.Np = NB * kBlock;
   g.tiles = tiles; g.meta = meta; g.key_off = key_off; g.pair_tok = pair_tok;
   g.nbl = nbl; g.stride = block_stride; g.offset = block_offset; g.active = nullptr; g.n_keys = 0;
   g.h = h; g.ldh = (int64_t)nbl * kBlock; g.err = err; g.num_sms = sms;
@@ -320,7 +320,7 @@ int fp_pattention_token_fwd(const void* x, int64_t M, int D, int NB, int dtype, 
 }
 
 int fp_pattention_pooled_fwd(const void* x, int64_t M, int D, int NB, int dtype, const void* k_gate,
-                             const void* k_up, const void* v, const void* v_t, const int32_t* active,
+                             const void* k_up, const void* v, const void* w_gu, const void* v_t, const int32_t* active,
                              int n_active, const float* ctx16, const void* out_proj, void* y, int y_f32,
                              void* workspace, size_t workspace_bytes, void* stream) {
   FP_TRY(check_common(dtype, M, D, NB));
@@ -329,8 +329,7 @@ int fp_pattention_pooled_fwd(const void* x, int64_t M, int D, int NB, int dtype,
     return FP_ERR_INVALID_ARG;
   if (ctx16 && !out_proj) return FP_ERR_INVALID_ARG;
   const bool tc = tensor_path(dtype, D);
-  if (tc && (!v_t || !aligned16(v_t) || !aligned16(x) || !aligned16(k_gate) || !aligned16(k_up)))
-    return FP_ERR_INVALID_ARG;
+  if (tc && (!v_t || !w_gu || !aligned16(v_t) || !aligned16(w_gu) || !aligned16(x))) return FP_ERR_INVALID_ARG;
   if (!tc && D > 32 * 256) return FP_ERR_UNSUPPORTED;
   const PooledLayout L = pooled_layout(dtype, M, D, NB, n_active);
   if (workspace_bytes < L.total) return FP_ERR_WORKSPACE;
@@ -350,7 +349,7 @@ int fp_pattention_pooled_fwd(const void* x, int64_t M, int D, int NB, int dtype,
   }
   void* h = at<void>(workspace, L.h);
   GateUpArgs g{};
-  g.x = x; g.k_gate = k_gate; g.k_up = k_up; g.M = M; g.D = D; g.Np = NB * kBlock;
+  g.x = x; g.w_gu = w_gu; g.M = M; g.D = D; g.Np = NB * kBlock;
   g.tiles = nullptr; g.meta = nullptr; g.key_off = nullptr; g.pair_tok = nullptr;
   g.nbl = n_active; g.stride = 1; g.offset = 0; g.active = active; g.n_keys = n_active;
   g.h = h; g.ldh = (int64_t)n_active * kBlock; g.err = err; g.num_sms = sms;

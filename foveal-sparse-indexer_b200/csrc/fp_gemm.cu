@@ -51,10 +51,10 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
   return ok;
 }
 
-__device__ __forceinline__ void pipe_init(PipeBars* bars, int epi_warps) {
+__device__ __forceinline__ void pipe_init(PipeBars* bars, int epi_warps, int full_count = 1) {
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->full[s], full_count);
       mbar_init(&bars->empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -121,7 +121,7 @@ __device__ __forceinline__ GuTile gu_decode(const GateUpArgs& a, int tile) {
     const int cnt = a.key_off[key + 1] - start;
     t.list = a.pair_tok + start + d.y;
     t.r0 = d.y;
-    t.n = min(kTileN, cnt - d.y);
+    t.n = min(balanced_rows(cnt), cnt - d.y);
   } else {
     const int key = tile % a.n_keys;  // token-tile-major order: concurrent tiles share rows of x
     const int64_t rt = tile / a.n_keys;
@@ -142,66 +142,88 @@ __device__ __forceinline__ int gu_token(const GuTile& t, int i) {
   return t.list ? t.list[i] : (int)(t.r0 + i);
 }
 
-__global__ void __launch_bounds__(kGemmThreads, 1)
-gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_kg,
-              const __grid_constant__ CUtensorMap tm_ku, const GateUpArgs a) {
+constexpr int kGuThreads = 320;  // + warps 6-9: token-row gathers (cp.async)
+constexpr int kGatherThreads = 128;
+
+__global__ void __launch_bounds__(kGuThreads, 1)
+gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+              const GateUpArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = aligned_smem(smem_raw);
   PipeBars* bars = reinterpret_cast<PipeBars*>(smem + kStages * kStageBytes);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool gathered = a.tiles != nullptr;  // token lists (cp.async gathers) or identity rows (TMA box)
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tm_x);
-    tma_prefetch_desc(&tm_kg);
-    tma_prefetch_desc(&tm_ku);
+    tma_prefetch_desc(&tm_w);
   }
-  pipe_init(bars, 4);
+  // full barrier: one expect_tx arrival (TMA) + one arrival per gather thread
+  pipe_init(bars, 4, 1 + kGatherThreads);
   const uint32_t tmem_base = bars->tmem;
-  const int ntiles = a.tiles ? a.meta[0] : a.n_keys * (int)((a.M + kTileN - 1) / kTileN);
+  const int ntiles = gathered ? a.meta[0] : a.n_keys * (int)((a.M + kTileN - 1) / kTileN);
   const int nkb = a.D / kTileK;
   uint32_t issued = 0;
 
   if (warp == 0) {
-    // ---------------- TMA producer: the whole warp issues.  Lane 0 arms the stage barrier, lanes 0-7
-    // load the eight 16-row weight boxes, and every lane issues the row gathers g = lane, lane + 32.
+    // ---------------- TMA producer: packed gate/up weight tile (one 128-row box per stage) and, for
+    // identity token ranges, the x tile (one 256-row box)
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        const GuTile t = gu_decode(a, tile);
+        if (t.n <= 0) continue;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1u;
+          if (!mbar_wait(&bars->empty[s], ph ^ 1u, a.err, kErrWaitEmpty)) { ok = false; break; }
+          uint8_t* As = smem + s * kStageBytes;
+          mbar_arrive_expect_tx(&bars->full[s], kABytes + (gathered ? 0u : kBBytes));
+          tma_load_2d(As, &tm_w, &bars->full[s], kb * kTileK, t.b * 2 * kBlock);
+          if (!gathered) tma_load_2d(As + kABytes, &tm_x, &bars->full[s], kb * kTileK, (int)t.r0);
+        }
+      }
+      issued = it;
+    }
+    __syncwarp();
+  } else if (warp >= 6) {
+    // ---------------- token-row gathers: thread g copies 16-byte chunk (g % 8) of rows g/8 + 16j,
+    // written in the 128-byte swizzle pattern TMA would use (chunk c of row r at c ^ (r % 8))
+    const int g = threadIdx.x - 192;
+    const int chunk = g & 7, row0 = g >> 3;
+    const uint32_t swz = (uint32_t)((chunk ^ (row0 & 7)) << 4);
+    const char* xbytes = reinterpret_cast<const char*>(a.x);
     uint32_t it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
       const GuTile t = gu_decode(a, tile);
       if (t.n <= 0) continue;
       const int npad = (t.n + 15) & ~15;
-      int ids[8];
+      int64_t src[16];
 #pragma unroll
-      for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          const int row = 4 * (lane + 32 * j) + r;
-          ids[4 * j + r] = row < npad ? gu_token(t, row < t.n ? row : t.n - 1) : 0;
-        }
-      const int wq = lane >> 1;
-      const void* wmap = (lane & 1) ? (const void*)&tm_ku : (const void*)&tm_kg;
+      for (int j = 0; j < 16; ++j) {
+        const int r = row0 + 16 * j;
+        const int tok = (gathered && r < npad) ? gu_token(t, r < t.n ? r : t.n - 1) : 0;
+        src[j] = (int64_t)tok * a.D * 2 + chunk * 16;
+      }
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int s = it % kStages;
         const uint32_t ph = (it / kStages) & 1u;
         if (!warp_wait(&bars->empty[s], ph ^ 1u, a.err, kErrWaitEmpty)) { ok = false; break; }
-        uint8_t* As = smem + s * kStageBytes;
-        uint8_t* Bs = As + kABytes;
-        if (lane == 0) mbar_arrive_expect_tx(&bars->full[s], kABytes + (uint32_t)npad * 128u);
-        __syncwarp();
-        const int kc = kb * kTileK;
-        // rows [32q, 32q+16) gate, [32q+16, 32q+32) up of channels 16q..16q+15
-        if (lane < 8)
-          tma_load_2d(As + (32 * wq + 16 * (lane & 1)) * 128, wmap, &bars->full[s], kc, t.b * kBlock + 16 * wq);
+        if (gathered) {
+          const uint32_t bs = smem_u32(smem + s * kStageBytes + kABytes) + swz;
+          const int64_t koff = (int64_t)kb * kTileK * 2;
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int g = lane + 32 * j;
-          if (4 * g < npad)
-            tma_gather4(Bs + 4 * g * 128, &tm_x, &bars->full[s], kc, ids[4 * j], ids[4 * j + 1], ids[4 * j + 2],
-                        ids[4 * j + 3]);
+          for (int j = 0; j < 16; ++j) {
+            const int r = row0 + 16 * j;
+            if (r < npad) cp_async_16(bs + r * 128, xbytes + src[j] + koff);
+          }
         }
+        cp_async_arrive_noinc(&bars->full[s]);
       }
     }
-    issued = it;
+    asm volatile("cp.async.wait_all;" ::: "memory");  // no copy of this thread outlives the CTA
   } else if (warp == 1) {
     // ---------------- MMA issuer (one thread)
     if (lane == 0) {
@@ -222,6 +244,7 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1u;
           if (!mbar_wait(&bars->full[s], ph, a.err, kErrWaitFull)) { ok = false; break; }
+          fence_proxy_async_smem();
           tc_fence_after();
           const uint64_t ad = umma_desc_sw128(smem_u32(smem + s * kStageBytes));
           const uint64_t bd = umma_desc_sw128(smem_u32(smem + s * kStageBytes + kABytes));
@@ -263,9 +286,9 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
           // lane L<16 holds gate(channel 16q+L), lane L+16 holds up(channel 16q+L), columns = tokens
           const uint32_t send = lane < 16 ? v[16 + j] : v[j];
           const float recv = __uint_as_float(__shfl_xor_sync(0xffffffffu, send, 16));
-          const float g = lane < 16 ? __uint_as_float(v[j]) : recv;
+          const float gv = lane < 16 ? __uint_as_float(v[j]) : recv;
           const float u = lane < 16 ? recv : __uint_as_float(v[16 + j]);
-          const float h = g / (1.0f + expf(-g)) * u;
+          const float h = gv / (1.0f + expf(-gv)) * u;
           const int tok = __shfl_sync(0xffffffffu, tok_l, lane < 16 ? j : 16 + j);
           if (tok >= 0) hbase[(int64_t)tok * a.ldh] = __float2bfloat16_rn(h);
         }
@@ -277,6 +300,22 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
     }
   }
   pipe_teardown(bars, issued, a.err);
+}
+
+// Packed gate/up layout of one parameter block b (128 rows): rows 32q .. 32q+15 are gate channels
+// 16q .. 16q+15 and rows 32q+16 .. 32q+31 the up channels 16q .. 16q+15 (q = 0..3), so that after the
+// MMA (A = these rows) each 32-lane TMEM quarter holds the gate and up values of the same 16 channels.
+__global__ void pack_gate_up_kernel(const uint4* __restrict__ kg, const uint4* __restrict__ ku, int64_t rows,
+                                    int vec_per_row, uint4* __restrict__ wgu) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // over 2*rows*vec_per_row
+  if (i >= 2 * rows * vec_per_row) return;
+  const int64_t orow = i / vec_per_row;
+  const int col = (int)(i % vec_per_row);
+  const int64_t b = orow / 128;
+  const int r = (int)(orow % 128);
+  const int q = r >> 5, w = r & 31;
+  const int64_t src_row = b * 64 + 16 * q + (w & 15);
+  wgu[i] = (w < 16 ? kg : ku)[src_row * vec_per_row + col];
 }
 
 // ============================================================================================
@@ -497,16 +536,23 @@ static int set_smem(const void* fn) {
 }
 
 int launch_gateup(const GateUpArgs& a, cudaStream_t st) {
-  CUtensorMap tx, tg, tu;
-  if (!encode_map_2d(&tx, a.x, a.D, a.M, (uint64_t)a.D * 2, kTileK, 1) ||
-      !encode_map_2d(&tg, a.k_gate, a.D, a.Np, (uint64_t)a.D * 2, kTileK, 16) ||
-      !encode_map_2d(&tu, a.k_up, a.D, a.Np, (uint64_t)a.D * 2, kTileK, 16))
+  CUtensorMap tx, tw;
+  if (!encode_map_2d(&tx, a.x, a.D, a.M, (uint64_t)a.D * 2, kTileK, a.tiles ? 1 : kTileN) ||
+      !encode_map_2d(&tw, a.w_gu, a.D, (uint64_t)a.Np * 2, (uint64_t)a.D * 2, kTileK, kTileM))
     return FP_ERR_CUDA;
   static std::once_flag once;
   static int attr = FP_OK;
   std::call_once(once, [] { attr = set_smem((const void*)gateup_kernel); });
   if (attr != FP_OK) return attr;
-  gateup_kernel<<<a.num_sms, kGemmThreads, kGemmSmem, st>>>(tx, tg, tu, a);
+  gateup_kernel<<<a.num_sms, kGuThreads, kGemmSmem, st>>>(tx, tw, a);
+  return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+}
+
+int launch_pack_gate_up(const void* kg, const void* ku, int Np, int D, void* wgu, cudaStream_t st) {
+  const int vec = D * 2 / 16;
+  const int64_t n = 2LL * Np * vec;
+  pack_gate_up_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>((const uint4*)kg, (const uint4*)ku, Np, vec,
+                                                                    (uint4*)wgu);
   return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
 }
 

@@ -30,9 +30,9 @@ int launch_select(const float* scores, int64_t M, int NB, int base, float top_p,
                   float* ctx16, float* stats, cudaStream_t st);
 int launch_convert_keys(const void* k16, int dtype, int n, float* out, cudaStream_t st);
 int launch_build_csr(const int32_t* ridx, const int32_t* rcnt, int64_t M, int base, int cap, int stride,
-                     int offset, int nbl, int chunk, int nkey, int tile_rows, int32_t* key_cnt,
-                     int32_t* key_off, int32_t* key_fill, int32_t* pair_tok, int2* tiles, int max_tiles,
-                     int32_t* meta, int* err, cudaStream_t st);
+                     int offset, int nbl, int chunk, int nkey, int32_t* key_cnt, int32_t* key_off,
+                     int32_t* key_fill, int32_t* pair_tok, int2* tiles, int max_tiles, int32_t* meta, int* err,
+                     cudaStream_t st);
 int launch_colmean(const void* a, int dtype, int64_t M, int D, float* part, float* mean, cudaStream_t st);
 int launch_pooled_topk(const float* mean_vec, const void* wq, const void* k16, int dtype, int D, int NB,
                        int base, int remote, int mode, int32_t* active, float* mean_scores_out,
@@ -41,8 +41,7 @@ int launch_pooled_topk(const float* mean_vec, const void* wq, const void* k16, i
 // ---- gemm.cu (tensor-core path, bf16)
 struct GateUpArgs {
   const void* x;        // [M, D] bf16
-  const void* k_gate;   // [Np, D] bf16
-  const void* k_up;     // [Np, D] bf16
+  const void* w_gu;     // [2 * Np, D] bf16, packed gate/up rows (launch_pack_gate_up)
   int64_t M;
   int D, Np;
   // work list: explicit (tiles/meta from the CSR builder) or implicit (pooled: n_keys x ceil(M/256))
@@ -59,6 +58,15 @@ struct GateUpArgs {
   int num_sms;
 };
 int launch_gateup(const GateUpArgs& a, cudaStream_t st);
+int launch_pack_gate_up(const void* kg, const void* ku, int Np, int D, void* wgu, cudaStream_t st);
+
+// Rows per gate/up tile of a block-CSR key with `cnt` tokens: ceil(cnt / kTileN) tiles of equal size,
+// rounded up to the UMMA N granularity (16).
+__host__ __device__ __forceinline__ int balanced_rows(int cnt) {
+  const int nt = (cnt + kTileN - 1) / kTileN;
+  const int per = nt > 0 ? (cnt + nt - 1) / nt : 0;
+  return (per + 15) & ~15;
+}
 
 struct DownArgs {
   const void* h;        // [M, K] bf16

@@ -109,6 +109,22 @@ __device__ __forceinline__ void tma_gather4(void* dst, const void* map, uint64_t
       : "memory");
 }
 
+// ---------------------------------------------------------------- cp.async (row gathers)
+// 16-byte global -> shared copy through L2 (bypassing L1).
+__device__ __forceinline__ void cp_async_16(uint32_t smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_dst), "l"(gsrc) : "memory");
+}
+// Arrive on `bar` once every cp.async issued so far by this thread has landed; counts as one of the
+// barrier's expected arrivals.
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// Orders shared-memory writes made through the generic proxy (cp.async) before later async-proxy
+// reads (tcgen05.mma operands) issued by this thread.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05 / TMEM
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"

@@ -129,62 +129,117 @@ __device__ __forceinline__ unsigned long long sel_key(float p, int b, bool remot
   return remote ? (((unsigned long long)(__float_as_uint(p) + 1u)) << 32) | lo : (unsigned long long)lo;
 }
 
+__device__ __forceinline__ unsigned long long shfl_xor_u64(unsigned long long v, int m) {
+  const uint32_t lo = __shfl_xor_sync(0xffffffffu, (uint32_t)v, m);
+  const uint32_t hi = __shfl_xor_sync(0xffffffffu, (uint32_t)(v >> 32), m);
+  return ((unsigned long long)hi << 32) | lo;
+}
+
+// Descending bitonic sort of N = 32*E keys held in registers, blocked layout: element i lives in
+// lane i / E, register i % E.  Partners closer than E are in the same lane; farther ones are one
+// shuffle away.  The network is fixed at compile time.
+template <int E>
+__device__ __forceinline__ void warp_bitonic_desc(unsigned long long (&v)[E], int lane) {
+  constexpr int N = 32 * E;
+#pragma unroll
+  for (int k = 2; k <= N; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j < E) {
+#pragma unroll
+        for (int r = 0; r < E; ++r) {
+          const int rp = r ^ j;
+          if (rp > r) {
+            const bool desc = (((lane * E + r) & k) == 0);
+            const unsigned long long a = v[r], b = v[rp];
+            const bool sw = desc ? (a < b) : (a > b);
+            v[r] = sw ? b : a;
+            v[rp] = sw ? a : b;
+          }
+        }
+      } else {
+        const int m = j / E;
+        const bool lower = (lane & m) == 0;
+#pragma unroll
+        for (int r = 0; r < E; ++r) {
+          const bool desc = (((lane * E + r) & k) == 0);
+          const unsigned long long o = shfl_xor_u64(v[r], m);
+          const bool keep_max = (desc == lower);
+          v[r] = keep_max ? (v[r] > o ? v[r] : o) : (v[r] < o ? v[r] : o);
+        }
+      }
+    }
+  }
+}
+
+// One warp per token row of scores.  Softmax over all blocks (core.py:36-43), base mass credit
+// (:104), stable descending order of remote probabilities (:105-108; ties -> lower id), fp64-accumulated
+// cumulative sum (:109), count clamp (:111-119), sorted ids (:121-123).  Optionally the additive-stream
+// context ctx16 = softmax(S/T) . K16 (foveal_pattention.py:339-340).
+template <int E>
 __global__ void __launch_bounds__(kSelWarps * 32)
-select_blocks_kernel(const float* __restrict__ scores, int64_t M, int NB, int nb_pad, int base,
-                     float top_p, int k_min, int k_max, int capacity, float temperature,
-                     int32_t* __restrict__ out_idx, int32_t* __restrict__ out_cnt,
-                     const float* __restrict__ k16f, float* __restrict__ ctx16,
-                     float* __restrict__ stats) {
-  extern __shared__ unsigned long long skeys[];  // [kSelWarps][nb_pad]
+select_blocks_kernel(const float* __restrict__ scores, int64_t M, int NB, int base, float top_p, int k_min,
+                     int k_max, int capacity, float temperature, int32_t* __restrict__ out_idx,
+                     int32_t* __restrict__ out_cnt, const float* __restrict__ k16f,
+                     float* __restrict__ ctx16, float* __restrict__ stats) {
+  constexpr int N = 32 * E;
+  __shared__ float spb[kSelWarps][N];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int64_t tok = (int64_t)blockIdx.x * kSelWarps + warp;
   if (tok >= M) return;
-  unsigned long long* keys = skeys + (size_t)warp * nb_pad;
-  float* pbuf = reinterpret_cast<float*>(skeys + (size_t)kSelWarps * nb_pad) + (size_t)warp * nb_pad;
+  float* pbuf = spb[warp];
   const float* srow = scores + tok * NB;
 
-  // softmax (core.py:36-43): max, exp(s - max), sum, divide
+  // blocked layout: lane owns blocks lane*E .. lane*E+E-1
+  float p[E];
   float mx = -INFINITY;
-  for (int b = lane; b < NB; b += 32) {
-    float s = srow[b];
-    if (temperature != 1.0f) s = __fdiv_rn(s, temperature);
-    pbuf[b] = s;
-    mx = fmaxf(mx, s);
+#pragma unroll
+  for (int r = 0; r < E; ++r) {
+    const int b = lane * E + r;
+    float sv = -INFINITY;
+    if (b < NB) {
+      sv = srow[b];
+      if (temperature != 1.0f) sv = __fdiv_rn(sv, temperature);
+    }
+    p[r] = sv;
+    mx = fmaxf(mx, sv);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if (!isfinite(mx)) mx = 0.f;
   float sum = 0.f;
-  for (int b = lane; b < NB; b += 32) {
-    const float e = expf(pbuf[b] - mx);
-    pbuf[b] = e;
+#pragma unroll
+  for (int r = 0; r < E; ++r) {
+    const int b = lane * E + r;
+    const float e = b < NB ? expf(p[r] - mx) : 0.f;
+    p[r] = e;
     sum += e;
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
   const float denom = fmaxf(sum, 1e-20f);
-  __syncwarp();
-  for (int b = lane; b < nb_pad; b += 32) {
-    if (b < NB) {
-      const float p = __fdiv_rn(pbuf[b], denom);
-      pbuf[b] = p;
-      keys[b] = sel_key(p, b, b >= base);
-    } else {
-      keys[b] = 0ull;
-    }
+  unsigned long long key[E];
+#pragma unroll
+  for (int r = 0; r < E; ++r) {
+    const int b = lane * E + r;
+    p[r] = __fdiv_rn(p[r], denom);
+    key[r] = b < NB ? sel_key(p[r], b, b >= base) : 0ull;
+    pbuf[b] = p[r];
   }
   __syncwarp();
 
-  // additive-stream context (foveal_pattention.py:339-340): ctx[j] = sum_b p[b] K16[b][j]
   if (ctx16) {
     float c[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) c[j] = 0.f;
-    for (int b = lane; b < NB; b += 32) {
-      const float p = pbuf[b];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) c[j] = fmaf(p, k16f[b * 16 + j], c[j]);
+    for (int r = 0; r < E; ++r) {
+      const int b = lane * E + r;
+      if (b < NB) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) c[j] = fmaf(p[r], k16f[b * 16 + j], c[j]);
+      }
     }
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
@@ -202,33 +257,25 @@ select_blocks_kernel(const float* __restrict__ scores, int64_t M, int NB, int nb
   }
   if (out_idx == nullptr) return;  // context-only mode
 
-  // bitonic sort, descending by key
-  for (int k = 2; k <= nb_pad; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int idx = lane; idx < (nb_pad >> 1); idx += 32) {
-        const int i = 2 * j * (idx / j) + (idx % j);
-        const int l = i + j;
-        const unsigned long long a = keys[i], bkey = keys[l];
-        const bool desc = (i & k) == 0;
-        if (desc ? (a < bkey) : (a > bkey)) {
-          keys[i] = bkey;
-          keys[l] = a;
-        }
-      }
-      __syncwarp();
-    }
-  }
+  // base (local) mass (core.py:104): sequential over the base blocks
+  float local_mass = 0.f;
+  if (lane == 0)
+    for (int b = 0; b < base && b < NB; ++b) local_mass += pbuf[b];
 
-  // remote_indices = sorted ids (core.py:121-123); entries past NB are zero padding
+  warp_bitonic_desc<E>(key, lane);
+
   int32_t* orow = out_idx + tok * capacity;
-  for (int i = lane; i < capacity; i += 32) {
-    orow[i] = i < NB ? (int32_t)(0xFFFFFFFFu - (uint32_t)(keys[i] & 0xFFFFFFFFull)) : 0;
+#pragma unroll
+  for (int r = 0; r < E; ++r) {
+    const int i = lane * E + r;
+    if (i < capacity) orow[i] = i < NB ? (int32_t)(0xFFFFFFFFu - (uint32_t)(key[r] & 0xFFFFFFFFull)) : 0;
+    const uint32_t hi = (uint32_t)(key[r] >> 32);
+    pbuf[i] = hi ? __uint_as_float(hi - 1u) : 0.f;  // sorted, clamped probabilities
   }
+  for (int i = N + lane; i < capacity; i += 32) orow[i] = 0;
+  __syncwarp();
 
   if (lane == 0) {
-    // base (local) mass (core.py:104), target (:111), needed/count (:115-119)
-    float local_mass = 0.f;
-    for (int b = 0; b < base && b < NB; ++b) local_mass += pbuf[b];
     float target = top_p - local_mass;
     target = target > 0.f ? target : 0.f;
     const int available = NB - base;
@@ -240,9 +287,7 @@ select_blocks_kernel(const float* __restrict__ scores, int64_t M, int NB, int nb
         double acc = 0.0;
         int n = 0;
         for (; n < X; ++n) {
-          const uint32_t hi = (uint32_t)(keys[n] >> 32);
-          const float p = hi ? __uint_as_float(hi - 1u) : 0.f;  // base/pad entries clamp to 0
-          acc += (double)p;
+          acc += (double)pbuf[n];
           if ((float)acc >= target) break;
         }
         needed = n + 1;  // #(cum < target) + 1; saturates at X + 1 when never reached within X
@@ -274,25 +319,36 @@ __device__ __forceinline__ int token_block(int s, int base, const int32_t* ridx,
   return r < cnt ? ridx[r] : -1;
 }
 
-__global__ void csr_count_kernel(const int32_t* __restrict__ ridx, const int32_t* __restrict__ rcnt,
-                                 int64_t M, int base, int cap, int stride, int offset, int nbl,
-                                 int chunk, int32_t* __restrict__ key_cnt) {
+// One CTA per kCsrTokens consecutive tokens (all inside one token chunk): block counts are gathered in
+// a shared-memory histogram and folded into the global counts with one atomic per touched key.
+constexpr int kCsrTokens = 128;
+
+__global__ void __launch_bounds__(256)
+csr_count_kernel(const int32_t* __restrict__ ridx, const int32_t* __restrict__ rcnt, int64_t M, int base,
+                 int cap, int stride, int offset, int nbl, int chunk, int32_t* __restrict__ key_cnt) {
+  extern __shared__ int32_t hist[];  // [nbl]
+  for (int i = threadIdx.x; i < nbl; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  const int64_t t0 = (int64_t)blockIdx.x * kCsrTokens;
   const int slots = base + cap;
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= M * slots) return;
-  const int64_t t = i / slots;
-  const int s = (int)(i % slots);
-  const int b = token_block(s, base, ridx + t * cap, cap, rcnt[t]);
-  if (b < 0 || (b % stride) != offset) return;
-  const int key = (int)(t / chunk) * nbl + b / stride;
-  atomicAdd(&key_cnt[key], 1);
+  const int64_t t_end = min(M, t0 + kCsrTokens);
+  for (int64_t i = (int64_t)threadIdx.x; i < (t_end - t0) * slots; i += blockDim.x) {
+    const int64_t t = t0 + i / slots;
+    const int b = token_block((int)(i % slots), base, ridx + t * cap, cap, rcnt[t]);
+    if (b >= 0 && (b % stride) == offset) atomicAdd(&hist[b / stride], 1);
+  }
+  __syncthreads();
+  const int kbase = (int)(t0 / chunk) * nbl;
+  for (int k = threadIdx.x; k < nbl; k += blockDim.x)
+    if (hist[k]) atomicAdd(&key_cnt[kbase + k], hist[k]);
 }
 
-// Single CTA: exclusive scan of key counts, tile list (key, first row) with <= tile_rows rows each.
+// Single CTA: exclusive scan of key counts and the tile list (key, first row); the tiles of one key
+// have equal size (balanced_rows).
 __global__ void __launch_bounds__(1024)
-csr_scan_kernel(const int32_t* __restrict__ key_cnt, int nkey, int tile_rows,
-                int32_t* __restrict__ key_off, int32_t* __restrict__ key_fill,
-                int2* __restrict__ tiles, int max_tiles, int32_t* __restrict__ meta, int* err) {
+csr_scan_kernel(const int32_t* __restrict__ key_cnt, int nkey, int32_t* __restrict__ key_off,
+                int32_t* __restrict__ key_fill, int2* __restrict__ tiles, int max_tiles,
+                int32_t* __restrict__ meta, int* err) {
   __shared__ int s_pairs[1024], s_tiles[1024];
   const int tid = threadIdx.x;
   const int per = (nkey + 1023) / 1024;
@@ -300,7 +356,7 @@ csr_scan_kernel(const int32_t* __restrict__ key_cnt, int nkey, int tile_rows,
   int pairs = 0, ntile = 0;
   for (int k = k0; k < k1; ++k) {
     pairs += key_cnt[k];
-    ntile += (key_cnt[k] + tile_rows - 1) / tile_rows;
+    ntile += (key_cnt[k] + kTileN - 1) / kTileN;
   }
   s_pairs[tid] = pairs;
   s_tiles[tid] = ntile;
@@ -318,7 +374,8 @@ csr_scan_kernel(const int32_t* __restrict__ key_cnt, int nkey, int tile_rows,
     const int c = key_cnt[k];
     key_off[k] = poff;
     key_fill[k] = 0;
-    for (int r = 0; r < c; r += tile_rows) {
+    const int rows = balanced_rows(c);
+    for (int r = 0; r < c; r += rows) {
       if (toff < max_tiles) tiles[toff] = make_int2(k, r);
       ++toff;
     }
@@ -333,20 +390,41 @@ csr_scan_kernel(const int32_t* __restrict__ key_cnt, int nkey, int tile_rows,
   }
 }
 
-__global__ void csr_fill_kernel(const int32_t* __restrict__ ridx, const int32_t* __restrict__ rcnt,
-                                int64_t M, int base, int cap, int stride, int offset, int nbl, int chunk,
-                                const int32_t* __restrict__ key_off, int32_t* __restrict__ key_fill,
-                                int32_t* __restrict__ pair_tok) {
+// Same partition as csr_count_kernel: local histogram, one global reservation per key, then the
+// scatter of token ids with shared-memory positions.
+__global__ void __launch_bounds__(256)
+csr_fill_kernel(const int32_t* __restrict__ ridx, const int32_t* __restrict__ rcnt, int64_t M, int base,
+                int cap, int stride, int offset, int nbl, int chunk, const int32_t* __restrict__ key_off,
+                int32_t* __restrict__ key_fill, int32_t* __restrict__ pair_tok) {
+  extern __shared__ int32_t sh[];  // hist[nbl], start[nbl]
+  int32_t* hist = sh;
+  int32_t* start = sh + nbl;
+  for (int i = threadIdx.x; i < nbl; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  const int64_t t0 = (int64_t)blockIdx.x * kCsrTokens;
   const int slots = base + cap;
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= M * slots) return;
-  const int64_t t = i / slots;
-  const int s = (int)(i % slots);
-  const int b = token_block(s, base, ridx + t * cap, cap, rcnt[t]);
-  if (b < 0 || (b % stride) != offset) return;
-  const int key = (int)(t / chunk) * nbl + b / stride;
-  const int pos = atomicAdd(&key_fill[key], 1);
-  pair_tok[key_off[key] + pos] = (int32_t)t;
+  const int64_t t_end = min(M, t0 + kCsrTokens);
+  const int64_t n = (t_end - t0) * slots;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const int64_t t = t0 + i / slots;
+    const int b = token_block((int)(i % slots), base, ridx + t * cap, cap, rcnt[t]);
+    if (b >= 0 && (b % stride) == offset) atomicAdd(&hist[b / stride], 1);
+  }
+  __syncthreads();
+  const int kbase = (int)(t0 / chunk) * nbl;
+  for (int k = threadIdx.x; k < nbl; k += blockDim.x) {
+    start[k] = hist[k] ? key_off[kbase + k] + atomicAdd(&key_fill[kbase + k], hist[k]) : 0;
+    hist[k] = 0;
+  }
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const int64_t t = t0 + i / slots;
+    const int b = token_block((int)(i % slots), base, ridx + t * cap, cap, rcnt[t]);
+    if (b >= 0 && (b % stride) == offset) {
+      const int k = b / stride;
+      pair_tok[start[k] + atomicAdd(&hist[k], 1)] = (int32_t)t;
+    }
+  }
 }
 
 // --------------------------------------------------------------------------------------------
@@ -482,16 +560,19 @@ int launch_select(const float* scores, int64_t M, int NB, int base, float top_p,
                   int capacity, float temperature, int32_t* idx, int32_t* cnt, const float* k16f,
                   float* ctx16, float* stats, cudaStream_t st) {
   if (M <= 0) return FP_OK;
-  const int nb_pad = pow2_at_least(NB);
-  const size_t smem = (size_t)kSelWarps * nb_pad * (sizeof(unsigned long long) + sizeof(float));
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(select_blocks_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-    return FP_ERR_CUDA;
   const int blocks = (int)((M + kSelWarps - 1) / kSelWarps);
-  select_blocks_kernel<<<blocks, kSelWarps * 32, smem, st>>>(scores, M, NB, nb_pad, base, top_p, k_min,
-                                                              k_max, capacity, temperature, idx, cnt,
-                                                              k16f, ctx16, stats);
-  return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+  auto go = [&](auto kern) {
+    kern<<<blocks, kSelWarps * 32, 0, st>>>(scores, M, NB, base, top_p, k_min, k_max, capacity, temperature,
+                                            idx, cnt, k16f, ctx16, stats);
+    return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+  };
+  if (NB <= 32) return go(select_blocks_kernel<1>);
+  if (NB <= 64) return go(select_blocks_kernel<2>);
+  if (NB <= 128) return go(select_blocks_kernel<4>);
+  if (NB <= 256) return go(select_blocks_kernel<8>);
+  if (NB <= 512) return go(select_blocks_kernel<16>);
+  if (NB <= 1024) return go(select_blocks_kernel<32>);
+  return FP_ERR_UNSUPPORTED;
 }
 
 int launch_convert_keys(const void* k16, int dtype, int n, float* out, cudaStream_t st) {
@@ -500,18 +581,19 @@ int launch_convert_keys(const void* k16, int dtype, int n, float* out, cudaStrea
 }
 
 int launch_build_csr(const int32_t* ridx, const int32_t* rcnt, int64_t M, int base, int cap, int stride,
-                     int offset, int nbl, int chunk, int nkey, int tile_rows, int32_t* key_cnt,
-                     int32_t* key_off, int32_t* key_fill, int32_t* pair_tok, int2* tiles, int max_tiles,
-                     int32_t* meta, int* err, cudaStream_t st) {
+                     int offset, int nbl, int chunk, int nkey, int32_t* key_cnt, int32_t* key_off,
+                     int32_t* key_fill, int32_t* pair_tok, int2* tiles, int max_tiles, int32_t* meta, int* err,
+                     cudaStream_t st) {
+  if (chunk % kCsrTokens) return FP_ERR_INVALID_ARG;
   if (cudaMemsetAsync(key_cnt, 0, sizeof(int32_t) * nkey, st) != cudaSuccess) return FP_ERR_CUDA;
-  const int64_t n = M * (int64_t)(base + cap);
-  const int blocks = (int)((n + 255) / 256);
-  if (n > 0)
-    csr_count_kernel<<<blocks, 256, 0, st>>>(ridx, rcnt, M, base, cap, stride, offset, nbl, chunk, key_cnt);
-  csr_scan_kernel<<<1, 1024, 0, st>>>(key_cnt, nkey, tile_rows, key_off, key_fill, tiles, max_tiles, meta, err);
-  if (n > 0)
-    csr_fill_kernel<<<blocks, 256, 0, st>>>(ridx, rcnt, M, base, cap, stride, offset, nbl, chunk, key_off,
-                                            key_fill, pair_tok);
+  const int blocks = (int)((M + kCsrTokens - 1) / kCsrTokens);
+  if (blocks > 0)
+    csr_count_kernel<<<blocks, 256, nbl * sizeof(int32_t), st>>>(ridx, rcnt, M, base, cap, stride, offset, nbl,
+                                                                chunk, key_cnt);
+  csr_scan_kernel<<<1, 1024, 0, st>>>(key_cnt, nkey, key_off, key_fill, tiles, max_tiles, meta, err);
+  if (blocks > 0)
+    csr_fill_kernel<<<blocks, 256, 2 * nbl * sizeof(int32_t), st>>>(ridx, rcnt, M, base, cap, stride, offset, nbl,
+                                                                    chunk, key_off, key_fill, pair_tok);
   return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
 }
 

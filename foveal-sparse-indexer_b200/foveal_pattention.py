@@ -104,8 +104,8 @@ class FovealPattentionMLP(nn.Module):
         self._cached_ku = None
         self._cached_v = None
         self._cached_active_blocks: Optional[Tensor] = None
-        self._vt = None
-        self._vt_key = None
+        self._packed_w = None
+        self._packed_key = None
         self._shard = None  # (rank, world, group) when parameter blocks are sharded
         self.reset_parameters()
 
@@ -161,18 +161,19 @@ class FovealPattentionMLP(nn.Module):
         return s.reshape(*shape[:-1], self.num_blocks)
 
     # ------------------------------------------------------------------ helpers
-    def _packed_v(self) -> Optional[Tensor]:
-        """V^T for the tensor-core path, rebuilt whenever ``v`` is replaced or modified in place."""
+    def _packed(self):
+        """Tensor-core weight layouts (packed gate/up rows, V^T), rebuilt whenever k_gate, k_up or v
+        is replaced or modified in place; None for fp32 models (CUDA-core path)."""
         if self.v.dtype != torch.bfloat16 or self.hidden_dim % 64:
             return None
-        key = (self.v.data_ptr(), self.v._version, self.v.device)
-        if self._vt is None or self._vt_key != key:
-            self._vt = kernels.pack_v(self.v.detach())
-            self._vt_key = key
-        return self._vt
+        key = tuple((p.data_ptr(), p._version) for p in (self.k_gate, self.k_up, self.v)) + (self.v.device,)
+        if self._packed_w is None or self._packed_key != key:
+            self._packed_w = kernels.pack_weights(self.k_gate.detach(), self.k_up.detach(), self.v.detach())
+            self._packed_key = key
+        return self._packed_w
 
     def _weights(self):
-        return (self.k_gate.detach(), self.k_up.detach(), self.v.detach(), self._packed_v(),
+        return (self.k_gate.detach(), self.k_up.detach(), self.v.detach(), self._packed(),
                 self.q_proj_16d.weight.detach(), self.block_keys_16d.detach(), self.out_proj_16d.weight.detach())
 
     def _attach_no_grad(self, y: Tensor, x: Tensor) -> Tensor:
@@ -200,11 +201,11 @@ class FovealPattentionMLP(nn.Module):
         return y
 
     def _forward_pooled(self, x2d: Tensor, orig_shape, return_router_info: bool):
-        kg, ku, v, vt, wq, k16, wout = self._weights()
+        kg, ku, v, packed, wq, k16, wout = self._weights()
         is_prefill = (len(orig_shape) >= 3 and orig_shape[-2] > 1) or (
             len(orig_shape) == 2 and orig_shape[0] > 1 and self.training)
         if not self.training and self._cached_active_blocks is not None and not is_prefill:
-            y = kernels.pooled_forward(x2d, kg, ku, v, vt, self._cached_active_blocks)
+            y = kernels.pooled_forward(x2d, kg, ku, v, packed, self._cached_active_blocks)
             return y, {"active_blocks": self._cached_active_blocks}
         scores = None
         ctx = None
@@ -222,7 +223,7 @@ class FovealPattentionMLP(nn.Module):
                                                  remote_blocks=self.remote_blocks, mode=0)
                 self.set_active_blocks(active)
             active = self._cached_active_blocks
-        y = kernels.pooled_forward(x2d, kg, ku, v, vt, active, ctx16=ctx, out_proj=wout if ctx is not None else None)
+        y = kernels.pooled_forward(x2d, kg, ku, v, packed, active, ctx16=ctx, out_proj=wout if ctx is not None else None)
         info = {}
         if return_router_info:
             if scores is None:
@@ -232,13 +233,13 @@ class FovealPattentionMLP(nn.Module):
         return y, info
 
     def _forward_token(self, x2d: Tensor, return_router_info: bool):
-        kg, ku, v, vt, wq, k16, wout = self._weights()
+        kg, ku, v, packed, wq, k16, wout = self._weights()
         if self._shard is not None:
             from .sharding import sharded_token_forward
             y, ridx, cnt, S = sharded_token_forward(self, x2d, want_routes=return_router_info)
         else:
             y, ridx, cnt, S = kernels.token_forward(
-                x2d, kg, ku, v, vt, wq, k16, wout, base_blocks=self.base_blocks, top_p=self.top_p,
+                x2d, kg, ku, v, packed, wq, k16, wout, base_blocks=self.base_blocks, top_p=self.top_p,
                 min_remote=self.min_remote_blocks, max_remote=self.max_remote_blocks,
                 temperature=self.temperature, additive=True, want_routes=return_router_info)
         info = {}

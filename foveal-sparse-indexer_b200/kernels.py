@@ -86,23 +86,27 @@ def pooled_route(x2d: Optional[torch.Tensor], q_proj: torch.Tensor, block_keys: 
     return active, mean_scores
 
 
-def pack_v(v: torch.Tensor) -> torch.Tensor:
-    """V^T [D, Np] for the tensor-core path (derived layout of FovealPattentionMLP.v)."""
-    dev = require_cuda(v)
-    v = contig(v.detach())
+def pack_weights(k_gate: torch.Tensor, k_up: torch.Tensor, v: torch.Tensor):
+    """Derived tensor-core layouts (``fp_pack_weights``): packed gate/up rows w_gu [2 Np, D] and
+    V^T [D, Np].  bf16 only."""
+    dev = require_cuda(k_gate, k_up, v)
+    k_gate, k_up, v = contig(k_gate.detach()), contig(k_up.detach()), contig(v.detach())
     Np, D = v.shape
+    w_gu = torch.empty(2 * Np, D, dtype=v.dtype, device=dev)
     vt = torch.empty(D, Np, dtype=v.dtype, device=dev)
-    rc = _lib.load().fp_pack_v(ptr(v), dtype_code(v.dtype), Np, D, ptr(vt), stream_handle(dev))
-    check(rc, "fp_pack_v")
-    return vt
+    rc = _lib.load().fp_pack_weights(ptr(k_gate), ptr(k_up), ptr(v), dtype_code(v.dtype), Np, D, ptr(w_gu),
+                                     ptr(vt), stream_handle(dev))
+    check(rc, "fp_pack_weights")
+    return w_gu, vt
 
 
-def token_forward(x2d, k_gate, k_up, v, v_t, q_proj, block_keys, out_proj, *, base_blocks: int,
+def token_forward(x2d, k_gate, k_up, v, packed, q_proj, block_keys, out_proj, *, base_blocks: int,
                   top_p: float, min_remote: int, max_remote: int, temperature: float = 1.0,
                   additive: bool = True, block_stride: int = 1, block_offset: int = 0,
                   out_f32: bool = False, want_routes: bool = False, y: Optional[torch.Tensor] = None):
     """Per-token routed forward, one ``fp_pattention_token_fwd`` call.
 
+    ``packed`` is (w_gu, v_t) from :func:`pack_weights` (bf16) or None (fp32 CUDA-core path).
     Returns (y [M, D], remote_indices or None, remote_counts or None, scores or None)."""
     dev = require_cuda(x2d, k_gate, k_up, v, q_proj, block_keys)
     dtt = x2d.dtype
@@ -116,6 +120,7 @@ def token_forward(x2d, k_gate, k_up, v, v_t, q_proj, block_keys, out_proj, *, ba
     if y is None:
         y = torch.empty(M, D, dtype=torch.float32 if out_f32 else dtt, device=dev)
     cap = max(int(max_remote), 1)
+    w_gu, v_t = packed if packed is not None else (None, None)
     ridx = cnt = S = None
     if want_routes:
         ridx = torch.empty(M, cap, dtype=torch.int32, device=dev)
@@ -125,7 +130,7 @@ def token_forward(x2d, k_gate, k_up, v, v_t, q_proj, block_keys, out_proj, *, ba
     nbytes = lib.fp_token_workspace_size(dt, M, D, NB, int(base_blocks), int(max_remote), int(block_stride))
     ws = _lib.workspace(dev, nbytes)
     rc = lib.fp_pattention_token_fwd(
-        ptr(x2d), M, D, NB, dt, ptr(k_gate), ptr(k_up), ptr(v), ptr(v_t), ptr(q_proj), ptr(block_keys),
+        ptr(x2d), M, D, NB, dt, ptr(k_gate), ptr(k_up), ptr(v), ptr(w_gu), ptr(v_t), ptr(q_proj), ptr(block_keys),
         ptr(out_proj), int(base_blocks), float(top_p), int(min_remote), int(max_remote), float(temperature),
         1 if additive else 0, int(block_stride), int(block_offset), ptr(y), 1 if out_f32 else 0, ptr(ridx),
         ptr(cnt), ptr(S), ptr(ws), ws.numel(), stream_handle(dev))
@@ -133,8 +138,9 @@ def token_forward(x2d, k_gate, k_up, v, v_t, q_proj, block_keys, out_proj, *, ba
     return y, ridx, cnt, S
 
 
-def pooled_forward(x2d, k_gate, k_up, v, v_t, active, *, ctx16=None, out_proj=None, out_f32: bool = False):
-    """Forward over one shared active set (``fp_pattention_pooled_fwd``); y [M, D]."""
+def pooled_forward(x2d, k_gate, k_up, v, packed, active, *, ctx16=None, out_proj=None, out_f32: bool = False):
+    """Forward over one shared active set (``fp_pattention_pooled_fwd``); y [M, D].  ``packed`` as in
+    :func:`token_forward`."""
     dev = require_cuda(x2d, k_gate, k_up, v, active)
     dtt = x2d.dtype
     dt = dtype_code(dtt)
@@ -149,7 +155,8 @@ def pooled_forward(x2d, k_gate, k_up, v, v_t, active, *, ctx16=None, out_proj=No
     n_active = active.numel()
     nbytes = lib.fp_pooled_workspace_size(dt, M, D, NB, n_active)
     ws = _lib.workspace(dev, nbytes)
-    rc = lib.fp_pattention_pooled_fwd(ptr(x2d), M, D, NB, dt, ptr(k_gate), ptr(k_up), ptr(v), ptr(v_t),
+    w_gu, v_t = packed if packed is not None else (None, None)
+    rc = lib.fp_pattention_pooled_fwd(ptr(x2d), M, D, NB, dt, ptr(k_gate), ptr(k_up), ptr(v), ptr(w_gu), ptr(v_t),
                                       ptr(active), n_active, ptr(ctx16), ptr(out_proj), ptr(y),
                                       1 if out_f32 else 0, ptr(ws), ws.numel(), stream_handle(dev))
     check(rc, "fp_pattention_pooled_fwd")

@@ -37,9 +37,9 @@ def owned_blocks(num_blocks: int, rank: int, world: int):
 
 
 def _cuda_partial(module, x2d, world: int, rank: int, additive: bool, want_routes: bool):
-    kg, ku, v, vt, wq, k16, wout = module._weights()
+    kg, ku, v, packed, wq, k16, wout = module._weights()
     return kernels.token_forward(
-        x2d, kg, ku, v, vt, wq, k16, wout, base_blocks=module.base_blocks, top_p=module.top_p,
+        x2d, kg, ku, v, packed, wq, k16, wout, base_blocks=module.base_blocks, top_p=module.top_p,
         min_remote=module.min_remote_blocks, max_remote=module.max_remote_blocks,
         temperature=module.temperature, additive=additive, block_stride=world, block_offset=rank,
         out_f32=True, want_routes=want_routes)

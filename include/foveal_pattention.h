@@ -95,10 +95,15 @@ FP_API int fp_pooled_route(const void* x, const void* q_proj, const void* block_
                     void* stream);
 
 /*
- * V layout for the tensor-core path: v_t[D, Np] = v[Np, D]^T (FovealPattentionMLP.v, which stores
- * W_down^T, foveal_pattention.py:88 and :169).  Call once per weight update; bf16 only.
+ * Weight layouts for the tensor-core path (bf16), derived from the reference parameters
+ * (FovealPattentionMLP.k_gate / k_up / v, foveal_pattention.py:86-88; v stores W_down^T, :169):
+ *   w_gu [2 * Np, D]: per parameter block b, 128 rows; rows 32q..32q+15 = k_gate channels 16q..16q+15
+ *                     and rows 32q+16..32q+31 = k_up channels 16q..16q+15 of the block (q = 0..3)
+ *   v_t  [D, Np]:     v transposed
+ * Call once per weight update.  Np % 64 == 0, D % 64 == 0.
  */
-FP_API int fp_pack_v(const void* v, int dtype, int Np, int D, void* v_t, void* stream);
+FP_API int fp_pack_weights(const void* k_gate, const void* k_up, const void* v, int dtype, int Np, int D,
+                           void* w_gu, void* v_t, void* stream);
 
 /* Workspace bytes of fp_pattention_token_fwd (block_stride = 1 unless blocks are sharded). */
 FP_API size_t fp_token_workspace_size(int dtype, int64_t M, int D, int NB, int base_blocks, int max_remote,
@@ -112,8 +117,9 @@ FP_API size_t fp_pooled_workspace_size(int dtype, int64_t M, int D, int NB, int 
  * composition compute_router_scores -> select_blocks(non-causal, base) -> per-token Pattention over
  * base ∪ selected (pattention_triton.py:280-311, "swiglu", block_n = 64) -> + out_proj_16d(softmax(S/T) K_16)
  * (foveal_pattention.py:257-262, core.py:46-160, foveal_pattention.py:338-342).
- *   x [M, D]; k_gate, k_up, v [Np, D] (Np = NB * 64); v_t [D, Np] from fp_pack_v (bf16 path, may be
- *   NULL for fp32); q_proj [16, D]; block_keys [NB, 16]; out_proj [D, 16]; all in `dtype`.
+ *   x [M, D]; k_gate, k_up, v [Np, D] (Np = NB * 64); w_gu [2 Np, D] and v_t [D, Np] from
+ *   fp_pack_weights (bf16 tensor-core path; may be NULL for fp32); q_proj [16, D]; block_keys [NB, 16];
+ *   out_proj [D, 16]; all in `dtype`.
  *   additive: 1 adds the additive stream.
  *   block_stride / block_offset: this call computes only blocks b with b % block_stride == block_offset
  *   (parameter-block sharding across GPUs; 1 / 0 = all blocks).  Routing still covers all blocks.
@@ -122,7 +128,7 @@ FP_API size_t fp_pooled_workspace_size(int dtype, int64_t M, int D, int NB, int 
  *   outputs (NULL = keep inside the workspace).
  */
 FP_API int fp_pattention_token_fwd(const void* x, int64_t M, int D, int NB, int dtype, const void* k_gate,
-                            const void* k_up, const void* v, const void* v_t, const void* q_proj,
+                            const void* k_up, const void* v, const void* w_gu, const void* v_t, const void* q_proj,
                             const void* block_keys, const void* out_proj, int base_blocks, float top_p,
                             int min_remote, int max_remote, float temperature, int additive,
                             int block_stride, int block_offset, void* y, int y_f32,
@@ -137,7 +143,7 @@ FP_API int fp_pattention_token_fwd(const void* x, int64_t M, int D, int NB, int 
  *   with capacity 0) or NULL; other tensors as in fp_pattention_token_fwd.
  */
 FP_API int fp_pattention_pooled_fwd(const void* x, int64_t M, int D, int NB, int dtype, const void* k_gate,
-                             const void* k_up, const void* v, const void* v_t, const int32_t* active,
+                             const void* k_up, const void* v, const void* w_gu, const void* v_t, const int32_t* active,
                              int n_active, const float* ctx16, const void* out_proj, void* y, int y_f32,
                              void* workspace, size_t workspace_bytes, void* stream);
 

@@ -217,11 +217,11 @@ def test_block_shards_sum_to_full():
     w = configs.make_weights(wl)
     x2d = configs.make_x(wl).reshape(-1, wl.hidden_dim)[:1000].contiguous().to(DEV, torch.bfloat16)
     m = module_for(wl, w)
-    kg, ku, v, vt, wq, k16, wout = m._weights()
+    kg, ku, v, packed, wq, k16, wout = m._weights()
     kw = dict(base_blocks=wl.base_blocks, top_p=wl.top_p, min_remote=wl.min_remote_blocks,
               max_remote=wl.max_remote_blocks)
-    full, _, _, _ = fsi.kernels.token_forward(x2d, kg, ku, v, vt, wq, k16, wout, out_f32=True, **kw)
-    parts = [fsi.kernels.token_forward(x2d, kg, ku, v, vt, wq, k16, wout, out_f32=True, block_stride=4,
+    full, _, _, _ = fsi.kernels.token_forward(x2d, kg, ku, v, packed, wq, k16, wout, out_f32=True, **kw)
+    parts = [fsi.kernels.token_forward(x2d, kg, ku, v, packed, wq, k16, wout, out_f32=True, block_stride=4,
                                        block_offset=r, additive=(r == 0), **kw)[0] for r in range(4)]
     assert rel_err(sum(parts).cpu(), full.cpu()) < 1e-5
 
@@ -232,8 +232,8 @@ def test_all_blocks_active_equals_dense():
     x2d = configs.make_x(wl).reshape(-1, wl.hidden_dim)[:300].contiguous()
     m = module_for(wl, w, routing="pooled", remote_blocks=wl.num_blocks - wl.base_blocks)
     active = torch.arange(wl.num_blocks, dtype=torch.int32, device=DEV)
-    kg, ku, v, vt, *_ = m._weights()
-    y = fsi.kernels.pooled_forward(x2d.to(DEV, torch.bfloat16), kg, ku, v, vt, active)
+    kg, ku, v, packed, *_ = m._weights()
+    y = fsi.kernels.pooled_forward(x2d.to(DEV, torch.bfloat16), kg, ku, v, packed, active)
     check_y(y.cpu(), oracle.dense_swiglu(x2d, w), "bf16")
 
 
