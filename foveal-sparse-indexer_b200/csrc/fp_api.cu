@@ -32,7 +32,8 @@ int local_blocks(int NB, int stride, int offset) {
 bool tensor_path(int dtype, int D) { return dtype == FP_DTYPE_BF16 && D % 64 == 0 && D >= 64; }
 
 struct TokenLayout {
-  size_t err, meta, k16f, scores, ridx, rcnt, ctx, key_cnt, key_off, key_fill, pair_tok, tiles, h, total;
+  size_t err, meta, k16f, scores, ridx, rcnt, ctx, key_cnt, key_off, key_fill, pair_tok, tiles, h, yacc, total;
+  int ksplit;
   int nbl, chunk, nkey, max_tiles;
 };
 
@@ -59,13 +60,16 @@ TokenLayout token_layout(int dtype, int64_t M, int D, int NB, int base, int kmax
     L.pair_tok = c.take((size_t)pairs * 4);
     L.tiles = c.take((size_t)L.max_tiles * 8);
     L.h = c.take((size_t)M * L.nbl * kBlock * 2);
+    L.ksplit = down_ksplit(M, D, std::max(L.nbl, 1));
+    if (L.ksplit > 1) L.yacc = c.take((size_t)M * D * 4);
   }
   L.total = c.off;
   return L;
 }
 
 struct PooledLayout {
-  size_t err, part, mean, h, total;
+  size_t err, part, mean, h, yacc, total;
+  int ksplit;
 };
 
 PooledLayout pooled_layout(int dtype, int64_t M, int D, int NB, int n_active) {
@@ -76,7 +80,11 @@ PooledLayout pooled_layout(int dtype, int64_t M, int D, int NB, int n_active) {
   const int width = std::max(D, NB);
   L.part = c.take((size_t)nchunk * width * 4);
   L.mean = c.take((size_t)width * 4);
-  if (tensor_path(dtype, D)) L.h = c.take((size_t)M * std::max(n_active, 1) * kBlock * 2);
+  if (tensor_path(dtype, D)) {
+    L.h = c.take((size_t)M * std::max(n_active, 1) * kBlock * 2);
+    L.ksplit = down_ksplit(M, D, std::max(n_active, 1));
+    if (L.ksplit > 1) L.yacc = c.take((size_t)M * D * 4);
+  }
   L.total = c.off;
   return L;
 }
@@ -314,6 +322,7 @@ int fp_pattention_token_fwd(const void* x, int64_t M, int D, int NB, int dtype, 
   d.h = h; d.v_t = v_t; d.M = M; d.D = D; d.Np = NB * kBlock; d.K = nbl * kBlock; d.bmap = nullptr;
   d.stride = block_stride; d.offset = block_offset; d.ctx16 = ctx; d.out_proj = out_proj;
   d.out_proj_f32 = dtype == FP_DTYPE_F32; d.y = y; d.y_f32 = y_f32; d.err = err; d.num_sms = sms;
+  d.ksplit = L.ksplit; d.y_acc = L.ksplit > 1 ? at<float>(workspace, L.yacc) : nullptr;
   FP_TRY(launch_down(d, st));
   stage_mark(4, st);
   return FP_OK;
@@ -360,6 +369,7 @@ int fp_pattention_pooled_fwd(const void* x, int64_t M, int D, int NB, int dtype,
   d.h = h; d.v_t = v_t; d.M = M; d.D = D; d.Np = NB * kBlock; d.K = n_active * kBlock; d.bmap = active;
   d.stride = 1; d.offset = 0; d.ctx16 = ctx16; d.out_proj = out_proj; d.out_proj_f32 = dtype == FP_DTYPE_F32;
   d.y = y; d.y_f32 = y_f32; d.err = err; d.num_sms = sms;
+  d.ksplit = L.ksplit; d.y_acc = L.ksplit > 1 ? at<float>(workspace, L.yacc) : nullptr;
   FP_TRY(launch_down(d, st));
   stage_mark(2, st);
   return FP_OK;

@@ -288,7 +288,7 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
           const float recv = __uint_as_float(__shfl_xor_sync(0xffffffffu, send, 16));
           const float gv = lane < 16 ? __uint_as_float(v[j]) : recv;
           const float u = lane < 16 ? recv : __uint_as_float(v[16 + j]);
-          const float h = gv / (1.0f + expf(-gv)) * u;
+          const float h = __fdividef(gv, 1.0f + __expf(-gv)) * u;  // silu(g) * u
           const int tok = __shfl_sync(0xffffffffu, tok_l, lane < 16 ? j : 16 + j);
           if (tok >= 0) hbase[(int64_t)tok * a.ldh] = __float2bfloat16_rn(h);
         }
@@ -348,8 +348,9 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
   const uint32_t tmem_base = bars->tmem;
   const int m_tiles = (int)((a.M + kTileM - 1) / kTileM);
   const int n_tiles = (a.D + kTileN - 1) / kTileN;
-  const int ntiles = m_tiles * n_tiles;
-  const int nkb = a.K / kTileK;
+  const int ks = a.ksplit > 1 ? a.ksplit : 1;
+  const int ntiles = m_tiles * n_tiles * ks;
+  const int nkb_all = a.K / kTileK;
   uint32_t issued = 0;
 
   if (warp == 0) {
@@ -358,8 +359,10 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
       bool ok = true;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
         int m, n;
-        down_tile(tile, m_tiles, n_tiles, m, n);
-        for (int kb = 0; kb < nkb; ++kb, ++it) {
+        down_tile(tile / ks, m_tiles, n_tiles, m, n);
+        const int sp = tile % ks;
+        const int kb0 = (int)((int64_t)sp * nkb_all / ks), kb1 = (int)((int64_t)(sp + 1) * nkb_all / ks);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1u;
           if (!mbar_wait(&bars->empty[s], ph ^ 1u, a.err, kErrWaitEmpty)) { ok = false; break; }
@@ -381,12 +384,14 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
       bool ok = true;
       const uint32_t idesc = umma_idesc_bf16(kTileM, kTileN);
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        const int sp = tile % ks;
+        const int kb0 = (int)((int64_t)sp * nkb_all / ks), kb1 = (int)((int64_t)(sp + 1) * nkb_all / ks);
         const int acc = local & 1;
         const uint32_t aph = (local >> 1) & 1;
         if (!mbar_wait(&bars->acce[acc], aph ^ 1u, a.err, kErrWaitAccEmpty)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kTileN;
-        for (int kb = 0; kb < nkb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1u;
           if (!mbar_wait(&bars->full[s], ph, a.err, kErrWaitFull)) { ok = false; break; }
@@ -395,7 +400,7 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
           const uint64_t bd = umma_desc_sw128(smem_u32(smem + s * kStageBytes + kABytes));
 #pragma unroll
           for (int k = 0; k < kTileK / 16; ++k)
-            umma_bf16(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+            umma_bf16(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
           umma_commit(&bars->empty[s]);
           ++it;
         }
@@ -411,7 +416,8 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
     int local = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
       int m, n;
-      down_tile(tile, m_tiles, n_tiles, m, n);
+      down_tile(tile / ks, m_tiles, n_tiles, m, n);
+      const bool lead_split = (tile % ks) == 0;  // the additive stream is added by one split only
       const int acc = local & 1;
       const uint32_t aph = (local >> 1) & 1;
       if (!warp_wait(&bars->accf[acc], aph, a.err, kErrWaitAccFull)) break;
@@ -440,7 +446,7 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
         float o[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) o[i] = __uint_as_float(v[i]);
-        if (a.ctx16 && col0 < a.D) {
+        if (a.ctx16 && lead_split && col0 < a.D) {
           float w[16];
           const int64_t wrow = (int64_t)(col0 + lane) * 16;
           if (a.out_proj_f32) {
@@ -472,7 +478,11 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
           }
         }
         if (row_ok && col0 < a.D) {
-        if (a.y_f32) {
+        if (ks > 1) {
+          float4* yp = reinterpret_cast<float4*>(a.y_acc + row * a.D + col0);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) atomicAdd(yp + i, make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]));
+        } else if (a.y_f32) {
           float4* yp = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.y) + row * a.D + col0);
 #pragma unroll
           for (int i = 0; i < 8; ++i) yp[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
@@ -498,6 +508,13 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
     }
   }
   pipe_teardown(bars, issued, a.err);
+}
+
+__global__ void f32_to_out_kernel(const float* __restrict__ in, int64_t n, void* out, int out_f32) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  if (out_f32) reinterpret_cast<float*>(out)[i] = in[i];
+  else reinterpret_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(in[i]);
 }
 
 // ============================================================================================
@@ -565,11 +582,28 @@ int launch_down(const DownArgs& a, cudaStream_t st) {
   static int attr = FP_OK;
   std::call_once(once, [] { attr = set_smem((const void*)down_kernel); });
   if (attr != FP_OK) return attr;
-  const int64_t tiles = ((a.M + kTileM - 1) / kTileM) * ((a.D + kTileN - 1) / kTileN);
+  const int ks = a.ksplit > 1 ? a.ksplit : 1;
+  const int64_t tiles = ((a.M + kTileM - 1) / kTileM) * ((a.D + kTileN - 1) / kTileN) * ks;
   const int grid = (int)std::min<int64_t>(tiles, a.num_sms);
   if (grid <= 0) return FP_OK;
+  if (ks > 1 && (!a.y_acc || cudaMemsetAsync(a.y_acc, 0, (size_t)a.M * a.D * sizeof(float), st) != cudaSuccess))
+    return FP_ERR_CUDA;
   down_kernel<<<grid, kGemmThreads, kGemmSmem, st>>>(th, tv, a);
-  return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+  if (cudaGetLastError() != cudaSuccess) return FP_ERR_CUDA;
+  if (ks > 1) {
+    const int64_t n = a.M * (int64_t)a.D;
+    f32_to_out_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a.y_acc, n, a.y, a.y_f32);
+    if (cudaGetLastError() != cudaSuccess) return FP_ERR_CUDA;
+  }
+  return FP_OK;
+}
+
+int down_ksplit(int64_t M, int D, int nkb) {
+  const int64_t tiles = ((M + kTileM - 1) / kTileM) * ((D + kTileN - 1) / kTileN);
+  if (tiles <= 0 || tiles >= 64) return 1;
+  int ks = (int)((128 + tiles - 1) / tiles);  // aim at ~128 CTAs
+  ks = std::min(ks, std::max(1, nkb / 4));     // at least 4 k-blocks per split
+  return std::max(ks, 1);
 }
 
 }  // namespace fp

@@ -80,10 +80,15 @@ struct DownArgs {
   int out_proj_f32;
   void* y;              // [M, D]
   int y_f32;
+  int ksplit;           // > 1: split the k-blocks over CTAs and add fp32 partials into y_acc
+  float* y_acc;         // [M, D] fp32, zeroed by the launcher (ksplit > 1)
   int* err;
   int num_sms;
 };
 int launch_down(const DownArgs& a, cudaStream_t st);
+// Split-K factor used by the down projection for M tokens (1 = none).  Small batches (decode) have too
+// few output tiles to occupy the GPU, so the contraction over parameter blocks is split instead.
+int down_ksplit(int64_t M, int D, int nkb);
 
 // ---- simt.cu (CUDA-core path: fp32 models and shapes the tensor-core path does not tile)
 struct SimtArgs {

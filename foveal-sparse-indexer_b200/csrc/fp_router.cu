@@ -11,6 +11,8 @@
 // fp32, as PyTorch's CPU cumsum does).  Ties in probability are broken toward the lower block id.
 #include "fp_internal.cuh"
 
+#include <algorithm>
+
 namespace fp {
 
 // --------------------------------------------------------------------------------------------
@@ -44,8 +46,8 @@ __global__ void __launch_bounds__(kScoreWarps * 32)
 router_scores_kernel(const T* __restrict__ x, const T* __restrict__ wq, const T* __restrict__ k16,
                      int64_t M, int D, int NB, float inv_scale_div, float temperature,
                      float* __restrict__ scores, float* __restrict__ q16_out) {
-  extern __shared__ float sk[];  // [NB][16] fp32 block keys
-  for (int i = threadIdx.x; i < NB * 16; i += blockDim.x) sk[i] = to_f32(k16[i]);
+  extern __shared__ float sk[];  // [16][NB] fp32 block keys, transposed: lanes read consecutive blocks
+  for (int i = threadIdx.x; i < NB * 16; i += blockDim.x) sk[(i & 15) * NB + (i >> 4)] = to_f32(k16[i]);
   __syncthreads();
 
   const int lane = threadIdx.x & 31;
@@ -107,7 +109,7 @@ router_scores_kernel(const T* __restrict__ x, const T* __restrict__ wq, const T*
     for (int b = lane; b < NB; b += 32) {
       float s = 0.f;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) s = fmaf(q[j], sk[b * 16 + j], s);
+      for (int j = 0; j < 16; ++j) s = fmaf(q[j], sk[j * NB + b], s);
       s = s * inv_scale_div;            // / sqrt(16): exact power-of-two scaling
       if (temperature != 1.0f) s = __fdiv_rn(s, temperature);
       scores[tok * NB + b] = s;
@@ -121,7 +123,7 @@ router_scores_kernel(const T* __restrict__ x, const T* __restrict__ wq, const T*
 // fp64-accumulated cumulative sum, count clamped to [K_min, min(available, K_max)].  Optionally the
 // additive-stream context ctx16 = softmax(S/T) . K16.
 // --------------------------------------------------------------------------------------------
-constexpr int kSelWarps = 4;
+constexpr int kSelWarps = 8;
 
 __device__ __forceinline__ unsigned long long sel_key(float p, int b, bool remote) {
   // remote: (bits(p)+1, ~b) so that higher p first, then lower id; base: below every remote key.
@@ -184,11 +186,15 @@ select_blocks_kernel(const float* __restrict__ scores, int64_t M, int NB, int ba
                      float* __restrict__ ctx16, float* __restrict__ stats) {
   constexpr int N = 32 * E;
   __shared__ float spb[kSelWarps][N];
+  extern __shared__ float sk16[];  // [NB][16] fp32 block keys (only when ctx16 is requested)
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const int64_t tok = (int64_t)blockIdx.x * kSelWarps + warp;
-  if (tok >= M) return;
+  if (ctx16) {
+    for (int i = threadIdx.x; i < NB * 16; i += blockDim.x) sk16[i] = k16f[i];
+    __syncthreads();
+  }
   float* pbuf = spb[warp];
+  for (int64_t tok = (int64_t)blockIdx.x * kSelWarps + warp; tok < M; tok += (int64_t)gridDim.x * kSelWarps) {
   const float* srow = scores + tok * NB;
 
   // blocked layout: lane owns blocks lane*E .. lane*E+E-1
@@ -230,32 +236,15 @@ select_blocks_kernel(const float* __restrict__ scores, int64_t M, int NB, int ba
   __syncwarp();
 
   if (ctx16) {
-    float c[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) c[j] = 0.f;
-#pragma unroll
-    for (int r = 0; r < E; ++r) {
-      const int b = lane * E + r;
-      if (b < NB) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) c[j] = fmaf(p[r], k16f[b * 16 + j], c[j]);
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      float v = c[j];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      c[j] = v;
-    }
-    if (lane < 16) {
-      float v = c[0];
-#pragma unroll
-      for (int j = 1; j < 16; ++j) v = (lane == j) ? c[j] : v;
-      ctx16[tok * 16 + lane] = v;
-    }
+    // lane L accumulates channel j = L % 16 over blocks b = L / 16, L / 16 + 2, ...: each load step reads
+    // two contiguous 64-byte key rows; the two halves are combined with one shuffle
+    const int j = lane & 15;
+    float c = 0.f;
+    for (int b = lane >> 4; b < NB; b += 2) c = fmaf(pbuf[b], sk16[b * 16 + j], c);
+    c += __shfl_xor_sync(0xffffffffu, c, 16);
+    if (lane < 16) ctx16[tok * 16 + j] = c;
   }
-  if (out_idx == nullptr) return;  // context-only mode
+  if (out_idx == nullptr) { __syncwarp(); continue; }  // context-only mode
 
   // base (local) mass (core.py:104): sequential over the base blocks
   float local_mass = 0.f;
@@ -305,6 +294,8 @@ select_blocks_kernel(const float* __restrict__ scores, int64_t M, int NB, int ba
       atomicAdd(&stats[1], (float)counts);
       atomicAdd(&stats[2], counts == 0 ? 1.f : 0.f);
     }
+  }
+  __syncwarp();  // pbuf is rewritten by the next token of this warp
   }
 }
 
@@ -560,10 +551,18 @@ int launch_select(const float* scores, int64_t M, int NB, int base, float top_p,
                   int capacity, float temperature, int32_t* idx, int32_t* cnt, const float* k16f,
                   float* ctx16, float* stats, cudaStream_t st) {
   if (M <= 0) return FP_OK;
-  const int blocks = (int)((M + kSelWarps - 1) / kSelWarps);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t need = (M + kSelWarps - 1) / kSelWarps;
+  const int blocks = (int)std::min<int64_t>(need, (int64_t)sms * 8);
+  const size_t smem = ctx16 ? (size_t)NB * 16 * sizeof(float) : 0;
   auto go = [&](auto kern) {
-    kern<<<blocks, kSelWarps * 32, 0, st>>>(scores, M, NB, base, top_p, k_min, k_max, capacity, temperature,
-                                            idx, cnt, k16f, ctx16, stats);
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return FP_ERR_CUDA;
+    kern<<<blocks, kSelWarps * 32, smem, st>>>(scores, M, NB, base, top_p, k_min, k_max, capacity, temperature,
+                                               idx, cnt, k16f, ctx16, stats);
     return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
   };
   if (NB <= 32) return go(select_blocks_kernel<1>);
