@@ -61,7 +61,7 @@ TokenLayout token_layout(int dtype, int64_t M, int D, int NB, int base, int kmax
     L.tiles = c.take((size_t)L.max_tiles * 8);
     L.h = c.take((size_t)M * L.nbl * kBlock * 2);
     L.ksplit = down_ksplit(M, D, std::max(L.nbl, 1));
-    if (L.ksplit > 1) L.yacc = c.take((size_t)M * D * 4);
+    if (L.ksplit > 1) L.yacc = c.take((size_t)L.ksplit * M * D * 4);
   }
   L.total = c.off;
   return L;
@@ -83,7 +83,7 @@ PooledLayout pooled_layout(int dtype, int64_t M, int D, int NB, int n_active) {
   if (tensor_path(dtype, D)) {
     L.h = c.take((size_t)M * std::max(n_active, 1) * kBlock * 2);
     L.ksplit = down_ksplit(M, D, std::max(n_active, 1));
-    if (L.ksplit > 1) L.yacc = c.take((size_t)M * D * 4);
+    if (L.ksplit > 1) L.yacc = c.take((size_t)L.ksplit * M * D * 4);
   }
   L.total = c.off;
   return L;

@@ -417,7 +417,8 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
       int m, n;
       down_tile(tile / ks, m_tiles, n_tiles, m, n);
-      const bool lead_split = (tile % ks) == 0;  // the additive stream is added by one split only
+      const int split = tile % ks;
+      const bool lead_split = split == 0;  // the additive stream is added by one split only
       const int acc = local & 1;
       const uint32_t aph = (local >> 1) & 1;
       if (!warp_wait(&bars->accf[acc], aph, a.err, kErrWaitAccFull)) break;
@@ -478,10 +479,10 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
           }
         }
         if (row_ok && col0 < a.D) {
-        if (ks > 1) {
-          float4* yp = reinterpret_cast<float4*>(a.y_acc + row * a.D + col0);
+        if (ks > 1) {  // partial of this split; summed in split order by splitk_reduce_kernel
+          float4* yp = reinterpret_cast<float4*>(a.y_acc + ((int64_t)split * a.M + row) * a.D + col0);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) atomicAdd(yp + i, make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]));
+          for (int i = 0; i < 8; ++i) yp[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
         } else if (a.y_f32) {
           float4* yp = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.y) + row * a.D + col0);
 #pragma unroll
@@ -510,11 +511,14 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
   pipe_teardown(bars, issued, a.err);
 }
 
-__global__ void f32_to_out_kernel(const float* __restrict__ in, int64_t n, void* out, int out_f32) {
+// Sums the split-K partials [ks][n] in split order (deterministic) and writes the output dtype.
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, int ks, int64_t n, void* out, int out_f32) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
-  if (out_f32) reinterpret_cast<float*>(out)[i] = in[i];
-  else reinterpret_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(in[i]);
+  float s = part[i];
+  for (int k = 1; k < ks; ++k) s += part[(int64_t)k * n + i];
+  if (out_f32) reinterpret_cast<float*>(out)[i] = s;
+  else reinterpret_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(s);
 }
 
 // ============================================================================================
@@ -586,13 +590,12 @@ int launch_down(const DownArgs& a, cudaStream_t st) {
   const int64_t tiles = ((a.M + kTileM - 1) / kTileM) * ((a.D + kTileN - 1) / kTileN) * ks;
   const int grid = (int)std::min<int64_t>(tiles, a.num_sms);
   if (grid <= 0) return FP_OK;
-  if (ks > 1 && (!a.y_acc || cudaMemsetAsync(a.y_acc, 0, (size_t)a.M * a.D * sizeof(float), st) != cudaSuccess))
-    return FP_ERR_CUDA;
+  if (ks > 1 && !a.y_acc) return FP_ERR_INVALID_ARG;
   down_kernel<<<grid, kGemmThreads, kGemmSmem, st>>>(th, tv, a);
   if (cudaGetLastError() != cudaSuccess) return FP_ERR_CUDA;
   if (ks > 1) {
     const int64_t n = a.M * (int64_t)a.D;
-    f32_to_out_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a.y_acc, n, a.y, a.y_f32);
+    splitk_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a.y_acc, ks, n, a.y, a.y_f32);
     if (cudaGetLastError() != cudaSuccess) return FP_ERR_CUDA;
   }
   return FP_OK;

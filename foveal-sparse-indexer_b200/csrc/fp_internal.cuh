@@ -80,8 +80,8 @@ struct DownArgs {
   int out_proj_f32;
   void* y;              // [M, D]
   int y_f32;
-  int ksplit;           // > 1: split the k-blocks over CTAs and add fp32 partials into y_acc
-  float* y_acc;         // [M, D] fp32, zeroed by the launcher (ksplit > 1)
+  int ksplit;           // > 1: split the k-blocks over CTAs; each split writes its fp32 partial
+  float* y_acc;         // [ksplit, M, D] fp32 partials (ksplit > 1), summed in split order
   int* err;
   int num_sms;
 };
