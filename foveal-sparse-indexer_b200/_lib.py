@@ -39,6 +39,9 @@ SIGNATURES = {
                                          _c_int, _c_p, _c_p, _c_p, _c_p, _c_sz, _c_p]),
     "fp_pattention_pooled_fwd": (_c_int, [_c_p, _c_i64, _c_int, _c_int, _c_int, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
                                           _c_int, _c_p, _c_p, _c_p, _c_int, _c_p, _c_sz, _c_p]),
+    "fp_pattention_token_fwd_noalloc": (_c_int, [_c_p, _c_i64, _c_int, _c_int, _c_int, _c_p, _c_p, _c_p, _c_p, _c_p,
+                                                 _c_p, _c_p, _c_p, _c_int, _c_f, _c_int, _c_int, _c_f, _c_int, _c_int,
+                                                 _c_int, _c_p, _c_int, _c_p, _c_p, _c_p, _c_p]),
     "fp_set_stage_events": (_c_int, [ctypes.POINTER(_c_p), _c_int]),
     "fp_device_error": (_c_int, [_c_p, _c_p, _c_p]),
 }

@@ -148,6 +148,25 @@ FP_API int fp_pattention_pooled_fwd(const void* x, int64_t M, int D, int NB, int
                              void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Allocation-free token-routed forward (no counterpart in the reference).  Same arguments and result
+ * as fp_pattention_token_fwd, without the workspace: it runs in a FP_NOALLOC_SCRATCH_BYTES scratch
+ * array that the library keeps on each GPU it is loaded on, so callers that cannot allocate device
+ * memory per call (plugin interfaces that only pass input/output pointers, serving loops with a
+ * device-memory budget fixed at start-up) can still run the layer.  Calls needing more scratch than
+ * the array holds (large batches; sized for decode-step batches) return FP_ERR_WORKSPACE.  All calls
+ * on a device share the array: calls that overlap on the GPU race, so serialise them.  The first call
+ * on a device looks up the array's address; make it before any stream capture.
+ */
+#define FP_NOALLOC_SCRATCH_BYTES (16u << 20)
+FP_API int fp_pattention_token_fwd_noalloc(const void* x, int64_t M, int D, int NB, int dtype,
+                                           const void* k_gate, const void* k_up, const void* v, const void* w_gu,
+                                           const void* v_t, const void* q_proj, const void* block_keys,
+                                           const void* out_proj, int base_blocks, float top_p, int min_remote,
+                                           int max_remote, float temperature, int additive, int block_stride,
+                                           int block_offset, void* y, int y_f32, int32_t* remote_indices,
+                                           int32_t* remote_counts, float* scores, void* stream);
+
+/*
  * Measurement hook (no counterpart in the reference): for the calling host thread, the forward entry
  * points record events[i] (cudaEvent_t handles) on their stream at stage boundaries:
  *   fp_pattention_token_fwd:  0 start, 1 routed (scores + selection), 2 block CSR built and H cleared,
