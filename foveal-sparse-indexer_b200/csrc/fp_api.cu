@@ -284,8 +284,11 @@ int fp_pattention_token_fwd(const void* x, int64_t M, int D, int NB, int dtype, 
   stage_mark(0, st);
   FP_TRY(launch_router_scores(x, q_proj, block_keys, dtype, M, D, NB, 1.0f, S, nullptr, st));
   FP_TRY(launch_convert_keys(block_keys, dtype, NB * 16, k16f, st));
+  // the tensor-core path's masked activations H must read zero for unselected (token, block) pairs:
+  // the selection kernel clears each token's row while it works (HBM is otherwise idle there)
+  void* hclear = (tc && L.nbl > 0) ? at<void>(workspace, L.h) : nullptr;
   FP_TRY(launch_select(S, M, NB, base_blocks, top_p, min_remote, max_remote, cap, temperature, ridx, rcnt,
-                       additive ? k16f : nullptr, ctx, nullptr, st));
+                       additive ? k16f : nullptr, ctx, nullptr, st, hclear, (int64_t)L.nbl * kBlock * 2));
   stage_mark(1, st);
 
   if (!tc || L.nbl == 0) {
@@ -308,8 +311,6 @@ int fp_pattention_token_fwd(const void* x, int64_t M, int D, int NB, int dtype, 
   const int nbl = L.nbl;
   FP_TRY(launch_build_csr(ridx, rcnt, M, base_blocks, cap, block_stride, block_offset, nbl, L.chunk, L.nkey,
                           key_cnt, key_off, key_fill, pair_tok, tiles, L.max_tiles, meta, err, st));
-  // H is "dense masked": every (token, block) pair the token did not select must read as zero.
-  if (cudaMemsetAsync(h, 0, (size_t)M * nbl * kBlock * 2, st) != cudaSuccess) return FP_ERR_CUDA;
   stage_mark(2, st);
   GateUpArgs g{};
   g.x = x; g.w_gu = w_gu; g.M = M; g.D = D; g.Np = NB * kBlock;

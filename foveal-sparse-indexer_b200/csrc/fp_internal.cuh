@@ -25,9 +25,10 @@ constexpr int kGemmThreads = 192; // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 // ---- router.cu
 int launch_router_scores(const void* x, const void* wq, const void* k16, int dtype, int64_t M, int D,
                          int NB, float temperature, float* scores, float* q16, cudaStream_t st);
+// hzero (optional): rows of hrow_bytes (multiple of 16) per token, cleared by the warp of that token
 int launch_select(const float* scores, int64_t M, int NB, int base, float top_p, int k_min, int k_max,
                   int capacity, float temperature, int32_t* idx, int32_t* cnt, const float* k16f,
-                  float* ctx16, float* stats, cudaStream_t st);
+                  float* ctx16, float* stats, cudaStream_t st, void* hzero = nullptr, int64_t hrow_bytes = 0);
 int launch_convert_keys(const void* k16, int dtype, int n, float* out, cudaStream_t st);
 int launch_build_csr(const int32_t* ridx, const int32_t* rcnt, int64_t M, int base, int cap, int stride,
                      int offset, int nbl, int chunk, int nkey, int32_t* key_cnt, int32_t* key_off,

@@ -118,6 +118,95 @@ router_scores_kernel(const T* __restrict__ x, const T* __restrict__ wq, const T*
 }
 
 // --------------------------------------------------------------------------------------------
+// bf16 scores with tensor-core MMA (mma.sync m16n8k16, fp32 accumulate).  One warp computes the 16
+// projections of 16 tokens.  The contraction index is permuted inside each 64-element chunk so that
+// every lane reads contiguous 32-byte pieces of x and W_q: lane (g, t) of k-step s uses elements
+// 16t + 4s + {0..3}, which is where the fragment layout wants columns {2t, 2t+1, 2t+8, 2t+9} of
+// that step; A and B share the permutation, so the sum is unchanged.
+// --------------------------------------------------------------------------------------------
+constexpr int kMmaWarps = 4;
+
+__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                               uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ld32B(const __nv_bfloat16* p, uint32_t (&w)[8]) {
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+  const uint4 v = __ldg(reinterpret_cast<const uint4*>(p) + 1);
+  w[0] = u.x; w[1] = u.y; w[2] = u.z; w[3] = u.w; w[4] = v.x; w[5] = v.y; w[6] = v.z; w[7] = v.w;
+}
+
+__global__ void __launch_bounds__(kMmaWarps * 32)
+router_scores_mma_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ wq,
+                         const __nv_bfloat16* __restrict__ k16, int64_t M, int D, int NB,
+                         float* __restrict__ scores, float* __restrict__ q16_out) {
+  extern __shared__ float sk[];  // [16][NB] transposed block keys, then [kMmaWarps][16][17] projections
+  float* sq = sk + 16 * NB;
+  for (int i = threadIdx.x; i < NB * 16; i += blockDim.x) sk[(i & 15) * NB + (i >> 4)] = __bfloat162float(k16[i]);
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int64_t tok0 = ((int64_t)blockIdx.x * kMmaWarps + warp) * 16;
+  if (tok0 >= M) return;
+  const __nv_bfloat16* xa = x + (tok0 + g < M ? tok0 + g : M - 1) * (int64_t)D + 16 * t;
+  const __nv_bfloat16* xb = x + (tok0 + g + 8 < M ? tok0 + g + 8 : M - 1) * (int64_t)D + 16 * t;
+  const __nv_bfloat16* wa = wq + (int64_t)g * D + 16 * t;
+  const __nv_bfloat16* wb = wq + (int64_t)(8 + g) * D + 16 * t;
+  float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 2
+  for (int k0 = 0; k0 < D; k0 += 64) {
+    uint32_t A0[8], A1[8], B0[8], B1[8];
+    ld32B(xa + k0, A0);
+    ld32B(xb + k0, A1);
+    ld32B(wa + k0, B0);
+    ld32B(wb + k0, B1);
+#pragma unroll
+    for (int st = 0; st < 4; ++st) {
+      mma_bf16_16816(c0, A0[2 * st], A1[2 * st], A0[2 * st + 1], A1[2 * st + 1], B0[2 * st], B0[2 * st + 1]);
+      mma_bf16_16816(c1, A0[2 * st], A1[2 * st], A0[2 * st + 1], A1[2 * st + 1], B1[2 * st], B1[2 * st + 1]);
+    }
+  }
+  // c0: projections j = 2t, 2t+1 of rows g (c0[0..1]) and g+8 (c0[2..3]); c1: j = 8 + 2t, 9 + 2t
+  float* q = sq + warp * 16 * 17;
+  q[g * 17 + 2 * t] = c0[0];
+  q[g * 17 + 2 * t + 1] = c0[1];
+  q[(g + 8) * 17 + 2 * t] = c0[2];
+  q[(g + 8) * 17 + 2 * t + 1] = c0[3];
+  q[g * 17 + 8 + 2 * t] = c1[0];
+  q[g * 17 + 9 + 2 * t] = c1[1];
+  q[(g + 8) * 17 + 8 + 2 * t] = c1[2];
+  q[(g + 8) * 17 + 9 + 2 * t] = c1[3];
+  __syncwarp();
+  const float eps = 1.1920928955078125e-07f;  // torch.finfo(float32).eps: F.rms_norm's default
+  for (int r = 0; r < 16; ++r) {
+    const int64_t tok = tok0 + r;
+    if (tok >= M) break;
+    float qv[16];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      qv[j] = q[r * 17 + j];
+      ss = fmaf(qv[j], qv[j], ss);
+    }
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(ss * (1.0f / 16.0f) + eps));
+#pragma unroll
+    for (int j = 0; j < 16; ++j) qv[j] *= inv;
+    if (q16_out && lane < 16) q16_out[tok * 16 + lane] = q[r * 17 + lane] * inv;
+    for (int b = lane; b < NB; b += 32) {
+      float sc = 0.f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) sc = fmaf(qv[j], sk[j * NB + b], sc);
+      scores[tok * NB + b] = sc * 0.25f;  // / sqrt(16)
+    }
+  }
+}
+
+// --------------------------------------------------------------------------------------------
 // Selection: one warp per token row of scores.  Softmax over all blocks, base mass credit, stable
 // descending order of remote probabilities (bitonic sort of 64-bit keys in per-warp shared memory),
 // fp64-accumulated cumulative sum, count clamped to [K_min, min(available, K_max)].  Optionally the
@@ -183,7 +272,8 @@ __global__ void __launch_bounds__(kSelWarps * 32)
 select_blocks_kernel(const float* __restrict__ scores, int64_t M, int NB, int base, float top_p, int k_min,
                      int k_max, int capacity, float temperature, int32_t* __restrict__ out_idx,
                      int32_t* __restrict__ out_cnt, const float* __restrict__ k16f,
-                     float* __restrict__ ctx16, float* __restrict__ stats) {
+                     float* __restrict__ ctx16, float* __restrict__ stats, uint4* __restrict__ hzero,
+                     int64_t hrow_vec) {
   constexpr int N = 32 * E;
   __shared__ float spb[kSelWarps][N];
   extern __shared__ float sk16[];  // [NB][16] fp32 block keys (only when ctx16 is requested)
@@ -196,6 +286,10 @@ select_blocks_kernel(const float* __restrict__ scores, int64_t M, int NB, int ba
   float* pbuf = spb[warp];
   for (int64_t tok = (int64_t)blockIdx.x * kSelWarps + warp; tok < M; tok += (int64_t)gridDim.x * kSelWarps) {
   const float* srow = scores + tok * NB;
+  if (hzero) {  // clear this token's row of the masked activations H while the warp computes
+    uint4* hr = hzero + tok * hrow_vec;
+    for (int64_t i = lane; i < hrow_vec; i += 32) hr[i] = make_uint4(0u, 0u, 0u, 0u);
+  }
 
   // blocked layout: lane owns blocks lane*E .. lane*E+E-1
   float p[E];
@@ -517,6 +611,17 @@ pooled_topk_kernel(const float* __restrict__ mean_vec, const T* __restrict__ wq,
 int launch_router_scores(const void* x, const void* wq, const void* k16, int dtype, int64_t M, int D,
                          int NB, float temperature, float* scores, float* q16, cudaStream_t st) {
   if (M <= 0) return FP_OK;
+  if (dtype == FP_DTYPE_BF16 && D % 64 == 0 && temperature == 1.0f) {
+    const size_t smem = (size_t)NB * 16 * sizeof(float) + kMmaWarps * 16 * 17 * sizeof(float);
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(router_scores_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+      return FP_ERR_CUDA;
+    const int blocks = (int)((M + kMmaWarps * 16 - 1) / (kMmaWarps * 16));
+    router_scores_mma_kernel<<<blocks, kMmaWarps * 32, smem, st>>>(
+        (const __nv_bfloat16*)x, (const __nv_bfloat16*)wq, (const __nv_bfloat16*)k16, M, D, NB, scores, q16);
+    return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+  }
   const int blocks = (int)((M + kScoreWarps * kScoreTPW - 1) / (kScoreWarps * kScoreTPW));
   const size_t smem = (size_t)NB * 16 * sizeof(float);
   if (smem > 48 * 1024) {
@@ -549,7 +654,7 @@ __global__ void convert_keys_kernel(const void* k16, int dtype, int n, float* ou
 
 int launch_select(const float* scores, int64_t M, int NB, int base, float top_p, int k_min, int k_max,
                   int capacity, float temperature, int32_t* idx, int32_t* cnt, const float* k16f,
-                  float* ctx16, float* stats, cudaStream_t st) {
+                  float* ctx16, float* stats, cudaStream_t st, void* hzero, int64_t hrow_bytes) {
   if (M <= 0) return FP_OK;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -562,7 +667,7 @@ int launch_select(const float* scores, int64_t M, int NB, int base, float top_p,
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return FP_ERR_CUDA;
     kern<<<blocks, kSelWarps * 32, smem, st>>>(scores, M, NB, base, top_p, k_min, k_max, capacity, temperature,
-                                               idx, cnt, k16f, ctx16, stats);
+                                               idx, cnt, k16f, ctx16, stats, (uint4*)hzero, hrow_bytes / 16);
     return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
   };
   if (NB <= 32) return go(select_blocks_kernel<1>);

@@ -232,6 +232,79 @@ class FovealPattentionMLP(nn.Module):
                     "sparsity": (1.0 - self.total_active_blocks / self.num_blocks) * 100.0}
         return y, info
 
+    def forward_host(self, x_host: Tensor, out: Optional[Tensor] = None, chunk_tokens: int = 2048) -> Tensor:
+        """Token-routed forward of a batch held in host memory.
+
+        The batch is processed in chunks of ``chunk_tokens`` tokens on three CUDA streams of the module's
+        device: the host-to-device copy of chunk i+1 and the device-to-host copy of chunk i-1 run while
+        chunk i is computed.  Tokens are routed independently, so the result equals ``forward`` on the
+        whole batch.  ``x_host`` (and ``out``, if given) should be pinned for the copies to overlap.
+        Returns the output in host memory; it is complete once the caller's current stream has been
+        synchronised (the current stream is made to wait for the last copy).
+        """
+        if self.routing != "token":
+            raise ValueError("forward_host needs routing='token' (pooled routing pools over the whole call)")
+        if x_host.is_cuda:
+            raise ValueError("forward_host takes a host tensor; use forward for device tensors")
+        dev = self.k_gate.device
+        if dev.type != "cuda":
+            raise RuntimeError("the module's parameters must be on a CUDA device")
+        D = x_host.shape[-1]
+        x2d = x_host.reshape(-1, D)
+        M = x2d.shape[0]
+        dt = self.k_gate.dtype
+        if x2d.dtype != dt:
+            raise TypeError(f"x must already have the module dtype {dt} for the streamed copy")
+        if out is None:
+            out = torch.empty(x_host.shape[:-1] + (D,), dtype=dt, pin_memory=True)
+        y2d = out.reshape(-1, D)
+        kg, ku, v, packed, wq, k16, wout = self._weights()
+        ch = max(1, min(int(chunk_tokens), M))
+        st = getattr(self, "_host_streams", None)
+        if st is None or st[0].device != dev:
+            st = tuple(torch.cuda.Stream(device=dev) for _ in range(3))
+            self._host_streams = st
+        s_in, s_cmp, s_out = st
+        bufs = getattr(self, "_host_bufs", None)
+        if bufs is None or bufs[0].shape[0] < ch or bufs[0].shape[1] != D or bufs[0].dtype != dt:
+            bufs = [torch.empty(ch, D, dtype=dt, device=dev) for _ in range(4)]  # x0, x1, y0, y1
+            self._host_bufs = bufs
+        cur = torch.cuda.current_stream(dev)
+        for s_ in st:
+            s_.wait_stream(cur)
+        x_free = [None, None]
+        y_free = [None, None]
+        for i, c0 in enumerate(range(0, M, ch)):
+            n = min(ch, M - c0)
+            slot = i & 1
+            xb, yb = bufs[slot][:n], bufs[2 + slot][:n]
+            with torch.cuda.stream(s_in):
+                if x_free[slot] is not None:
+                    s_in.wait_event(x_free[slot])
+                xb.copy_(x2d[c0:c0 + n], non_blocking=True)
+                e_in = torch.cuda.Event()
+                e_in.record(s_in)
+            with torch.cuda.stream(s_cmp):
+                s_cmp.wait_event(e_in)
+                if y_free[slot] is not None:
+                    s_cmp.wait_event(y_free[slot])
+                kernels.token_forward(xb, kg, ku, v, packed, wq, k16, wout, base_blocks=self.base_blocks,
+                                      top_p=self.top_p, min_remote=self.min_remote_blocks,
+                                      max_remote=self.max_remote_blocks, temperature=self.temperature,
+                                      additive=True, y=yb)
+                e_cmp = torch.cuda.Event()
+                e_cmp.record(s_cmp)
+                x_free[slot] = e_cmp
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(e_cmp)
+                y2d[c0:c0 + n].copy_(yb, non_blocking=True)
+                e_out = torch.cuda.Event()
+                e_out.record(s_out)
+                y_free[slot] = e_out
+        for s_ in st:
+            cur.wait_stream(s_)
+        return out
+
     def _forward_token(self, x2d: Tensor, return_router_info: bool):
         kg, ku, v, packed, wq, k16, wout = self._weights()
         if self._shard is not None:

@@ -237,6 +237,20 @@ def test_all_blocks_active_equals_dense():
     check_y(y.cpu(), oracle.dense_swiglu(x2d, w), "bf16")
 
 
+def test_forward_host_matches_forward():
+    """Chunked host-buffer forward (copies overlapped with compute) equals the device forward."""
+    wl = configs.CONFIGS["8b"]
+    w = configs.make_weights(wl)
+    x2d = configs.make_x(wl).reshape(-1, wl.hidden_dim)[:5000].contiguous().to(torch.bfloat16)
+    m = module_for(wl, w)
+    with torch.no_grad():
+        ref = m(x2d.to(DEV))
+        y = m.forward_host(x2d.pin_memory(), chunk_tokens=2048)
+    torch.cuda.synchronize()
+    assert y.device.type == "cpu" and y.shape == ref.shape
+    assert rel_err(y.float(), ref.float().cpu()) < 1e-3
+
+
 # ------------------------------------------------------------------ edge cases
 @pytest.mark.parametrize("M", [1, 7, 129, 300])
 def test_ragged_token_counts(M):
