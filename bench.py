@@ -50,7 +50,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", default="8b")
+    ap.add_argument("--config", default="8b", help="8b (default) or 70b for the main measurement")
+    ap.add_argument("--mode", choices=["default", "decode", "sweep"], default="default",
+                    help="decode / sweep print one JSON line per point instead of the bench line")
     ap.add_argument("--e2e-steps", type=int, default=0)
     ap.add_argument("--chunk-tokens", type=int, default=2048)
     ap.add_argument("--cpu-sample", type=int, default=256)
@@ -338,10 +340,96 @@ def run_ours(args):
         print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------ extra measurement modes
+def _module_for(wl, w, dev):
+    m = fsi.FovealPattentionMLP(hidden_dim=wl.hidden_dim, intermediate_dim=wl.intermediate_dim,
+                                base_blocks=wl.base_blocks, remote_blocks=wl.max_remote_blocks,
+                                temperature=wl.temperature, dtype=torch.bfloat16, routing="token", top_p=wl.top_p,
+                                min_remote_blocks=wl.min_remote_blocks, max_remote_blocks=wl.max_remote_blocks)
+    m.load_state_dict({k: t.to(torch.bfloat16) for k, t in w.state_dict().items()}, strict=False)
+    return m.to(dev).eval()
+
+
+def _time_calls(fn, n, warm=5):
+    for _ in range(warm):
+        fn()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+    torch.cuda.synchronize()
+    for a, b in ev:
+        a.record()
+        fn()
+        b.record()
+    torch.cuda.synchronize()
+    return sorted(a.elapsed_time(b) for a, b in ev)
+
+
+def run_decode(args):
+    """Decode step (64 tokens, 8B shape), K_max in {8, 16, 32}: p50 latency per call and GB/s."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peaks, src = load_peaks()
+    for wl in configs.decode_points():
+        w = configs.make_weights(wl)
+        m = _module_for(wl, w, dev)
+        x = configs.make_x(wl).reshape(-1, wl.hidden_dim).to(dev, torch.bfloat16)
+        with torch.no_grad():
+            _, info = m(x, return_router_info=True)
+            cnt, idx = info["remote_counts"], info["remote_indices"]
+            used = torch.zeros(wl.num_blocks, dtype=torch.bool, device=dev)
+            used[:wl.base_blocks] = True
+            for t in range(x.shape[0]):
+                used[idx[t, :int(cnt[t])].long()] = True
+            nb = int(used.sum())
+            ts = _time_calls(lambda: m(x), 200)
+        p50 = ts[len(ts) // 2]
+        D = wl.hidden_dim
+        alg_bytes = 3 * 64 * D * 2 * nb + 2 * x.numel() * 2          # touched blocks (gate, up, v) + x + y
+        moved = (2 * 64 * D * 2 * nb) + wl.intermediate_dim * D * 2 + 2 * x.numel() * 2  # v_t read whole
+        print(json.dumps({"mode": "decode", "config": wl.name, "tokens": x.shape[0], "k_max": wl.max_remote_blocks,
+                          "p50_ms": p50, "p10_ms": ts[len(ts) // 10], "p90_ms": ts[9 * len(ts) // 10],
+                          "tokens_per_s": x.shape[0] / (p50 / 1e3), "blocks_touched": nb,
+                          "algorithmic_GBps": alg_bytes / (p50 / 1e3) / 1e9,
+                          "moved_GBps": moved / (p50 / 1e3) / 1e9, "hbm_peak_GBps": peaks["hbm_gbs"]}), flush=True)
+
+
+def run_sweep(args):
+    """Sparsity sweep (x [4, 4096, 4096], 8B shape): tokens/s per (top_p, K_max) and the speedup over
+    the dense SwiGLU equivalent (all 224 blocks, same kernels; and cuBLAS through torch)."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    pts = configs.sweep_points()
+    w = configs.make_weights(pts[0])
+    x = configs.make_x(pts[0]).reshape(-1, pts[0].hidden_dim).to(dev, torch.bfloat16)
+    M = x.shape[0]
+    with torch.no_grad():
+        m = _module_for(pts[0], w, dev)
+        kg, ku, v, packed, wq, k16, wout = m._weights()
+        active = torch.arange(pts[0].num_blocks, dtype=torch.int32, device=dev)
+        dense_ours = _time_calls(lambda: fsi.kernels.pooled_forward(x, kg, ku, v, packed, active), 10)
+        import torch.nn.functional as F
+        dense_torch = _time_calls(lambda: F.linear(F.silu(F.linear(x, kg)) * F.linear(x, ku), v.t()), 10)
+        d_ours, d_torch = dense_ours[len(dense_ours) // 2], dense_torch[len(dense_torch) // 2]
+        for wl in pts:
+            mm = _module_for(wl, w, dev)
+            _, info = mm(x, return_router_info=True)
+            a_mean = wl.base_blocks + float(info["remote_counts"].float().mean())
+            ts = _time_calls(lambda: mm(x), 10)
+            t = ts[len(ts) // 2]
+            print(json.dumps({"mode": "sweep", "top_p": wl.top_p, "k_max": wl.max_remote_blocks,
+                              "active_blocks_per_token": a_mean, "active_fraction": a_mean / wl.num_blocks,
+                              "ms": t, "tokens_per_s": M / (t / 1e3),
+                              "speedup_vs_dense_same_kernels": d_ours / t, "speedup_vs_dense_cublas": d_torch / t,
+                              "dense_ms_same_kernels": d_ours, "dense_ms_cublas": d_torch}), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.mode == "decode":
+        run_decode(args)
+    elif args.mode == "sweep":
+        run_sweep(args)
     else:
         run_ours(args)
 
