@@ -381,12 +381,27 @@ def run_decode(args):
                 used[idx[t, :int(cnt[t])].long()] = True
             nb = int(used.sum())
             ts = _time_calls(lambda: m(x), 200)
+            # the same call captured once in a CUDA graph and replayed (how a decode loop runs it)
+            gs = torch.cuda.Stream(dev)
+            gs.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(gs):
+                for _ in range(3):
+                    m(x)
+            torch.cuda.current_stream(dev).wait_stream(gs)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                m(x)
+            tg = _time_calls(graph.replay, 200)
+            del graph
         p50 = ts[len(ts) // 2]
+        g50 = tg[len(tg) // 2]
         D = wl.hidden_dim
         alg_bytes = 3 * 64 * D * 2 * nb + 2 * x.numel() * 2          # touched blocks (gate, up, v) + x + y
         moved = (2 * 64 * D * 2 * nb) + wl.intermediate_dim * D * 2 + 2 * x.numel() * 2  # v_t read whole
         print(json.dumps({"mode": "decode", "config": wl.name, "tokens": x.shape[0], "k_max": wl.max_remote_blocks,
                           "p50_ms": p50, "p10_ms": ts[len(ts) // 10], "p90_ms": ts[9 * len(ts) // 10],
+                          "graph_p50_ms": g50, "graph_tokens_per_s": x.shape[0] / (g50 / 1e3),
+                          "graph_algorithmic_GBps": alg_bytes / (g50 / 1e3) / 1e9,
                           "tokens_per_s": x.shape[0] / (p50 / 1e3), "blocks_touched": nb,
                           "algorithmic_GBps": alg_bytes / (p50 / 1e3) / 1e9,
                           "moved_GBps": moved / (p50 / 1e3) / 1e9, "hbm_peak_GBps": peaks["hbm_gbs"]}), flush=True)

@@ -52,7 +52,7 @@ TokenLayout token_layout(int dtype, int64_t M, int D, int NB, int base, int kmax
   const int64_t nchunks = (M + L.chunk - 1) / L.chunk;
   L.nkey = (int)(nchunks * std::max(L.nbl, 1));
   const int64_t pairs = M * (int64_t)(base + kmax);
-  L.max_tiles = (int)(pairs / kTileN + L.nkey + 1);
+  L.max_tiles = (int)(pairs / kGuN + L.nkey + 1);
   if (tensor_path(dtype, D)) {
     L.key_cnt = c.take((size_t)L.nkey * 4);
     L.key_off = c.take(((size_t)L.nkey + 1) * 4);

@@ -26,17 +26,25 @@ constexpr uint32_t kBBytes = kTileN * kTileK * 2;  // 32 KB
 constexpr uint32_t kStageBytes = kABytes + kBBytes;
 constexpr uint32_t kTmemCols = 512;
 
-struct __align__(8) PipeBars {
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
+template <int S>
+struct __align__(8) PipeBarsT {
+  static constexpr int kStagesN = S;
+  uint64_t full[S];
+  uint64_t empty[S];
   uint64_t accf[2];
   uint64_t acce[2];
   uint64_t done;
   uint32_t tmem;
   int32_t consumed;
 };
+using PipeBars = PipeBarsT<kStages>;     // down kernel
+using GuBars = PipeBarsT<kGuStages>;     // gate/up kernel
 
+constexpr uint32_t kGuBBytes = kGuN * kTileK * 2;
+constexpr uint32_t kGuStageBytes = kABytes + kGuBBytes;
 constexpr size_t kGemmSmem = 1024 + kStages * kStageBytes + sizeof(PipeBars) + 64;
+constexpr size_t kGuSmem = 1024 + kGuStages * kGuStageBytes + sizeof(GuBars) + 64;
+static_assert(kGuSmem <= 227 * 1024, "gate/up shared memory");
 
 __device__ __forceinline__ uint8_t* aligned_smem(uint8_t* raw) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
@@ -51,9 +59,10 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
   return ok;
 }
 
-__device__ __forceinline__ void pipe_init(PipeBars* bars, int epi_warps, int full_count = 1) {
+template <class Bars>
+__device__ __forceinline__ void pipe_init(Bars* bars, int epi_warps, int full_count = 1) {
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < Bars::kStagesN; ++s) {
       mbar_init(&bars->full[s], full_count);
       mbar_init(&bars->empty[s], 1);
     }
@@ -75,12 +84,14 @@ __device__ __forceinline__ void pipe_init(PipeBars* bars, int epi_warps, int ful
 }
 
 // After every role has left its loop: make sure no TMA copy or MMA is still in flight, then free TMEM.
-__device__ __forceinline__ void pipe_teardown(PipeBars* bars, uint32_t issued, int* err) {
+template <class Bars>
+__device__ __forceinline__ void pipe_teardown(Bars* bars, uint32_t issued, int* err) {
+  constexpr int S = Bars::kStagesN;
   tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0 && aborted(err)) {
     for (uint32_t i = (uint32_t)bars->consumed; i < issued; ++i)
-      if (!mbar_wait(&bars->full[i % kStages], (i / kStages) & 1u, nullptr, 0)) {
+      if (!mbar_wait(&bars->full[i % S], (i / S) & 1u, nullptr, 0)) {
         record_error(err, kErrDrain);
         break;
       }
@@ -93,7 +104,8 @@ __device__ __forceinline__ void pipe_teardown(PipeBars* bars, uint32_t issued, i
 }
 
 // MMA issuer tail: wait until every tcgen05.mma issued by this thread has completed.
-__device__ __forceinline__ void mma_quiesce(PipeBars* bars, uint32_t consumed, int* err) {
+template <class Bars>
+__device__ __forceinline__ void mma_quiesce(Bars* bars, uint32_t consumed, int* err) {
   bars->consumed = (int32_t)consumed;
   umma_commit(&bars->done);
   if (!mbar_wait(&bars->done, 0, nullptr, 0)) record_error(err, kErrDrain);
@@ -128,8 +140,8 @@ __device__ __forceinline__ GuTile gu_decode(const GateUpArgs& a, int tile) {
     t.slot = key;
     t.b = a.active[key];
     t.list = nullptr;
-    t.r0 = rt * kTileN;
-    t.n = (int)((a.M - t.r0) < (int64_t)kTileN ? (a.M - t.r0) : (int64_t)kTileN);
+    t.r0 = rt * kGuN;
+    t.n = (int)((a.M - t.r0) < (int64_t)kGuN ? (a.M - t.r0) : (int64_t)kGuN);
   }
   if (t.b < 0 || (int64_t)(t.b + 1) * kBlock > a.Np) {
     record_error(a.err, kErrBadTile);
@@ -142,15 +154,18 @@ __device__ __forceinline__ int gu_token(const GuTile& t, int i) {
   return t.list ? t.list[i] : (int)(t.r0 + i);
 }
 
-constexpr int kGuThreads = 320;  // + warps 6-9: token-row gathers (cp.async)
-constexpr int kGatherThreads = 128;
+constexpr int kGatherWarps = 16;                         // token-row gather warps (cp.async)
+constexpr int kGatherThreads = 32 * kGatherWarps;
+constexpr int kGuThreads = 192 + kGatherThreads;         // warps 6.. gather
+constexpr int kRowsPerGatherThread = kGuN * 8 / kGatherThreads;  // 16-byte chunks per thread per stage
+static_assert(kRowsPerGatherThread * kGatherThreads == kGuN * 8, "gather split");
 
 __global__ void __launch_bounds__(kGuThreads, 1)
 gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
               const GateUpArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = aligned_smem(smem_raw);
-  PipeBars* bars = reinterpret_cast<PipeBars*>(smem + kStages * kStageBytes);
+  GuBars* bars = reinterpret_cast<GuBars*>(smem + kGuStages * kGuStageBytes);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool gathered = a.tiles != nullptr;  // token lists (cp.async gathers) or identity rows (TMA box)
 
@@ -161,7 +176,7 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
   // full barrier: one expect_tx arrival (TMA) + one arrival per gather thread
   pipe_init(bars, 4, 1 + kGatherThreads);
   const uint32_t tmem_base = bars->tmem;
-  const int ntiles = gathered ? a.meta[0] : a.n_keys * (int)((a.M + kTileN - 1) / kTileN);
+  const int ntiles = gathered ? a.meta[0] : a.n_keys * (int)((a.M + kGuN - 1) / kGuN);
   const int nkb = a.D / kTileK;
   uint32_t issued = 0;
 
@@ -175,11 +190,11 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
         const GuTile t = gu_decode(a, tile);
         if (t.n <= 0) continue;
         for (int kb = 0; kb < nkb; ++kb, ++it) {
-          const int s = it % kStages;
-          const uint32_t ph = (it / kStages) & 1u;
+          const int s = it % kGuStages;
+          const uint32_t ph = (it / kGuStages) & 1u;
           if (!mbar_wait(&bars->empty[s], ph ^ 1u, a.err, kErrWaitEmpty)) { ok = false; break; }
-          uint8_t* As = smem + s * kStageBytes;
-          mbar_arrive_expect_tx(&bars->full[s], kABytes + (gathered ? 0u : kBBytes));
+          uint8_t* As = smem + s * kGuStageBytes;
+          mbar_arrive_expect_tx(&bars->full[s], kABytes + (gathered ? 0u : kGuBBytes));
           tma_load_2d(As, &tm_w, &bars->full[s], kb * kTileK, t.b * 2 * kBlock);
           if (!gathered) tma_load_2d(As + kABytes, &tm_x, &bars->full[s], kb * kTileK, (int)t.r0);
         }
@@ -188,11 +203,12 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
     }
     __syncwarp();
   } else if (warp >= 6) {
-    // ---------------- token-row gathers: thread g copies 16-byte chunk (g % 8) of rows g/8 + 16j,
+    // ---------------- token-row gathers: thread g copies 16-byte chunk (g % 8) of rows g/8 + kRowStep*j,
     // written in the 128-byte swizzle pattern TMA would use (chunk c of row r at c ^ (r % 8))
+    constexpr int kRowStep = kGatherThreads / 8;  // rows covered by one pass of the gather threads
     const int g = threadIdx.x - 192;
     const int chunk = g & 7, row0 = g >> 3;
-    const uint32_t swz = (uint32_t)((chunk ^ (row0 & 7)) << 4);
+    const uint32_t swz = (uint32_t)((chunk ^ (row0 & 7)) << 4);  // kRowStep is a multiple of 8
     const char* xbytes = reinterpret_cast<const char*>(a.x);
     uint32_t it = 0;
     bool ok = true;
@@ -200,23 +216,23 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
       const GuTile t = gu_decode(a, tile);
       if (t.n <= 0) continue;
       const int npad = (t.n + 15) & ~15;
-      int64_t src[16];
+      int64_t src[kRowsPerGatherThread];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int r = row0 + 16 * j;
+      for (int j = 0; j < kRowsPerGatherThread; ++j) {
+        const int r = row0 + kRowStep * j;
         const int tok = (gathered && r < npad) ? gu_token(t, r < t.n ? r : t.n - 1) : 0;
         src[j] = (int64_t)tok * a.D * 2 + chunk * 16;
       }
       for (int kb = 0; kb < nkb; ++kb, ++it) {
-        const int s = it % kStages;
-        const uint32_t ph = (it / kStages) & 1u;
+        const int s = it % kGuStages;
+        const uint32_t ph = (it / kGuStages) & 1u;
         if (!warp_wait(&bars->empty[s], ph ^ 1u, a.err, kErrWaitEmpty)) { ok = false; break; }
         if (gathered) {
-          const uint32_t bs = smem_u32(smem + s * kStageBytes + kABytes) + swz;
+          const uint32_t bs = smem_u32(smem + s * kGuStageBytes + kABytes) + swz;
           const int64_t koff = (int64_t)kb * kTileK * 2;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int r = row0 + 16 * j;
+          for (int j = 0; j < kRowsPerGatherThread; ++j) {
+            const int r = row0 + kRowStep * j;
             if (r < npad) cp_async_16(bs + r * 128, xbytes + src[j] + koff);
           }
         }
@@ -241,13 +257,13 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
         const uint32_t d_tmem = tmem_base + acc * kTileN;
         const uint32_t idesc = umma_idesc_bf16(kTileM, npad);
         for (int kb = 0; kb < nkb; ++kb) {
-          const int s = it % kStages;
-          const uint32_t ph = (it / kStages) & 1u;
+          const int s = it % kGuStages;
+          const uint32_t ph = (it / kGuStages) & 1u;
           if (!mbar_wait(&bars->full[s], ph, a.err, kErrWaitFull)) { ok = false; break; }
           fence_proxy_async_smem();
           tc_fence_after();
-          const uint64_t ad = umma_desc_sw128(smem_u32(smem + s * kStageBytes));
-          const uint64_t bd = umma_desc_sw128(smem_u32(smem + s * kStageBytes + kABytes));
+          const uint64_t ad = umma_desc_sw128(smem_u32(smem + s * kGuStageBytes));
+          const uint64_t bd = umma_desc_sw128(smem_u32(smem + s * kGuStageBytes + kABytes));
 #pragma unroll
           for (int k = 0; k < kTileK / 16; ++k)
             umma_bf16(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
@@ -558,14 +574,17 @@ static int set_smem(const void* fn) {
 
 int launch_gateup(const GateUpArgs& a, cudaStream_t st) {
   CUtensorMap tx, tw;
-  if (!encode_map_2d(&tx, a.x, a.D, a.M, (uint64_t)a.D * 2, kTileK, a.tiles ? 1 : kTileN) ||
+  if (!encode_map_2d(&tx, a.x, a.D, a.M, (uint64_t)a.D * 2, kTileK, a.tiles ? 1 : kGuN) ||
       !encode_map_2d(&tw, a.w_gu, a.D, (uint64_t)a.Np * 2, (uint64_t)a.D * 2, kTileK, kTileM))
     return FP_ERR_CUDA;
   static std::once_flag once;
   static int attr = FP_OK;
-  std::call_once(once, [] { attr = set_smem((const void*)gateup_kernel); });
+  std::call_once(once, [] {
+    attr = cudaFuncSetAttribute((const void*)gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)kGuSmem) == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+  });
   if (attr != FP_OK) return attr;
-  gateup_kernel<<<a.num_sms, kGuThreads, kGemmSmem, st>>>(tx, tw, a);
+  gateup_kernel<<<a.num_sms, kGuThreads, kGuSmem, st>>>(tx, tw, a);
   return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
 }
 

@@ -21,6 +21,10 @@ constexpr int kTileK = 64;        // one 128-byte swizzle row of bf16 = one para
 constexpr int kStages = 4;
 constexpr int kBlock = 64;        // parameter tokens per block
 constexpr int kGemmThreads = 192; // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+// gate/up kernel: at most kGuN tokens per tile (balanced tiles of a block's token list) and kGuStages
+// pipeline stages of 16 KB (weights) + kGuN x 128 B (token rows) in shared memory
+constexpr int kGuN = 256;
+constexpr int kGuStages = 4;
 
 // ---- router.cu
 int launch_router_scores(const void* x, const void* wq, const void* k16, int dtype, int64_t M, int D,
@@ -61,10 +65,10 @@ struct GateUpArgs {
 int launch_gateup(const GateUpArgs& a, cudaStream_t st);
 int launch_pack_gate_up(const void* kg, const void* ku, int Np, int D, void* wgu, cudaStream_t st);
 
-// Rows per gate/up tile of a block-CSR key with `cnt` tokens: ceil(cnt / kTileN) tiles of equal size,
+// Rows per gate/up tile of a block-CSR key with `cnt` tokens: ceil(cnt / kGuN) tiles of equal size,
 // rounded up to the UMMA N granularity (16).
 __host__ __device__ __forceinline__ int balanced_rows(int cnt) {
-  const int nt = (cnt + kTileN - 1) / kTileN;
+  const int nt = (cnt + kGuN - 1) / kGuN;
   const int per = nt > 0 ? (cnt + nt - 1) / nt : 0;
   return (per + 15) & ~15;
 }

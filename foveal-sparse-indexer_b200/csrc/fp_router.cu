@@ -141,25 +141,28 @@ __device__ __forceinline__ void ld32B(const __nv_bfloat16* p, uint32_t (&w)[8]) 
   w[0] = u.x; w[1] = u.y; w[2] = u.z; w[3] = u.w; w[4] = v.x; w[5] = v.y; w[6] = v.z; w[7] = v.w;
 }
 
+// One CTA of kMmaWarps warps per 16 tokens: warp w accumulates the D-range [w*D/4, (w+1)*D/4) (four
+// times the memory-level parallelism of one warp per group), partial projections are summed in
+// shared memory, then each warp finishes 4 of the 16 tokens (RMSNorm, 16-D scores).
 __global__ void __launch_bounds__(kMmaWarps * 32)
 router_scores_mma_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ wq,
                          const __nv_bfloat16* __restrict__ k16, int64_t M, int D, int NB,
                          float* __restrict__ scores, float* __restrict__ q16_out) {
-  extern __shared__ float sk[];  // [16][NB] transposed block keys, then [kMmaWarps][16][17] projections
+  extern __shared__ float sk[];  // [16][NB] transposed block keys, then [kMmaWarps][16][17] partials
   float* sq = sk + 16 * NB;
   for (int i = threadIdx.x; i < NB * 16; i += blockDim.x) sk[(i & 15) * NB + (i >> 4)] = __bfloat162float(k16[i]);
-  __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
-  const int64_t tok0 = ((int64_t)blockIdx.x * kMmaWarps + warp) * 16;
-  if (tok0 >= M) return;
-  const __nv_bfloat16* xa = x + (tok0 + g < M ? tok0 + g : M - 1) * (int64_t)D + 16 * t;
-  const __nv_bfloat16* xb = x + (tok0 + g + 8 < M ? tok0 + g + 8 : M - 1) * (int64_t)D + 16 * t;
-  const __nv_bfloat16* wa = wq + (int64_t)g * D + 16 * t;
-  const __nv_bfloat16* wb = wq + (int64_t)(8 + g) * D + 16 * t;
+  const int64_t tok0 = (int64_t)blockIdx.x * 16;
+  const int dpart = D / kMmaWarps;  // multiple of 64 (D % 256 == 0)
+  const int kbeg = warp * dpart;
+  const __nv_bfloat16* xa = x + (tok0 + g < M ? tok0 + g : M - 1) * (int64_t)D + kbeg + 16 * t;
+  const __nv_bfloat16* xb = x + (tok0 + g + 8 < M ? tok0 + g + 8 : M - 1) * (int64_t)D + kbeg + 16 * t;
+  const __nv_bfloat16* wa = wq + (int64_t)g * D + kbeg + 16 * t;
+  const __nv_bfloat16* wb = wq + (int64_t)(8 + g) * D + kbeg + 16 * t;
   float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 2
-  for (int k0 = 0; k0 < D; k0 += 64) {
+  for (int k0 = 0; k0 < dpart; k0 += 64) {
     uint32_t A0[8], A1[8], B0[8], B1[8];
     ld32B(xa + k0, A0);
     ld32B(xb + k0, A1);
@@ -181,22 +184,29 @@ router_scores_mma_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat1
   q[g * 17 + 9 + 2 * t] = c1[1];
   q[(g + 8) * 17 + 8 + 2 * t] = c1[2];
   q[(g + 8) * 17 + 9 + 2 * t] = c1[3];
-  __syncwarp();
+  __syncthreads();
   const float eps = 1.1920928955078125e-07f;  // torch.finfo(float32).eps: F.rms_norm's default
-  for (int r = 0; r < 16; ++r) {
+  for (int r = warp * 4; r < warp * 4 + 4; ++r) {
     const int64_t tok = tok0 + r;
     if (tok >= M) break;
     float qv[16];
     float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-      qv[j] = q[r * 17 + j];
-      ss = fmaf(qv[j], qv[j], ss);
+      float v = sq[r * 17 + j];
+#pragma unroll
+      for (int w = 1; w < kMmaWarps; ++w) v += sq[w * 16 * 17 + r * 17 + j];
+      qv[j] = v;
+      ss = fmaf(v, v, ss);
     }
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(ss * (1.0f / 16.0f) + eps));
+    float qown = 0.f;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) qv[j] *= inv;
-    if (q16_out && lane < 16) q16_out[tok * 16 + lane] = q[r * 17 + lane] * inv;
+    for (int j = 0; j < 16; ++j) {
+      if (lane == j) qown = qv[j];
+      qv[j] *= inv;
+    }
+    if (q16_out && lane < 16) q16_out[tok * 16 + lane] = qown * inv;
     for (int b = lane; b < NB; b += 32) {
       float sc = 0.f;
 #pragma unroll
@@ -441,7 +451,7 @@ csr_scan_kernel(const int32_t* __restrict__ key_cnt, int nkey, int32_t* __restri
   int pairs = 0, ntile = 0;
   for (int k = k0; k < k1; ++k) {
     pairs += key_cnt[k];
-    ntile += (key_cnt[k] + kTileN - 1) / kTileN;
+    ntile += (key_cnt[k] + kGuN - 1) / kGuN;
   }
   s_pairs[tid] = pairs;
   s_tiles[tid] = ntile;
@@ -611,13 +621,13 @@ pooled_topk_kernel(const float* __restrict__ mean_vec, const T* __restrict__ wq,
 int launch_router_scores(const void* x, const void* wq, const void* k16, int dtype, int64_t M, int D,
                          int NB, float temperature, float* scores, float* q16, cudaStream_t st) {
   if (M <= 0) return FP_OK;
-  if (dtype == FP_DTYPE_BF16 && D % 64 == 0 && temperature == 1.0f) {
+  if (dtype == FP_DTYPE_BF16 && D % (64 * kMmaWarps) == 0 && temperature == 1.0f) {
     const size_t smem = (size_t)NB * 16 * sizeof(float) + kMmaWarps * 16 * 17 * sizeof(float);
     if (smem > 48 * 1024 &&
         cudaFuncSetAttribute(router_scores_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
             cudaSuccess)
       return FP_ERR_CUDA;
-    const int blocks = (int)((M + kMmaWarps * 16 - 1) / (kMmaWarps * 16));
+    const int blocks = (int)((M + 15) / 16);
     router_scores_mma_kernel<<<blocks, kMmaWarps * 32, smem, st>>>(
         (const __nv_bfloat16*)x, (const __nv_bfloat16*)wq, (const __nv_bfloat16*)k16, M, D, NB, scores, q16);
     return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;

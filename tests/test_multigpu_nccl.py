@@ -1,0 +1,87 @@
+"""Parameter-block sharding over NCCL on 2 GPUs (skipped with fewer than 2 visible GPUs).
+
+Each rank computes the partial output of the blocks it owns (b % 2 == rank) for all tokens; one NCCL
+all-reduce (or reduce-scatter over token rows) sums the fp32 partials.  The result must match the
+single-GPU forward within the bf16 tolerance, and the routes must be identical on both ranks.
+"""
+
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+import sys
+import tempfile
+import time
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(HERE)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, out_dir):
+    sys.path.insert(0, REPO)
+    sys.path.insert(0, HERE)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    from conftest import configs, fsi, rel_err
+    wl = configs.CONFIGS["8b"]
+    w = configs.make_weights(wl)
+    x = configs.make_x(wl).reshape(-1, wl.hidden_dim)[:2048].contiguous().to(dev, torch.bfloat16)
+
+    def module():
+        m = fsi.FovealPattentionMLP(hidden_dim=wl.hidden_dim, intermediate_dim=wl.intermediate_dim,
+                                    base_blocks=wl.base_blocks, remote_blocks=wl.max_remote_blocks,
+                                    dtype=torch.bfloat16, routing="token", top_p=wl.top_p,
+                                    min_remote_blocks=wl.min_remote_blocks, max_remote_blocks=wl.max_remote_blocks)
+        m.load_state_dict({k: t.to(torch.bfloat16) for k, t in w.state_dict().items()}, strict=False)
+        return m.to(dev).eval()
+
+    with torch.no_grad():
+        full, info_full = module()(x, return_router_info=True)
+        m = module()
+        fsi.sharding.shard_parameter_blocks(m)
+        y, info = m(x, return_router_info=True)
+        ys, _, _, _ = fsi.sharding.sharded_token_forward(m, x, reduce="scatter")
+    torch.cuda.synchronize()
+    e_all = rel_err(y.float(), full.float())
+    rows = slice(rank * 1024, (rank + 1) * 1024)
+    e_sc = rel_err(ys.float(), full[rows].float())
+    same_routes = bool(torch.equal(info["remote_indices"], info_full["remote_indices"]))
+    with open(os.path.join(out_dir, f"r{rank}.txt"), "w") as f:
+        f.write(f"{e_all} {e_sc} {int(same_routes)}")
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_block_sharded_forward_over_nccl_matches_single_gpu():
+    port = _free_port()
+    with tempfile.TemporaryDirectory() as d:
+        ctx = mp.spawn(_worker, args=(2, port, d), nprocs=2, join=False)
+        deadline = time.time() + 600
+        while not ctx.join(timeout=5):
+            if time.time() > deadline:
+                for p in ctx.processes:
+                    if p.is_alive():
+                        p.kill()
+                pytest.fail("sharded forward did not finish")
+        for r in range(2):
+            e_all, e_sc, same = open(os.path.join(d, f"r{r}.txt")).read().split()
+            assert float(e_all) < 2e-2 and float(e_sc) < 2e-2 and same == "1", (r, e_all, e_sc, same)
