@@ -41,7 +41,7 @@ configs = fsi.configs
 
 METRIC = "Pattention-MLP fwd tokens/s & % bf16 tensor peak (8B shape), 1/2/4/8 B200 vs host CPU"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-KERNELS_PER_STEP = 8  # router_scores, convert_keys, select, csr_count, csr_scan, csr_fill, gateup, down
+KERNELS_PER_STEP = 4  # route_proj, route (selection + block lists), gateup, down
 
 
 def parse():
@@ -54,7 +54,7 @@ def parse():
     ap.add_argument("--mode", choices=["default", "decode", "sweep"], default="default",
                     help="decode / sweep print one JSON line per point instead of the bench line")
     ap.add_argument("--e2e-steps", type=int, default=0)
-    ap.add_argument("--chunk-tokens", type=int, default=2048)
+    ap.add_argument("--chunk-tokens", type=int, default=4096)
     ap.add_argument("--cpu-sample", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -304,7 +304,9 @@ def run_ours(args):
     peak_sus = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
     gu_flops = 4.0 * D * 64 * a_mean * M
     dn_flops = 2.0 * D * 64 * a_mean * M
-    names = ["route", "csr", "gateup", "down"]
+    # stage events: 0 start, 1 routed (block lists built in the same kernel), 2 = 1, 3 gate/up, 4 down
+    stage = [stage[0] + stage[1], 0.0, stage[2], stage[3]]
+    names = ["route", "lists", "gateup", "down"]
     dom = 2 if stage[2] >= stage[3] else 3
     dom_flops = gu_flops if dom == 2 else dn_flops
     achieved = dom_flops / (stage[dom] / 1e3) / 1e12
@@ -317,7 +319,7 @@ def run_ours(args):
         "config": config_block(wl, world),
         "tensor_peak_frac": total_flops / (ms_step / 1e3) / 1e12 / peak_sus,
         "active_blocks_per_token": a_mean,
-        "stages_ms": {n: s for n, s in zip(names, stage)},
+        "stages_ms": {n: s for n, s in zip(names, stage) if n != "lists"},
         "roofline": {"bound": "tensor", "kernel": names[dom], "achieved": achieved, "peak": peak_sus,
                      "unit": "TFLOP/s", "frac": achieved / peak_sus, "traffic": traffic,
                      "peak_source": f"{src} bf16 sustained (MEASURED_PEAKS.json)" if src == "measured"

@@ -32,32 +32,36 @@ int local_blocks(int NB, int stride, int offset) {
 bool tensor_path(int dtype, int D) { return dtype == FP_DTYPE_BF16 && D % 64 == 0 && D >= 64; }
 
 struct TokenLayout {
-  size_t err, meta, k16f, scores, ridx, rcnt, ctx, key_cnt, key_off, key_fill, pair_tok, tiles, h, yacc, total;
+  size_t err, zero_bytes, key_cnt, meta, qraw, ridx, rcnt, ctx, pair_tok, tiles, h, yacc, total;
   int ksplit;
   int nbl, chunk, nkey, max_tiles;
+  int64_t key_cap;
 };
+
+constexpr size_t kTicketOffset = 128;  // CTA completion counter of the routing kernel, in the error area
 
 TokenLayout token_layout(int dtype, int64_t M, int D, int NB, int base, int kmax, int stride, int offset) {
   TokenLayout L{};
   Carve c;
-  L.err = c.take(256);
-  L.meta = c.take(64);
-  L.k16f = c.take((size_t)NB * 16 * 4);
-  L.scores = c.take((size_t)M * NB * 4);
-  L.ridx = c.take((size_t)M * std::max(kmax, 1) * 4);
-  L.rcnt = c.take((size_t)M * 4);
-  L.ctx = c.take((size_t)M * 16 * 4);
   L.nbl = local_blocks(NB, stride, offset);
   L.chunk = csr_chunk(D);
   const int64_t nchunks = (M + L.chunk - 1) / L.chunk;
   L.nkey = (int)(nchunks * std::max(L.nbl, 1));
+  L.key_cap = std::min<int64_t>(L.chunk, std::max<int64_t>(M, 1));
+  const bool tc = tensor_path(dtype, D);
+  // error word, completion ticket and the block-CSR key counters: cleared by one memset per call
+  L.zero_bytes = 256 + (tc ? (size_t)L.nkey * 4 : 0);
+  L.err = c.take(L.zero_bytes);
+  L.key_cnt = L.err + 256;
+  L.meta = c.take(64);
+  L.qraw = c.take((size_t)M * 16 * 4);
+  L.ridx = c.take((size_t)M * std::max(kmax, 1) * 4);
+  L.rcnt = c.take((size_t)M * 4);
+  L.ctx = c.take((size_t)M * 16 * 4);
   const int64_t pairs = M * (int64_t)(base + kmax);
   L.max_tiles = (int)(pairs / kGuN + L.nkey + 1);
-  if (tensor_path(dtype, D)) {
-    L.key_cnt = c.take((size_t)L.nkey * 4);
-    L.key_off = c.take(((size_t)L.nkey + 1) * 4);
-    L.key_fill = c.take((size_t)L.nkey * 4);
-    L.pair_tok = c.take((size_t)pairs * 4);
+  if (tc) {
+    L.pair_tok = c.take((size_t)L.nkey * L.key_cap * 4);
     L.tiles = c.take((size_t)L.max_tiles * 8);
     L.h = c.take((size_t)M * L.nbl * kBlock * 2);
     L.ksplit = down_ksplit(M, D, std::max(L.nbl, 1));
@@ -94,7 +98,11 @@ T* at(void* ws, size_t off) { return reinterpret_cast<T*>(reinterpret_cast<char*
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Every launching entry point starts here.  Launch checks read the runtime's per-thread last error, so a
+// non-sticky error left by earlier, unrelated calls of the caller's thread is cleared first (a sticky
+// error, such as a fault of the context, still fails every launch).
 int device_info(int& num_sms) {
+  (void)cudaGetLastError();
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return FP_ERR_CUDA;
   static int cache_sms[64] = {0};
@@ -262,8 +270,9 @@ int fp_pattention_token_fwd(const void* x, int64_t M, int D, int NB, int dtype, 
   if (base_blocks < 0 || base_blocks > NB || min_remote < 0 || max_remote < 0) return FP_ERR_INVALID_ARG;
   if (block_stride < 1 || block_offset < 0 || block_offset >= block_stride) return FP_ERR_INVALID_ARG;
   if (!(temperature > 0.f)) return FP_ERR_INVALID_ARG;
+  if (!aligned16(x) || !aligned16(q_proj)) return FP_ERR_INVALID_ARG;
   const bool tc = tensor_path(dtype, D);
-  if (tc && (!v_t || !w_gu || !aligned16(v_t) || !aligned16(w_gu) || !aligned16(x))) return FP_ERR_INVALID_ARG;
+  if (tc && (!v_t || !w_gu || !aligned16(v_t) || !aligned16(w_gu))) return FP_ERR_INVALID_ARG;
   if (!tc && D > 32 * 256) return FP_ERR_UNSUPPORTED;
   const int cap = std::max(max_remote, 1);
   const TokenLayout L = token_layout(dtype, M, D, NB, base_blocks, max_remote, block_stride, block_offset);
@@ -272,26 +281,38 @@ int fp_pattention_token_fwd(const void* x, int64_t M, int D, int NB, int dtype, 
   FP_TRY(device_info(sms));
   cudaStream_t st = (cudaStream_t)stream;
   int* err = at<int>(workspace, L.err);
-  if (cudaMemsetAsync(err, 0, 256, st) != cudaSuccess) return FP_ERR_CUDA;
-  if (M == 0) return FP_OK;
+  if (cudaMemsetAsync(err, 0, L.zero_bytes, st) != cudaSuccess) return FP_ERR_CUDA;
 
-  float* S = scores ? scores : at<float>(workspace, L.scores);
   int32_t* ridx = remote_indices ? remote_indices : at<int32_t>(workspace, L.ridx);
   int32_t* rcnt = remote_counts ? remote_counts : at<int32_t>(workspace, L.rcnt);
-  float* k16f = at<float>(workspace, L.k16f);
   float* ctx = additive ? at<float>(workspace, L.ctx) : nullptr;
+  const int nbl = L.nbl;
+  const bool csr = tc && nbl > 0;
 
   stage_mark(0, st);
-  FP_TRY(launch_router_scores(x, q_proj, block_keys, dtype, M, D, NB, 1.0f, S, nullptr, st));
-  FP_TRY(launch_convert_keys(block_keys, dtype, NB * 16, k16f, st));
-  // the tensor-core path's masked activations H must read zero for unselected (token, block) pairs:
-  // the selection kernel clears each token's row while it works (HBM is otherwise idle there)
-  void* hclear = (tc && L.nbl > 0) ? at<void>(workspace, L.h) : nullptr;
-  FP_TRY(launch_select(S, M, NB, base_blocks, top_p, min_remote, max_remote, cap, temperature, ridx, rcnt,
-                       additive ? k16f : nullptr, ctx, nullptr, st, hclear, (int64_t)L.nbl * kBlock * 2));
+  // scores, selection and (tensor-core path) the block-major token lists in one kernel; the masked
+  // activations H must read zero for unselected (token, block) pairs, so the routing warps clear each
+  // token's row of H while they work (HBM is otherwise idle there)
+  RouteArgs r{};
+  r.x = x; r.wq = q_proj; r.k16 = block_keys; r.M = M; r.D = D; r.NB = NB; r.temperature = temperature;
+  r.sel = SelectOut{NB, base_blocks, top_p, min_remote, max_remote, cap, ridx, rcnt, ctx, nullptr};
+  r.scores = scores; r.q16 = nullptr; r.qraw = at<float>(workspace, L.qraw); r.err = err; r.num_sms = sms;
+  int32_t* key_cnt = at<int32_t>(workspace, L.key_cnt);
+  int32_t* pair_tok = csr ? at<int32_t>(workspace, L.pair_tok) : nullptr;
+  int2* tiles = csr ? at<int2>(workspace, L.tiles) : nullptr;
+  int32_t* meta = at<int32_t>(workspace, L.meta);
+  void* h = csr ? at<void>(workspace, L.h) : nullptr;
+  if (csr) {
+    r.hzero = static_cast<uint4*>(h); r.hrow_vec = (int64_t)nbl * kBlock * 2 / 16;
+    r.key_cnt = key_cnt; r.pair_tok = pair_tok; r.key_cap = L.key_cap;
+    r.stride = block_stride; r.offset = block_offset; r.nbl = nbl; r.chunk = L.chunk; r.nkey = L.nkey;
+    r.tiles = tiles; r.max_tiles = L.max_tiles; r.meta = meta;
+    r.ticket = reinterpret_cast<unsigned int*>(at<char>(workspace, L.err + kTicketOffset));
+  }
+  FP_TRY(launch_route(r, dtype, st));
   stage_mark(1, st);
 
-  if (!tc || L.nbl == 0) {
+  if (!csr) {
     // CUDA-core path; a shard that owns no block contributes only the additive stream (or zeros).
     SimtArgs a{};
     a.x = x; a.k_gate = k_gate; a.k_up = k_up; a.v = v; a.dtype = dtype; a.M = M; a.D = D; a.NB = NB;
@@ -301,20 +322,10 @@ int fp_pattention_token_fwd(const void* x, int64_t M, int D, int NB, int dtype, 
     a.y_f32 = y_f32;
     return launch_simt(a, st);
   }
-  int32_t* key_cnt = at<int32_t>(workspace, L.key_cnt);
-  int32_t* key_off = at<int32_t>(workspace, L.key_off);
-  int32_t* key_fill = at<int32_t>(workspace, L.key_fill);
-  int32_t* pair_tok = at<int32_t>(workspace, L.pair_tok);
-  int2* tiles = at<int2>(workspace, L.tiles);
-  int32_t* meta = at<int32_t>(workspace, L.meta);
-  void* h = at<void>(workspace, L.h);
-  const int nbl = L.nbl;
-  FP_TRY(launch_build_csr(ridx, rcnt, M, base_blocks, cap, block_stride, block_offset, nbl, L.chunk, L.nkey,
-                          key_cnt, key_off, key_fill, pair_tok, tiles, L.max_tiles, meta, err, st));
   stage_mark(2, st);
   GateUpArgs g{};
   g.x = x; g.w_gu = w_gu; g.M = M; g.D = D; g.Np = NB * kBlock;
-  g.tiles = tiles; g.meta = meta; g.key_off = key_off; g.pair_tok = pair_tok;
+  g.tiles = tiles; g.meta = meta; g.key_cnt = key_cnt; g.pair_tok = pair_tok; g.key_cap = L.key_cap;
   g.nbl = nbl; g.stride = block_stride; g.offset = block_offset; g.active = nullptr; g.n_keys = 0;
   g.h = h; g.ldh = (int64_t)nbl * kBlock; g.err = err; g.num_sms = sms;
   FP_TRY(launch_gateup(g, st));
@@ -360,7 +371,7 @@ int fp_pattention_pooled_fwd(const void* x, int64_t M, int D, int NB, int dtype,
   void* h = at<void>(workspace, L.h);
   GateUpArgs g{};
   g.x = x; g.w_gu = w_gu; g.M = M; g.D = D; g.Np = NB * kBlock;
-  g.tiles = nullptr; g.meta = nullptr; g.key_off = nullptr; g.pair_tok = nullptr;
+  g.tiles = nullptr; g.meta = nullptr; g.key_cnt = nullptr; g.pair_tok = nullptr; g.key_cap = 0;
   g.nbl = n_active; g.stride = 1; g.offset = 0; g.active = active; g.n_keys = n_active;
   g.h = h; g.ldh = (int64_t)n_active * kBlock; g.err = err; g.num_sms = sms;
   stage_mark(0, st);

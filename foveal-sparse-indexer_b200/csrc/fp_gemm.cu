@@ -129,9 +129,8 @@ __device__ __forceinline__ GuTile gu_decode(const GateUpArgs& a, int tile) {
     const int key = d.x;
     t.slot = key % a.nbl;
     t.b = t.slot * a.stride + a.offset;
-    const int start = a.key_off[key];
-    const int cnt = a.key_off[key + 1] - start;
-    t.list = a.pair_tok + start + d.y;
+    const int cnt = a.key_cnt[key];
+    t.list = a.pair_tok + (int64_t)key * a.key_cap + d.y;
     t.r0 = d.y;
     t.n = min(balanced_rows(cnt), cnt - d.y);
   } else {
@@ -150,8 +149,16 @@ __device__ __forceinline__ GuTile gu_decode(const GateUpArgs& a, int tile) {
   return t;
 }
 
-__device__ __forceinline__ int gu_token(const GuTile& t, int i) {
-  return t.list ? t.list[i] : (int)(t.r0 + i);
+// Token of row i of a tile.  Listed ids outside [0, M) (a corrupt work list) are reported and returned as
+// -1: the gathers then read token 0's row and the epilogue skips the store, so no access leaves x or H.
+__device__ __forceinline__ int gu_token(const GuTile& t, int i, const GateUpArgs& a) {
+  if (!t.list) return (int)(t.r0 + i);
+  const int tok = t.list[i];
+  if ((unsigned)tok >= (unsigned long long)a.M) {
+    record_error(a.err, kErrBadTile);
+    return -1;
+  }
+  return tok;
 }
 
 constexpr int kGatherWarps = 16;                         // token-row gather warps (cp.async)
@@ -220,7 +227,8 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
 #pragma unroll
       for (int j = 0; j < kRowsPerGatherThread; ++j) {
         const int r = row0 + kRowStep * j;
-        const int tok = (gathered && r < npad) ? gu_token(t, r < t.n ? r : t.n - 1) : 0;
+        const int tl = (gathered && r < npad) ? gu_token(t, r < t.n ? r : t.n - 1, a) : 0;
+        const int tok = tl < 0 ? 0 : tl;
         src[j] = (int64_t)tok * a.D * 2 + chunk * 16;
       }
       for (int kb = 0; kb < nkb; ++kb, ++it) {
@@ -296,7 +304,7 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
         tmem_ld32(tmem_base + acc * kTileN + c * 32 + ((uint32_t)(32 * q) << 16), v);
         tmem_ld_wait();
         const int ni = c * 32 + lane;
-        const int tok_l = ni < t.n ? gu_token(t, ni) : -1;
+        const int tok_l = ni < t.n ? gu_token(t, ni, a) : -1;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           // lane L<16 holds gate(channel 16q+L), lane L+16 holds up(channel 16q+L), columns = tokens

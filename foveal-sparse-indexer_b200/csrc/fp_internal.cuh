@@ -29,19 +29,53 @@ constexpr int kGuStages = 4;
 // ---- router.cu
 int launch_router_scores(const void* x, const void* wq, const void* k16, int dtype, int64_t M, int D,
                          int NB, float temperature, float* scores, float* q16, cudaStream_t st);
-// hzero (optional): rows of hrow_bytes (multiple of 16) per token, cleared by the warp of that token
 int launch_select(const float* scores, int64_t M, int NB, int base, float top_p, int k_min, int k_max,
                   int capacity, float temperature, int32_t* idx, int32_t* cnt, const float* k16f,
-                  float* ctx16, float* stats, cudaStream_t st, void* hzero = nullptr, int64_t hrow_bytes = 0);
-int launch_convert_keys(const void* k16, int dtype, int n, float* out, cudaStream_t st);
-int launch_build_csr(const int32_t* ridx, const int32_t* rcnt, int64_t M, int base, int cap, int stride,
-                     int offset, int nbl, int chunk, int nkey, int32_t* key_cnt, int32_t* key_off,
-                     int32_t* key_fill, int32_t* pair_tok, int2* tiles, int max_tiles, int32_t* meta, int* err,
-                     cudaStream_t st);
+                  float* ctx16, float* stats, cudaStream_t st);
 int launch_colmean(const void* a, int dtype, int64_t M, int D, float* part, float* mean, cudaStream_t st);
 int launch_pooled_topk(const float* mean_vec, const void* wq, const void* k16, int dtype, int D, int NB,
                        int base, int remote, int mode, int32_t* active, float* mean_scores_out,
                        cudaStream_t st);
+
+// Outputs and parameters of the per-token selection (select_blocks, core.py:46-160).
+struct SelectOut {
+  int NB, base;
+  float top_p;
+  int k_min, k_max, capacity;
+  int32_t* idx;   // [M, capacity] sorted remote ids (nullptr: context-only mode)
+  int32_t* cnt;   // [M]
+  float* ctx16;   // optional [M, 16] additive-stream context softmax(S/T) . K16
+  float* stats;   // optional [3]: capped tokens, sum of counts, base-only tokens
+};
+
+// Fused token routing (scores + selection + block CSR) of the token-routed forward.
+// Block CSR: key = chunk(t) * nbl + slot(b) for the local blocks (b % stride == offset, slot = b / stride);
+// each key owns a bucket of key_cap entries of pair_tok.  key_cnt and *ticket must be zero on entry.
+struct RouteArgs {
+  const void* x;        // [M, D]
+  const void* wq;       // [16, D]
+  const void* k16;      // [NB, 16]
+  int64_t M;
+  int D, NB;
+  float temperature;
+  SelectOut sel;
+  float* scores;        // optional [M, NB] router scores S (before the temperature)
+  float* q16;           // optional [M, 16] normalised queries
+  float* qraw;          // [M, 16] raw projections x W_q^T (workspace)
+  uint4* hzero;         // optional: per-token rows of hrow_vec 16-byte words cleared (masked H)
+  int64_t hrow_vec;
+  int32_t* key_cnt;     // optional block CSR: [nkey] counters
+  int32_t* pair_tok;    // [nkey * key_cap] token ids
+  int64_t key_cap;
+  int stride, offset, nbl, chunk, nkey;
+  int2* tiles;          // gate/up work list: (key, first row) per tile
+  int max_tiles;
+  int32_t* meta;        // meta[0] = number of tiles, meta[1] = number of pairs
+  unsigned int* ticket; // CTA completion counter
+  int* err;
+  int num_sms;
+};
+int launch_route(const RouteArgs& a, int dtype, cudaStream_t st);
 
 // ---- gemm.cu (tensor-core path, bf16)
 struct GateUpArgs {
@@ -49,11 +83,12 @@ struct GateUpArgs {
   const void* w_gu;     // [2 * Np, D] bf16, packed gate/up rows (launch_pack_gate_up)
   int64_t M;
   int D, Np;
-  // work list: explicit (tiles/meta from the CSR builder) or implicit (pooled: n_keys x ceil(M/256))
+  // work list: explicit (tiles/meta from the routing kernel) or implicit (pooled: n_keys x ceil(M/256))
   const int2* tiles;
   const int32_t* meta;      // meta[0] = number of tiles (explicit mode)
-  const int32_t* key_off;   // [nkey + 1] (explicit mode)
-  const int32_t* pair_tok;  // token ids grouped by key (explicit mode)
+  const int32_t* key_cnt;   // [nkey] tokens per key (explicit mode)
+  const int32_t* pair_tok;  // token ids of key k at pair_tok[k * key_cap ...] (explicit mode)
+  int64_t key_cap;
   int nbl, stride, offset;  // explicit mode: slot = key % nbl, block = slot * stride + offset
   const int32_t* active;    // implicit mode: block id of key j
   int n_keys;               // implicit mode: number of active blocks

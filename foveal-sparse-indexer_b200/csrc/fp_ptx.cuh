@@ -122,6 +122,18 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
 }
 // Orders shared-memory writes made through the generic proxy (cp.async) before later async-proxy
 // reads (tcgen05.mma operands) issued by this thread.
+// Bulk (non-tensor) copy shared -> global through the async proxy: both addresses 16-byte aligned,
+// size a multiple of 16.  Completion is tracked per thread with bulk groups.
+__device__ __forceinline__ void bulk_store(void* gdst, uint32_t smem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_src), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Wait until at most N bulk groups of this thread still read their shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory"); }
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -12,6 +12,8 @@
 #include "fp_internal.cuh"
 
 #include <algorithm>
+#include <type_traits>
+#include <mutex>
 
 namespace fp {
 
@@ -217,10 +219,10 @@ router_scores_mma_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat1
 }
 
 // --------------------------------------------------------------------------------------------
-// Selection: one warp per token row of scores.  Softmax over all blocks, base mass credit, stable
-// descending order of remote probabilities (bitonic sort of 64-bit keys in per-warp shared memory),
-// fp64-accumulated cumulative sum, count clamped to [K_min, min(available, K_max)].  Optionally the
-// additive-stream context ctx16 = softmax(S/T) . K16.
+// Selection: one warp per token.  Softmax over all blocks, base mass credit, stable descending order
+// of remote probabilities (bitonic sort of 64-bit keys in registers), fp64-accumulated cumulative
+// sum, count clamped to [K_min, min(available, K_max)].  Optionally the additive-stream context
+// ctx16 = softmax(S/T) . K16.
 // --------------------------------------------------------------------------------------------
 constexpr int kSelWarps = 8;
 
@@ -236,17 +238,30 @@ __device__ __forceinline__ unsigned long long shfl_xor_u64(unsigned long long v,
   return ((unsigned long long)hi << 32) | lo;
 }
 
-// Descending bitonic sort of N = 32*E keys held in registers, blocked layout: element i lives in
-// lane i / E, register i % E.  Partners closer than E are in the same lane; farther ones are one
-// shuffle away.  The network is fixed at compile time.
+// Descending bitonic sort of N = 32*E keys held in registers.  The result is in blocked layout
+// (element i in lane i / E, register i % E); the input arrangement is arbitrary.  Merge stages are
+// runtime loops (small code: one warp sorts one token while its neighbours run the same few hundred
+// instructions); only the register-local steps are unrolled.
 template <int E>
 __device__ __forceinline__ void warp_bitonic_desc(unsigned long long (&v)[E], int lane) {
   constexpr int N = 32 * E;
-#pragma unroll
+#pragma unroll 1
   for (int k = 2; k <= N; k <<= 1) {
+#pragma unroll 1
+    for (int j = k >> 1; j >= E; j >>= 1) {  // partner in lane ^ (j / E)
+      const int m = j / E;
+      const bool lower = (lane & m) == 0;
 #pragma unroll
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      if (j < E) {
+      for (int r = 0; r < E; ++r) {
+        const bool desc = (((lane * E + r) & k) == 0);
+        const unsigned long long o = shfl_xor_u64(v[r], m);
+        const bool keep_max = (desc == lower);
+        v[r] = keep_max ? (v[r] > o ? v[r] : o) : (v[r] < o ? v[r] : o);
+      }
+    }
+#pragma unroll
+    for (int j = E >> 1; j > 0; j >>= 1) {  // partner in the same lane
+      if (j < k) {
 #pragma unroll
         for (int r = 0; r < E; ++r) {
           const int rp = r ^ j;
@@ -258,268 +273,668 @@ __device__ __forceinline__ void warp_bitonic_desc(unsigned long long (&v)[E], in
             v[rp] = sw ? a : b;
           }
         }
-      } else {
-        const int m = j / E;
-        const bool lower = (lane & m) == 0;
-#pragma unroll
-        for (int r = 0; r < E; ++r) {
-          const bool desc = (((lane * E + r) & k) == 0);
-          const unsigned long long o = shfl_xor_u64(v[r], m);
-          const bool keep_max = (desc == lower);
-          v[r] = keep_max ? (v[r] > o ? v[r] : o) : (v[r] < o ? v[r] : o);
-        }
       }
     }
   }
 }
 
-// One warp per token row of scores.  Softmax over all blocks (core.py:36-43), base mass credit
-// (:104), stable descending order of remote probabilities (:105-108; ties -> lower id), fp64-accumulated
-// cumulative sum (:109), count clamp (:111-119), sorted ids (:121-123).  Optionally the additive-stream
-// context ctx16 = softmax(S/T) . K16 (foveal_pattention.py:339-340).
-template <int E>
-__global__ void __launch_bounds__(kSelWarps * 32)
-select_blocks_kernel(const float* __restrict__ scores, int64_t M, int NB, int base, float top_p, int k_min,
-                     int k_max, int capacity, float temperature, int32_t* __restrict__ out_idx,
-                     int32_t* __restrict__ out_cnt, const float* __restrict__ k16f,
-                     float* __restrict__ ctx16, float* __restrict__ stats, uint4* __restrict__ hzero,
-                     int64_t hrow_vec) {
-  constexpr int N = 32 * E;
-  __shared__ float spb[kSelWarps][N];
-  extern __shared__ float sk16[];  // [NB][16] fp32 block keys (only when ctx16 is requested)
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  if (ctx16) {
-    for (int i = threadIdx.x; i < NB * 16; i += blockDim.x) sk16[i] = k16f[i];
-    __syncthreads();
+// Top `need` keys in descending order without sorting all N: the need-th largest probability word T
+// is found by a bitwise search with warp-wide counts (only the bits below the common prefix of the
+// smallest and largest remote word are searched), the keys with hi word >= T are compacted into cbuf
+// (C slots) and only those are sorted.  Result in blocked layout (position lane*(C/32) + q in out[q]).
+// Returns false, with nothing sorted, when more than C keys tie at or above T.
+template <int E, int C>
+__device__ __forceinline__ bool sort_top(const unsigned long long (&key)[E], int need, unsigned long long* cbuf,
+                                         unsigned long long (&out)[C / 32], int lane) {
+  uint32_t hi[E];
+  uint32_t mx = 0u, mn = 0xFFFFFFFFu;
+#pragma unroll
+  for (int r = 0; r < E; ++r) {
+    hi[r] = (uint32_t)(key[r] >> 32);  // remote keys: bits(p) + 1 >= 1; base and padding: 0
+    mx = hi[r] > mx ? hi[r] : mx;
+    if (hi[r] != 0u && hi[r] < mn) mn = hi[r];
   }
-  float* pbuf = spb[warp];
-  for (int64_t tok = (int64_t)blockIdx.x * kSelWarps + warp; tok < M; tok += (int64_t)gridDim.x * kSelWarps) {
-  const float* srow = scores + tok * NB;
-  if (hzero) {  // clear this token's row of the masked activations H while the warp computes
-    uint4* hr = hzero + tok * hrow_vec;
-    for (int64_t i = lane; i < hrow_vec; i += 32) hr[i] = make_uint4(0u, 0u, 0u, 0u);
+  mx = __reduce_max_sync(0xffffffffu, mx);
+  mn = __reduce_min_sync(0xffffffffu, mn);
+  const uint32_t diff = mn ^ mx;
+  int bit = diff ? 31 - __clz(diff) : -1;
+  uint32_t T = diff ? (mx & ~((2u << bit) - 1u)) : mx;  // bits above `bit` are common to [mn, mx]
+  for (; bit >= 0; --bit) {
+    const uint32_t cand = T | (1u << bit);
+    int c = 0;
+#pragma unroll
+    for (int r = 0; r < E; ++r) c += hi[r] >= cand ? 1 : 0;
+    if (__reduce_add_sync(0xffffffffu, c) >= need) T = cand;
   }
+  int total = 0;
+  const uint32_t lt = (1u << lane) - 1u;
+#pragma unroll
+  for (int r = 0; r < E; ++r) {
+    const bool f = hi[r] >= T;
+    const uint32_t bal = __ballot_sync(0xffffffffu, f);
+    const int pos = total + __popc(bal & lt);
+    if (f && pos < C) cbuf[pos] = key[r];
+    total += __popc(bal);
+  }
+  if (total > C) return false;
+  __syncwarp();
+#pragma unroll
+  for (int q = 0; q < C / 32; ++q) {
+    const int i = lane * (C / 32) + q;
+    out[q] = i < total ? cbuf[i] : 0ull;
+  }
+  __syncwarp();  // cbuf may be rewritten from here on
+  warp_bitonic_desc<C / 32>(out, lane);
+  return true;
+}
 
-  // blocked layout: lane owns blocks lane*E .. lane*E+E-1
-  float p[E];
+// Selection of one token on one warp.  s[r] is the (temperature-scaled) score of block r*32 + lane.
+// pbuf: this warp's shared row of 32*E floats; sbuf (optional): shared row receiving the sorted block
+// ids; skT (needed with ctx16): [16][ks] fp32 block keys, transposed (row stride ks >= NB).  Returns the
+// remote count on every lane (0 in context-only mode).
+// Reference: masked_softmax core.py:36-43; select_blocks core.py:101-123 (base mass :104, stable
+// descending order :105-108 with ties to the lower id, cumsum :109, clamp :111-119, ids :121-123);
+// context foveal_pattention.py:339-340.
+template <int E>
+__device__ __forceinline__ int select_token(float (&s)[E], int64_t tok, const SelectOut& o, float* pbuf,
+                                            int32_t* sbuf, const float* skT, int ks, int lane) {
+  constexpr int N = 32 * E;
+  const int NB = o.NB;
   float mx = -INFINITY;
 #pragma unroll
   for (int r = 0; r < E; ++r) {
-    const int b = lane * E + r;
-    float sv = -INFINITY;
-    if (b < NB) {
-      sv = srow[b];
-      if (temperature != 1.0f) sv = __fdiv_rn(sv, temperature);
-    }
-    p[r] = sv;
-    mx = fmaxf(mx, sv);
+    if (r * 32 + lane >= NB) s[r] = -INFINITY;
+    mx = fmaxf(mx, s[r]);
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  for (int m = 16; m > 0; m >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m));
   if (!isfinite(mx)) mx = 0.f;
   float sum = 0.f;
 #pragma unroll
   for (int r = 0; r < E; ++r) {
-    const int b = lane * E + r;
-    const float e = b < NB ? expf(p[r] - mx) : 0.f;
-    p[r] = e;
+    const float e = r * 32 + lane < NB ? expf(s[r] - mx) : 0.f;
+    s[r] = e;
     sum += e;
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  for (int m = 16; m > 0; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
   const float denom = fmaxf(sum, 1e-20f);
   unsigned long long key[E];
 #pragma unroll
   for (int r = 0; r < E; ++r) {
-    const int b = lane * E + r;
-    p[r] = __fdiv_rn(p[r], denom);
-    key[r] = b < NB ? sel_key(p[r], b, b >= base) : 0ull;
-    pbuf[b] = p[r];
+    const int b = r * 32 + lane;
+    s[r] = __fdiv_rn(s[r], denom);
+    key[r] = b < NB ? sel_key(s[r], b, b >= o.base) : 0ull;
+    pbuf[b] = s[r];
   }
+  if (o.ctx16) {
+    // lane-partial context over this lane's blocks, then a butterfly reduce-scatter: after the steps
+    // over lane bits 4..1 lane L holds channel (L >> 1) summed over 16 lanes; the last step adds L ^ 1
+    float c[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) c[j] = 0.f;
+#pragma unroll
+    for (int r = 0; r < E; ++r) {
+      const int b = r * 32 + lane;
+      if (b < NB) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) c[j] = fmaf(s[r], skT[j * ks + b], c[j]);
+      }
+    }
+#pragma unroll
+    for (int h = 8; h >= 1; h >>= 1) {  // 16 -> 8 -> 4 -> 2 -> 1 values per lane
+      const bool up = (lane & (2 * h)) != 0;
+#pragma unroll
+      for (int i = 0; i < h; ++i) {
+        const float send = up ? c[i] : c[i + h];
+        const float keep = up ? c[i + h] : c[i];
+        c[i] = keep + __shfl_xor_sync(0xffffffffu, send, 2 * h);
+      }
+    }
+    c[0] += __shfl_xor_sync(0xffffffffu, c[0], 1);
+    if ((lane & 1) == 0) o.ctx16[tok * 16 + (lane >> 1)] = c[0];
+  }
+  if (o.idx == nullptr) return 0;  // context-only mode
   __syncwarp();
-
-  if (ctx16) {
-    // lane L accumulates channel j = L % 16 over blocks b = L / 16, L / 16 + 2, ...: each load step reads
-    // two contiguous 64-byte key rows; the two halves are combined with one shuffle
-    const int j = lane & 15;
-    float c = 0.f;
-    for (int b = lane >> 4; b < NB; b += 2) c = fmaf(pbuf[b], sk16[b * 16 + j], c);
-    c += __shfl_xor_sync(0xffffffffu, c, 16);
-    if (lane < 16) ctx16[tok * 16 + j] = c;
-  }
-  if (out_idx == nullptr) { __syncwarp(); continue; }  // context-only mode
 
   // base (local) mass (core.py:104): sequential over the base blocks
   float local_mass = 0.f;
   if (lane == 0)
-    for (int b = 0; b < base && b < NB; ++b) local_mass += pbuf[b];
-
-  warp_bitonic_desc<E>(key, lane);
-
-  int32_t* orow = out_idx + tok * capacity;
-#pragma unroll
-  for (int r = 0; r < E; ++r) {
-    const int i = lane * E + r;
-    if (i < capacity) orow[i] = i < NB ? (int32_t)(0xFFFFFFFFu - (uint32_t)(key[r] & 0xFFFFFFFFull)) : 0;
-    const uint32_t hi = (uint32_t)(key[r] >> 32);
-    pbuf[i] = hi ? __uint_as_float(hi - 1u) : 0.f;  // sorted, clamped probabilities
-  }
-  for (int i = N + lane; i < capacity; i += 32) orow[i] = 0;
+    for (int b = 0; b < o.base && b < NB; ++b) local_mass += pbuf[b];
   __syncwarp();
 
-  if (lane == 0) {
-    float target = top_p - local_mass;
-    target = target > 0.f ? target : 0.f;
-    const int available = NB - base;
-    int counts = 0;
-    if (available > 0) {
-      const int X = available < k_max ? available : k_max;
-      int needed;
-      if (target > 0.f) {
-        double acc = 0.0;
-        int n = 0;
-        for (; n < X; ++n) {
-          acc += (double)pbuf[n];
-          if ((float)acc >= target) break;
-        }
-        needed = n + 1;  // #(cum < target) + 1; saturates at X + 1 when never reached within X
-      } else {
-        needed = 0;
+  const int avail = NB - o.base;
+  const int X = avail < o.k_max ? avail : o.k_max;  // positions the cumulative sum may need
+  const int need = o.capacity > X ? o.capacity : X;  // sorted positions required
+  int32_t* orow = o.idx + tok * o.capacity;
+  bool done = false;
+  auto emit = [&](unsigned long long kv, int i) {
+    const int32_t id = i < NB ? (int32_t)(0xFFFFFFFFu - (uint32_t)(kv & 0xFFFFFFFFull)) : 0;
+    if (i < o.capacity) orow[i] = id;
+    if (sbuf) sbuf[i] = id;
+    const uint32_t hi = (uint32_t)(kv >> 32);
+    pbuf[i] = hi ? __uint_as_float(hi - 1u) : 0.f;  // sorted, clamped probabilities
+  };
+  float target = o.top_p - local_mass;  // lane 0's local mass; broadcast below
+  target = __shfl_sync(0xffffffffu, target, 0);
+  target = target > 0.f ? target : 0.f;
+  int below = -1;  // #(cum < target) among the first X sorted probabilities, when found in registers
+  // Cumulative sum of the sorted probabilities held in registers (Q consecutive positions per lane).
+  // The reference accumulates sequentially in fp64 and rounds each prefix to fp32.  When every summand
+  // is 0 or >= 2^-29, all partial sums are multiples of 2^-52 below 2, so fp64 addition is exact and
+  // a warp scan gives the same prefixes; otherwise the sequential loop below runs.
+  auto scan_count = [&](const auto& top, auto qconst) {
+    constexpr int Q = decltype(qconst)::value;
+    float pv[Q];
+    bool ok = true;
+#pragma unroll
+    for (int q = 0; q < Q; ++q) {
+      const uint32_t hi = (uint32_t)(top[q] >> 32);
+      pv[q] = (lane * Q + q < X && hi) ? __uint_as_float(hi - 1u) : 0.f;
+      ok = ok && (pv[q] == 0.f || pv[q] >= 0x1p-29f);
+    }
+    if (!__all_sync(0xffffffffu, ok)) return;
+    double own = 0.0;
+#pragma unroll
+    for (int q = 0; q < Q; ++q) own += (double)pv[q];
+    double incl = own;
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+      const double up = __shfl_up_sync(0xffffffffu, incl, m);
+      if (lane >= m) incl += up;
+    }
+    double c = incl - own;  // exact (all values are multiples of 2^-52 below 2)
+    int n = 0;
+#pragma unroll
+    for (int q = 0; q < Q; ++q) {
+      c += (double)pv[q];
+      n += __popc(__ballot_sync(0xffffffffu, lane * Q + q < X && (float)c < target));
+    }
+    below = n;
+  };
+  if constexpr (E >= 4) {
+    if (need >= 1 && need <= 64 && avail >= need) {
+      unsigned long long top[2];
+      if (sort_top<E, 64>(key, need, reinterpret_cast<unsigned long long*>(pbuf), top, lane)) {
+        emit(top[0], 2 * lane);
+        emit(top[1], 2 * lane + 1);
+        if (target > 0.f) scan_count(top, std::integral_constant<int, 2>{});
+        done = true;
       }
-      needed = needed > k_min ? needed : k_min;
-      counts = needed < available ? needed : available;
-      counts = counts < k_max ? counts : k_max;
+    }
+  }
+  if constexpr (E >= 8) {
+    if (!done && need > 64 && need <= 128 && avail >= need) {
+      unsigned long long top[4];
+      if (sort_top<E, 128>(key, need, reinterpret_cast<unsigned long long*>(pbuf), top, lane)) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) emit(top[q], 4 * lane + q);
+        if (target > 0.f) scan_count(top, std::integral_constant<int, 4>{});
+        done = true;
+      }
+    }
+  }
+  if (!done) {  // full sort of all N keys
+    warp_bitonic_desc<E>(key, lane);
+#pragma unroll
+    for (int r = 0; r < E; ++r) emit(key[r], lane * E + r);
+    for (int i = N + lane; i < o.capacity; i += 32) orow[i] = 0;
+  }
+  __syncwarp();
+
+  int counts = 0;
+  if (lane == 0) {
+    if (avail > 0) {
+      int needed = 0;
+      if (target > 0.f) {
+        if (below < 0) {
+          // sequential fp64 cumulative sum over the first X sorted probabilities (the prefix is
+          // monotone, so counting prefixes below the target equals the reference's count once clamped)
+          double acc = 0.0;
+          below = 0;
+          for (int q = 0; q < X; q += 4) {
+            const float4 v4 = *reinterpret_cast<const float4*>(pbuf + q);
+            const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              if (q + u < X) {
+                acc += (double)vv[u];
+                below += (float)acc < target ? 1 : 0;
+              }
+            }
+          }
+        }
+        needed = below + 1;
+      }
+      needed = needed > o.k_min ? needed : o.k_min;
+      counts = needed < avail ? needed : avail;
+      counts = counts < o.k_max ? counts : o.k_max;
       if (counts < 0) counts = 0;
     }
-    out_cnt[tok] = counts;
-    if (stats) {
-      atomicAdd(&stats[0], (k_max > 0 && counts >= k_max) ? 1.f : 0.f);
-      atomicAdd(&stats[1], (float)counts);
-      atomicAdd(&stats[2], counts == 0 ? 1.f : 0.f);
+    o.cnt[tok] = counts;
+    if (o.stats) {
+      atomicAdd(&o.stats[0], (o.k_max > 0 && counts >= o.k_max) ? 1.f : 0.f);
+      atomicAdd(&o.stats[1], (float)counts);
+      atomicAdd(&o.stats[2], counts == 0 ? 1.f : 0.f);
     }
   }
-  __syncwarp();  // pbuf is rewritten by the next token of this warp
+  counts = __shfl_sync(0xffffffffu, counts, 0);
+  return counts;
+}
+
+// Standalone selection over a score matrix (fp_select_blocks): one warp per token row, persistent.
+template <int E>
+__global__ void __launch_bounds__(kSelWarps * 32)
+select_blocks_kernel(const float* __restrict__ scores, int64_t M, float temperature, const SelectOut o,
+                     const float* __restrict__ k16f) {
+  constexpr int N = 32 * E;
+  extern __shared__ float4 sel_smem4[];
+  float* pball = reinterpret_cast<float*>(sel_smem4);  // [kSelWarps][N]
+  float* skT = pball + kSelWarps * N;                  // [16][NB] (only with ctx16)
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  if (o.ctx16) {
+    for (int i = threadIdx.x; i < o.NB * 16; i += blockDim.x) {
+      const int j = i / o.NB, b = i - j * o.NB;
+      skT[i] = k16f[b * 16 + j];
+    }
+    __syncthreads();
+  }
+  float* pbuf = pball + warp * N;
+  for (int64_t tok = (int64_t)blockIdx.x * kSelWarps + warp; tok < M; tok += (int64_t)gridDim.x * kSelWarps) {
+    const float* srow = scores + tok * o.NB;
+    float s[E];
+#pragma unroll
+    for (int r = 0; r < E; ++r) {
+      const int b = r * 32 + lane;
+      float v = -INFINITY;
+      if (b < o.NB) {
+        v = srow[b];
+        if (temperature != 1.0f) v = __fdiv_rn(v, temperature);
+      }
+      s[r] = v;
+    }
+    select_token<E>(s, tok, o, pbuf, nullptr, skT, o.NB, lane);
+    __syncwarp();  // pbuf is rewritten by the next token of this warp
   }
 }
 
 // --------------------------------------------------------------------------------------------
-// Block CSR (block-major token lists) in token chunks: key = chunk(t) * NBL + slot(b), where only
-// blocks with b % stride == offset are local and slot(b) = b / stride.
+// Fused token routing of the forward: scores, selection and the block-major token lists in one
+// kernel.  A CTA routes 16 tokens: its warps first split the 16-D projection x W_q^T over the hidden
+// dimension (mma.sync bf16, or fp32 FFMA with one warp per token), then each warp finishes its
+// token(s): RMSNorm, the NB block scores, the selection, and the block-CSR entries.
+//
+// Block CSR: key = chunk(t) * NBL + slot(b) (token chunks of `chunk` tokens; only blocks with
+// b % stride == offset are local, slot(b) = b / stride).  Every key owns a fixed bucket of key_cap
+// entries of pair_tok (a token enters a key at most once), filled through an atomic counter per key,
+// so no separate counting pass is needed; the order of tokens inside a bucket does not change any
+// result (each token column of a gate/up tile is computed independently).  The last CTA to finish
+// (atomic ticket) turns the key counts into the gate/up tile list.
 // --------------------------------------------------------------------------------------------
-__device__ __forceinline__ int token_block(int s, int base, const int32_t* ridx, int cap, int cnt) {
-  // slot s < base: base block s; otherwise the (s-base)-th selected remote block, or -1
-  if (s < base) return s;
-  const int r = s - base;
-  return r < cnt ? ridx[r] : -1;
+// Raises a kernel's dynamic shared-memory limit once per kernel (to the largest size asked so far).
+template <auto Kern>
+int ensure_smem(size_t smem) {
+  static std::mutex mu;
+  static size_t granted = 48 * 1024;
+  if (smem <= 48 * 1024) return FP_OK;
+  std::lock_guard<std::mutex> lock(mu);
+  if (smem <= granted) return FP_OK;
+  if (cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return FP_ERR_CUDA;
+  granted = smem;
+  return FP_OK;
 }
 
-// One CTA per kCsrTokens consecutive tokens (all inside one token chunk): block counts are gathered in
-// a shared-memory histogram and folded into the global counts with one atomic per touched key.
-constexpr int kCsrTokens = 128;
+constexpr int kRouteWarps = 8;
+constexpr int kRouteTokens = 16;                          // the mma.sync M dimension
+constexpr int kRouteTPW = kRouteTokens / kRouteWarps;     // tokens per warp in the per-token phase
+constexpr uint32_t kRouteZeroBytes = 16384;               // zero source of the bulk H clears
 
-__global__ void __launch_bounds__(256)
-csr_count_kernel(const int32_t* __restrict__ ridx, const int32_t* __restrict__ rcnt, int64_t M, int base,
-                 int cap, int stride, int offset, int nbl, int chunk, int32_t* __restrict__ key_cnt) {
-  extern __shared__ int32_t hist[];  // [nbl]
-  for (int i = threadIdx.x; i < nbl; i += blockDim.x) hist[i] = 0;
-  __syncthreads();
-  const int64_t t0 = (int64_t)blockIdx.x * kCsrTokens;
-  const int slots = base + cap;
-  const int64_t t_end = min(M, t0 + kCsrTokens);
-  for (int64_t i = (int64_t)threadIdx.x; i < (t_end - t0) * slots; i += blockDim.x) {
-    const int64_t t = t0 + i / slots;
-    const int b = token_block((int)(i % slots), base, ridx + t * cap, cap, rcnt[t]);
-    if (b >= 0 && (b % stride) == offset) atomicAdd(&hist[b / stride], 1);
-  }
-  __syncthreads();
-  const int kbase = (int)(t0 / chunk) * nbl;
-  for (int k = threadIdx.x; k < nbl; k += blockDim.x)
-    if (hist[k]) atomicAdd(&key_cnt[kbase + k], hist[k]);
+// Dynamic shared-memory layout of route_kernel (byte offsets, 16-byte aligned).
+struct RouteSmem {
+  int zbuf, skT, pbuf, sbuf, plist, cnt, kbase, total;
+};
+__host__ __device__ inline RouteSmem route_smem(int NB, int nbl, int E, bool hz, bool csr) {
+  auto al = [](int v) { return (v + 15) & ~15; };
+  const int N = 32 * E, nbp = (NB + 3) & ~3;
+  RouteSmem L;
+  int o = 0;
+  L.zbuf = o;  o += hz ? (int)kRouteZeroBytes : 0;
+  L.skT = o;   o += al(16 * nbp * 4);
+  L.pbuf = o;  o += kRouteWarps * N * 4;
+  L.sbuf = o;  o += kRouteWarps * N * 4;
+  L.plist = o; o += csr ? kRouteTokens * N * 4 : 0;
+  L.cnt = o;   o += csr ? al(nbl * 4) : 0;
+  L.kbase = o; o += csr ? al(nbl * 4) : 0;
+  L.total = o;
+  return L;
 }
 
-// Single CTA: exclusive scan of key counts and the tile list (key, first row); the tiles of one key
-// have equal size (balanced_rows).
-__global__ void __launch_bounds__(1024)
-csr_scan_kernel(const int32_t* __restrict__ key_cnt, int nkey, int32_t* __restrict__ key_off,
-                int32_t* __restrict__ key_fill, int2* __restrict__ tiles, int max_tiles,
-                int32_t* __restrict__ meta, int* err) {
-  __shared__ int s_pairs[1024], s_tiles[1024];
-  const int tid = threadIdx.x;
-  const int per = (nkey + 1023) / 1024;
-  const int k0 = tid * per, k1 = min(nkey, k0 + per);
+// Gate/up tile list from the key counts (one CTA): exclusive scan of per-key tile counts, then the
+// (key, first row) descriptor of every tile in key order.
+__device__ void build_tile_list(const RouteArgs& a) {
+  __shared__ int s_wp[32], s_wt[32];
+  const int tid = threadIdx.x, nth = blockDim.x, lane = tid & 31, warp = tid >> 5;
+  const int per = (a.nkey + nth - 1) / nth;
+  const int k0 = min(a.nkey, tid * per), k1 = min(a.nkey, k0 + per);
   int pairs = 0, ntile = 0;
   for (int k = k0; k < k1; ++k) {
-    pairs += key_cnt[k];
-    ntile += (key_cnt[k] + kGuN - 1) / kGuN;
+    const int c = __ldcg(&a.key_cnt[k]);
+    pairs += c;
+    ntile += (c + kGuN - 1) / kGuN;
   }
-  s_pairs[tid] = pairs;
-  s_tiles[tid] = ntile;
+  int ip = pairs, it = ntile;  // inclusive warp scan
+#pragma unroll
+  for (int m = 1; m < 32; m <<= 1) {
+    const int up = __shfl_up_sync(0xffffffffu, ip, m), ut = __shfl_up_sync(0xffffffffu, it, m);
+    if (lane >= m) { ip += up; it += ut; }
+  }
+  if (lane == 31) { s_wp[warp] = ip; s_wt[warp] = it; }
   __syncthreads();
-  for (int o = 1; o < 1024; o <<= 1) {  // Hillis-Steele inclusive scan
-    const int a = tid >= o ? s_pairs[tid - o] : 0;
-    const int b = tid >= o ? s_tiles[tid - o] : 0;
-    __syncthreads();
-    s_pairs[tid] += a;
-    s_tiles[tid] += b;
-    __syncthreads();
+  if (warp == 0) {
+    const int nw = nth >> 5;
+    int wp = lane < nw ? s_wp[lane] : 0, wt = lane < nw ? s_wt[lane] : 0;
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+      const int up = __shfl_up_sync(0xffffffffu, wp, m), ut = __shfl_up_sync(0xffffffffu, wt, m);
+      if (lane >= m) { wp += up; wt += ut; }
+    }
+    if (lane < nw) { s_wp[lane] = wp; s_wt[lane] = wt; }  // inclusive over warps
   }
-  int poff = s_pairs[tid] - pairs, toff = s_tiles[tid] - ntile;
+  __syncthreads();
+  int toff = (warp > 0 ? s_wt[warp - 1] : 0) + it - ntile;
   for (int k = k0; k < k1; ++k) {
-    const int c = key_cnt[k];
-    key_off[k] = poff;
-    key_fill[k] = 0;
+    const int c = __ldcg(&a.key_cnt[k]);
     const int rows = balanced_rows(c);
     for (int r = 0; r < c; r += rows) {
-      if (toff < max_tiles) tiles[toff] = make_int2(k, r);
+      if (toff < a.max_tiles) a.tiles[toff] = make_int2(k, r);
       ++toff;
     }
-    poff += c;
   }
-  if (tid == 1023) {
-    key_off[nkey] = s_pairs[1023];
-    const int nt = s_tiles[1023];
-    meta[0] = nt < max_tiles ? nt : max_tiles;
-    meta[1] = s_pairs[1023];
-    if (nt > max_tiles) record_error(err, kErrBadTile);
+  if (tid == nth - 1) {
+    const int nw = nth >> 5;
+    const int nt = s_wt[nw - 1];
+    a.meta[0] = nt < a.max_tiles ? nt : a.max_tiles;
+    a.meta[1] = s_wp[nw - 1];
+    if (nt > a.max_tiles) record_error(a.err, kErrBadTile);
   }
 }
 
-// Same partition as csr_count_kernel: local histogram, one global reservation per key, then the
-// scatter of token ids with shared-memory positions.
-__global__ void __launch_bounds__(256)
-csr_fill_kernel(const int32_t* __restrict__ ridx, const int32_t* __restrict__ rcnt, int64_t M, int base,
-                int cap, int stride, int offset, int nbl, int chunk, const int32_t* __restrict__ key_off,
-                int32_t* __restrict__ key_fill, int32_t* __restrict__ pair_tok) {
-  extern __shared__ int32_t sh[];  // hist[nbl], start[nbl]
-  int32_t* hist = sh;
-  int32_t* start = sh + nbl;
-  for (int i = threadIdx.x; i < nbl; i += blockDim.x) hist[i] = 0;
-  __syncthreads();
-  const int64_t t0 = (int64_t)blockIdx.x * kCsrTokens;
-  const int slots = base + cap;
-  const int64_t t_end = min(M, t0 + kCsrTokens);
-  const int64_t n = (t_end - t0) * slots;
-  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
-    const int64_t t = t0 + i / slots;
-    const int b = token_block((int)(i % slots), base, ridx + t * cap, cap, rcnt[t]);
-    if (b >= 0 && (b % stride) == offset) atomicAdd(&hist[b / stride], 1);
+// Stage the block keys K16 [NB][16] transposed into skT[16][nbp] (fp32).  One thread per key row:
+// vector loads when the rows are 16-byte aligned.
+template <typename T>
+__device__ __forceinline__ void stage_keys(const T* __restrict__ k16, int NB, int nbp, float* skT) {
+  const bool vec = (reinterpret_cast<uintptr_t>(k16) & 15u) == 0;
+  for (int b = threadIdx.x; b < NB; b += blockDim.x) {
+    float kv[16];
+    if (vec) {
+      const uint4* src = reinterpret_cast<const uint4*>(k16 + (int64_t)b * 16);
+      constexpr int kVec = 16 * (int)sizeof(T) / 16;
+      uint4 u[kVec];
+#pragma unroll
+      for (int i = 0; i < kVec; ++i) u[i] = __ldg(src + i);
+      const T* tv = reinterpret_cast<const T*>(u);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) kv[j] = to_f32(tv[j]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) kv[j] = to_f32(k16[(int64_t)b * 16 + j]);
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) skT[j * nbp + b] = kv[j];
   }
-  __syncthreads();
-  const int kbase = (int)(t0 / chunk) * nbl;
-  for (int k = threadIdx.x; k < nbl; k += blockDim.x) {
-    start[k] = hist[k] ? key_off[kbase + k] + atomicAdd(&key_fill[kbase + k], hist[k]) : 0;
-    hist[k] = 0;
-  }
-  __syncthreads();
-  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
-    const int64_t t = t0 + i / slots;
-    const int b = token_block((int)(i % slots), base, ridx + t * cap, cap, rcnt[t]);
-    if (b >= 0 && (b % stride) == offset) {
-      const int k = b / stride;
-      pair_tok[start[k] + atomicAdd(&hist[k], 1)] = (int32_t)t;
+}
+
+// Raw 16-D router projections x W_q^T of 16 tokens per CTA -> qraw [M, 16] (fp32).
+// bf16 with D % 64 == 0: mma.sync over 64-element chunks of the hidden dimension, interleaved over the
+// warps, partials summed in warp order.  Otherwise fp32 FFMA, two tokens per warp: lanes split the
+// hidden dimension in 8-element vectors, then a butterfly sum.
+template <typename T, bool kMma>
+__global__ void __launch_bounds__(kRouteWarps * 32, 2)
+route_proj_kernel(const T* __restrict__ x, const T* __restrict__ wq, int64_t M, int D, float* __restrict__ qraw) {
+  constexpr int W = kRouteWarps, TPW = kRouteTPW;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t tok0 = (int64_t)blockIdx.x * kRouteTokens;
+  if constexpr (kMma) {
+    __shared__ float part[W * 16 * 17];
+    const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(x);
+    const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(wq);
+    const int g = lane >> 2, t = lane & 3;
+    const int64_t ra = tok0 + g < M ? tok0 + g : M - 1;
+    const int64_t rb = tok0 + g + 8 < M ? tok0 + g + 8 : M - 1;
+    const __nv_bfloat16* pa = xb + ra * D + 16 * t;
+    const __nv_bfloat16* pb = xb + rb * D + 16 * t;
+    const __nv_bfloat16* qa = wb + (int64_t)g * D + 16 * t;
+    const __nv_bfloat16* qb = wb + (int64_t)(8 + g) * D + 16 * t;
+    float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+    const int nk = D / 64;
+#pragma unroll 2
+    for (int kc = warp; kc < nk; kc += W) {
+      uint32_t A0[8], A1[8], B0[8], B1[8];
+      const int k0 = kc * 64;
+      ld32B(pa + k0, A0);
+      ld32B(pb + k0, A1);
+      ld32B(qa + k0, B0);
+      ld32B(qb + k0, B1);
+#pragma unroll
+      for (int st = 0; st < 4; ++st) {
+        mma_bf16_16816(c0, A0[2 * st], A1[2 * st], A0[2 * st + 1], A1[2 * st + 1], B0[2 * st], B0[2 * st + 1]);
+        mma_bf16_16816(c1, A0[2 * st], A1[2 * st], A0[2 * st + 1], A1[2 * st + 1], B1[2 * st], B1[2 * st + 1]);
+      }
+    }
+    // c0: projections 2t, 2t+1 of tokens g (c0[0..1]) and g+8 (c0[2..3]); c1: projections 8+2t, 9+2t
+    float* q = part + warp * 16 * 17;
+    q[g * 17 + 2 * t] = c0[0];
+    q[g * 17 + 2 * t + 1] = c0[1];
+    q[(g + 8) * 17 + 2 * t] = c0[2];
+    q[(g + 8) * 17 + 2 * t + 1] = c0[3];
+    q[g * 17 + 8 + 2 * t] = c1[0];
+    q[g * 17 + 9 + 2 * t] = c1[1];
+    q[(g + 8) * 17 + 8 + 2 * t] = c1[2];
+    q[(g + 8) * 17 + 9 + 2 * t] = c1[3];
+    __syncthreads();
+    const int r = warp * TPW + (lane >> 4), j = lane & 15;  // lane (tt, j) of token warp*TPW + tt
+    float v = part[r * 17 + j];
+#pragma unroll
+    for (int w = 1; w < W; ++w) v += part[w * 16 * 17 + r * 17 + j];
+    if (tok0 + r < M) qraw[(tok0 + r) * 16 + j] = v;
+  } else {
+    float acc[TPW][16];
+#pragma unroll
+    for (int tt = 0; tt < TPW; ++tt)
+#pragma unroll
+      for (int j = 0; j < 16; ++j) acc[tt][j] = 0.f;
+    for (int c = lane * 8; c < D; c += 256) {
+      float xv[TPW][8];
+#pragma unroll
+      for (int tt = 0; tt < TPW; ++tt) {
+        const int64_t tk = tok0 + warp * TPW + tt;
+        load8<T>(x + (tk < M ? tk : M - 1) * D + c, xv[tt]);
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        float wv[8];
+        load8<T>(wq + (int64_t)j * D + c, wv);
+#pragma unroll
+        for (int tt = 0; tt < TPW; ++tt)
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[tt][j] = fmaf(xv[tt][e], wv[e], acc[tt][j]);
+      }
+    }
+#pragma unroll
+    for (int tt = 0; tt < TPW; ++tt) {
+      float mine = 0.f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        float v = acc[tt][j];
+#pragma unroll
+        for (int m = 16; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+        if (lane == j) mine = v;
+      }
+      const int64_t tk = tok0 + warp * TPW + tt;
+      if (lane < 16 && tk < M) qraw[tk * 16 + lane] = mine;
     }
   }
+}
+
+// Persistent: each CTA stages the keys once, then routes groups of 16 tokens from their raw 16-D
+// projections (route_proj_kernel).
+template <typename T, int E>
+__global__ void __launch_bounds__(kRouteWarps * 32, E <= 8 ? 3 : 1)
+route_kernel(const RouteArgs a) {
+  constexpr int TPW = kRouteTPW, N = 32 * E;
+  extern __shared__ float4 route_smem4[];
+  char* smb = reinterpret_cast<char*>(route_smem4);
+  const bool csr = a.key_cnt != nullptr;
+  const RouteSmem L = route_smem(a.NB, a.nbl, E, a.hzero != nullptr, csr);
+  const int nbp = (a.NB + 3) & ~3;
+  float* skT = reinterpret_cast<float*>(smb + L.skT);       // [16][nbp] fp32 block keys, transposed
+  int32_t* s_cnt = reinterpret_cast<int32_t*>(smb + L.cnt); // [nbl] group-local pairs per key
+  int32_t* s_kb = reinterpret_cast<int32_t*>(smb + L.kbase);// [nbl] reserved start in the key bucket
+  __shared__ float qsm[kRouteTokens][16];                   // raw 16-D projections of the group
+  __shared__ int s_npair[kRouteTokens];
+  __shared__ unsigned int s_ticket;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int NB = a.NB;
+  const int64_t ngroups = (a.M + kRouteTokens - 1) / kRouteTokens;
+  const uint64_t hrow = (uint64_t)a.hrow_vec * 16;
+
+  // ---- once per CTA: keys, the zero source of the H clears, the key counters
+  stage_keys<T>(static_cast<const T*>(a.k16), NB, nbp, skT);
+  if (a.hzero) {
+    uint4* z = reinterpret_cast<uint4*>(smb + L.zbuf);
+    for (int i = threadIdx.x; i < (int)(kRouteZeroBytes / 16); i += blockDim.x) z[i] = make_uint4(0u, 0u, 0u, 0u);
+    fence_proxy_async_smem();
+  }
+  if (csr)
+    for (int i = threadIdx.x; i < a.nbl; i += blockDim.x) s_cnt[i] = 0;
+  __syncthreads();
+
+  for (int64_t grp = blockIdx.x; grp < ngroups; grp += gridDim.x) {
+    const int64_t tok0 = grp * kRouteTokens;
+    const int ntok = (int)((a.M - tok0) < kRouteTokens ? (a.M - tok0) : kRouteTokens);
+    if (a.hzero && threadIdx.x == 0) {
+      // the masked activations H must read zero for unselected (token, block) pairs: clear the group's
+      // contiguous rows with bulk copies from the zero buffer while the warps route
+      bulk_wait_read<2>();  // bound the clears in flight
+      char* dst = reinterpret_cast<char*>(a.hzero) + (uint64_t)tok0 * hrow;
+      const uint64_t total = (uint64_t)ntok * hrow;
+      const uint32_t zs = smem_u32(smb + L.zbuf);
+      for (uint64_t off = 0; off < total; off += kRouteZeroBytes) {
+        const uint64_t rest = total - off;
+        bulk_store(dst + off, zs, (uint32_t)(rest < kRouteZeroBytes ? rest : kRouteZeroBytes));
+      }
+      bulk_commit();
+    }
+    {  // this warp's tokens only (other warps may already be working on theirs): lane (tt, j)
+      const int r = warp * TPW + (lane >> 4);
+      if (tok0 + r < a.M) qsm[r][lane & 15] = __ldcg(&a.qraw[(tok0 + r) * 16 + (lane & 15)]);
+      if (lane < TPW) s_npair[warp * TPW + lane] = 0;
+    }
+    __syncwarp();
+
+    // ---- per token: RMSNorm, scores, selection, group-local CSR entries
+    float* pbuf = reinterpret_cast<float*>(smb + L.pbuf) + warp * N;
+    int32_t* sbuf = reinterpret_cast<int32_t*>(smb + L.sbuf) + warp * N;
+    const float eps = 1.1920928955078125e-07f;  // torch.finfo(float32).eps: F.rms_norm's default
+#pragma unroll 1
+    for (int tt = 0; tt < TPW; ++tt) {
+      const int r = warp * TPW + tt;
+      const int64_t tok = tok0 + r;
+      if (tok >= a.M) break;
+      float qn[16];
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        qn[j] = qsm[r][j];
+        ss = fmaf(qn[j], qn[j], ss);
+      }
+      const float inv = __fdiv_rn(1.0f, __fsqrt_rn(ss * (1.0f / 16.0f) + eps));
+      float qown = 0.f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        if (lane == j) qown = qn[j];
+        qn[j] *= inv;
+      }
+      if (a.q16 && lane < 16) a.q16[tok * 16 + lane] = qown * inv;
+      float s[E];
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const int b = e * 32 + lane;
+        float sc = -INFINITY;
+        if (b < NB) {
+          float acc = 0.f;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc = fmaf(qn[j], skT[j * nbp + b], acc);
+          acc *= 0.25f;  // / sqrt(16): exact power-of-two scaling
+          if (a.scores) a.scores[tok * NB + b] = acc;
+          sc = a.temperature != 1.0f ? __fdiv_rn(acc, a.temperature) : acc;
+        }
+        s[e] = sc;
+      }
+      const int counts = select_token<E>(s, tok, a.sel, pbuf, csr ? sbuf : nullptr, skT, nbp, lane);
+      if (csr) {
+        __syncwarp();
+        // pair list entry: (local key << 4) | position among this group's tokens of that key, or -1
+        int32_t* pl = reinterpret_cast<int32_t*>(smb + L.plist) + r * N;
+        const int npair = a.sel.base + counts;
+        for (int sl = lane; sl < npair; sl += 32) {
+          const int b = sl < a.sel.base ? sl : sbuf[sl - a.sel.base];
+          int e = -1;
+          if (b % a.stride == a.offset) {
+            const int kl = b / a.stride;
+            e = (kl << 4) | atomicAdd(&s_cnt[kl], 1);
+          }
+          pl[sl] = e;
+        }
+        if (lane == 0) s_npair[r] = npair;
+      }
+      __syncwarp();  // pbuf / sbuf are rewritten by the next token of this warp
+    }
+
+    __syncthreads();  // qsm, part, the pair lists and the key counters of the group are complete
+    if (csr) {
+      // one global reservation per key for the group's tokens (all in one token chunk), then the scatter
+      const int64_t kb = (tok0 / a.chunk) * a.nbl;
+      for (int k = threadIdx.x; k < a.nbl; k += blockDim.x) {
+        const int c = s_cnt[k];
+        s_kb[k] = c ? atomicAdd(&a.key_cnt[kb + k], c) : 0;
+        s_cnt[k] = 0;  // ready for the next group
+      }
+      __syncthreads();
+#pragma unroll 1
+      for (int tt = 0; tt < TPW; ++tt) {
+        const int r = warp * TPW + tt;
+        const int32_t* pl = reinterpret_cast<const int32_t*>(smb + L.plist) + r * N;
+        const int npair = s_npair[r];
+        for (int sl = lane; sl < npair; sl += 32) {
+          const int e = pl[sl];
+          if (e >= 0) {
+            const int kl = e >> 4;
+            const int64_t pos = (int64_t)s_kb[kl] + (e & 15);
+            if (pos < a.key_cap) a.pair_tok[(kb + kl) * a.key_cap + pos] = (int32_t)(tok0 + r);
+            else record_error(a.err, kErrBadTile);
+          }
+        }
+      }
+      __syncthreads();  // s_kb and the pair lists are reused by the next group
+    }
+  }
+
+  if (csr) {
+    // the last CTA to finish turns the key counts into the gate/up tile list
+    if (threadIdx.x == 0) {
+      __threadfence();
+      s_ticket = atomicAdd(a.ticket, 1u);
+    }
+    __syncthreads();
+    if (s_ticket == gridDim.x - 1) {
+      __threadfence();
+      build_tile_list(a);
+    }
+  }
+  if (a.hzero && threadIdx.x == 0) bulk_wait_all();  // the H clears complete before the CTA retires
 }
 
 // --------------------------------------------------------------------------------------------
@@ -650,65 +1065,71 @@ int launch_router_scores(const void* x, const void* wq, const void* k16, int dty
   return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
 }
 
-static int pow2_at_least(int n) {
-  int p = 32;
-  while (p < n) p <<= 1;
-  return p;
-}
-
-__global__ void convert_keys_kernel(const void* k16, int dtype, int n, float* out) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  out[i] = dtype == FP_DTYPE_BF16 ? __bfloat162float(((const __nv_bfloat16*)k16)[i]) : ((const float*)k16)[i];
-}
-
-int launch_select(const float* scores, int64_t M, int NB, int base, float top_p, int k_min, int k_max,
-                  int capacity, float temperature, int32_t* idx, int32_t* cnt, const float* k16f,
-                  float* ctx16, float* stats, cudaStream_t st, void* hzero, int64_t hrow_bytes) {
-  if (M <= 0) return FP_OK;
+template <int E>
+int select_go(const float* scores, int64_t M, float temperature, const SelectOut& o, const float* k16f,
+              cudaStream_t st) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t need = (M + kSelWarps - 1) / kSelWarps;
   const int blocks = (int)std::min<int64_t>(need, (int64_t)sms * 8);
-  const size_t smem = ctx16 ? (size_t)NB * 16 * sizeof(float) : 0;
-  auto go = [&](auto kern) {
-    if (smem > 48 * 1024 &&
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return FP_ERR_CUDA;
-    kern<<<blocks, kSelWarps * 32, smem, st>>>(scores, M, NB, base, top_p, k_min, k_max, capacity, temperature,
-                                               idx, cnt, k16f, ctx16, stats, (uint4*)hzero, hrow_bytes / 16);
-    return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
-  };
-  if (NB <= 32) return go(select_blocks_kernel<1>);
-  if (NB <= 64) return go(select_blocks_kernel<2>);
-  if (NB <= 128) return go(select_blocks_kernel<4>);
-  if (NB <= 256) return go(select_blocks_kernel<8>);
-  if (NB <= 512) return go(select_blocks_kernel<16>);
-  if (NB <= 1024) return go(select_blocks_kernel<32>);
+  const size_t smem = (size_t)kSelWarps * 32 * E * sizeof(float) + (o.ctx16 ? (size_t)o.NB * 16 * sizeof(float) : 0);
+  if (ensure_smem<select_blocks_kernel<E>>(smem) != FP_OK) return FP_ERR_CUDA;
+  select_blocks_kernel<E><<<blocks, kSelWarps * 32, smem, st>>>(scores, M, temperature, o, k16f);
+  return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+}
+
+int launch_select(const float* scores, int64_t M, int NB, int base, float top_p, int k_min, int k_max,
+                  int capacity, float temperature, int32_t* idx, int32_t* cnt, const float* k16f,
+                  float* ctx16, float* stats, cudaStream_t st) {
+  if (M <= 0) return FP_OK;
+  const SelectOut o{NB, base, top_p, k_min, k_max, capacity, idx, cnt, ctx16, stats};
+  if (NB <= 32) return select_go<1>(scores, M, temperature, o, k16f, st);
+  if (NB <= 64) return select_go<2>(scores, M, temperature, o, k16f, st);
+  if (NB <= 128) return select_go<4>(scores, M, temperature, o, k16f, st);
+  if (NB <= 256) return select_go<8>(scores, M, temperature, o, k16f, st);
+  if (NB <= 512) return select_go<16>(scores, M, temperature, o, k16f, st);
+  if (NB <= 1024) return select_go<32>(scores, M, temperature, o, k16f, st);
   return FP_ERR_UNSUPPORTED;
 }
 
-int launch_convert_keys(const void* k16, int dtype, int n, float* out, cudaStream_t st) {
-  convert_keys_kernel<<<(n + 255) / 256, 256, 0, st>>>(k16, dtype, n, out);
+template <typename T, int E>
+int route_go(const RouteArgs& a, bool mma, cudaStream_t st) {
+  const int64_t groups = (a.M + kRouteTokens - 1) / kRouteTokens;
+  if (mma)
+    route_proj_kernel<__nv_bfloat16, true><<<(unsigned)groups, kRouteWarps * 32, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(a.x), static_cast<const __nv_bfloat16*>(a.wq), a.M, a.D, a.qraw);
+  else
+    route_proj_kernel<T, false><<<(unsigned)groups, kRouteWarps * 32, 0, st>>>(
+        static_cast<const T*>(a.x), static_cast<const T*>(a.wq), a.M, a.D, a.qraw);
+  if (cudaGetLastError() != cudaSuccess) return FP_ERR_CUDA;
+  const size_t smem = (size_t)route_smem(a.NB, a.nbl, E, a.hzero != nullptr, a.key_cnt != nullptr).total;
+  if (ensure_smem<route_kernel<T, E>>(smem) != FP_OK) return FP_ERR_CUDA;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, route_kernel<T, E>, kRouteWarps * 32, smem) !=
+      cudaSuccess)
+    return FP_ERR_CUDA;
+  const int64_t blocks = std::min<int64_t>(groups, (int64_t)std::max(per_sm, 1) * std::max(a.num_sms, 1));
+  route_kernel<T, E><<<(unsigned)blocks, kRouteWarps * 32, smem, st>>>(a);
   return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
 }
 
-int launch_build_csr(const int32_t* ridx, const int32_t* rcnt, int64_t M, int base, int cap, int stride,
-                     int offset, int nbl, int chunk, int nkey, int32_t* key_cnt, int32_t* key_off,
-                     int32_t* key_fill, int32_t* pair_tok, int2* tiles, int max_tiles, int32_t* meta, int* err,
-                     cudaStream_t st) {
-  if (chunk % kCsrTokens) return FP_ERR_INVALID_ARG;
-  if (cudaMemsetAsync(key_cnt, 0, sizeof(int32_t) * nkey, st) != cudaSuccess) return FP_ERR_CUDA;
-  const int blocks = (int)((M + kCsrTokens - 1) / kCsrTokens);
-  if (blocks > 0)
-    csr_count_kernel<<<blocks, 256, nbl * sizeof(int32_t), st>>>(ridx, rcnt, M, base, cap, stride, offset, nbl,
-                                                                chunk, key_cnt);
-  csr_scan_kernel<<<1, 1024, 0, st>>>(key_cnt, nkey, key_off, key_fill, tiles, max_tiles, meta, err);
-  if (blocks > 0)
-    csr_fill_kernel<<<blocks, 256, 2 * nbl * sizeof(int32_t), st>>>(ridx, rcnt, M, base, cap, stride, offset, nbl,
-                                                                    chunk, key_off, key_fill, pair_tok);
-  return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+template <int E>
+int route_dtype(const RouteArgs& a, int dtype, cudaStream_t st) {
+  if (dtype == FP_DTYPE_F32) return route_go<float, E>(a, false, st);
+  return route_go<__nv_bfloat16, E>(a, a.D % 64 == 0, st);
+}
+
+int launch_route(const RouteArgs& a, int dtype, cudaStream_t st) {
+  if (a.M <= 0) return FP_OK;
+  if (dtype != FP_DTYPE_F32 && dtype != FP_DTYPE_BF16) return FP_ERR_UNSUPPORTED;
+  if (a.NB <= 32) return route_dtype<1>(a, dtype, st);
+  if (a.NB <= 64) return route_dtype<2>(a, dtype, st);
+  if (a.NB <= 128) return route_dtype<4>(a, dtype, st);
+  if (a.NB <= 256) return route_dtype<8>(a, dtype, st);
+  if (a.NB <= 512) return route_dtype<16>(a, dtype, st);
+  if (a.NB <= 1024) return route_dtype<32>(a, dtype, st);
+  return FP_ERR_UNSUPPORTED;
 }
 
 int launch_colmean(const void* a, int dtype, int64_t M, int D, float* part, float* mean, cudaStream_t st) {
@@ -720,6 +1141,12 @@ int launch_colmean(const void* a, int dtype, int64_t M, int D, float* part, floa
     colsum_partial_kernel<float><<<g, 256, 0, st>>>((const float*)a, M, D, part);
   colsum_final_kernel<<<(D + 255) / 256, 256, 0, st>>>(part, nchunk, M, D, mean);
   return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+}
+
+static int pow2_at_least(int n) {
+  int p = 32;
+  while (p < n) p <<= 1;
+  return p;
 }
 
 int launch_pooled_topk(const float* mean_vec, const void* wq, const void* k16, int dtype, int D, int NB,

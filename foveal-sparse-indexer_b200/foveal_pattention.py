@@ -29,6 +29,28 @@ from torch import Tensor, nn
 from . import kernels
 
 
+def _chunk_plan(M: int, ch: int) -> list:
+    """Chunk sizes for the host-streamed forward: ``ch`` tokens in the middle, ``ch/4`` and ``ch/2``
+    at both ends when the batch is long enough (a short first chunk starts compute early; a short last
+    chunk shortens the final copy-out)."""
+    ramp = [c for c in (ch // 4, ch // 2) if c >= 256]
+    head, tail, left = [], [], M
+    for c in ramp:
+        if left <= 0:
+            break
+        head.append(min(c, left))
+        left -= head[-1]
+    for c in ramp:
+        if left > ch + c:
+            tail.insert(0, c)
+            left -= c
+    mid = []
+    while left > 0:
+        mid.append(min(ch, left))
+        left -= mid[-1]
+    return head + mid + tail
+
+
 class _ForwardOnly(torch.autograd.Function):
     """Attaches a backward that raises, so a training graph through the kernels fails loudly."""
 
@@ -232,15 +254,17 @@ class FovealPattentionMLP(nn.Module):
                     "sparsity": (1.0 - self.total_active_blocks / self.num_blocks) * 100.0}
         return y, info
 
-    def forward_host(self, x_host: Tensor, out: Optional[Tensor] = None, chunk_tokens: int = 2048) -> Tensor:
+    def forward_host(self, x_host: Tensor, out: Optional[Tensor] = None, chunk_tokens: int = 4096) -> Tensor:
         """Token-routed forward of a batch held in host memory.
 
-        The batch is processed in chunks of ``chunk_tokens`` tokens on three CUDA streams of the module's
-        device: the host-to-device copy of chunk i+1 and the device-to-host copy of chunk i-1 run while
-        chunk i is computed.  Tokens are routed independently, so the result equals ``forward`` on the
-        whole batch.  ``x_host`` (and ``out``, if given) should be pinned for the copies to overlap.
-        Returns the output in host memory; it is complete once the caller's current stream has been
-        synchronised (the current stream is made to wait for the last copy).
+        The batch is processed in chunks on CUDA streams of the module's device: one stream copies
+        chunks in, one copies results out, and two compute streams take alternate chunks, so that the
+        kernels of one chunk overlap the tail of the previous one and both copies overlap compute.  The
+        first and last chunks are smaller (``chunk_tokens`` / 4, / 2) to shorten the pipeline fill and
+        drain.  Tokens are routed independently, so the result equals ``forward`` on the whole batch.
+        ``x_host`` (and ``out``, if given) should be pinned for the copies to overlap.  Returns the output
+        in host memory; it is complete once the caller's current stream has been synchronised (the
+        current stream is made to wait for the last copy).
         """
         if self.routing != "token":
             raise ValueError("forward_host needs routing='token' (pooled routing pools over the whole call)")
@@ -259,25 +283,28 @@ class FovealPattentionMLP(nn.Module):
             out = torch.empty(x_host.shape[:-1] + (D,), dtype=dt, pin_memory=True)
         y2d = out.reshape(-1, D)
         kg, ku, v, packed, wq, k16, wout = self._weights()
-        ch = max(1, min(int(chunk_tokens), M))
+        plan = _chunk_plan(M, max(1, int(chunk_tokens)))
+        ch = max(plan) if plan else 1
         st = getattr(self, "_host_streams", None)
         if st is None or st[0].device != dev:
-            st = tuple(torch.cuda.Stream(device=dev) for _ in range(3))
+            st = tuple(torch.cuda.Stream(device=dev) for _ in range(4))
             self._host_streams = st
-        s_in, s_cmp, s_out = st
+        s_in, s_out, s_c0, s_c1 = st
+        nslot = 3
         bufs = getattr(self, "_host_bufs", None)
         if bufs is None or bufs[0].shape[0] < ch or bufs[0].shape[1] != D or bufs[0].dtype != dt:
-            bufs = [torch.empty(ch, D, dtype=dt, device=dev) for _ in range(4)]  # x0, x1, y0, y1
+            bufs = [torch.empty(ch, D, dtype=dt, device=dev) for _ in range(2 * nslot)]  # x slots, y slots
             self._host_bufs = bufs
         cur = torch.cuda.current_stream(dev)
         for s_ in st:
             s_.wait_stream(cur)
-        x_free = [None, None]
-        y_free = [None, None]
-        for i, c0 in enumerate(range(0, M, ch)):
-            n = min(ch, M - c0)
-            slot = i & 1
-            xb, yb = bufs[slot][:n], bufs[2 + slot][:n]
+        x_free = [None] * nslot  # compute of the slot's previous chunk done
+        y_free = [None] * nslot  # copy-out of the slot's previous chunk done
+        c0 = 0
+        for i, n in enumerate(plan):
+            slot = i % nslot
+            s_cmp = s_c0 if i % 2 == 0 else s_c1
+            xb, yb = bufs[slot][:n], bufs[nslot + slot][:n]
             with torch.cuda.stream(s_in):
                 if x_free[slot] is not None:
                     s_in.wait_event(x_free[slot])
@@ -301,6 +328,7 @@ class FovealPattentionMLP(nn.Module):
                 e_out = torch.cuda.Event()
                 e_out.record(s_out)
                 y_free[slot] = e_out
+            c0 += n
         for s_ in st:
             cur.wait_stream(s_)
         return out

@@ -243,12 +243,14 @@ def test_forward_host_matches_forward():
     w = configs.make_weights(wl)
     x2d = configs.make_x(wl).reshape(-1, wl.hidden_dim)[:5000].contiguous().to(torch.bfloat16)
     m = module_for(wl, w)
+    xh = x2d.pin_memory()
     with torch.no_grad():
         ref = m(x2d.to(DEV))
-        y = m.forward_host(x2d.pin_memory(), chunk_tokens=2048)
+        ys = [m.forward_host(xh, chunk_tokens=c) for c in (1024, 4096)]  # 9 and 3 chunks, 2 compute streams
     torch.cuda.synchronize()
-    assert y.device.type == "cpu" and y.shape == ref.shape
-    assert rel_err(y.float(), ref.float().cpu()) < 1e-3
+    for y in ys:
+        assert y.device.type == "cpu" and y.shape == ref.shape
+        assert rel_err(y.float(), ref.float().cpu()) < 1e-3
 
 
 # ------------------------------------------------------------------ edge cases
