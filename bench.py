@@ -54,7 +54,7 @@ def parse():
     ap.add_argument("--mode", choices=["default", "decode", "sweep"], default="default",
                     help="decode / sweep print one JSON line per point instead of the bench line")
     ap.add_argument("--e2e-steps", type=int, default=0)
-    ap.add_argument("--chunk-tokens", type=int, default=4096)
+    ap.add_argument("--chunk-tokens", type=int, default=2048)
     ap.add_argument("--cpu-sample", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()

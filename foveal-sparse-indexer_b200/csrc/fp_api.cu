@@ -31,6 +31,8 @@ int local_blocks(int NB, int stride, int offset) {
 
 bool tensor_path(int dtype, int D) { return dtype == FP_DTYPE_BF16 && D % 64 == 0 && D >= 64; }
 
+int layout_sms();
+
 struct TokenLayout {
   size_t err, zero_bytes, key_cnt, meta, qraw, ridx, rcnt, ctx, pair_tok, tiles, h, yacc, total;
   int ksplit;
@@ -64,7 +66,7 @@ TokenLayout token_layout(int dtype, int64_t M, int D, int NB, int base, int kmax
     L.pair_tok = c.take((size_t)L.nkey * L.key_cap * 4);
     L.tiles = c.take((size_t)L.max_tiles * 8);
     L.h = c.take((size_t)M * L.nbl * kBlock * 2);
-    L.ksplit = down_ksplit(M, D, std::max(L.nbl, 1));
+    L.ksplit = down_ksplit(M, D, std::max(L.nbl, 1), layout_sms());
     if (L.ksplit > 1) L.yacc = c.take((size_t)L.ksplit * M * D * 4);
   }
   L.total = c.off;
@@ -86,7 +88,7 @@ PooledLayout pooled_layout(int dtype, int64_t M, int D, int NB, int n_active) {
   L.mean = c.take((size_t)width * 4);
   if (tensor_path(dtype, D)) {
     L.h = c.take((size_t)M * std::max(n_active, 1) * kBlock * 2);
-    L.ksplit = down_ksplit(M, D, std::max(n_active, 1));
+    L.ksplit = down_ksplit(M, D, std::max(n_active, 1), layout_sms());
     if (L.ksplit > 1) L.yacc = c.take((size_t)L.ksplit * M * D * 4);
   }
   L.total = c.off;
@@ -121,6 +123,14 @@ int device_info(int& num_sms) {
   }
   num_sms = sms;
   return major == 10 ? FP_OK : FP_ERR_DEVICE;
+}
+
+// SM count the split-K choice of the workspace layout is made for; kMaxSms when no device can be queried
+// (a layout for more splits is never smaller).
+int layout_sms() {
+  int sms = 0;
+  if (device_info(sms) == FP_OK && sms > 0 && sms <= kMaxSms) return sms;
+  return kMaxSms;
 }
 
 int check_common(int dtype, int64_t M, int D, int NB) {

@@ -628,11 +628,15 @@ int launch_down(const DownArgs& a, cudaStream_t st) {
   return FP_OK;
 }
 
-int down_ksplit(int64_t M, int D, int nkb) {
+int down_ksplit(int64_t M, int D, int nkb, int num_sms) {
+  // Only batches whose output tiles fill at most half of the SMs are split: every split then streams the
+  // same k-blocks of V_t at the same time as the other tiles (all CTAs move through the contraction in
+  // step, so each V_t block is read from HBM once).  Shares of a tile that run at different k positions
+  // (stream-K) were measured to re-read V_t from HBM several times at these shapes (V_t is 117 MB at 8B).
   const int64_t tiles = ((M + kTileM - 1) / kTileM) * ((D + kTileN - 1) / kTileN);
-  if (tiles <= 0 || tiles >= 64) return 1;
-  int ks = (int)((128 + tiles - 1) / tiles);  // aim at ~128 CTAs
-  ks = std::min(ks, std::max(1, nkb / 4));     // at least 4 k-blocks per split
+  if (tiles <= 0 || 2 * tiles > num_sms) return 1;
+  int ks = (int)(num_sms / tiles);
+  ks = std::min(ks, std::max(1, nkb / 4));  // at least 4 k-blocks per split
   return std::max(ks, 1);
 }
 

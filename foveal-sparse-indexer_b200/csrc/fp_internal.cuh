@@ -128,7 +128,8 @@ struct DownArgs {
 int launch_down(const DownArgs& a, cudaStream_t st);
 // Split-K factor used by the down projection for M tokens (1 = none).  Small batches (decode) have too
 // few output tiles to occupy the GPU, so the contraction over parameter blocks is split instead.
-int down_ksplit(int64_t M, int D, int nkb);
+int down_ksplit(int64_t M, int D, int nkb, int num_sms);
+constexpr int kMaxSms = 256;  // SM count assumed when the workspace is sized without a device to query
 
 // ---- simt.cu (CUDA-core path: fp32 models and shapes the tensor-core path does not tile)
 struct SimtArgs {

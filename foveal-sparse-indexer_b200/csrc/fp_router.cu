@@ -587,8 +587,11 @@ int ensure_smem(size_t smem) {
 }
 
 constexpr int kRouteWarps = 8;
-constexpr int kRouteTokens = 16;                          // the mma.sync M dimension
-constexpr int kRouteTPW = kRouteTokens / kRouteWarps;     // tokens per warp in the per-token phase
+constexpr int kProjTokens = 16;                           // tokens per projection CTA (the mma.sync M dimension)
+constexpr int kProjTPW = kProjTokens / kRouteWarps;       // tokens per warp of the projection's FFMA form
+constexpr int kRouteTPW = 1;                              // tokens per warp in a routing group
+constexpr int kRouteTokens = kRouteWarps * kRouteTPW;     // tokens per routing group (at most 16)
+static_assert(kRouteTokens <= 16, "group-local pair positions are packed in 4 bits");
 constexpr uint32_t kRouteZeroBytes = 16384;               // zero source of the bulk H clears
 
 // Dynamic shared-memory layout of route_kernel (byte offsets, 16-byte aligned).
@@ -693,9 +696,9 @@ __device__ __forceinline__ void stage_keys(const T* __restrict__ k16, int NB, in
 template <typename T, bool kMma>
 __global__ void __launch_bounds__(kRouteWarps * 32, 2)
 route_proj_kernel(const T* __restrict__ x, const T* __restrict__ wq, int64_t M, int D, float* __restrict__ qraw) {
-  constexpr int W = kRouteWarps, TPW = kRouteTPW;
+  constexpr int W = kRouteWarps, TPW = kProjTPW;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t tok0 = (int64_t)blockIdx.x * kRouteTokens;
+  const int64_t tok0 = (int64_t)blockIdx.x * kProjTokens;
   if constexpr (kMma) {
     __shared__ float part[W * 16 * 17];
     const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(x);
@@ -829,7 +832,7 @@ route_kernel(const RouteArgs a) {
     }
     {  // this warp's tokens only (other warps may already be working on theirs): lane (tt, j)
       const int r = warp * TPW + (lane >> 4);
-      if (tok0 + r < a.M) qsm[r][lane & 15] = __ldcg(&a.qraw[(tok0 + r) * 16 + (lane & 15)]);
+      if (lane < 16 * TPW && tok0 + r < a.M) qsm[r][lane & 15] = __ldcg(&a.qraw[(tok0 + r) * 16 + (lane & 15)]);
       if (lane < TPW) s_npair[warp * TPW + lane] = 0;
     }
     __syncwarp();
@@ -1095,12 +1098,13 @@ int launch_select(const float* scores, int64_t M, int NB, int base, float top_p,
 
 template <typename T, int E>
 int route_go(const RouteArgs& a, bool mma, cudaStream_t st) {
+  const int64_t pblocks = (a.M + kProjTokens - 1) / kProjTokens;
   const int64_t groups = (a.M + kRouteTokens - 1) / kRouteTokens;
   if (mma)
-    route_proj_kernel<__nv_bfloat16, true><<<(unsigned)groups, kRouteWarps * 32, 0, st>>>(
+    route_proj_kernel<__nv_bfloat16, true><<<(unsigned)pblocks, kRouteWarps * 32, 0, st>>>(
         static_cast<const __nv_bfloat16*>(a.x), static_cast<const __nv_bfloat16*>(a.wq), a.M, a.D, a.qraw);
   else
-    route_proj_kernel<T, false><<<(unsigned)groups, kRouteWarps * 32, 0, st>>>(
+    route_proj_kernel<T, false><<<(unsigned)pblocks, kRouteWarps * 32, 0, st>>>(
         static_cast<const T*>(a.x), static_cast<const T*>(a.wq), a.M, a.D, a.qraw);
   if (cudaGetLastError() != cudaSuccess) return FP_ERR_CUDA;
   const size_t smem = (size_t)route_smem(a.NB, a.nbl, E, a.hzero != nullptr, a.key_cnt != nullptr).total;

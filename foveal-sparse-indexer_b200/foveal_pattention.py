@@ -254,7 +254,7 @@ class FovealPattentionMLP(nn.Module):
                     "sparsity": (1.0 - self.total_active_blocks / self.num_blocks) * 100.0}
         return y, info
 
-    def forward_host(self, x_host: Tensor, out: Optional[Tensor] = None, chunk_tokens: int = 4096) -> Tensor:
+    def forward_host(self, x_host: Tensor, out: Optional[Tensor] = None, chunk_tokens: int = 2048) -> Tensor:
         """Token-routed forward of a batch held in host memory.
 
         The batch is processed in chunks on CUDA streams of the module's device: one stream copies
