@@ -51,8 +51,11 @@ def parse():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="8b", help="8b (default) or 70b for the main measurement")
-    ap.add_argument("--mode", choices=["default", "decode", "sweep"], default="default",
-                    help="decode / sweep print one JSON line per point instead of the bench line")
+    ap.add_argument("--mode", choices=["default", "decode", "sweep", "blockshard"], default="default",
+                    help="decode / sweep print one JSON line per point instead of the bench line; blockshard "
+                         "(torchrun, >= 2 ranks) times the parameter-block-sharded forward of --config")
+    ap.add_argument("--chunks", type=int, default=1, help="blockshard: token chunks whose reduce-scatter "
+                    "overlaps the next chunk's compute")
     ap.add_argument("--e2e-steps", type=int, default=0)
     ap.add_argument("--chunk-tokens", type=int, default=2048)
     ap.add_argument("--cpu-sample", type=int, default=256)
@@ -439,6 +442,72 @@ def run_sweep(args):
                               "dense_ms_same_kernels": d_ours, "dense_ms_cublas": d_torch}), flush=True)
 
 
+def run_blockshard(args):
+    """Parameter-block sharding (strong scaling): every rank holds the same batch, computes the blocks
+    b % world == rank, and the fp32 partials are reduce-scattered over token rows chunk by chunk (NCCL on
+    a side stream, overlapping the next chunk's compute).  One JSON line: tokens/s of the whole batch
+    (max over ranks), and the same forward without the collectives for reference."""
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world < 2:
+        raise SystemExit("--mode blockshard needs torchrun with at least 2 ranks")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    wl = configs.CONFIGS[args.config if args.config != "8b" else "70b"]
+    w = configs.make_weights(wl)
+    m = fsi.FovealPattentionMLP(hidden_dim=wl.hidden_dim, intermediate_dim=wl.intermediate_dim,
+                                base_blocks=wl.base_blocks, remote_blocks=wl.max_remote_blocks,
+                                temperature=wl.temperature, dtype=torch.bfloat16, routing="token", top_p=wl.top_p,
+                                min_remote_blocks=wl.min_remote_blocks, max_remote_blocks=wl.max_remote_blocks)
+    m.load_state_dict({k: t.to(torch.bfloat16) for k, t in w.state_dict().items()}, strict=False)
+    m = m.to(dev).eval()
+    fsi.sharding.shard_parameter_blocks(m)
+    x = configs.make_x(wl).reshape(-1, wl.hidden_dim).to(dev, torch.bfloat16)
+    M, D = x.shape
+    chunks = max(1, args.chunks)
+
+    def step():
+        fsi.sharding.sharded_token_forward(m, x, reduce="scatter", chunks=chunks)
+
+    def compute_only():
+        fsi.sharding._cuda_partial(m, x, world, rank, rank == 0, False)
+
+    def timed(fn, K):
+        dist.barrier()
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(K):
+            fn()
+        s1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([s0.elapsed_time(s1) / K], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    with torch.no_grad():
+        for _ in range(max(3, args.warmup)):
+            step()
+            compute_only()
+        ms = timed(step, args.steps)
+        ms_compute = timed(compute_only, args.steps)
+    if rank == 0:
+        line = {"mode": "blockshard", "metric": METRIC, "value": M / (ms / 1e3), "unit": "tokens/s",
+                "n_gpus": world, "steps": args.steps, "ms_per_step": ms, "scaling": "strong",
+                "higher_is_better": True, "dtype": "bf16", "data": "synthetic (seeded)",
+                "config": {"workload": f"{wl.name}: token-routed forward, parameter blocks sharded b % {world}",
+                           "tokens": M, "d_model": D, "blocks": wl.num_blocks, "chunks": chunks,
+                           "parallelism": f"block-shard x{world} + NCCL reduce-scatter (fp32 partials)"},
+                "compute_only_ms": ms_compute,
+                "collective_bytes_per_rank": M * D * 4}
+        print(json.dumps(line), flush=True)
+    dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -447,6 +516,8 @@ def main():
         run_decode(args)
     elif args.mode == "sweep":
         run_sweep(args)
+    elif args.mode == "blockshard":
+        run_blockshard(args)
     else:
         run_ours(args)
 

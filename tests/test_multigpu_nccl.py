@@ -1,7 +1,8 @@
 """Parameter-block sharding over NCCL on 2 GPUs (skipped with fewer than 2 visible GPUs).
 
-Each rank computes the partial output of the blocks it owns (b % 2 == rank) for all tokens; one NCCL
-all-reduce (or reduce-scatter over token rows) sums the fp32 partials.  The result must match the
+Each rank computes the partial output of the blocks it owns (b % 2 == rank) for all tokens; an NCCL
+all-reduce (or reduce-scatter over token rows) sums the fp32 partials, in one piece or chunk by chunk
+with each chunk's collective overlapping the next chunk's compute.  The result must match the
 single-GPU forward within the bf16 tolerance, and the routes must be identical on both ranks.
 """
 
@@ -59,10 +60,13 @@ def _worker(rank, world, port, out_dir):
         fsi.sharding.shard_parameter_blocks(m)
         y, info = m(x, return_router_info=True)
         ys, _, _, _ = fsi.sharding.sharded_token_forward(m, x, reduce="scatter")
+        # chunked: each chunk's collective overlaps the next chunk's compute
+        yc, _, _, _ = fsi.sharding.sharded_token_forward(m, x, reduce="all", chunks=3)
+        ysc, _, _, _ = fsi.sharding.sharded_token_forward(m, x, reduce="scatter", chunks=4)
     torch.cuda.synchronize()
-    e_all = rel_err(y.float(), full.float())
     rows = slice(rank * 1024, (rank + 1) * 1024)
-    e_sc = rel_err(ys.float(), full[rows].float())
+    e_all = max(rel_err(y.float(), full.float()), rel_err(yc.float(), full.float()))
+    e_sc = max(rel_err(ys.float(), full[rows].float()), rel_err(ysc.float(), full[rows].float()))
     same_routes = bool(torch.equal(info["remote_indices"], info_full["remote_indices"]))
     with open(os.path.join(out_dir, f"r{rank}.txt"), "w") as f:
         f.write(f"{e_all} {e_sc} {int(same_routes)}")

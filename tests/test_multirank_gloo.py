@@ -1,8 +1,8 @@
 """Multi-rank host logic on CPU (gloo, world_size 2).
 
 * Parameter-block sharding: every rank routes all tokens, computes the partial output of the blocks it
-  owns (b % world == rank; the additive stream only on rank 0), and one all-reduce (or reduce-scatter)
-  sums the partials.  The partials here come from the CPU oracle restricted to the owned blocks, so the
+  owns (b % world == rank; the additive stream only on rank 0), and an all-reduce (or reduce-scatter)
+  sums the partials, in one piece or chunk by chunk.  The partials here come from the CPU oracle restricted to the owned blocks, so the
   test checks the decomposition and the collective wiring of ``sharding.sharded_token_forward``.
 * Failure detection: a rank that leaves before the collective makes the other rank's collective end
   with an error within the process-group timeout instead of hanging.
@@ -88,12 +88,18 @@ def _shard_worker(rank, world, port, out_dir):
     assert fsi.sharding.owned_blocks(10, rank, world) == list(range(rank, 10, world))
     y, _, _, _ = fsi.sharding.sharded_token_forward(m, x2d, compute_partial=_oracle_partial)
     ys, _, _, _ = fsi.sharding.sharded_token_forward(m, x2d, compute_partial=_oracle_partial, reduce="scatter")
+    # chunked: the collective of chunk i overlaps chunk i+1 on GPUs; here the decomposition and, for
+    # reduce-scatter, the rank-major chunk layout that keeps each rank's rows contiguous
+    yc, _, _, _ = fsi.sharding.sharded_token_forward(m, x2d, compute_partial=_oracle_partial, chunks=3)
+    ysc, _, _, _ = fsi.sharding.sharded_token_forward(m, x2d, compute_partial=_oracle_partial, reduce="scatter",
+                                                     chunks=4)
     ref = oracle.token_forward(x2d, m_weights(m), base_blocks=2, top_p=0.7, min_remote_blocks=1,
                                max_remote_blocks=3)["y"]
-    err = float((y - ref).norm() / ref.norm())
-    errs = float((ys - ref[rank * 16:(rank + 1) * 16]).norm() / ref[rank * 16:(rank + 1) * 16].norm())
+    mine = ref[rank * 16:(rank + 1) * 16]
+    errs_all = [float((t - ref).norm() / ref.norm()) for t in (y, yc)]
+    errs_sc = [float((t - mine).norm() / mine.norm()) for t in (ys, ysc)]
     with open(os.path.join(out_dir, f"r{rank}.txt"), "w") as f:
-        f.write(f"{err} {errs}")
+        f.write(" ".join(str(e) for e in errs_all + errs_sc))
     dist.destroy_process_group()
 
 
@@ -108,8 +114,8 @@ def test_block_sharded_forward_matches_full():
     with tempfile.TemporaryDirectory() as d:
         mp.spawn(_shard_worker, args=(2, port, d), nprocs=2, join=True)
         for r in range(2):
-            err, errs = map(float, open(os.path.join(d, f"r{r}.txt")).read().split())
-            assert err < 1e-5 and errs < 1e-5, (r, err, errs)
+            errs = list(map(float, open(os.path.join(d, f"r{r}.txt")).read().split()))
+            assert len(errs) == 4 and max(errs) < 1e-5, (r, errs)
 
 
 def _token_split_worker(rank, world, port, out_dir):
