@@ -42,6 +42,9 @@ SIGNATURES = {
     "fp_pattention_token_fwd_noalloc": (_c_int, [_c_p, _c_i64, _c_int, _c_int, _c_int, _c_p, _c_p, _c_p, _c_p, _c_p,
                                                  _c_p, _c_p, _c_p, _c_int, _c_f, _c_int, _c_int, _c_f, _c_int, _c_int,
                                                  _c_int, _c_p, _c_int, _c_p, _c_p, _c_p, _c_p]),
+    "fp_block_energy_workspace_size": (ctypes.c_size_t, [_c_i64, _c_int]),
+    "fp_block_energy": (_c_int, [_c_p, _c_i64, _c_int, _c_int, _c_int, _c_p, _c_p, _c_p, _c_p, ctypes.c_size_t,
+                                 _c_p]),
     "fp_set_stage_events": (_c_int, [ctypes.POINTER(_c_p), _c_int]),
     "fp_device_error": (_c_int, [_c_p, _c_p, _c_p]),
 }

@@ -108,6 +108,13 @@ def decode_points() -> List[Workload]:
             for k in DECODE_KMAX]
 
 
+def calib_workload() -> Workload:
+    """Offline router calibration case: the PR1 shape (D 512, 32 blocks) with
+    bf16-rounded weights and 512 bf16-rounded calibration tokens, so that the bf16 tensor-core path
+    and the fp32 reference see the same values."""
+    return CONFIGS["pr1"].with_(name="calib", dtype="bf16")
+
+
 @dataclass
 class Weights:
     """Parameter tensors with the reference module's names and shapes (fp32 storage, values already

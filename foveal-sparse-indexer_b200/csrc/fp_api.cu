@@ -397,6 +397,40 @@ int fp_pattention_pooled_fwd(const void* x, int64_t M, int D, int NB, int dtype,
   return FP_OK;
 }
 
+size_t fp_block_energy_workspace_size(int64_t M, int NB) {
+  Carve c;
+  c.take(256);                                   // error word
+  c.take((size_t)std::max(NB, 1) * 4);           // active ids 0..NB-1
+  c.take((size_t)4 * std::max<int64_t>(M, 0) * std::max(NB, 1) * 4);  // per-quarter partial energies
+  return c.off;
+}
+
+int fp_block_energy(const void* x, int64_t M, int D, int NB, int dtype, const void* w_gu, const float* vnorm,
+                    float* energy, void* workspace, size_t workspace_bytes, void* stream) {
+  FP_TRY(check_common(dtype, M, D, NB));
+  if (M == 0) return FP_OK;
+  if (!x || !w_gu || !vnorm || !energy || !workspace) return FP_ERR_INVALID_ARG;
+  if (!tensor_path(dtype, D)) return FP_ERR_UNSUPPORTED;
+  if (!aligned16(x) || !aligned16(w_gu)) return FP_ERR_INVALID_ARG;
+  if (workspace_bytes < fp_block_energy_workspace_size(M, NB)) return FP_ERR_WORKSPACE;
+  int sms;
+  FP_TRY(device_info(sms));
+  cudaStream_t st = (cudaStream_t)stream;
+  Carve c;
+  int* err = at<int>(workspace, c.take(256));
+  int32_t* act = at<int32_t>(workspace, c.take((size_t)NB * 4));
+  float* part = at<float>(workspace, c.take((size_t)4 * M * NB * 4));
+  if (cudaMemsetAsync(err, 0, 256, st) != cudaSuccess) return FP_ERR_CUDA;
+  FP_TRY(launch_iota(act, NB, st));
+  GateUpArgs g{};
+  g.x = x; g.w_gu = w_gu; g.M = M; g.D = D; g.Np = NB * kBlock;
+  g.tiles = nullptr; g.meta = nullptr; g.key_cnt = nullptr; g.pair_tok = nullptr; g.key_cap = 0;
+  g.nbl = NB; g.stride = 1; g.offset = 0; g.active = act; g.n_keys = NB;
+  g.h = nullptr; g.ldh = 0; g.energy = part; g.err = err; g.num_sms = sms;
+  FP_TRY(launch_gateup(g, st));
+  return launch_energy_combine(part, M, NB, vnorm, energy, st);
+}
+
 int fp_set_stage_events(void* const* events, int n_events) {
   if (n_events < 0 || n_events > 8 || (n_events > 0 && !events)) return FP_ERR_INVALID_ARG;
   for (int i = 0; i < 8; ++i) g_stage_events[i] = i < n_events ? (cudaEvent_t)events[i] : nullptr;

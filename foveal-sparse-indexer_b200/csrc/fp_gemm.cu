@@ -314,7 +314,17 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
           const float u = lane < 16 ? recv : __uint_as_float(v[16 + j]);
           const float h = __fdividef(gv, 1.0f + __expf(-gv)) * u;  // silu(g) * u
           const int tok = __shfl_sync(0xffffffffu, tok_l, lane < 16 ? j : 16 + j);
-          if (tok >= 0) hbase[(int64_t)tok * a.ldh] = __float2bfloat16_rn(h);
+          if (a.energy) {
+            // |h| summed over this half-warp's 16 channels (fixed order), one partial per TMEM quarter
+            float e = fabsf(h);
+            e += __shfl_xor_sync(0xffffffffu, e, 8);
+            e += __shfl_xor_sync(0xffffffffu, e, 4);
+            e += __shfl_xor_sync(0xffffffffu, e, 2);
+            e += __shfl_xor_sync(0xffffffffu, e, 1);
+            if ((lane & 15) == 0 && tok >= 0) a.energy[((int64_t)q * a.M + tok) * a.nbl + t.slot] = e;
+          } else if (tok >= 0) {
+            hbase[(int64_t)tok * a.ldh] = __float2bfloat16_rn(h);
+          }
         }
       }
       tc_fence_before();
@@ -593,6 +603,33 @@ int launch_gateup(const GateUpArgs& a, cudaStream_t st) {
   });
   if (attr != FP_OK) return attr;
   gateup_kernel<<<a.num_sms, kGuThreads, kGuSmem, st>>>(tx, tw, a);
+  return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+}
+
+__global__ void energy_combine_kernel(const float* __restrict__ part, int64_t M, int NB, const float* __restrict__ vnorm,
+                                      float* __restrict__ E) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // over M * NB
+  if (i >= M * NB) return;
+  const int64_t n = M * NB;
+  const float s = ((part[i] + part[n + i]) + part[2 * n + i]) + part[3 * n + i];
+  E[i] = s / 64.0f * vnorm[i % NB];
+}
+
+__global__ void iota_kernel(int32_t* out, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = i;
+}
+
+int launch_energy_combine(const float* part, int64_t M, int NB, const float* vnorm, float* E, cudaStream_t st) {
+  const int64_t n = M * NB;
+  if (n <= 0) return FP_OK;
+  energy_combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(part, M, NB, vnorm, E);
+  return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+}
+
+int launch_iota(int32_t* out, int n, cudaStream_t st) {
+  if (n <= 0) return FP_OK;
+  iota_kernel<<<(n + 255) / 256, 256, 0, st>>>(out, n);
   return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
 }
 

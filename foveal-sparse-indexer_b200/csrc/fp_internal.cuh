@@ -94,10 +94,16 @@ struct GateUpArgs {
   int n_keys;               // implicit mode: number of active blocks
   void* h;                  // [M, ldh] bf16 activations
   int64_t ldh;
+  // energy mode (instead of writing h): energy[q][t][key] = sum over the 16 channels of TMEM quarter q of
+  // |h[t, channel]| (fp32), for the teacher block energies of the offline calibration
+  float* energy;
   int* err;
   int num_sms;
 };
 int launch_gateup(const GateUpArgs& a, cudaStream_t st);
+// E[t, b] = (sum_q part[q][t][b]) / 64 * vnorm[b], quarters summed in order
+int launch_energy_combine(const float* part, int64_t M, int NB, const float* vnorm, float* E, cudaStream_t st);
+int launch_iota(int32_t* out, int n, cudaStream_t st);
 int launch_pack_gate_up(const void* kg, const void* ku, int Np, int D, void* wgu, cudaStream_t st);
 
 // Rows per gate/up tile of a block-CSR key with `cnt` tokens: ceil(cnt / kGuN) tiles of equal size,

@@ -20,6 +20,8 @@ differentiable: calling ``backward`` through it raises ``NotImplementedError``.
 
 from __future__ import annotations
 
+import math
+
 from typing import Any, Dict, List, Optional, Tuple
 
 import torch
@@ -171,9 +173,63 @@ class FovealPattentionMLP(nn.Module):
             nn.init.zeros_(m.out_proj_16d.weight)
         return m
 
+    @torch.no_grad()
     def calibrate_offline_svd(self, features: Tensor, ridge_lambda: float = 1e-2) -> Dict[str, float]:
-        raise NotImplementedError("offline SVD router calibration (foveal_pattention.py:175-255) is not "
-                                  "part of the forward library yet")
+        """Offline calibration of the 16-D router on the module's GPU (foveal_pattention.py:175-255):
+        q_proj_16d <- top-16 right singular vectors of the calibration tokens; block_keys_16d <- ridge
+        regression of the normalised 16-D projections onto softmax(teacher block energy / T); the
+        active set <- base blocks + the top ``remote_blocks`` mean calibrated scores.  Returns the
+        reference's dict (explained variance of the 16 directions, initial KL, active blocks, sparsity).
+
+        The teacher energies (the dense SwiGLU of every calibration token over every block) run on the
+        gate/up tensor-core kernel for bf16 modules (``fp_block_energy``; the calibration tokens are
+        taken in bf16, the module's own precision); the SVD, the 16 x 16 ridge solve and the small
+        reductions are cuSOLVER / PyTorch operations on the same GPU."""
+        dev = self.k_gate.device
+        if dev.type != "cuda":
+            raise RuntimeError("calibrate_offline_svd runs on the module's CUDA device; move the module first")
+        orig_dtype = self.k_gate.dtype
+        X = features.to(device=dev, dtype=torch.float32).reshape(-1, self.hidden_dim)
+        _, S, Vh = torch.linalg.svd(X, full_matrices=False)
+        if Vh.shape[0] < self.index_dim:
+            pad = torch.randn(self.index_dim - Vh.shape[0], self.hidden_dim, device=dev)
+            Vh = torch.cat([Vh, pad], dim=0)
+        V16 = Vh[: self.index_dim, :].T
+        self.q_proj_16d.weight.data.copy_(V16.T.to(dtype=orig_dtype))
+        Z = F.rms_norm(X @ V16, (self.index_dim,))
+        teacher = self._teacher_block_energy(X)
+        target = F.softmax(teacher / self.temperature, dim=-1)
+        reg = ridge_lambda * torch.eye(self.index_dim, device=dev)
+        block_keys = torch.linalg.solve(Z.T @ Z + reg, Z.T @ target).T
+        self.block_keys_16d.data.copy_(block_keys.to(dtype=orig_dtype))
+        scores = (Z @ block_keys.T) / math.sqrt(self.index_dim)
+        student = F.softmax(scores / self.temperature, dim=-1)
+        kl = F.kl_div(student.log(), target, reduction="batchmean").item()
+        mean_scores = scores.mean(dim=0)
+        _, top_rem = torch.topk(mean_scores[self.base_blocks:], k=self.remote_blocks)
+        calib_active = torch.cat([torch.arange(self.base_blocks, device=dev, dtype=torch.int32),
+                                  (top_rem + self.base_blocks).to(torch.int32)])
+        self.set_active_blocks(calib_active)
+        total_var = (S ** 2).sum().item()
+        top16_var = (S[: self.index_dim] ** 2).sum().item()
+        return {
+            "top16_explained_variance": top16_var / max(total_var, 1e-12),
+            "initial_kl_divergence": kl,
+            "num_blocks": self.num_blocks,
+            "active_blocks": self.total_active_blocks,
+            "calib_active_blocks": calib_active.tolist(),
+            "sparsity_pct": (1.0 - self.total_active_blocks / self.num_blocks) * 100.0,
+        }
+
+    def _teacher_block_energy(self, X: Tensor) -> Tensor:
+        """E[t, b] = mean_{j in b} |silu(x_t k_gate_j) (x_t k_up_j)| * ||v_b||_F  (foveal_pattention.py:205-216)."""
+        vnorm = self.v.detach().float().view(self.num_blocks, self.block_size, self.hidden_dim).norm(dim=(1, 2))
+        packed = self._packed()
+        if packed is not None:
+            return kernels.block_energy(X.to(torch.bfloat16), packed[0], vnorm, self.num_blocks)
+        # fp32 modules (and shapes the tensor-core tiles do not cover): the same expression with cuBLAS
+        A = F.silu(X @ self.k_gate.detach().float().t()) * (X @ self.k_up.detach().float().t())
+        return A.abs().view(X.shape[0], self.num_blocks, self.block_size).mean(dim=-1) * vnorm
 
     def compute_router_scores(self, x: Tensor) -> Tensor:
         """Per-token 16-D router scores (foveal_pattention.py:257-262), computed in fp32."""

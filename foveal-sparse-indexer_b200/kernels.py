@@ -100,6 +100,23 @@ def pack_weights(k_gate: torch.Tensor, k_up: torch.Tensor, v: torch.Tensor):
     return w_gu, vt
 
 
+def block_energy(x2d: torch.Tensor, w_gu: torch.Tensor, vnorm: torch.Tensor, num_blocks: int) -> torch.Tensor:
+    """Teacher block energies of the offline calibration (``fp_block_energy``): [M, NB] fp32 with
+    E[t, b] = mean over block b's channels of |silu(gate) * up| times ``vnorm[b]``.  bf16 x and packed
+    weights (:func:`pack_weights`)."""
+    dev = require_cuda(x2d, w_gu, vnorm)
+    x2d = contig(x2d)
+    vnorm = contig(vnorm.float())
+    M, D = x2d.shape
+    E = torch.empty(M, num_blocks, dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    ws = _lib.workspace(dev, lib.fp_block_energy_workspace_size(M, num_blocks))
+    rc = lib.fp_block_energy(ptr(x2d), M, D, num_blocks, dtype_code(x2d.dtype), ptr(w_gu), ptr(vnorm), ptr(E),
+                             ptr(ws), ws.numel(), stream_handle(dev))
+    check(rc, "fp_block_energy")
+    return E
+
+
 def token_forward(x2d, k_gate, k_up, v, packed, q_proj, block_keys, out_proj, *, base_blocks: int,
                   top_p: float, min_remote: int, max_remote: int, temperature: float = 1.0,
                   additive: bool = True, block_stride: int = 1, block_offset: int = 0,

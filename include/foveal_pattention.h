@@ -148,6 +148,20 @@ FP_API int fp_pattention_pooled_fwd(const void* x, int64_t M, int D, int NB, int
                              void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Teacher block energies of the offline router calibration (FovealPattentionMLP.calibrate_offline_svd,
+ * foveal_pattention.py:205-218):
+ *   energy[t, b] = mean_{j in block b} |silu(x_t . k_gate_j) * (x_t . k_up_j)| * vnorm[b]
+ * over all NB blocks (the dense SwiGLU of the calibration tokens), computed by the gate/up tensor-core
+ * kernel with an fp32 reduction in its epilogue instead of writing the activations.
+ *   x [M, D] bf16; w_gu from fp_pack_weights; vnorm [NB] fp32 (Frobenius norms of the blocks of v);
+ *   energy [M, NB] fp32.  bf16 only, D % 64 == 0.
+ */
+FP_API size_t fp_block_energy_workspace_size(int64_t M, int NB);
+FP_API int fp_block_energy(const void* x, int64_t M, int D, int NB, int dtype, const void* w_gu,
+                           const float* vnorm, float* energy, void* workspace, size_t workspace_bytes,
+                           void* stream);
+
+/*
  * Allocation-free token-routed forward (no counterpart in the reference).  Same arguments and result
  * as fp_pattention_token_fwd, without the workspace: it runs in a FP_NOALLOC_SCRATCH_BYTES scratch
  * array that the library keeps on each GPU it is loaded on, so callers that cannot allocate device
@@ -169,8 +183,9 @@ FP_API int fp_pattention_token_fwd_noalloc(const void* x, int64_t M, int D, int 
 /*
  * Measurement hook (no counterpart in the reference): for the calling host thread, the forward entry
  * points record events[i] (cudaEvent_t handles) on their stream at stage boundaries:
- *   fp_pattention_token_fwd:  0 start, 1 routed (scores + selection), 2 block CSR built and H cleared,
- *                             3 gate/up kernel done, 4 down kernel done
+ *   fp_pattention_token_fwd:  0 start, 1 and 2 routed (scores, selection, block lists and H clears are
+ *                             one projection kernel and one routing kernel), 3 gate/up kernel done,
+ *                             4 down kernel done
  *   fp_pattention_pooled_fwd: 0 start, 1 gate/up kernel done, 2 down kernel done
  * Boundaries past n_events are not recorded.  events = NULL or n_events = 0 turns the hook off.
  */

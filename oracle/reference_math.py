@@ -36,6 +36,8 @@ __all__ = [
     "pooled_forward",
     "boundary_margins",
     "dense_swiglu",
+    "teacher_block_energy",
+    "calibrate_offline_svd",
 ]
 
 
@@ -292,3 +294,45 @@ def dense_swiglu(x2d, w) -> torch.Tensor:
     """Dense SwiGLU with the reparameterised weights (foveal_pattention.py:162-169):
     ``(silu(x W_gate^T) * (x W_up^T)) W_down^T`` with ``W_down^T = v``."""
     return torch.matmul(F.silu(x2d @ w.k_gate.t()) * (x2d @ w.k_up.t()), w.v)
+
+
+def teacher_block_energy(x2d, k_gate, k_up, v, block_size: int = 64) -> torch.Tensor:
+    """Dense SwiGLU block activation energy of the offline calibration (foveal_pattention.py:205-216):
+    ``E[t, b] = mean_{j in b} |silu(x_t k_gate_j) * (x_t k_up_j)| * ||v_b||_F``, [M, NB]."""
+    A = F.silu(x2d @ k_gate.t()) * (x2d @ k_up.t())
+    nb = k_gate.shape[0] // block_size
+    out = []
+    for b in range(nb):
+        rows = slice(b * block_size, (b + 1) * block_size)
+        out.append(A[:, rows].abs().mean(dim=-1) * v[rows].norm())
+    return torch.stack(out, dim=-1)
+
+
+def calibrate_offline_svd(x2d, w, *, base_blocks: int, remote_blocks: int, temperature: float = 1.0,
+                          ridge_lambda: float = 1e-2, index_dim: int = 16, block_size: int = 64):
+    """Offline SVD + ridge calibration of the 16-D router (foveal_pattention.py:175-255).  Returns
+    ``(q_proj [16, D], block_keys [NB, 16], info)``; info holds the reference's returned figures plus
+    ``scores`` (the calibrated router scores of the calibration tokens, invariant to the sign of each
+    singular vector) and ``mean_scores``."""
+    X = x2d.float()
+    _, S, Vh = torch.linalg.svd(X, full_matrices=False)                   # :195
+    if Vh.shape[0] < index_dim:                                           # :196-198
+        pad = torch.randn(index_dim - Vh.shape[0], X.shape[1])
+        Vh = torch.cat([Vh, pad], dim=0)
+    V16 = Vh[:index_dim, :].T                                             # :199
+    Z = F.rms_norm(X @ V16, (index_dim,))                                  # :203
+    teacher = teacher_block_energy(X, w.k_gate.float(), w.k_up.float(), w.v.float(), block_size)  # :206-216
+    target = F.softmax(teacher / temperature, dim=-1)                     # :217
+    reg = ridge_lambda * torch.eye(index_dim)                             # :220
+    block_keys = torch.linalg.solve(Z.T @ Z + reg, Z.T @ target).T        # :221
+    scores = (Z @ block_keys.T) / math.sqrt(index_dim)                    # :225
+    student = F.softmax(scores / temperature, dim=-1)                      # :226
+    kl = F.kl_div(student.log(), target, reduction="batchmean").item()    # :227
+    mean_scores = scores.mean(dim=0)                                       # :230
+    _, top = torch.topk(mean_scores[base_blocks:], k=remote_blocks)       # :231
+    active = torch.cat([torch.arange(base_blocks, dtype=torch.int32), (top + base_blocks).to(torch.int32)])
+    total_var = (S ** 2).sum().item()                                      # :242-244
+    top_var = (S[:index_dim] ** 2).sum().item()
+    info = {"top16_explained_variance": top_var / max(total_var, 1e-12), "initial_kl_divergence": kl,
+            "calib_active_blocks": active, "scores": scores, "mean_scores": mean_scores, "teacher": teacher}
+    return V16.T.contiguous(), block_keys, info

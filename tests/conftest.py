@@ -88,3 +88,19 @@ def compare_routes(idx, cnt, ref_idx, ref_cnt, margins=None, tie_eps: float = TI
         if (a[t] != b[t] or cnt[t] != ref_cnt[t]) and not near:
             bad += 1
     return bad, ties
+
+
+def active_set_matches(active, gold_scores, base: int, remote: int, rel_tol: float) -> bool:
+    """Calibrated active set (base blocks + top ``remote`` mean scores) against the reference's
+    calibration scores: blocks may differ only where the reference's mean scores sit within
+    ``rel_tol`` (relative to their mean magnitude) of the top-``remote`` boundary."""
+    ms = torch.as_tensor(gold_scores).double().mean(dim=0)
+    rem = ms[base:]
+    order = rem.sort(descending=True).values
+    thr = 0.5 * float(order[remote - 1] + order[remote])
+    tol = rel_tol * float(rem.abs().mean())
+    gold = set(range(base)) | {int(b) + base for b in rem.topk(remote).indices}
+    mine = set(int(b) for b in active)
+    if len(mine) != base + remote or not set(range(base)) <= mine:
+        return False
+    return all(abs(float(ms[b]) - thr) <= tol for b in mine ^ gold)

@@ -120,15 +120,47 @@ def flat(prefix, d):
     return {f"{prefix}{k}": v for k, v in d.items()}
 
 
+CALIB = {"base_blocks": 1, "remote_blocks": 8, "ridge_lambda": 1e-2}
+
+
+def calib_case(ref, seed):
+    """The reference's FovealPattentionMLP.calibrate_offline_svd on bf16-rounded PR1-shape weights and
+    512 bf16-rounded calibration tokens (fp32 module).  Stores its returned figures, the calibrated
+    router's scores on the calibration tokens (invariant to singular-vector signs) and the teacher block
+    energies it fitted (computed with the same expression as foveal_pattention.py:205-216)."""
+    FovealPattentionMLP = ref[0]
+    wl = cfgmod.calib_workload()
+    w, x = cfgmod.make_weights(wl, seed), cfgmod.make_x(wl, seed)
+    x2d = x.reshape(-1, wl.hidden_dim)
+    m = build_module(FovealPattentionMLP, wl, w, CALIB["remote_blocks"])
+    with torch.no_grad():
+        A = F.silu(x2d @ m.k_gate.t()) * (x2d @ m.k_up.t())
+        teacher = torch.stack([A[:, b * 64:(b + 1) * 64].abs().mean(dim=-1) * m.v[b * 64:(b + 1) * 64].norm()
+                               for b in range(m.num_blocks)], dim=-1)
+    info = m.calibrate_offline_svd(x2d, ridge_lambda=CALIB["ridge_lambda"])
+    with torch.no_grad():
+        z = F.rms_norm(x2d @ m.q_proj_16d.weight.t(), (16,))
+        scores = z @ m.block_keys_16d.t() / 4.0
+    return {"explained": np.float64(info["top16_explained_variance"]),
+            "kl": np.float64(info["initial_kl_divergence"]),
+            "active": np.array(info["calib_active_blocks"], dtype=np.int32),
+            "scores": scores.numpy().astype(np.float32), "teacher": teacher.numpy().astype(np.float32)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--only", default="", help="comma-separated fixture names to regenerate (default: all)")
     args = ap.parse_args()
     ref = load_reference(args.ref)
     torch.set_num_threads(os.cpu_count())
     C = cfgmod.CONFIGS
     meta_common = {"seed": args.seed, "torch": torch.__version__}
+    only = set(filter(None, args.only.split(",")))
+    if only == {"calib"}:
+        save("calib", {**meta_common, "config": "calib", **CALIB}, calib_case(ref, args.seed))
+        return
 
     # 1. PR1 (fp32, full size): token mode, pooled eval and pooled train.
     wl = C["pr1"]
@@ -204,6 +236,9 @@ def main():
         arr[f"{name}_counts"] = r.remote_counts.numpy()
         arr[f"{name}_cap_rate"] = np.float32(r.cap_rate)
     save("router_kat", {**meta_common, "config": "router"}, arr)
+
+    # 7. Offline SVD router calibration.
+    save("calib", {**meta_common, "config": "calib", **CALIB}, calib_case(ref, args.seed))
 
 
 if __name__ == "__main__":
