@@ -322,6 +322,17 @@ class FovealPattentionMLP(nn.Module):
         in host memory; it is complete once the caller's current stream has been synchronised (the
         current stream is made to wait for the last copy).
         """
+        out, done = self.forward_host_async(x_host, out, chunk_tokens)
+        torch.cuda.current_stream(self.k_gate.device).wait_event(done)
+        return out
+
+    def forward_host_async(self, x_host: Tensor, out: Optional[Tensor] = None,
+                           chunk_tokens: int = 2048) -> Tuple[Tensor, "torch.cuda.Event"]:
+        """:meth:`forward_host` without joining the caller's stream: returns ``(out, done)`` where
+        ``out`` is complete once the CUDA event ``done`` has completed (``done.synchronize()`` or a
+        stream's ``wait_event``).  Consecutive calls pipeline: the copy-in of the next batch overlaps the
+        last chunks of this one (the device buffers are reused as soon as the chunk that held them is
+        done).  Keep ``x_host`` unchanged and do not read ``out`` until ``done``."""
         if self.routing != "token":
             raise ValueError("forward_host needs routing='token' (pooled routing pools over the whole call)")
         if x_host.is_cuda:
@@ -341,23 +352,29 @@ class FovealPattentionMLP(nn.Module):
         kg, ku, v, packed, wq, k16, wout = self._weights()
         plan = _chunk_plan(M, max(1, int(chunk_tokens)))
         ch = max(plan) if plan else 1
-        st = getattr(self, "_host_streams", None)
-        if st is None or st[0].device != dev:
-            st = tuple(torch.cuda.Stream(device=dev) for _ in range(4))
-            self._host_streams = st
-        s_in, s_out, s_c0, s_c1 = st
         nslot = 3
-        bufs = getattr(self, "_host_bufs", None)
+        hs = getattr(self, "_host_state", None)
+        if hs is None or hs["device"] != dev:
+            hs = {"device": dev, "streams": tuple(torch.cuda.Stream(device=dev) for _ in range(4)),
+                  "bufs": None, "x_free": [None] * nslot, "y_free": [None] * nslot, "n": 0}
+            self._host_state = hs
+        s_in, s_out, s_c0, s_c1 = hs["streams"]
+        bufs = hs["bufs"]
         if bufs is None or bufs[0].shape[0] < ch or bufs[0].shape[1] != D or bufs[0].dtype != dt:
+            for s_ in hs["streams"]:  # earlier calls may still use the old buffers
+                s_.synchronize()
             bufs = [torch.empty(ch, D, dtype=dt, device=dev) for _ in range(2 * nslot)]  # x slots, y slots
-            self._host_bufs = bufs
+            hs["bufs"] = bufs
+            hs["x_free"] = [None] * nslot
+            hs["y_free"] = [None] * nslot
         cur = torch.cuda.current_stream(dev)
-        for s_ in st:
+        for s_ in hs["streams"]:
             s_.wait_stream(cur)
-        x_free = [None] * nslot  # compute of the slot's previous chunk done
-        y_free = [None] * nslot  # copy-out of the slot's previous chunk done
+        x_free, y_free = hs["x_free"], hs["y_free"]  # per slot: compute done / copy-out done
         c0 = 0
-        for i, n in enumerate(plan):
+        for n in plan:
+            i = hs["n"]
+            hs["n"] += 1
             slot = i % nslot
             s_cmp = s_c0 if i % 2 == 0 else s_c1
             xb, yb = bufs[slot][:n], bufs[nslot + slot][:n]
@@ -385,9 +402,9 @@ class FovealPattentionMLP(nn.Module):
                 e_out.record(s_out)
                 y_free[slot] = e_out
             c0 += n
-        for s_ in st:
-            cur.wait_stream(s_)
-        return out
+        done = torch.cuda.Event()
+        done.record(s_out)
+        return out, done
 
     def _forward_token(self, x2d: Tensor, return_router_info: bool):
         kg, ku, v, packed, wq, k16, wout = self._weights()

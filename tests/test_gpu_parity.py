@@ -268,6 +268,13 @@ def test_forward_host_matches_forward():
     with torch.no_grad():
         ref = m(x2d.to(DEV))
         ys = [m.forward_host(xh, chunk_tokens=c) for c in (1024, 4096)]  # 9 and 3 chunks, 2 compute streams
+        # two pipelined batches in flight at once (the second's copy-in overlaps the first's last chunks)
+        xa, xb = x2d[:2500].contiguous().pin_memory(), x2d[2500:].contiguous().pin_memory()
+        oa, da = m.forward_host_async(xa, chunk_tokens=1024)
+        ob, db = m.forward_host_async(xb, chunk_tokens=1024)
+        da.synchronize()
+        db.synchronize()
+        ys.append(torch.cat([oa, ob]))
     torch.cuda.synchronize()
     for y in ys:
         assert y.device.type == "cpu" and y.shape == ref.shape
