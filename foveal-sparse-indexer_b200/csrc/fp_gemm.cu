@@ -38,13 +38,24 @@ struct __align__(8) PipeBarsT {
   int32_t consumed;
 };
 using PipeBars = PipeBarsT<kStages>;     // down kernel
-using GuBars = PipeBarsT<kGuStages>;     // gate/up kernel
-
-constexpr uint32_t kGuBBytes = kGuN * kTileK * 2;
-constexpr uint32_t kGuStageBytes = kABytes + kGuBBytes;
 constexpr size_t kGemmSmem = 1024 + kStages * kStageBytes + sizeof(PipeBars) + 64;
-constexpr size_t kGuSmem = 1024 + kGuStages * kGuStageBytes + sizeof(GuBars) + 64;
-static_assert(kGuSmem <= 227 * 1024, "gate/up shared memory");
+
+// Gate/up kernel configurations: at most NMAX tokens per tile and STAGES shared-memory stages of
+// 16 KB (weights) + NMAX x 128 B (token rows).  <256, 4> in general; <64, 8> for batches of at most 64
+// tokens (decode), whose tiles are small and whose time is the streaming of the blocks' weights: twice
+// the stages keep twice the bytes in flight per SM.
+template <int NMAX, int STAGES>
+struct GuCfg {
+  static constexpr int kN = NMAX;
+  static constexpr int kS = STAGES;
+  using Bars = PipeBarsT<STAGES>;
+  static constexpr uint32_t kBBytes = NMAX * kTileK * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr size_t kSmem = 1024 + STAGES * kStageBytes + sizeof(Bars) + 64;
+  static_assert(kSmem <= 227 * 1024, "gate/up shared memory");
+};
+using GuBig = GuCfg<kGuN, kGuStages>;
+using GuSmall = GuCfg<64, 8>;
 
 __device__ __forceinline__ uint8_t* aligned_smem(uint8_t* raw) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
@@ -122,6 +133,7 @@ struct GuTile {
   int n;               // valid tokens in this tile (0: skip)
 };
 
+template <int NMAX>
 __device__ __forceinline__ GuTile gu_decode(const GateUpArgs& a, int tile) {
   GuTile t;
   if (a.tiles) {
@@ -139,8 +151,8 @@ __device__ __forceinline__ GuTile gu_decode(const GateUpArgs& a, int tile) {
     t.slot = key;
     t.b = a.active[key];
     t.list = nullptr;
-    t.r0 = rt * kGuN;
-    t.n = (int)((a.M - t.r0) < (int64_t)kGuN ? (a.M - t.r0) : (int64_t)kGuN);
+    t.r0 = rt * NMAX;
+    t.n = (int)((a.M - t.r0) < (int64_t)NMAX ? (a.M - t.r0) : (int64_t)NMAX);
   }
   if (t.b < 0 || (int64_t)(t.b + 1) * kBlock > a.Np) {
     record_error(a.err, kErrBadTile);
@@ -164,15 +176,19 @@ __device__ __forceinline__ int gu_token(const GuTile& t, int i, const GateUpArgs
 constexpr int kGatherWarps = 16;                         // token-row gather warps (cp.async)
 constexpr int kGatherThreads = 32 * kGatherWarps;
 constexpr int kGuThreads = 192 + kGatherThreads;         // warps 6.. gather
-constexpr int kRowsPerGatherThread = kGuN * 8 / kGatherThreads;  // 16-byte chunks per thread per stage
-static_assert(kRowsPerGatherThread * kGatherThreads == kGuN * 8, "gather split");
 
+template <class Cfg>
 __global__ void __launch_bounds__(kGuThreads, 1)
 gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
               const GateUpArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = aligned_smem(smem_raw);
-  GuBars* bars = reinterpret_cast<GuBars*>(smem + kGuStages * kGuStageBytes);
+  constexpr int kN = Cfg::kN, kS = Cfg::kS;
+  constexpr uint32_t kStage = Cfg::kStageBytes;
+  constexpr int kRowsPerGatherThread = kN * 8 / kGatherThreads;  // 16-byte chunks per thread per stage
+  static_assert(kRowsPerGatherThread * kGatherThreads == kN * 8, "gather split");
+  using Bars = typename Cfg::Bars;
+  Bars* bars = reinterpret_cast<Bars*>(smem + kS * kStage);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool gathered = a.tiles != nullptr;  // token lists (cp.async gathers) or identity rows (TMA box)
 
@@ -183,7 +199,7 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
   // full barrier: one expect_tx arrival (TMA) + one arrival per gather thread
   pipe_init(bars, 4, 1 + kGatherThreads);
   const uint32_t tmem_base = bars->tmem;
-  const int ntiles = gathered ? a.meta[0] : a.n_keys * (int)((a.M + kGuN - 1) / kGuN);
+  const int ntiles = gathered ? a.meta[0] : a.n_keys * (int)((a.M + kN - 1) / kN);
   const int nkb = a.D / kTileK;
   uint32_t issued = 0;
 
@@ -194,14 +210,14 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
       uint32_t it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-        const GuTile t = gu_decode(a, tile);
+        const GuTile t = gu_decode<kN>(a, tile);
         if (t.n <= 0) continue;
         for (int kb = 0; kb < nkb; ++kb, ++it) {
-          const int s = it % kGuStages;
-          const uint32_t ph = (it / kGuStages) & 1u;
+          const int s = it % kS;
+          const uint32_t ph = (it / kS) & 1u;
           if (!mbar_wait(&bars->empty[s], ph ^ 1u, a.err, kErrWaitEmpty)) { ok = false; break; }
-          uint8_t* As = smem + s * kGuStageBytes;
-          mbar_arrive_expect_tx(&bars->full[s], kABytes + (gathered ? 0u : kGuBBytes));
+          uint8_t* As = smem + s * kStage;
+          mbar_arrive_expect_tx(&bars->full[s], kABytes + (gathered ? 0u : Cfg::kBBytes));
           tma_load_2d(As, &tm_w, &bars->full[s], kb * kTileK, t.b * 2 * kBlock);
           if (!gathered) tma_load_2d(As + kABytes, &tm_x, &bars->full[s], kb * kTileK, (int)t.r0);
         }
@@ -220,7 +236,7 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
     uint32_t it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-      const GuTile t = gu_decode(a, tile);
+      const GuTile t = gu_decode<kN>(a, tile);
       if (t.n <= 0) continue;
       const int npad = (t.n + 15) & ~15;
       int64_t src[kRowsPerGatherThread];
@@ -232,11 +248,11 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
         src[j] = (int64_t)tok * a.D * 2 + chunk * 16;
       }
       for (int kb = 0; kb < nkb; ++kb, ++it) {
-        const int s = it % kGuStages;
-        const uint32_t ph = (it / kGuStages) & 1u;
+        const int s = it % kS;
+        const uint32_t ph = (it / kS) & 1u;
         if (!warp_wait(&bars->empty[s], ph ^ 1u, a.err, kErrWaitEmpty)) { ok = false; break; }
         if (gathered) {
-          const uint32_t bs = smem_u32(smem + s * kGuStageBytes + kABytes) + swz;
+          const uint32_t bs = smem_u32(smem + s * kStage + kABytes) + swz;
           const int64_t koff = (int64_t)kb * kTileK * 2;
 #pragma unroll
           for (int j = 0; j < kRowsPerGatherThread; ++j) {
@@ -255,7 +271,7 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
       int local = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-        const GuTile t = gu_decode(a, tile);
+        const GuTile t = gu_decode<kN>(a, tile);
         if (t.n <= 0) continue;
         const int npad = (t.n + 15) & ~15;
         const int acc = local & 1;
@@ -265,13 +281,13 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
         const uint32_t d_tmem = tmem_base + acc * kTileN;
         const uint32_t idesc = umma_idesc_bf16(kTileM, npad);
         for (int kb = 0; kb < nkb; ++kb) {
-          const int s = it % kGuStages;
-          const uint32_t ph = (it / kGuStages) & 1u;
+          const int s = it % kS;
+          const uint32_t ph = (it / kS) & 1u;
           if (!mbar_wait(&bars->full[s], ph, a.err, kErrWaitFull)) { ok = false; break; }
           fence_proxy_async_smem();
           tc_fence_after();
-          const uint64_t ad = umma_desc_sw128(smem_u32(smem + s * kGuStageBytes));
-          const uint64_t bd = umma_desc_sw128(smem_u32(smem + s * kGuStageBytes + kABytes));
+          const uint64_t ad = umma_desc_sw128(smem_u32(smem + s * kStage));
+          const uint64_t bd = umma_desc_sw128(smem_u32(smem + s * kStage + kABytes));
 #pragma unroll
           for (int k = 0; k < kTileK / 16; ++k)
             umma_bf16(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
@@ -290,7 +306,7 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
     const int q = warp & 3;
     int local = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-      const GuTile t = gu_decode(a, tile);
+      const GuTile t = gu_decode<kN>(a, tile);
       if (t.n <= 0) continue;
       const int npad = (t.n + 15) & ~15;
       const int acc = local & 1;
@@ -590,20 +606,27 @@ static int set_smem(const void* fn) {
              ? FP_OK : FP_ERR_CUDA;
 }
 
-int launch_gateup(const GateUpArgs& a, cudaStream_t st) {
+template <class Cfg>
+static int launch_gateup_cfg(const GateUpArgs& a, cudaStream_t st) {
   CUtensorMap tx, tw;
-  if (!encode_map_2d(&tx, a.x, a.D, a.M, (uint64_t)a.D * 2, kTileK, a.tiles ? 1 : kGuN) ||
+  if (!encode_map_2d(&tx, a.x, a.D, a.M, (uint64_t)a.D * 2, kTileK, a.tiles ? 1 : Cfg::kN) ||
       !encode_map_2d(&tw, a.w_gu, a.D, (uint64_t)a.Np * 2, (uint64_t)a.D * 2, kTileK, kTileM))
     return FP_ERR_CUDA;
   static std::once_flag once;
   static int attr = FP_OK;
   std::call_once(once, [] {
-    attr = cudaFuncSetAttribute((const void*)gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)kGuSmem) == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+    attr = cudaFuncSetAttribute((const void*)gateup_kernel<Cfg>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)Cfg::kSmem) == cudaSuccess ? FP_OK : FP_ERR_CUDA;
   });
   if (attr != FP_OK) return attr;
-  gateup_kernel<<<a.num_sms, kGuThreads, kGuSmem, st>>>(tx, tw, a);
+  gateup_kernel<Cfg><<<a.num_sms, kGuThreads, Cfg::kSmem, st>>>(tx, tw, a);
   return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+}
+
+int launch_gateup(const GateUpArgs& a, cudaStream_t st) {
+  // every tile of a batch of at most 64 tokens holds at most 64 tokens (a key's tokens are distinct)
+  if (a.M <= GuSmall::kN) return launch_gateup_cfg<GuSmall>(a, st);
+  return launch_gateup_cfg<GuBig>(a, st);
 }
 
 __global__ void energy_combine_kernel(const float* __restrict__ part, int64_t M, int NB, const float* __restrict__ vnorm,
