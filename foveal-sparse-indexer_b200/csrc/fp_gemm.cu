@@ -561,6 +561,241 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
   pipe_teardown(bars, issued, a.err);
 }
 
+// Additive stream and store of 32 consecutive output columns [col0, col0 + 32) of one row per lane (the
+// warp's lanes hold 32 rows).  `add`: add ctx16 . W_out^T (done by exactly one contributor of a tile).
+// With split-K (ks > 1) the fp32 partial of split `split` is stored instead of the output.
+__device__ __forceinline__ void down_store_chunk(const DownArgs& a, float (&o)[32], const float (&ctx)[16],
+                                                 int64_t row, bool row_ok, int col0, bool add, int split, int ks) {
+  const int lane = threadIdx.x & 31;
+  if (a.ctx16 && add && col0 < a.D) {
+    // o[i] += sum_k ctx[k] * W_out[col0 + i][k]; lane L loads row col0 + L of W_out and the warp broadcasts
+    // it (all lanes of a chunk share the same 32 columns)
+    float wv[16];
+    const int64_t wrow = (int64_t)(col0 + lane) * 16;
+    if (a.out_proj_f32) {
+      const float4* wp = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.out_proj) + wrow);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float4 f = __ldg(wp + k);
+        wv[4 * k] = f.x; wv[4 * k + 1] = f.y; wv[4 * k + 2] = f.z; wv[4 * k + 3] = f.w;
+      }
+    } else {
+      const uint4* wp = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.out_proj) + wrow);
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const uint4 u = __ldg(wp + k);
+        const uint32_t ww[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          wv[8 * k + 2 * e] = __uint_as_float(ww[e] << 16);
+          wv[8 * k + 2 * e + 1] = __uint_as_float(ww[e] & 0xFFFF0000u);
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      float sacc = 0.f;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) sacc = fmaf(ctx[k], __shfl_sync(0xffffffffu, wv[k], i), sacc);
+      o[i] += sacc;
+    }
+  }
+  if (!row_ok || col0 >= a.D) return;
+  if (ks > 1) {  // partial of this split; summed in split order by splitk_reduce_kernel
+    float4* yp = reinterpret_cast<float4*>(a.y_acc + ((int64_t)split * a.M + row) * a.D + col0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) yp[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+  } else if (a.y_f32) {
+    float4* yp = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.y) + row * a.D + col0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) yp[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+  } else {
+    uint4* yp = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.y) + row * a.D + col0);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint32_t pk[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const __nv_bfloat162 b2 = __floats2bfloat162_rn(o[8 * i + 2 * e], o[8 * i + 2 * e + 1]);
+        pk[e] = *reinterpret_cast<const uint32_t*>(&b2);
+      }
+      yp[i] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    }
+  }
+}
+
+// ============================================================================================
+// Down projection on CTA pairs (cluster of 2, tcgen05 cta_group::2): a pair computes a 256-token x
+// 256-column tile.  Each CTA loads its 128 rows of H and its 128 rows (output columns) of V_t per
+// k-block (32 KB per stage instead of 48 KB for a 128 x 256 tile on one SM), the leader (even CTA)
+// issues the pair MMAs, and each CTA drains its own 128 x 256 accumulator.  Six stages in flight.
+// ============================================================================================
+constexpr int kPairStages = 6;
+constexpr uint32_t kPairABytes = kTileM * kTileK * 2;          // 16 KB: 128 rows of H
+constexpr uint32_t kPairBBytes = (kTileN / 2) * kTileK * 2;    // 16 KB: 128 rows of V_t
+constexpr uint32_t kPairStageBytes = kPairABytes + kPairBBytes;
+using PairBars = PipeBarsT<kPairStages>;
+constexpr size_t kPairSmem = 1024 + kPairStages * kPairStageBytes + sizeof(PairBars) + 64;
+static_assert(kPairSmem <= 227 * 1024, "pair down shared memory");
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+down2_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CUtensorMap tm_vt,
+             const DownArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = aligned_smem(smem_raw);
+  PairBars* bars = reinterpret_cast<PairBars*>(smem + kPairStages * kPairStageBytes);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tm_h);
+    tma_prefetch_desc(&tm_vt);
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&bars->full[s], 1);   // leader: one expect_tx arrival + both CTAs' bytes
+      mbar_init(&bars->empty[s], 1);  // arrival from the leader's commit
+    }
+    for (int c = 0; c < 2; ++c) {
+      mbar_init(&bars->accf[c], 1);   // arrival from the leader's commit
+      mbar_init(&bars->acce[c], 8);   // leader: the 4 epilogue warps of both CTAs
+    }
+    mbar_init(&bars->done, 1);
+    bars->consumed = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc2(&bars->tmem, kTmemCols);
+    tmem_relinquish2();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before any remote arrival or pair commit
+  tc_fence_after();
+  const uint32_t tmem_base = bars->tmem;
+  const int m_pairs = (int)((a.M + 2 * kTileM - 1) / (2 * kTileM));
+  const int n_tiles = (a.D + kTileN - 1) / kTileN;
+  const int tiles = m_pairs * n_tiles;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int nkb = a.K / kTileK;
+  uint32_t issued = 0;
+
+  if (warp == 0) {
+    // ---------------- producer (both CTAs): own rows of H, own half of the V_t tile
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = pair; tile < tiles && ok; tile += npairs) {
+        int m, n;
+        down_tile(tile, m_pairs, n_tiles, m, n);
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % kPairStages;
+          const uint32_t ph = (it / kPairStages) & 1u;
+          if (!mbar_wait(&bars->empty[s], ph ^ 1u, a.err, kErrWaitEmpty)) { ok = false; break; }
+          uint8_t* As = smem + s * kPairStageBytes;
+          uint8_t* Bs = As + kPairABytes;
+          const int gb = a.bmap ? a.bmap[kb] : kb * a.stride + a.offset;
+          if (leader) mbar_arrive_expect_tx(&bars->full[s], 2 * kPairStageBytes);
+          tma_load_2d_pair(As, &tm_h, &bars->full[s], kb * kTileK, m * 2 * kTileM + (int)rank * kTileM);
+          tma_load_2d_pair(Bs, &tm_vt, &bars->full[s], gb * kBlock, n * kTileN + (int)rank * (kTileN / 2));
+        }
+      }
+      issued = it;
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- pair MMA issuer (leader only)
+    if (leader && lane == 0) {
+      uint32_t it = 0;
+      int local = 0;
+      bool ok = true;
+      const uint32_t idesc = umma_idesc_bf16(2 * kTileM, kTileN);
+      for (int tile = pair; tile < tiles && ok; tile += npairs) {
+        const int acc = local & 1;
+        const uint32_t aph = (local >> 1) & 1;
+        if (!mbar_wait_cluster(&bars->acce[acc], aph ^ 1u, a.err, kErrWaitAccEmpty)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kTileN;
+        for (int kb = 0; kb < nkb; ++kb) {
+          const int s = it % kPairStages;
+          const uint32_t ph = (it / kPairStages) & 1u;
+          if (!mbar_wait_cluster(&bars->full[s], ph, a.err, kErrWaitFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t ad = umma_desc_sw128(smem_u32(smem + s * kPairStageBytes));
+          const uint64_t bd = umma_desc_sw128(smem_u32(smem + s * kPairStageBytes + kPairABytes));
+#pragma unroll
+          for (int k = 0; k < kTileK / 16; ++k)
+            umma2_bf16(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+          umma2_commit(&bars->empty[s], 0x3);
+          ++it;
+        }
+        if (!ok) break;
+        umma2_commit(&bars->accf[acc], 0x3);
+        ++local;
+      }
+      bars->consumed = (int32_t)it;
+      umma2_commit(&bars->done, 0x1);
+      if (!mbar_wait(&bars->done, 0, nullptr, 0)) record_error(a.err, kErrDrain);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue (both CTAs): warp w drains TMEM lanes [32*(w%4), +32) of its CTA
+    const int q = warp & 3;
+    int local = 0;
+    for (int tile = pair; tile < tiles; tile += npairs) {
+      int m, n;
+      down_tile(tile, m_pairs, n_tiles, m, n);
+      const int acc = local & 1;
+      const uint32_t aph = (local >> 1) & 1;
+      if (!warp_wait(&bars->accf[acc], aph, a.err, kErrWaitAccFull)) break;
+      tc_fence_after();
+      const int64_t row = (int64_t)m * 2 * kTileM + (int64_t)rank * kTileM + 32 * q + lane;
+      const bool row_ok = row < a.M;
+      float ctx[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) ctx[k] = 0.f;
+      if (a.ctx16 && row_ok) {
+        const float4* cp = reinterpret_cast<const float4*>(a.ctx16 + row * 16);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 f = __ldg(cp + i);
+          ctx[4 * i] = f.x; ctx[4 * i + 1] = f.y; ctx[4 * i + 2] = f.z; ctx[4 * i + 3] = f.w;
+        }
+      }
+      for (int c = 0; c < kTileN / 32; ++c) {
+        uint32_t v[32];
+        __syncwarp();
+        tmem_ld32(tmem_base + acc * kTileN + c * 32 + ((uint32_t)(32 * q) << 16), v);
+        tmem_ld_wait();
+        float o[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = __uint_as_float(v[i]);
+        down_store_chunk(a, o, ctx, row, row_ok, n * kTileN + c * 32, true, 0, 1);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_leader(&bars->acce[acc]);
+      ++local;
+    }
+  }
+
+  // ---------------- teardown: every MMA has completed (leader: done barrier; peer: its last accf), no
+  // load of this CTA is in flight unless it aborted; then both CTAs free the pair's TMEM
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && leader && aborted(a.err)) {
+    for (uint32_t i = (uint32_t)bars->consumed; i < issued; ++i)
+      if (!mbar_wait(&bars->full[i % kPairStages], (i / kPairStages) & 1u, nullptr, 0)) {
+        record_error(a.err, kErrDrain);
+        break;
+      }
+  }
+  __syncthreads();
+  cluster_sync();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc2(tmem_base, kTmemCols);
+  }
+}
+
 // Sums the split-K partials [ks][n] in split order (deterministic) and writes the output dtype.
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int ks, int64_t n, void* out, int out_f32) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -674,6 +909,42 @@ int launch_down(const DownArgs& a, cudaStream_t st) {
   std::call_once(once, [] { attr = set_smem((const void*)down_kernel); });
   if (attr != FP_OK) return attr;
   const int ks = a.ksplit > 1 ? a.ksplit : 1;
+  if (ks == 1 && a.M >= 2 * kTileM && a.num_sms >= 2) {
+    // CTA pairs: 256 x 256 tiles, each CTA loading 128 rows of H and half of the V_t tile
+    CUtensorMap tv2;
+    if (!encode_map_2d(&tv2, a.v_t, a.Np, a.D, (uint64_t)a.Np * 2, kTileK, kTileN / 2)) return FP_ERR_CUDA;
+    static std::once_flag once2;
+    static int attr2 = FP_OK;
+    std::call_once(once2, [] {
+      attr2 = cudaFuncSetAttribute((const void*)down2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)kPairSmem) == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+    });
+    if (attr2 != FP_OK) return attr2;
+    // pairs that can be resident at once (a pair needs two SMs of one GPC with ~200 KB free each)
+    static std::once_flag once3;
+    static int max_pairs = 0;
+    std::call_once(once3, [&] {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(a.num_sms & ~1);
+      cfg.blockDim = dim3(kGemmThreads);
+      cfg.dynamicSmemBytes = kPairSmem;
+      cudaLaunchAttribute attr;
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = 2;
+      attr.val.clusterDim.y = 1;
+      attr.val.clusterDim.z = 1;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, (const void*)down2_kernel, &cfg) != cudaSuccess) n = 0;
+      max_pairs = n;
+    });
+    if (max_pairs <= 0) return FP_ERR_CUDA;
+    const int64_t ptiles = ((a.M + 2 * kTileM - 1) / (2 * kTileM)) * ((a.D + kTileN - 1) / kTileN);
+    const int grid2 = 2 * (int)std::min<int64_t>(ptiles, std::min(max_pairs, a.num_sms / 2));
+    down2_kernel<<<grid2, kGemmThreads, kPairSmem, st>>>(th, tv2, a);
+    return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+  }
   const int64_t tiles = ((a.M + kTileM - 1) / kTileM) * ((a.D + kTileN - 1) / kTileN) * ks;
   const int grid = (int)std::min<int64_t>(tiles, a.num_sms);
   if (grid <= 0) return FP_OK;
