@@ -104,3 +104,18 @@ def active_set_matches(active, gold_scores, base: int, remote: int, rel_tol: flo
     if len(mine) != base + remote or not set(range(base)) <= mine:
         return False
     return all(abs(float(ms[b]) - thr) <= tol for b in mine ^ gold)
+
+
+def serve_model(cfgd: dict, dtype=torch.float32):
+    """Tiny seeded Llama causal LM for the whole-model serving case (random init from the seed, weights
+    rounded to bf16 values), built identically by tests/golden/make_golden.py and the GPU test."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+    cfg = LlamaConfig(vocab_size=cfgd["vocab"], hidden_size=cfgd["hidden"], intermediate_size=cfgd["intermediate"],
+                      num_hidden_layers=cfgd["layers"], num_attention_heads=cfgd["heads"],
+                      num_key_value_heads=cfgd["heads"], max_position_embeddings=256)
+    torch.manual_seed(cfgd["model_seed"])
+    m = LlamaForCausalLM(cfg).eval()
+    with torch.no_grad():
+        for p_ in m.parameters():
+            p_.copy_(p_.to(torch.bfloat16).float())
+    return m.to(dtype)

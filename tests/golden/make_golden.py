@@ -29,6 +29,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 cfgmod = importlib.import_module("foveal-sparse-indexer_b200.configs")
+sys.path.insert(0, os.path.dirname(HERE))
+from conftest import serve_model  # noqa: E402  (tiny seeded Llama shared with the GPU test)
 
 
 def load_reference(ref_root: str):
@@ -147,6 +149,39 @@ def calib_case(ref, seed):
             "scores": scores.numpy().astype(np.float32), "teacher": teacher.numpy().astype(np.float32)}
 
 
+SERVE = {"vocab": 256, "hidden": 512, "intermediate": 2048, "layers": 2, "heads": 8, "prompt": 48, "decode": 8,
+         "base_blocks": 2, "remote_blocks": 8, "model_seed": 1234, "prompt_seed": 99}
+
+
+def serve_case(seed_unused=0):
+    """Whole-model surgery and decode serving (foveal_pattention.py:355-387 and the eval cache :278-288,
+    :309-325): the reference's sparsify_model_with_foveal_pattention on a tiny Llama, prefill on a
+    48-token prompt (routes once, caches the active set), then 8 decode steps fed with the argmax tokens."""
+    from foveal_indexer.foveal_pattention import sparsify_model_with_foveal_pattention
+    m = serve_model(SERVE)
+    sparsify_model_with_foveal_pattention(m, base_blocks=SERVE["base_blocks"], remote_blocks=SERVE["remote_blocks"],
+                                          use_fused_kernel=False)
+    m.eval()  # the new MLP modules start in training mode; serving runs in eval mode
+    g = torch.Generator().manual_seed(SERVE["prompt_seed"])
+    ids = torch.randint(0, SERVE["vocab"], (1, SERVE["prompt"]), generator=g)
+    with torch.no_grad():
+        out = m(ids, use_cache=True)
+        prefill = out.logits[0].float()
+        past = out.past_key_values
+        toks, dec = [], []
+        nxt = int(prefill[-1].argmax())
+        for _ in range(SERVE["decode"]):
+            toks.append(nxt)
+            o = m(torch.tensor([[nxt]]), past_key_values=past, use_cache=True)
+            past = o.past_key_values
+            dec.append(o.logits[0, -1].float())
+            nxt = int(dec[-1].argmax())
+    active = torch.stack([layer.mlp._cached_active_blocks for layer in m.model.layers])
+    return {"prompt": ids.numpy().astype(np.int64), "prefill_logits": prefill.numpy().astype(np.float32),
+            "decode_tokens": np.array(toks, dtype=np.int64), "decode_logits": torch.stack(dec).numpy().astype(np.float32),
+            "active": active.numpy().astype(np.int32)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True)
@@ -158,8 +193,11 @@ def main():
     C = cfgmod.CONFIGS
     meta_common = {"seed": args.seed, "torch": torch.__version__}
     only = set(filter(None, args.only.split(",")))
-    if only == {"calib"}:
-        save("calib", {**meta_common, "config": "calib", **CALIB}, calib_case(ref, args.seed))
+    if only and only <= {"calib", "serve"}:
+        if "calib" in only:
+            save("calib", {**meta_common, "config": "calib", **CALIB}, calib_case(ref, args.seed))
+        if "serve" in only:
+            save("serve", {**meta_common, "config": "serve", **SERVE}, serve_case())
         return
 
     # 1. PR1 (fp32, full size): token mode, pooled eval and pooled train.
@@ -239,6 +277,9 @@ def main():
 
     # 7. Offline SVD router calibration.
     save("calib", {**meta_common, "config": "calib", **CALIB}, calib_case(ref, args.seed))
+
+    # 8. Whole-model surgery and decode serving with the active-set cache.
+    save("serve", {**meta_common, "config": "serve", **SERVE}, serve_case())
 
 
 if __name__ == "__main__":

@@ -13,7 +13,7 @@ import pytest
 import torch
 
 import oracle
-from conftest import active_set_matches, compare_routes, configs, fsi, golden, max_rel, rel_err
+from conftest import active_set_matches, serve_model, compare_routes, configs, fsi, golden, max_rel, rel_err
 
 pytestmark = pytest.mark.gpu
 
@@ -315,6 +315,35 @@ def test_calibrate_offline_svd_matches_reference(dtype):
     assert active_set_matches(info["calib_active_blocks"], g["scores"], g.meta["base_blocks"],
                               g.meta["remote_blocks"], 1e-3)
     assert m._cached_active_blocks.tolist() == info["calib_active_blocks"]
+
+
+# ------------------------------------------------------------------ whole-model serving
+@pytest.mark.parametrize("dtype", ["fp32", "bf16"])
+def test_sparsified_model_prefill_and_decode(dtype):
+    """Model surgery + decode serving (foveal_pattention.py:355-387; eval cache :278-288, :309-325): a tiny
+    Llama whose MLPs are replaced by ``sparsify_model_with_foveal_pattention``, prefilled on a 48-token
+    prompt (each layer routes once on its pooled query and caches the active set) and decoded for 8 steps
+    on the reference's tokens, against the reference's own run of the same model."""
+    g = golden("serve")
+    cfgd = g.meta
+    tdt = torch.float32 if dtype == "fp32" else torch.bfloat16
+    m = serve_model(cfgd)
+    fsi.sparsify_model_with_foveal_pattention(m, base_blocks=cfgd["base_blocks"], remote_blocks=cfgd["remote_blocks"])
+    m = m.to(DEV, tdt).eval()
+    tol = 1e-3 if dtype == "fp32" else 8e-2
+    with torch.no_grad():
+        out = m(torch.from_numpy(g["prompt"]).to(DEV), use_cache=True)
+        assert rel_err(out.logits[0].float().cpu(), torch.from_numpy(g["prefill_logits"])) < tol
+        for layer, ref_active in zip(m.model.layers, g["active"]):
+            assert set(layer.mlp._cached_active_blocks.tolist()) == set(ref_active.tolist())
+        past = out.past_key_values
+        for i, tok in enumerate(g["decode_tokens"].tolist()):
+            o = m(torch.tensor([[tok]], device=DEV), past_key_values=past, use_cache=True)
+            past = o.past_key_values
+            lg = o.logits[0, -1].float().cpu()
+            assert rel_err(lg, torch.from_numpy(g["decode_logits"][i])) < tol, i
+            if dtype == "fp32":
+                assert int(lg.argmax()) == int(g["decode_logits"][i].argmax())
 
 
 # ------------------------------------------------------------------ edge cases
