@@ -57,7 +57,7 @@ def parse():
     ap.add_argument("--chunks", type=int, default=1, help="blockshard: token chunks whose reduce-scatter "
                     "overlaps the next chunk's compute")
     ap.add_argument("--e2e-steps", type=int, default=0)
-    ap.add_argument("--chunk-tokens", type=int, default=2048)
+    ap.add_argument("--chunk-tokens", type=int, default=4096)
     ap.add_argument("--cpu-sample", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()

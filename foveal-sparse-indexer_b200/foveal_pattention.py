@@ -352,9 +352,9 @@ class FovealPattentionMLP(nn.Module):
         kg, ku, v, packed, wq, k16, wout = self._weights()
         plan = _chunk_plan(M, max(1, int(chunk_tokens)))
         ch = max(plan) if plan else 1
-        nslot = 3
+        nslot = max(2, int(getattr(self, "host_slots", 3)))  # device buffer pairs in flight
         hs = getattr(self, "_host_state", None)
-        if hs is None or hs["device"] != dev:
+        if hs is None or hs["device"] != dev or len(hs["x_free"]) != nslot:
             hs = {"device": dev, "streams": tuple(torch.cuda.Stream(device=dev) for _ in range(4)),
                   "bufs": None, "x_free": [None] * nslot, "y_free": [None] * nslot, "n": 0}
             self._host_state = hs
