@@ -45,6 +45,7 @@ SIGNATURES = {
     "fp_block_energy_workspace_size": (ctypes.c_size_t, [_c_i64, _c_int]),
     "fp_block_energy": (_c_int, [_c_p, _c_i64, _c_int, _c_int, _c_int, _c_p, _c_p, _c_p, _c_p, ctypes.c_size_t,
                                  _c_p]),
+    "fp_swiglu_bwd": (_c_int, [_c_p, _c_p, _c_p, _c_int, _c_i64, _c_p, _c_p, _c_p, _c_p]),
     "fp_set_stage_events": (_c_int, [ctypes.POINTER(_c_p), _c_int]),
     "fp_device_error": (_c_int, [_c_p, _c_p, _c_p]),
 }

@@ -115,6 +115,13 @@ def calib_workload() -> Workload:
     return CONFIGS["pr1"].with_(name="calib", dtype="bf16")
 
 
+def train_workload() -> Workload:
+    """Training-mode (pooled routing + additive stream) gradient case: 64 tokens, D 256, 16 blocks, base 1
+    and 4 pooled remote blocks (``max_remote_blocks`` doubles as the pooled remote count)."""
+    return CONFIGS["pr1"].with_(name="train", batch=2, seq_len=32, hidden_dim=256, intermediate_dim=1024,
+                                max_remote_blocks=4, min_remote_blocks=1)
+
+
 @dataclass
 class Weights:
     """Parameter tensors with the reference module's names and shapes (fp32 storage, values already

@@ -53,6 +53,68 @@ def _chunk_plan(M: int, ch: int) -> list:
     return head + mid + tail
 
 
+class _PooledTrain(torch.autograd.Function):
+    """Training-mode pooled forward (foveal_pattention.py:290-342) with its backward.
+
+    Forward on the library kernels: per-token router scores, active set = top-k of their token mean
+    (no gradient through the selection, as in the reference), gated contraction over the active blocks
+    plus the additive stream out_proj(softmax(S/T) K_16).  Backward: the fused SwiGLU backward kernel
+    (``fp_swiglu_bwd``, replacing the reference's Triton ``_swiglu_bwd_kernel``, pattention_triton.py:49-96)
+    between plain GEMMs over the gathered active rows, and the chain rule of the additive stream through
+    the softmax, the 16-D scores and the RMSNorm of the query into q_proj, block_keys, out_proj and x."""
+
+    @staticmethod
+    def forward(ctx, module, x2d, k_gate, k_up, v, wq, k16, wout):
+        packed = module._packed()
+        scores, _ = kernels.router_scores(x2d, wq, k16)
+        active, _ = kernels.pooled_route(None, wq, k16, base_blocks=module.base_blocks,
+                                         remote_blocks=module.remote_blocks, mode=1, token_scores=scores,
+                                         dtype=x2d.dtype, D=x2d.shape[1])
+        _, _, c16, _ = kernels.select(scores, base_blocks=module.base_blocks, top_p=1.0, min_remote=0, max_remote=0,
+                                      capacity=0, temperature=module.temperature, block_keys=k16, want_routes=False)
+        y = kernels.pooled_forward(x2d, k_gate, k_up, v, packed, active, ctx16=c16, out_proj=wout)
+        ctx.save_for_backward(x2d, k_gate, k_up, v, wq, k16, wout, scores, active)
+        ctx.temperature = module.temperature
+        ctx.block_size = module.block_size
+        ctx.mark_non_differentiable(scores, active)
+        return y, scores, active
+
+    @staticmethod
+    def backward(ctx, dy, _dscores, _dactive):
+        x, kg, ku, v, wq, k16, wout, S, active = ctx.saved_tensors
+        T, bs = ctx.temperature, ctx.block_size
+        M, D = x.shape
+        dt = x.dtype
+        dy = dy.reshape(M, D).to(dt).contiguous()
+        idx = (active.long()[:, None] * bs + torch.arange(bs, device=x.device)).flatten()
+        kg_a, ku_a, v_a = kg.detach()[idx], ku.detach()[idx], v.detach()[idx]
+        G = x @ kg_a.t()
+        U = x @ ku_a.t()
+        dG, dU, H = kernels.swiglu_bwd(dy @ v_a.t(), G, U)
+        dx = (dG @ kg_a + dU @ ku_a).float()
+        dkg = torch.zeros_like(kg).index_copy_(0, idx, (dG.t() @ x).to(kg.dtype))
+        dku = torch.zeros_like(ku).index_copy_(0, idx, (dU.t() @ x).to(ku.dtype))
+        dv = torch.zeros_like(v).index_copy_(0, idx, (H.t() @ dy).to(v.dtype))
+        # additive stream and router (fp32, as the forward's router): S = rms_norm(x Wq^T) K16^T / 4
+        xf, dyf = x.float(), dy.float()
+        k16f, wqf, woutf = k16.detach().float(), wq.detach().float(), wout.detach().float()
+        soft = torch.softmax(S / T, dim=-1)
+        dwout = dyf.t() @ (soft @ k16f)
+        dctx = dyf @ woutf
+        dk16 = soft.t() @ dctx
+        dsoft = dctx @ k16f.t()
+        dS = soft * (dsoft - (dsoft * soft).sum(dim=-1, keepdim=True)) / T
+        q = xf @ wqf.t()
+        r = torch.rsqrt((q * q).mean(dim=-1, keepdim=True) + torch.finfo(torch.float32).eps)
+        qn = q * r
+        dqn = (dS @ k16f) * 0.25
+        dk16 = dk16 + (dS.t() @ qn) * 0.25
+        dq = r * (dqn - qn * (dqn * qn).mean(dim=-1, keepdim=True))
+        dwq = dq.t() @ xf
+        dx = dx + dq @ wqf
+        return (None, dx.to(dt), dkg, dku, dv, dwq.to(wq.dtype), dk16.to(k16.dtype), dwout.to(wout.dtype))
+
+
 class _ForwardOnly(torch.autograd.Function):
     """Attaches a backward that raises, so a training graph through the kernels fails loudly."""
 
@@ -62,7 +124,8 @@ class _ForwardOnly(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, *grads):
-        raise NotImplementedError("the B200 Foveal Pattention forward has no backward kernels yet")
+        raise NotImplementedError("backward is implemented for the training-mode pooled forward (the reference's "
+                                  "training path); token routing is an inference path")
 
 
 class FovealPattentionMLP(nn.Module):
@@ -264,6 +327,9 @@ class FovealPattentionMLP(nn.Module):
     def forward(self, x: Tensor, return_router_info: bool = False) -> Tensor | Tuple[Tensor, Dict[str, Any]]:
         orig_shape = x.shape
         D = orig_shape[-1]
+        if (self.training and self.routing == "pooled" and torch.is_grad_enabled()
+                and (x.requires_grad or any(p.requires_grad for p in self.parameters()))):
+            return self._forward_pooled_train(x, return_router_info)
         x_in = x
         x2d = x.reshape(-1, D)
         if x2d.dtype != self.k_gate.dtype:
@@ -276,6 +342,17 @@ class FovealPattentionMLP(nn.Module):
         y = self._attach_no_grad(y.reshape(*orig_shape[:-1], y.shape[-1]), x_in)
         if return_router_info:
             return y, info
+        return y
+
+    def _forward_pooled_train(self, x: Tensor, return_router_info: bool):
+        D = x.shape[-1]
+        x2d = x.reshape(-1, D).to(self.k_gate.dtype).contiguous()
+        y, scores, active = _PooledTrain.apply(self, x2d, self.k_gate, self.k_up, self.v, self.q_proj_16d.weight,
+                                               self.block_keys_16d, self.out_proj_16d.weight)
+        y = y.reshape(*x.shape[:-1], D)
+        if return_router_info:
+            return y, {"scores": scores, "active_blocks": active,
+                       "sparsity": (1.0 - self.total_active_blocks / self.num_blocks) * 100.0}
         return y
 
     def _forward_pooled(self, x2d: Tensor, orig_shape, return_router_info: bool):

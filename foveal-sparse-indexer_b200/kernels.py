@@ -117,6 +117,18 @@ def block_energy(x2d: torch.Tensor, w_gu: torch.Tensor, vnorm: torch.Tensor, num
     return E
 
 
+def swiglu_bwd(dout: torch.Tensor, g: torch.Tensor, u: torch.Tensor, want_h: bool = True):
+    """Fused SwiGLU backward (``fp_swiglu_bwd``): returns (dg, du, h or None), same dtype as ``g``."""
+    dev = require_cuda(dout, g, u)
+    dout, g, u = contig(dout.to(g.dtype)), contig(g), contig(u)
+    dg, du = torch.empty_like(g), torch.empty_like(g)
+    h = torch.empty_like(g) if want_h else None
+    rc = _lib.load().fp_swiglu_bwd(ptr(dout), ptr(g), ptr(u), dtype_code(g.dtype), g.numel(), ptr(dg), ptr(du), ptr(h),
+                                   stream_handle(dev))
+    check(rc, "fp_swiglu_bwd")
+    return dg, du, h
+
+
 def token_forward(x2d, k_gate, k_up, v, packed, q_proj, block_keys, out_proj, *, base_blocks: int,
                   top_p: float, min_remote: int, max_remote: int, temperature: float = 1.0,
                   additive: bool = True, block_stride: int = 1, block_offset: int = 0,

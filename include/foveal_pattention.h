@@ -162,6 +162,15 @@ FP_API int fp_block_energy(const void* x, int64_t M, int D, int NB, int dtype, c
                            void* stream);
 
 /*
+ * Fused SwiGLU backward of the active-set contraction (TritonFusedSwiGLUFunction.backward,
+ * pattention_triton.py:49-96): for n elements of the gate / up pre-activations g, u and the upstream
+ * gradient dout, dg = dout * u * silu'(g), du = dout * silu(g), and (optional, h may be NULL) the
+ * activation h = silu(g) * u; fp32 arithmetic, all tensors in `dtype`.
+ */
+FP_API int fp_swiglu_bwd(const void* dout, const void* g, const void* u, int dtype, int64_t n, void* dg, void* du,
+                         void* h, void* stream);
+
+/*
  * Allocation-free token-routed forward (no counterpart in the reference).  Same arguments and result
  * as fp_pattention_token_fwd, without the workspace: it runs in a FP_NOALLOC_SCRATCH_BYTES scratch
  * array that the library keeps on each GPU it is loaded on, so callers that cannot allocate device

@@ -182,6 +182,32 @@ def serve_case(seed_unused=0):
             "active": active.numpy().astype(np.int32)}
 
 
+GRAD_NAMES = ("x", "k_gate", "k_up", "v", "q_proj_16d", "block_keys_16d", "out_proj_16d")
+
+
+def train_case(ref, seed):
+    """Training-mode forward and backward of the reference module (pooled routing, additive stream;
+    foveal_pattention.py:290-342 under autograd): gradients of x and of every parameter for the loss
+    sum(y * dy) with a seeded dy."""
+    FovealPattentionMLP = ref[0]
+    wl = cfgmod.train_workload()
+    w, x = cfgmod.make_weights(wl, seed), cfgmod.make_x(wl, seed)
+    m = build_module(FovealPattentionMLP, wl, w, wl.max_remote_blocks)
+    m.train()
+    x = x.clone().requires_grad_(True)
+    dy = torch.randn(x.shape, generator=torch.Generator().manual_seed(seed + 7))
+    y, info = m(x, return_router_info=True)
+    (y * dy).sum().backward()
+    grads = {"x": x.grad, "k_gate": m.k_gate.grad, "k_up": m.k_up.grad, "v": m.v.grad,
+             "q_proj_16d": m.q_proj_16d.weight.grad, "block_keys_16d": m.block_keys_16d.grad,
+             "out_proj_16d": m.out_proj_16d.weight.grad}
+    out = {f"grad_{k}": grads[k].detach().numpy().astype(np.float32) for k in GRAD_NAMES}
+    out["y"] = y.detach().numpy().astype(np.float32)
+    out["dy"] = dy.numpy().astype(np.float32)
+    out["active"] = info["active_blocks"].numpy().astype(np.int32)
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True)
@@ -193,11 +219,13 @@ def main():
     C = cfgmod.CONFIGS
     meta_common = {"seed": args.seed, "torch": torch.__version__}
     only = set(filter(None, args.only.split(",")))
-    if only and only <= {"calib", "serve"}:
+    if only and only <= {"calib", "serve", "train"}:
         if "calib" in only:
             save("calib", {**meta_common, "config": "calib", **CALIB}, calib_case(ref, args.seed))
         if "serve" in only:
             save("serve", {**meta_common, "config": "serve", **SERVE}, serve_case())
+        if "train" in only:
+            save("train", {**meta_common, "config": "train"}, train_case(ref, args.seed))
         return
 
     # 1. PR1 (fp32, full size): token mode, pooled eval and pooled train.
@@ -280,6 +308,9 @@ def main():
 
     # 8. Whole-model surgery and decode serving with the active-set cache.
     save("serve", {**meta_common, "config": "serve", **SERVE}, serve_case())
+
+    # 9. Training-mode forward and backward (pooled routing, additive stream).
+    save("train", {**meta_common, "config": "train"}, train_case(ref, args.seed))
 
 
 if __name__ == "__main__":

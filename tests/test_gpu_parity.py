@@ -317,6 +317,30 @@ def test_calibrate_offline_svd_matches_reference(dtype):
     assert m._cached_active_blocks.tolist() == info["calib_active_blocks"]
 
 
+# ------------------------------------------------------------------ training (pooled routing) backward
+@pytest.mark.parametrize("dtype", ["fp32", "bf16"])
+def test_training_backward_matches_reference(dtype):
+    """Training-mode forward on the kernels and its backward (fused SwiGLU backward kernel, GEMMs over the
+    active rows, additive-stream / router chain rule) against the reference module's autograd."""
+    g = golden("train")
+    base_wl = configs.train_workload()
+    wl = base_wl.with_(dtype=dtype)
+    w, x = configs.make_weights(base_wl), configs.make_x(base_wl)
+    m = module_for(wl, w, routing="pooled", remote_blocks=base_wl.max_remote_blocks).train()
+    xg = x.to(DEV, wl.torch_dtype).requires_grad_(True)
+    y, info = m(xg, return_router_info=True)
+    assert torch.equal(info["active_blocks"].cpu().to(torch.int32), torch.from_numpy(g["active"]))
+    (y.float() * torch.from_numpy(g["dy"]).to(DEV)).sum().backward()
+    tol = 1e-4 if dtype == "fp32" else 3e-2
+    assert rel_err(y.float().cpu(), torch.from_numpy(g["y"])) < tol
+    got = {"x": xg.grad, "k_gate": m.k_gate.grad, "k_up": m.k_up.grad, "v": m.v.grad,
+           "q_proj_16d": m.q_proj_16d.weight.grad, "block_keys_16d": m.block_keys_16d.grad,
+           "out_proj_16d": m.out_proj_16d.weight.grad}
+    for name, t in got.items():
+        assert t is not None, name
+        assert rel_err(t.float().cpu(), torch.from_numpy(g[f"grad_{name}"])) < tol, name
+
+
 # ------------------------------------------------------------------ whole-model serving
 @pytest.mark.parametrize("dtype", ["fp32", "bf16"])
 def test_sparsified_model_prefill_and_decode(dtype):
@@ -410,8 +434,9 @@ def test_reference_module_tests_on_gpu():
     patt.train()
     out, info = patt(x, return_router_info=True)
     assert out.shape == (2, 16, 256) and "scores" in info and "active_blocks" in info
-    with pytest.raises(NotImplementedError):
-        out.sum().backward()
+    out.sum().backward()  # the reference's gradient check (:86-92)
+    assert patt.q_proj_16d.weight.grad is not None and patt.block_keys_16d.grad is not None
+    assert patt.out_proj_16d.weight.grad is not None
     patt0 = fsi.FovealPattentionMLP.from_dense_mlp(dense, block_size=64, base_blocks=0, remote_blocks=4).eval()
     with torch.no_grad():
         out, info = patt0(x, return_router_info=True)
