@@ -3,17 +3,21 @@
 //   gate/up:  for each work tile (parameter block b, up to 256 tokens that selected b):
 //             D[128 x n] = [K_gate,b ; K_up,b] (128 x D) . X[tokens]^T (D x n)   (A = weights, B = tokens)
 //             h[t, c] = silu(D[gate c, t]) * D[up c, t]  ->  H[t, slot(b)*64 + c]  (bf16)
-//   down:     Y[128 tokens x 256 cols] = sum over k-blocks j of H[:, j*64:+64] . V_b(j)^T ; + ctx16 . W_out^T
+//   down:     Y[tokens x 256 cols] = sum over k-blocks j of H[:, j*64:+64] . V_b(j)^T ; + ctx16 . W_out^T
+//             on CTA pairs (cta_group::2, 256-token tiles) from 256 tokens up, on one SM below
+//   energy:   the gate/up kernel with an fp32 |h| reduction per (token, block) instead of writing H
+//             (teacher block energies of the offline calibration)
 //
 // Reference semantics: foveal_indexer/foveal_pattention.py:329-335 (two projections, SwiGLU, V
 // projection over the active blocks), per-token form foveal_indexer/pattention_triton.py:280-311,
 // additive stream foveal_pattention.py:338-342.
 //
-// Both kernels are persistent (one CTA per SM), warp-specialised: warp 0 issues TMA loads into a
-// 4-stage shared-memory ring, warp 1 (one thread) issues tcgen05.mma into one of two TMEM
-// accumulators (2 x 256 fp32 columns), warps 2-5 drain the other accumulator (epilogue overlaps the
-// next tile's MMAs).  Operand tiles are K-major with the 128-byte swizzle: one 64-element k-block is
-// exactly one parameter block's worth of the contraction dimension of the down projection.
+// All kernels are persistent (one CTA per SM) and warp-specialised: warp 0 issues TMA loads into a
+// shared-memory ring (gate/up: plus 16 cp.async warps gathering token rows), warp 1 (one thread)
+// issues tcgen05.mma into one of two TMEM accumulators (2 x 256 fp32 columns), warps 2-5 drain the
+// other accumulator (the epilogue overlaps the next tile's MMAs).  Operand tiles are K-major with the
+// 128-byte swizzle: one 64-element k-block is exactly one parameter block's worth of the contraction
+// dimension of the down projection.
 #include "fp_internal.cuh"
 
 #include <cudaTypedefs.h>

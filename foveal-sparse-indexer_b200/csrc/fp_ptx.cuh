@@ -1,4 +1,4 @@
-// Inline-PTX helpers for sm_100a: mbarriers with bounded waits, TMA tile / gather4 loads,
+// Inline-PTX helpers for sm_100a: mbarriers with bounded waits, TMA tile loads (one CTA or a CTA pair),
 // tcgen05 (TMEM allocation, UMMA issue, commit, TMEM -> register loads) and the UMMA descriptors.
 //
 // Every wait in this file is bounded: a wait that has not completed after FP_WAIT_LIMIT_NS of
@@ -142,17 +142,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* map, uint64_t
       ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
       : "memory");
 }
-// Row gather: four rows r0..r3 of a 2-D tensor map whose box is {box0, 1}, starting at column c0,
-// written to four consecutive box-sized rows at `dst`.
-__device__ __forceinline__ void tma_gather4(void* dst, const void* map, uint64_t* bar, int c0,
-                                            int r0, int r1, int r2, int r3) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];"
-      ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
-      : "memory");
-}
-
 // Tile load into this CTA's shared memory whose completion (bytes) is counted on the leader CTA's
 // barrier; each CTA loads only its own part of the pair's operands, into its own shared memory.
 __device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* map, uint64_t* bar, int c0, int c1) {
