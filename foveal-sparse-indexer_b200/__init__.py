@@ -4,6 +4,8 @@ Public API (same names as the reference package ``foveal_indexer``):
 
     FovealPattentionMLP, sparsify_model_with_foveal_pattention   (foveal_indexer/foveal_pattention.py)
     FovealIndexer, Route, select_blocks, masked_softmax           (foveal_indexer/core.py)
+    BlockSparseLinear                                             (foveal_indexer/block_matmul.py)
+    FovealTokenformerLinear, FovealTokenformerFFN                 (foveal_indexer/tokenformer.py)
 
 Compute runs in ``libfovealpatt.so`` (hand-written sm_100a CUDA behind the C ABI of
 ``include/foveal_pattention.h``); build it with ``build.py``.  The directory name contains hyphens, so
@@ -13,10 +15,12 @@ alias ``foveal_sparse_indexer_b200`` is registered in ``sys.modules``.
 
 import sys as _sys
 
-from . import configs, kernels, sharding
+from . import block_matmul, configs, kernels, sharding, tokenformer
 from ._lib import LIB_PATH, FovealKernelError, load as load_library
+from .block_matmul import BlockSparseLinear
 from .core import FovealIndexer, Route, masked_softmax, select_blocks
 from .foveal_pattention import FovealPattentionMLP, sparsify_model_with_foveal_pattention
+from .tokenformer import FovealTokenformerFFN, FovealTokenformerLinear
 
 _sys.modules.setdefault("foveal_sparse_indexer_b200", _sys.modules[__name__])
 
@@ -27,6 +31,9 @@ __all__ = [
     "Route",
     "select_blocks",
     "masked_softmax",
+    "BlockSparseLinear",
+    "FovealTokenformerLinear",
+    "FovealTokenformerFFN",
     "FovealKernelError",
     "LIB_PATH",
     "load_library",

@@ -46,6 +46,17 @@ SIGNATURES = {
     "fp_block_energy": (_c_int, [_c_p, _c_i64, _c_int, _c_int, _c_int, _c_p, _c_p, _c_p, _c_p, ctypes.c_size_t,
                                  _c_p]),
     "fp_swiglu_bwd": (_c_int, [_c_p, _c_p, _c_p, _c_int, _c_i64, _c_p, _c_p, _c_p, _c_p]),
+    "fp_param_blocks_16d": (_c_int, [_c_p, _c_p, _c_p, _c_int, _c_i64, _c_int, _c_p, _c_p, _c_p]),
+    "fp_cosine_block_scores": (_c_int, [_c_p, _c_p, _c_p, _c_int, _c_i64, _c_int, _c_int, _c_p, _c_p, _c_p]),
+    "fp_select_remote_top_p": (_c_int, [_c_p, _c_i64, _c_int, _c_int, _c_f, _c_int, _c_int, _c_p, _c_p, _c_p,
+                                        _c_p]),
+    "fp_union_blocks": (_c_int, [_c_p, _c_p, _c_i64, _c_int, _c_int, _c_int, _c_p, _c_p, _c_p]),
+    "fp_block_sparse_linear_fwd": (_c_int, [_c_p, _c_i64, _c_int, _c_p, _c_p, _c_int, _c_int, _c_p, _c_p, _c_p,
+                                            _c_p, _c_p, _c_p, _c_sz, _c_p]),
+    "fp_tokenformer_workspace_size": (_c_sz, [_c_int, _c_i64, _c_int]),
+    "fp_tokenformer_fwd": (_c_int, [_c_p, _c_i64, _c_int, _c_p, _c_p, _c_p, _c_int, _c_int, _c_int, _c_int, _c_p,
+                                    _c_p, _c_p, _c_p, _c_p, _c_p, _c_sz, _c_p]),
+    "fp_transpose": (_c_int, [_c_p, _c_i64, _c_i64, _c_int, _c_p, _c_p]),
     "fp_set_stage_events": (_c_int, [ctypes.POINTER(_c_p), _c_int]),
     "fp_device_error": (_c_int, [_c_p, _c_p, _c_p]),
 }

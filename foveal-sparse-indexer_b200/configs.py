@@ -165,3 +165,67 @@ def make_weights(w: Workload, seed: int = 0) -> Weights:
 def make_x(w: Workload, seed: int = 0) -> torch.Tensor:
     g = torch.Generator().manual_seed(seed + 1)
     return _round(torch.randn(w.batch, w.seq_len, w.hidden_dim, generator=g), w.dtype)
+
+
+# ---------------------------------------------------------------------------------------------------
+# Layers that share the router: BlockSparseLinear ("bsl"), FovealTokenformerLinear ("tf") and
+# FovealTokenformerFFN ("ffn").  Parity cases (small, CPU-runnable) and one bench shape each.
+# Parameters are drawn in sorted state_dict key order from a generator seeded with ``seed + 11``: matrices
+# ~ N(0, fan_in^-0.5), biases and the 16-D output projections ~ N(0, 0.05) (large enough that the
+# additive stream is visible in the outputs); x ~ N(0, 1) from ``seed + 12``.
+# ---------------------------------------------------------------------------------------------------
+VARIANT_CASES: Dict[str, dict] = {
+    "bsl_a": dict(kind="bsl", in_features=256, out_features=2048, base_blocks=2, top_p=0.9, min_remote_blocks=0,
+                  max_remote_blocks=4, remote_capacity=4, bias=True, use_additive_stream=True, x_shape=(2, 5, 256)),
+    "bsl_b": dict(kind="bsl", in_features=512, out_features=1024, base_blocks=1, top_p=0.3, min_remote_blocks=1,
+                  max_remote_blocks=6, remote_capacity=6, bias=False, use_additive_stream=False, x_shape=(12, 512)),
+    "bsl_c": dict(kind="bsl", in_features=128, out_features=256, base_blocks=2, top_p=0.95, min_remote_blocks=0,
+                  max_remote_blocks=8, remote_capacity=8, bias=True, use_additive_stream=True, x_shape=(3, 7, 128)),
+    "tf_softmax": dict(kind="tf", in_features=256, out_features=256, num_param_tokens=2048, base_blocks=2, top_p=0.9,
+                       min_remote_blocks=0, max_remote_blocks=4, remote_capacity=4, activation="softmax",
+                       x_shape=(2, 6, 256)),
+    "tf_gelu": dict(kind="tf", in_features=256, out_features=512, num_param_tokens=1024, base_blocks=2, top_p=0.5,
+                    min_remote_blocks=1, max_remote_blocks=3, remote_capacity=4, activation="gelu_l2",
+                    x_shape=(1, 9, 256)),
+    "ffn": dict(kind="ffn", hidden_size=256, intermediate_size=512, num_param_tokens=512, base_blocks=2, top_p=0.95,
+                max_remote_blocks=4, x_shape=(2, 4, 256)),
+}
+
+# Bench shapes (bf16): a BlockSparseLinear with the 8B MLP's up-projection shape and a Tokenformer FFN.
+VARIANT_BENCH: Dict[str, dict] = {
+    "bsl_8b": dict(kind="bsl", in_features=4096, out_features=14336, base_blocks=4, top_p=0.8, min_remote_blocks=0,
+                   max_remote_blocks=8, remote_capacity=8, bias=False, use_additive_stream=True, x_shape=(4, 4096, 4096)),
+    "tf_ffn": dict(kind="ffn", hidden_size=2048, intermediate_size=2048, num_param_tokens=4096, base_blocks=4,
+                   top_p=0.95, max_remote_blocks=8, x_shape=(4, 4096, 2048)),
+}
+
+_MODULE_KEYS = {
+    "bsl": ("in_features", "out_features", "base_blocks", "top_p", "min_remote_blocks", "max_remote_blocks",
+            "remote_capacity", "use_additive_stream", "bias"),
+    "tf": ("in_features", "out_features", "num_param_tokens", "base_blocks", "top_p", "min_remote_blocks",
+           "max_remote_blocks", "remote_capacity", "activation"),
+    "ffn": ("hidden_size", "intermediate_size", "num_param_tokens", "base_blocks", "top_p", "max_remote_blocks"),
+}
+
+
+def variant_kwargs(case: dict) -> dict:
+    """Constructor keyword arguments of the case's module (the same for the reference's class)."""
+    return {k: case[k] for k in _MODULE_KEYS[case["kind"]]}
+
+
+def variant_params(module, seed: int = 0, dtype: str = "fp32") -> Dict[str, torch.Tensor]:
+    """Seeded values for every tensor of ``module.state_dict()`` (same keys in the reference's class)."""
+    g = torch.Generator().manual_seed(seed + 11)
+    out = {}
+    sd = module.state_dict()
+    for k in sorted(sd):  # key order, independent of the class's registration order
+        t = sd[k]
+        small = k.endswith("bias") or k.endswith("out_proj.weight")
+        std = 0.05 if small else (t.shape[-1] ** -0.5)
+        out[k] = _round(torch.randn(tuple(t.shape), generator=g) * std, dtype)
+    return out
+
+
+def variant_x(case: dict, seed: int = 0, dtype: str = "fp32") -> torch.Tensor:
+    g = torch.Generator().manual_seed(seed + 12)
+    return _round(torch.randn(case["x_shape"], generator=g), dtype)

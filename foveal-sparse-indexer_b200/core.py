@@ -1,10 +1,12 @@
 """Router core: ``Route``, ``select_blocks``, ``masked_softmax`` and ``FovealIndexer``.
 
-Mirrors ``foveal_indexer/core.py`` of the reference for the parts on the Pattention MLP hot path:
-the non-causal top-p selection with base-block reservation (core.py:46-160, branch :90-99) and the
-normalised 16-D query (core.py:214-223), both computed by the CUDA library.  The causal routing
-branch, block-key pooling, cosine block scores and the distillation loss belong to the reference's
-attention and training paths and are not part of this library; they raise ``NotImplementedError``.
+Mirrors ``foveal_indexer/core.py`` of the reference for the parts on the Pattention MLP hot path and
+on the layers that share its router (BlockSparseLinear, FovealTokenformerLinear): the non-causal
+top-p selection with base-block reservation (core.py:46-160, branch :90-99), the normalised 16-D
+query (core.py:214-223), the pooled 16-D block keys / values (core.py:225-252) and the cosine block
+scores (core.py:254-266), all computed by the CUDA library.  The causal routing branch and the
+indexer's own attention additive stream belong to the reference's attention path and raise
+``NotImplementedError``.
 """
 
 from __future__ import annotations
@@ -157,14 +159,61 @@ class FovealIndexer(nn.Module):
             remote_capacity=self.remote_capacity)
 
     def compute_kv_blocks_16d(self, x: Tensor):
-        raise NotImplementedError("block-key pooling belongs to the reference's attention path")
+        """Pooled 16-D key (L2-normalised) and value per block of ``block_size`` rows (core.py:225-252).
+
+        x: (B, N, D) or (N, D) with N % block_size == 0 -> (k_blocks, v_blocks), each (B, N / bs, 16) in
+        x's dtype (one ``fp_param_blocks_16d`` call per batch row)."""
+        if self.block_size != 64:
+            raise NotImplementedError("the CUDA kernels pool blocks of 64 rows")
+        if x.ndim == 2:
+            x = x.unsqueeze(0)
+        if x.shape[1] % self.block_size != 0:
+            raise ValueError(f"Element length {x.shape[1]} must be divisible by block_size={self.block_size}")
+        ks, vs = [], []
+        for b in range(x.shape[0]):
+            kb, vb = kernels.param_blocks_16d(x[b], self.k_proj.weight, self.v_proj.weight)
+            ks.append(kb)
+            vs.append(vb)
+        return torch.stack(ks).to(x.dtype), torch.stack(vs).to(x.dtype)
 
     def compute_block_scores(self, q_blocks: Tensor, k_blocks: Tensor) -> Tensor:
-        raise NotImplementedError("cosine block scores belong to the reference's attention path")
+        """``normalize(q) . normalize(k)^T / sqrt(16)`` (core.py:254-266): (B, Q, 16) x (B, NB, 16) ->
+        (B, Q, NB) fp32.  Runs the cosine-score kernel with the queries as inputs and an identity
+        projection (its rms_norm before the L2 normalisation does not change the direction)."""
+        require_cuda(q_blocks, k_blocks)
+        B, Q, _ = q_blocks.shape
+        eye = torch.eye(16, dtype=q_blocks.dtype, device=q_blocks.device)
+        out = []
+        for b in range(B):
+            kb = k_blocks[b if k_blocks.shape[0] > 1 else 0]
+            s, _ = kernels.cosine_block_scores(q_blocks[b], eye, kb)
+            out.append(s)
+        return torch.stack(out)
 
     def additive_stream(self, block_scores: Tensor, v_blocks: Tensor) -> Tensor:
         raise NotImplementedError("the indexer's attention additive stream is not part of this library; "
                                   "the Pattention MLP's additive stream is fused into its forward")
 
-    def distillation_loss(self, *args, **kwargs) -> Tensor:
-        raise NotImplementedError("the distillation loss is training-only and not part of this library")
+    def distillation_loss(self, student_scores: Tensor, teacher_block_mass: Tensor,
+                          valid_mask: Optional[Tensor] = None) -> Tensor:
+        """Cross-entropy of the student block distribution against the teacher block mass
+        (core.py:310-353), non-causal indexers: ``mean_q -sum_b target * log_softmax(s / T)`` with the
+        teacher mass clamped at 0 and normalised (uniform where it sums to ~0).  A scalar training loss
+        on [B, Q, NB] tensors, computed with torch on the scores' device."""
+        require_cuda(student_scores, teacher_block_mass)
+        if valid_mask is None:
+            if self.causal:
+                raise NotImplementedError("causal distillation masks belong to the reference's attention path")
+            valid_mask = torch.ones_like(student_scores, dtype=torch.bool)
+        masked = student_scores.masked_fill(~valid_mask, -float("inf"))
+        log_student = torch.log_softmax(masked.float() / self.distill_temperature, dim=-1)
+        log_student = torch.where(valid_mask, log_student, torch.zeros_like(log_student))
+        teacher = teacher_block_mass.float().clamp_min(0.0).masked_fill(~valid_mask, 0.0)
+        denom = teacher.sum(dim=-1, keepdim=True)
+        uniform = valid_mask.float() / valid_mask.float().sum(dim=-1, keepdim=True).clamp_min(1.0)
+        target = torch.where(denom > 1e-12, teacher / denom.clamp_min(1e-12), uniform)
+        kl = -(target.detach() * log_student).sum(dim=-1)
+        has_valid = valid_mask.any(dim=-1)
+        if bool(has_valid.any()):
+            return kl[has_valid].mean()
+        return student_scores.sum() * 0.0

@@ -438,6 +438,185 @@ int fp_set_stage_events(void* const* events, int n_events) {
   return FP_OK;
 }
 
+// ---------------------------------------------------------------- union-contraction layers
+int fp_param_blocks_16d(const void* P, const void* k_proj, const void* v_proj, int dtype, int64_t N, int D,
+                        float* k_blocks, float* v_blocks, void* stream) {
+  if (dtype != FP_DTYPE_F32 && dtype != FP_DTYPE_BF16) return FP_ERR_UNSUPPORTED;
+  if (!P || !k_proj || !v_proj || !k_blocks || !v_blocks || N <= 0 || D <= 0 || N % 64 != 0) return FP_ERR_INVALID_ARG;
+  if (N / 64 > INT32_MAX) return FP_ERR_UNSUPPORTED;
+  int sms;
+  FP_TRY(device_info(sms));
+  return launch_param_blocks_16d(P, k_proj, v_proj, dtype, N, D, k_blocks, v_blocks, (cudaStream_t)stream);
+}
+
+int fp_cosine_block_scores(const void* x, const void* q_proj, const float* k_blocks, int dtype, int64_t M, int D,
+                           int NB, float* scores, float* q16, void* stream) {
+  FP_TRY(check_common(dtype, M, D, NB));
+  if (!x || !q_proj || !k_blocks || !scores) return FP_ERR_INVALID_ARG;
+  if (!aligned16(x) || !aligned16(q_proj)) return FP_ERR_INVALID_ARG;
+  int sms;
+  FP_TRY(device_info(sms));
+  return launch_router_scores(x, q_proj, k_blocks, dtype, M, D, NB, 1.0f, scores, q16, (cudaStream_t)stream,
+                              k_blocks);
+}
+
+int fp_select_remote_top_p(const float* scores, int64_t M, int NB, int base, float top_p, int max_remote,
+                           int capacity, int32_t* remote_indices, int32_t* remote_counts, float* stats,
+                           void* stream) {
+  if (M < 0 || NB <= 0 || base < 0 || base > NB || capacity < 0 || max_remote < 0) return FP_ERR_INVALID_ARG;
+  if (!scores || !remote_counts || (capacity > 0 && !remote_indices)) return FP_ERR_INVALID_ARG;
+  if (NB - base > 1024) return FP_ERR_UNSUPPORTED;
+  int sms;
+  FP_TRY(device_info(sms));
+  cudaStream_t st = (cudaStream_t)stream;
+  if (M == 0) return FP_OK;
+  if (NB == base) {  // no remote columns: the reference keeps the base blocks only (block_matmul.py:202-205)
+    if (cudaMemsetAsync(remote_counts, 0, (size_t)M * 4, st) != cudaSuccess) return FP_ERR_CUDA;
+    if (capacity > 0 && cudaMemsetAsync(remote_indices, 0, (size_t)M * capacity * 4, st) != cudaSuccess)
+      return FP_ERR_CUDA;
+    return FP_OK;
+  }
+  SelectOut o{NB - base, 0, top_p, 0, max_remote, capacity, remote_indices, remote_counts, nullptr, stats};
+  o.ld = NB;
+  o.id_offset = base;
+  o.fast = 1;
+  return launch_select_out(scores + base, M, 1.0f, o, nullptr, st);
+}
+
+int fp_union_blocks(const int32_t* remote_indices, const int32_t* remote_counts, int64_t M, int capacity, int NB,
+                    int base, int32_t* blocks, int32_t* n_active, void* stream) {
+  if (M < 0 || capacity < 0 || NB <= 0 || base < 0 || !blocks || !n_active) return FP_ERR_INVALID_ARG;
+  if (M > 0 && capacity > 0 && (!remote_indices || !remote_counts)) return FP_ERR_INVALID_ARG;
+  int sms;
+  FP_TRY(device_info(sms));
+  return launch_union(remote_indices, remote_counts, M, capacity, NB, std::min(base, NB), blocks, n_active,
+                      (cudaStream_t)stream);
+}
+
+int fp_block_sparse_linear_fwd(const void* x, int64_t M, int D_in, const void* weight, const void* bias,
+                               int out_features, int dtype, const int32_t* blocks, const int32_t* n_active,
+                               const float* ctx16, const void* out_proj, void* out, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  if (dtype != FP_DTYPE_F32 && dtype != FP_DTYPE_BF16) return FP_ERR_UNSUPPORTED;
+  if (M < 0 || D_in <= 0 || out_features <= 0 || out_features % 64 != 0) return FP_ERR_INVALID_ARG;
+  if (!x || !weight || !blocks || !n_active || !out || (ctx16 && !out_proj)) return FP_ERR_INVALID_ARG;
+  if (!workspace || workspace_bytes < FP_VARIANT_WORKSPACE_MIN) return FP_ERR_WORKSPACE;
+  if (M > (int64_t)INT32_MAX / 8) return FP_ERR_UNSUPPORTED;
+  int sms;
+  FP_TRY(device_info(sms));
+  cudaStream_t st = (cudaStream_t)stream;
+  if (M == 0) return FP_OK;
+  const int NB = out_features / 64;
+  int* err = static_cast<int*>(workspace);
+  if (cudaMemsetAsync(workspace, 0, FP_VARIANT_WORKSPACE_MIN, st) != cudaSuccess) return FP_ERR_CUDA;
+  const int f32 = dtype == FP_DTYPE_F32;
+  if (tensor_path(dtype, D_in) && aligned16(x) && aligned16(weight) && aligned16(out) &&
+      (!out_proj || aligned16(out_proj))) {
+    DownArgs d{};
+    d.h = x; d.v_t = weight; d.M = M; d.D = out_features; d.Np = D_in; d.K = D_in;
+    d.stride = 1; d.offset = 0;
+    d.ctx16 = ctx16; d.out_proj = out_proj; d.out_proj_f32 = 0;
+    d.y = out; d.y_f32 = 0; d.ksplit = 1; d.err = err; d.num_sms = sms;
+    d.nmap = blocks; d.omap = blocks; d.ncnt = n_active; d.bias = bias; d.bias_f32 = 0; d.ldy = out_features;
+    FP_TRY(launch_down(d, st));
+  } else {
+    MappedGemm g{};
+    g.a = x; g.lda = D_in; g.a_f32 = f32;
+    g.b = weight; g.ldb = D_in; g.b_f32 = f32; g.nn = 0;
+    g.M = M; g.K = D_in; g.N = out_features;
+    g.nmap = blocks; g.omap = blocks; g.ncnt = n_active;
+    g.bias = bias; g.bias_f32 = f32;
+    g.ctx16 = ctx16; g.out_proj = out_proj; g.out_proj_f32 = f32;
+    g.y = out; g.ldy = out_features; g.y_f32 = f32;
+    FP_TRY(launch_mapped_gemm_simt(g, st));
+  }
+  return launch_fill_inactive(blocks, n_active, NB, M, ctx16, out_proj, dtype, out, out_features, sms, st);
+}
+
+namespace {
+struct TfLayout {
+  size_t s, p, total;
+};
+TfLayout tf_layout(int dtype, int64_t M, int Np) {
+  TfLayout L{};
+  Carve c;
+  c.take(FP_VARIANT_WORKSPACE_MIN);  // device error word
+  L.s = c.take((size_t)M * Np * 4);
+  L.p = c.take((size_t)M * Np * (dtype == FP_DTYPE_BF16 ? 2 : 4));
+  L.total = c.off;
+  return L;
+}
+}  // namespace
+
+size_t fp_tokenformer_workspace_size(int dtype, int64_t M, int num_param_tokens) {
+  return tf_layout(dtype, std::max<int64_t>(M, 0), std::max(num_param_tokens, 0)).total;
+}
+
+int fp_tokenformer_fwd(const void* x, int64_t M, int D_in, const void* k_param, const void* v_param,
+                       const void* v_param_t, int num_param_tokens, int D_out, int dtype, int activation,
+                       const int32_t* blocks, const int32_t* n_active, const float* ctx16, const void* out_proj,
+                       void* out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (dtype != FP_DTYPE_F32 && dtype != FP_DTYPE_BF16) return FP_ERR_UNSUPPORTED;
+  const int Np = num_param_tokens;
+  if (M < 0 || D_in <= 0 || D_out <= 0 || Np <= 0 || Np % 64 != 0) return FP_ERR_INVALID_ARG;
+  if (activation != 0 && activation != 1) return FP_ERR_INVALID_ARG;
+  if (!x || !k_param || !v_param || !blocks || !n_active || !out || (ctx16 && !out_proj)) return FP_ERR_INVALID_ARG;
+  if (M > (int64_t)INT32_MAX / 8) return FP_ERR_UNSUPPORTED;
+  const TfLayout L = tf_layout(dtype, M, Np);
+  if (!workspace || workspace_bytes < L.total) return FP_ERR_WORKSPACE;
+  int sms;
+  FP_TRY(device_info(sms));
+  cudaStream_t st = (cudaStream_t)stream;
+  if (M == 0) return FP_OK;
+  char* ws = static_cast<char*>(workspace);
+  int* err = reinterpret_cast<int*>(ws);
+  float* S = reinterpret_cast<float*>(ws + L.s);
+  void* P = ws + L.p;
+  if (cudaMemsetAsync(workspace, 0, FP_VARIANT_WORKSPACE_MIN, st) != cudaSuccess) return FP_ERR_CUDA;
+  const int f32 = dtype == FP_DTYPE_F32;
+  const float div = sqrtf((float)D_in);  // math.sqrt(in_features) as the fp32 divisor (tokenformer.py:104)
+  const bool tc = tensor_path(dtype, D_in) && D_out % 64 == 0 && v_param_t && aligned16(x) && aligned16(k_param) &&
+                  aligned16(v_param_t) && aligned16(out) && (!out_proj || aligned16(out_proj));
+  if (tc) {
+    DownArgs g1{};  // S[:, j*64 + c] = x . k_param[blocks[j]*64 + c]
+    g1.h = x; g1.v_t = k_param; g1.M = M; g1.D = Np; g1.Np = D_in; g1.K = D_in; g1.stride = 1;
+    g1.y = S; g1.y_f32 = 1; g1.ksplit = 1; g1.err = err; g1.num_sms = sms;
+    g1.nmap = blocks; g1.ncnt = n_active; g1.ldy = Np;
+    FP_TRY(launch_down(g1, st));
+    FP_TRY(launch_rowact(S, Np, M, n_active, activation, div, P, Np, 0, st));
+    DownArgs g2{};  // out = P[:, :64 n] . v_param[blocks] + ctx16 . out_proj^T
+    g2.h = P; g2.v_t = v_param_t; g2.M = M; g2.D = D_out; g2.Np = Np; g2.K = Np; g2.stride = 1;
+    g2.bmap = blocks; g2.kcnt = n_active;
+    g2.ctx16 = ctx16; g2.out_proj = out_proj; g2.out_proj_f32 = 0;
+    g2.y = out; g2.y_f32 = 0; g2.ksplit = 1; g2.err = err; g2.num_sms = sms; g2.ldy = D_out;
+    return launch_down(g2, st);
+  }
+  MappedGemm g1{};
+  g1.a = x; g1.lda = D_in; g1.a_f32 = f32;
+  g1.b = k_param; g1.ldb = D_in; g1.b_f32 = f32; g1.nn = 0;
+  g1.M = M; g1.K = D_in; g1.N = Np;
+  g1.nmap = blocks; g1.ncnt = n_active;
+  g1.y = S; g1.ldy = Np; g1.y_f32 = 1;
+  FP_TRY(launch_mapped_gemm_simt(g1, st));
+  FP_TRY(launch_rowact(S, Np, M, n_active, activation, div, P, Np, 1, st));
+  MappedGemm g2{};
+  g2.a = P; g2.lda = Np; g2.a_f32 = 1;
+  g2.b = v_param; g2.ldb = D_out; g2.b_f32 = f32; g2.nn = 1;
+  g2.M = M; g2.K = Np; g2.N = D_out;
+  g2.kmap = blocks; g2.kcnt = n_active;
+  g2.ctx16 = ctx16; g2.out_proj = out_proj; g2.out_proj_f32 = f32;
+  g2.y = out; g2.ldy = D_out; g2.y_f32 = f32;
+  return launch_mapped_gemm_simt(g2, st);
+}
+
+int fp_transpose(const void* src, int64_t rows, int64_t cols, int dtype, void* dst, void* stream) {
+  if (dtype != FP_DTYPE_F32 && dtype != FP_DTYPE_BF16) return FP_ERR_UNSUPPORTED;
+  if (!src || !dst || rows < 0 || cols < 0) return FP_ERR_INVALID_ARG;
+  int sms;
+  FP_TRY(device_info(sms));
+  return launch_transpose(src, rows, cols, dtype, dst, (cudaStream_t)stream);
+}
+
 int fp_device_error(void* workspace, void* stream, int* code) {
   if (!workspace) return FP_ERR_INVALID_ARG;
   int host = 0;

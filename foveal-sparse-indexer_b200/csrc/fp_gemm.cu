@@ -387,6 +387,85 @@ __device__ __forceinline__ void down_tile(int tile, int m_tiles, int n_tiles, in
   n = r / gsz;
 }
 
+// Additive stream, bias and store of 32 consecutive computed columns [col0, col0 + 32) of one row per lane
+// (the warp's lanes hold 32 rows).  `add`: add ctx16 . W_out^T and the bias (done by exactly one
+// contributor of a tile).  With split-K (ks > 1) the fp32 partial of split `split` is stored instead of
+// the output.  Computed column c lands in Y column omap[c / 64] * 64 + c % 64 (block-mapped form) or c;
+// columns at or beyond `ncols` are not stored.
+__device__ __forceinline__ void down_store_chunk(const DownArgs& a, float (&o)[32], const float (&ctx)[16],
+                                                 int64_t row, bool row_ok, int col0, bool add, int split, int ks,
+                                                 int ncols) {
+  const int lane = threadIdx.x & 31;
+  if (col0 >= ncols) return;  // uniform over the warp
+  const int ocol0 = a.omap ? a.omap[col0 >> 6] * kBlock + (col0 & 63) : col0;
+  if (a.ctx16 && add) {
+    // o[i] += sum_k ctx[k] * W_out[ocol0 + i][k]; lane L loads row ocol0 + L of W_out and the warp
+    // broadcasts it (all lanes of a chunk share the same 32 columns)
+    float wv[16];
+    const int64_t wrow = (int64_t)(ocol0 + lane) * 16;
+    if (a.out_proj_f32) {
+      const float4* wp = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.out_proj) + wrow);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float4 f = __ldg(wp + k);
+        wv[4 * k] = f.x; wv[4 * k + 1] = f.y; wv[4 * k + 2] = f.z; wv[4 * k + 3] = f.w;
+      }
+    } else {
+      const uint4* wp = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.out_proj) + wrow);
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const uint4 u = __ldg(wp + k);
+        const uint32_t ww[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          wv[8 * k + 2 * e] = __uint_as_float(ww[e] << 16);
+          wv[8 * k + 2 * e + 1] = __uint_as_float(ww[e] & 0xFFFF0000u);
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      float sacc = 0.f;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) sacc = fmaf(ctx[k], __shfl_sync(0xffffffffu, wv[k], i), sacc);
+      o[i] += sacc;
+    }
+  }
+  if (a.bias && add) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      o[i] += a.bias_f32 ? __ldg(reinterpret_cast<const float*>(a.bias) + ocol0 + i)
+                         : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.bias)[ocol0 + i]);
+  }
+  if (!row_ok) return;
+  const int64_t ldy = a.ldy > 0 ? a.ldy : (int64_t)a.D;
+  if (ks > 1) {  // partial of this split; summed in split order by splitk_reduce_kernel
+    float4* yp = reinterpret_cast<float4*>(a.y_acc + ((int64_t)split * a.M + row) * a.D + col0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) yp[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+  } else if (a.y_f32) {
+    float4* yp = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.y) + row * ldy + ocol0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) yp[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+  } else {
+    uint4* yp = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.y) + row * ldy + ocol0);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint32_t pk[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const __nv_bfloat162 b2 = __floats2bfloat162_rn(o[8 * i + 2 * e], o[8 * i + 2 * e + 1]);
+        pk[e] = *reinterpret_cast<const uint32_t*>(&b2);
+      }
+      yp[i] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    }
+  }
+}
+
+// Block-mapped form (DownArgs.nmap / omap / ncnt / kcnt): the B tile of a 256-column tile is loaded as
+// four 64-row boxes from rows nmap[j]*64 (one box per column block j), tiles past the device count of
+// column blocks are skipped by every role, and the k-loop runs over the device count of k-blocks (none:
+// the tile's accumulator is taken as zero).
 __global__ void __launch_bounds__(kGemmThreads, 1)
 down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CUtensorMap tm_vt,
             const DownArgs a) {
@@ -404,7 +483,10 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
   const int n_tiles = (a.D + kTileN - 1) / kTileN;
   const int ks = a.ksplit > 1 ? a.ksplit : 1;
   const int ntiles = m_tiles * n_tiles * ks;
-  const int nkb_all = a.K / kTileK;
+  int nkb_all = a.K / kTileK;
+  if (a.kcnt) nkb_all = max(0, min(nkb_all, *a.kcnt));
+  int ncols = a.D;
+  if (a.ncnt) ncols = max(0, min(a.D / kBlock, *a.ncnt)) * kBlock;
   uint32_t issued = 0;
 
   if (warp == 0) {
@@ -414,8 +496,10 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
         int m, n;
         down_tile(tile / ks, m_tiles, n_tiles, m, n);
+        if (n * kTileN >= ncols) continue;
         const int sp = tile % ks;
         const int kb0 = (int)((int64_t)sp * nkb_all / ks), kb1 = (int)((int64_t)(sp + 1) * nkb_all / ks);
+        const int nv = a.nmap ? min(kTileN / kBlock, (ncols - n * kTileN) / kBlock) : 0;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1u;
@@ -423,9 +507,17 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
           uint8_t* As = smem + s * kStageBytes;
           uint8_t* Bs = As + kABytes;
           const int gb = a.bmap ? a.bmap[kb] : kb * a.stride + a.offset;
-          mbar_arrive_expect_tx(&bars->full[s], kStageBytes);
-          tma_load_2d(As, &tm_h, &bars->full[s], kb * kTileK, m * kTileM);
-          tma_load_2d(Bs, &tm_vt, &bars->full[s], gb * kBlock, n * kTileN);
+          if (a.nmap) {
+            mbar_arrive_expect_tx(&bars->full[s], kABytes + (uint32_t)nv * (kBlock * kTileK * 2));
+            tma_load_2d(As, &tm_h, &bars->full[s], kb * kTileK, m * kTileM);
+            for (int i = 0; i < nv; ++i)
+              tma_load_2d(Bs + i * (kBlock * kTileK * 2), &tm_vt, &bars->full[s], gb * kBlock,
+                          a.nmap[n * (kTileN / kBlock) + i] * kBlock);
+          } else {
+            mbar_arrive_expect_tx(&bars->full[s], kStageBytes);
+            tma_load_2d(As, &tm_h, &bars->full[s], kb * kTileK, m * kTileM);
+            tma_load_2d(Bs, &tm_vt, &bars->full[s], gb * kBlock, n * kTileN);
+          }
         }
       }
       issued = it;
@@ -438,6 +530,9 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
       bool ok = true;
       const uint32_t idesc = umma_idesc_bf16(kTileM, kTileN);
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        int m, n;
+        down_tile(tile / ks, m_tiles, n_tiles, m, n);
+        if (n * kTileN >= ncols) continue;
         const int sp = tile % ks;
         const int kb0 = (int)((int64_t)sp * nkb_all / ks), kb1 = (int)((int64_t)(sp + 1) * nkb_all / ks);
         const int acc = local & 1;
@@ -471,8 +566,9 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
       int m, n;
       down_tile(tile / ks, m_tiles, n_tiles, m, n);
+      if (n * kTileN >= ncols) continue;
       const int split = tile % ks;
-      const bool lead_split = split == 0;  // the additive stream is added by one split only
+      const bool kempty = (int)((int64_t)(split + 1) * nkb_all / ks) <= (int)((int64_t)split * nkb_all / ks);
       const int acc = local & 1;
       const uint32_t aph = (local >> 1) & 1;
       if (!warp_wait(&bars->accf[acc], aph, a.err, kErrWaitAccFull)) break;
@@ -491,70 +587,15 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
         }
       }
       for (int c = 0; c < kTileN / 32; ++c) {
-        const int col0 = n * kTileN + c * 32;
         uint32_t v[32];
         __syncwarp();
         tmem_ld32(tmem_base + acc * kTileN + c * 32 + ((uint32_t)(32 * q) << 16), v);
         tmem_ld_wait();
-        // additive stream: o[i] += sum_k ctx[k] * W_out[col0 + i][k]; lane L loads row col0 + L of
-        // W_out and the warp broadcasts it (all lanes of a chunk share the same 32 columns)
         float o[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = __uint_as_float(v[i]);
-        if (a.ctx16 && lead_split && col0 < a.D) {
-          float w[16];
-          const int64_t wrow = (int64_t)(col0 + lane) * 16;
-          if (a.out_proj_f32) {
-            const float4* wp = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.out_proj) + wrow);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float4 f = __ldg(wp + k);
-              w[4 * k] = f.x; w[4 * k + 1] = f.y; w[4 * k + 2] = f.z; w[4 * k + 3] = f.w;
-            }
-          } else {
-            const uint4* wp = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.out_proj) + wrow);
-#pragma unroll
-            for (int k = 0; k < 2; ++k) {
-              const uint4 u = __ldg(wp + k);
-              const uint32_t ww[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                w[8 * k + 2 * e] = __uint_as_float(ww[e] << 16);
-                w[8 * k + 2 * e + 1] = __uint_as_float(ww[e] & 0xFFFF0000u);
-              }
-            }
-          }
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            float s = 0.f;
-#pragma unroll
-            for (int k = 0; k < 16; ++k) s = fmaf(ctx[k], __shfl_sync(0xffffffffu, w[k], i), s);
-            o[i] += s;
-          }
-        }
-        if (row_ok && col0 < a.D) {
-        if (ks > 1) {  // partial of this split; summed in split order by splitk_reduce_kernel
-          float4* yp = reinterpret_cast<float4*>(a.y_acc + ((int64_t)split * a.M + row) * a.D + col0);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) yp[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
-        } else if (a.y_f32) {
-          float4* yp = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.y) + row * a.D + col0);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) yp[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
-        } else {
-          uint4* yp = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.y) + row * a.D + col0);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            uint32_t p[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const __nv_bfloat162 b2 = __floats2bfloat162_rn(o[8 * i + 2 * e], o[8 * i + 2 * e + 1]);
-              p[e] = *reinterpret_cast<const uint32_t*>(&b2);
-            }
-            yp[i] = make_uint4(p[0], p[1], p[2], p[3]);
-          }
-        }
-        }
+        for (int i = 0; i < 32; ++i) o[i] = kempty ? 0.f : __uint_as_float(v[i]);
+        // the additive stream and the bias are added by one split only
+        down_store_chunk(a, o, ctx, row, row_ok, n * kTileN + c * 32, split == 0, split, ks, ncols);
       }
       tc_fence_before();
       __syncwarp();
@@ -563,69 +604,6 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
     }
   }
   pipe_teardown(bars, issued, a.err);
-}
-
-// Additive stream and store of 32 consecutive output columns [col0, col0 + 32) of one row per lane (the
-// warp's lanes hold 32 rows).  `add`: add ctx16 . W_out^T (done by exactly one contributor of a tile).
-// With split-K (ks > 1) the fp32 partial of split `split` is stored instead of the output.
-__device__ __forceinline__ void down_store_chunk(const DownArgs& a, float (&o)[32], const float (&ctx)[16],
-                                                 int64_t row, bool row_ok, int col0, bool add, int split, int ks) {
-  const int lane = threadIdx.x & 31;
-  if (a.ctx16 && add && col0 < a.D) {
-    // o[i] += sum_k ctx[k] * W_out[col0 + i][k]; lane L loads row col0 + L of W_out and the warp broadcasts
-    // it (all lanes of a chunk share the same 32 columns)
-    float wv[16];
-    const int64_t wrow = (int64_t)(col0 + lane) * 16;
-    if (a.out_proj_f32) {
-      const float4* wp = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.out_proj) + wrow);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float4 f = __ldg(wp + k);
-        wv[4 * k] = f.x; wv[4 * k + 1] = f.y; wv[4 * k + 2] = f.z; wv[4 * k + 3] = f.w;
-      }
-    } else {
-      const uint4* wp = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.out_proj) + wrow);
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const uint4 u = __ldg(wp + k);
-        const uint32_t ww[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          wv[8 * k + 2 * e] = __uint_as_float(ww[e] << 16);
-          wv[8 * k + 2 * e + 1] = __uint_as_float(ww[e] & 0xFFFF0000u);
-        }
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      float sacc = 0.f;
-#pragma unroll
-      for (int k = 0; k < 16; ++k) sacc = fmaf(ctx[k], __shfl_sync(0xffffffffu, wv[k], i), sacc);
-      o[i] += sacc;
-    }
-  }
-  if (!row_ok || col0 >= a.D) return;
-  if (ks > 1) {  // partial of this split; summed in split order by splitk_reduce_kernel
-    float4* yp = reinterpret_cast<float4*>(a.y_acc + ((int64_t)split * a.M + row) * a.D + col0);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) yp[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
-  } else if (a.y_f32) {
-    float4* yp = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.y) + row * a.D + col0);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) yp[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
-  } else {
-    uint4* yp = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.y) + row * a.D + col0);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      uint32_t pk[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const __nv_bfloat162 b2 = __floats2bfloat162_rn(o[8 * i + 2 * e], o[8 * i + 2 * e + 1]);
-        pk[e] = *reinterpret_cast<const uint32_t*>(&b2);
-      }
-      yp[i] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-    }
-  }
 }
 
 // ============================================================================================
@@ -772,7 +750,7 @@ down2_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ C
         float o[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) o[i] = __uint_as_float(v[i]);
-        down_store_chunk(a, o, ctx, row, row_ok, n * kTileN + c * 32, true, 0, 1);
+        down_store_chunk(a, o, ctx, row, row_ok, n * kTileN + c * 32, true, 0, 1, a.D);
       }
       tc_fence_before();
       __syncwarp();
@@ -904,16 +882,18 @@ int launch_pack_gate_up(const void* kg, const void* ku, int Np, int D, void* wgu
 }
 
 int launch_down(const DownArgs& a, cudaStream_t st) {
+  const bool mapped = a.nmap || a.omap || a.ncnt || a.kcnt || a.bias || a.ldy > 0;
+  const int ks = a.ksplit > 1 ? a.ksplit : 1;
+  if (mapped && (ks != 1 || a.D % kBlock != 0)) return FP_ERR_INVALID_ARG;
   CUtensorMap th, tv;
   if (!encode_map_2d(&th, a.h, a.K, a.M, (uint64_t)a.K * 2, kTileK, kTileM) ||
-      !encode_map_2d(&tv, a.v_t, a.Np, a.D, (uint64_t)a.Np * 2, kTileK, kTileN))
+      !encode_map_2d(&tv, a.v_t, a.Np, a.D, (uint64_t)a.Np * 2, kTileK, a.nmap ? kBlock : kTileN))
     return FP_ERR_CUDA;
   static std::once_flag once;
   static int attr = FP_OK;
   std::call_once(once, [] { attr = set_smem((const void*)down_kernel); });
   if (attr != FP_OK) return attr;
-  const int ks = a.ksplit > 1 ? a.ksplit : 1;
-  if (ks == 1 && a.M >= 2 * kTileM && a.num_sms >= 2) {
+  if (!mapped && ks == 1 && a.M >= 2 * kTileM && a.num_sms >= 2) {
     // CTA pairs: 256 x 256 tiles, each CTA loading 128 rows of H and half of the V_t tile
     CUtensorMap tv2;
     if (!encode_map_2d(&tv2, a.v_t, a.Np, a.D, (uint64_t)a.Np * 2, kTileK, kTileN / 2)) return FP_ERR_CUDA;

@@ -27,11 +27,17 @@ constexpr int kGuN = 256;
 constexpr int kGuStages = 4;
 
 // ---- router.cu
+// k16f_cos (optional): fp32 block keys [NB, 16] of the cosine form (both sides L2-normalised,
+// compute_block_scores core.py:254-266) used instead of k16.
 int launch_router_scores(const void* x, const void* wq, const void* k16, int dtype, int64_t M, int D,
-                         int NB, float temperature, float* scores, float* q16, cudaStream_t st);
+                         int NB, float temperature, float* scores, float* q16, cudaStream_t st,
+                         const float* k16f_cos = nullptr);
+struct SelectOut;
 int launch_select(const float* scores, int64_t M, int NB, int base, float top_p, int k_min, int k_max,
                   int capacity, float temperature, int32_t* idx, int32_t* cnt, const float* k16f,
                   float* ctx16, float* stats, cudaStream_t st);
+int launch_select_out(const float* scores, int64_t M, float temperature, const SelectOut& o, const float* k16f,
+                      cudaStream_t st);
 int launch_colmean(const void* a, int dtype, int64_t M, int D, float* part, float* mean, cudaStream_t st);
 int launch_pooled_topk(const float* mean_vec, const void* wq, const void* k16, int dtype, int D, int NB,
                        int base, int remote, int mode, int32_t* active, float* mean_scores_out,
@@ -46,6 +52,10 @@ struct SelectOut {
   int32_t* cnt;   // [M]
   float* ctx16;   // optional [M, 16] additive-stream context softmax(S/T) . K16
   float* stats;   // optional [3]: capped tokens, sum of counts, base-only tokens
+  int64_t ld = 0;     // row stride of the score matrix (0: NB)
+  int id_offset = 0;  // added to every written block id
+  int fast = 0;       // BlockSparseLinear's inference rule: count = min(#(cum < top_p) + 1, K_max), no
+                      // clamp to the available blocks (block_matmul.py:190-193)
 };
 
 // Fused token routing (scores + selection + block CSR) of the token-routed forward.
@@ -130,6 +140,15 @@ struct DownArgs {
   float* y_acc;         // [ksplit, M, D] fp32 partials (ksplit > 1), summed in split order
   int* err;
   int num_sms;
+  // Block-mapped form (one-SM kernel only; the union contractions of BlockSparseLinear and the
+  // Tokenformer layer).  Output columns are handled in 64-wide column blocks j < D / 64:
+  const int32_t* nmap = nullptr;  // B rows of column block j = v_t rows [nmap[j]*64, +64) (else j*64 + n)
+  const int32_t* omap = nullptr;  // Y columns of column block j = [omap[j]*64, +64) (else [j*64, +64))
+  const int32_t* ncnt = nullptr;  // device count of valid column blocks (else D / 64)
+  const int32_t* kcnt = nullptr;  // device count of k-blocks (else K / 64)
+  const void* bias = nullptr;     // optional per-Y-column bias (bf16, or fp32 per bias_f32)
+  int bias_f32 = 0;
+  int64_t ldy = 0;                // Y row stride in elements (0: D)
 };
 int launch_down(const DownArgs& a, cudaStream_t st);
 // Split-K factor used by the down projection for M tokens (1 = none).  Small batches (decode) have too
@@ -160,6 +179,29 @@ struct SimtArgs {
   int y_f32;
 };
 int launch_simt(const SimtArgs& a, cudaStream_t st);
+
+// ---- variants.cu (BlockSparseLinear / Tokenformer contractions over the union of selected blocks)
+int launch_param_blocks_16d(const void* P, const void* wk, const void* wv, int dtype, int64_t N, int D,
+                            float* kb, float* vb, cudaStream_t st);
+int launch_union(const int32_t* idx, const int32_t* cnt, int64_t M, int capacity, int NB, int base,
+                 int32_t* active, int32_t* n_active, cudaStream_t st);
+int launch_rowact(const float* S, int64_t lds, int64_t M, const int32_t* n_active, int mode, float div, void* P,
+                  int64_t ldp, int p_f32, cudaStream_t st);
+int launch_fill_inactive(const int32_t* blocks, const int32_t* n_active, int NB, int64_t M, const float* ctx16,
+                         const void* out_proj, int dtype, void* out, int64_t ldo, int num_sms, cudaStream_t st);
+int launch_transpose(const void* src, int64_t rows, int64_t cols, int dtype, void* dst, cudaStream_t st);
+// CUDA-core contraction over mapped 64-wide blocks (see mapped_gemm_simt_kernel).
+struct MappedGemm {
+  const void* a; int64_t lda; int a_f32;
+  const void* b; int64_t ldb; int b_f32;
+  int nn;                 // 0: B rows are output columns (B[row(c), k]); 1: B rows are contraction indices
+  int64_t M; int K, N;    // contraction length and computed columns (upper bounds)
+  const int32_t* nmap; const int32_t* kmap; const int32_t* omap; const int32_t* ncnt; const int32_t* kcnt;
+  const void* bias; int bias_f32;
+  const float* ctx16; const void* out_proj; int out_proj_f32;
+  void* y; int64_t ldy; int y_f32;
+};
+int launch_mapped_gemm_simt(const MappedGemm& g, cudaStream_t st);
 
 // ---- tensor maps
 bool encode_map_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,

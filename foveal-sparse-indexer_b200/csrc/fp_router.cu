@@ -47,9 +47,24 @@ template <typename T>
 __global__ void __launch_bounds__(kScoreWarps * 32)
 router_scores_kernel(const T* __restrict__ x, const T* __restrict__ wq, const T* __restrict__ k16,
                      int64_t M, int D, int NB, float inv_scale_div, float temperature,
-                     float* __restrict__ scores, float* __restrict__ q16_out) {
+                     float* __restrict__ scores, float* __restrict__ q16_out, const float* __restrict__ kcos) {
   extern __shared__ float sk[];  // [16][NB] fp32 block keys, transposed: lanes read consecutive blocks
-  for (int i = threadIdx.x; i < NB * 16; i += blockDim.x) sk[(i & 15) * NB + (i >> 4)] = to_f32(k16[i]);
+  if (kcos) {
+    // cosine form: keys L2-normalised in fp32 (F.normalize: k / max(||k||, 1e-12))
+    for (int b = threadIdx.x; b < NB; b += blockDim.x) {
+      float kv[16], ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        kv[j] = kcos[b * 16 + j];
+        ss = fmaf(kv[j], kv[j], ss);
+      }
+      const float nrm = fmaxf(__fsqrt_rn(ss), 1e-12f);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) sk[j * NB + b] = __fdiv_rn(kv[j], nrm);
+    }
+  } else {
+    for (int i = threadIdx.x; i < NB * 16; i += blockDim.x) sk[(i & 15) * NB + (i >> 4)] = to_f32(k16[i]);
+  }
   __syncthreads();
 
   const int lane = threadIdx.x & 31;
@@ -107,6 +122,14 @@ router_scores_kernel(const T* __restrict__ x, const T* __restrict__ wq, const T*
 #pragma unroll
       for (int j = 1; j < 16; ++j) qv = (lane == j) ? q[j] : qv;
       q16_out[tok * 16 + lane] = qv;
+    }
+    if (kcos) {  // normalize(rms_norm(q)) of compute_block_scores
+      float qq = 0.f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) qq = fmaf(q[j], q[j], qq);
+      const float nrm = fmaxf(__fsqrt_rn(qq), 1e-12f);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) q[j] = __fdiv_rn(q[j], nrm);
     }
     for (int b = lane; b < NB; b += 32) {
       float s = 0.f;
@@ -409,7 +432,7 @@ __device__ __forceinline__ int select_token(float (&s)[E], int64_t tok, const Se
   int32_t* orow = o.idx + tok * o.capacity;
   bool done = false;
   auto emit = [&](unsigned long long kv, int i) {
-    const int32_t id = i < NB ? (int32_t)(0xFFFFFFFFu - (uint32_t)(kv & 0xFFFFFFFFull)) : 0;
+    const int32_t id = i < NB ? (int32_t)(0xFFFFFFFFu - (uint32_t)(kv & 0xFFFFFFFFull)) + o.id_offset : 0;
     if (i < o.capacity) orow[i] = id;
     if (sbuf) sbuf[i] = id;
     const uint32_t hi = (uint32_t)(kv >> 32);
@@ -505,9 +528,11 @@ __device__ __forceinline__ int select_token(float (&s)[E], int64_t tok, const Se
           }
         }
         needed = below + 1;
+      } else if (o.fast) {
+        needed = 1;
       }
       needed = needed > o.k_min ? needed : o.k_min;
-      counts = needed < avail ? needed : avail;
+      counts = (o.fast || needed < avail) ? needed : avail;
       counts = counts < o.k_max ? counts : o.k_max;
       if (counts < 0) counts = 0;
     }
@@ -542,7 +567,7 @@ select_blocks_kernel(const float* __restrict__ scores, int64_t M, float temperat
   }
   float* pbuf = pball + warp * N;
   for (int64_t tok = (int64_t)blockIdx.x * kSelWarps + warp; tok < M; tok += (int64_t)gridDim.x * kSelWarps) {
-    const float* srow = scores + tok * o.NB;
+    const float* srow = scores + tok * (o.ld > 0 ? o.ld : (int64_t)o.NB);
     float s[E];
 #pragma unroll
     for (int r = 0; r < E; ++r) {
@@ -1037,9 +1062,10 @@ pooled_topk_kernel(const float* __restrict__ mean_vec, const T* __restrict__ wq,
 // Host launchers
 // ============================================================================================
 int launch_router_scores(const void* x, const void* wq, const void* k16, int dtype, int64_t M, int D,
-                         int NB, float temperature, float* scores, float* q16, cudaStream_t st) {
+                         int NB, float temperature, float* scores, float* q16, cudaStream_t st,
+                         const float* kcos) {
   if (M <= 0) return FP_OK;
-  if (dtype == FP_DTYPE_BF16 && D % (64 * kMmaWarps) == 0 && temperature == 1.0f) {
+  if (dtype == FP_DTYPE_BF16 && D % (64 * kMmaWarps) == 0 && temperature == 1.0f && !kcos) {
     const size_t smem = (size_t)NB * 16 * sizeof(float) + kMmaWarps * 16 * 17 * sizeof(float);
     if (smem > 48 * 1024 &&
         cudaFuncSetAttribute(router_scores_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
@@ -1061,10 +1087,10 @@ int launch_router_scores(const void* x, const void* wq, const void* k16, int dty
   if (dtype == FP_DTYPE_BF16)
     router_scores_kernel<__nv_bfloat16><<<blocks, kScoreWarps * 32, smem, st>>>(
         (const __nv_bfloat16*)x, (const __nv_bfloat16*)wq, (const __nv_bfloat16*)k16, M, D, NB, 0.25f,
-        temperature, scores, q16);
+        temperature, scores, q16, kcos);
   else
     router_scores_kernel<float><<<blocks, kScoreWarps * 32, smem, st>>>(
-        (const float*)x, (const float*)wq, (const float*)k16, M, D, NB, 0.25f, temperature, scores, q16);
+        (const float*)x, (const float*)wq, (const float*)k16, M, D, NB, 0.25f, temperature, scores, q16, kcos);
   return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
 }
 
@@ -1085,8 +1111,14 @@ int select_go(const float* scores, int64_t M, float temperature, const SelectOut
 int launch_select(const float* scores, int64_t M, int NB, int base, float top_p, int k_min, int k_max,
                   int capacity, float temperature, int32_t* idx, int32_t* cnt, const float* k16f,
                   float* ctx16, float* stats, cudaStream_t st) {
-  if (M <= 0) return FP_OK;
   const SelectOut o{NB, base, top_p, k_min, k_max, capacity, idx, cnt, ctx16, stats};
+  return launch_select_out(scores, M, temperature, o, k16f, st);
+}
+
+int launch_select_out(const float* scores, int64_t M, float temperature, const SelectOut& o, const float* k16f,
+                      cudaStream_t st) {
+  if (M <= 0) return FP_OK;
+  const int NB = o.NB;
   if (NB <= 32) return select_go<1>(scores, M, temperature, o, k16f, st);
   if (NB <= 64) return select_go<2>(scores, M, temperature, o, k16f, st);
   if (NB <= 128) return select_go<4>(scores, M, temperature, o, k16f, st);

@@ -190,3 +190,130 @@ def pooled_forward(x2d, k_gate, k_up, v, packed, active, *, ctx16=None, out_proj
                                       1 if out_f32 else 0, ptr(ws), ws.numel(), stream_handle(dev))
     check(rc, "fp_pattention_pooled_fwd")
     return y
+
+
+# ---------------------------------------------------------------------------------------------------
+# Union-contraction layers (BlockSparseLinear, FovealTokenformerLinear)
+# ---------------------------------------------------------------------------------------------------
+
+def param_blocks_16d(P: torch.Tensor, k_proj: torch.Tensor, v_proj: torch.Tensor):
+    """Pooled 16-D key (normalised) and value of every 64-row block of ``P`` (``fp_param_blocks_16d``;
+    core.py:225-252, block_matmul.py:107-127).  Returns fp32 (k_blocks [N/64, 16], v_blocks [N/64, 16])."""
+    dev = require_cuda(P, k_proj, v_proj)
+    dtt = P.dtype
+    P, k_proj, v_proj = contig(P.detach()), contig(k_proj.detach().to(dtt)), contig(v_proj.detach().to(dtt))
+    N, D = P.shape
+    kb = torch.empty(N // 64, 16, dtype=torch.float32, device=dev)
+    vb = torch.empty(N // 64, 16, dtype=torch.float32, device=dev)
+    rc = _lib.load().fp_param_blocks_16d(ptr(P), ptr(k_proj), ptr(v_proj), dtype_code(dtt), N, D, ptr(kb), ptr(vb),
+                                         stream_handle(dev))
+    check(rc, "fp_param_blocks_16d")
+    return kb, vb
+
+
+def cosine_block_scores(x2d: torch.Tensor, q_proj: torch.Tensor, k_blocks: torch.Tensor,
+                        want_q16: bool = False) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """``normalize(rms_norm(x W_q^T)) . normalize(k_blocks)^T / 4`` (``fp_cosine_block_scores``;
+    core.py:214-223 then :254-266); fp32 [M, NB]."""
+    dev = require_cuda(x2d, q_proj, k_blocks)
+    x2d, q_proj = contig(x2d), contig(q_proj.detach().to(x2d.dtype))
+    k_blocks = contig(k_blocks.detach().float())
+    M, D = x2d.shape
+    NB = k_blocks.shape[0]
+    scores = torch.empty(M, NB, dtype=torch.float32, device=dev)
+    q16 = torch.empty(M, 16, dtype=torch.float32, device=dev) if want_q16 else None
+    rc = _lib.load().fp_cosine_block_scores(ptr(x2d), ptr(q_proj), ptr(k_blocks), dtype_code(x2d.dtype), M, D, NB,
+                                            ptr(scores), ptr(q16), stream_handle(dev))
+    check(rc, "fp_cosine_block_scores")
+    return scores, q16
+
+
+def select_remote_top_p(scores: torch.Tensor, *, base_blocks: int, top_p: float, max_remote: int,
+                        want_stats: bool = False):
+    """BlockSparseLinear's inference selection (``fp_select_remote_top_p``; block_matmul.py:185-201).
+    Returns (remote_indices [M, cap] int32 absolute ids, remote_counts [M] int32, stats [3] or None) with
+    cap = min(max_remote, NB - base) (at least 1)."""
+    dev = require_cuda(scores)
+    scores = contig(scores.float())
+    M, NB = scores.shape
+    cap = max(1, min(int(max_remote), NB - int(base_blocks)))
+    idx = torch.empty(M, cap, dtype=torch.int32, device=dev)
+    cnt = torch.empty(M, dtype=torch.int32, device=dev)
+    stats = torch.zeros(3, dtype=torch.float32, device=dev) if want_stats else None
+    rc = _lib.load().fp_select_remote_top_p(ptr(scores), M, NB, int(base_blocks), float(top_p), int(max_remote), cap,
+                                            ptr(idx), ptr(cnt), ptr(stats), stream_handle(dev))
+    check(rc, "fp_select_remote_top_p")
+    return idx, cnt, stats
+
+
+def union_blocks(remote_indices: torch.Tensor, remote_counts: torch.Tensor, num_blocks: int, base_blocks: int):
+    """Union of the selected blocks (``fp_union_blocks``): (blocks [NB] int32, n_active [1] int32), both on
+    the device; blocks[:n] are the selected ids ascending, blocks[n:] the others ascending."""
+    dev = require_cuda(remote_indices, remote_counts)
+    idx = contig(remote_indices.reshape(-1, remote_indices.shape[-1]).to(torch.int32))
+    cnt = contig(remote_counts.reshape(-1).to(torch.int32))
+    blocks = torch.empty(num_blocks, dtype=torch.int32, device=dev)
+    n_active = torch.empty(1, dtype=torch.int32, device=dev)
+    rc = _lib.load().fp_union_blocks(ptr(idx), ptr(cnt), cnt.numel(), idx.shape[1], int(num_blocks), int(base_blocks),
+                                     ptr(blocks), ptr(n_active), stream_handle(dev))
+    check(rc, "fp_union_blocks")
+    return blocks, n_active
+
+
+def block_sparse_linear(x2d: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], blocks: torch.Tensor,
+                        n_active: torch.Tensor, ctx16: Optional[torch.Tensor] = None,
+                        out_proj: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """BlockSparseLinear contraction over the union (``fp_block_sparse_linear_fwd``;
+    block_matmul.py:233-254): out [M, out_features] in x's dtype."""
+    dev = require_cuda(x2d, weight, blocks, n_active)
+    dtt = x2d.dtype
+    x2d, weight = contig(x2d), contig(weight.detach().to(dtt))
+    bias = contig(bias.detach().to(dtt)) if bias is not None else None
+    out_proj = contig(out_proj.detach().to(dtt)) if out_proj is not None else None
+    ctx16 = contig(ctx16.float()) if ctx16 is not None else None
+    M, D_in = x2d.shape
+    out_features = weight.shape[0]
+    out = torch.empty(M, out_features, dtype=dtt, device=dev)
+    ws = _lib.workspace(dev, 256)
+    rc = _lib.load().fp_block_sparse_linear_fwd(ptr(x2d), M, D_in, ptr(weight), ptr(bias), out_features,
+                                                dtype_code(dtt), ptr(blocks), ptr(n_active), ptr(ctx16), ptr(out_proj),
+                                                ptr(out), ptr(ws), ws.numel(), stream_handle(dev))
+    check(rc, "fp_block_sparse_linear_fwd")
+    return out
+
+
+ACTIVATIONS = {"softmax": 0, "gelu_l2": 1}
+
+
+def tokenformer(x2d: torch.Tensor, k_param: torch.Tensor, v_param: torch.Tensor, v_param_t: Optional[torch.Tensor],
+                activation: str, blocks: torch.Tensor, n_active: torch.Tensor, ctx16: Optional[torch.Tensor] = None,
+                out_proj: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Tokenformer contraction over the active parameter tokens (``fp_tokenformer_fwd``;
+    tokenformer.py:183-203): out [M, D_out] in x's dtype."""
+    dev = require_cuda(x2d, k_param, v_param, blocks, n_active)
+    dtt = x2d.dtype
+    x2d, k_param, v_param = contig(x2d), contig(k_param.detach().to(dtt)), contig(v_param.detach().to(dtt))
+    v_param_t = contig(v_param_t.detach().to(dtt)) if v_param_t is not None else None
+    out_proj = contig(out_proj.detach().to(dtt)) if out_proj is not None else None
+    ctx16 = contig(ctx16.float()) if ctx16 is not None else None
+    M, D_in = x2d.shape
+    Np, D_out = v_param.shape
+    out = torch.empty(M, D_out, dtype=dtt, device=dev)
+    lib = _lib.load()
+    ws = _lib.workspace(dev, lib.fp_tokenformer_workspace_size(dtype_code(dtt), M, Np))
+    rc = lib.fp_tokenformer_fwd(ptr(x2d), M, D_in, ptr(k_param), ptr(v_param), ptr(v_param_t), Np, D_out,
+                                dtype_code(dtt), ACTIVATIONS[activation], ptr(blocks), ptr(n_active), ptr(ctx16),
+                                ptr(out_proj), ptr(out), ptr(ws), ws.numel(), stream_handle(dev))
+    check(rc, "fp_tokenformer_fwd")
+    return out
+
+
+def transpose(t: torch.Tensor) -> torch.Tensor:
+    """``t.t().contiguous()`` by ``fp_transpose`` (2-D, fp32 or bf16)."""
+    dev = require_cuda(t)
+    t = contig(t.detach())
+    rows, cols = t.shape
+    out = torch.empty(cols, rows, dtype=t.dtype, device=dev)
+    check(_lib.load().fp_transpose(ptr(t), rows, cols, dtype_code(t.dtype), ptr(out), stream_handle(dev)),
+          "fp_transpose")
+    return out

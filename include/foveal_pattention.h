@@ -189,6 +189,92 @@ FP_API int fp_pattention_token_fwd_noalloc(const void* x, int64_t M, int D, int 
                                            int block_offset, void* y, int y_f32, int32_t* remote_indices,
                                            int32_t* remote_counts, float* scores, void* stream);
 
+/* ------------------------------------------------------------------------------------------------
+ * Layers that share the 16-D router but contract over the UNION of the blocks a call's tokens
+ * selected: BlockSparseLinear (foveal_indexer/block_matmul.py:129-282) and FovealTokenformerLinear
+ * (foveal_indexer/tokenformer.py:132-228).  A forward is: fp_param_blocks_16d (once per weight
+ * update) -> fp_cosine_block_scores -> fp_select_blocks (routes and/or the additive-stream context
+ * softmax(S) . v_blocks with temperature 1) or fp_select_remote_top_p -> fp_union_blocks ->
+ * fp_block_sparse_linear_fwd or fp_tokenformer_fwd.  The union count stays on the device: no call of
+ * the sequence synchronizes the host.
+ * ------------------------------------------------------------------------------------------------ */
+
+/*
+ * Pooled 16-D key and value of every 64-row block of a parameter matrix P [N, D] (N % 64 == 0):
+ *   k_blocks[b] = normalize(mean_{rows r of b} rms_norm(P[r] . k_proj^T))   fp32 [N / 64, 16]
+ *   v_blocks[b] = mean_{rows r of b} P[r] . v_proj^T                        fp32 [N / 64, 16]
+ * Replaces FovealIndexer.compute_kv_blocks_16d (core.py:225-252; Tokenformer's parameter keys,
+ * tokenformer.py:150-155) and BlockSparseLinear.get_block_keys_and_values (block_matmul.py:107-127).
+ * k_proj, v_proj [16, D] in `dtype`.
+ */
+FP_API int fp_param_blocks_16d(const void* P, const void* k_proj, const void* v_proj, int dtype, int64_t N, int D,
+                               float* k_blocks, float* v_blocks, void* stream);
+
+/*
+ * Cosine block scores (FovealIndexer.compute_query_16d core.py:214-223, then compute_block_scores
+ * core.py:254-266):  scores[m, b] = normalize(rms_norm(x[m] . q_proj^T)) . normalize(k_blocks[b]) / 4
+ * x [M, D], q_proj [16, D] in `dtype`; k_blocks [NB, 16] fp32; scores [M, NB] fp32; q16 (optional)
+ * [M, 16] fp32 receives rms_norm(x . q_proj^T).  D % 8 == 0, NB <= 1024.
+ */
+FP_API int fp_cosine_block_scores(const void* x, const void* q_proj, const float* k_blocks, int dtype, int64_t M,
+                                  int D, int NB, float* scores, float* q16, void* stream);
+
+/*
+ * BlockSparseLinear's inference selection (block_matmul.py:185-201): per token, softmax over the
+ * remote columns [base, NB) of scores [M, NB] only, and the first
+ * count = min(#(cumsum < top_p) + 1, max_remote) block ids by descending probability (ties to the
+ * lower id).  remote_indices [M, capacity] int32 receives absolute block ids; remote_counts [M] int32
+ * the count, which (as in the reference) may exceed the NB - base available blocks by one when the
+ * mass never reaches top_p; consumers read min(count, capacity) ids.  stats as in fp_select_blocks.
+ */
+FP_API int fp_select_remote_top_p(const float* scores, int64_t M, int NB, int base, float top_p, int max_remote,
+                                  int capacity, int32_t* remote_indices, int32_t* remote_counts, float* stats,
+                                  void* stream);
+
+/*
+ * Union of the selected blocks: blocks[0..n) = ascending ids of [0, base) and of every
+ * remote_indices[m, i] with i < min(remote_counts[m], capacity); blocks[n..NB) = the other ids
+ * ascending; *n_active = n (device int32).  block_matmul.py:206-217 (torch.where of the active mask),
+ * tokenformer.py:171-181 (torch.unique after the base blocks).  NB <= 8192.
+ */
+FP_API int fp_union_blocks(const int32_t* remote_indices, const int32_t* remote_counts, int64_t M, int capacity,
+                           int NB, int base, int32_t* blocks, int32_t* n_active, void* stream);
+
+/*
+ * BlockSparseLinear contraction (block_matmul.py:233-254):
+ *   out[m, c] = x[m] . weight[c] + bias[c] + ctx16[m] . out_proj[c]   for c in an active block
+ *   out[m, c] = ctx16[m] . out_proj[c]                                for c in an inactive block
+ * (the ctx16 terms only when ctx16 != NULL; otherwise inactive columns are 0).  x [M, D_in],
+ * weight [out_features, D_in], bias [out_features] (optional), out_proj [out_features, 16] and out
+ * [M, out_features] in `dtype`; blocks / n_active from fp_union_blocks; ctx16 [M, 16] fp32.
+ * out_features % 64 == 0.  bf16 with D_in % 64 == 0 runs on the tensor cores (tcgen05), everything
+ * else on CUDA cores.  Workspace: FP_VARIANT_WORKSPACE_MIN bytes (device error word).
+ */
+#define FP_VARIANT_WORKSPACE_MIN 256u
+FP_API int fp_block_sparse_linear_fwd(const void* x, int64_t M, int D_in, const void* weight, const void* bias,
+                                      int out_features, int dtype, const int32_t* blocks, const int32_t* n_active,
+                                      const float* ctx16, const void* out_proj, void* out, void* workspace,
+                                      size_t workspace_bytes, void* stream);
+
+/*
+ * FovealTokenformerLinear contraction over the active parameter tokens (tokenformer.py:183-203):
+ *   s = x . K_act^T,  p = softmax(s / sqrt(D_in)) (activation 0) or gelu(normalize(s)) (activation 1),
+ *   out = p . V_act + ctx16 . out_proj^T
+ * where K_act / V_act are the rows of k_param [Np, D_in] / v_param [Np, D_out] of the blocks
+ * blocks[0..n_active) in that order.  v_param_t [D_out, Np] = v_param transposed (fp_transpose; the
+ * tensor-core operand, may be NULL for fp32).  ctx16 optional.  bf16 with D_in % 64 == 0 and
+ * D_out % 64 == 0 runs on the tensor cores, everything else on CUDA cores.
+ */
+FP_API size_t fp_tokenformer_workspace_size(int dtype, int64_t M, int num_param_tokens);
+FP_API int fp_tokenformer_fwd(const void* x, int64_t M, int D_in, const void* k_param, const void* v_param,
+                              const void* v_param_t, int num_param_tokens, int D_out, int dtype, int activation,
+                              const int32_t* blocks, const int32_t* n_active, const float* ctx16,
+                              const void* out_proj, void* out, void* workspace, size_t workspace_bytes,
+                              void* stream);
+
+/* dst [cols, rows] = src [rows, cols] transposed, in `dtype`. */
+FP_API int fp_transpose(const void* src, int64_t rows, int64_t cols, int dtype, void* dst, void* stream);
+
 /*
  * Measurement hook (no counterpart in the reference): for the calling host thread, the forward entry
  * points record events[i] (cudaEvent_t handles) on their stream at stage boundaries:

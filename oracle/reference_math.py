@@ -38,6 +38,12 @@ __all__ = [
     "dense_swiglu",
     "teacher_block_energy",
     "calibrate_offline_svd",
+    "param_blocks_16d",
+    "cosine_block_scores",
+    "union_blocks",
+    "fast_remote_route",
+    "block_sparse_linear",
+    "tokenformer_linear",
 ]
 
 
@@ -336,3 +342,123 @@ def calibrate_offline_svd(x2d, w, *, base_blocks: int, remote_blocks: int, tempe
     info = {"top16_explained_variance": top_var / max(total_var, 1e-12), "initial_kl_divergence": kl,
             "calib_active_blocks": active, "scores": scores, "mean_scores": mean_scores, "teacher": teacher}
     return V16.T.contiguous(), block_keys, info
+
+
+# ------------------------------------------------------------------------------------------------
+# Variants sharing the router: BlockSparseLinear (block_matmul.py) and FovealTokenformerLinear
+# (tokenformer.py).  Both route every token with the 16-D indexer, take the UNION of the selected
+# blocks over the whole call, and run one dense contraction over that union.
+# ------------------------------------------------------------------------------------------------
+
+def param_blocks_16d(P: torch.Tensor, k_proj: torch.Tensor, v_proj: torch.Tensor, block_size: int = 64):
+    """Pooled 16-D key and value per block of ``block_size`` rows of ``P`` [N, D]:
+    ``k_b = normalize(mean_{rows of b} rms_norm(P W_k^T))``, ``v_b = mean_{rows of b} P W_v^T``.
+    FovealIndexer.compute_kv_blocks_16d (core.py:225-252) and BlockSparseLinear.get_block_keys_and_values
+    (block_matmul.py:107-127) are the same formula with different projection weights."""
+    n, d = P.shape
+    nb = n // block_size
+    k_elem = F.rms_norm(P @ k_proj.t(), (k_proj.shape[0],))
+    v_elem = P @ v_proj.t()
+    k_blocks = k_elem.view(nb, block_size, -1).mean(dim=1)
+    v_blocks = v_elem.view(nb, block_size, -1).mean(dim=1)
+    return F.normalize(k_blocks.float(), dim=-1), v_blocks
+
+
+def cosine_block_scores(x2d: torch.Tensor, q_proj: torch.Tensor, k_blocks: torch.Tensor) -> torch.Tensor:
+    """``normalize(rms_norm(x W_q^T)) . normalize(k_blocks)^T / sqrt(16)``: compute_query_16d
+    (core.py:214-223) followed by FovealIndexer.compute_block_scores (core.py:254-266)."""
+    q = F.rms_norm(x2d @ q_proj.t(), (q_proj.shape[0],))
+    qn = F.normalize(q.float(), dim=-1)
+    kn = F.normalize(k_blocks.float(), dim=-1)
+    return (qn @ kn.t()) / math.sqrt(q_proj.shape[0])
+
+
+def union_blocks(base: int, remote_indices: torch.Tensor, remote_counts: torch.Tensor, num_blocks: int,
+                 index_offset: int = 0) -> torch.Tensor:
+    """Ascending ids of ``[0, base)`` united with every token's selected remote blocks
+    (block_matmul.py:206-217 ``torch.where(active_block_mask)``; tokenformer.py:176-181
+    ``torch.unique`` after the base blocks)."""
+    mask = torch.zeros(num_blocks, dtype=torch.bool)
+    mask[:base] = True
+    cap = remote_indices.shape[-1]
+    idx = remote_indices.reshape(-1, cap).long() + index_offset
+    cnt = remote_counts.reshape(-1).long()
+    valid = torch.arange(cap).view(1, -1) < cnt.view(-1, 1)
+    sel = idx[valid]
+    sel = sel[sel >= base]
+    if sel.numel():
+        mask[sel] = True
+    return torch.where(mask)[0].to(torch.int32)
+
+
+def fast_remote_route(scores: torch.Tensor, base: int, top_p: float, max_remote: int):
+    """BlockSparseLinear's inference selection (block_matmul.py:185-201): softmax over the remote
+    columns only, ``needed = clamp(#(cumsum < top_p) + 1, 0, K_max)`` leading blocks by descending
+    probability (ties to the lower id).  This is select_blocks (core.py:46-160) on the remote columns
+    with no base blocks and K_min = 0, returned with block ids offset back by ``base``."""
+    rem = scores[:, base:]
+    n_rem = rem.shape[1]
+    r = select_blocks_noncausal(rem[None], local_window_blocks=0, top_p=top_p, min_remote_blocks=0,
+                                max_remote_blocks=max_remote, remote_capacity=min(max_remote, n_rem))
+    return r.remote_indices[0].long() + base, r.remote_counts[0]
+
+
+def block_sparse_linear(x2d, weight, bias, q_proj, weight_to_k, weight_to_v, out_proj, *, block_size: int,
+                        base_blocks: int, top_p: float, min_remote_blocks: int, max_remote_blocks: int,
+                        remote_capacity: int, fast_rule: bool, use_additive_stream: bool = True):
+    """BlockSparseLinear.forward (block_matmul.py:129-282) without the teacher loss.  ``fast_rule``:
+    the eval/no-grad selection (:185-201); otherwise FovealIndexer.route (:202-217).  Returns
+    ``(out [M, out_features], active ids, remote_indices, remote_counts, scores)``."""
+    nb = weight.shape[0] // block_size
+    base = min(base_blocks, nb)
+    k_blocks, v_blocks = param_blocks_16d(weight, weight_to_k, weight_to_v, block_size)   # :108-127
+    scores = cosine_block_scores(x2d, q_proj, k_blocks)                                    # :176
+    if fast_rule:
+        idx, cnt = fast_remote_route(scores, base, top_p, max_remote_blocks)
+        active = union_blocks(base, idx, cnt, nb)
+    else:
+        r = select_blocks_noncausal(scores[None], local_window_blocks=base, top_p=top_p,
+                                    min_remote_blocks=min_remote_blocks, max_remote_blocks=max_remote_blocks,
+                                    remote_capacity=remote_capacity)
+        idx, cnt = r.remote_indices[0], r.remote_counts[0]
+        active = union_blocks(base, idx, cnt, nb)
+    chan = (active.long().view(-1, 1) * block_size + torch.arange(block_size)).flatten()   # :234-236
+    out = torch.zeros(x2d.shape[0], weight.shape[0])
+    out[:, chan] = x2d @ weight[chan].t()                                                   # :238-243
+    if bias is not None:                                                                   # :245-247
+        out[:, chan] = out[:, chan] + bias[chan]
+    if use_additive_stream:                                                                # :250-254
+        probs = F.softmax(scores, dim=-1)
+        out = out + (probs @ v_blocks) @ out_proj.t()
+    return out, active, idx, cnt, scores
+
+
+def tokenformer_linear(x2d, k_param, v_param, q_proj, k_proj, v_proj, out_proj, *, block_size: int,
+                       base_blocks: int, top_p: float, min_remote_blocks: int, max_remote_blocks: int,
+                       remote_capacity: int, activation: str, use_additive_stream: bool = True):
+    """FovealTokenformerLinear.forward (tokenformer.py:132-228) without the teacher loss: route with
+    FovealIndexer.route (:163), union of the selected blocks (:171-181), then
+    ``act(x K_act^T) V_act`` with ``act`` = softmax(s / sqrt(D_in)) or gelu(normalize(s)) (:101-110),
+    plus the additive stream (:197-203).  Returns ``(out, active ids, remote_indices, remote_counts,
+    scores)``."""
+    nb = k_param.shape[0] // block_size
+    k_blocks, v_blocks = param_blocks_16d(k_param, k_proj, v_proj, block_size)             # :150-155
+    scores = cosine_block_scores(x2d, q_proj, k_blocks)                                    # :160
+    r = select_blocks_noncausal(scores[None], local_window_blocks=base_blocks, top_p=top_p,
+                                min_remote_blocks=min_remote_blocks, max_remote_blocks=max_remote_blocks,
+                                remote_capacity=remote_capacity)
+    idx, cnt = r.remote_indices[0], r.remote_counts[0]
+    active = union_blocks(base_blocks, idx, cnt, nb)
+    rows = (active.long().view(-1, 1) * block_size + torch.arange(block_size)).flatten()
+    raw = x2d @ k_param[rows].t()                                                          # :186
+    if activation == "softmax":
+        w = F.softmax(raw / math.sqrt(x2d.shape[1]), dim=-1)
+    elif activation == "gelu_l2":
+        w = F.gelu(F.normalize(raw, p=2, dim=-1))
+    else:
+        raise ValueError(activation)
+    out = w @ v_param[rows]                                                                 # :188
+    if use_additive_stream:
+        probs = F.softmax(scores, dim=-1)
+        out = out + (probs @ v_blocks) @ out_proj.t()
+    return out, active, idx, cnt, scores

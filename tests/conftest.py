@@ -119,3 +119,29 @@ def serve_model(cfgd: dict, dtype=torch.float32):
         for p_ in m.parameters():
             p_.copy_(p_.to(torch.bfloat16).float())
     return m.to(dtype)
+
+
+# ---------------------------------------------------------------- layers that share the router
+VARIANT_NAMES = list(configs.VARIANT_CASES)
+
+
+def variant_setup(name: str, dt: str = "fp32"):
+    """(case, seeded parameters keyed like the module's state_dict, x) of a parity case; the same values
+    the golden generator loaded into the reference's module."""
+    case = configs.VARIANT_CASES[name]
+    cls = {"bsl": fsi.BlockSparseLinear, "tf": fsi.FovealTokenformerLinear,
+           "ffn": fsi.FovealTokenformerFFN}[case["kind"]]
+    m = cls(**configs.variant_kwargs(case))
+    return case, configs.variant_params(m, 0, dt), configs.variant_x(case, 0, dt)
+
+
+def tf_kwargs(case: dict, layer: str = ""):
+    """Keyword arguments of one Tokenformer layer of a "tf" case or of layer "fc1" / "fc2" of an "ffn" case."""
+    if case["kind"] == "tf":
+        return {k: case[k] for k in ("in_features", "out_features", "base_blocks", "top_p", "min_remote_blocks",
+                                     "max_remote_blocks", "remote_capacity", "activation")}
+    h, i = case["hidden_size"], case["intermediate_size"]
+    return dict(in_features=h if layer == "fc1" else i, out_features=i if layer == "fc1" else h,
+                base_blocks=case["base_blocks"], top_p=case["top_p"], min_remote_blocks=0,
+                max_remote_blocks=case["max_remote_blocks"], remote_capacity=4,
+                activation="gelu_l2" if layer == "fc1" else "softmax")

@@ -208,6 +208,52 @@ def train_case(ref, seed):
     return out
 
 
+def variants_case(ref_root: str, seed: int):
+    """BlockSparseLinear, FovealTokenformerLinear and FovealTokenformerFFN of the reference (fp32 modules;
+    the "bf16" entries use bf16-rounded parameters and inputs): outputs in eval without autograd (the
+    BlockSparseLinear inference selection) and, for BlockSparseLinear, in training mode under no_grad
+    (FovealIndexer.route), with the aux figures, the routes and, for one case each, the distillation
+    loss."""
+    sys.path.insert(0, ref_root)
+    from foveal_indexer.block_matmul import BlockSparseLinear
+    from foveal_indexer.tokenformer import FovealTokenformerFFN, FovealTokenformerLinear
+    classes = {"bsl": BlockSparseLinear, "tf": FovealTokenformerLinear, "ffn": FovealTokenformerFFN}
+    arr = {}
+    for name, case in cfgmod.VARIANT_CASES.items():
+        for dt in ("fp32", "bf16"):
+            pre = f"{name}_{dt}_"
+            m = classes[case["kind"]](**cfgmod.variant_kwargs(case))
+            m.load_state_dict(cfgmod.variant_params(m, seed, dt))
+            x = cfgmod.variant_x(case, seed, dt)
+            m.eval()
+            with torch.no_grad():
+                y, aux = m(x, compute_teacher_loss=(dt == "fp32"))
+            arr[pre + "eval_out"] = y.numpy().astype(np.float32)
+            if dt == "fp32":
+                arr[pre + "distill"] = np.float32(aux["distill_loss"])
+            if case["kind"] == "bsl":
+                arr[pre + "eval_union"] = np.int32(aux["active_blocks_union"])
+                arr[pre + "eval_mean_active"] = np.float64(aux["mean_active_blocks"])
+                m.train()
+                with torch.no_grad():
+                    y, aux = m(x)
+                arr[pre + "train_out"] = y.numpy().astype(np.float32)
+                arr[pre + "train_union"] = np.int32(aux["active_blocks_union"])
+                arr[pre + "train_idx"] = aux["route"].remote_indices.numpy().astype(np.int32)
+                arr[pre + "train_cnt"] = aux["route"].remote_counts.numpy().astype(np.int32)
+            elif case["kind"] == "tf":
+                arr[pre + "eval_union"] = np.int32(aux["active_param_tokens_union"])
+                arr[pre + "eval_mean_active"] = np.float64(aux["mean_active_param_tokens"])
+                arr[pre + "eval_idx"] = aux["route"].remote_indices.numpy().astype(np.int32)
+                arr[pre + "eval_cnt"] = aux["route"].remote_counts.numpy().astype(np.int32)
+            else:
+                for f in ("fc1", "fc2"):
+                    a = aux[f + "_aux"]
+                    arr[pre + f + "_union"] = np.int32(a["active_param_tokens_union"])
+                    arr[pre + f + "_mean_active"] = np.float64(a["mean_active_param_tokens"])
+    return arr
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True)
@@ -219,7 +265,10 @@ def main():
     C = cfgmod.CONFIGS
     meta_common = {"seed": args.seed, "torch": torch.__version__}
     only = set(filter(None, args.only.split(",")))
-    if only and only <= {"calib", "serve", "train"}:
+    if only and only <= {"calib", "serve", "train", "variants"}:
+        if "variants" in only:
+            save("variants", {**meta_common, "config": "variants", "cases": cfgmod.VARIANT_CASES},
+                 variants_case(args.ref, args.seed))
         if "calib" in only:
             save("calib", {**meta_common, "config": "calib", **CALIB}, calib_case(ref, args.seed))
         if "serve" in only:
@@ -311,6 +360,10 @@ def main():
 
     # 9. Training-mode forward and backward (pooled routing, additive stream).
     save("train", {**meta_common, "config": "train"}, train_case(ref, args.seed))
+
+    # 10. Layers that share the router: BlockSparseLinear, FovealTokenformerLinear / FFN.
+    save("variants", {**meta_common, "config": "variants", "cases": cfgmod.VARIANT_CASES},
+         variants_case(args.ref, args.seed))
 
 
 if __name__ == "__main__":

@@ -125,7 +125,31 @@ def test_from_dense_mlp_shares_weights():
 def test_indexer_interface():
     idx = fsi.FovealIndexer(hidden_size=32, index_dim=16, block_size=16, local_window_blocks=1, top_p=0.9)
     assert idx.q_proj.weight.shape == (16, 32) and idx.out_proj.weight.shape == (32, 16)
-    with pytest.raises(NotImplementedError):
-        idx.distillation_loss(None, None)
+    with pytest.raises(NotImplementedError):  # the kernels pool 64-row blocks
+        idx.compute_kv_blocks_16d(torch.zeros(32, 32))
+    with pytest.raises(RuntimeError):  # no CPU fallback
+        idx.distillation_loss(torch.zeros(1, 2, 4), torch.ones(1, 2, 4))
     with pytest.raises(NotImplementedError):
         fsi.select_blocks(torch.zeros(1, 2, 4), causal=True)
+
+
+def test_variant_layers_interface():
+    """BlockSparseLinear / FovealTokenformerLinear / FovealTokenformerFFN: the reference's constructor
+    arguments, parameter shapes and init; CPU inputs raise instead of computing on the host."""
+    bsl = fsi.BlockSparseLinear(128, 256, base_blocks=2, bias=True)
+    assert bsl.weight.shape == (256, 128) and bsl.bias.shape == (256,) and bsl.num_blocks == 4
+    assert bsl.indexer.out_proj.weight.shape == (256, 16) and bsl.weight_to_k.weight.shape == (16, 128)
+    with pytest.raises(NotImplementedError):
+        fsi.BlockSparseLinear(128, 256, block_size=128)
+    with pytest.raises(ValueError):
+        fsi.BlockSparseLinear(128, 100)
+    tf = fsi.FovealTokenformerLinear(64, 96, num_param_tokens=256, activation="gelu_l2")
+    assert tf.k_param.shape == (256, 64) and tf.v_param.shape == (256, 96) and tf.num_blocks == 4
+    with pytest.raises(ValueError):
+        fsi.FovealTokenformerLinear(64, 96, num_param_tokens=100)
+    ffn = fsi.FovealTokenformerFFN(64, 128, num_param_tokens=256)
+    assert ffn.fc1.activation == "gelu_l2" and ffn.fc2.activation == "softmax"
+    with pytest.raises(RuntimeError):
+        bsl(torch.zeros(1, 3, 128))
+    with pytest.raises(RuntimeError):
+        tf(torch.zeros(1, 3, 64))
