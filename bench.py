@@ -25,6 +25,7 @@ import argparse
 import datetime
 import importlib
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -51,9 +52,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="8b", help="8b (default) or 70b for the main measurement")
-    ap.add_argument("--mode", choices=["default", "decode", "sweep", "blockshard"], default="default",
-                    help="decode / sweep print one JSON line per point instead of the bench line; blockshard "
-                         "(torchrun, >= 2 ranks) times the parameter-block-sharded forward of --config")
+    ap.add_argument("--mode", choices=["default", "decode", "sweep", "blockshard", "variants"], default="default",
+                    help="decode / sweep / variants print one JSON line per point instead of the bench line; "
+                         "blockshard (torchrun, >= 2 ranks) times the parameter-block-sharded forward of --config")
     ap.add_argument("--chunks", type=int, default=1, help="blockshard: token chunks whose reduce-scatter "
                     "overlaps the next chunk's compute")
     ap.add_argument("--e2e-steps", type=int, default=0)
@@ -454,6 +455,99 @@ def run_sweep(args):
                               "dense_ms_same_kernels": d_ours, "dense_ms_cublas": d_torch}), flush=True)
 
 
+def _variant_module(case, dev):
+    kind = case["kind"]
+    cls = {"bsl": fsi.BlockSparseLinear, "tf": fsi.FovealTokenformerLinear, "ffn": fsi.FovealTokenformerFFN}[kind]
+    m = cls(**configs.variant_kwargs(case))
+    m.load_state_dict(configs.variant_params(m, 0, "bf16"))
+    return m.to(dev, torch.bfloat16).eval()
+
+
+def run_variants(args):
+    """Layers that share the router (bf16, inference): BlockSparseLinear with the 8B MLP's up-projection
+    shape at 16384 / 64 / 1 tokens and a Tokenformer FFN at 16384 tokens.  Per point: the routed
+    forward (block keys cached; scores, selection, union, contraction; no host synchronisation) and the
+    contraction alone, both by CUDA events (median of 20), the union size, useful TFLOP/s (over the
+    union) against the measured bf16 peak, the dense equivalent through cuBLAS (torch) and the oracle
+    on the host cores for a 64-token sample."""
+    import oracle  # CPU baseline only
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peaks, src = load_peaks()
+    peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+    for name, token_counts in (("bsl_8b", (16384, 64, 1)), ("tf_ffn", (16384,))):
+        case = configs.VARIANT_BENCH[name]
+        m = _variant_module(case, dev)
+        x_all = configs.variant_x(case, 0, "bf16").reshape(-1, case["x_shape"][-1])
+        for M in token_counts:
+            x = x_all[:M].to(dev, torch.bfloat16).contiguous()
+            with torch.no_grad():
+                if case["kind"] == "bsl":
+                    r = m.forward_kernels(x, fast=True)
+                    n_act = int(r["n_active"].item())
+                    blocks, n_active, ctx16 = r["blocks"], r["n_active"], r["ctx16"]
+                    t_all = _time_calls(lambda: m.forward_kernels(x, fast=True), 20)
+                    t_mm = _time_calls(lambda: fsi.kernels.block_sparse_linear(
+                        x, m.weight, m.bias, blocks, n_active, ctx16, m.indexer.out_proj.weight), 20)
+                    flops = 2.0 * M * case["in_features"] * n_act * 64
+                    W = m.weight
+                    t_dense = _time_calls(lambda: torch.nn.functional.linear(x, W), 20)
+                    union = {"union_blocks": n_act, "total_blocks": m.num_blocks}
+                else:
+                    t_all = _time_calls(lambda: m.forward_kernels(x), 20)
+                    unions, flops = [], 0.0
+                    h = x
+                    for layer in (m.fc1, m.fc2):
+                        r = layer.forward_kernels(h)
+                        n_act = int(r["n_active"].item())
+                        unions.append(n_act)
+                        flops += 2.0 * M * n_act * 64 * (layer.in_features + layer.out_features)
+                        h = r["out"]
+                    t_mm = None
+                    kp1, vp1, kp2, vp2 = m.fc1.k_param, m.fc1.v_param, m.fc2.k_param, m.fc2.v_param
+
+                    def dense():
+                        a = torch.nn.functional.gelu(torch.nn.functional.normalize(x @ kp1.t(), dim=-1)) @ vp1
+                        return torch.softmax((a @ kp2.t()) / math.sqrt(m.fc2.in_features), dim=-1) @ vp2
+                    t_dense = _time_calls(dense, 20)
+                    union = {"union_blocks_fc1_fc2": unions, "total_blocks": m.fc1.num_blocks}
+            tm = t_all[len(t_all) // 2]
+            line = {"mode": "variants", "layer": name, "tokens": M, **union, "ms": tm,
+                    "tokens_per_s": M / (tm / 1e3), "useful_tflops": flops / (tm / 1e3) / 1e12,
+                    "tensor_peak_frac": flops / (tm / 1e3) / 1e12 / peak, "peak_tflops": peak, "peak_source": src,
+                    "dense_torch_cublas_ms": t_dense[len(t_dense) // 2]}
+            if t_mm is not None:
+                c = t_mm[len(t_mm) // 2]
+                line.update({"contraction_ms": c, "contraction_tflops": flops / (c / 1e3) / 1e12})
+            print(json.dumps(line), flush=True)
+        # CPU baseline: the oracle on a 64-token sample on the host cores
+        if not args.no_cpu_baseline:
+            xs = x_all[:64].float()
+            p = {k: v.detach().float().cpu() for k, v in m.state_dict().items()}
+            t0 = time.perf_counter()
+            if case["kind"] == "bsl":
+                oracle.block_sparse_linear(xs, p["weight"], p.get("bias"), p["indexer.q_proj.weight"],
+                                           p["weight_to_k.weight"], p["weight_to_v.weight"],
+                                           p["indexer.out_proj.weight"], block_size=64,
+                                           base_blocks=case["base_blocks"], top_p=case["top_p"], min_remote_blocks=0,
+                                           max_remote_blocks=case["max_remote_blocks"],
+                                           remote_capacity=case["remote_capacity"], fast_rule=True)
+            else:
+                h = xs
+                for f, act in (("fc1.", "gelu_l2"), ("fc2.", "softmax")):
+                    h = oracle.tokenformer_linear(h, p[f + "k_param"], p[f + "v_param"], p[f + "indexer.q_proj.weight"],
+                                                  p[f + "indexer.k_proj.weight"], p[f + "indexer.v_proj.weight"],
+                                                  p[f + "indexer.out_proj.weight"], block_size=64,
+                                                  base_blocks=case["base_blocks"], top_p=case["top_p"],
+                                                  min_remote_blocks=0, max_remote_blocks=case["max_remote_blocks"],
+                                                  remote_capacity=4, activation=act)[0]
+            dt = time.perf_counter() - t0
+            print(json.dumps({"mode": "variants", "layer": name, "cpu_baseline": {
+                "value": 64 / dt, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+                "sample": "64 tokens, oracle (fp32 torch CPU) incl. block keys"}}), flush=True)
+
+
 def run_blockshard(args):
     """Parameter-block sharding (strong scaling): every rank holds the same batch, computes the blocks
     b % world == rank, and the fp32 partials are reduce-scattered over token rows chunk by chunk (NCCL on
@@ -530,6 +624,8 @@ def main():
         run_sweep(args)
     elif args.mode == "blockshard":
         run_blockshard(args)
+    elif args.mode == "variants":
+        run_variants(args)
     else:
         run_ours(args)
 

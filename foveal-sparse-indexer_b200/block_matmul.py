@@ -110,15 +110,13 @@ class BlockSparseLinear(nn.Module):
         with torch.no_grad():
             self._cached_kp, self._cached_vp = self._blocks_16d()
 
-    def forward(self, x: Tensor, compute_teacher_loss: bool = False) -> Tuple[Tensor, Dict[str, Any]]:
-        orig_ndim = x.ndim
-        if orig_ndim == 2:
-            x = x.unsqueeze(1)
-        batch, seq_len, in_feat = x.shape
-        dev = x.device
-        x_in = x
-        x2d = x.reshape(-1, in_feat).to(self.weight.dtype)
+    def forward_kernels(self, x2d: Tensor, fast: bool, batch_shape=None) -> Dict[str, Any]:
+        """The routed forward of [M, in_features] tokens as one stream of kernel launches, without any host
+        synchronisation: ``fast`` selects the inference rule (block_matmul.py:185-201) instead of
+        FovealIndexer.route.  Returns the device tensors (out, scores, route or (idx, cnt, stats),
+        blocks, n_active, ctx16)."""
         M, NB, base = x2d.shape[0], self.num_blocks, self.base_blocks
+        dev = x2d.device
         # 1-2. block keys / values (cached in eval, :160-167) and the queries' cosine scores (:170-176)
         if not self.training and self._cached_kp is not None:
             kb, vb = self._cached_kp, self._cached_vp
@@ -128,27 +126,43 @@ class BlockSparseLinear(nn.Module):
                 self._cached_kp, self._cached_vp = kb, vb
         scores, _ = kernels.cosine_block_scores(x2d, self.indexer.q_proj.weight, kb)
         # 3-4. selection and union of the selected blocks
-        route = None
-        if not self.training and not torch.is_grad_enabled():
+        route, stats = None, None
+        if fast:
             if NB - base > 0:
                 idx, cnt, stats = kernels.select_remote_top_p(scores, base_blocks=base, top_p=self.indexer.top_p,
                                                               max_remote=self.indexer.max_remote_blocks,
                                                               want_stats=True)
-                mean_remote = float(stats[1].item()) / max(M, 1)
             else:
                 idx = torch.zeros(M, 1, dtype=torch.int32, device=dev)
                 cnt = torch.zeros(M, dtype=torch.int32, device=dev)
-                mean_remote = 0.0
         else:
-            route = self.indexer.route(scores.view(batch, seq_len, NB))
+            route = self.indexer.route(scores.view(*(batch_shape or (1, M)), NB))
             idx, cnt = route.remote_indices, route.remote_counts
-            mean_remote = float(route.mean_remote_blocks.item())
         blocks, n_active = kernels.union_blocks(idx, cnt, NB, base)
         # 5-6. contraction over the union (+ bias) with the additive stream in the epilogue
         ctx16 = additive_context(scores, vb) if self.use_additive_stream else None
         out2d = kernels.block_sparse_linear(x2d, self.weight, self.bias, blocks, n_active, ctx16,
                                             self.indexer.out_proj.weight)
-        out = out2d.view(batch, seq_len, self.out_features)
+        return {"out": out2d, "scores": scores, "route": route, "stats": stats, "blocks": blocks,
+                "n_active": n_active, "ctx16": ctx16}
+
+    def forward(self, x: Tensor, compute_teacher_loss: bool = False) -> Tuple[Tensor, Dict[str, Any]]:
+        orig_ndim = x.ndim
+        if orig_ndim == 2:
+            x = x.unsqueeze(1)
+        batch, seq_len, in_feat = x.shape
+        dev = x.device
+        x_in = x
+        x2d = x.reshape(-1, in_feat).to(self.weight.dtype)
+        M, NB, base = x2d.shape[0], self.num_blocks, self.base_blocks
+        fast = not self.training and not torch.is_grad_enabled()
+        r = self.forward_kernels(x2d, fast, (batch, seq_len))
+        route, scores, ctx16, n_active = r["route"], r["scores"], r["ctx16"], r["n_active"]
+        if route is not None:
+            mean_remote = float(route.mean_remote_blocks.item())
+        else:
+            mean_remote = float(r["stats"][1].item()) / max(M, 1) if r["stats"] is not None else 0.0
+        out = r["out"].view(batch, seq_len, self.out_features)
         additive_out = None
         if ctx16 is not None:
             # the additive term alone, for the aux dict (the output already contains it)

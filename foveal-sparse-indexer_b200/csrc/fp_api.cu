@@ -583,7 +583,7 @@ int fp_tokenformer_fwd(const void* x, int64_t M, int D_in, const void* k_param, 
     g1.y = S; g1.y_f32 = 1; g1.ksplit = 1; g1.err = err; g1.num_sms = sms;
     g1.nmap = blocks; g1.ncnt = n_active; g1.ldy = Np;
     FP_TRY(launch_down(g1, st));
-    FP_TRY(launch_rowact(S, Np, M, n_active, activation, div, P, Np, 0, st));
+    FP_TRY(launch_rowact(S, Np, M, n_active, activation, div, P, Np, 0, st, Np));
     DownArgs g2{};  // out = P[:, :64 n] . v_param[blocks] + ctx16 . out_proj^T
     g2.h = P; g2.v_t = v_param_t; g2.M = M; g2.D = D_out; g2.Np = Np; g2.K = Np; g2.stride = 1;
     g2.bmap = blocks; g2.kcnt = n_active;
@@ -598,7 +598,7 @@ int fp_tokenformer_fwd(const void* x, int64_t M, int D_in, const void* k_param, 
   g1.nmap = blocks; g1.ncnt = n_active;
   g1.y = S; g1.ldy = Np; g1.y_f32 = 1;
   FP_TRY(launch_mapped_gemm_simt(g1, st));
-  FP_TRY(launch_rowact(S, Np, M, n_active, activation, div, P, Np, 1, st));
+  FP_TRY(launch_rowact(S, Np, M, n_active, activation, div, P, Np, 1, st, Np));
   MappedGemm g2{};
   g2.a = P; g2.lda = Np; g2.a_f32 = 1;
   g2.b = v_param; g2.ldb = D_out; g2.b_f32 = f32; g2.nn = 1;

@@ -393,11 +393,10 @@ __device__ __forceinline__ void down_tile(int tile, int m_tiles, int n_tiles, in
 // the output.  Computed column c lands in Y column omap[c / 64] * 64 + c % 64 (block-mapped form) or c;
 // columns at or beyond `ncols` are not stored.
 __device__ __forceinline__ void down_store_chunk(const DownArgs& a, float (&o)[32], const float (&ctx)[16],
-                                                 int64_t row, bool row_ok, int col0, bool add, int split, int ks,
-                                                 int ncols) {
+                                                 int64_t row, bool row_ok, int col0, int ocol0, bool add, int split,
+                                                 int ks, int ncols) {
   const int lane = threadIdx.x & 31;
   if (col0 >= ncols) return;  // uniform over the warp
-  const int ocol0 = a.omap ? a.omap[col0 >> 6] * kBlock + (col0 & 63) : col0;
   if (a.ctx16 && add) {
     // o[i] += sum_k ctx[k] * W_out[ocol0 + i][k]; lane L loads row ocol0 + L of W_out and the warp
     // broadcasts it (all lanes of a chunk share the same 32 columns)
@@ -500,19 +499,26 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
         const int sp = tile % ks;
         const int kb0 = (int)((int64_t)sp * nkb_all / ks), kb1 = (int)((int64_t)(sp + 1) * nkb_all / ks);
         const int nv = a.nmap ? min(kTileN / kBlock, (ncols - n * kTileN) / kBlock) : 0;
+        int nb[kTileN / kBlock];  // V_t row block of each valid column block, read once per tile
+#pragma unroll
+        for (int i = 0; i < kTileN / kBlock; ++i) nb[i] = i < nv ? a.nmap[n * (kTileN / kBlock) + i] : 0;
+        // parameter block of the next k-block, loaded one iteration ahead so that the load's latency
+        // overlaps the wait for a free stage
+        int gb_next = kb0 < kb1 ? (a.bmap ? a.bmap[kb0] : kb0 * a.stride + a.offset) : 0;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int gb = gb_next;
+          if (kb + 1 < kb1) gb_next = a.bmap ? a.bmap[kb + 1] : (kb + 1) * a.stride + a.offset;
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1u;
           if (!mbar_wait(&bars->empty[s], ph ^ 1u, a.err, kErrWaitEmpty)) { ok = false; break; }
           uint8_t* As = smem + s * kStageBytes;
           uint8_t* Bs = As + kABytes;
-          const int gb = a.bmap ? a.bmap[kb] : kb * a.stride + a.offset;
           if (a.nmap) {
             mbar_arrive_expect_tx(&bars->full[s], kABytes + (uint32_t)nv * (kBlock * kTileK * 2));
             tma_load_2d(As, &tm_h, &bars->full[s], kb * kTileK, m * kTileM);
-            for (int i = 0; i < nv; ++i)
-              tma_load_2d(Bs + i * (kBlock * kTileK * 2), &tm_vt, &bars->full[s], gb * kBlock,
-                          a.nmap[n * (kTileN / kBlock) + i] * kBlock);
+#pragma unroll
+            for (int i = 0; i < kTileN / kBlock; ++i)
+              if (i < nv) tma_load_2d(Bs + i * (kBlock * kTileK * 2), &tm_vt, &bars->full[s], gb * kBlock, nb[i] * kBlock);
           } else {
             mbar_arrive_expect_tx(&bars->full[s], kStageBytes);
             tma_load_2d(As, &tm_h, &bars->full[s], kb * kTileK, m * kTileM);
@@ -575,6 +581,12 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
       tc_fence_after();
       const int64_t row = (int64_t)m * kTileM + 32 * q + lane;
       const bool row_ok = row < a.M;
+      // Y column of each of the tile's 4 column blocks (read once per tile)
+      const int jb = n * (kTileN / kBlock);
+      auto ocol_of = [&](int i) {
+        return (a.omap && (jb + i) * kBlock < ncols) ? a.omap[jb + i] * kBlock : (jb + i) * kBlock;
+      };
+      const int ocb0 = ocol_of(0), ocb1 = ocol_of(1), ocb2 = ocol_of(2), ocb3 = ocol_of(3);
       float ctx[16];
 #pragma unroll
       for (int k = 0; k < 16; ++k) ctx[k] = 0.f;
@@ -595,7 +607,8 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
 #pragma unroll
         for (int i = 0; i < 32; ++i) o[i] = kempty ? 0.f : __uint_as_float(v[i]);
         // the additive stream and the bias are added by one split only
-        down_store_chunk(a, o, ctx, row, row_ok, n * kTileN + c * 32, split == 0, split, ks, ncols);
+        const int col0 = n * kTileN + c * 32;
+        down_store_chunk(a, o, ctx, row, row_ok, col0, ((c >> 1) == 0 ? ocb0 : (c >> 1) == 1 ? ocb1 : (c >> 1) == 2 ? ocb2 : ocb3) + (col0 & 63), split == 0, split, ks, ncols);
       }
       tc_fence_before();
       __syncwarp();
@@ -622,7 +635,7 @@ static_assert(kPairSmem <= 227 * 1024, "pair down shared memory");
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
 down2_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CUtensorMap tm_vt,
-             const DownArgs a) {
+             const __grid_constant__ CUtensorMap tm_vt_wide, const DownArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = aligned_smem(smem_raw);
   PairBars* bars = reinterpret_cast<PairBars*>(smem + kPairStages * kPairStageBytes);
@@ -632,6 +645,7 @@ down2_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ C
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tm_h);
     tma_prefetch_desc(&tm_vt);
+    if (a.nmap) tma_prefetch_desc(&tm_vt_wide);
     for (int s = 0; s < kPairStages; ++s) {
       mbar_init(&bars->full[s], 1);   // leader: one expect_tx arrival + both CTAs' bytes
       mbar_init(&bars->empty[s], 1);  // arrival from the leader's commit
@@ -657,27 +671,54 @@ down2_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ C
   const int n_tiles = (a.D + kTileN - 1) / kTileN;
   const int tiles = m_pairs * n_tiles;
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-  const int nkb = a.K / kTileK;
+  // block-mapped form: both CTAs of a pair read the same device counts, so they skip the same tiles
+  int nkb = a.K / kTileK;
+  if (a.kcnt) nkb = max(0, min(nkb, *a.kcnt));
+  int ncols = a.D;
+  if (a.ncnt) ncols = max(0, min(a.D / kBlock, *a.ncnt)) * kBlock;
+  constexpr uint32_t kBoxBytes = kBlock * kTileK * 2;  // one 64-row box of V_t
   uint32_t issued = 0;
 
   if (warp == 0) {
-    // ---------------- producer (both CTAs): own rows of H, own half of the V_t tile
+    // ---------------- producer (both CTAs): own rows of H, own half of the V_t tile (block-mapped form:
+    // column blocks 2 * rank and 2 * rank + 1 of the tile, one 64-row box each)
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
       for (int tile = pair; tile < tiles && ok; tile += npairs) {
         int m, n;
         down_tile(tile, m_pairs, n_tiles, m, n);
+        if (n * kTileN >= ncols) continue;
+        const int nv = min(kTileN / kBlock, (ncols - n * kTileN) / kBlock);  // valid column blocks of the tile
+        // this CTA's column blocks 2 * rank, 2 * rank + 1 of the tile: V_t row blocks, read once per tile
+        const int j0 = n * (kTileN / kBlock) + 2 * (int)rank;
+        const int mine = a.nmap ? max(0, min(2, nv - 2 * (int)rank)) : 0;
+        const int b0 = mine > 0 ? a.nmap[j0] : 0;
+        const int b1 = mine > 1 ? a.nmap[j0 + 1] : 0;
+        const bool wide = mine == 2 && b1 == b0 + 1;  // consecutive blocks (the common case): one 128-row box
+        int gb_next = nkb > 0 ? (a.bmap ? a.bmap[0] : a.offset) : 0;  // one k-block ahead (see down_kernel)
         for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int gb = gb_next;
+          if (kb + 1 < nkb) gb_next = a.bmap ? a.bmap[kb + 1] : (kb + 1) * a.stride + a.offset;
           const int s = it % kPairStages;
           const uint32_t ph = (it / kPairStages) & 1u;
           if (!mbar_wait(&bars->empty[s], ph ^ 1u, a.err, kErrWaitEmpty)) { ok = false; break; }
           uint8_t* As = smem + s * kPairStageBytes;
           uint8_t* Bs = As + kPairABytes;
-          const int gb = a.bmap ? a.bmap[kb] : kb * a.stride + a.offset;
-          if (leader) mbar_arrive_expect_tx(&bars->full[s], 2 * kPairStageBytes);
-          tma_load_2d_pair(As, &tm_h, &bars->full[s], kb * kTileK, m * 2 * kTileM + (int)rank * kTileM);
-          tma_load_2d_pair(Bs, &tm_vt, &bars->full[s], gb * kBlock, n * kTileN + (int)rank * (kTileN / 2));
+          if (a.nmap) {
+            if (leader) mbar_arrive_expect_tx(&bars->full[s], 2 * kPairABytes + (uint32_t)nv * kBoxBytes);
+            tma_load_2d_pair(As, &tm_h, &bars->full[s], kb * kTileK, m * 2 * kTileM + (int)rank * kTileM);
+            if (wide) {
+              tma_load_2d_pair(Bs, &tm_vt_wide, &bars->full[s], gb * kBlock, b0 * kBlock);
+            } else {
+              if (mine > 0) tma_load_2d_pair(Bs, &tm_vt, &bars->full[s], gb * kBlock, b0 * kBlock);
+              if (mine > 1) tma_load_2d_pair(Bs + kBoxBytes, &tm_vt, &bars->full[s], gb * kBlock, b1 * kBlock);
+            }
+          } else {
+            if (leader) mbar_arrive_expect_tx(&bars->full[s], 2 * kPairStageBytes);
+            tma_load_2d_pair(As, &tm_h, &bars->full[s], kb * kTileK, m * 2 * kTileM + (int)rank * kTileM);
+            tma_load_2d_pair(Bs, &tm_vt, &bars->full[s], gb * kBlock, n * kTileN + (int)rank * (kTileN / 2));
+          }
         }
       }
       issued = it;
@@ -691,6 +732,9 @@ down2_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ C
       bool ok = true;
       const uint32_t idesc = umma_idesc_bf16(2 * kTileM, kTileN);
       for (int tile = pair; tile < tiles && ok; tile += npairs) {
+        int m, n;
+        down_tile(tile, m_pairs, n_tiles, m, n);
+        if (n * kTileN >= ncols) continue;
         const int acc = local & 1;
         const uint32_t aph = (local >> 1) & 1;
         if (!mbar_wait_cluster(&bars->acce[acc], aph ^ 1u, a.err, kErrWaitAccEmpty)) break;
@@ -725,12 +769,19 @@ down2_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ C
     for (int tile = pair; tile < tiles; tile += npairs) {
       int m, n;
       down_tile(tile, m_pairs, n_tiles, m, n);
+      if (n * kTileN >= ncols) continue;
       const int acc = local & 1;
       const uint32_t aph = (local >> 1) & 1;
       if (!warp_wait(&bars->accf[acc], aph, a.err, kErrWaitAccFull)) break;
       tc_fence_after();
       const int64_t row = (int64_t)m * 2 * kTileM + (int64_t)rank * kTileM + 32 * q + lane;
       const bool row_ok = row < a.M;
+      // Y column of each of the tile's 4 column blocks (read once per tile)
+      const int jb = n * (kTileN / kBlock);
+      auto ocol_of = [&](int i) {
+        return (a.omap && (jb + i) * kBlock < ncols) ? a.omap[jb + i] * kBlock : (jb + i) * kBlock;
+      };
+      const int ocb0 = ocol_of(0), ocb1 = ocol_of(1), ocb2 = ocol_of(2), ocb3 = ocol_of(3);
       float ctx[16];
 #pragma unroll
       for (int k = 0; k < 16; ++k) ctx[k] = 0.f;
@@ -749,8 +800,9 @@ down2_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ C
         tmem_ld_wait();
         float o[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = __uint_as_float(v[i]);
-        down_store_chunk(a, o, ctx, row, row_ok, n * kTileN + c * 32, true, 0, 1, a.D);
+        for (int i = 0; i < 32; ++i) o[i] = nkb > 0 ? __uint_as_float(v[i]) : 0.f;  // no k-block: zero
+        const int col0 = n * kTileN + c * 32;
+        down_store_chunk(a, o, ctx, row, row_ok, col0, ((c >> 1) == 0 ? ocb0 : (c >> 1) == 1 ? ocb1 : (c >> 1) == 2 ? ocb2 : ocb3) + (col0 & 63), true, 0, 1, ncols);
       }
       tc_fence_before();
       __syncwarp();
@@ -893,10 +945,13 @@ int launch_down(const DownArgs& a, cudaStream_t st) {
   static int attr = FP_OK;
   std::call_once(once, [] { attr = set_smem((const void*)down_kernel); });
   if (attr != FP_OK) return attr;
-  if (!mapped && ks == 1 && a.M >= 2 * kTileM && a.num_sms >= 2) {
-    // CTA pairs: 256 x 256 tiles, each CTA loading 128 rows of H and half of the V_t tile
-    CUtensorMap tv2;
-    if (!encode_map_2d(&tv2, a.v_t, a.Np, a.D, (uint64_t)a.Np * 2, kTileK, kTileN / 2)) return FP_ERR_CUDA;
+  if (ks == 1 && a.M >= 2 * kTileM && a.num_sms >= 2) {
+    // CTA pairs: 256 x 256 tiles, each CTA loading 128 rows of H and half of the V_t tile (two 64-row
+    // boxes in the block-mapped form)
+    CUtensorMap tv2, tvw;
+    if (!encode_map_2d(&tv2, a.v_t, a.Np, a.D, (uint64_t)a.Np * 2, kTileK, a.nmap ? kBlock : kTileN / 2) ||
+        !encode_map_2d(&tvw, a.v_t, a.Np, a.D, (uint64_t)a.Np * 2, kTileK, kTileN / 2))
+      return FP_ERR_CUDA;
     static std::once_flag once2;
     static int attr2 = FP_OK;
     std::call_once(once2, [] {
@@ -926,7 +981,7 @@ int launch_down(const DownArgs& a, cudaStream_t st) {
     if (max_pairs <= 0) return FP_ERR_CUDA;
     const int64_t ptiles = ((a.M + 2 * kTileM - 1) / (2 * kTileM)) * ((a.D + kTileN - 1) / kTileN);
     const int grid2 = 2 * (int)std::min<int64_t>(ptiles, std::min(max_pairs, a.num_sms / 2));
-    down2_kernel<<<grid2, kGemmThreads, kPairSmem, st>>>(th, tv2, a);
+    down2_kernel<<<grid2, kGemmThreads, kPairSmem, st>>>(th, tv2, tvw, a);
     return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
   }
   const int64_t tiles = ((a.M + kTileM - 1) / kTileM) * ((a.D + kTileN - 1) / kTileN) * ks;

@@ -172,10 +172,25 @@ __device__ __forceinline__ void ld32B(const __nv_bfloat16* p, uint32_t (&w)[8]) 
 __global__ void __launch_bounds__(kMmaWarps * 32)
 router_scores_mma_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ wq,
                          const __nv_bfloat16* __restrict__ k16, int64_t M, int D, int NB,
-                         float* __restrict__ scores, float* __restrict__ q16_out) {
+                         float* __restrict__ scores, float* __restrict__ q16_out, const float* __restrict__ kcos) {
   extern __shared__ float sk[];  // [16][NB] transposed block keys, then [kMmaWarps][16][17] partials
   float* sq = sk + 16 * NB;
-  for (int i = threadIdx.x; i < NB * 16; i += blockDim.x) sk[(i & 15) * NB + (i >> 4)] = __bfloat162float(k16[i]);
+  if (kcos) {
+    // cosine form: fp32 keys, L2-normalised (F.normalize: k / max(||k||, 1e-12))
+    for (int b = threadIdx.x; b < NB; b += blockDim.x) {
+      float kv[16], ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        kv[j] = kcos[b * 16 + j];
+        ss = fmaf(kv[j], kv[j], ss);
+      }
+      const float nrm = fmaxf(__fsqrt_rn(ss), 1e-12f);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) sk[j * NB + b] = __fdiv_rn(kv[j], nrm);
+    }
+  } else {
+    for (int i = threadIdx.x; i < NB * 16; i += blockDim.x) sk[(i & 15) * NB + (i >> 4)] = __bfloat162float(k16[i]);
+  }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int64_t tok0 = (int64_t)blockIdx.x * 16;
@@ -232,6 +247,14 @@ router_scores_mma_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat1
       qv[j] *= inv;
     }
     if (q16_out && lane < 16) q16_out[tok * 16 + lane] = qown * inv;
+    if (kcos) {  // normalize(rms_norm(q)) of compute_block_scores
+      float qq = 0.f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) qq = fmaf(qv[j], qv[j], qq);
+      const float nrm = fmaxf(__fsqrt_rn(qq), 1e-12f);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) qv[j] = __fdiv_rn(qv[j], nrm);
+    }
     for (int b = lane; b < NB; b += 32) {
       float sc = 0.f;
 #pragma unroll
@@ -537,11 +560,6 @@ __device__ __forceinline__ int select_token(float (&s)[E], int64_t tok, const Se
       if (counts < 0) counts = 0;
     }
     o.cnt[tok] = counts;
-    if (o.stats) {
-      atomicAdd(&o.stats[0], (o.k_max > 0 && counts >= o.k_max) ? 1.f : 0.f);
-      atomicAdd(&o.stats[1], (float)counts);
-      atomicAdd(&o.stats[2], counts == 0 ? 1.f : 0.f);
-    }
   }
   counts = __shfl_sync(0xffffffffu, counts, 0);
   return counts;
@@ -566,6 +584,10 @@ select_blocks_kernel(const float* __restrict__ scores, int64_t M, float temperat
     __syncthreads();
   }
   float* pbuf = pball + warp * N;
+  // statistics (capped tokens, sum of counts, base-only tokens): integers, summed per warp in registers,
+  // then per CTA, with one atomic per CTA and statistic
+  int st_cap = 0, st_zero = 0;
+  long long st_sum = 0;
   for (int64_t tok = (int64_t)blockIdx.x * kSelWarps + warp; tok < M; tok += (int64_t)gridDim.x * kSelWarps) {
     const float* srow = scores + tok * (o.ld > 0 ? o.ld : (int64_t)o.NB);
     float s[E];
@@ -579,8 +601,25 @@ select_blocks_kernel(const float* __restrict__ scores, int64_t M, float temperat
       }
       s[r] = v;
     }
-    select_token<E>(s, tok, o, pbuf, nullptr, skT, o.NB, lane);
+    const int c = select_token<E>(s, tok, o, pbuf, nullptr, skT, o.NB, lane);
+    st_cap += (o.k_max > 0 && c >= o.k_max) ? 1 : 0;
+    st_sum += c;
+    st_zero += c == 0 ? 1 : 0;
     __syncwarp();  // pbuf is rewritten by the next token of this warp
+  }
+  if (o.stats && o.idx) {
+    __shared__ long long red[kSelWarps][3];
+    if (lane == 0) {
+      red[warp][0] = st_cap;
+      red[warp][1] = st_sum;
+      red[warp][2] = st_zero;
+    }
+    __syncthreads();
+    if (threadIdx.x < 3) {
+      long long t = 0;
+      for (int w = 0; w < kSelWarps; ++w) t += red[w][threadIdx.x];
+      if (t) atomicAdd(&o.stats[threadIdx.x], (float)t);
+    }
   }
 }
 
@@ -1065,7 +1104,7 @@ int launch_router_scores(const void* x, const void* wq, const void* k16, int dty
                          int NB, float temperature, float* scores, float* q16, cudaStream_t st,
                          const float* kcos) {
   if (M <= 0) return FP_OK;
-  if (dtype == FP_DTYPE_BF16 && D % (64 * kMmaWarps) == 0 && temperature == 1.0f && !kcos) {
+  if (dtype == FP_DTYPE_BF16 && D % (64 * kMmaWarps) == 0 && temperature == 1.0f) {
     const size_t smem = (size_t)NB * 16 * sizeof(float) + kMmaWarps * 16 * 17 * sizeof(float);
     if (smem > 48 * 1024 &&
         cudaFuncSetAttribute(router_scores_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
@@ -1073,7 +1112,7 @@ int launch_router_scores(const void* x, const void* wq, const void* k16, int dty
       return FP_ERR_CUDA;
     const int blocks = (int)((M + 15) / 16);
     router_scores_mma_kernel<<<blocks, kMmaWarps * 32, smem, st>>>(
-        (const __nv_bfloat16*)x, (const __nv_bfloat16*)wq, (const __nv_bfloat16*)k16, M, D, NB, scores, q16);
+        (const __nv_bfloat16*)x, (const __nv_bfloat16*)wq, (const __nv_bfloat16*)k16, M, D, NB, scores, q16, kcos);
     return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
   }
   const int blocks = (int)((M + kScoreWarps * kScoreTPW - 1) / (kScoreWarps * kScoreTPW));

@@ -224,15 +224,86 @@ __global__ void __launch_bounds__(256) rowact_kernel(const float* __restrict__ S
   }
 }
 
+// Single-pass form for rows of at most 256 * EPT active columns: the row is read once into registers
+// (element i * 256 + thread of each thread), reduced, and written; same arithmetic as rowact_kernel.
+template <typename OutT, int EPT>
+__global__ void __launch_bounds__(256) rowact_reg_kernel(const float* __restrict__ S, int64_t lds,
+                                                         const int32_t* __restrict__ n_active, int mode, float div,
+                                                         OutT* __restrict__ P, int64_t ldp) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const int n = min(*n_active * 64, 256 * EPT);
+  const float* s = S + row * lds;
+  OutT* p = P + row * ldp;
+  float v[EPT];
+#pragma unroll
+  for (int i = 0; i < EPT; ++i) {
+    const int c = i * 256 + threadIdx.x;
+    v[i] = c < n ? s[c] : 0.f;
+  }
+  // The per-row divisors (sqrt(D_in), the exponential sum, the row norm) are applied as one reciprocal
+  // and a multiply per element (within one rounding of a division); the kernel is otherwise bound by
+  // the issue of IEEE divisions rather than by its memory traffic.
+  if (mode == 0) {
+    const float inv_div = __frcp_rn(div);
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < EPT; ++i) {
+      if (i * 256 + (int)threadIdx.x < n) {
+        v[i] *= inv_div;
+        mx = fmaxf(mx, v[i]);
+      }
+    }
+    mx = block_max(mx, red);
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < EPT; ++i) {
+      if (i * 256 + (int)threadIdx.x < n) {
+        v[i] = expf(v[i] - mx);
+        sum += v[i];
+      }
+    }
+    sum = block_sum(sum, red);
+    const float inv_sum = __frcp_rn(sum);
+#pragma unroll
+    for (int i = 0; i < EPT; ++i) {
+      const int c = i * 256 + threadIdx.x;
+      if (c < n) p[c] = (OutT)(v[i] * inv_sum);
+    }
+  } else {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < EPT; ++i) ss = fmaf(v[i], v[i], ss);  // zero beyond n
+    ss = block_sum(ss, red);
+    const float inv_nrm = __frcp_rn(fmaxf(__fsqrt_rn(ss), 1e-12f));
+#pragma unroll
+    for (int i = 0; i < EPT; ++i) {
+      const int c = i * 256 + threadIdx.x;
+      if (c < n) {
+        const float u = v[i] * inv_nrm;
+        p[c] = (OutT)(u * 0.5f * (1.0f + erff(u * 0.70710678118654752440f)));
+      }
+    }
+  }
+}
+
+// max_cols: an upper bound of 64 * n_active (the parameter-token count), known on the host.
 int launch_rowact(const float* S, int64_t lds, int64_t M, const int32_t* n_active, int mode, float div, void* P,
-                  int64_t ldp, int p_f32, cudaStream_t st) {
+                  int64_t ldp, int p_f32, cudaStream_t st, int max_cols) {
   if (M <= 0) return FP_OK;
   if (M > INT32_MAX) return FP_ERR_UNSUPPORTED;
-  if (p_f32)
-    rowact_kernel<float><<<(unsigned)M, 256, 0, st>>>(S, lds, n_active, mode, div, (float*)P, ldp);
-  else
-    rowact_kernel<__nv_bfloat16><<<(unsigned)M, 256, 0, st>>>(S, lds, n_active, mode, div, (__nv_bfloat16*)P, ldp);
-  return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+  auto go = [&](auto out_tag) -> int {
+    using OutT = decltype(out_tag);
+    OutT* Pt = static_cast<OutT*>(P);
+    const unsigned g = (unsigned)M;
+    if (max_cols <= 256 * 4) rowact_reg_kernel<OutT, 4><<<g, 256, 0, st>>>(S, lds, n_active, mode, div, Pt, ldp);
+    else if (max_cols <= 256 * 8) rowact_reg_kernel<OutT, 8><<<g, 256, 0, st>>>(S, lds, n_active, mode, div, Pt, ldp);
+    else if (max_cols <= 256 * 16) rowact_reg_kernel<OutT, 16><<<g, 256, 0, st>>>(S, lds, n_active, mode, div, Pt, ldp);
+    else if (max_cols <= 256 * 32) rowact_reg_kernel<OutT, 32><<<g, 256, 0, st>>>(S, lds, n_active, mode, div, Pt, ldp);
+    else rowact_kernel<OutT><<<g, 256, 0, st>>>(S, lds, n_active, mode, div, Pt, ldp);
+    return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+  };
+  return p_f32 ? go(float{}) : go(__nv_bfloat16{});
 }
 
 // ---------------------------------------------------------------- BlockSparseLinear inactive columns

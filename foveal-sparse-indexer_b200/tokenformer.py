@@ -98,11 +98,10 @@ class FovealTokenformerLinear(nn.Module):
         block_mass = attn.clamp_min(0.0).view(batch, seq_len, self.num_blocks, self.param_block_size).sum(dim=-1)
         return dense_out, block_mass
 
-    def forward(self, x: Tensor, compute_teacher_loss: bool = False) -> Tuple[Tensor, Dict[str, Any]]:
-        batch, seq_len, _ = x.shape
-        dev = x.device
-        x2d = x.reshape(-1, self.in_features).to(self.k_param.dtype)
-        NB, bs = self.num_blocks, self.param_block_size
+    def forward_kernels(self, x2d: Tensor, batch_shape=None) -> Dict[str, Any]:
+        """The routed forward of [M, in_features] tokens as one stream of kernel launches, without any host
+        synchronisation.  Returns the device tensors (out, scores, route, blocks, n_active, ctx16)."""
+        M, NB = x2d.shape[0], self.num_blocks
         # 1-3. block keys / values (cached in eval, :146-155), cosine scores (:160)
         if not self.training and self._cached_kp is not None:
             kb, vb = self._cached_kp, self._cached_vp
@@ -112,13 +111,22 @@ class FovealTokenformerLinear(nn.Module):
                 self._cached_kp, self._cached_vp = kb, vb
         scores, _ = kernels.cosine_block_scores(x2d, self.indexer.q_proj.weight, kb)
         # 4. route every token (:163), union of the selected blocks (:171-181)
-        route = self.indexer.route(scores.view(batch, seq_len, NB))
+        route = self.indexer.route(scores.view(*(batch_shape or (1, M)), NB))
         blocks, n_active = kernels.union_blocks(route.remote_indices, route.remote_counts, NB, self.base_blocks)
         # 5-6. act(x K_act^T) V_act with the additive stream in the epilogue (:183-203)
         ctx16 = additive_context(scores, vb) if self.use_additive_stream else None
         out2d = kernels.tokenformer(x2d, self.k_param, self.v_param, self._v_param_t(), self.activation, blocks,
                                     n_active, ctx16, self.indexer.out_proj.weight)
-        out = out2d.view(batch, seq_len, self.out_features)
+        return {"out": out2d, "scores": scores, "route": route, "blocks": blocks, "n_active": n_active, "ctx16": ctx16}
+
+    def forward(self, x: Tensor, compute_teacher_loss: bool = False) -> Tuple[Tensor, Dict[str, Any]]:
+        batch, seq_len, _ = x.shape
+        dev = x.device
+        x2d = x.reshape(-1, self.in_features).to(self.k_param.dtype)
+        NB, bs = self.num_blocks, self.param_block_size
+        r = self.forward_kernels(x2d, (batch, seq_len))
+        route, scores, ctx16, n_active = r["route"], r["scores"], r["ctx16"], r["n_active"]
+        out = r["out"].view(batch, seq_len, self.out_features)
         additive_out = None
         if ctx16 is not None:
             additive_out = (ctx16 @ self.indexer.out_proj.weight.detach().float().t()).to(out.dtype)
@@ -156,6 +164,12 @@ class FovealTokenformerFFN(nn.Module):
                                            num_param_tokens=num_param_tokens, param_block_size=param_block_size,
                                            base_blocks=base_blocks, index_dim=index_dim, top_p=top_p,
                                            max_remote_blocks=max_remote_blocks, activation="softmax")
+
+    def forward_kernels(self, x2d: Tensor) -> Tensor:
+        """Both layers as one stream of kernel launches without host synchronisation: [M, hidden] ->
+        [M, hidden]."""
+        h = self.fc1.forward_kernels(x2d)["out"]
+        return self.fc2.forward_kernels(h)["out"]
 
     def forward(self, x: Tensor, compute_teacher_loss: bool = False) -> Tuple[Tensor, Dict[str, Any]]:
         h, aux1 = self.fc1(x, compute_teacher_loss=compute_teacher_loss)
