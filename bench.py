@@ -494,6 +494,20 @@ def run_variants(args):
                     W = m.weight
                     t_dense = _time_calls(lambda: torch.nn.functional.linear(x, W), 20)
                     union = {"union_blocks": n_act, "total_blocks": m.num_blocks}
+                    if M <= 64:
+                        # decode-sized batches run from a CUDA graph (no host work per call)
+                        gs = torch.cuda.Stream(dev)
+                        gs.wait_stream(torch.cuda.current_stream(dev))
+                        with torch.cuda.stream(gs):
+                            for _ in range(3):
+                                m.forward_kernels(x, fast=True)
+                        torch.cuda.current_stream(dev).wait_stream(gs)
+                        graph = torch.cuda.CUDAGraph()
+                        with torch.cuda.graph(graph):
+                            m.forward_kernels(x, fast=True)
+                        tg = _time_calls(graph.replay, 50)
+                        union["graph_ms"] = tg[len(tg) // 2]
+                        del graph
                 else:
                     t_all = _time_calls(lambda: m.forward_kernels(x), 20)
                     unions, flops = [], 0.0
