@@ -141,21 +141,6 @@ int check_common(int dtype, int64_t M, int D, int NB) {
   return FP_OK;
 }
 
-template <typename T>
-__global__ void transpose_kernel(const T* __restrict__ in, int rows, int cols, T* __restrict__ out) {
-  __shared__ T tile[32][33];
-  const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
-  for (int i = threadIdx.y; i < 32; i += 8) {
-    const int r = r0 + i, c = c0 + threadIdx.x;
-    if (r < rows && c < cols) tile[i][threadIdx.x] = in[(int64_t)r * cols + c];
-  }
-  __syncthreads();
-  for (int i = threadIdx.y; i < 32; i += 8) {
-    const int c = c0 + i, r = r0 + threadIdx.x;
-    if (r < rows && c < cols) out[(int64_t)c * rows + r] = tile[threadIdx.x][i];
-  }
-}
-
 thread_local cudaEvent_t g_stage_events[8];
 thread_local int g_n_stage = 0;
 
@@ -261,9 +246,7 @@ int fp_pack_weights(const void* k_gate, const void* k_up, const void* v, int dty
   FP_TRY(device_info(sms));
   cudaStream_t st = (cudaStream_t)stream;
   FP_TRY(launch_pack_gate_up(k_gate, k_up, Np, D, w_gu, st));
-  dim3 grid((D + 31) / 32, (Np + 31) / 32), block(32, 8);
-  transpose_kernel<__nv_bfloat16><<<grid, block, 0, st>>>((const __nv_bfloat16*)v, Np, D, (__nv_bfloat16*)v_t);
-  return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+  return launch_transpose(v, Np, D, FP_DTYPE_BF16, v_t, st);  // v_t = v^T
 }
 
 int fp_pattention_token_fwd(const void* x, int64_t M, int D, int NB, int dtype, const void* k_gate,

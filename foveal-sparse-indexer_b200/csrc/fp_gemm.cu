@@ -7,6 +7,9 @@
 //             on CTA pairs (cta_group::2, 256-token tiles) from 256 tokens up, on one SM below
 //   energy:   the gate/up kernel with an fp32 |h| reduction per (token, block) instead of writing H
 //             (teacher block energies of the offline calibration)
+//   mapped:   the down kernels in a block-mapped form for the union contractions of BlockSparseLinear and
+//             the Tokenformer layers: B rows and Y columns through per-64-column block maps, tile and
+//             k-loop bounds from device counts, bias in the epilogue (DownArgs.nmap / omap / ncnt / kcnt)
 //
 // Reference semantics: foveal_indexer/foveal_pattention.py:329-335 (two projections, SwiGLU, V
 // projection over the active blocks), per-token form foveal_indexer/pattention_triton.py:280-311,

@@ -15,7 +15,8 @@
 //   mapped_gemm_simt   CUDA-core contraction over mapped 64-wide blocks, for fp32 layers (the 1e-4
 //                      tolerance of fp32 rules out bf16/tf32 tensor cores) and untileable shapes; the
 //                      bf16 tensor-core form is the block-mapped down kernel of fp_gemm.cu
-//   transpose          v_param -> v_param^T (K-major operand of the tensor-core contraction)
+//   transpose          v -> v_t (fp_pack_weights) and v_param -> v_param^T: the K-major operands of the
+//                      tensor-core contractions
 #include "fp_internal.cuh"
 
 #include <algorithm>
