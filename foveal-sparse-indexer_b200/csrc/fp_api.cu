@@ -246,7 +246,7 @@ int fp_pack_weights(const void* k_gate, const void* k_up, const void* v, int dty
   FP_TRY(device_info(sms));
   cudaStream_t st = (cudaStream_t)stream;
   FP_TRY(launch_pack_gate_up(k_gate, k_up, Np, D, w_gu, st));
-  return launch_transpose(v, Np, D, FP_DTYPE_BF16, v_t, st);  // v_t = v^T
+  return launch_pack_vt(v, Np, D, v_t, st);
 }
 
 int fp_pattention_token_fwd(const void* x, int64_t M, int D, int NB, int dtype, const void* k_gate,
@@ -324,7 +324,7 @@ int fp_pattention_token_fwd(const void* x, int64_t M, int D, int NB, int dtype, 
   FP_TRY(launch_gateup(g, st));
   stage_mark(3, st);
   DownArgs d{};
-  d.h = h; d.v_t = v_t; d.M = M; d.D = D; d.Np = NB * kBlock; d.K = nbl * kBlock; d.bmap = nullptr;
+  d.h = h; d.v_t = v_t; d.vt_tiled = 1; d.M = M; d.D = D; d.Np = NB * kBlock; d.K = nbl * kBlock; d.bmap = nullptr;
   d.stride = block_stride; d.offset = block_offset; d.ctx16 = ctx; d.out_proj = out_proj;
   d.out_proj_f32 = dtype == FP_DTYPE_F32; d.y = y; d.y_f32 = y_f32; d.err = err; d.num_sms = sms;
   d.ksplit = L.ksplit; d.y_acc = L.ksplit > 1 ? at<float>(workspace, L.yacc) : nullptr;
@@ -371,7 +371,7 @@ int fp_pattention_pooled_fwd(const void* x, int64_t M, int D, int NB, int dtype,
   FP_TRY(launch_gateup(g, st));
   stage_mark(1, st);
   DownArgs d{};
-  d.h = h; d.v_t = v_t; d.M = M; d.D = D; d.Np = NB * kBlock; d.K = n_active * kBlock; d.bmap = active;
+  d.h = h; d.v_t = v_t; d.vt_tiled = 1; d.M = M; d.D = D; d.Np = NB * kBlock; d.K = n_active * kBlock; d.bmap = active;
   d.stride = 1; d.offset = 0; d.ctx16 = ctx16; d.out_proj = out_proj; d.out_proj_f32 = dtype == FP_DTYPE_F32;
   d.y = y; d.y_f32 = y_f32; d.err = err; d.num_sms = sms;
   d.ksplit = L.ksplit; d.y_acc = L.ksplit > 1 ? at<float>(workspace, L.yacc) : nullptr;

@@ -225,7 +225,7 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
           if (!mbar_wait(&bars->empty[s], ph ^ 1u, a.err, kErrWaitEmpty)) { ok = false; break; }
           uint8_t* As = smem + s * kStage;
           mbar_arrive_expect_tx(&bars->full[s], kABytes + (gathered ? 0u : Cfg::kBBytes));
-          tma_load_2d(As, &tm_w, &bars->full[s], kb * kTileK, t.b * 2 * kBlock);
+          tma_load_2d(As, &tm_w, &bars->full[s], 0, (t.b * nkb + kb) * kTileM);
           if (!gathered) tma_load_2d(As + kABytes, &tm_x, &bars->full[s], kb * kTileK, (int)t.r0);
         }
       }
@@ -362,17 +362,51 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
 // Packed gate/up layout of one parameter block b (128 rows): rows 32q .. 32q+15 are gate channels
 // 16q .. 16q+15 and rows 32q+16 .. 32q+31 the up channels 16q .. 16q+15 (q = 0..3), so that after the
 // MMA (A = these rows) each 32-lane TMEM quarter holds the gate and up values of the same 16 channels.
+// Tile-contiguous: the 128 rows x 64 columns [kb*64, +64) of block b that one pipeline stage loads are
+// one contiguous 16 KB tile, tile index b * nkb + kb (nkb = D / 64), so every TMA box streams whole DRAM
+// pages instead of 128 bytes from each of 128 rows D * 2 bytes apart.
 __global__ void pack_gate_up_kernel(const uint4* __restrict__ kg, const uint4* __restrict__ ku, int64_t rows,
                                     int vec_per_row, uint4* __restrict__ wgu) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // over 2*rows*vec_per_row
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // over 2*rows*vec_per_row 16-byte words
   if (i >= 2 * rows * vec_per_row) return;
-  const int64_t orow = i / vec_per_row;
-  const int col = (int)(i % vec_per_row);
-  const int64_t b = orow / 128;
-  const int r = (int)(orow % 128);
+  const int nkb = vec_per_row / 8;       // 8 words = one 64-element row of a tile
+  const int c = (int)(i & 7);
+  const int r = (int)((i >> 3) & 127);   // packed row inside the block
+  const int64_t t = i >> 10;             // tile = b * nkb + kb
+  const int64_t b = t / nkb;
+  const int kb = (int)(t - b * nkb);
   const int q = r >> 5, w = r & 31;
   const int64_t src_row = b * 64 + 16 * q + (w & 15);
-  wgu[i] = (w < 16 ? kg : ku)[src_row * vec_per_row + col];
+  wgu[i] = (w < 16 ? kg : ku)[src_row * vec_per_row + kb * 8 + c];
+}
+
+// V^T in tile-contiguous form for the down projection: the 256 output columns [n*256, +256) x 64
+// parameter tokens of block gb that one stage loads are one contiguous 32 KB tile (rows = output columns,
+// 64 elements each), tile index n * NB + gb; columns past D are zero.  One CTA transposes one tile
+// through shared memory (v rows of 512 contiguous bytes in, 128-byte tile rows out).
+__global__ void __launch_bounds__(256) pack_vt_kernel(const __nv_bfloat16* __restrict__ v, int D, int NB,
+                                                      __nv_bfloat16* __restrict__ vt) {
+  __shared__ __nv_bfloat16 tile[64][kTileN + 8];
+  const int gb = blockIdx.x, n = blockIdx.y;
+  for (int e = threadIdx.x; e < 64 * (kTileN / 8); e += blockDim.x) {
+    const int p = e / (kTileN / 8), c8 = (e % (kTileN / 8)) * 8;
+    const int d = n * kTileN + c8;
+    const __nv_bfloat16* src = v + ((int64_t)gb * 64 + p) * D + d;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) tile[p][c8 + j] = d + j < D ? src[j] : __float2bfloat16_rn(0.f);
+  }
+  __syncthreads();
+  uint4* out = reinterpret_cast<uint4*>(vt + ((int64_t)n * NB + gb) * kTileN * 64);
+  for (int e = threadIdx.x; e < kTileN * 8; e += blockDim.x) {
+    const int r = e >> 3, p0 = (e & 7) * 8;
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const __nv_bfloat162 b2 = __halves2bfloat162(tile[p0 + 2 * j][r], tile[p0 + 2 * j + 1][r]);
+      w[j] = *reinterpret_cast<const uint32_t*>(&b2);
+    }
+    out[e] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
 }
 
 // ============================================================================================
@@ -525,7 +559,10 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
           } else {
             mbar_arrive_expect_tx(&bars->full[s], kStageBytes);
             tma_load_2d(As, &tm_h, &bars->full[s], kb * kTileK, m * kTileM);
-            tma_load_2d(Bs, &tm_vt, &bars->full[s], gb * kBlock, n * kTileN);
+            if (a.vt_tiled)  // tile (n, gb) of the tile-contiguous V^T
+              tma_load_2d(Bs, &tm_vt, &bars->full[s], 0, (n * (a.Np / kBlock) + gb) * kTileN);
+            else
+              tma_load_2d(Bs, &tm_vt, &bars->full[s], gb * kBlock, n * kTileN);
           }
         }
       }
@@ -720,7 +757,11 @@ down2_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ C
           } else {
             if (leader) mbar_arrive_expect_tx(&bars->full[s], 2 * kPairStageBytes);
             tma_load_2d_pair(As, &tm_h, &bars->full[s], kb * kTileK, m * 2 * kTileM + (int)rank * kTileM);
-            tma_load_2d_pair(Bs, &tm_vt, &bars->full[s], gb * kBlock, n * kTileN + (int)rank * (kTileN / 2));
+            if (a.vt_tiled)  // this CTA's half of tile (n, gb) of the tile-contiguous V^T
+              tma_load_2d_pair(Bs, &tm_vt, &bars->full[s], 0,
+                               (n * (a.Np / kBlock) + gb) * kTileN + (int)rank * (kTileN / 2));
+            else
+              tma_load_2d_pair(Bs, &tm_vt, &bars->full[s], gb * kBlock, n * kTileN + (int)rank * (kTileN / 2));
           }
         }
       }
@@ -881,8 +922,9 @@ static int set_smem(const void* fn) {
 template <class Cfg>
 static int launch_gateup_cfg(const GateUpArgs& a, cudaStream_t st) {
   CUtensorMap tx, tw;
+  // w_gu in tile-contiguous form: rows of 64 elements, tile (b, kb) = rows [(b * nkb + kb) * 128, +128)
   if (!encode_map_2d(&tx, a.x, a.D, a.M, (uint64_t)a.D * 2, kTileK, a.tiles ? 1 : Cfg::kN) ||
-      !encode_map_2d(&tw, a.w_gu, a.D, (uint64_t)a.Np * 2, (uint64_t)a.D * 2, kTileK, kTileM))
+      !encode_map_2d(&tw, a.w_gu, kTileK, (uint64_t)a.Np * 2 * (a.D / kTileK), kTileK * 2, kTileK, kTileM))
     return FP_ERR_CUDA;
   static std::once_flag once;
   static int attr = FP_OK;
@@ -936,13 +978,25 @@ int launch_pack_gate_up(const void* kg, const void* ku, int Np, int D, void* wgu
   return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
 }
 
+int launch_pack_vt(const void* v, int Np, int D, void* vt, cudaStream_t st) {
+  const int NB = Np / kBlock, ntiles = (D + kTileN - 1) / kTileN;
+  if (ntiles > 65535) return FP_ERR_UNSUPPORTED;
+  pack_vt_kernel<<<dim3((unsigned)NB, (unsigned)ntiles), 256, 0, st>>>((const __nv_bfloat16*)v, D, NB,
+                                                                        (__nv_bfloat16*)vt);
+  return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+}
+
 int launch_down(const DownArgs& a, cudaStream_t st) {
   const bool mapped = a.nmap || a.omap || a.ncnt || a.kcnt || a.bias || a.ldy > 0;
   const int ks = a.ksplit > 1 ? a.ksplit : 1;
   if (mapped && (ks != 1 || a.D % kBlock != 0)) return FP_ERR_INVALID_ARG;
+  if (a.vt_tiled && a.nmap) return FP_ERR_INVALID_ARG;
+  // tile-contiguous V^T: rows of 64 elements, ceil(D / 256) * (Np / 64) tiles of 256 rows
+  const uint64_t vt_rows = (uint64_t)((a.D + kTileN - 1) / kTileN) * (a.Np / kBlock) * kTileN;
   CUtensorMap th, tv;
   if (!encode_map_2d(&th, a.h, a.K, a.M, (uint64_t)a.K * 2, kTileK, kTileM) ||
-      !encode_map_2d(&tv, a.v_t, a.Np, a.D, (uint64_t)a.Np * 2, kTileK, a.nmap ? kBlock : kTileN))
+      !(a.vt_tiled ? encode_map_2d(&tv, a.v_t, kTileK, vt_rows, kTileK * 2, kTileK, kTileN)
+                   : encode_map_2d(&tv, a.v_t, a.Np, a.D, (uint64_t)a.Np * 2, kTileK, a.nmap ? kBlock : kTileN)))
     return FP_ERR_CUDA;
   static std::once_flag once;
   static int attr = FP_OK;
@@ -952,9 +1006,13 @@ int launch_down(const DownArgs& a, cudaStream_t st) {
     // CTA pairs: 256 x 256 tiles, each CTA loading 128 rows of H and half of the V_t tile (two 64-row
     // boxes in the block-mapped form)
     CUtensorMap tv2, tvw;
-    if (!encode_map_2d(&tv2, a.v_t, a.Np, a.D, (uint64_t)a.Np * 2, kTileK, a.nmap ? kBlock : kTileN / 2) ||
-        !encode_map_2d(&tvw, a.v_t, a.Np, a.D, (uint64_t)a.Np * 2, kTileK, kTileN / 2))
+    if (a.vt_tiled) {
+      if (!encode_map_2d(&tv2, a.v_t, kTileK, vt_rows, kTileK * 2, kTileK, kTileN / 2)) return FP_ERR_CUDA;
+      tvw = tv2;
+    } else if (!encode_map_2d(&tv2, a.v_t, a.Np, a.D, (uint64_t)a.Np * 2, kTileK, a.nmap ? kBlock : kTileN / 2) ||
+               !encode_map_2d(&tvw, a.v_t, a.Np, a.D, (uint64_t)a.Np * 2, kTileK, kTileN / 2)) {
       return FP_ERR_CUDA;
+    }
     static std::once_flag once2;
     static int attr2 = FP_OK;
     std::call_once(once2, [] {

@@ -90,7 +90,7 @@ int launch_route(const RouteArgs& a, int dtype, cudaStream_t st);
 // ---- gemm.cu (tensor-core path, bf16)
 struct GateUpArgs {
   const void* x;        // [M, D] bf16
-  const void* w_gu;     // [2 * Np, D] bf16, packed gate/up rows (launch_pack_gate_up)
+  const void* w_gu;     // [2 * Np, D] bf16, packed gate/up rows in tile-contiguous form (launch_pack_gate_up)
   int64_t M;
   int D, Np;
   // work list: explicit (tiles/meta from the routing kernel) or implicit (pooled: n_keys x ceil(M/256))
@@ -115,6 +115,8 @@ int launch_gateup(const GateUpArgs& a, cudaStream_t st);
 int launch_energy_combine(const float* part, int64_t M, int NB, const float* vnorm, float* E, cudaStream_t st);
 int launch_iota(int32_t* out, int n, cudaStream_t st);
 int launch_pack_gate_up(const void* kg, const void* ku, int Np, int D, void* wgu, cudaStream_t st);
+// V^T tile-contiguous: ceil(D / 256) * (Np / 64) tiles of 256 x 64 (bf16), tile (n, b) at index n * NB + b.
+int launch_pack_vt(const void* v, int Np, int D, void* vt, cudaStream_t st);
 
 // Rows per gate/up tile of a block-CSR key with `cnt` tokens: ceil(cnt / kGuN) tiles of equal size,
 // rounded up to the UMMA N granularity (16).
@@ -149,6 +151,7 @@ struct DownArgs {
   const void* bias = nullptr;     // optional per-Y-column bias (bf16, or fp32 per bias_f32)
   int bias_f32 = 0;
   int64_t ldy = 0;                // Y row stride in elements (0: D)
+  int vt_tiled = 0;               // v_t in the tile-contiguous form of launch_pack_vt (the MLP's packed V)
 };
 int launch_down(const DownArgs& a, cudaStream_t st);
 // Split-K factor used by the down projection for M tokens (1 = none).  Small batches (decode) have too

@@ -87,13 +87,14 @@ def pooled_route(x2d: Optional[torch.Tensor], q_proj: torch.Tensor, block_keys: 
 
 
 def pack_weights(k_gate: torch.Tensor, k_up: torch.Tensor, v: torch.Tensor):
-    """Derived tensor-core layouts (``fp_pack_weights``): packed gate/up rows w_gu [2 Np, D] and
-    V^T [D, Np].  bf16 only."""
+    """Derived tensor-core layouts (``fp_pack_weights``), both tile-contiguous: packed gate/up rows
+    (2 Np x D elements) and V^T (ceil(D / 256) * 256 x Np elements).  bf16 only; opaque buffers for the
+    forward entry points."""
     dev = require_cuda(k_gate, k_up, v)
     k_gate, k_up, v = contig(k_gate.detach()), contig(k_up.detach()), contig(v.detach())
     Np, D = v.shape
     w_gu = torch.empty(2 * Np, D, dtype=v.dtype, device=dev)
-    vt = torch.empty(D, Np, dtype=v.dtype, device=dev)
+    vt = torch.empty((D + 255) // 256 * 256, Np, dtype=v.dtype, device=dev)
     rc = _lib.load().fp_pack_weights(ptr(k_gate), ptr(k_up), ptr(v), dtype_code(v.dtype), Np, D, ptr(w_gu),
                                      ptr(vt), stream_handle(dev))
     check(rc, "fp_pack_weights")

@@ -96,10 +96,15 @@ FP_API int fp_pooled_route(const void* x, const void* q_proj, const void* block_
 
 /*
  * Weight layouts for the tensor-core path (bf16), derived from the reference parameters
- * (FovealPattentionMLP.k_gate / k_up / v, foveal_pattention.py:86-88; v stores W_down^T, :169):
- *   w_gu [2 * Np, D]: per parameter block b, 128 rows; rows 32q..32q+15 = k_gate channels 16q..16q+15
- *                     and rows 32q+16..32q+31 = k_up channels 16q..16q+15 of the block (q = 0..3)
- *   v_t  [D, Np]:     v transposed
+ * (FovealPattentionMLP.k_gate / k_up / v, foveal_pattention.py:86-88; v stores W_down^T, :169).  Both
+ * are tile-contiguous, so that each pipeline stage of the contraction kernels streams one contiguous
+ * tile:
+ *   w_gu (2 * Np * D elements): per parameter block b, 128 packed rows (rows 32q..32q+15 = k_gate
+ *        channels 16q..16q+15 and rows 32q+16..32q+31 = k_up channels 16q..16q+15 of the block, q = 0..3);
+ *        the 128 x 64 tile of columns [kb*64, +64) is contiguous at element offset (b * D/64 + kb) * 8192
+ *   v_t  (ceil(D / 256) * 256 * Np elements): v transposed in 256 x 64 tiles; the tile of output columns
+ *        [n*256, +256) and parameter tokens [b*64, +64) is contiguous (row = output column, 64 elements)
+ *        at element offset (n * Np/64 + b) * 16384; columns past D are zero
  * Call once per weight update.  Np % 64 == 0, D % 64 == 0.
  */
 FP_API int fp_pack_weights(const void* k_gate, const void* k_up, const void* v, int dtype, int Np, int D,
@@ -117,7 +122,7 @@ FP_API size_t fp_pooled_workspace_size(int dtype, int64_t M, int D, int NB, int 
  * composition compute_router_scores -> select_blocks(non-causal, base) -> per-token Pattention over
  * base ∪ selected (pattention_triton.py:280-311, "swiglu", block_n = 64) -> + out_proj_16d(softmax(S/T) K_16)
  * (foveal_pattention.py:257-262, core.py:46-160, foveal_pattention.py:338-342).
- *   x [M, D]; k_gate, k_up, v [Np, D] (Np = NB * 64); w_gu [2 Np, D] and v_t [D, Np] from
+ *   x [M, D]; k_gate, k_up, v [Np, D] (Np = NB * 64); w_gu and v_t (tile-contiguous) from
  *   fp_pack_weights (bf16 tensor-core path; may be NULL for fp32); q_proj [16, D]; block_keys [NB, 16];
  *   out_proj [D, 16]; all in `dtype`.
  *   additive: 1 adds the additive stream.
