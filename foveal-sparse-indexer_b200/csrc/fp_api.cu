@@ -524,8 +524,11 @@ TfLayout tf_layout(int dtype, int64_t M, int Np) {
   TfLayout L{};
   Carve c;
   c.take(FP_VARIANT_WORKSPACE_MIN);  // device error word
+  // scores and activation weights: bf16 on the tensor-core path, fp32 on the CUDA-core path (which bf16
+  // layers also take for shapes the tensor path does not tile), so 4 bytes per element cover both
+  (void)dtype;
   L.s = c.take((size_t)M * Np * 4);
-  L.p = c.take((size_t)M * Np * (dtype == FP_DTYPE_BF16 ? 2 : 4));
+  L.p = c.take((size_t)M * Np * 4);
   L.total = c.off;
   return L;
 }
@@ -553,7 +556,7 @@ int fp_tokenformer_fwd(const void* x, int64_t M, int D_in, const void* k_param, 
   if (M == 0) return FP_OK;
   char* ws = static_cast<char*>(workspace);
   int* err = reinterpret_cast<int*>(ws);
-  float* S = reinterpret_cast<float*>(ws + L.s);
+  void* S = ws + L.s;
   void* P = ws + L.p;
   if (cudaMemsetAsync(workspace, 0, FP_VARIANT_WORKSPACE_MIN, st) != cudaSuccess) return FP_ERR_CUDA;
   const int f32 = dtype == FP_DTYPE_F32;
@@ -563,10 +566,10 @@ int fp_tokenformer_fwd(const void* x, int64_t M, int D_in, const void* k_param, 
   if (tc) {
     DownArgs g1{};  // S[:, j*64 + c] = x . k_param[blocks[j]*64 + c]
     g1.h = x; g1.v_t = k_param; g1.M = M; g1.D = Np; g1.Np = D_in; g1.K = D_in; g1.stride = 1;
-    g1.y = S; g1.y_f32 = 1; g1.ksplit = 1; g1.err = err; g1.num_sms = sms;
+    g1.y = S; g1.y_f32 = 0; g1.ksplit = 1; g1.err = err; g1.num_sms = sms;  // bf16 scores
     g1.nmap = blocks; g1.ncnt = n_active; g1.ldy = Np;
     FP_TRY(launch_down(g1, st));
-    FP_TRY(launch_rowact(S, Np, M, n_active, activation, div, P, Np, 0, st, Np));
+    FP_TRY(launch_rowact(S, 1, Np, M, n_active, activation, div, P, Np, 0, st, Np));
     DownArgs g2{};  // out = P[:, :64 n] . v_param[blocks] + ctx16 . out_proj^T
     g2.h = P; g2.v_t = v_param_t; g2.M = M; g2.D = D_out; g2.Np = Np; g2.K = Np; g2.stride = 1;
     g2.bmap = blocks; g2.kcnt = n_active;
@@ -581,7 +584,7 @@ int fp_tokenformer_fwd(const void* x, int64_t M, int D_in, const void* k_param, 
   g1.nmap = blocks; g1.ncnt = n_active;
   g1.y = S; g1.ldy = Np; g1.y_f32 = 1;
   FP_TRY(launch_mapped_gemm_simt(g1, st));
-  FP_TRY(launch_rowact(S, Np, M, n_active, activation, div, P, Np, 1, st, Np));
+  FP_TRY(launch_rowact(S, 0, Np, M, n_active, activation, div, P, Np, 1, st, Np));
   MappedGemm g2{};
   g2.a = P; g2.lda = Np; g2.a_f32 = 1;
   g2.b = v_param; g2.ldb = D_out; g2.b_f32 = f32; g2.nn = 1;

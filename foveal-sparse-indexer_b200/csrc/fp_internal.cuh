@@ -188,8 +188,8 @@ int launch_param_blocks_16d(const void* P, const void* wk, const void* wv, int d
                             float* kb, float* vb, cudaStream_t st);
 int launch_union(const int32_t* idx, const int32_t* cnt, int64_t M, int capacity, int NB, int base,
                  int32_t* active, int32_t* n_active, cudaStream_t st);
-int launch_rowact(const float* S, int64_t lds, int64_t M, const int32_t* n_active, int mode, float div, void* P,
-                  int64_t ldp, int p_f32, cudaStream_t st, int max_cols);
+int launch_rowact(const void* S, int s_bf16, int64_t lds, int64_t M, const int32_t* n_active, int mode, float div,
+                  void* P, int64_t ldp, int p_f32, cudaStream_t st, int max_cols);
 int launch_fill_inactive(const int32_t* blocks, const int32_t* n_active, int NB, int64_t M, const float* ctx16,
                          const void* out_proj, int dtype, void* out, int64_t ldo, int num_sms, cudaStream_t st);
 int launch_transpose(const void* src, int64_t rows, int64_t cols, int dtype, void* dst, cudaStream_t st);

@@ -193,33 +193,36 @@ int launch_union(const int32_t* idx, const int32_t* cnt, int64_t M, int capacity
 // Row m of S [M, lds] (fp32 raw scores x . k_param^T of the active parameter tokens, in union order)
 // -> P [M, ldp] over the first 64 * n_active columns.  mode 0: softmax(s / div); mode 1:
 // gelu(s / max(||s||_2, 1e-12)) with the exact (erf) GELU.
-template <typename OutT>
-__global__ void __launch_bounds__(256) rowact_kernel(const float* __restrict__ S, int64_t lds,
+__device__ __forceinline__ float ld_score(const float* p, int c) { return p[c]; }
+__device__ __forceinline__ float ld_score(const __nv_bfloat16* p, int c) { return __bfloat162float(p[c]); }
+
+template <typename InT, typename OutT>
+__global__ void __launch_bounds__(256) rowact_kernel(const InT* __restrict__ S, int64_t lds,
                                                      const int32_t* __restrict__ n_active, int mode, float div,
                                                      OutT* __restrict__ P, int64_t ldp) {
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const int n = *n_active * 64;
-  const float* s = S + row * lds;
+  const InT* s = S + row * lds;
   OutT* p = P + row * ldp;
   if (mode == 0) {
     float mx = -INFINITY;
-    for (int c = threadIdx.x; c < n; c += blockDim.x) mx = fmaxf(mx, __fdiv_rn(s[c], div));
+    for (int c = threadIdx.x; c < n; c += blockDim.x) mx = fmaxf(mx, __fdiv_rn(ld_score(s, c), div));
     mx = block_max(mx, red);
     float sum = 0.f;
-    for (int c = threadIdx.x; c < n; c += blockDim.x) sum += expf(__fdiv_rn(s[c], div) - mx);
+    for (int c = threadIdx.x; c < n; c += blockDim.x) sum += expf(__fdiv_rn(ld_score(s, c), div) - mx);
     sum = block_sum(sum, red);
     for (int c = threadIdx.x; c < n; c += blockDim.x) {
-      const float v = __fdiv_rn(expf(__fdiv_rn(s[c], div) - mx), sum);
+      const float v = __fdiv_rn(expf(__fdiv_rn(ld_score(s, c), div) - mx), sum);
       p[c] = (OutT)v;
     }
   } else {
     float ss = 0.f;
-    for (int c = threadIdx.x; c < n; c += blockDim.x) ss = fmaf(s[c], s[c], ss);
+    for (int c = threadIdx.x; c < n; c += blockDim.x) ss = fmaf(ld_score(s, c), ld_score(s, c), ss);
     ss = block_sum(ss, red);
     const float nrm = fmaxf(__fsqrt_rn(ss), 1e-12f);
     for (int c = threadIdx.x; c < n; c += blockDim.x) {
-      const float u = __fdiv_rn(s[c], nrm);
+      const float u = __fdiv_rn(ld_score(s, c), nrm);
       p[c] = (OutT)(u * 0.5f * (1.0f + erff(u * 0.70710678118654752440f)));
     }
   }
@@ -227,20 +230,20 @@ __global__ void __launch_bounds__(256) rowact_kernel(const float* __restrict__ S
 
 // Single-pass form for rows of at most 256 * EPT active columns: the row is read once into registers
 // (element i * 256 + thread of each thread), reduced, and written; same arithmetic as rowact_kernel.
-template <typename OutT, int EPT>
-__global__ void __launch_bounds__(256) rowact_reg_kernel(const float* __restrict__ S, int64_t lds,
+template <typename InT, typename OutT, int EPT>
+__global__ void __launch_bounds__(256) rowact_reg_kernel(const InT* __restrict__ S, int64_t lds,
                                                          const int32_t* __restrict__ n_active, int mode, float div,
                                                          OutT* __restrict__ P, int64_t ldp) {
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const int n = min(*n_active * 64, 256 * EPT);
-  const float* s = S + row * lds;
+  const InT* s = S + row * lds;
   OutT* p = P + row * ldp;
   float v[EPT];
 #pragma unroll
   for (int i = 0; i < EPT; ++i) {
     const int c = i * 256 + threadIdx.x;
-    v[i] = c < n ? s[c] : 0.f;
+    v[i] = c < n ? ld_score(s, c) : 0.f;
   }
   // The per-row divisors (sqrt(D_in), the exponential sum, the row norm) are applied as one reciprocal
   // and a multiply per element (within one rounding of a division); the kernel is otherwise bound by
@@ -288,23 +291,28 @@ __global__ void __launch_bounds__(256) rowact_reg_kernel(const float* __restrict
   }
 }
 
-// max_cols: an upper bound of 64 * n_active (the parameter-token count), known on the host.
-int launch_rowact(const float* S, int64_t lds, int64_t M, const int32_t* n_active, int mode, float div, void* P,
-                  int64_t ldp, int p_f32, cudaStream_t st, int max_cols) {
+// max_cols: an upper bound of 64 * n_active (the parameter-token count), known on the host.  S is fp32, or
+// bf16 (s_bf16) on the tensor-core path, where the scores are rounded to bf16 as the reference's bf16
+// layer rounds its raw scores.
+int launch_rowact(const void* S, int s_bf16, int64_t lds, int64_t M, const int32_t* n_active, int mode, float div,
+                  void* P, int64_t ldp, int p_f32, cudaStream_t st, int max_cols) {
   if (M <= 0) return FP_OK;
   if (M > INT32_MAX) return FP_ERR_UNSUPPORTED;
-  auto go = [&](auto out_tag) -> int {
+  auto go = [&](auto in_tag, auto out_tag) -> int {
+    using InT = decltype(in_tag);
     using OutT = decltype(out_tag);
+    const InT* St = static_cast<const InT*>(S);
     OutT* Pt = static_cast<OutT*>(P);
     const unsigned g = (unsigned)M;
-    if (max_cols <= 256 * 4) rowact_reg_kernel<OutT, 4><<<g, 256, 0, st>>>(S, lds, n_active, mode, div, Pt, ldp);
-    else if (max_cols <= 256 * 8) rowact_reg_kernel<OutT, 8><<<g, 256, 0, st>>>(S, lds, n_active, mode, div, Pt, ldp);
-    else if (max_cols <= 256 * 16) rowact_reg_kernel<OutT, 16><<<g, 256, 0, st>>>(S, lds, n_active, mode, div, Pt, ldp);
-    else if (max_cols <= 256 * 32) rowact_reg_kernel<OutT, 32><<<g, 256, 0, st>>>(S, lds, n_active, mode, div, Pt, ldp);
-    else rowact_kernel<OutT><<<g, 256, 0, st>>>(S, lds, n_active, mode, div, Pt, ldp);
+    if (max_cols <= 256 * 4) rowact_reg_kernel<InT, OutT, 4><<<g, 256, 0, st>>>(St, lds, n_active, mode, div, Pt, ldp);
+    else if (max_cols <= 256 * 8) rowact_reg_kernel<InT, OutT, 8><<<g, 256, 0, st>>>(St, lds, n_active, mode, div, Pt, ldp);
+    else if (max_cols <= 256 * 16) rowact_reg_kernel<InT, OutT, 16><<<g, 256, 0, st>>>(St, lds, n_active, mode, div, Pt, ldp);
+    else if (max_cols <= 256 * 32) rowact_reg_kernel<InT, OutT, 32><<<g, 256, 0, st>>>(St, lds, n_active, mode, div, Pt, ldp);
+    else rowact_kernel<InT, OutT><<<g, 256, 0, st>>>(St, lds, n_active, mode, div, Pt, ldp);
     return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
   };
-  return p_f32 ? go(float{}) : go(__nv_bfloat16{});
+  if (s_bf16) return p_f32 ? go(__nv_bfloat16{}, float{}) : go(__nv_bfloat16{}, __nv_bfloat16{});
+  return p_f32 ? go(float{}, float{}) : go(float{}, __nv_bfloat16{});
 }
 
 // ---------------------------------------------------------------- BlockSparseLinear inactive columns

@@ -253,3 +253,44 @@ def test_backward_raises():
     y, _ = m(torch.randn(1, 4, 64, device=DEV))
     with pytest.raises(NotImplementedError):
         y.sum().backward()
+
+
+@pytest.mark.parametrize("activation", ["softmax", "gelu_l2"])
+def test_bf16_cuda_core_fallback(activation):
+    """bf16 layers whose widths the tensor-core path does not tile (D_in % 64 != 0) run on CUDA cores with
+    fp32 scores in the workspace; same parity bar."""
+    g = torch.Generator().manual_seed(11)
+    M, D_in, D_out, Np = 37, 136, 200, 512
+    x = torch.randn(M, D_in, generator=g)
+    kp = torch.randn(Np, D_in, generator=g) * D_in ** -0.5
+    vp = torch.randn(Np, D_out, generator=g) * D_out ** -0.5
+    wq, wk, wv = (torch.randn(16, D_in, generator=g) * D_in ** -0.5 for _ in range(3))
+    wo = torch.randn(D_out, 16, generator=g) * 0.05
+    x, kp, vp, wq, wk, wv, wo = (t.to(torch.bfloat16).float() for t in (x, kp, vp, wq, wk, wv, wo))
+    ref, active, _, _, _ = oracle.tokenformer_linear(x, kp, vp, wq, wk, wv, wo, block_size=64, base_blocks=1, top_p=0.9,
+                                                     min_remote_blocks=0, max_remote_blocks=3, remote_capacity=3,
+                                                     activation=activation)
+    m = fsi.FovealTokenformerLinear(D_in, D_out, num_param_tokens=Np, base_blocks=1, top_p=0.9, max_remote_blocks=3,
+                                    remote_capacity=3, activation=activation)
+    m.load_state_dict({"k_param": kp, "v_param": vp, "indexer.q_proj.weight": wq, "indexer.k_proj.weight": wk,
+                       "indexer.v_proj.weight": wv, "indexer.out_proj.weight": wo})
+    m = m.to(DEV, torch.bfloat16).eval()
+    with torch.no_grad():
+        y, aux = m(x.to(DEV, torch.bfloat16).unsqueeze(0))
+    assert aux["active_param_tokens_union"] == active.numel() * 64
+    assert rel_err(y[0].float().cpu(), ref) < 2e-2
+    # BlockSparseLinear with the same odd input width
+    W = (torch.randn(Np, D_in, generator=g) * D_in ** -0.5).to(torch.bfloat16).float()
+    wo_b = (torch.randn(Np, 16, generator=g) * 0.05).to(torch.bfloat16).float()
+    ref_b, active_b, _, _, _ = oracle.block_sparse_linear(x, W, None, wq, wk, wv, wo_b, block_size=64, base_blocks=1,
+                                                         top_p=0.9, min_remote_blocks=0, max_remote_blocks=3,
+                                                         remote_capacity=3, fast_rule=True)
+    b = fsi.BlockSparseLinear(D_in, Np, base_blocks=1, top_p=0.9, max_remote_blocks=3, remote_capacity=3)
+    b.load_state_dict({"weight": W, "indexer.q_proj.weight": wq, "indexer.k_proj.weight": wk,
+                       "indexer.v_proj.weight": wv, "indexer.out_proj.weight": wo_b,
+                       "weight_to_k.weight": wk, "weight_to_v.weight": wv})
+    b = b.to(DEV, torch.bfloat16).eval()
+    with torch.no_grad():
+        yb, auxb = b(x.to(DEV, torch.bfloat16))
+    assert auxb["active_blocks_union"] == active_b.numel()
+    assert rel_err(yb.float().cpu(), ref_b) < 2e-2
