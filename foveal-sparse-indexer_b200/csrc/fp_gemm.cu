@@ -434,6 +434,10 @@ __device__ __forceinline__ void down_store_chunk(const DownArgs& a, float (&o)[3
                                                  int ks, int ncols) {
   const int lane = threadIdx.x & 31;
   if (col0 >= ncols) return;  // uniform over the warp
+  if (a.omap && (ocol0 < 0 || ocol0 + 32 > (a.ldy > 0 ? (int64_t)a.ldy : (int64_t)a.D))) {
+    record_error(a.err, kErrBadTile);  // a block map entry outside Y: reported, nothing stored
+    return;
+  }
   if (a.ctx16 && add) {
     // o[i] += sum_k ctx[k] * W_out[ocol0 + i][k]; lane L loads row ocol0 + L of W_out and the warp
     // broadcasts it (all lanes of a chunk share the same 32 columns)

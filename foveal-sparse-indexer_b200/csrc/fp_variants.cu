@@ -202,7 +202,7 @@ __global__ void __launch_bounds__(256) rowact_kernel(const InT* __restrict__ S, 
                                                      OutT* __restrict__ P, int64_t ldp) {
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
-  const int n = *n_active * 64;
+  const int n = (int)min((int64_t)*n_active * 64, lds);  // never past the row
   const InT* s = S + row * lds;
   OutT* p = P + row * ldp;
   if (mode == 0) {
@@ -236,7 +236,7 @@ __global__ void __launch_bounds__(256) rowact_reg_kernel(const InT* __restrict__
                                                          OutT* __restrict__ P, int64_t ldp) {
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
-  const int n = min(*n_active * 64, 256 * EPT);
+  const int n = (int)min(min((int64_t)*n_active * 64, lds), (int64_t)256 * EPT);  // never past the row
   const InT* s = S + row * lds;
   OutT* p = P + row * ldp;
   float v[EPT];
@@ -326,7 +326,9 @@ __global__ void fill_inactive_kernel(const int32_t* __restrict__ blocks, const i
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t m = i / cols;
     const int cc = (int)(i - m * cols);
-    const int col = blocks[n + cc / 64] * 64 + cc % 64;
+    const int blk = blocks[n + cc / 64];
+    if ((unsigned)blk >= (unsigned)NB) continue;  // not a block of this layer (a corrupt list): skipped
+    const int col = blk * 64 + cc % 64;
     float v = 0.f;
     if (ctx16) {
 #pragma unroll
@@ -370,6 +372,10 @@ __global__ void __launch_bounds__(256) mapped_gemm_simt_kernel(const MappedGemm 
   if (c0 >= ncols) return;
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int64_t brow_c = g.nn ? 0 : (g.nmap ? (int64_t)g.nmap[c0 / 64] * 64 : c0);  // nn = 0: B rows of this tile
+  const int64_t ocol_c = g.omap ? (int64_t)g.omap[c0 / 64] * 64 : c0;               // Y columns of this tile
+  // map entries outside B or Y (a corrupt block list) leave the tile untouched
+  if ((g.nmap && !g.nn && (brow_c < 0 || brow_c + 64 > g.N)) || (g.omap && (ocol_c < 0 || ocol_c + 64 > g.ldy)))
+    return;
   float acc[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
@@ -391,7 +397,7 @@ __global__ void __launch_bounds__(256) mapped_gemm_simt_kernel(const MappedGemm 
         const int k = k0 + kk, c = c0 + cc;
         if (k < kcols && c < ncols) {
           const int64_t row = g.kmap ? (int64_t)g.kmap[k / 64] * 64 + k % 64 : k;
-          v = ld_any(g.b, row * g.ldb + c, g.b_f32);
+          if (row >= 0 && row < g.K) v = ld_any(g.b, row * g.ldb + c, g.b_f32);
         }
         Bs[kk][cc] = v;
       } else {
@@ -424,7 +430,7 @@ __global__ void __launch_bounds__(256) mapped_gemm_simt_kernel(const MappedGemm 
     for (int j = 0; j < 4; ++j) {
       const int c = c0 + tx * 4 + j;
       if (c >= ncols) continue;
-      const int64_t col = g.omap ? (int64_t)g.omap[c / 64] * 64 + c % 64 : c;
+      const int64_t col = ocol_c + (c - c0);
       float v = acc[i][j];
       if (g.bias) v += ld_any(g.bias, col, g.bias_f32);
       if (g.ctx16) {
