@@ -59,7 +59,8 @@ def parse():
                     "overlaps the next chunk's compute")
     ap.add_argument("--e2e-steps", type=int, default=0)
     ap.add_argument("--chunk-tokens", type=int, default=4096)
-    ap.add_argument("--cpu-sample", type=int, default=256)
+    ap.add_argument("--cpu-sample", type=int, default=8192,
+                    help="tokens of the CPU-baseline sample (about 10-30 s of host work over 3 timed calls)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
