@@ -205,6 +205,8 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
   }
   // full barrier: one expect_tx arrival (TMA) + one arrival per gather thread
   pipe_init(bars, 4, 1 + kGatherThreads);
+  griddep_wait();  // the routing kernel's work list, token lists and cleared H are complete
+  griddep_launch_dependents();
   const uint32_t tmem_base = bars->tmem;
   const int ntiles = gathered ? a.meta[0] : a.n_keys * (int)((a.M + kN - 1) / kN);
   const int nkb = a.D / kTileK;
@@ -518,6 +520,8 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
     tma_prefetch_desc(&tm_vt);
   }
   pipe_init(bars, 4);
+  griddep_wait();  // H (gate/up kernel) and the device counts are complete
+  griddep_launch_dependents();
   const uint32_t tmem_base = bars->tmem;
   const int m_tiles = (int)((a.M + kTileM - 1) / kTileM);
   const int n_tiles = (a.D + kTileN - 1) / kTileN;
@@ -710,6 +714,8 @@ down2_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ C
   __syncthreads();
   cluster_sync();  // both CTAs' barriers exist before any remote arrival or pair commit
   tc_fence_after();
+  griddep_wait();  // H (gate/up kernel) and the device counts are complete
+  griddep_launch_dependents();
   const uint32_t tmem_base = bars->tmem;
   const int m_pairs = (int)((a.M + 2 * kTileM - 1) / (2 * kTileM));
   const int n_tiles = (a.D + kTileN - 1) / kTileN;
@@ -880,6 +886,7 @@ down2_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ C
 
 // Sums the split-K partials [ks][n] in split order (deterministic) and writes the output dtype.
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int ks, int64_t n, void* out, int out_f32) {
+  griddep_wait();  // every split's partial is stored
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   float s = part[i];
@@ -937,8 +944,8 @@ static int launch_gateup_cfg(const GateUpArgs& a, cudaStream_t st) {
                                 (int)Cfg::kSmem) == cudaSuccess ? FP_OK : FP_ERR_CUDA;
   });
   if (attr != FP_OK) return attr;
-  gateup_kernel<Cfg><<<a.num_sms, kGuThreads, Cfg::kSmem, st>>>(tx, tw, a);
-  return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+  return launch_pdl(gateup_kernel<Cfg>, dim3(a.num_sms), dim3(kGuThreads), Cfg::kSmem, st, tx, tw, a) == cudaSuccess
+             ? FP_OK : FP_ERR_CUDA;
 }
 
 int launch_gateup(const GateUpArgs& a, cudaStream_t st) {
@@ -1046,19 +1053,20 @@ int launch_down(const DownArgs& a, cudaStream_t st) {
     if (max_pairs <= 0) return FP_ERR_CUDA;
     const int64_t ptiles = ((a.M + 2 * kTileM - 1) / (2 * kTileM)) * ((a.D + kTileN - 1) / kTileN);
     const int grid2 = 2 * (int)std::min<int64_t>(ptiles, std::min(max_pairs, a.num_sms / 2));
-    down2_kernel<<<grid2, kGemmThreads, kPairSmem, st>>>(th, tv2, tvw, a);
-    return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+    return launch_pdl(down2_kernel, dim3(grid2), dim3(kGemmThreads), kPairSmem, st, th, tv2, tvw, a) == cudaSuccess
+               ? FP_OK : FP_ERR_CUDA;
   }
   const int64_t tiles = ((a.M + kTileM - 1) / kTileM) * ((a.D + kTileN - 1) / kTileN) * ks;
   const int grid = (int)std::min<int64_t>(tiles, a.num_sms);
   if (grid <= 0) return FP_OK;
   if (ks > 1 && !a.y_acc) return FP_ERR_INVALID_ARG;
-  down_kernel<<<grid, kGemmThreads, kGemmSmem, st>>>(th, tv, a);
-  if (cudaGetLastError() != cudaSuccess) return FP_ERR_CUDA;
+  if (launch_pdl(down_kernel, dim3(grid), dim3(kGemmThreads), kGemmSmem, st, th, tv, a) != cudaSuccess)
+    return FP_ERR_CUDA;
   if (ks > 1) {
     const int64_t n = a.M * (int64_t)a.D;
-    splitk_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a.y_acc, ks, n, a.y, a.y_f32);
-    if (cudaGetLastError() != cudaSuccess) return FP_ERR_CUDA;
+    if (launch_pdl(splitk_reduce_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, (const float*)a.y_acc,
+                   ks, n, a.y, a.y_f32) != cudaSuccess)
+      return FP_ERR_CUDA;
   }
   return FP_OK;
 }

@@ -206,6 +206,24 @@ struct MappedGemm {
 };
 int launch_mapped_gemm_simt(const MappedGemm& g, cudaStream_t st);
 
+// Launch `kern` with programmatic stream serialization (it may start during the previous kernel of the
+// stream and must call griddep_wait() before reading that kernel's results).
+template <typename... Exp, typename... Act>
+inline cudaError_t launch_pdl(void (*kern)(Exp...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Act&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<Act&&>(args)...);
+}
+
 // ---- tensor maps
 bool encode_map_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                    uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer);

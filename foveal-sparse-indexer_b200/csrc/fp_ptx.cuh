@@ -152,6 +152,15 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* map, uin
       : "memory");
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start while the previous kernel of the
+// stream is still running; griddep_wait() blocks until that kernel has completed and its memory is
+// visible (a no-op for a normally launched kernel), so every read of upstream data comes after it.
+// griddep_launch_dependents() lets the next kernel of the stream launch once every CTA of this grid has
+// called it or exited (its CTAs then take SMs as this grid's CTAs leave).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
 // ---------------------------------------------------------------- cp.async (row gathers)
 // 16-byte global -> shared copy through L2 (bypassing L1).
 __device__ __forceinline__ void cp_async_16(uint32_t smem_dst, const void* gsrc) {

@@ -762,6 +762,7 @@ __global__ void __launch_bounds__(kRouteWarps * 32, 2)
 route_proj_kernel(const T* __restrict__ x, const T* __restrict__ wq, int64_t M, int D, float* __restrict__ qraw) {
   constexpr int W = kRouteWarps, TPW = kProjTPW;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  griddep_launch_dependents();  // the routing kernel may launch; it waits for this grid before reading qraw
   const int64_t tok0 = (int64_t)blockIdx.x * kProjTokens;
   if constexpr (kMma) {
     __shared__ float part[W * 16 * 17];
@@ -851,6 +852,8 @@ template <typename T, int E>
 __global__ void __launch_bounds__(kRouteWarps * 32, E <= 8 ? 3 : 1)
 route_kernel(const RouteArgs a) {
   constexpr int TPW = kRouteTPW, N = 32 * E;
+  griddep_wait();  // the projection kernel's queries are complete and visible
+  griddep_launch_dependents();
   extern __shared__ float4 route_smem4[];
   char* smb = reinterpret_cast<char*>(route_smem4);
   const bool csr = a.key_cnt != nullptr;
@@ -1185,8 +1188,8 @@ int route_go(const RouteArgs& a, bool mma, cudaStream_t st) {
       cudaSuccess)
     return FP_ERR_CUDA;
   const int64_t blocks = std::min<int64_t>(groups, (int64_t)std::max(per_sm, 1) * std::max(a.num_sms, 1));
-  route_kernel<T, E><<<(unsigned)blocks, kRouteWarps * 32, smem, st>>>(a);
-  return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+  return launch_pdl(route_kernel<T, E>, dim3((unsigned)blocks), dim3(kRouteWarps * 32), smem, st, a) == cudaSuccess
+             ? FP_OK : FP_ERR_CUDA;
 }
 
 template <int E>
