@@ -181,6 +181,9 @@ VARIANT_CASES: Dict[str, dict] = {
                   max_remote_blocks=6, remote_capacity=6, bias=False, use_additive_stream=False, x_shape=(12, 512)),
     "bsl_c": dict(kind="bsl", in_features=128, out_features=256, base_blocks=2, top_p=0.95, min_remote_blocks=0,
                   max_remote_blocks=8, remote_capacity=8, bias=True, use_additive_stream=True, x_shape=(3, 7, 128)),
+    # mass never reaches top_p: the inference rule counts one block past the two available ones
+    "bsl_d": dict(kind="bsl", in_features=192, out_features=256, base_blocks=2, top_p=1.5, min_remote_blocks=0,
+                  max_remote_blocks=8, remote_capacity=8, bias=False, use_additive_stream=True, x_shape=(2, 3, 192)),
     "tf_softmax": dict(kind="tf", in_features=256, out_features=256, num_param_tokens=2048, base_blocks=2, top_p=0.9,
                        min_remote_blocks=0, max_remote_blocks=4, remote_capacity=4, activation="softmax",
                        x_shape=(2, 6, 256)),

@@ -42,6 +42,7 @@ __all__ = [
     "cosine_block_scores",
     "union_blocks",
     "fast_remote_route",
+    "fast_rule_counts",
     "block_sparse_linear",
     "tokenformer_linear",
 ]
@@ -401,6 +402,15 @@ def fast_remote_route(scores: torch.Tensor, base: int, top_p: float, max_remote:
     r = select_blocks_noncausal(rem[None], local_window_blocks=0, top_p=top_p, min_remote_blocks=0,
                                 max_remote_blocks=max_remote, remote_capacity=min(max_remote, n_rem))
     return r.remote_indices[0].long() + base, r.remote_counts[0]
+
+
+def fast_rule_counts(scores: torch.Tensor, base: int, top_p: float, max_remote: int) -> torch.Tensor:
+    """The inference rule's per-token count as the reference computes it (block_matmul.py:188-193):
+    ``clamp(#(cumsum of the sorted remote softmax < top_p) + 1, 0, K_max)``, not clamped to the available
+    blocks (so it can exceed them by one when the mass never reaches top_p)."""
+    probs = F.softmax(scores[:, base:], dim=-1)
+    cum = probs.sort(dim=-1, descending=True, stable=True).values.cumsum(dim=-1)
+    return torch.clamp((cum < top_p).sum(dim=-1) + 1, 0, max_remote)
 
 
 def block_sparse_linear(x2d, weight, bias, q_proj, weight_to_k, weight_to_v, out_proj, *, block_size: int,
