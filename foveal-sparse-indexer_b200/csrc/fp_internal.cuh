@@ -90,7 +90,7 @@ int launch_route(const RouteArgs& a, int dtype, cudaStream_t st);
 // ---- gemm.cu (tensor-core path, bf16)
 struct GateUpArgs {
   const void* x;        // [M, D] bf16
-  const void* w_gu;     // [2 * Np, D] bf16, packed gate/up rows in tile-contiguous form (launch_pack_gate_up)
+  const void* w_gu;     // 2 * Np * D bf16: packed gate/up rows, tile-contiguous (launch_pack_gate_up)
   int64_t M;
   int D, Np;
   // work list: explicit (tiles/meta from the routing kernel) or implicit (pooled: n_keys x ceil(M/256))
@@ -128,7 +128,7 @@ __host__ __device__ __forceinline__ int balanced_rows(int cnt) {
 
 struct DownArgs {
   const void* h;        // [M, K] bf16
-  const void* v_t;      // [D, Np] bf16 (V transposed)
+  const void* v_t;      // B operand: V^T tile-contiguous (vt_tiled, launch_pack_vt) or row-major [D, Np] bf16
   int64_t M;
   int D, Np, K;         // K = number of k-blocks * 64 read from h
   const int32_t* bmap;  // optional: global block of k-block j (pooled); else j*stride+offset
