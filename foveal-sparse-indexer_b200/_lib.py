@@ -51,8 +51,9 @@ SIGNATURES = {
     "fp_select_remote_top_p": (_c_int, [_c_p, _c_i64, _c_int, _c_int, _c_f, _c_int, _c_int, _c_p, _c_p, _c_p,
                                         _c_p]),
     "fp_union_blocks": (_c_int, [_c_p, _c_p, _c_i64, _c_int, _c_int, _c_int, _c_p, _c_p, _c_p]),
-    "fp_block_sparse_linear_fwd": (_c_int, [_c_p, _c_i64, _c_int, _c_p, _c_p, _c_int, _c_int, _c_p, _c_p, _c_p,
-                                            _c_p, _c_p, _c_p, _c_sz, _c_p]),
+    "fp_block_sparse_linear_workspace_size": (_c_sz, [_c_int, _c_i64, _c_int, _c_int, _c_int]),
+    "fp_block_sparse_linear_fwd": (_c_int, [_c_p, _c_i64, _c_int, _c_p, _c_p, _c_int, _c_int, _c_p, _c_p, _c_int,
+                                            _c_p, _c_p, _c_p, _c_p, _c_sz, _c_p]),
     "fp_tokenformer_workspace_size": (_c_sz, [_c_int, _c_i64, _c_int]),
     "fp_tokenformer_fwd": (_c_int, [_c_p, _c_i64, _c_int, _c_p, _c_p, _c_p, _c_int, _c_int, _c_int, _c_int, _c_p,
                                     _c_p, _c_p, _c_p, _c_p, _c_p, _c_sz, _c_p]),

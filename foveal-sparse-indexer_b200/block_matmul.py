@@ -141,8 +141,9 @@ class BlockSparseLinear(nn.Module):
         blocks, n_active = kernels.union_blocks(idx, cnt, NB, base)
         # 5-6. contraction over the union (+ bias) with the additive stream in the epilogue
         ctx16 = additive_context(scores, vb) if self.use_additive_stream else None
+        max_active = min(NB, base + M * idx.shape[-1])  # host-side bound of the union
         out2d = kernels.block_sparse_linear(x2d, self.weight, self.bias, blocks, n_active, ctx16,
-                                            self.indexer.out_proj.weight)
+                                            self.indexer.out_proj.weight, max_active=max_active)
         return {"out": out2d, "scores": scores, "route": route, "stats": stats, "blocks": blocks,
                 "n_active": n_active, "ctx16": ctx16}
 

@@ -476,9 +476,30 @@ int fp_union_blocks(const int32_t* remote_indices, const int32_t* remote_counts,
                       (cudaStream_t)stream);
 }
 
+namespace {
+// Split-K factor of the BlockSparseLinear contraction on the one-SM tensor-core kernel (batches under 256
+// tokens): the output tiles of at most max_active blocks cannot occupy the GPU, so the contraction over
+// D_in is split (as down_ksplit does for the MLP's down projection).
+int bsl_ksplit(int dtype, int64_t M, int D_in, int out_features, int max_active, int sms) {
+  if (!tensor_path(dtype, D_in) || M >= 2 * kTileM) return 1;
+  const int NB = out_features / kBlock;
+  const int nact = max_active > 0 ? std::min(max_active, NB) : NB;
+  return down_ksplit(M, nact * kBlock, D_in / kTileK, sms);
+}
+size_t bsl_workspace(int ks, int64_t M, int out_features) {
+  return ks > 1 ? align_up(FP_VARIANT_WORKSPACE_MIN) + (size_t)ks * M * out_features * 4
+                : (size_t)FP_VARIANT_WORKSPACE_MIN;
+}
+}  // namespace
+
+size_t fp_block_sparse_linear_workspace_size(int dtype, int64_t M, int D_in, int out_features, int max_active) {
+  if (M <= 0 || D_in <= 0 || out_features <= 0) return FP_VARIANT_WORKSPACE_MIN;
+  return bsl_workspace(bsl_ksplit(dtype, M, D_in, out_features, max_active, layout_sms()), M, out_features);
+}
+
 int fp_block_sparse_linear_fwd(const void* x, int64_t M, int D_in, const void* weight, const void* bias,
                                int out_features, int dtype, const int32_t* blocks, const int32_t* n_active,
-                               const float* ctx16, const void* out_proj, void* out, void* workspace,
+                               int max_active, const float* ctx16, const void* out_proj, void* out, void* workspace,
                                size_t workspace_bytes, void* stream) {
   if (dtype != FP_DTYPE_F32 && dtype != FP_DTYPE_BF16) return FP_ERR_UNSUPPORTED;
   if (M < 0 || D_in <= 0 || out_features <= 0 || out_features % 64 != 0) return FP_ERR_INVALID_ARG;
@@ -495,11 +516,15 @@ int fp_block_sparse_linear_fwd(const void* x, int64_t M, int D_in, const void* w
   const int f32 = dtype == FP_DTYPE_F32;
   if (tensor_path(dtype, D_in) && aligned16(x) && aligned16(weight) && aligned16(out) &&
       (!out_proj || aligned16(out_proj))) {
+    const int ks = bsl_ksplit(dtype, M, D_in, out_features, max_active, sms);
+    if (workspace_bytes < bsl_workspace(ks, M, out_features)) return FP_ERR_WORKSPACE;
     DownArgs d{};
     d.h = x; d.v_t = weight; d.M = M; d.D = out_features; d.Np = D_in; d.K = D_in;
     d.stride = 1; d.offset = 0;
     d.ctx16 = ctx16; d.out_proj = out_proj; d.out_proj_f32 = 0;
-    d.y = out; d.y_f32 = 0; d.ksplit = 1; d.err = err; d.num_sms = sms;
+    d.y = out; d.y_f32 = 0; d.ksplit = ks; d.err = err; d.num_sms = sms;
+    d.y_acc = ks > 1 ? reinterpret_cast<float*>(static_cast<char*>(workspace) + align_up(FP_VARIANT_WORKSPACE_MIN))
+                     : nullptr;
     d.nmap = blocks; d.omap = blocks; d.ncnt = n_active; d.bias = bias; d.bias_f32 = 0; d.ldy = out_features;
     FP_TRY(launch_down(d, st));
   } else {

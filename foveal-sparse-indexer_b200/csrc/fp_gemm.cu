@@ -481,7 +481,7 @@ __device__ __forceinline__ void down_store_chunk(const DownArgs& a, float (&o)[3
   }
   if (!row_ok) return;
   const int64_t ldy = a.ldy > 0 ? a.ldy : (int64_t)a.D;
-  if (ks > 1) {  // partial of this split; summed in split order by splitk_reduce_kernel
+  if (ks > 1) {  // partial of this split; summed in split order by a split-K reduce kernel
     float4* yp = reinterpret_cast<float4*>(a.y_acc + ((int64_t)split * a.M + row) * a.D + col0);
 #pragma unroll
     for (int i = 0; i < 8; ++i) yp[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
@@ -895,6 +895,26 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, int ks, int
   else reinterpret_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(s);
 }
 
+// Block-mapped form: sums the split partials [ks][M][D] (computed columns) of the first 64 * ncnt
+// columns in split order and stores column c of row m at Y column omap[c / 64] * 64 + c % 64 (or c).
+__global__ void splitk_reduce_mapped_kernel(const float* __restrict__ part, int ks, int64_t M, int D,
+                                            const int32_t* __restrict__ ncnt, const int32_t* __restrict__ omap,
+                                            void* out, int64_t ldy, int out_f32) {
+  griddep_wait();  // every split's partial is stored
+  const int ncols = ncnt ? max(0, min(D / kBlock, *ncnt)) * kBlock : D;
+  const int64_t n = M * ncols;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / ncols;
+    const int c = (int)(i - m * ncols);
+    float s = part[m * D + c];
+    for (int k = 1; k < ks; ++k) s += part[((int64_t)k * M + m) * D + c];
+    const int64_t col = omap ? (int64_t)omap[c / kBlock] * kBlock + c % kBlock : c;
+    if (col < 0 || col >= ldy) continue;  // a block map entry outside Y (reported by the contraction)
+    if (out_f32) reinterpret_cast<float*>(out)[m * ldy + col] = s;
+    else reinterpret_cast<__nv_bfloat16*>(out)[m * ldy + col] = __float2bfloat16_rn(s);
+  }
+}
+
 // ============================================================================================
 // Host side
 // ============================================================================================
@@ -1000,7 +1020,7 @@ int launch_pack_vt(const void* v, int Np, int D, void* vt, cudaStream_t st) {
 int launch_down(const DownArgs& a, cudaStream_t st) {
   const bool mapped = a.nmap || a.omap || a.ncnt || a.kcnt || a.bias || a.ldy > 0;
   const int ks = a.ksplit > 1 ? a.ksplit : 1;
-  if (mapped && (ks != 1 || a.D % kBlock != 0)) return FP_ERR_INVALID_ARG;
+  if (mapped && a.D % kBlock != 0) return FP_ERR_INVALID_ARG;
   if (a.vt_tiled && a.nmap) return FP_ERR_INVALID_ARG;
   // tile-contiguous V^T: rows of 64 elements, ceil(D / 256) * (Np / 64) tiles of 256 rows
   const uint64_t vt_rows = (uint64_t)((a.D + kTileN - 1) / kTileN) * (a.Np / kBlock) * kTileN;
@@ -1062,7 +1082,13 @@ int launch_down(const DownArgs& a, cudaStream_t st) {
   if (ks > 1 && !a.y_acc) return FP_ERR_INVALID_ARG;
   if (launch_pdl(down_kernel, dim3(grid), dim3(kGemmThreads), kGemmSmem, st, th, tv, a) != cudaSuccess)
     return FP_ERR_CUDA;
-  if (ks > 1) {
+  if (ks > 1 && mapped) {
+    const int64_t n = a.M * (int64_t)a.D;
+    const int rgrid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (int64_t)a.num_sms * 8));
+    if (launch_pdl(splitk_reduce_mapped_kernel, dim3(rgrid), dim3(256), 0, st, (const float*)a.y_acc, ks, a.M, a.D,
+                   a.ncnt, a.omap, a.y, a.ldy > 0 ? a.ldy : (int64_t)a.D, a.y_f32) != cudaSuccess)
+      return FP_ERR_CUDA;
+  } else if (ks > 1) {
     const int64_t n = a.M * (int64_t)a.D;
     if (launch_pdl(splitk_reduce_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, (const float*)a.y_acc,
                    ks, n, a.y, a.y_f32) != cudaSuccess)

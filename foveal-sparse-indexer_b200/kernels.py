@@ -263,9 +263,10 @@ def union_blocks(remote_indices: torch.Tensor, remote_counts: torch.Tensor, num_
 
 def block_sparse_linear(x2d: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], blocks: torch.Tensor,
                         n_active: torch.Tensor, ctx16: Optional[torch.Tensor] = None,
-                        out_proj: Optional[torch.Tensor] = None) -> torch.Tensor:
+                        out_proj: Optional[torch.Tensor] = None, max_active: int = 0) -> torch.Tensor:
     """BlockSparseLinear contraction over the union (``fp_block_sparse_linear_fwd``;
-    block_matmul.py:233-254): out [M, out_features] in x's dtype."""
+    block_matmul.py:233-254): out [M, out_features] in x's dtype.  ``max_active``: a host-side upper
+    bound of the union size (0 = all blocks), which lets small batches split the contraction."""
     dev = require_cuda(x2d, weight, blocks, n_active)
     dtt = x2d.dtype
     x2d, weight = contig(x2d), contig(weight.detach().to(dtt))
@@ -275,10 +276,12 @@ def block_sparse_linear(x2d: torch.Tensor, weight: torch.Tensor, bias: Optional[
     M, D_in = x2d.shape
     out_features = weight.shape[0]
     out = torch.empty(M, out_features, dtype=dtt, device=dev)
-    ws = _lib.workspace(dev, 256)
-    rc = _lib.load().fp_block_sparse_linear_fwd(ptr(x2d), M, D_in, ptr(weight), ptr(bias), out_features,
-                                                dtype_code(dtt), ptr(blocks), ptr(n_active), ptr(ctx16), ptr(out_proj),
-                                                ptr(out), ptr(ws), ws.numel(), stream_handle(dev))
+    lib = _lib.load()
+    ws = _lib.workspace(dev, lib.fp_block_sparse_linear_workspace_size(dtype_code(dtt), M, D_in, out_features,
+                                                                      int(max_active)))
+    rc = lib.fp_block_sparse_linear_fwd(ptr(x2d), M, D_in, ptr(weight), ptr(bias), out_features, dtype_code(dtt),
+                                        ptr(blocks), ptr(n_active), int(max_active), ptr(ctx16), ptr(out_proj),
+                                        ptr(out), ptr(ws), ws.numel(), stream_handle(dev))
     check(rc, "fp_block_sparse_linear_fwd")
     return out
 

@@ -245,6 +245,9 @@ FP_API int fp_select_remote_top_p(const float* scores, int64_t M, int NB, int ba
 FP_API int fp_union_blocks(const int32_t* remote_indices, const int32_t* remote_counts, int64_t M, int capacity,
                            int NB, int base, int32_t* blocks, int32_t* n_active, void* stream);
 
+/* Workspace bytes of fp_block_sparse_linear_fwd (max_active as there). */
+FP_API size_t fp_block_sparse_linear_workspace_size(int dtype, int64_t M, int D_in, int out_features, int max_active);
+
 /*
  * BlockSparseLinear contraction (block_matmul.py:233-254):
  *   out[m, c] = x[m] . weight[c] + bias[c] + ctx16[m] . out_proj[c]   for c in an active block
@@ -253,13 +256,16 @@ FP_API int fp_union_blocks(const int32_t* remote_indices, const int32_t* remote_
  * weight [out_features, D_in], bias [out_features] (optional), out_proj [out_features, 16] and out
  * [M, out_features] in `dtype`; blocks / n_active from fp_union_blocks; ctx16 [M, 16] fp32.
  * out_features % 64 == 0.  bf16 with D_in % 64 == 0 runs on the tensor cores (tcgen05), everything
- * else on CUDA cores.  Workspace: FP_VARIANT_WORKSPACE_MIN bytes (device error word).
+ * else on CUDA cores.  max_active: an upper bound of *n_active known on the host (e.g. base +
+ * M * capacity; <= 0 = out_features / 64), from which batches of few tokens size a split of the
+ * contraction.  Workspace: fp_block_sparse_linear_workspace_size bytes, at least
+ * FP_VARIANT_WORKSPACE_MIN (device error word).
  */
 #define FP_VARIANT_WORKSPACE_MIN 256u
 FP_API int fp_block_sparse_linear_fwd(const void* x, int64_t M, int D_in, const void* weight, const void* bias,
                                       int out_features, int dtype, const int32_t* blocks, const int32_t* n_active,
-                                      const float* ctx16, const void* out_proj, void* out, void* workspace,
-                                      size_t workspace_bytes, void* stream);
+                                      int max_active, const float* ctx16, const void* out_proj, void* out,
+                                      void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * FovealTokenformerLinear contraction over the active parameter tokens (tokenformer.py:183-203):

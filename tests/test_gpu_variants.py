@@ -144,6 +144,8 @@ def _bsl_case(M, D_in, out_features, base, kmax, top_p, bias, dt, seed):
     (600, 1024, 4096, 8, 0.8, True),     # ragged token count, partial union
     (130, 512, 1536, 24, 0.95, False),   # output width not a multiple of 256
     (1, 256, 8192, 4, 0.5, True),        # one token: a sparse union (tensor path, most tiles skipped)
+    (64, 1024, 4096, 8, 0.8, True),      # decode-sized batch: the contraction is split over D_in (split-K)
+    (1, 1024, 14336, 8, 0.8, False),     # one token at the 8B width: a 10-block bound, split-K over 3 tiles
 ])
 def test_block_sparse_linear_tensor_path(M, D_in, out_features, kmax, top_p, bias):
     x, W, b, wq, wk, wv, wo = _bsl_case(M, D_in, out_features, 2, kmax, top_p, bias, "bf16", M)
