@@ -8,9 +8,9 @@ Public API (same names as the reference package ``foveal_indexer``):
     FovealTokenformerLinear, FovealTokenformerFFN                 (foveal_indexer/tokenformer.py)
 
 Compute runs in ``libfovealpatt.so`` (hand-written sm_100a CUDA behind the C ABI of
-``include/foveal_pattention.h``); build it with ``build.py``.  The directory name contains hyphens, so
-import it with ``importlib.import_module("foveal-sparse-indexer_b200")``; after that first import the
-alias ``foveal_sparse_indexer_b200`` is registered in ``sys.modules``.
+``include/foveal_pattention.h``); build it with ``build.py``.  The directory name contains hyphens: with
+the repository root on ``sys.path``, ``import foveal_sparse_indexer_b200`` loads it (the module of that
+name at the root binds to this package), as does ``importlib.import_module("foveal-sparse-indexer_b200")``.
 """
 
 import sys as _sys

@@ -60,6 +60,7 @@ SIGNATURES = {
     "fp_transpose": (_c_int, [_c_p, _c_i64, _c_i64, _c_int, _c_p, _c_p]),
     "fp_set_stage_events": (_c_int, [ctypes.POINTER(_c_p), _c_int]),
     "fp_device_error": (_c_int, [_c_p, _c_p, _c_p]),
+    "fp_noalloc_device_error": (_c_int, [_c_p, _c_p]),
 }
 
 _lock = threading.Lock()

@@ -2,7 +2,8 @@
 foveal router, on the CUDA library (mirrors ``foveal_indexer/block_matmul.py:25-282``).
 
 Same constructor, parameter names, initialisation, ``state_dict`` keys and ``(out, aux)`` result as the
-reference.  A forward is: pooled 16-D block keys / values of the weight (cached in eval), cosine block
+reference; the aux statistics (union size, mean active blocks, sparsity) are 0-d device tensors instead
+of Python numbers, so a forward never waits for the GPU (``int()`` / ``float()`` read them).  A forward is: pooled 16-D block keys / values of the weight (cached in eval), cosine block
 scores of the tokens, the selection (the inference rule of block_matmul.py:185-201 in eval without
 autograd, ``FovealIndexer.route`` otherwise), the union of the selected blocks, and one contraction over
 that union with the bias and the 16-D additive stream in its epilogue (tcgen05 tensor cores for bf16).
@@ -159,10 +160,13 @@ class BlockSparseLinear(nn.Module):
         fast = not self.training and not torch.is_grad_enabled()
         r = self.forward_kernels(x2d, fast, (batch, seq_len))
         route, scores, ctx16, n_active = r["route"], r["scores"], r["ctx16"], r["n_active"]
+        # the aux statistics stay on the device (0-d tensors): the forward never waits for the GPU
         if route is not None:
-            mean_remote = float(route.mean_remote_blocks.item())
+            mean_remote = route.mean_remote_blocks
+        elif r["stats"] is not None:
+            mean_remote = r["stats"][1] / max(M, 1)
         else:
-            mean_remote = float(r["stats"][1].item()) / max(M, 1) if r["stats"] is not None else 0.0
+            mean_remote = torch.zeros((), dtype=torch.float32, device=dev)
         out = r["out"].view(batch, seq_len, self.out_features)
         additive_out = None
         if ctx16 is not None:
@@ -172,7 +176,7 @@ class BlockSparseLinear(nn.Module):
         out = forward_only(out, self, x_in)
         if orig_ndim == 2:
             out = out.squeeze(1)
-        num_active = int(n_active.item())
+        num_active = n_active.reshape(())
         mean_active = base + mean_remote
         aux: Dict[str, Any] = {
             "route": route,

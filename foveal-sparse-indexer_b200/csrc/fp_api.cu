@@ -51,7 +51,8 @@ TokenLayout token_layout(int dtype, int64_t M, int D, int NB, int base, int kmax
   L.nkey = (int)(nchunks * std::max(L.nbl, 1));
   L.key_cap = std::min<int64_t>(L.chunk, std::max<int64_t>(M, 1));
   const bool tc = tensor_path(dtype, D);
-  // error word, completion ticket and the block-CSR key counters: cleared by one memset per call
+  // error word, completion ticket and the block-CSR key counters: cleared by one memset per call.  The
+  // error word stays at offset 0 (fp_noalloc_device_error reads it there in the library's scratch array).
   L.zero_bytes = 256 + (tc ? (size_t)L.nkey * 4 : 0);
   L.err = c.take(L.zero_bytes);
   L.key_cnt = L.err + 256;

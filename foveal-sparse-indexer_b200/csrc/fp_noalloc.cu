@@ -16,8 +16,9 @@
 //     or threads without ordering between them) race on the array: serialise them.
 //   * The first call on a device looks up the array's device address (cudaGetSymbolAddress with
 //     that device current) and caches it; make that first call before any stream capture.
-//   * The bounded-wait error word of this variant lives in the shared array and is not exposed;
-//     callers that need fp_device_error use fp_pattention_token_fwd with their own workspace.
+//   * The bounded-wait error word of a call lives at the start of the shared array (the workspace
+//     layout of the token forward puts it at offset 0).  fp_noalloc_device_error reads and clears it;
+//     read it before the next no-alloc call on the device, which clears it again.
 #include "fp_internal.cuh"
 
 #include <mutex>
@@ -72,6 +73,13 @@ int fp_pattention_token_fwd_noalloc(const void* x, int64_t M, int D, int NB, int
                                  base_blocks, top_p, min_remote, max_remote, temperature, additive, block_stride,
                                  block_offset, y, y_f32, remote_indices, remote_counts, scores, scratch,
                                  fp::kNoAllocScratchBytes, stream);
+}
+
+int fp_noalloc_device_error(void* stream, int* code) {
+  void* scratch = nullptr;
+  const int rc = fp::scratch_on_current_device(&scratch);
+  if (rc != FP_OK) return rc;
+  return fp_device_error(scratch, stream, code);  // error word at offset 0 of the token-forward layout
 }
 
 }  // extern "C"

@@ -3,7 +3,8 @@
 ``FovealTokenformerLinear`` replaces a linear projection by attention from the input tokens to learnable
 parameter tokens (K_P, V_P), restricted to the union of the 64-token parameter blocks the call's
 tokens select with the 16-D foveal router.  Same constructor, parameter names, initialisation,
-``state_dict`` keys and ``(out, aux)`` result as the reference.  A forward is: pooled 16-D keys / values
+``state_dict`` keys and ``(out, aux)`` result as the reference (the aux counts are 0-d device tensors, so
+the forward never waits for the GPU).  A forward is: pooled 16-D keys / values
 of the parameter blocks (cached in eval), cosine block scores, ``FovealIndexer.route``, the union of the
 selected blocks, then ``act(x K_act^T) V_act`` (two tensor-core contractions for bf16 around a row
 activation kernel) with the 16-D additive stream in the second contraction's epilogue.  Forward-only.
@@ -136,8 +137,9 @@ class FovealTokenformerLinear(nn.Module):
         aux: Dict[str, Any] = {
             "route": route,
             "additive_out": additive_out,
-            "active_param_tokens_union": int(n_active.item()) * bs,
-            "mean_active_param_tokens": base_param_count + float(route.mean_remote_blocks.item()) * bs,
+            # device 0-d tensors: the forward never waits for the GPU to fill the aux dict
+            "active_param_tokens_union": n_active.reshape(()) * bs,
+            "mean_active_param_tokens": base_param_count + route.mean_remote_blocks * bs,
             "total_param_tokens": self.num_param_tokens,
             "distill_loss": torch.tensor(0.0, device=dev),
         }

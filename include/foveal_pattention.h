@@ -183,7 +183,9 @@ FP_API int fp_swiglu_bwd(const void* dout, const void* g, const void* u, int dty
  * device-memory budget fixed at start-up) can still run the layer.  Calls needing more scratch than
  * the array holds (large batches; sized for decode-step batches) return FP_ERR_WORKSPACE.  All calls
  * on a device share the array: calls that overlap on the GPU race, so serialise them.  The first call
- * on a device looks up the array's address; make it before any stream capture.
+ * on a device looks up the array's address; make it before any stream capture.  The bounded-wait
+ * error word of a call lives in the array: read it with fp_noalloc_device_error before the next
+ * no-alloc call on that device (which clears it).
  */
 #define FP_NOALLOC_SCRATCH_BYTES (16u << 20)
 FP_API int fp_pattention_token_fwd_noalloc(const void* x, int64_t M, int D, int NB, int dtype,
@@ -193,6 +195,14 @@ FP_API int fp_pattention_token_fwd_noalloc(const void* x, int64_t M, int D, int 
                                            int max_remote, float temperature, int additive, int block_stride,
                                            int block_offset, void* y, int y_f32, int32_t* remote_indices,
                                            int32_t* remote_counts, float* scores, void* stream);
+
+/*
+ * Device error word of the last fp_pattention_token_fwd_noalloc call on the current device (no
+ * counterpart in the reference): synchronizes `stream`, returns FP_OK, FP_ERR_TIMEOUT (a bounded wait
+ * of that call ran out, so its outputs are incomplete) or FP_ERR_CUDA, writes the raw code to *code and
+ * clears the word, like fp_device_error on a caller's workspace.  Allocates nothing.
+ */
+FP_API int fp_noalloc_device_error(void* stream, int* code);
 
 /* ------------------------------------------------------------------------------------------------
  * Layers that share the 16-D router but contract over the UNION of the blocks a call's tokens

@@ -69,25 +69,72 @@ def route_sets(idx, cnt):
     return [frozenset(idx[t, :int(cnt[t])].tolist()) for t in range(len(cnt))]
 
 
-# Probabilities closer than this (fp32, absolute) at the selection boundary are rounding-level ties:
-# their order may legitimately differ between two correct fp32 implementations.
+# Probabilities closer than this (fp32, absolute) at the selection boundary are rounding-level near
+# ties: 0 < p[K-1] - p[K] < TIE_EPS.  Two correct fp32 implementations may order such a pair differently
+# (exp, the softmax denominator and the D-long projection round differently on every platform), so a
+# differing set there is counted and reported, not failed.  A margin of exactly 0 is a bit-equal tie:
+# the lower block id must win (stable descending order), and a differing set there fails.
 TIE_EPS = 2e-8
 
+# Tie accounting of every route comparison made in this session, printed at the end of the run.
+TIE_REPORTS: list = []
 
-def compare_routes(idx, cnt, ref_idx, ref_cnt, margins=None, tie_eps: float = TIE_EPS):
+
+class RouteTieReport(dict):
+    """Per-comparison route accounting: tokens, mismatches outside the band, near ties in the band and
+    how many of them differ, bit-equal ties and how many of them differ, and the smallest reference
+    margin among differing tokens (None when every set matches)."""
+
+
+def compare_routes(idx, cnt, ref_idx, ref_cnt, margins=None, tie_eps: float = TIE_EPS, label: str = ""):
     """Counts must match exactly; selected sets must match exactly except on tokens whose reference
-    boundary margin is below ``tie_eps``.  Returns (n_mismatch_outside_ties, n_near_ties)."""
+    boundary margin lies in (0, ``tie_eps``).  Returns (n_mismatch_not_excused, n_near_ties) and records
+    a :class:`RouteTieReport` in ``TIE_REPORTS`` when ``label`` is given.  Mismatches on bit-equal ties
+    (margin exactly 0: the lower id must win) are never excused."""
     cnt = np.asarray(cnt)
     ref_cnt = np.asarray(ref_cnt)
     a, b = route_sets(idx, cnt), route_sets(ref_idx, ref_cnt)
-    bad = 0
-    ties = 0
+    m = None if margins is None else np.asarray(margins, dtype=np.float64)
+    rep = RouteTieReport(label=label, tokens=len(a), differ_outside_band=0, in_band=0, in_band_differ=0,
+                         exact_ties=0, exact_tie_differ=0, min_margin_differ=None,
+                         min_margin=None if m is None or m.size == 0 else float(m.min()))
     for t in range(len(a)):
-        near = margins is not None and float(margins[t]) < tie_eps
-        ties += int(near)
-        if (a[t] != b[t] or cnt[t] != ref_cnt[t]) and not near:
-            bad += 1
-    return bad, ties
+        mt = None if m is None else float(m[t])
+        exact = mt is not None and mt == 0.0
+        near = mt is not None and 0.0 < mt < tie_eps
+        rep["exact_ties"] += int(exact)
+        rep["in_band"] += int(near)
+        if a[t] != b[t] or cnt[t] != ref_cnt[t]:
+            if near:
+                rep["in_band_differ"] += 1
+            elif exact:
+                rep["exact_tie_differ"] += 1
+            else:
+                rep["differ_outside_band"] += 1
+            if mt is not None:
+                cur = rep["min_margin_differ"]
+                rep["min_margin_differ"] = mt if cur is None else min(cur, mt)
+    if label:
+        TIE_REPORTS.append(rep)
+        path = os.environ.get("FP_TIE_REPORT")
+        if path:
+            with open(path, "a") as f:
+                f.write(json.dumps(dict(rep)) + "\n")
+    return rep["differ_outside_band"] + rep["exact_tie_differ"], rep["in_band"]
+
+
+def pytest_terminal_summary(terminalreporter, exitstatus, config):
+    """One line per route comparison: how many tokens sat in the rounding band and how many of those
+    differed (every difference outside the band, or on a bit-equal tie, already failed its test)."""
+    if not TIE_REPORTS:
+        return
+    tr = terminalreporter
+    tr.section("route tie accounting (TIE_EPS = %.0e)" % TIE_EPS)
+    for r in TIE_REPORTS:
+        mmd = "-" if r["min_margin_differ"] is None else "%.2e" % r["min_margin_differ"]
+        tr.write_line(f"{r['label']}: tokens {r['tokens']}, in band {r['in_band']} (differ {r['in_band_differ']}), "
+                      f"bit-equal {r['exact_ties']} (differ {r['exact_tie_differ']}), "
+                      f"differ outside {r['differ_outside_band']}, min margin of differing {mmd}")
 
 
 def active_set_matches(active, gold_scores, base: int, remote: int, rel_tol: float) -> bool:

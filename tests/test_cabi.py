@@ -153,3 +153,11 @@ def test_variant_layers_interface():
         bsl(torch.zeros(1, 3, 128))
     with pytest.raises(RuntimeError):
         tf(torch.zeros(1, 3, 64))
+
+
+def test_package_imports_by_plain_name():
+    """``import foveal_sparse_indexer_b200`` (repository root on sys.path) binds to the package whose
+    directory name contains hyphens."""
+    import foveal_sparse_indexer_b200 as alias
+    assert alias is fsi
+    assert alias.FovealPattentionMLP is fsi.FovealPattentionMLP

@@ -1,12 +1,15 @@
 """GPU parity: the CUDA path (through the C ABI) against the golden vectors and the CPU oracle.
 
-Bars: active-block sets and counts bit-exact (tokens whose reference boundary margin is below
-TIE_EPS are rounding-level ties and are counted, not failed); outputs within 1e-4 relative (fp32
-configuration) or 2e-2 relative (bf16 configurations) of the fp32 reference, measured as
-||y - ref|| / ||ref|| and as max|y - ref| / max|ref|.
+Bars: active-block sets and counts bit-exact.  Tokens whose reference boundary margin lies in
+(0, TIE_EPS) are rounding-level near ties: they are counted (in the band, and how many of them
+differ) and reported at the end of the run, not failed; a bit-equal tie (margin 0) must go to the
+lower block id.  Outputs within 1e-4 relative (fp32 configuration) or 2e-2 relative (bf16
+configurations) of the fp32 reference, measured as ||y - ref|| / ||ref|| and as max|y - ref| / max|ref|.
 """
 
 from __future__ import annotations
+
+import dataclasses
 
 import numpy as np
 import pytest
@@ -87,11 +90,12 @@ def test_router_scores_match_oracle():
 
 
 # ------------------------------------------------------------------ token mode vs golden
-def token_vs_golden(wl, w, x2d, g, prefix, n_out):
+def token_vs_golden(wl, w, x2d, g, prefix, n_out, label=None):
     m = module_for(wl, w)
     y, info = run_token(m, x2d)
     bad, ties = compare_routes(info["remote_indices"].cpu(), info["remote_counts"].cpu(),
-                               g[f"{prefix}remote_indices"], g[f"{prefix}remote_counts"], g[f"{prefix}margins"])
+                               g[f"{prefix}remote_indices"], g[f"{prefix}remote_counts"], g[f"{prefix}margins"],
+                               label=label or f"{wl.name} golden ({x2d.shape[0]} tokens)")
     assert bad == 0, f"{bad} routes differ outside near ties ({ties} ties)"
     if n_out:
         check_y(y[:n_out].cpu(), torch.from_numpy(g[f"{prefix}y"]), wl.dtype)
@@ -133,7 +137,7 @@ def test_token_sweep_slice():
     xs = configs.make_x(pts[0]).reshape(-1, pts[0].hidden_dim)[:64].contiguous()
     for i, wl in enumerate(pts):
         n_out = g[f"p{i}_y"].shape[0] if f"p{i}_y" in g else 0
-        token_vs_golden(wl, w, xs, g, f"p{i}_", n_out)
+        token_vs_golden(wl, w, xs, g, f"p{i}_", n_out, label=f"sweep top_p {wl.top_p} K_max {wl.max_remote_blocks}")
 
 
 # ------------------------------------------------------------------ pooled mode vs golden
@@ -191,7 +195,8 @@ def full_size_check(name, n_out):
                                        remote_capacity=wl.max_remote_blocks)
     idx, cnt = r.remote_indices[0], r.remote_counts[0]
     margins = oracle.boundary_margins(r.remote_probs_sorted[0], cnt)
-    bad, ties = compare_routes(info["remote_indices"].cpu(), info["remote_counts"].cpu(), idx, cnt, margins)
+    bad, ties = compare_routes(info["remote_indices"].cpu(), info["remote_counts"].cpu(), idx, cnt, margins,
+                               label=f"{name} full ({x2d.shape[0]} tokens)")
     assert bad == 0, f"{bad} of {x2d.shape[0]} routes differ outside near ties ({ties} ties)"
     sel = torch.randperm(x2d.shape[0], generator=torch.Generator().manual_seed(7))[:n_out].sort().values
     ref = oracle.token_pattention(x2d[sel], w.k_gate, w.k_up, w.v, wl.base_blocks, idx[sel], cnt[sel])
@@ -204,6 +209,70 @@ def full_size_check(name, n_out):
 def test_full_8b_config():
     y = full_size_check("8b", 128)
     assert torch.isfinite(y).all()
+
+
+def test_full_sweep_routes():
+    """Every token of the sweep workload (16384 tokens, 8B shape) at all 20 (top_p, K_max) points: routes
+    against the oracle, with the tie accounting of each point recorded."""
+    pts = configs.sweep_points()
+    w = configs.make_weights(pts[0])
+    x2d = configs.make_x(pts[0]).reshape(-1, pts[0].hidden_dim)
+    S = oracle.router_scores(x2d, w.q_proj_16d, w.block_keys_16d)
+    for wl in pts:
+        m = module_for(wl, w)
+        _, info = run_token(m, x2d)
+        r = oracle.select_blocks_noncausal(S[None] / wl.temperature, local_window_blocks=wl.base_blocks,
+                                           top_p=wl.top_p, min_remote_blocks=wl.min_remote_blocks,
+                                           max_remote_blocks=wl.max_remote_blocks,
+                                           remote_capacity=wl.max_remote_blocks)
+        idx, cnt = r.remote_indices[0], r.remote_counts[0]
+        margins = oracle.boundary_margins(r.remote_probs_sorted[0], cnt)
+        bad, ties = compare_routes(info["remote_indices"].cpu(), info["remote_counts"].cpu(), idx, cnt, margins,
+                                   label=f"sweep full top_p {wl.top_p} K_max {wl.max_remote_blocks}")
+        assert bad == 0, f"top_p {wl.top_p} K_max {wl.max_remote_blocks}: {bad} routes differ ({ties} near ties)"
+    device_error_is_clear()
+
+
+def test_bit_equal_ties_go_to_lower_block_ids():
+    """Bit-equal probabilities at the selection boundary: the lower block id wins (stable descending
+    order), in both selection kernels.
+
+    * ``fp_select_blocks`` on scores quantised to multiples of 1/4 (many exactly equal scores per row).
+    * The fused routing kernel of the token forward with block keys repeated in groups of three (every
+      block of a group scores bit-identically for every token), so that most tokens' K_max boundary falls
+      inside a group.
+    Every token must match the oracle's stable-sort route; the test also requires that bit-equal ties
+    were actually exercised."""
+    g = torch.Generator().manual_seed(11)
+    s = (torch.randn(1, 512, 96, generator=g) * 4).round() / 4
+    r = fsi.select_blocks(s.to(DEV), causal=False, local_window_blocks=3, top_p=0.9, min_remote_blocks=2,
+                          max_remote_blocks=12, remote_capacity=12)
+    o = oracle.select_blocks_noncausal(s, local_window_blocks=3, top_p=0.9, min_remote_blocks=2,
+                                       max_remote_blocks=12, remote_capacity=12)
+    mg = oracle.boundary_margins(o.remote_probs_sorted[0], o.remote_counts[0])
+    bad, _ = compare_routes(r.remote_indices[0].cpu(), r.remote_counts[0].cpu(), o.remote_indices[0],
+                            o.remote_counts[0], mg, label="exact ties: fp_select_blocks (quantised scores)")
+    assert bad == 0
+    assert int((mg == 0).sum()) > 100, "the case must exercise bit-equal ties"
+
+    wl = configs.CONFIGS["8b"].with_(name="ties", hidden_dim=512, intermediate_dim=2048, base_blocks=2,
+                                     max_remote_blocks=8, min_remote_blocks=2, top_p=0.95)
+    w = configs.make_weights(wl)
+    grp = torch.arange(wl.num_blocks) // 3 * 3
+    w = dataclasses.replace(w, block_keys_16d=w.block_keys_16d[grp].contiguous() * 8)  # groups of 3 identical keys
+    x2d = configs.make_x(wl).reshape(-1, wl.hidden_dim)[:1024].contiguous()
+    ref = oracle.token_forward(x2d, w, base_blocks=wl.base_blocks, top_p=wl.top_p,
+                               min_remote_blocks=wl.min_remote_blocks, max_remote_blocks=wl.max_remote_blocks)
+    sp = ref["sorted_probs"]
+    mg = oracle.boundary_margins(sp, ref["remote_counts"])
+    m = module_for(wl, w)
+    y, info = run_token(m, x2d)
+    bad, _ = compare_routes(info["remote_indices"].cpu(), info["remote_counts"].cpu(), ref["remote_indices"],
+                            ref["remote_counts"], mg, label="exact ties: fused routing kernel (repeated keys)")
+    assert bad == 0
+    assert int((mg == 0).sum()) > 100, "the case must exercise bit-equal ties"
+    check_y(y.cpu(), ref["y"].reshape(x2d.shape[0], -1), "bf16")
+    device_error_is_clear()
 
 
 def test_full_70b_config():

@@ -5,7 +5,8 @@ over input and output pointers, or serving loops whose device-memory budget is f
 The no-alloc entry point serves them from scratch memory the library keeps on each GPU.  This test
 drives both entry points through the C ABI on the same decode-step inputs and requires the no-alloc
 results of two consecutive calls (which share and reuse that scratch) to match the workspace entry
-point within the bf16 tolerance of the other parity tests, and an oversized batch to be refused.
+point within the bf16 tolerance of the other parity tests, each call's device error word (read back
+from the scratch with ``fp_noalloc_device_error``) to be clear, and an oversized batch to be refused.
 The file is named so that pytest collects it last.
 """
 
@@ -62,6 +63,9 @@ def test_noalloc_matches_workspace_entry_point():
         assert e1 < BF16_TOL and e2 < BF16_TOL, f"call {call}: rel_l2 {e1:.3e}, max_rel {e2:.3e}"
         bad, _ = compare_routes(idx.cpu(), cnt.cpu(), idx_ref.cpu(), cnt_ref.cpu())
         assert bad == 0
+        # the call's bounded-wait error word, read from the library's scratch array: no wait ran out
+        code = ctypes.c_int(-1)
+        assert lib.fp_noalloc_device_error(stream, ctypes.byref(code)) == 0 and code.value == 0
 
 
 def test_noalloc_refuses_batches_beyond_its_scratch():
