@@ -5,15 +5,20 @@
 
 One step = one token-routed forward (router + selection + block CSR + gated contraction + additive
 stream) over one batch of the configuration's synthetic input (Llama-3-8B MLP shape by default:
-x [8, 2048, 4096] bf16, 224 blocks, base 4, top-p 0.8, K in [8, 56]).  With N > 1 (torchrun, one
-process per GPU) every rank processes its own batch with replicated weights: tokens are independent,
-so there is no collective and the scaling is weak.
+x [8, 2048, 4096] bf16, 224 blocks, base 4, top-p 0.8, K in [8, 56]).
 
-Prints one JSON line (rank 0): ``value`` = tokens/s over all ranks with inputs resident in HBM,
-timed with CUDA events around exactly K steps (max over ranks); ``e2e`` = the same through the public
-``FovealPattentionMLP.forward_host`` with the input copied from pinned host memory and the output
-copied back every step (copies overlapped with compute, chunk by chunk); ``roofline`` = the dominant kernel's algorithmic FLOP rate against the measured bf16
-peak; ``cpu_baseline`` = the CPU oracle on a token sample (rank 0, N = 1).
+N = 1: ``value`` = tokens/s with inputs resident in HBM, CUDA events around exactly K steps; ``e2e`` =
+the same through ``FovealPattentionMLP.forward_host_async`` with pinned host input and output every step;
+``roofline`` = the dominant kernel's useful FLOP rate against the measured bf16 peak (burst, or sustained
+when the clock record of the timed region shows the power cap); ``cpu_baseline`` = the CPU oracle on a
+token sample.  Extra keys timed in the same run: ``decode`` (config 3), ``sweep`` (config 5), ``70b``
+(config 4 on one GPU) and ``pooled`` (the reference's default pooled routing against its cuBLAS path).
+
+N > 1 (torchrun, one process per GPU, NCCL): one global batch of the configuration, parameter blocks
+sharded over the ranks and bf16 partial outputs reduce-scattered over token rows chunk by chunk (strong
+scaling, max over ranks); ``token_split`` (every rank its own batch, no collective), ``e2e`` from each
+rank's slice of the batch in pinned host memory, and ``blockshard_70b`` (the 70B configuration sharded,
+with its 1-GPU time measured by the same processes).
 
 ``--impl reference`` times the CPU restatement of the reference path (oracle/, all host threads) on a
 bounded token sample per step, on rank 0 only.
@@ -52,16 +57,18 @@ def parse():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="8b", help="8b (default) or 70b for the main measurement")
-    ap.add_argument("--mode", choices=["default", "decode", "sweep", "blockshard", "variants"], default="default",
-                    help="decode / sweep / variants print one JSON line per point instead of the bench line; "
-                         "blockshard (torchrun, >= 2 ranks) times the parameter-block-sharded forward of --config")
-    ap.add_argument("--chunks", type=int, default=1, help="blockshard: token chunks whose reduce-scatter "
-                    "overlaps the next chunk's compute")
+    ap.add_argument("--mode", choices=["default", "decode", "sweep", "pooled", "70b", "variants"], default="default",
+                    help="decode / sweep / pooled / 70b print one of the N = 1 line's extra keys alone; variants "
+                         "prints one JSON line per BlockSparseLinear / Tokenformer point")
     ap.add_argument("--e2e-steps", type=int, default=0)
     ap.add_argument("--chunk-tokens", type=int, default=4096)
     ap.add_argument("--cpu-sample", type=int, default=8192,
                     help="tokens of the CPU-baseline sample (about 10-30 s of host work over 3 timed calls)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the decode / sweep / 70B / pooled keys")
+    ap.add_argument("--shard-chunks", type=int, default=4, help="N > 1: token chunks of the block-sharded step")
+    ap.add_argument("--partial-dtype", choices=["bf16", "fp32"], default="bf16",
+                    help="N > 1: dtype of the partial outputs the reduce-scatter sums")
     return ap.parse_args()
 
 
@@ -108,13 +115,14 @@ def load_traffic():
     return {}
 
 
-def config_block(wl, world):
+def config_block(wl, world, parallelism, global_tokens=None):
     return {"workload": f"{wl.name}: token-routed Pattention MLP fwd", "model": "Llama-3-8B MLP shape"
-            if wl.name == "8b" else wl.name, "tokens_per_rank": wl.tokens, "batch": wl.batch,
+            if wl.name == "8b" else wl.name, "batch": wl.batch,
             "seq_len": wl.seq_len, "d_model": wl.hidden_dim, "param_tokens": wl.intermediate_dim,
             "blocks": wl.num_blocks, "base_blocks": wl.base_blocks, "top_p": wl.top_p,
             "k_min": wl.min_remote_blocks, "k_max": wl.max_remote_blocks, "routing": "token",
-            "global_batch_tokens": wl.tokens * world, "parallelism": f"token-split x{world} (no collective)",
+            "global_batch_tokens": wl.tokens if global_tokens is None else global_tokens,
+            "parallelism": parallelism,
             "l2": "inputs larger than L2: x 134 MB + weights 352 MB + activations 470 MB per step vs 126 MB L2"}
 
 
@@ -227,7 +235,7 @@ def run_reference(args):
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) x, N(0,0.02) weights)",
-        "impl": "reference", "config": config_block(wl, 1),
+        "impl": "reference", "config": config_block(wl, 1, "host CPU (oracle port, all threads)"),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
                          "cpu_model": cpu_model(),
                          "sample": f"{sample} tokens per step of the {wl.name} workload (oracle token_forward, "
@@ -238,6 +246,86 @@ def run_reference(args):
 
 
 # ------------------------------------------------------------------ our arm
+def make_module(wl, w, dev, routing="token", remote_blocks=None):
+    """bf16 module of workload ``wl`` on ``dev`` holding the values of ``w`` (CPU or device tensors)."""
+    m = fsi.FovealPattentionMLP(hidden_dim=wl.hidden_dim, intermediate_dim=wl.intermediate_dim,
+                                base_blocks=wl.base_blocks,
+                                remote_blocks=wl.max_remote_blocks if remote_blocks is None else remote_blocks,
+                                temperature=wl.temperature, dtype=torch.bfloat16, routing=routing, top_p=wl.top_p,
+                                min_remote_blocks=wl.min_remote_blocks, max_remote_blocks=wl.max_remote_blocks,
+                                device=dev)
+    with torch.no_grad():
+        for k, t in w.state_dict().items():
+            m.get_parameter(k).copy_(t.to(dev, torch.bfloat16))
+    return m.eval()
+
+
+def set_router(m, wl):
+    """Point a token-routed module at another workload's router settings (same weights)."""
+    m.top_p, m.min_remote_blocks, m.max_remote_blocks = wl.top_p, wl.min_remote_blocks, wl.max_remote_blocks
+
+
+def timed_steps(step, K, dev, world, clocks=None):
+    """K calls of ``step`` between a barrier + synchronize on both sides; CUDA events on the current stream.
+    Returns (ms over the K steps, max over ranks; clock record or None)."""
+    import torch.distributed as dist
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    if clocks is not None:
+        clocks.start()
+        time.sleep(0.3)  # let the sampler attach before the timed region
+    s0.record()
+    for _ in range(K):
+        step()
+    s1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop() if clocks is not None else None
+    t = s0.elapsed_time(s1)
+    if world > 1:
+        tt = torch.tensor([t], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t = float(tt.item())
+    return t, clk
+
+
+def mean_active(m, x):
+    """Mean active blocks per token (base + remote count) of one forward of ``x``."""
+    _, info = m(x, return_router_info=True)
+    return m.base_blocks + float(info["remote_counts"].float().mean())
+
+
+def roofline_block(stage, a_mean, M, D, clk, names=("route", "gateup", "down")):
+    """The dominant tensor-core kernel's useful FLOP rate against the bf16 peak."""
+    gu_flops = 4.0 * D * 64 * a_mean * M
+    dn_flops = 2.0 * D * 64 * a_mean * M
+    dom = "gateup" if stage["gateup"] >= stage["down"] else "down"
+    dom_flops = gu_flops if dom == "gateup" else dn_flops
+    achieved = dom_flops / (stage[dom] / 1e3) / 1e12
+    peak, note, peaks_all = tensor_peak(clk)
+    return {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+            "frac": achieved / peak, "traffic": load_traffic().get(f"8b_{dom}"), "peak_source": note,
+            "frac_both": {k: achieved / v for k, v in peaks_all.items()},
+            "algorithmic_flops_per_launch": dom_flops}, gu_flops + dn_flops, peak, peaks_all
+
+
+def stage_split(run, K=10):
+    """Mean CUDA-event stage times (ms) of ``run`` (one token-routed forward): route, gate/up, down."""
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(K)]
+    for row in ev:
+        for e in row:
+            e.record()
+    torch.cuda.synchronize()
+    for k in range(K):
+        fsi._lib.set_stage_events(ev[k])
+        run()
+    torch.cuda.synchronize()
+    fsi._lib.set_stage_events(None)
+    st = [statistics.mean(ev[k][i].elapsed_time(ev[k][i + 1]) for k in range(K)) for i in range(4)]
+    return {"route": st[0] + st[1], "gateup": st[2], "down": st[3]}
+
+
 def run_ours(args):
     import torch.distributed as dist
 
@@ -250,152 +338,354 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
+    if world > 1:
+        line = run_ours_sharded(args, rank, world, local, dev)
+        dist.barrier()
+        dist.destroy_process_group()
+    else:
+        line = run_ours_single(args, local, dev)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_ours_single(args, local, dev):
+    """N = 1: the token-routed forward of --config, device-resident and end to end, plus (unless
+    --no-extras) the decode, sparsity-sweep, 70B and pooled-routing figures of the other configurations,
+    each timed in this run."""
     wl = configs.CONFIGS[args.config]
     w = configs.make_weights(wl)
-    m = fsi.FovealPattentionMLP(hidden_dim=wl.hidden_dim, intermediate_dim=wl.intermediate_dim,
-                                base_blocks=wl.base_blocks, remote_blocks=wl.max_remote_blocks,
-                                temperature=wl.temperature, dtype=torch.bfloat16, routing="token", top_p=wl.top_p,
-                                min_remote_blocks=wl.min_remote_blocks, max_remote_blocks=wl.max_remote_blocks)
-    m.load_state_dict({k: t.to(torch.bfloat16) for k, t in w.state_dict().items()}, strict=False)
-    m = m.to(dev).eval()
-    x_cpu = configs.make_x(wl, seed=rank).reshape(-1, wl.hidden_dim)
+    m = make_module(wl, w, dev)
+    x_cpu = configs.make_x(wl).reshape(-1, wl.hidden_dim)
     x = x_cpu.to(dev, torch.bfloat16)
     M, D = x.shape
     kg, ku, v, packed, wq, k16, wout = m._weights()
     kw = dict(base_blocks=wl.base_blocks, top_p=wl.top_p, min_remote=wl.min_remote_blocks,
               max_remote=wl.max_remote_blocks, temperature=wl.temperature, additive=True)
-
-    def step(y_out):
-        fsi.kernels.token_forward(x, kg, ku, v, packed, wq, k16, wout, y=y_out, **kw)
-
     y = torch.empty(M, D, dtype=torch.bfloat16, device=dev)
+
+    def step():
+        fsi.kernels.token_forward(x, kg, ku, v, packed, wq, k16, wout, y=y, **kw)
+
+    K = args.steps
     with torch.no_grad():
         for _ in range(args.warmup):
-            step(y)
-        # mean active blocks per token of this workload (for the algorithmic FLOP count)
-        _, _, cnt, _ = fsi.kernels.token_forward(x, kg, ku, v, packed, wq, k16, wout, want_routes=True, **kw)
-        a_mean = wl.base_blocks + float(cnt.float().mean())
-        torch.cuda.synchronize()
-
-        K = args.steps
-        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(K)]
-        for row in ev:
-            for e in row:
-                e.record()
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        clocks = ClockSampler(gpu_smi_id(dev, local))
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        clocks.start()
-        time.sleep(0.3)  # let the sampler attach before the timed region
-        start.record()
-        for k in range(K):
-            fsi._lib.set_stage_events(ev[k])
-            step(y)
-        end.record()
-        torch.cuda.synchronize()
-        fsi._lib.set_stage_events(None)
-        clk = clocks.stop()
-        t_ms = start.elapsed_time(end)
-        if world > 1:
-            t = torch.tensor([t_ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            t_ms = float(t.item())
-        stage = [statistics.mean(ev[k][i].elapsed_time(ev[k][i + 1]) for k in range(K)) for i in range(4)]
-
+            step()
+        a_mean = mean_active(m, x)
+        t_ms, clk = timed_steps(step, K, dev, 1, ClockSampler(gpu_smi_id(dev, local)))
+        stage = stage_split(step)
         err = fsi._lib.device_error(fsi._lib.workspace(dev, 0))
+        e2e = measure_e2e_single(args, m, x_cpu, dev)
 
-        # e2e through the public API: pinned host input -> forward -> pinned host output, every step
-        E = args.e2e_steps or max(10, K // 10)
-        x_host = x_cpu.to(torch.bfloat16).pin_memory()
-        y_hosts = [torch.empty(M, D, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
-        cur = torch.cuda.current_stream(dev)
-
-        def e2e_step(k):
-            # pipelined batches: batch k+1's copy-in overlaps batch k's last chunks; the output buffer
-            # of batch k is reused by batch k+2 only after batch k's result is complete
-            y_host = y_hosts[k % 2]
-            if done[k % 2] is not None:
-                done[k % 2].synchronize()
-            _, done[k % 2] = m.forward_host_async(x_host, out=y_host, chunk_tokens=args.chunk_tokens)
-
-        done = [None, None]
-        for k in range(3):
-            e2e_step(k)
-        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        done = [None, None]
-        s2.record()
-        for k in range(E):
-            e2e_step(k)
-        for d_ in done:
-            if d_ is not None:
-                cur.wait_event(d_)
-        e2.record()
-        torch.cuda.synchronize()
-        e2_ms = s2.elapsed_time(e2)
-        if world > 1:
-            t = torch.tensor([e2_ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e2_ms = float(t.item())
-
-    value = world * M * K / (t_ms / 1e3)
     ms_step = t_ms / K
-    peak, peak_note, peaks_all = tensor_peak(clk)
-    gu_flops = 4.0 * D * 64 * a_mean * M
-    dn_flops = 2.0 * D * 64 * a_mean * M
-    # stage events: 0 start, 1 routed (block lists built in the same kernel), 2 = 1, 3 gate/up, 4 down
-    stage = [stage[0] + stage[1], 0.0, stage[2], stage[3]]
-    names = ["route", "lists", "gateup", "down"]
-    dom = 2 if stage[2] >= stage[3] else 3
-    dom_flops = gu_flops if dom == 2 else dn_flops
-    achieved = dom_flops / (stage[dom] / 1e3) / 1e12
-    traffic = load_traffic().get(f"{wl.name}_{names[dom]}")
-    total_flops = gu_flops + dn_flops
+    roof, total_flops, peak, peaks_all = roofline_block(stage, a_mean, M, D, clk)
     line = {
-        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
+        "metric": METRIC, "value": M * K / (t_ms / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": K,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) x, N(0,0.02) weights)",
-        "config": config_block(wl, world),
+        "config": config_block(wl, 1, "single GPU"),
         "tensor_peak_frac": total_flops / (ms_step / 1e3) / 1e12 / peak,
-        "tensor_peak_frac_both": {k: total_flops / (ms_step / 1e3) / 1e12 / v for k, v in peaks_all.items()},
+        "tensor_peak_frac_both": {k: total_flops / (ms_step / 1e3) / 1e12 / p_ for k, p_ in peaks_all.items()},
         "active_blocks_per_token": a_mean,
-        "stages_ms": {n: s for n, s in zip(names, stage) if n != "lists"},
-        "roofline": {"bound": "tensor", "kernel": names[dom], "achieved": achieved, "peak": peak,
-                     "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic, "peak_source": peak_note,
-                     "frac_both": {k: achieved / v for k, v in peaks_all.items()},
-                     "algorithmic_flops_per_launch": dom_flops},
-        "e2e": {"value": world * M * E / (e2_ms / 1e3), "unit": "tokens/s",
-                "h2d_bytes_per_step": M * D * 2, "d2h_bytes_per_step": M * D * 2,
-                "path": "FovealPattentionMLP.forward_host_async: pinned host x -> device -> pinned host y, "
-                        f"{args.chunk_tokens}-token chunks, copies overlapped with compute, consecutive "
-                        "batches pipelined"},
+        "stages_ms": stage,
+        "roofline": roof,
+        "e2e": e2e,
         "gpu_launches": KERNELS_PER_STEP * K,
         "clocks": clk,
         "device_error": err,
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if not args.no_extras:
+        with torch.no_grad():
+            line["decode"] = extra_decode(m, x, dev)
+            line["sweep"] = extra_sweep(m, x, dev)
+            line["pooled"] = extra_pooled(wl, m, x, dev)
+            del kg, ku, v, packed, wq, k16, wout
+            del m
+            fsi._lib.release_workspaces()
+            torch.cuda.empty_cache()
+            line["70b"] = extra_70b(args, dev)
+    if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_oracle_rate(wl, w, x_cpu, args.cpu_sample)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+    return line
+
+
+def measure_e2e_single(args, m, x_cpu, dev):
+    """The same forward through the public API with host buffers: pinned host x -> device -> pinned host y
+    every step (FovealPattentionMLP.forward_host_async, consecutive batches pipelined)."""
+    M, D = x_cpu.shape
+    E = args.e2e_steps or max(10, args.steps // 10)
+    x_host = x_cpu.to(torch.bfloat16).pin_memory()
+    y_hosts = [torch.empty(M, D, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    cur = torch.cuda.current_stream(dev)
+    done = [None, None]
+
+    def e2e_step(k):
+        # batch k+1's copy-in overlaps batch k's last chunks; batch k's output buffer is reused by batch
+        # k+2 only after batch k's result is complete
+        if done[k % 2] is not None:
+            done[k % 2].synchronize()
+        _, done[k % 2] = m.forward_host_async(x_host, out=y_hosts[k % 2], chunk_tokens=args.chunk_tokens)
+
+    for k in range(3):
+        e2e_step(k)
+    torch.cuda.synchronize()
+    done = [None, None]
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for k in range(E):
+        e2e_step(k)
+    for d_ in done:
+        if d_ is not None:
+            cur.wait_event(d_)
+    e2.record()
+    torch.cuda.synchronize()
+    e2_ms = s2.elapsed_time(e2)
+    return {"value": M * E / (e2_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": M * D * 2,
+            "d2h_bytes_per_step": M * D * 2, "steps": E,
+            "path": "FovealPattentionMLP.forward_host_async: pinned host x -> device -> pinned host y, "
+                    f"{args.chunk_tokens}-token chunks, copies overlapped with compute, consecutive batches "
+                    "pipelined"}
+
+
+# ------------------------------------------------------------------ the other configurations (N = 1)
+def extra_decode(m, x8, dev):
+    """Config 3: 64 decode tokens (the first 64 rows of the 8B input, the same weights), top-p 0.9,
+    K_max 8 / 16 / 32.  p50 per call, eager and replayed from a CUDA graph, and GB/s of the blocks the
+    call touches (gate, up and v rows) plus x and y, against the measured HBM copy bandwidth."""
+    peaks, _ = load_peaks()
+    x = x8[:64].contiguous()
+    out = []
+    for wl in configs.decode_points():
+        set_router(m, wl)
+        _, info = m(x, return_router_info=True)
+        cnt, idx = info["remote_counts"], info["remote_indices"]
+        used = torch.zeros(wl.num_blocks, dtype=torch.bool, device=dev)
+        used[:wl.base_blocks] = True
+        used[idx.long().masked_fill(torch.arange(idx.shape[1], device=dev)[None] >= cnt[:, None].long(), 0)] = True
+        nb = int(used.sum())
+        ts = _time_calls(lambda: m(x), 100)
+        gs = torch.cuda.Stream(dev)
+        gs.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(gs):
+            for _ in range(3):
+                m(x)
+        torch.cuda.current_stream(dev).wait_stream(gs)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            m(x)
+        tg = _time_calls(graph.replay, 100)
+        del graph
+        D = wl.hidden_dim
+        alg_bytes = 3 * 64 * D * 2 * nb + 2 * x.numel() * 2
+        p50, g50 = ts[len(ts) // 2], tg[len(tg) // 2]
+        out.append({"k_max": wl.max_remote_blocks, "p50_ms": round(p50, 5), "graph_p50_ms": round(g50, 5),
+                    "blocks_touched": nb, "GBps": round(alg_bytes / (g50 / 1e3) / 1e9, 1),
+                    "hbm_frac": round(alg_bytes / (g50 / 1e3) / 1e9 / peaks["hbm_gbs"], 3)})
+    set_router(m, configs.CONFIGS["8b"])
+    return {"tokens": 64, "top_p": 0.9, "points": out,
+            "bytes": "gate, up and v rows of the touched blocks + x + y (graph p50)"}
+
+
+def extra_sweep(m, x, dev):
+    """Config 5 (x [4, 4096, 4096]: the same 16384 rows and weights as the 8B input): tokens/s of the
+    token-routed forward at every (top_p, K_max) point and its speed-up over the dense SwiGLU (all 224
+    blocks) through this library's kernels and through cuBLAS (torch)."""
+    import torch.nn.functional as F
+    kg, ku, v, packed, *_ = m._weights()
+    active = torch.arange(m.num_blocks, dtype=torch.int32, device=dev)
+    d_ours = _median(_time_calls(lambda: fsi.kernels.pooled_forward(x, kg, ku, v, packed, active), 10))
+    d_cublas = _median(_time_calls(lambda: F.linear(F.silu(F.linear(x, kg)) * F.linear(x, ku), v.t()), 10))
+    pts = []
+    for wl in configs.sweep_points():
+        set_router(m, wl)
+        a = mean_active(m, x)
+        t = _median(_time_calls(lambda: m(x), 10))
+        pts.append([wl.top_p, wl.max_remote_blocks, round(a, 1), round(x.shape[0] / (t / 1e3) / 1e6, 3),
+                    round(d_ours / t, 2), round(d_cublas / t, 2)])
+    set_router(m, configs.CONFIGS["8b"])
+    return {"columns": ["top_p", "k_max", "active_blocks_per_token", "Mtokens_per_s", "x_dense_same_kernels",
+                        "x_dense_cublas"], "points": pts, "dense_ms_same_kernels": round(d_ours, 4),
+            "dense_ms_cublas": round(d_cublas, 4)}
+
+
+def extra_pooled(wl, m_tok, x, dev):
+    """The reference's default routing (pooled, eval: one active set of base 4 + 20 remote blocks, cached)
+    at the 8B shape, against the reference's own GPU execution of that path restated with torch (the
+    cached active rows gathered once, then two cuBLAS projections, SiLU * up, and the cuBLAS down
+    projection; foveal_pattention.py:278-288 / :329-335, its Triton SwiGLU replaced by torch
+    elementwise)."""
+    import torch.nn.functional as F
+    mp_ = fsi.FovealPattentionMLP(hidden_dim=wl.hidden_dim, intermediate_dim=wl.intermediate_dim,
+                                  base_blocks=4, remote_blocks=20, dtype=torch.bfloat16, device=dev).eval()
+    with torch.no_grad():
+        for k in ("k_gate", "k_up", "v", "q_proj_16d.weight", "block_keys_16d", "out_proj_16d.weight"):
+            mp_.get_parameter(k).copy_(m_tok.get_parameter(k))
+    x3 = x.view(8, -1, wl.hidden_dim)
+    mp_(x3)  # routes once on the pooled query and caches the active set
+    t_ours = _median(_time_calls(lambda: mp_(x3), 20))
+    idx = (mp_._cached_active_blocks.long()[:, None] * 64 + torch.arange(64, device=dev)).flatten()
+    kg_a, ku_a, v_a = (mp_.k_gate[idx].detach().contiguous(), mp_.k_up[idx].detach().contiguous(),
+                       mp_.v[idx].detach().contiguous())
+    t_ref = _median(_time_calls(lambda: F.linear(F.silu(F.linear(x, kg_a)) * F.linear(x, ku_a), v_a.t()), 20))
+    flops = 6.0 * wl.hidden_dim * 64 * 24 * x.shape[0]
+    return {"active_blocks": 24, "tokens": x.shape[0], "ms": round(t_ours, 4), "tflops": round(flops / t_ours / 1e9, 1),
+            "reference_gpu_path_ms": round(t_ref, 4), "speedup_vs_reference_gpu_path": round(t_ref / t_ours, 3)}
+
+
+def extra_70b(args, dev):
+    """Config 4 on one GPU: x [4, 4096, 8192], 448 blocks, top-p 0.8, K in [16, 112] (weights and x drawn
+    on the device)."""
+    wl = configs.CONFIGS["70b"]
+    w = configs.make_weights(wl, device=dev)
+    m = make_module(wl, w, dev)
+    del w
+    x = configs.make_x(wl, device=dev).reshape(-1, wl.hidden_dim).to(torch.bfloat16)
+    for _ in range(3):
+        m(x)
+    a = mean_active(m, x)
+    t = _median(_time_calls(lambda: m(x), 10, warm=2))
+    st = stage_split(lambda: m(x), K=3)
+    flops = 6.0 * wl.hidden_dim * 64 * a * x.shape[0]
+    peak, _, _ = tensor_peak(None)
+    out = {"tokens": x.shape[0], "ms": round(t, 4), "tokens_per_s": x.shape[0] / (t / 1e3),
+           "active_blocks_per_token": a, "stages_ms": {k: round(v_, 4) for k, v_ in st.items()},
+           "tensor_peak_frac_burst": round(flops / (t / 1e3) / 1e12 / peak, 4)}
+    del m
+    fsi._lib.release_workspaces()
+    torch.cuda.empty_cache()
+    return out
+
+
+def _median(ts):
+    return ts[len(ts) // 2]
+
+
+# ------------------------------------------------------------------ N > 1
+def run_ours_sharded(args, rank, world, local, dev):
+    """N > 1: the 8B configuration's one global batch of 16384 tokens, parameter blocks sharded over the
+    ranks (b % N) and the partials reduce-scattered over token rows with NCCL (bf16 partials, token
+    chunks whose collective overlaps the next chunk's compute); strong scaling.  Extra keys: the token
+    split (every rank its own batch, no collective), the same block-sharded forward end to end from each
+    rank's slice of the batch in host memory, and the 70B configuration block-sharded with its 1-GPU
+    time measured by the same processes."""
+    import torch.distributed as dist
+    wl = configs.CONFIGS[args.config]
+    pd = torch.bfloat16 if args.partial_dtype == "bf16" else torch.float32
+    w = configs.make_weights(wl)
+    m = make_module(wl, w, dev)
+    x_cpu = configs.make_x(wl).reshape(-1, wl.hidden_dim)
+    x = x_cpu.to(dev, torch.bfloat16)  # replicated on every rank
+    M, D = x.shape
+    K, ch = args.steps, args.shard_chunks
+    with torch.no_grad():
+        a_mean = mean_active(m, x)
+        # token split: every rank its own batch (drawn on the device), replicated weights, no collective
+        x_own = configs.make_x(wl, seed=1000 + rank, device=dev).reshape(-1, wl.hidden_dim).to(torch.bfloat16)
+        for _ in range(args.warmup):
+            m(x_own)
+        t_split, _ = timed_steps(lambda: m(x_own), K, dev, world)
+        del x_own
+        # block sharding
+        fsi.sharding.shard_parameter_blocks(m, partial_dtype=pd)
+
+        def step():
+            fsi.sharding.sharded_token_forward(m, x, reduce="scatter", chunks=ch)
+
+        for _ in range(args.warmup):
+            step()
+        t_ms, clk = timed_steps(step, K, dev, world, ClockSampler(gpu_smi_id(dev, local)))
+        # where the time goes on this rank: the shard's kernels for the whole batch in one piece (routing is
+        # replicated on every rank), and the reduce-scatter alone
+        stage = stage_split(lambda: fsi.sharding._cuda_partial(m, x, world, rank, rank == 0, False))
+        part = torch.empty(M, D, dtype=pd, device=dev)
+        ys = torch.empty(M // world, D, dtype=pd, device=dev)
+        t_rs, _ = timed_steps(lambda: dist.reduce_scatter_tensor(ys, part), 10, dev, world)
+        err = fsi._lib.device_error(fsi._lib.workspace(dev, 0))
+        e2e = measure_e2e_sharded(args, m, x_cpu, rank, world, dev)
+        del m, x, part, ys
+        fsi._lib.release_workspaces()
+        torch.cuda.empty_cache()
+        bs70 = None if args.no_extras else blockshard_70b(args, rank, world, dev, pd)
+    ms_step = t_ms / K
+    roof, total_flops, peak, peaks_all = roofline_block(stage, a_mean, M, D, clk)
+    roof["note"] = ("per rank: the shard's kernels over all tokens; useful FLOPs = this rank's 1/N share of the "
+                    "active-block FLOPs")
+    for key in ("achieved", "frac"):
+        roof[key] /= world
+    roof["frac_both"] = {k: v_ / world for k, v_ in roof["frac_both"].items()}
+    roof["algorithmic_flops_per_launch"] /= world
+    line = {
+        "metric": METRIC, "value": M * K / (t_ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) x, N(0,0.02) weights)",
+        "config": config_block(wl, world, f"parameter blocks sharded b % {world} + NCCL reduce-scatter of "
+                                          f"{args.partial_dtype} partials, {ch} token chunks overlapped",
+                               global_tokens=M),
+        "tensor_peak_frac": total_flops / (ms_step / 1e3) / 1e12 / (peak * world),
+        "active_blocks_per_token": a_mean,
+        "stages_ms_rank0_unchunked": stage,
+        "reduce_scatter_ms": t_rs / 10, "collective_bytes_per_rank": M * D * (2 if pd == torch.bfloat16 else 4),
+        "roofline": roof,
+        "e2e": e2e,
+        "token_split": {"value": world * M * K / (t_split / 1e3), "unit": "tokens/s", "scaling": "weak",
+                        "ms_per_step": t_split / K, "tokens_per_rank": M,
+                        "parallelism": f"token split x{world} (no collective)"},
+        "gpu_launches": KERNELS_PER_STEP * ch * K,
+        "clocks": clk,
+        "device_error": err,
+    }
+    if bs70 is not None:
+        line["blockshard_70b"] = bs70
+    return line
+
+
+def measure_e2e_sharded(args, m, x_cpu, rank, world, dev):
+    """Block-sharded forward end to end: every rank starts from its own slice of the batch in pinned host
+    memory and ends with its output rows in pinned host memory (sharding.sharded_forward_host: copy-in,
+    NVLink all-gather, shard compute, reduce-scatter, copy-out, chunk by chunk)."""
+    M, D = x_cpu.shape
+    s = M // world
+    x_host = x_cpu[rank * s:(rank + 1) * s].to(torch.bfloat16).pin_memory()
+    y_host = torch.empty(s, D, dtype=torch.bfloat16).pin_memory()
+    E = args.e2e_steps or max(10, args.steps // 10)
+    step = lambda: fsi.sharding.sharded_forward_host(m, x_host, out=y_host, chunks=args.shard_chunks)  # noqa: E731
+    for _ in range(3):
+        step()
+    t, _ = timed_steps(step, E, dev, world)
+    return {"value": M * E / (t / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": M * D * 2,
+            "d2h_bytes_per_step": M * D * 2, "steps": E, "bytes_note": "summed over ranks (each copies its slice)",
+            "path": "sharding.sharded_forward_host: each rank's slice from pinned host memory, NVLink all-gather, "
+                    "shard compute, reduce-scatter, pinned host output slice"}
+
+
+def blockshard_70b(args, rank, world, dev, pd):
+    """70B configuration (x [4, 4096, 8192], 448 blocks): 1-GPU time (every rank runs the unsharded forward
+    on its own GPU at the same time; max over ranks) and the block-sharded time; efficiency =
+    t_1 / (N * t_N)."""
+    wl = configs.CONFIGS["70b"]
+    w = configs.make_weights(wl, device=dev)
+    m = make_module(wl, w, dev)
+    del w
+    x = configs.make_x(wl, device=dev).reshape(-1, wl.hidden_dim).to(torch.bfloat16)
+    K = max(5, min(args.steps, 20))
+    for _ in range(3):
+        m(x)
+    t1, _ = timed_steps(lambda: m(x), K, dev, world)
+    fsi.sharding.shard_parameter_blocks(m, partial_dtype=pd)
+    step = lambda: fsi.sharding.sharded_token_forward(m, x, reduce="scatter", chunks=args.shard_chunks)  # noqa: E731
+    for _ in range(3):
+        step()
+    tn, _ = timed_steps(step, K, dev, world)
+    M = x.shape[0]
+    out = {"tokens": M, "value": M * K / (tn / 1e3), "unit": "tokens/s", "ms_per_step": tn / K,
+           "one_gpu_ms_per_step": t1 / K, "efficiency": (t1 / K) / (world * tn / K),
+           "speedup": t1 / tn}
+    del m, x
+    fsi._lib.release_workspaces()
+    torch.cuda.empty_cache()
+    return out
 
 
 # ------------------------------------------------------------------ extra measurement modes
-def _module_for(wl, w, dev):
-    m = fsi.FovealPattentionMLP(hidden_dim=wl.hidden_dim, intermediate_dim=wl.intermediate_dim,
-                                base_blocks=wl.base_blocks, remote_blocks=wl.max_remote_blocks,
-                                temperature=wl.temperature, dtype=torch.bfloat16, routing="token", top_p=wl.top_p,
-                                min_remote_blocks=wl.min_remote_blocks, max_remote_blocks=wl.max_remote_blocks)
-    m.load_state_dict({k: t.to(torch.bfloat16) for k, t in w.state_dict().items()}, strict=False)
-    return m.to(dev).eval()
-
-
 def _time_calls(fn, n, warm=5):
     for _ in range(warm):
         fn()
@@ -409,78 +699,20 @@ def _time_calls(fn, n, warm=5):
     return sorted(a.elapsed_time(b) for a, b in ev)
 
 
-def run_decode(args):
-    """Decode step (64 tokens, 8B shape), K_max in {8, 16, 32}: p50 latency per call and GB/s."""
+def run_extra_mode(args):
+    """--mode decode / sweep / pooled / 70b: one of the N = 1 line's extra keys on its own."""
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    peaks, src = load_peaks()
-    for wl in configs.decode_points():
-        w = configs.make_weights(wl)
-        m = _module_for(wl, w, dev)
-        x = configs.make_x(wl).reshape(-1, wl.hidden_dim).to(dev, torch.bfloat16)
-        with torch.no_grad():
-            _, info = m(x, return_router_info=True)
-            cnt, idx = info["remote_counts"], info["remote_indices"]
-            used = torch.zeros(wl.num_blocks, dtype=torch.bool, device=dev)
-            used[:wl.base_blocks] = True
-            for t in range(x.shape[0]):
-                used[idx[t, :int(cnt[t])].long()] = True
-            nb = int(used.sum())
-            ts = _time_calls(lambda: m(x), 200)
-            # the same call captured once in a CUDA graph and replayed (how a decode loop runs it)
-            gs = torch.cuda.Stream(dev)
-            gs.wait_stream(torch.cuda.current_stream(dev))
-            with torch.cuda.stream(gs):
-                for _ in range(3):
-                    m(x)
-            torch.cuda.current_stream(dev).wait_stream(gs)
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                m(x)
-            tg = _time_calls(graph.replay, 200)
-            del graph
-        p50 = ts[len(ts) // 2]
-        g50 = tg[len(tg) // 2]
-        D = wl.hidden_dim
-        alg_bytes = 3 * 64 * D * 2 * nb + 2 * x.numel() * 2          # touched blocks (gate, up, v) + x + y
-        moved = (2 * 64 * D * 2 * nb) + wl.intermediate_dim * D * 2 + 2 * x.numel() * 2  # v_t read whole
-        print(json.dumps({"mode": "decode", "config": wl.name, "tokens": x.shape[0], "k_max": wl.max_remote_blocks,
-                          "p50_ms": p50, "p10_ms": ts[len(ts) // 10], "p90_ms": ts[9 * len(ts) // 10],
-                          "graph_p50_ms": g50, "graph_tokens_per_s": x.shape[0] / (g50 / 1e3),
-                          "graph_algorithmic_GBps": alg_bytes / (g50 / 1e3) / 1e9,
-                          "tokens_per_s": x.shape[0] / (p50 / 1e3), "blocks_touched": nb,
-                          "algorithmic_GBps": alg_bytes / (p50 / 1e3) / 1e9,
-                          "moved_GBps": moved / (p50 / 1e3) / 1e9, "hbm_peak_GBps": peaks["hbm_gbs"]}), flush=True)
-
-
-def run_sweep(args):
-    """Sparsity sweep (x [4, 4096, 4096], 8B shape): tokens/s per (top_p, K_max) and the speedup over
-    the dense SwiGLU equivalent (all 224 blocks, same kernels; and cuBLAS through torch)."""
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    pts = configs.sweep_points()
-    w = configs.make_weights(pts[0])
-    x = configs.make_x(pts[0]).reshape(-1, pts[0].hidden_dim).to(dev, torch.bfloat16)
-    M = x.shape[0]
     with torch.no_grad():
-        m = _module_for(pts[0], w, dev)
-        kg, ku, v, packed, wq, k16, wout = m._weights()
-        active = torch.arange(pts[0].num_blocks, dtype=torch.int32, device=dev)
-        dense_ours = _time_calls(lambda: fsi.kernels.pooled_forward(x, kg, ku, v, packed, active), 10)
-        import torch.nn.functional as F
-        dense_torch = _time_calls(lambda: F.linear(F.silu(F.linear(x, kg)) * F.linear(x, ku), v.t()), 10)
-        d_ours, d_torch = dense_ours[len(dense_ours) // 2], dense_torch[len(dense_torch) // 2]
-        for wl in pts:
-            mm = _module_for(wl, w, dev)
-            _, info = mm(x, return_router_info=True)
-            a_mean = wl.base_blocks + float(info["remote_counts"].float().mean())
-            ts = _time_calls(lambda: mm(x), 10)
-            t = ts[len(ts) // 2]
-            print(json.dumps({"mode": "sweep", "top_p": wl.top_p, "k_max": wl.max_remote_blocks,
-                              "active_blocks_per_token": a_mean, "active_fraction": a_mean / wl.num_blocks,
-                              "ms": t, "tokens_per_s": M / (t / 1e3),
-                              "speedup_vs_dense_same_kernels": d_ours / t, "speedup_vs_dense_cublas": d_torch / t,
-                              "dense_ms_same_kernels": d_ours, "dense_ms_cublas": d_torch}), flush=True)
+        if args.mode == "70b":
+            out = extra_70b(args, dev)
+        else:
+            wl = configs.CONFIGS["8b"]
+            m = make_module(wl, configs.make_weights(wl), dev)
+            x = configs.make_x(wl).reshape(-1, wl.hidden_dim).to(dev, torch.bfloat16)
+            out = {"decode": extra_decode, "sweep": extra_sweep,
+                   "pooled": lambda m_, x_, d_: extra_pooled(wl, m_, x_, d_)}[args.mode](m, x, dev)
+    print(json.dumps({"mode": args.mode, **out}), flush=True)
 
 
 def _variant_module(case, dev):
@@ -590,82 +822,12 @@ def run_variants(args):
                 "sample": "64 tokens, oracle (fp32 torch CPU) incl. block keys"}}), flush=True)
 
 
-def run_blockshard(args):
-    """Parameter-block sharding (strong scaling): every rank holds the same batch, computes the blocks
-    b % world == rank, and the fp32 partials are reduce-scattered over token rows chunk by chunk (NCCL on
-    a side stream, overlapping the next chunk's compute).  One JSON line: tokens/s of the whole batch
-    (max over ranks), and the same forward without the collectives for reference."""
-    import torch.distributed as dist
-
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world < 2:
-        raise SystemExit("--mode blockshard needs torchrun with at least 2 ranks")
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-    wl = configs.CONFIGS[args.config if args.config != "8b" else "70b"]
-    w = configs.make_weights(wl)
-    m = fsi.FovealPattentionMLP(hidden_dim=wl.hidden_dim, intermediate_dim=wl.intermediate_dim,
-                                base_blocks=wl.base_blocks, remote_blocks=wl.max_remote_blocks,
-                                temperature=wl.temperature, dtype=torch.bfloat16, routing="token", top_p=wl.top_p,
-                                min_remote_blocks=wl.min_remote_blocks, max_remote_blocks=wl.max_remote_blocks)
-    m.load_state_dict({k: t.to(torch.bfloat16) for k, t in w.state_dict().items()}, strict=False)
-    m = m.to(dev).eval()
-    fsi.sharding.shard_parameter_blocks(m)
-    x = configs.make_x(wl).reshape(-1, wl.hidden_dim).to(dev, torch.bfloat16)
-    M, D = x.shape
-    chunks = max(1, args.chunks)
-
-    def step():
-        fsi.sharding.sharded_token_forward(m, x, reduce="scatter", chunks=chunks)
-
-    def compute_only():
-        fsi.sharding._cuda_partial(m, x, world, rank, rank == 0, False)
-
-    def timed(fn, K):
-        dist.barrier()
-        torch.cuda.synchronize()
-        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s0.record()
-        for _ in range(K):
-            fn()
-        s1.record()
-        torch.cuda.synchronize()
-        t = torch.tensor([s0.elapsed_time(s1) / K], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    with torch.no_grad():
-        for _ in range(max(3, args.warmup)):
-            step()
-            compute_only()
-        ms = timed(step, args.steps)
-        ms_compute = timed(compute_only, args.steps)
-    if rank == 0:
-        line = {"mode": "blockshard", "metric": METRIC, "value": M / (ms / 1e3), "unit": "tokens/s",
-                "n_gpus": world, "steps": args.steps, "ms_per_step": ms, "scaling": "strong",
-                "higher_is_better": True, "dtype": "bf16", "data": "synthetic (seeded)",
-                "config": {"workload": f"{wl.name}: token-routed forward, parameter blocks sharded b % {world}",
-                           "tokens": M, "d_model": D, "blocks": wl.num_blocks, "chunks": chunks,
-                           "parallelism": f"block-shard x{world} + NCCL reduce-scatter (fp32 partials)"},
-                "compute_only_ms": ms_compute,
-                "collective_bytes_per_rank": M * D * 4}
-        print(json.dumps(line), flush=True)
-    dist.destroy_process_group()
-
-
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
-    elif args.mode == "decode":
-        run_decode(args)
-    elif args.mode == "sweep":
-        run_sweep(args)
-    elif args.mode == "blockshard":
-        run_blockshard(args)
+    elif args.mode in ("decode", "sweep", "pooled", "70b"):
+        run_extra_mode(args)
     elif args.mode == "variants":
         run_variants(args)
     else:

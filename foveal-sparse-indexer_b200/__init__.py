@@ -6,6 +6,8 @@ Public API (same names as the reference package ``foveal_indexer``):
     FovealIndexer, Route, select_blocks, masked_softmax           (foveal_indexer/core.py)
     BlockSparseLinear                                             (foveal_indexer/block_matmul.py)
     FovealTokenformerLinear, FovealTokenformerFFN                 (foveal_indexer/tokenformer.py)
+    triton_pattention, triton_fused_swiglu, TritonFusedSwiGLUFunction,
+    TritonSwiGLUPattentionMLP, convert_llm_mlp_to_pattention      (foveal_indexer/pattention_triton.py)
 
 Compute runs in ``libfovealpatt.so`` (hand-written sm_100a CUDA behind the C ABI of
 ``include/foveal_pattention.h``); build it with ``build.py``.  The directory name contains hyphens: with
@@ -15,11 +17,13 @@ name at the root binds to this package), as does ``importlib.import_module("fove
 
 import sys as _sys
 
-from . import block_matmul, configs, kernels, sharding, tokenformer
+from . import block_matmul, configs, kernels, pattention, sharding, tokenformer
 from ._lib import LIB_PATH, FovealKernelError, load as load_library
 from .block_matmul import BlockSparseLinear
 from .core import FovealIndexer, Route, masked_softmax, select_blocks
 from .foveal_pattention import FovealPattentionMLP, sparsify_model_with_foveal_pattention
+from .pattention import (TritonFusedSwiGLUFunction, TritonSwiGLUPattentionMLP, convert_llm_mlp_to_pattention,
+                         triton_fused_swiglu, triton_pattention)
 from .tokenformer import FovealTokenformerFFN, FovealTokenformerLinear
 
 _sys.modules.setdefault("foveal_sparse_indexer_b200", _sys.modules[__name__])
@@ -34,10 +38,16 @@ __all__ = [
     "BlockSparseLinear",
     "FovealTokenformerLinear",
     "FovealTokenformerFFN",
+    "triton_pattention",
+    "triton_fused_swiglu",
+    "TritonFusedSwiGLUFunction",
+    "TritonSwiGLUPattentionMLP",
+    "convert_llm_mlp_to_pattention",
     "FovealKernelError",
     "LIB_PATH",
     "load_library",
     "configs",
     "kernels",
+    "pattention",
     "sharding",
 ]

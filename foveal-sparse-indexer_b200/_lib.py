@@ -61,6 +61,11 @@ SIGNATURES = {
     "fp_set_stage_events": (_c_int, [ctypes.POINTER(_c_p), _c_int]),
     "fp_device_error": (_c_int, [_c_p, _c_p, _c_p]),
     "fp_noalloc_device_error": (_c_int, [_c_p, _c_p]),
+    "fp_pack_pattention_weights": (_c_int, [_c_p, _c_p, _c_p, _c_int, _c_int, _c_int, _c_int, _c_p, _c_p, _c_p]),
+    "fp_pattention_workspace_size": (_c_sz, [_c_int, _c_i64, _c_int, _c_int, _c_int, _c_int]),
+    "fp_pattention_fwd": (_c_int, [_c_p, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_p, _c_p, _c_p, _c_p, _c_p,
+                                   _c_p, _c_int, _c_int, _c_p, _c_p, _c_sz, _c_p]),
+    "fp_swiglu_fwd": (_c_int, [_c_p, _c_p, _c_int, _c_i64, _c_p, _c_p]),
 }
 
 _lock = threading.Lock()

@@ -151,20 +151,23 @@ def _round(t: torch.Tensor, dtype: str) -> torch.Tensor:
     return t if dtype == "fp32" else t.to(torch.bfloat16).to(torch.float32)
 
 
-def make_weights(w: Workload, seed: int = 0) -> Weights:
-    g = torch.Generator().manual_seed(seed)
+def make_weights(w: Workload, seed: int = 0, device=None) -> Weights:
+    """Seeded weights.  ``device="cuda"`` draws them on the GPU with a CUDA generator (same distributions
+    and draw order, different values than the CPU generator; used by the benchmark for the large shapes,
+    where drawing on the host would take most of the run)."""
+    g = torch.Generator(device=device or "cpu").manual_seed(seed)
     D, Np, NB = w.hidden_dim, w.intermediate_dim, w.num_blocks
 
     def draw(*shape):
-        return _round(torch.randn(*shape, generator=g) * WEIGHT_STD, w.dtype)
+        return _round(torch.randn(*shape, generator=g, device=device) * WEIGHT_STD, w.dtype)
 
     return Weights(draw(Np, D), draw(Np, D), draw(Np, D), draw(INDEX_DIM, D),
                    draw(NB, INDEX_DIM), draw(D, INDEX_DIM))
 
 
-def make_x(w: Workload, seed: int = 0) -> torch.Tensor:
-    g = torch.Generator().manual_seed(seed + 1)
-    return _round(torch.randn(w.batch, w.seq_len, w.hidden_dim, generator=g), w.dtype)
+def make_x(w: Workload, seed: int = 0, device=None) -> torch.Tensor:
+    g = torch.Generator(device=device or "cpu").manual_seed(seed + 1)
+    return _round(torch.randn(w.batch, w.seq_len, w.hidden_dim, generator=g, device=device), w.dtype)
 
 
 # ---------------------------------------------------------------------------------------------------
@@ -232,3 +235,55 @@ def variant_params(module, seed: int = 0, dtype: str = "fp32") -> Dict[str, torc
 def variant_x(case: dict, seed: int = 0, dtype: str = "fp32") -> torch.Tensor:
     g = torch.Generator().manual_seed(seed + 12)
     return _round(torch.randn(case["x_shape"], generator=g), dtype)
+
+
+# ---------------------------------------------------------------------------------------------------
+# Function-level Pattention (``triton_pattention(x, k_gate, v, k_up, active_blocks, activation)``,
+# pattention_triton.py:204-311): one shared active-block list for every token, five activations, the
+# gated (SwiGLU, k_up given) and non-gated forms, D_out different from the input width.  Tensors are
+# drawn from a generator seeded with ``seed + 21``: x ~ N(0, 1), k_gate / k_up ~ N(0, K^-0.5),
+# v ~ N(0, N_p^-0.5); "tc" cases have tensor-core shapes (K, D_out multiples of 64).
+# ---------------------------------------------------------------------------------------------------
+PATTENTION_CASES: Dict[str, dict] = {
+    "swiglu_sparse": dict(M=21, K=256, Np=512, D_out=256, activation="swiglu", gated=True, active=[0, 3, 5]),
+    "swiglu_dense": dict(M=21, K=256, Np=512, D_out=256, activation="swiglu", gated=True, active=None),
+    "silu": dict(M=33, K=256, Np=512, D_out=192, activation="silu", gated=False, active=[1, 2, 7]),
+    "gelu": dict(M=33, K=256, Np=512, D_out=192, activation="gelu", gated=False, active=[6, 0, 4]),
+    "relu": dict(M=33, K=256, Np=512, D_out=192, activation="relu", gated=False, active=[2, 3]),
+    "relu2": dict(M=33, K=256, Np=512, D_out=192, activation="relu2", gated=False, active=None),
+    "gelu_kup_unused": dict(M=9, K=256, Np=512, D_out=256, activation="gelu", gated=True, active=[5, 1]),
+    "odd_width": dict(M=17, K=200, Np=256, D_out=136, activation="swiglu", gated=True, active=[3, 1]),
+    "swiglu_tc": dict(M=300, K=512, Np=1024, D_out=320, activation="swiglu", gated=True,
+                      active=[0, 2, 3, 9, 10, 11, 15]),
+    "relu2_tc": dict(M=272, K=512, Np=1024, D_out=192, activation="relu2", gated=False, active=None),
+    "silu_tc": dict(M=260, K=384, Np=768, D_out=256, activation="silu", gated=False, active=[11, 4, 7, 0]),
+}
+# dtypes with golden outputs per case: the tensor-core shapes only in bf16 (fp32 runs on CUDA cores)
+PATTENTION_DTYPES = {k: (("bf16",) if k.endswith("_tc") else ("fp32", "bf16")) for k in PATTENTION_CASES}
+
+
+def pattention_tensors(case: dict, seed: int = 0, dtype: str = "fp32"):
+    """(x [M, K], k_gate [Np, K], k_up [Np, K] or None, v [Np, D_out], active int64 or None) of a case."""
+    g = torch.Generator().manual_seed(seed + 21)
+    M, K, Np, Do = case["M"], case["K"], case["Np"], case["D_out"]
+    x = _round(torch.randn(M, K, generator=g), dtype)
+    kg = _round(torch.randn(Np, K, generator=g) * K ** -0.5, dtype)
+    ku = _round(torch.randn(Np, K, generator=g) * K ** -0.5, dtype)
+    v = _round(torch.randn(Np, Do, generator=g) * Np ** -0.5, dtype)
+    act = None if case["active"] is None else torch.tensor(case["active"], dtype=torch.int64)
+    return x, kg, (ku if case["gated"] else None), v, act
+
+
+# A dense SwiGLU MLP converted by TritonSwiGLUPattentionMLP.from_dense_mlp (pattention_triton.py:348-368)
+PATTENTION_MLP = dict(hidden=256, intermediate=512, x_shape=(2, 5, 256), active=[1, 2, 6])
+
+
+def pattention_mlp_weights(seed: int = 0):
+    """(gate_proj, up_proj, down_proj) weights of the dense MLP (nn.Linear layout) and x."""
+    g = torch.Generator().manual_seed(seed + 23)
+    h, i = PATTENTION_MLP["hidden"], PATTENTION_MLP["intermediate"]
+    wg = torch.randn(i, h, generator=g) * h ** -0.5
+    wu = torch.randn(i, h, generator=g) * h ** -0.5
+    wd = torch.randn(h, i, generator=g) * i ** -0.5
+    x = torch.randn(*PATTENTION_MLP["x_shape"], generator=g)
+    return wg, wu, wd, x

@@ -381,6 +381,104 @@ int fp_pattention_pooled_fwd(const void* x, int64_t M, int D, int NB, int dtype,
   return FP_OK;
 }
 
+// ---------------------------------------------------------------- function-level Pattention
+namespace {
+struct SharedLayout {
+  size_t err, act, h, yacc, total;
+  int ksplit;
+  bool tc;
+};
+
+// Workspace of fp_pattention_fwd: error word, the all-blocks id list (active = NULL), and for the
+// tensor-core path the activations H [M, n_active * 64] and the split-K partials of small batches.
+SharedLayout shared_layout(int dtype, int64_t M, int K, int Do, int NB, int n_active) {
+  SharedLayout L{};
+  Carve c;
+  L.err = c.take(256);
+  L.act = c.take((size_t)std::max(NB, 1) * 4);
+  L.tc = tensor_path(dtype, K) && Do % 64 == 0;
+  if (L.tc) {
+    L.h = c.take((size_t)M * std::max(n_active, 1) * kBlock * 2);
+    L.ksplit = down_ksplit(M, Do, std::max(n_active, 1), layout_sms());
+    if (L.ksplit > 1) L.yacc = c.take((size_t)L.ksplit * M * Do * 4);
+  }
+  L.total = c.off;
+  return L;
+}
+}  // namespace
+
+int fp_pack_pattention_weights(const void* k_gate, const void* k_up, const void* v, int dtype, int Np, int K,
+                               int D_out, void* w_gu, void* v_t, void* stream) {
+  if (!k_gate || !v || !w_gu || !v_t || Np <= 0 || K <= 0 || D_out <= 0) return FP_ERR_INVALID_ARG;
+  if (dtype != FP_DTYPE_BF16) return FP_ERR_UNSUPPORTED;
+  if (Np % kBlock || K % 64 || D_out % 64) return FP_ERR_UNSUPPORTED;
+  const void* ku = k_up ? k_up : k_gate;  // non-gated forms: the gate rows fill both halves
+  if (!aligned16(k_gate) || !aligned16(ku) || !aligned16(w_gu) || !aligned16(v_t)) return FP_ERR_INVALID_ARG;
+  int sms;
+  FP_TRY(device_info(sms));
+  cudaStream_t st = (cudaStream_t)stream;
+  FP_TRY(launch_pack_gate_up(k_gate, ku, Np, K, w_gu, st));
+  return launch_pack_vt(v, Np, D_out, v_t, st);
+}
+
+size_t fp_pattention_workspace_size(int dtype, int64_t M, int K, int Np, int D_out, int n_active) {
+  return shared_layout(dtype, std::max<int64_t>(M, 0), K, D_out, std::max(Np / kBlock, 1), std::max(n_active, 0))
+      .total;
+}
+
+int fp_pattention_fwd(const void* x, int64_t M, int K, int Np, int D_out, int dtype, const void* k_gate,
+                      const void* k_up, const void* v, const void* w_gu, const void* v_t, const int32_t* active,
+                      int n_active, int activation, void* y, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  if (dtype != FP_DTYPE_F32 && dtype != FP_DTYPE_BF16) return FP_ERR_UNSUPPORTED;
+  if (M < 0 || K <= 0 || Np <= 0 || D_out <= 0 || Np % kBlock) return FP_ERR_INVALID_ARG;
+  if (activation < FP_ACT_SWIGLU || activation > FP_ACT_RELU2) return FP_ERR_INVALID_ARG;
+  if (activation == FP_ACT_SWIGLU && !k_up) return FP_ERR_INVALID_ARG;
+  if (active && n_active < 0) return FP_ERR_INVALID_ARG;
+  if (M > (int64_t)INT32_MAX / 8) return FP_ERR_UNSUPPORTED;
+  const int NB = Np / kBlock;
+  const int nact = active ? n_active : NB;
+  if (M == 0) return FP_OK;
+  if (!x || !k_gate || !v || !y || !workspace) return FP_ERR_INVALID_ARG;
+  const SharedLayout L = shared_layout(dtype, M, K, D_out, NB, nact);
+  if (workspace_bytes < L.total) return FP_ERR_WORKSPACE;
+  int sms;
+  FP_TRY(device_info(sms));
+  cudaStream_t st = (cudaStream_t)stream;
+  int* err = at<int>(workspace, L.err);
+  if (cudaMemsetAsync(err, 0, 256, st) != cudaSuccess) return FP_ERR_CUDA;
+  const int32_t* list = active;
+  if (!list) {
+    int32_t* all = at<int32_t>(workspace, L.act);
+    FP_TRY(launch_iota(all, NB, st));
+    list = all;
+  }
+  const bool tc = L.tc && nact > 0 && w_gu && v_t && aligned16(x) && aligned16(w_gu) && aligned16(v_t) &&
+                  aligned16(y);
+  if (!tc) {
+    // CUDA cores: fp32 (1e-4 tolerance), widths that are not multiples of 64, or no packed layouts
+    if (K > 56 * 1024 || D_out > 32 * 256) return FP_ERR_UNSUPPORTED;
+    SimtArgs a{};
+    a.x = x; a.k_gate = k_gate; a.k_up = k_up; a.v = v; a.dtype = dtype; a.M = M; a.D = K; a.NB = NB;
+    a.active = list; a.n_active = nact; a.stride = 1; a.offset = 0; a.ctx16 = nullptr; a.out_proj = nullptr;
+    a.y = y; a.y_f32 = 0; a.D_out = D_out; a.act = activation;
+    return launch_simt(a, st);
+  }
+  void* h = at<void>(workspace, L.h);
+  GateUpArgs g{};
+  g.x = x; g.w_gu = w_gu; g.M = M; g.D = K; g.Np = Np;
+  g.tiles = nullptr; g.meta = nullptr; g.key_cnt = nullptr; g.pair_tok = nullptr; g.key_cap = 0;
+  g.nbl = nact; g.stride = 1; g.offset = 0; g.active = list; g.n_keys = nact;
+  g.h = h; g.ldh = (int64_t)nact * kBlock; g.err = err; g.num_sms = sms; g.act = activation;
+  FP_TRY(launch_gateup(g, st));
+  DownArgs d{};
+  d.h = h; d.v_t = v_t; d.vt_tiled = 1; d.M = M; d.D = D_out; d.Np = Np; d.K = nact * kBlock; d.bmap = list;
+  d.stride = 1; d.offset = 0; d.ctx16 = nullptr; d.out_proj = nullptr; d.out_proj_f32 = 0;
+  d.y = y; d.y_f32 = 0; d.err = err; d.num_sms = sms;
+  d.ksplit = L.ksplit; d.y_acc = L.ksplit > 1 ? at<float>(workspace, L.yacc) : nullptr;
+  return launch_down(d, st);
+}
+
 size_t fp_block_energy_workspace_size(int64_t M, int NB) {
   Carve c;
   c.take(256);                                   // error word

@@ -337,7 +337,7 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
           const float recv = __uint_as_float(__shfl_xor_sync(0xffffffffu, send, 16));
           const float gv = lane < 16 ? __uint_as_float(v[j]) : recv;
           const float u = lane < 16 ? recv : __uint_as_float(v[16 + j]);
-          const float h = __fdividef(gv, 1.0f + __expf(-gv)) * u;  // silu(g) * u
+          const float h = pattention_act<false>(a.act, gv, u);  // silu(g) * u for SwiGLU
           const int tok = __shfl_sync(0xffffffffu, tok_l, lane < 16 ? j : 16 + j);
           if (a.energy) {
             // |h| summed over this half-warp's 16 channels (fixed order), one partial per TMEM quarter

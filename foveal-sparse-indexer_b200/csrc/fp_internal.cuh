@@ -14,6 +14,25 @@ namespace fp {
 __device__ __forceinline__ float to_f32(float v) { return v; }
 __device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
 
+// Activation of the Pattention scores (pattention_triton.py:172-191 codes, :296-309 semantics): g = x.k_gate,
+// u = x.k_up (used by SwiGLU only).  GELU is the erf form (F.gelu's default).  The tensor-core epilogue
+// uses the fast exponential and division intrinsics (bf16 outputs); the CUDA-core path (fp32 models,
+// 1e-4 tolerance) uses expf and an IEEE division.
+template <bool kPrecise>
+__device__ __forceinline__ float pattention_act(int act, float g, float u) {
+  const float silu = kPrecise ? g / (1.0f + expf(-g)) : __fdividef(g, 1.0f + __expf(-g));
+  switch (act) {
+    case FP_ACT_SILU: return silu;
+    case FP_ACT_GELU: return 0.5f * g * (1.0f + erff(g * 0.7071067811865476f));
+    case FP_ACT_RELU: return fmaxf(g, 0.0f);
+    case FP_ACT_RELU2: {
+      const float r = fmaxf(g, 0.0f);
+      return r * r;
+    }
+    default: return silu * u;  // FP_ACT_SWIGLU
+  }
+}
+
 // Tile shapes of the tensor-core path.
 constexpr int kTileM = 128;       // UMMA M: weight rows (gate/up) or tokens (down)
 constexpr int kTileN = 256;       // UMMA N: tokens (gate/up) or output columns (down)
@@ -109,6 +128,7 @@ struct GateUpArgs {
   float* energy;
   int* err;
   int num_sms;
+  int act = FP_ACT_SWIGLU;  // activation of the epilogue (non-gated forms ignore the up rows)
 };
 int launch_gateup(const GateUpArgs& a, cudaStream_t st);
 // E[t, b] = (sum_q part[q][t][b]) / 64 * vnorm[b], quarters summed in order
@@ -180,6 +200,8 @@ struct SimtArgs {
   const void* out_proj;
   void* y;
   int y_f32;
+  int D_out = 0;            // output width = v's columns (0: D)
+  int act = FP_ACT_SWIGLU;  // activation; k_up may be null unless SwiGLU
 };
 int launch_simt(const SimtArgs& a, cudaStream_t st);
 

@@ -1,12 +1,12 @@
-// CUDA-core (FFMA) path of the gated Pattention contraction.
+// CUDA-core (FFMA) path of the Pattention contraction.
 //
 // Used for fp32 models, where the 1e-4 relative tolerance rules out tensor-core bf16/tf32 math, and for
-// bf16 shapes the tensor-core kernels do not tile (hidden size not a multiple of 64).  One CTA per
-// token: for each active block b of the token,
-//     g = x . K_gate[b]^T, u = x . K_up[b]^T (64 each), h = silu(g) * u, y += h . V[b]
-// then y += ctx16 . W_out^T (additive stream) when requested.
-// Reference: foveal_indexer/pattention_triton.py:280-311 (per-token fallback, "swiglu"),
-//            foveal_indexer/foveal_pattention.py:329-342.
+// bf16 shapes the tensor-core kernels do not tile (widths not multiples of 64).  One CTA per token: for
+// each active block b of the token,
+//     g = x . K_gate[b]^T, u = x . K_up[b]^T (64 each; u only for SwiGLU), h = act(g, u), y += h . V[b]
+// then y += ctx16 . W_out^T (additive stream) when requested.  y has D_out columns (v's width).
+// Reference: foveal_indexer/pattention_triton.py:280-311 (per-token / shared-list fallback, all five
+//            activations), foveal_indexer/foveal_pattention.py:329-342.
 #include "fp_internal.cuh"
 
 namespace fp {
@@ -31,6 +31,8 @@ simt_pattention_kernel(const SimtArgs a) {
   float* xs = sh;
   float* gu = sh + a.D;
   const int D = a.D;
+  const int Do = a.D_out > 0 ? a.D_out : a.D;
+  const bool gated = a.act == FP_ACT_SWIGLU;
   const int64_t t = blockIdx.x;
   const T* x = reinterpret_cast<const T*>(a.x) + t * D;
   const T* kg = reinterpret_cast<const T*>(a.k_gate);
@@ -56,6 +58,7 @@ simt_pattention_kernel(const SimtArgs a) {
     if (b < 0 || b >= a.NB) continue;
     // 128 dot products: warp w computes rows 16w .. 16w+15 of [gate(64); up(64)]
     for (int r = warp * 16; r < warp * 16 + 16; ++r) {
+      if (!gated && r >= 64) break;  // non-gated forms need the gate rows only
       const T* wrow = (r < 64 ? kg + ((int64_t)b * 64 + r) * D : ku + ((int64_t)b * 64 + r - 64) * D);
       float s = 0.f;
       for (int d = lane; d < D; d += 32) s = fmaf(xs[d], to_f32(wrow[d]), s);
@@ -66,16 +69,16 @@ simt_pattention_kernel(const SimtArgs a) {
     __syncthreads();
     if (threadIdx.x < 64) {
       const float g = gu[threadIdx.x];
-      gu[threadIdx.x] = g / (1.0f + expf(-g)) * gu[64 + threadIdx.x];
+      gu[threadIdx.x] = pattention_act<true>(a.act, g, gated ? gu[64 + threadIdx.x] : 0.0f);
     }
     __syncthreads();
-    const T* vb = v + (int64_t)b * 64 * D;
+    const T* vb = v + (int64_t)b * 64 * Do;
 #pragma unroll
     for (int i = 0; i < CPT; ++i) {
       const int d = threadIdx.x + i * kSimtThreads;
-      if (d < D) {
+      if (d < Do) {
         float s = acc[i];
-        for (int j = 0; j < 64; ++j) s = fmaf(gu[j], to_f32(vb[(int64_t)j * D + d]), s);
+        for (int j = 0; j < 64; ++j) s = fmaf(gu[j], to_f32(vb[(int64_t)j * Do + d]), s);
         acc[i] = s;
       }
     }
@@ -91,7 +94,7 @@ simt_pattention_kernel(const SimtArgs a) {
 #pragma unroll
   for (int i = 0; i < CPT; ++i) {
     const int d = threadIdx.x + i * kSimtThreads;
-    if (d < D) {
+    if (d < Do) {
       float o = acc[i];
       if (a.ctx16) {
         float s = 0.f;
@@ -99,7 +102,7 @@ simt_pattention_kernel(const SimtArgs a) {
         for (int k = 0; k < 16; ++k) s = fmaf(ctx[k], to_f32(wo[(int64_t)d * 16 + k]), s);
         o += s;
       }
-      store_out<T>(a.y, t * D + d, o, a.y_f32);
+      store_out<T>(a.y, t * Do + d, o, a.y_f32);
     }
   }
 }
@@ -107,7 +110,7 @@ simt_pattention_kernel(const SimtArgs a) {
 template <typename T>
 static int launch_simt_t(const SimtArgs& a, cudaStream_t st) {
   const size_t smem = ((size_t)a.D + 128) * sizeof(float);
-  const int cpt = (a.D + kSimtThreads - 1) / kSimtThreads;
+  const int cpt = ((a.D_out > 0 ? a.D_out : a.D) + kSimtThreads - 1) / kSimtThreads;
   auto go = [&](auto kern) -> int {
     if (smem > 48 * 1024 &&
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)

@@ -130,6 +130,64 @@ def swiglu_bwd(dout: torch.Tensor, g: torch.Tensor, u: torch.Tensor, want_h: boo
     return dg, du, h
 
 
+def swiglu_fwd(g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
+    """h = silu(g) * u (``fp_swiglu_fwd``), same dtype and shape as ``g``."""
+    dev = require_cuda(g, u)
+    if g.shape != u.shape:
+        raise ValueError(f"g and u must have the same shape, got {tuple(g.shape)} and {tuple(u.shape)}")
+    g, u = contig(g), contig(u.to(g.dtype))
+    h = torch.empty_like(g)
+    check(_lib.load().fp_swiglu_fwd(ptr(g), ptr(u), dtype_code(g.dtype), g.numel(), ptr(h), stream_handle(dev)),
+          "fp_swiglu_fwd")
+    return h
+
+
+PATTENTION_ACTIVATIONS = {"swiglu": 0, "silu": 1, "gelu": 2, "relu": 3, "relu2": 4}
+
+
+def pack_pattention_weights(k_gate: torch.Tensor, k_up: Optional[torch.Tensor], v: torch.Tensor):
+    """Tensor-core layouts of a function-level Pattention's weights (``fp_pack_pattention_weights``):
+    (w_gu [2 Np, K], v_t [ceil(D_out / 256) * 256, Np]); None when the shape or dtype runs on CUDA cores."""
+    Np, K = k_gate.shape
+    D_out = v.shape[1]
+    if v.dtype != torch.bfloat16 or K % 64 or D_out % 64 or Np % 64:
+        return None
+    dev = require_cuda(k_gate, k_up, v)
+    kg, v = contig(k_gate.detach()), contig(v.detach())
+    ku = contig(k_up.detach().to(v.dtype)) if k_up is not None else None
+    w_gu = torch.empty(2 * Np, K, dtype=v.dtype, device=dev)
+    vt = torch.empty((D_out + 255) // 256 * 256, Np, dtype=v.dtype, device=dev)
+    rc = _lib.load().fp_pack_pattention_weights(ptr(kg.to(v.dtype)), ptr(ku), ptr(v), dtype_code(v.dtype), Np, K,
+                                                D_out, ptr(w_gu), ptr(vt), stream_handle(dev))
+    check(rc, "fp_pack_pattention_weights")
+    return w_gu, vt
+
+
+def pattention_forward(x2d: torch.Tensor, k_gate: torch.Tensor, k_up: Optional[torch.Tensor], v: torch.Tensor,
+                       packed, active: Optional[torch.Tensor], activation: str) -> torch.Tensor:
+    """Function-level Pattention over one shared active list (``fp_pattention_fwd``): y [M, D_out] in x's
+    dtype.  ``packed`` from :func:`pack_pattention_weights` (or None: CUDA cores)."""
+    dev = require_cuda(x2d, k_gate, v, k_up, active)
+    dtt = x2d.dtype
+    x2d = contig(x2d)
+    M, K = x2d.shape
+    Np, D_out = v.shape
+    kg, v = contig(k_gate.detach().to(dtt)), contig(v.detach().to(dtt))
+    ku = contig(k_up.detach().to(dtt)) if k_up is not None else None
+    act = contig(active.to(torch.int32)) if active is not None else None
+    n_active = act.numel() if act is not None else Np // 64
+    y = torch.empty(M, D_out, dtype=dtt, device=dev)
+    lib = _lib.load()
+    code = dtype_code(dtt)
+    ws = _lib.workspace(dev, lib.fp_pattention_workspace_size(code, M, K, Np, D_out, n_active))
+    w_gu, v_t = packed if packed is not None else (None, None)
+    rc = lib.fp_pattention_fwd(ptr(x2d), M, K, Np, D_out, code, ptr(kg), ptr(ku), ptr(v), ptr(w_gu), ptr(v_t),
+                               ptr(act), n_active, PATTENTION_ACTIVATIONS[activation], ptr(y), ptr(ws), ws.numel(),
+                               stream_handle(dev))
+    check(rc, "fp_pattention_fwd")
+    return y
+
+
 def token_forward(x2d, k_gate, k_up, v, packed, q_proj, block_keys, out_proj, *, base_blocks: int,
                   top_p: float, min_remote: int, max_remote: int, temperature: float = 1.0,
                   additive: bool = True, block_stride: int = 1, block_offset: int = 0,

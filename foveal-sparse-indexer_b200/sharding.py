@@ -24,18 +24,30 @@ import torch.distributed as dist
 from . import kernels
 
 
-def shard_parameter_blocks(module, group=None) -> None:
-    """Makes ``module`` (routing="token") compute only the parameter blocks of this rank."""
+def shard_parameter_blocks(module, group=None, partial_dtype: Optional[torch.dtype] = None) -> None:
+    """Makes ``module`` (routing="token") compute only the parameter blocks of this rank.
+
+    ``partial_dtype``: dtype of the partial outputs that the collective sums (default: the module's
+    dtype, so a bf16 model moves bf16 partials, half the bytes of fp32; the reduction of N bf16 partials
+    stays well inside the 2e-2 relative bar of bf16 outputs).  ``torch.float32`` keeps fp32 partials."""
     if module.routing != "token":
         raise ValueError("parameter-block sharding applies to routing='token'")
     rank = dist.get_rank(group)
     world = dist.get_world_size(group)
     module._shard = (rank, world, group)
+    pd = partial_dtype or module.k_gate.dtype
+    if pd not in (torch.float32, torch.bfloat16):
+        raise ValueError("partial_dtype must be torch.float32 or torch.bfloat16")
+    module._shard_partial_dtype = pd
 
 
 def owned_blocks(num_blocks: int, rank: int, world: int):
     """Block ids owned by ``rank``: b % world == rank."""
     return list(range(rank, num_blocks, world))
+
+
+def _partial_dtype(module) -> torch.dtype:
+    return getattr(module, "_shard_partial_dtype", None) or torch.float32
 
 
 def _cuda_partial(module, x2d, world: int, rank: int, additive: bool, want_routes: bool, out=None):
@@ -44,7 +56,7 @@ def _cuda_partial(module, x2d, world: int, rank: int, additive: bool, want_route
         x2d, kg, ku, v, packed, wq, k16, wout, base_blocks=module.base_blocks, top_p=module.top_p,
         min_remote=module.min_remote_blocks, max_remote=module.max_remote_blocks,
         temperature=module.temperature, additive=additive, block_stride=world, block_offset=rank,
-        out_f32=True, want_routes=want_routes, y=out)
+        out_f32=_partial_dtype(module) == torch.float32, want_routes=want_routes, y=out)
 
 
 def _comm_stream(module, device) -> torch.cuda.Stream:
@@ -73,6 +85,7 @@ def sharded_token_forward(module, x2d: torch.Tensor, *, want_routes: bool = Fals
         raise ValueError("reduce='scatter' needs the token count to divide by the world size")
     if chunks <= 1 or want_routes:
         y_part, ridx, cnt, S = fn(module, x2d, world, rank, rank == 0, want_routes)
+        y_part = y_part.to(_partial_dtype(module))
         if reduce == "all":
             dist.all_reduce(y_part, op=dist.ReduceOp.SUM, group=group)
             y = y_part
@@ -100,8 +113,9 @@ def sharded_token_forward(module, x2d: torch.Tensor, *, want_routes: bool = Fals
         return torch.cuda.stream(comm)
 
     works = []
+    pd = _partial_dtype(module)
     if reduce == "all":
-        y = torch.empty(M, D, dtype=torch.float32, device=x2d.device)
+        y = torch.empty(M, D, dtype=pd, device=x2d.device)
         bounds = [M * i // chunks for i in range(chunks + 1)]
         for i in range(chunks):
             lo, hi = bounds[i], bounds[i + 1]
@@ -109,7 +123,7 @@ def sharded_token_forward(module, x2d: torch.Tensor, *, want_routes: bool = Fals
                 part = fn(module, x2d[lo:hi], world, rank, rank == 0, False, out=y[lo:hi])[0]
             else:
                 part = fn(module, x2d[lo:hi], world, rank, rank == 0, False)[0]
-                y[lo:hi].copy_(part)
+                y[lo:hi].copy_(part.to(pd))
                 part = y[lo:hi]
             with after_compute():
                 works.append(dist.all_reduce(part, op=dist.ReduceOp.SUM, group=group, async_op=True))
@@ -119,16 +133,121 @@ def sharded_token_forward(module, x2d: torch.Tensor, *, want_routes: bool = Fals
 
     s = M // (world * chunks)  # rows of one rank's piece of one chunk
     xv = x2d.view(world, chunks, s, D)
-    y = torch.empty(M // world, D, dtype=torch.float32, device=x2d.device)
+    y = torch.empty(M // world, D, dtype=pd, device=x2d.device)
     for i in range(chunks):
         xc = xv[:, i].reshape(world * s, D)  # rank-major: piece i of every rank's slice
         part, _, _, _ = fn(module, xc, world, rank, rank == 0, False)
+        part = part.to(pd)
         with after_compute():
             out = y[i * s:(i + 1) * s]
             works.append(dist.reduce_scatter_tensor(out, part, op=dist.ReduceOp.SUM, group=group, async_op=True))
     for w in works:
         w.wait()
     return y.to(x2d.dtype), None, None, None
+
+
+def sharded_forward_slices(module, x_slice: torch.Tensor, *, chunks: int = 1,
+                           compute_partial: Optional[Callable] = None) -> torch.Tensor:
+    """Block-sharded forward of a token batch that is partitioned over the ranks.
+
+    Every rank passes its own contiguous slice of the batch's token rows (the same number on every rank)
+    and receives the output rows of that slice.  Per chunk: an all-gather brings piece i of every rank's
+    slice to every rank (NVLink, rank-major), each rank computes the partial output of its parameter
+    blocks over those rows, and a reduce-scatter returns to every rank the sum for its own piece.  Chunk
+    i+1's all-gather is issued before chunk i's reduce-scatter, so on GPUs the collectives of one chunk
+    run while another chunk computes.  No rank ever holds more than its slice of the input at the start:
+    the host-to-device traffic of a job is split over the ranks' links instead of every rank copying the
+    whole batch."""
+    rank, world, group = module._shard
+    fn = compute_partial or _cuda_partial
+    s_all, D = x_slice.shape
+    chunks = max(1, min(int(chunks), s_all)) if s_all else 1
+    if s_all % chunks:
+        raise ValueError("the slice's token count must divide by the number of chunks")
+    s = s_all // chunks
+    pd = _partial_dtype(module)
+    dev = x_slice.device
+    y = torch.empty(s_all, D, dtype=pd, device=dev)
+    if s_all == 0:
+        return y.to(x_slice.dtype)
+    gathered = [torch.empty(world * s, D, dtype=x_slice.dtype, device=dev) for _ in range(chunks)]
+
+    def gather(i):
+        return dist.all_gather_into_tensor(gathered[i], x_slice[i * s:(i + 1) * s].contiguous(), group=group,
+                                           async_op=True)
+
+    ag = [gather(0)] + ([gather(1)] if chunks > 1 else [])
+    rs = []
+    for i in range(chunks):
+        ag[i].wait()  # the current stream waits for chunk i's rows
+        part = fn(module, gathered[i], world, rank, rank == 0, False)[0].to(pd)
+        rs.append(dist.reduce_scatter_tensor(y[i * s:(i + 1) * s], part, op=dist.ReduceOp.SUM, group=group,
+                                             async_op=True))
+        if i + 2 < chunks:
+            ag.append(gather(i + 2))
+    for w in rs:
+        w.wait()
+    return y.to(x_slice.dtype)
+
+
+def sharded_forward_host(module, x_host: torch.Tensor, out: Optional[torch.Tensor] = None, *,
+                         chunks: int = 4) -> torch.Tensor:
+    """:func:`sharded_forward_slices` for a slice held in host memory (pinned for the copies to overlap):
+    each chunk's rows are copied to the device on a copy stream, gathered, computed and reduce-scattered,
+    and its output rows copied back on another stream while later chunks run.  Returns the output slice
+    in host memory, complete once the caller's current stream has been synchronised."""
+    rank, world, group = module._shard
+    dev = module.k_gate.device
+    s_all, D = x_host.shape
+    chunks = max(1, min(int(chunks), s_all)) if s_all else 1
+    if s_all % chunks:
+        raise ValueError("the slice's token count must divide by the number of chunks")
+    s = s_all // chunks
+    if out is None:
+        out = torch.empty(s_all, D, dtype=x_host.dtype, pin_memory=True)
+    if s_all == 0:
+        return out
+    st = getattr(module, "_shard_host_streams", None)
+    if st is None or st[0].device != dev:
+        st = tuple(torch.cuda.Stream(device=dev) for _ in range(3))
+        module._shard_host_streams = st
+    s_in, s_ag, s_out = st
+    cur = torch.cuda.current_stream(dev)
+    for st_ in st:
+        st_.wait_stream(cur)
+    pd = _partial_dtype(module)
+    x_dev = torch.empty(s_all, D, dtype=x_host.dtype, device=dev)
+    y_dev = torch.empty(s_all, D, dtype=pd, device=dev)
+    gathered = [torch.empty(world * s, D, dtype=x_host.dtype, device=dev) for _ in range(chunks)]
+    copied = []
+    with torch.cuda.stream(s_in):  # every chunk's copy-in is queued at once; each signals its own event
+        for i in range(chunks):
+            x_dev[i * s:(i + 1) * s].copy_(x_host[i * s:(i + 1) * s], non_blocking=True)
+            copied.append(torch.cuda.Event())
+            copied[-1].record(s_in)
+
+    def gather(i):
+        s_ag.wait_event(copied[i])
+        with torch.cuda.stream(s_ag):  # the collective waits for chunk i's copy-in only
+            return dist.all_gather_into_tensor(gathered[i], x_dev[i * s:(i + 1) * s], group=group, async_op=True)
+
+    ag = [gather(0)] + ([gather(1)] if chunks > 1 else [])
+    for i in range(chunks):
+        ag[i].wait()
+        part = _cuda_partial(module, gathered[i], world, rank, rank == 0, False)[0]
+        w = dist.reduce_scatter_tensor(y_dev[i * s:(i + 1) * s], part, op=dist.ReduceOp.SUM, group=group,
+                                       async_op=True)
+        with torch.cuda.stream(s_out):
+            w.wait()
+            yv = y_dev[i * s:(i + 1) * s]
+            out[i * s:(i + 1) * s].copy_(yv if pd == x_host.dtype else yv.to(x_host.dtype), non_blocking=True)
+        if i + 2 < chunks:
+            ag.append(gather(i + 2))
+    cur.wait_stream(s_out)
+    for t in (x_dev, y_dev, *gathered):
+        for st_ in st:
+            t.record_stream(st_)
+    return out
 
 
 def split_tokens(x2d: torch.Tensor, rank: int, world: int) -> torch.Tensor:

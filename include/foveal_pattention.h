@@ -48,6 +48,17 @@ typedef enum fp_status {
 
 typedef enum fp_dtype { FP_DTYPE_F32 = 0, FP_DTYPE_BF16 = 1 } fp_dtype;
 
+/* Activations of fp_pattention_fwd, numbered like the reference's ACTIVATION_CODE
+ * (pattention_triton.py:121, :172-191): SwiGLU silu(g) * u, SiLU silu(g), GELU (erf form, as
+ * F.gelu in _pytorch_pattention_fallback, :303), ReLU, squared ReLU. */
+typedef enum fp_activation {
+  FP_ACT_SWIGLU = 0,
+  FP_ACT_SILU = 1,
+  FP_ACT_GELU = 2,
+  FP_ACT_RELU = 3,
+  FP_ACT_RELU2 = 4
+} fp_activation;
+
 /* ABI version (FP_ABI_VERSION of the built library). */
 FP_API int fp_abi_version(void);
 
@@ -151,6 +162,34 @@ FP_API int fp_pattention_pooled_fwd(const void* x, int64_t M, int D, int NB, int
                              const void* k_up, const void* v, const void* w_gu, const void* v_t, const int32_t* active,
                              int n_active, const float* ctx16, const void* out_proj, void* y, int y_f32,
                              void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Function-level Pattention with one active-block list shared by every token: replaces
+ * triton_pattention(x, k_gate, v, k_up=None, active_blocks=None, activation, block_n=64)
+ * (pattention_triton.py:204-277; semantics of _pytorch_pattention_fallback, :280-311).
+ *   y = act(x . K_gate[A]^T, x . K_up[A]^T) . V[A],  A = the rows of blocks active[0 .. n_active)
+ *   x [M, K]; k_gate, k_up [Np, K]; v [Np, D_out]; y [M, D_out]; all in `dtype`.
+ *   k_up may be NULL unless activation == FP_ACT_SWIGLU (the other activations read k_gate only).
+ *   active [n_active] int32 device ids, or NULL for every block (n_active ignored).
+ *   w_gu, v_t: the tensor-core layouts from fp_pack_pattention_weights (bf16 with K % 64 == 0 and
+ *   D_out % 64 == 0; NULL otherwise, and every other shape or fp32 runs on CUDA cores).
+ * fp_pack_pattention_weights is fp_pack_weights with separate widths: w_gu holds 2 * Np * K elements
+ * (with k_up NULL the gate rows fill both halves of each packed block), v_t ceil(D_out / 256) * 256 * Np.
+ */
+FP_API int fp_pack_pattention_weights(const void* k_gate, const void* k_up, const void* v, int dtype, int Np,
+                                      int K, int D_out, void* w_gu, void* v_t, void* stream);
+FP_API size_t fp_pattention_workspace_size(int dtype, int64_t M, int K, int Np, int D_out, int n_active);
+FP_API int fp_pattention_fwd(const void* x, int64_t M, int K, int Np, int D_out, int dtype, const void* k_gate,
+                             const void* k_up, const void* v, const void* w_gu, const void* v_t,
+                             const int32_t* active, int n_active, int activation, void* y, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
+/*
+ * SwiGLU of two pre-activation tensors, h = silu(g) * u (n elements, fp32 arithmetic, `dtype` in and
+ * out): the forward of triton_fused_swiglu / TritonFusedSwiGLUFunction (pattention_triton.py:30-47,
+ * :79-104).  Its backward is fp_swiglu_bwd.
+ */
+FP_API int fp_swiglu_fwd(const void* g, const void* u, int dtype, int64_t n, void* h, void* stream);
 
 /*
  * Teacher block energies of the offline router calibration (FovealPattentionMLP.calibrate_offline_svd,

@@ -36,6 +36,8 @@ __all__ = [
     "pooled_forward",
     "boundary_margins",
     "dense_swiglu",
+    "pattention",
+    "PATTENTION_ACTIVATIONS",
     "teacher_block_energy",
     "calibrate_offline_svd",
     "param_blocks_16d",
@@ -71,6 +73,10 @@ class OracleRoute:
     mean_remote_blocks: torch.Tensor
     base_only_rate: torch.Tensor
     remote_probs_sorted: torch.Tensor  # [B, Q, NB] fp32, the sorted probabilities (for margins)
+    # [B, Q] fp64: distance of the top-p target from the nearest cumulative mass that decides the count
+    # (inf where the K_min / K_max clamps make the count insensitive to it); a tiny value marks a token
+    # whose count depends on the last bits of its probabilities
+    count_margins: Optional[torch.Tensor] = None
 
 
 def select_blocks_noncausal(
@@ -122,6 +128,24 @@ def select_blocks_noncausal(
     counts = torch.minimum(needed, available)
     counts = torch.minimum(counts, max_remote_t)
 
+    # count boundary (test instrumentation, not part of the reference's result): with c = #(cum < target)
+    # the count moves by one when cum[c-1] or cum[c] crosses the target; it cannot move when every count
+    # in needed-1 .. needed+1 is clamped to the same value
+    n_sorted = cumulative.shape[-1]
+    c = (cumulative < target[..., None]).sum(dim=-1)
+    lo = cumulative.gather(-1, (c - 1).clamp(0, n_sorted - 1)[..., None])[..., 0].double()
+    hi = cumulative.gather(-1, c.clamp(0, n_sorted - 1)[..., None])[..., 0].double()
+    tgt = target.double()
+    cm = torch.minimum(torch.where(c > 0, tgt - lo, torch.full_like(tgt, float("inf"))),
+                       torch.where(c < n_sorted, hi - tgt, torch.full_like(tgt, float("inf"))))
+    cap_n = torch.minimum(available, max_remote_t.expand_as(available))
+
+    def clamp_count(n):
+        return torch.minimum(torch.maximum(n, min_remote_t), cap_n)
+
+    frozen = (clamp_count(needed - 1) == clamp_count(needed)) & (clamp_count(needed + 1) == clamp_count(needed))
+    cm = torch.where(frozen | (target <= 0), torch.full_like(cm, float("inf")), cm)
+
     indices = sorted_idx[..., :remote_capacity].to(torch.int32)
     if indices.shape[-1] < remote_capacity:
         indices = F.pad(indices, (0, remote_capacity - indices.shape[-1]))
@@ -150,6 +174,7 @@ def select_blocks_noncausal(
         mean_remote_blocks=counts.float().mean(),
         base_only_rate=(counts == 0).float().mean(),
         remote_probs_sorted=sorted_prob,
+        count_margins=cm,
     )
 
 
@@ -295,6 +320,41 @@ def boundary_margins(sorted_probs: torch.Tensor, counts: torch.Tensor) -> torch.
     c = counts.long().clamp(1, n - 1)
     ar = torch.arange(M)
     return sorted_probs[ar, c - 1] - sorted_probs[ar, c]
+
+
+PATTENTION_ACTIVATIONS = ("swiglu", "silu", "gelu", "relu", "relu2")
+
+
+def pattention(x, k_gate, v, k_up=None, active_blocks=None, activation: str = "swiglu",
+               block_n: int = 64) -> torch.Tensor:
+    """Function-level Pattention with one shared active-block list (pattention_triton.py:280-311, the
+    semantics of ``triton_pattention``, :204-277): gather the active blocks' rows, g = x K_gate^T,
+    act = silu(g) * (x K_up^T) for "swiglu", silu(g) / gelu(g) (erf form) / relu(g) / relu(g)^2
+    otherwise, out = act V; fp32 on the CPU."""
+    if activation not in PATTENTION_ACTIVATIONS:
+        raise ValueError(f"unknown activation {activation!r}")
+    shape = x.shape
+    x2d = x.reshape(-1, shape[-1]).float()
+    kg, v = k_gate.float(), v.float()
+    ku = None if k_up is None else k_up.float()
+    if active_blocks is not None:
+        idx = (active_blocks.long().view(-1, 1) * block_n + torch.arange(block_n)).flatten()
+        kg, v = kg[idx], v[idx]
+        ku = None if ku is None else ku[idx]
+    g = x2d @ kg.t()
+    if activation == "swiglu":
+        if ku is None:
+            raise ValueError("k_up is required for swiglu")
+        act = F.silu(g) * (x2d @ ku.t())
+    elif activation == "silu":
+        act = F.silu(g)
+    elif activation == "gelu":
+        act = F.gelu(g)
+    elif activation == "relu":
+        act = F.relu(g)
+    else:
+        act = F.relu(g) ** 2
+    return (act @ v).reshape(*shape[:-1], v.shape[-1])
 
 
 def dense_swiglu(x2d, w) -> torch.Tensor:

@@ -70,57 +70,73 @@ def route_sets(idx, cnt):
 
 
 # Probabilities closer than this (fp32, absolute) at the selection boundary are rounding-level near
-# ties: 0 < p[K-1] - p[K] < TIE_EPS.  Two correct fp32 implementations may order such a pair differently
+# ties: p[K-1] - p[K] < TIE_EPS.  Two correct fp32 implementations may order such a pair differently
 # (exp, the softmax denominator and the D-long projection round differently on every platform), so a
-# differing set there is counted and reported, not failed.  A margin of exactly 0 is a bit-equal tie:
-# the lower block id must win (stable descending order), and a differing set there fails.
+# differing set there is counted and reported, not failed.  A margin of exactly 0 in the reference's
+# fp32 values is a coincidence of that implementation's rounding unless both sides compute the two
+# probabilities from identical inputs (repeated block keys, equal scores); there the tie is bit-equal on
+# both sides, the lower block id must win, and ``strict_exact=True`` fails any differing set.
 TIE_EPS = 2e-8
+# Cumulative masses (~0.1-1, fp32 ulp up to 6e-8) closer than this to the top-p target decide the count
+# by their last bits: each probability may differ by an ulp between implementations, and the prefix sums
+# carry ~150 of them.
+COUNT_EPS = 2e-7
 
 # Tie accounting of every route comparison made in this session, printed at the end of the run.
 TIE_REPORTS: list = []
 
 
 class RouteTieReport(dict):
-    """Per-comparison route accounting: tokens, mismatches outside the band, near ties in the band and
-    how many of them differ, bit-equal ties and how many of them differ, and the smallest reference
-    margin among differing tokens (None when every set matches)."""
+    """Per-comparison route accounting: tokens; mismatches outside the band; tokens in the band
+    (reference margin in [0, TIE_EPS)) and how many of them differ; the margin-0 tokens among them and how
+    many of those differ; the smallest and largest reference margin among differing tokens (None when
+    every set matches)."""
 
 
-def compare_routes(idx, cnt, ref_idx, ref_cnt, margins=None, tie_eps: float = TIE_EPS, label: str = ""):
+def compare_routes(idx, cnt, ref_idx, ref_cnt, margins=None, tie_eps: float = TIE_EPS, label: str = "",
+                   strict_exact: bool = False, count_margins=None):
     """Counts must match exactly; selected sets must match exactly except on tokens whose reference
-    boundary margin lies in (0, ``tie_eps``).  Returns (n_mismatch_not_excused, n_near_ties) and records
-    a :class:`RouteTieReport` in ``TIE_REPORTS`` when ``label`` is given.  Mismatches on bit-equal ties
-    (margin exactly 0: the lower id must win) are never excused."""
+    boundary margin is below ``tie_eps``.  With ``strict_exact`` (both sides compute bit-equal
+    probabilities for tied blocks) margin-0 tokens are not excused: the lower id must win.  Returns
+    (n_mismatch_not_excused, n_in_band) and records a :class:`RouteTieReport` in ``TIE_REPORTS`` when
+    ``label`` is given.  ``count_margins`` (the oracle's distance of the top-p target from the deciding
+    cumulative mass) adds the tokens whose count sits within ``COUNT_EPS`` of flipping to the band."""
     cnt = np.asarray(cnt)
     ref_cnt = np.asarray(ref_cnt)
     a, b = route_sets(idx, cnt), route_sets(ref_idx, ref_cnt)
     m = None if margins is None else np.asarray(margins, dtype=np.float64)
+    cm = None if count_margins is None else np.asarray(count_margins, dtype=np.float64).reshape(-1)
     rep = RouteTieReport(label=label, tokens=len(a), differ_outside_band=0, in_band=0, in_band_differ=0,
-                         exact_ties=0, exact_tie_differ=0, min_margin_differ=None,
-                         min_margin=None if m is None or m.size == 0 else float(m.min()))
+                         exact_ties=0, exact_tie_differ=0, min_margin_differ=None, max_margin_differ=None,
+                         strict_exact=strict_exact, count_band=0, count_band_differ=0)
     for t in range(len(a)):
         mt = None if m is None else float(m[t])
         exact = mt is not None and mt == 0.0
-        near = mt is not None and 0.0 < mt < tie_eps
+        count_near = cm is not None and float(cm[t]) < COUNT_EPS
+        rep["count_band"] += int(count_near)
+        near = (mt is not None and mt < tie_eps and not (exact and strict_exact)) or count_near
         rep["exact_ties"] += int(exact)
         rep["in_band"] += int(near)
         if a[t] != b[t] or cnt[t] != ref_cnt[t]:
+            if exact:
+                rep["exact_tie_differ"] += 1
+            if count_near:
+                rep["count_band_differ"] += 1
             if near:
                 rep["in_band_differ"] += 1
-            elif exact:
-                rep["exact_tie_differ"] += 1
             else:
                 rep["differ_outside_band"] += 1
             if mt is not None:
-                cur = rep["min_margin_differ"]
-                rep["min_margin_differ"] = mt if cur is None else min(cur, mt)
+                lo, hi = rep["min_margin_differ"], rep["max_margin_differ"]
+                rep["min_margin_differ"] = mt if lo is None else min(lo, mt)
+                rep["max_margin_differ"] = mt if hi is None else max(hi, mt)
     if label:
         TIE_REPORTS.append(rep)
         path = os.environ.get("FP_TIE_REPORT")
         if path:
             with open(path, "a") as f:
                 f.write(json.dumps(dict(rep)) + "\n")
-    return rep["differ_outside_band"] + rep["exact_tie_differ"], rep["in_band"]
+    return rep["differ_outside_band"], rep["in_band"]
 
 
 def pytest_terminal_summary(terminalreporter, exitstatus, config):
@@ -131,10 +147,13 @@ def pytest_terminal_summary(terminalreporter, exitstatus, config):
     tr = terminalreporter
     tr.section("route tie accounting (TIE_EPS = %.0e)" % TIE_EPS)
     for r in TIE_REPORTS:
-        mmd = "-" if r["min_margin_differ"] is None else "%.2e" % r["min_margin_differ"]
+        mg = "-" if r["min_margin_differ"] is None else "%.2e..%.2e" % (r["min_margin_differ"],
+                                                                      r["max_margin_differ"])
+        eq = "bit-equal on both sides" if r["strict_exact"] else "margin 0 in the reference"
         tr.write_line(f"{r['label']}: tokens {r['tokens']}, in band {r['in_band']} (differ {r['in_band_differ']}), "
-                      f"bit-equal {r['exact_ties']} (differ {r['exact_tie_differ']}), "
-                      f"differ outside {r['differ_outside_band']}, min margin of differing {mmd}")
+                      f"{eq} {r['exact_ties']} (differ {r['exact_tie_differ']}), "
+                      f"count band {r['count_band']} (differ {r['count_band_differ']}), "
+                      f"differ outside {r['differ_outside_band']}, set margins of differing {mg}")
 
 
 def active_set_matches(active, gold_scores, base: int, remote: int, rel_tol: float) -> bool:

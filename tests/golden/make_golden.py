@@ -254,6 +254,48 @@ def variants_case(ref_root: str, seed: int):
     return arr
 
 
+def pattention_case(ref_root: str, seed: int):
+    """The reference's function-level Pattention (``_pytorch_pattention_fallback``, the semantics of
+    ``triton_pattention``, pattention_triton.py:204-311) on every PATTENTION_CASES entry, fp32 and on
+    bf16-rounded values; ``TritonSwiGLUPattentionMLP.from_dense_mlp`` on a seeded dense MLP (sparse and
+    dense forward); ``convert_llm_mlp_to_pattention`` on the tiny Llama of the serving case (logits)."""
+    sys.path.insert(0, ref_root)
+    from foveal_indexer.pattention_triton import (TritonSwiGLUPattentionMLP, _pytorch_pattention_fallback,
+                                                  convert_llm_mlp_to_pattention)
+    arr = {}
+    for name, case in cfgmod.PATTENTION_CASES.items():
+        for dt in cfgmod.PATTENTION_DTYPES[name]:
+            x, kg, ku, v, act = cfgmod.pattention_tensors(case, seed, dt)
+            with torch.no_grad():
+                y = _pytorch_pattention_fallback(x, kg, v, ku, act, case["activation"], 64)
+            arr[f"{name}_{dt}_y"] = y.numpy().astype(np.float32)
+
+    class Dense(torch.nn.Module):
+        def __init__(self, h, i):
+            super().__init__()
+            self.gate_proj = torch.nn.Linear(h, i, bias=False)
+            self.up_proj = torch.nn.Linear(h, i, bias=False)
+            self.down_proj = torch.nn.Linear(i, h, bias=False)
+
+    cfg = cfgmod.PATTENTION_MLP
+    wg, wu, wd, x = cfgmod.pattention_mlp_weights(seed)
+    dense = Dense(cfg["hidden"], cfg["intermediate"])
+    with torch.no_grad():
+        dense.gate_proj.weight.copy_(wg)
+        dense.up_proj.weight.copy_(wu)
+        dense.down_proj.weight.copy_(wd)
+        mlp = TritonSwiGLUPattentionMLP.from_dense_mlp(dense)
+        arr["mlp_sparse_y"] = mlp(x, active_blocks=torch.tensor(cfg["active"])).numpy().astype(np.float32)
+        arr["mlp_dense_y"] = mlp(x).numpy().astype(np.float32)
+        model = serve_model(SERVE)
+        convert_llm_mlp_to_pattention(model)
+        ids = torch.randint(0, SERVE["vocab"], (1, 16), generator=torch.Generator().manual_seed(SERVE["prompt_seed"]))
+        arr["convert_prompt"] = ids.numpy()
+        arr["convert_logits"] = model(ids).logits[0].numpy().astype(np.float32)
+        arr["convert_types"] = np.array([type(layer.mlp).__name__ for layer in model.model.layers])
+    return arr
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True)
@@ -265,7 +307,10 @@ def main():
     C = cfgmod.CONFIGS
     meta_common = {"seed": args.seed, "torch": torch.__version__}
     only = set(filter(None, args.only.split(",")))
-    if only and only <= {"calib", "serve", "train", "variants"}:
+    if only and only <= {"calib", "serve", "train", "variants", "pattention"}:
+        if "pattention" in only:
+            save("pattention", {**meta_common, "config": "pattention", "cases": cfgmod.PATTENTION_CASES,
+                                "mlp": cfgmod.PATTENTION_MLP, "serve": SERVE}, pattention_case(args.ref, args.seed))
         if "variants" in only:
             save("variants", {**meta_common, "config": "variants", "cases": cfgmod.VARIANT_CASES},
                  variants_case(args.ref, args.seed))
@@ -364,6 +409,11 @@ def main():
     # 10. Layers that share the router: BlockSparseLinear, FovealTokenformerLinear / FFN.
     save("variants", {**meta_common, "config": "variants", "cases": cfgmod.VARIANT_CASES},
          variants_case(args.ref, args.seed))
+
+    # 11. Function-level Pattention (five activations, gated and non-gated), its MLP module and the model
+    #     conversion helper.
+    save("pattention", {**meta_common, "config": "pattention", "cases": cfgmod.PATTENTION_CASES,
+                        "mlp": cfgmod.PATTENTION_MLP, "serve": SERVE}, pattention_case(args.ref, args.seed))
 
 
 if __name__ == "__main__":

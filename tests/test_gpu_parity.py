@@ -1,9 +1,9 @@
 """GPU parity: the CUDA path (through the C ABI) against the golden vectors and the CPU oracle.
 
-Bars: active-block sets and counts bit-exact.  Tokens whose reference boundary margin lies in
-(0, TIE_EPS) are rounding-level near ties: they are counted (in the band, and how many of them
-differ) and reported at the end of the run, not failed; a bit-equal tie (margin 0) must go to the
-lower block id.  Outputs within 1e-4 relative (fp32 configuration) or 2e-2 relative (bf16
+Bars: active-block sets and counts bit-exact.  Tokens whose reference boundary margin lies below
+TIE_EPS are rounding-level near ties: they are counted (in the band, and how many of them differ) and
+reported at the end of the run, not failed.  Where both sides compute bit-equal probabilities for the
+tied blocks (repeated block keys, equal scores), the lower block id must win and nothing is excused.  Outputs within 1e-4 relative (fp32 configuration) or 2e-2 relative (bf16
 configurations) of the fp32 reference, measured as ||y - ref|| / ||ref|| and as max|y - ref| / max|ref|.
 """
 
@@ -196,7 +196,7 @@ def full_size_check(name, n_out):
     idx, cnt = r.remote_indices[0], r.remote_counts[0]
     margins = oracle.boundary_margins(r.remote_probs_sorted[0], cnt)
     bad, ties = compare_routes(info["remote_indices"].cpu(), info["remote_counts"].cpu(), idx, cnt, margins,
-                               label=f"{name} full ({x2d.shape[0]} tokens)")
+                               label=f"{name} full ({x2d.shape[0]} tokens)", count_margins=r.count_margins[0])
     assert bad == 0, f"{bad} of {x2d.shape[0]} routes differ outside near ties ({ties} ties)"
     sel = torch.randperm(x2d.shape[0], generator=torch.Generator().manual_seed(7))[:n_out].sort().values
     ref = oracle.token_pattention(x2d[sel], w.k_gate, w.k_up, w.v, wl.base_blocks, idx[sel], cnt[sel])
@@ -228,7 +228,8 @@ def test_full_sweep_routes():
         idx, cnt = r.remote_indices[0], r.remote_counts[0]
         margins = oracle.boundary_margins(r.remote_probs_sorted[0], cnt)
         bad, ties = compare_routes(info["remote_indices"].cpu(), info["remote_counts"].cpu(), idx, cnt, margins,
-                                   label=f"sweep full top_p {wl.top_p} K_max {wl.max_remote_blocks}")
+                                   label=f"sweep full top_p {wl.top_p} K_max {wl.max_remote_blocks}",
+                                   count_margins=r.count_margins[0])
         assert bad == 0, f"top_p {wl.top_p} K_max {wl.max_remote_blocks}: {bad} routes differ ({ties} near ties)"
     device_error_is_clear()
 
@@ -251,7 +252,8 @@ def test_bit_equal_ties_go_to_lower_block_ids():
                                        max_remote_blocks=12, remote_capacity=12)
     mg = oracle.boundary_margins(o.remote_probs_sorted[0], o.remote_counts[0])
     bad, _ = compare_routes(r.remote_indices[0].cpu(), r.remote_counts[0].cpu(), o.remote_indices[0],
-                            o.remote_counts[0], mg, label="exact ties: fp_select_blocks (quantised scores)")
+                            o.remote_counts[0], mg, label="exact ties: fp_select_blocks (quantised scores)",
+                            strict_exact=True)
     assert bad == 0
     assert int((mg == 0).sum()) > 100, "the case must exercise bit-equal ties"
 
@@ -268,7 +270,8 @@ def test_bit_equal_ties_go_to_lower_block_ids():
     m = module_for(wl, w)
     y, info = run_token(m, x2d)
     bad, _ = compare_routes(info["remote_indices"].cpu(), info["remote_counts"].cpu(), ref["remote_indices"],
-                            ref["remote_counts"], mg, label="exact ties: fused routing kernel (repeated keys)")
+                            ref["remote_counts"], mg, label="exact ties: fused routing kernel (repeated keys)",
+                            strict_exact=True)
     assert bad == 0
     assert int((mg == 0).sum()) > 100, "the case must exercise bit-equal ties"
     check_y(y.cpu(), ref["y"].reshape(x2d.shape[0], -1), "bf16")

@@ -1,8 +1,10 @@
 """Parameter-block sharding over NCCL on 2 GPUs (skipped with fewer than 2 visible GPUs).
 
 Each rank computes the partial output of the blocks it owns (b % 2 == rank) for all tokens; an NCCL
-all-reduce (or reduce-scatter over token rows) sums the fp32 partials, in one piece or chunk by chunk
-with each chunk's collective overlapping the next chunk's compute.  The result must match the
+all-reduce (or reduce-scatter over token rows) sums the fp32 or bf16 partials, in one piece or chunk by
+chunk with each chunk's collective overlapping the next chunk's compute; with the token-partitioned input
+each rank starts from its own slice of the batch (device or pinned host memory), which an all-gather
+brings to every rank.  The result must match the
 single-GPU forward within the bf16 tolerance, and the routes must be identical on both ranks.
 """
 
@@ -54,19 +56,27 @@ def _worker(rank, world, port, out_dir):
         m.load_state_dict({k: t.to(torch.bfloat16) for k, t in w.state_dict().items()}, strict=False)
         return m.to(dev).eval()
 
+    rows = slice(rank * 1024, (rank + 1) * 1024)
     with torch.no_grad():
         full, info_full = module()(x, return_router_info=True)
         m = module()
-        fsi.sharding.shard_parameter_blocks(m)
+        fsi.sharding.shard_parameter_blocks(m, partial_dtype=torch.float32)
         y, info = m(x, return_router_info=True)
         ys, _, _, _ = fsi.sharding.sharded_token_forward(m, x, reduce="scatter")
         # chunked: each chunk's collective overlaps the next chunk's compute
         yc, _, _, _ = fsi.sharding.sharded_token_forward(m, x, reduce="all", chunks=3)
         ysc, _, _, _ = fsi.sharding.sharded_token_forward(m, x, reduce="scatter", chunks=4)
+        # bf16 partials (the bf16 model's default): half the bytes on NVLink
+        mb = module()
+        fsi.sharding.shard_parameter_blocks(mb)
+        ysb, _, _, _ = fsi.sharding.sharded_token_forward(mb, x, reduce="scatter", chunks=4)
+        # token-partitioned input: each rank passes only its slice (all-gather, compute, reduce-scatter),
+        # from device memory and from pinned host memory
+        ysl = fsi.sharding.sharded_forward_slices(mb, x[rows].contiguous(), chunks=4)
+        yh = fsi.sharding.sharded_forward_host(mb, x[rows].cpu().pin_memory(), chunks=4)
     torch.cuda.synchronize()
-    rows = slice(rank * 1024, (rank + 1) * 1024)
     e_all = max(rel_err(y.float(), full.float()), rel_err(yc.float(), full.float()))
-    e_sc = max(rel_err(ys.float(), full[rows].float()), rel_err(ysc.float(), full[rows].float()))
+    e_sc = max(rel_err(t.float().cpu(), full[rows].float().cpu()) for t in (ys, ysc, ysb, ysl, yh))
     same_routes = bool(torch.equal(info["remote_indices"], info_full["remote_indices"]))
     with open(os.path.join(out_dir, f"r{rank}.txt"), "w") as f:
         f.write(f"{e_all} {e_sc} {int(same_routes)}")

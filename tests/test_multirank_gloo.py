@@ -118,6 +118,53 @@ def test_block_sharded_forward_matches_full():
             assert len(errs) == 4 and max(errs) < 1e-5, (r, errs)
 
 
+def _slices_worker(rank, world, port, out_dir, partial_dtype, chunks):
+    """Token-partitioned input: each rank holds only its slice of the batch; all-gather, block-sharded
+    partials (oracle restricted to the owned blocks, rounded to the partial dtype as the kernel stores
+    them) and reduce-scatter return this rank's output rows."""
+    _setup(rank, world, port)
+    from conftest import fsi
+    import oracle
+
+    torch.manual_seed(0)
+    m = fsi.FovealPattentionMLP(hidden_dim=128, intermediate_dim=2048, base_blocks=4, remote_blocks=8,
+                                dtype=torch.float32, routing="token", top_p=0.8, min_remote_blocks=2,
+                                max_remote_blocks=8)
+    with torch.no_grad():
+        for p_ in (m.k_gate, m.k_up, m.v, m.q_proj_16d.weight, m.block_keys_16d):
+            p_.normal_(std=0.05)
+        m.out_proj_16d.weight.normal_(std=0.05)
+    x2d = torch.randn(world * 24, 128)
+    pd = {"fp32": torch.float32, "bf16": torch.bfloat16}[partial_dtype]
+    fsi.sharding.shard_parameter_blocks(m, partial_dtype=pd)
+
+    def partial(mod, xg, w_, r_, additive, want_routes):
+        y, *rest = _oracle_partial(mod, xg, w_, r_, additive, want_routes)
+        return (y.to(pd), *rest)
+
+    mine = x2d[rank * 24:(rank + 1) * 24].contiguous()
+    y = fsi.sharding.sharded_forward_slices(m, mine, chunks=chunks, compute_partial=partial)
+    ref = oracle.token_forward(x2d, m_weights(m), base_blocks=4, top_p=0.8, min_remote_blocks=2,
+                               max_remote_blocks=8)["y"][rank * 24:(rank + 1) * 24]
+    err = float((y.float() - ref).norm() / ref.norm())
+    with open(os.path.join(out_dir, f"r{rank}.txt"), "w") as f:
+        f.write(f"{err} {tuple(y.shape) == (24, 128)}")
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,partial_dtype,chunks,tol", [(2, "fp32", 3, 1e-5), (4, "fp32", 1, 1e-5),
+                                                            (8, "bf16", 2, 2e-2)])
+def test_token_partitioned_block_sharding(world, partial_dtype, chunks, tol):
+    """sharded_forward_slices at 2, 4 and 8 ranks; at 8 ranks with bf16 partials (the bf16 model's
+    default), whose sum must stay within the 2e-2 relative bar of bf16 outputs."""
+    port = _free_port()
+    with tempfile.TemporaryDirectory() as d:
+        mp.spawn(_slices_worker, args=(world, port, d, partial_dtype, chunks), nprocs=world, join=True)
+        for r in range(world):
+            err, shape_ok = open(os.path.join(d, f"r{r}.txt")).read().split()
+            assert shape_ok == "True" and float(err) < tol, (r, err)
+
+
 def _token_split_worker(rank, world, port, out_dir):
     _setup(rank, world, port)
     from conftest import fsi
