@@ -180,6 +180,36 @@ __device__ __forceinline__ int gu_token(const GuTile& t, int i, const GateUpArgs
   return tok;
 }
 
+// Activation of one 32-column chunk of a gate/up accumulator read from TMEM and its store into H (or the
+// energy partials).  Warp quarter q, lane L: v = TMEM lane 32q + L (packed row: gate channel 16q + L for
+// L < 16, up channel 16q + L - 16 otherwise) over 32 token columns; tok_l = token of column L of the chunk
+// (-1: none).  Lanes L and L + 16 exchange halves so that each computes h for 16 of the 32 tokens.
+__device__ __forceinline__ void gu_store_chunk(const GateUpArgs& a, const uint32_t (&v)[32], int tok_l, int slot,
+                                               int q, int lane) {
+  __nv_bfloat16* hbase = reinterpret_cast<__nv_bfloat16*>(a.h) + (int64_t)slot * kBlock + 16 * q + (lane & 15);
+  const bool swiglu = a.act == FP_ACT_SWIGLU;  // uniform: the SwiGLU loop carries no activation switch
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const uint32_t send = lane < 16 ? v[16 + j] : v[j];
+    const float recv = __uint_as_float(__shfl_xor_sync(0xffffffffu, send, 16));
+    const float gv = lane < 16 ? __uint_as_float(v[j]) : recv;
+    const float u = lane < 16 ? recv : __uint_as_float(v[16 + j]);
+    const float h = swiglu ? __fdividef(gv, 1.0f + __expf(-gv)) * u : pattention_act<false>(a.act, gv, u);
+    const int tok = __shfl_sync(0xffffffffu, tok_l, lane < 16 ? j : 16 + j);
+    if (a.energy) {
+      // |h| summed over this half-warp's 16 channels (fixed order), one partial per TMEM quarter
+      float e = fabsf(h);
+      e += __shfl_xor_sync(0xffffffffu, e, 8);
+      e += __shfl_xor_sync(0xffffffffu, e, 4);
+      e += __shfl_xor_sync(0xffffffffu, e, 2);
+      e += __shfl_xor_sync(0xffffffffu, e, 1);
+      if ((lane & 15) == 0 && tok >= 0) a.energy[((int64_t)q * a.M + tok) * a.nbl + slot] = e;
+    } else if (tok >= 0) {
+      hbase[(int64_t)tok * a.ldh] = __float2bfloat16_rn(h);
+    }
+  }
+}
+
 constexpr int kGatherWarps = 16;                         // token-row gather warps (cp.async)
 constexpr int kGatherThreads = 32 * kGatherWarps;
 constexpr int kGuThreads = 192 + kGatherThreads;         // warps 6.. gather
@@ -322,35 +352,13 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
       const uint32_t aph = (local >> 1) & 1;
       if (!warp_wait(&bars->accf[acc], aph, a.err, kErrWaitAccFull)) break;
       tc_fence_after();
-      __nv_bfloat16* hbase = reinterpret_cast<__nv_bfloat16*>(a.h) + (int64_t)t.slot * kBlock + 16 * q + (lane & 15);
       for (int c = 0; c * 32 < npad; ++c) {
         uint32_t v[32];
         __syncwarp();
         tmem_ld32(tmem_base + acc * kTileN + c * 32 + ((uint32_t)(32 * q) << 16), v);
         tmem_ld_wait();
         const int ni = c * 32 + lane;
-        const int tok_l = ni < t.n ? gu_token(t, ni, a) : -1;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          // lane L<16 holds gate(channel 16q+L), lane L+16 holds up(channel 16q+L), columns = tokens
-          const uint32_t send = lane < 16 ? v[16 + j] : v[j];
-          const float recv = __uint_as_float(__shfl_xor_sync(0xffffffffu, send, 16));
-          const float gv = lane < 16 ? __uint_as_float(v[j]) : recv;
-          const float u = lane < 16 ? recv : __uint_as_float(v[16 + j]);
-          const float h = pattention_act<false>(a.act, gv, u);  // silu(g) * u for SwiGLU
-          const int tok = __shfl_sync(0xffffffffu, tok_l, lane < 16 ? j : 16 + j);
-          if (a.energy) {
-            // |h| summed over this half-warp's 16 channels (fixed order), one partial per TMEM quarter
-            float e = fabsf(h);
-            e += __shfl_xor_sync(0xffffffffu, e, 8);
-            e += __shfl_xor_sync(0xffffffffu, e, 4);
-            e += __shfl_xor_sync(0xffffffffu, e, 2);
-            e += __shfl_xor_sync(0xffffffffu, e, 1);
-            if ((lane & 15) == 0 && tok >= 0) a.energy[((int64_t)q * a.M + tok) * a.nbl + t.slot] = e;
-          } else if (tok >= 0) {
-            hbase[(int64_t)tok * a.ldh] = __float2bfloat16_rn(h);
-          }
-        }
+        gu_store_chunk(a, v, ni < t.n ? gu_token(t, ni, a) : -1, t.slot, q, lane);
       }
       tc_fence_before();
       __syncwarp();
@@ -884,6 +892,195 @@ down2_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ C
   }
 }
 
+// ============================================================================================
+// Gate/up on CTA pairs for one active list shared by every token (pooled routing, the function-level
+// Pattention, dense): a pair computes two parameter blocks x 256 tokens.  The even CTA's A operand is
+// the 128 packed rows of block active[2p], the odd CTA's those of active[2p + 1]; each CTA loads 128 of
+// the 256 token rows (TMA boxes of x), so both blocks share the token operand and one k-step moves
+// 32 KB into each SM for 4.2 MFLOP (a one-SM 128 x 256 tile moves 48 KB).  Tiles run in groups of
+// kGu2GroupP block pairs so that the concurrent tiles' weights and token rows stay in L2.  With an odd
+// number of active blocks the last pair's odd CTA repeats the even CTA's block and stores nothing.
+// ============================================================================================
+constexpr int kGu2Stages = 6;
+constexpr int kGu2GroupP = 8;
+constexpr uint32_t kGu2ABytes = kTileM * kTileK * 2;  // 16 KB: 128 packed weight rows
+constexpr uint32_t kGu2BBytes = kTileM * kTileK * 2;  // 16 KB: 128 token rows
+constexpr uint32_t kGu2StageBytes = kGu2ABytes + kGu2BBytes;
+using Gu2Bars = PipeBarsT<kGu2Stages>;
+constexpr size_t kGu2Smem = 1024 + kGu2Stages * kGu2StageBytes + sizeof(Gu2Bars) + 64;
+static_assert(kGu2Smem <= 227 * 1024, "pair gate/up shared memory");
+
+__device__ __forceinline__ void gu2_tile(int tile, int P, int T, int& p, int& m) {
+  const int per_group = kGu2GroupP * T;
+  const int group = tile / per_group;
+  const int first = group * kGu2GroupP;
+  const int gsz = min(P - first, kGu2GroupP);
+  const int r = tile % per_group;
+  p = first + r % gsz;
+  m = r / gsz;
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+gateup2_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+               const GateUpArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = aligned_smem(smem_raw);
+  Gu2Bars* bars = reinterpret_cast<Gu2Bars*>(smem + kGu2Stages * kGu2StageBytes);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tm_x);
+    tma_prefetch_desc(&tm_w);
+    for (int s = 0; s < kGu2Stages; ++s) {
+      mbar_init(&bars->full[s], 1);   // leader: one expect_tx arrival + both CTAs' bytes
+      mbar_init(&bars->empty[s], 1);  // arrival from the leader's commit
+    }
+    for (int c = 0; c < 2; ++c) {
+      mbar_init(&bars->accf[c], 1);   // arrival from the leader's commit
+      mbar_init(&bars->acce[c], 8);   // leader: the 4 epilogue warps of both CTAs
+    }
+    mbar_init(&bars->done, 1);
+    bars->consumed = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc2(&bars->tmem, kTmemCols);
+    tmem_relinquish2();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before any remote arrival or pair commit
+  tc_fence_after();
+  griddep_wait();  // the active list and x are complete
+  griddep_launch_dependents();
+  const uint32_t tmem_base = bars->tmem;
+  const int P = (a.n_keys + 1) / 2;
+  const int T = (int)((a.M + 2 * kTileM - 1) / (2 * kTileM));
+  const int tiles = P * T;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int nkb = a.D / kTileK;
+  uint32_t issued = 0;
+
+  // this CTA's key (slot of H) of pair p; the odd CTA of a lone last block repeats the even CTA's block
+  auto my_key = [&](int p, bool& store) {
+    const int key = 2 * p + (int)rank;
+    store = key < a.n_keys;
+    return store ? key : 2 * p;
+  };
+
+  if (warp == 0) {
+    // ---------------- producer (both CTAs): own block's packed rows, own half of the token rows
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = pair; tile < tiles && ok; tile += npairs) {
+        int p, m;
+        gu2_tile(tile, P, T, p, m);
+        bool store;
+        int b = a.active[my_key(p, store)];
+        if (b < 0 || (int64_t)(b + 1) * kBlock > a.Np) {
+          record_error(a.err, kErrBadTile);  // reported; the loads read block 0, the epilogue stores nothing
+          b = 0;
+        }
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % kGu2Stages;
+          const uint32_t ph = (it / kGu2Stages) & 1u;
+          if (!mbar_wait(&bars->empty[s], ph ^ 1u, a.err, kErrWaitEmpty)) { ok = false; break; }
+          uint8_t* As = smem + s * kGu2StageBytes;
+          if (leader) mbar_arrive_expect_tx(&bars->full[s], 2 * kGu2StageBytes);
+          tma_load_2d_pair(As, &tm_w, &bars->full[s], 0, (b * nkb + kb) * kTileM);
+          tma_load_2d_pair(As + kGu2ABytes, &tm_x, &bars->full[s], kb * kTileK, m * 2 * kTileM + (int)rank * kTileM);
+        }
+      }
+      issued = it;
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- pair MMA issuer (leader only)
+    if (leader && lane == 0) {
+      uint32_t it = 0;
+      int local = 0;
+      bool ok = true;
+      const uint32_t idesc = umma_idesc_bf16(2 * kTileM, kTileN);
+      for (int tile = pair; tile < tiles && ok; tile += npairs) {
+        const int acc = local & 1;
+        const uint32_t aph = (local >> 1) & 1;
+        if (!mbar_wait_cluster(&bars->acce[acc], aph ^ 1u, a.err, kErrWaitAccEmpty)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kTileN;
+        for (int kb = 0; kb < nkb; ++kb) {
+          const int s = it % kGu2Stages;
+          const uint32_t ph = (it / kGu2Stages) & 1u;
+          if (!mbar_wait_cluster(&bars->full[s], ph, a.err, kErrWaitFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t ad = umma_desc_sw128(smem_u32(smem + s * kGu2StageBytes));
+          const uint64_t bd = umma_desc_sw128(smem_u32(smem + s * kGu2StageBytes + kGu2ABytes));
+#pragma unroll
+          for (int k = 0; k < kTileK / 16; ++k)
+            umma2_bf16(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+          umma2_commit(&bars->empty[s], 0x3);
+          ++it;
+        }
+        if (!ok) break;
+        umma2_commit(&bars->accf[acc], 0x3);
+        ++local;
+      }
+      bars->consumed = (int32_t)it;
+      umma2_commit(&bars->done, 0x1);
+      if (!mbar_wait(&bars->done, 0, nullptr, 0)) record_error(a.err, kErrDrain);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue (both CTAs): this CTA's block over the pair's 256 tokens
+    const int q = warp & 3;
+    int local = 0;
+    for (int tile = pair; tile < tiles; tile += npairs) {
+      int p, m;
+      gu2_tile(tile, P, T, p, m);
+      bool store;
+      const int key = my_key(p, store);
+      const int b = a.active[key];
+      store = store && b >= 0 && (int64_t)(b + 1) * kBlock <= a.Np;
+      const int acc = local & 1;
+      const uint32_t aph = (local >> 1) & 1;
+      if (!warp_wait(&bars->accf[acc], aph, a.err, kErrWaitAccFull)) break;
+      tc_fence_after();
+      if (store) {
+        for (int c = 0; c < kTileN / 32; ++c) {
+          uint32_t v[32];
+          __syncwarp();
+          tmem_ld32(tmem_base + acc * kTileN + c * 32 + ((uint32_t)(32 * q) << 16), v);
+          tmem_ld_wait();
+          const int64_t tok = (int64_t)m * 2 * kTileM + c * 32 + lane;
+          gu_store_chunk(a, v, tok < a.M ? (int)tok : -1, key, q, lane);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_leader(&bars->acce[acc]);
+      ++local;
+    }
+  }
+
+  // ---------------- teardown (as in down2_kernel)
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && leader && aborted(a.err)) {
+    for (uint32_t i = (uint32_t)bars->consumed; i < issued; ++i)
+      if (!mbar_wait(&bars->full[i % kGu2Stages], (i / kGu2Stages) & 1u, nullptr, 0)) {
+        record_error(a.err, kErrDrain);
+        break;
+      }
+  }
+  __syncthreads();
+  cluster_sync();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc2(tmem_base, kTmemCols);
+  }
+}
+
 // Sums the split-K partials [ks][n] in split order (deterministic) and writes the output dtype.
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int ks, int64_t n, void* out, int out_f32) {
   griddep_wait();  // every split's partial is stored
@@ -968,7 +1165,48 @@ static int launch_gateup_cfg(const GateUpArgs& a, cudaStream_t st) {
              ? FP_OK : FP_ERR_CUDA;
 }
 
+// Pair gate/up for a shared active list (see gateup2_kernel).
+static int launch_gateup2(const GateUpArgs& a, cudaStream_t st) {
+  CUtensorMap tx, tw;
+  if (!encode_map_2d(&tx, a.x, a.D, a.M, (uint64_t)a.D * 2, kTileK, kTileM) ||
+      !encode_map_2d(&tw, a.w_gu, kTileK, (uint64_t)a.Np * 2 * (a.D / kTileK), kTileK * 2, kTileK, kTileM))
+    return FP_ERR_CUDA;
+  static std::once_flag once;
+  static int attr = FP_OK;
+  static int max_pairs = 0;
+  std::call_once(once, [&] {
+    if (cudaFuncSetAttribute((const void*)gateup2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kGu2Smem) != cudaSuccess) {
+      attr = FP_ERR_CUDA;
+      return;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.num_sms & ~1);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = kGu2Smem;
+    cudaLaunchAttribute cl;
+    cl.id = cudaLaunchAttributeClusterDimension;
+    cl.val.clusterDim.x = 2;
+    cl.val.clusterDim.y = 1;
+    cl.val.clusterDim.z = 1;
+    cfg.attrs = &cl;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, (const void*)gateup2_kernel, &cfg) != cudaSuccess) n = 0;
+    max_pairs = n;
+  });
+  if (attr != FP_OK) return attr;
+  if (max_pairs <= 0) return FP_ERR_CUDA;
+  const int64_t tiles = (int64_t)((a.n_keys + 1) / 2) * ((a.M + 2 * kTileM - 1) / (2 * kTileM));
+  if (tiles <= 0) return FP_OK;
+  const int grid = 2 * (int)std::min<int64_t>(tiles, std::min(max_pairs, a.num_sms / 2));
+  return launch_pdl(gateup2_kernel, dim3(grid), dim3(kGemmThreads), kGu2Smem, st, tx, tw, a) == cudaSuccess
+             ? FP_OK : FP_ERR_CUDA;
+}
+
 int launch_gateup(const GateUpArgs& a, cudaStream_t st) {
+  // a shared active list over more than 128 tokens: block pairs on CTA pairs
+  if (!a.tiles && !a.energy && a.M > kTileM && a.num_sms >= 2) return launch_gateup2(a, st);
   // every tile of a batch of at most 64 tokens holds at most 64 tokens (a key's tokens are distinct)
   if (a.M <= GuSmall::kN) return launch_gateup_cfg<GuSmall>(a, st);
   return launch_gateup_cfg<GuBig>(a, st);
