@@ -593,9 +593,18 @@ def run_ours_sharded(args, rank, world, local, dev):
         for _ in range(args.warmup):
             step()
         t_ms, clk = timed_steps(step, K, dev, world, ClockSampler(gpu_smi_id(dev, local)))
-        # where the time goes on this rank: the shard's kernels for the whole batch in one piece (routing is
-        # replicated on every rank), and the reduce-scatter alone
-        stage = stage_split(lambda: fsi.sharding._cuda_partial(m, x, world, rank, rank == 0, False))
+        # where the time goes on this rank, for the whole batch in one piece: routing of this rank's
+        # tokens, the all-gather of the routes, the shard's kernels from the given routes (block lists and
+        # H clears, gate/up, down) and the reduce-scatter alone
+        s_rows = M // world
+        x_mine = x[rank * s_rows:(rank + 1) * s_rows]
+        t_route, _ = timed_steps(lambda: fsi.sharding._cuda_route(m, x_mine), 10, dev, world)
+        t_rag, _ = timed_steps(lambda: fsi.sharding._gather_routes(m, x_mine, None, world, rank,
+                                                                  fsi.sharding._cuda_route), 10, dev, world)
+        ridx, cnt, ctx = fsi.sharding._gather_routes(m, x_mine, None, world, rank, fsi.sharding._cuda_route)
+        stage = stage_split(lambda: fsi.sharding._cuda_routed_partial(m, x, world, rank, ridx, cnt, ctx))
+        stage["route_own_tokens"] = t_route / 10
+        stage["route_and_allgather"] = t_rag / 10
         part = torch.empty(M, D, dtype=pd, device=dev)
         ys = torch.empty(M // world, D, dtype=pd, device=dev)
         t_rs, _ = timed_steps(lambda: dist.reduce_scatter_tensor(ys, part), 10, dev, world)
@@ -617,12 +626,16 @@ def run_ours_sharded(args, rank, world, local, dev):
         "metric": METRIC, "value": M * K / (t_ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) x, N(0,0.02) weights)",
-        "config": config_block(wl, world, f"parameter blocks sharded b % {world} + NCCL reduce-scatter of "
+        "config": config_block(wl, world, f"parameter blocks sharded b % {world}, routing split over the "
+                                          f"ranks (routes all-gathered) + NCCL reduce-scatter of "
                                           f"{args.partial_dtype} partials, {ch} token chunks overlapped",
                                global_tokens=M),
         "tensor_peak_frac": total_flops / (ms_step / 1e3) / 1e12 / (peak * world),
         "active_blocks_per_token": a_mean,
         "stages_ms_rank0_unchunked": stage,
+        "stages_note": "route = block lists and H clears from the given routes; route_own_tokens = routing of "
+                       "this rank's 1/N of the tokens; route_and_allgather = the same plus the all-gather of "
+                       "the routes",
         "reduce_scatter_ms": t_rs / 10, "collective_bytes_per_rank": M * D * (2 if pd == torch.bfloat16 else 4),
         "roofline": roof,
         "e2e": e2e,

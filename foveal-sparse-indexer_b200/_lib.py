@@ -66,6 +66,12 @@ SIGNATURES = {
     "fp_pattention_fwd": (_c_int, [_c_p, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_p, _c_p, _c_p, _c_p, _c_p,
                                    _c_p, _c_int, _c_int, _c_p, _c_p, _c_sz, _c_p]),
     "fp_swiglu_fwd": (_c_int, [_c_p, _c_p, _c_int, _c_i64, _c_p, _c_p]),
+    "fp_route_workspace_size": (_c_sz, [_c_i64]),
+    "fp_route_tokens": (_c_int, [_c_p, _c_i64, _c_int, _c_int, _c_int, _c_p, _c_p, _c_int, _c_f, _c_int, _c_int, _c_f,
+                                 _c_p, _c_p, _c_p, _c_p, _c_p, _c_sz, _c_p]),
+    "fp_pattention_routed_fwd": (_c_int, [_c_p, _c_i64, _c_int, _c_int, _c_int, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
+                                          _c_int, _c_int, _c_p, _c_p, _c_p, _c_int, _c_int, _c_p, _c_int, _c_p,
+                                          _c_sz, _c_p]),
 }
 
 _lock = threading.Lock()

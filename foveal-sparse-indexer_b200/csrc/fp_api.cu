@@ -334,6 +334,108 @@ int fp_pattention_token_fwd(const void* x, int64_t M, int D, int NB, int dtype, 
   return FP_OK;
 }
 
+size_t fp_route_workspace_size(int64_t M) {
+  Carve c;
+  c.take(256);                                            // error word
+  c.take((size_t)std::max<int64_t>(M, 0) * 16 * 4);       // raw 16-D queries
+  return c.off;
+}
+
+int fp_route_tokens(const void* x, int64_t M, int D, int NB, int dtype, const void* q_proj, const void* block_keys,
+                    int base_blocks, float top_p, int min_remote, int max_remote, float temperature,
+                    int32_t* remote_indices, int32_t* remote_counts, float* ctx16, float* scores, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  FP_TRY(check_common(dtype, M, D, NB));
+  if (M == 0) return FP_OK;
+  if (!x || !q_proj || !block_keys || !remote_indices || !remote_counts || !workspace) return FP_ERR_INVALID_ARG;
+  if (base_blocks < 0 || base_blocks > NB || min_remote < 0 || max_remote < 0) return FP_ERR_INVALID_ARG;
+  if (!(temperature > 0.f)) return FP_ERR_INVALID_ARG;
+  if (!aligned16(x) || !aligned16(q_proj)) return FP_ERR_INVALID_ARG;
+  if (workspace_bytes < fp_route_workspace_size(M)) return FP_ERR_WORKSPACE;
+  int sms;
+  FP_TRY(device_info(sms));
+  cudaStream_t st = (cudaStream_t)stream;
+  int* err = at<int>(workspace, 0);
+  if (cudaMemsetAsync(err, 0, 256, st) != cudaSuccess) return FP_ERR_CUDA;
+  RouteArgs r{};
+  r.x = x; r.wq = q_proj; r.k16 = block_keys; r.M = M; r.D = D; r.NB = NB; r.temperature = temperature;
+  r.sel = SelectOut{NB, base_blocks, top_p, min_remote, max_remote, std::max(max_remote, 1), remote_indices,
+                    remote_counts, ctx16, nullptr};
+  r.scores = scores; r.q16 = nullptr; r.qraw = at<float>(workspace, 256); r.err = err; r.num_sms = sms;
+  return launch_route(r, dtype, st);
+}
+
+int fp_pattention_routed_fwd(const void* x, int64_t M, int D, int NB, int dtype, const void* k_gate,
+                             const void* k_up, const void* v, const void* w_gu, const void* v_t, const void* out_proj,
+                             int base_blocks, int capacity, const int32_t* remote_indices,
+                             const int32_t* remote_counts, const float* ctx16, int block_stride, int block_offset,
+                             void* y, int y_f32, void* workspace, size_t workspace_bytes, void* stream) {
+  FP_TRY(check_common(dtype, M, D, NB));
+  if (M == 0) return FP_OK;
+  if (!x || !k_gate || !k_up || !v || !y || !workspace || !remote_counts) return FP_ERR_INVALID_ARG;
+  if (capacity < 0 || (capacity > 0 && !remote_indices)) return FP_ERR_INVALID_ARG;
+  if (ctx16 && !out_proj) return FP_ERR_INVALID_ARG;
+  if (base_blocks < 0 || base_blocks > NB) return FP_ERR_INVALID_ARG;
+  if (block_stride < 1 || block_offset < 0 || block_offset >= block_stride) return FP_ERR_INVALID_ARG;
+  if (!aligned16(x)) return FP_ERR_INVALID_ARG;
+  const bool tc = tensor_path(dtype, D);
+  if (tc && (!v_t || !w_gu || !aligned16(v_t) || !aligned16(w_gu))) return FP_ERR_INVALID_ARG;
+  if (!tc && D > 32 * 256) return FP_ERR_UNSUPPORTED;
+  const int cap = std::max(capacity, 1);
+  const TokenLayout L = token_layout(dtype, M, D, NB, base_blocks, capacity, block_stride, block_offset);
+  if (workspace_bytes < L.total) return FP_ERR_WORKSPACE;
+  int sms;
+  FP_TRY(device_info(sms));
+  cudaStream_t st = (cudaStream_t)stream;
+  int* err = at<int>(workspace, L.err);
+  if (cudaMemsetAsync(err, 0, L.zero_bytes, st) != cudaSuccess) return FP_ERR_CUDA;
+  const int nbl = L.nbl;
+  const bool csr = tc && nbl > 0;
+  if (!csr) {
+    SimtArgs a{};
+    a.x = x; a.k_gate = k_gate; a.k_up = k_up; a.v = v; a.dtype = dtype; a.M = M; a.D = D; a.NB = NB;
+    a.base = base_blocks; a.ridx = remote_indices; a.rcnt = remote_counts; a.cap = cap;
+    a.active = nbl == 0 ? remote_counts : nullptr; a.n_active = 0;
+    a.stride = block_stride; a.offset = block_offset; a.ctx16 = ctx16; a.out_proj = out_proj; a.y = y;
+    a.y_f32 = y_f32;
+    return launch_simt(a, st);
+  }
+  stage_mark(0, st);
+  RouteArgs r{};
+  r.x = x; r.M = M; r.D = D; r.NB = NB; r.temperature = 1.0f;
+  r.sel = SelectOut{NB, base_blocks, 1.0f, 0, 0, cap, nullptr, nullptr, nullptr, nullptr};
+  r.err = err; r.num_sms = sms;
+  r.given_idx = remote_indices; r.given_cnt = remote_counts; r.given_cap = capacity;
+  int32_t* key_cnt = at<int32_t>(workspace, L.key_cnt);
+  int32_t* pair_tok = at<int32_t>(workspace, L.pair_tok);
+  int2* tiles = at<int2>(workspace, L.tiles);
+  int32_t* meta = at<int32_t>(workspace, L.meta);
+  void* h = at<void>(workspace, L.h);
+  r.hzero = static_cast<uint4*>(h); r.hrow_vec = (int64_t)nbl * kBlock * 2 / 16;
+  r.key_cnt = key_cnt; r.pair_tok = pair_tok; r.key_cap = L.key_cap;
+  r.stride = block_stride; r.offset = block_offset; r.nbl = nbl; r.chunk = L.chunk; r.nkey = L.nkey;
+  r.tiles = tiles; r.max_tiles = L.max_tiles; r.meta = meta;
+  r.ticket = reinterpret_cast<unsigned int*>(at<char>(workspace, L.err + kTicketOffset));
+  FP_TRY(launch_route(r, dtype, st));
+  stage_mark(1, st);
+  stage_mark(2, st);
+  GateUpArgs g{};
+  g.x = x; g.w_gu = w_gu; g.M = M; g.D = D; g.Np = NB * kBlock;
+  g.tiles = tiles; g.meta = meta; g.key_cnt = key_cnt; g.pair_tok = pair_tok; g.key_cap = L.key_cap;
+  g.nbl = nbl; g.stride = block_stride; g.offset = block_offset; g.active = nullptr; g.n_keys = 0;
+  g.h = h; g.ldh = (int64_t)nbl * kBlock; g.err = err; g.num_sms = sms;
+  FP_TRY(launch_gateup(g, st));
+  stage_mark(3, st);
+  DownArgs d{};
+  d.h = h; d.v_t = v_t; d.vt_tiled = 1; d.M = M; d.D = D; d.Np = NB * kBlock; d.K = nbl * kBlock; d.bmap = nullptr;
+  d.stride = block_stride; d.offset = block_offset; d.ctx16 = ctx16; d.out_proj = out_proj;
+  d.out_proj_f32 = dtype == FP_DTYPE_F32; d.y = y; d.y_f32 = y_f32; d.err = err; d.num_sms = sms;
+  d.ksplit = L.ksplit; d.y_acc = L.ksplit > 1 ? at<float>(workspace, L.yacc) : nullptr;
+  FP_TRY(launch_down(d, st));
+  stage_mark(4, st);
+  return FP_OK;
+}
+
 int fp_pattention_pooled_fwd(const void* x, int64_t M, int D, int NB, int dtype, const void* k_gate,
                              const void* k_up, const void* v, const void* w_gu, const void* v_t, const int32_t* active,
                              int n_active, const float* ctx16, const void* out_proj, void* y, int y_f32,

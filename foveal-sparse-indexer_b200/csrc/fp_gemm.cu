@@ -240,6 +240,7 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
   const uint32_t tmem_base = bars->tmem;
   const int ntiles = gathered ? a.meta[0] : a.n_keys * (int)((a.M + kN - 1) / kN);
   const int nkb = a.D / kTileK;
+  const int nbt = a.Np / kBlock;  // blocks of the packed weight (tile kb * nbt + b)
   uint32_t issued = 0;
 
   if (warp == 0) {
@@ -257,7 +258,7 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
           if (!mbar_wait(&bars->empty[s], ph ^ 1u, a.err, kErrWaitEmpty)) { ok = false; break; }
           uint8_t* As = smem + s * kStage;
           mbar_arrive_expect_tx(&bars->full[s], kABytes + (gathered ? 0u : Cfg::kBBytes));
-          tma_load_2d(As, &tm_w, &bars->full[s], 0, (t.b * nkb + kb) * kTileM);
+          tma_load_2d(As, &tm_w, &bars->full[s], 0, (kb * nbt + t.b) * kTileM);
           if (!gathered) tma_load_2d(As + kABytes, &tm_x, &bars->full[s], kb * kTileK, (int)t.r0);
         }
       }
@@ -373,18 +374,20 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
 // 16q .. 16q+15 and rows 32q+16 .. 32q+31 the up channels 16q .. 16q+15 (q = 0..3), so that after the
 // MMA (A = these rows) each 32-lane TMEM quarter holds the gate and up values of the same 16 channels.
 // Tile-contiguous: the 128 rows x 64 columns [kb*64, +64) of block b that one pipeline stage loads are
-// one contiguous 16 KB tile, tile index b * nkb + kb (nkb = D / 64), so every TMA box streams whole DRAM
-// pages instead of 128 bytes from each of 128 rows D * 2 bytes apart.
+// one contiguous 16 KB tile, so every TMA box streams whole DRAM pages instead of 128 bytes from each of
+// 128 rows D * 2 bytes apart.  Tiles are k-block-major (tile index kb * NB + b): the 64 tiles of one block
+// lie NB tiles apart, spread over the whole packed region, so that a CTA streaming one block (decode
+// tiles) reads from all of the memory evenly.
 __global__ void pack_gate_up_kernel(const uint4* __restrict__ kg, const uint4* __restrict__ ku, int64_t rows,
                                     int vec_per_row, uint4* __restrict__ wgu) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // over 2*rows*vec_per_row 16-byte words
   if (i >= 2 * rows * vec_per_row) return;
-  const int nkb = vec_per_row / 8;       // 8 words = one 64-element row of a tile
-  const int c = (int)(i & 7);
+  const int64_t NB = rows / 64;
+  const int c = (int)(i & 7);            // 8 words = one 64-element row of a tile
   const int r = (int)((i >> 3) & 127);   // packed row inside the block
-  const int64_t t = i >> 10;             // tile = b * nkb + kb
-  const int64_t b = t / nkb;
-  const int kb = (int)(t - b * nkb);
+  const int64_t t = i >> 10;             // tile = kb * NB + b
+  const int kb = (int)(t / NB);
+  const int64_t b = t - (int64_t)kb * NB;
   const int q = r >> 5, w = r & 31;
   const int64_t src_row = b * 64 + 16 * q + (w & 15);
   wgu[i] = (w < 16 ? kg : ku)[src_row * vec_per_row + kb * 8 + c];
@@ -550,7 +553,10 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
         down_tile(tile / ks, m_tiles, n_tiles, m, n);
         if (n * kTileN >= ncols) continue;
         const int sp = tile % ks;
-        const int kb0 = (int)((int64_t)sp * nkb_all / ks), kb1 = (int)((int64_t)(sp + 1) * nkb_all / ks);
+        // split sp takes k-blocks sp, sp + ks, sp + 2 ks, ...: the splits of a tile read interleaved
+        // pieces of the operands instead of one contiguous range each, which keeps their DRAM traffic
+        // spread evenly over the memory (contiguous ranges per CTA measured up to 2x apart in time)
+        const int kb0 = sp, kb1 = nkb_all;
         const int nv = a.nmap ? min(kTileN / kBlock, (ncols - n * kTileN) / kBlock) : 0;
         int nb[kTileN / kBlock];  // V_t row block of each valid column block, read once per tile
 #pragma unroll
@@ -558,9 +564,9 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
         // parameter block of the next k-block, loaded one iteration ahead so that the load's latency
         // overlaps the wait for a free stage
         int gb_next = kb0 < kb1 ? (a.bmap ? a.bmap[kb0] : kb0 * a.stride + a.offset) : 0;
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; kb += ks, ++it) {
           const int gb = gb_next;
-          if (kb + 1 < kb1) gb_next = a.bmap ? a.bmap[kb + 1] : (kb + 1) * a.stride + a.offset;
+          if (kb + ks < kb1) gb_next = a.bmap ? a.bmap[kb + ks] : (kb + ks) * a.stride + a.offset;
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1u;
           if (!mbar_wait(&bars->empty[s], ph ^ 1u, a.err, kErrWaitEmpty)) { ok = false; break; }
@@ -596,13 +602,13 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
         down_tile(tile / ks, m_tiles, n_tiles, m, n);
         if (n * kTileN >= ncols) continue;
         const int sp = tile % ks;
-        const int kb0 = (int)((int64_t)sp * nkb_all / ks), kb1 = (int)((int64_t)(sp + 1) * nkb_all / ks);
+        const int kb0 = sp, kb1 = nkb_all;  // interleaved k-blocks of split sp (see the producer)
         const int acc = local & 1;
         const uint32_t aph = (local >> 1) & 1;
         if (!mbar_wait(&bars->acce[acc], aph ^ 1u, a.err, kErrWaitAccEmpty)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kTileN;
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int kb = kb0; kb < kb1; kb += ks) {
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1u;
           if (!mbar_wait(&bars->full[s], ph, a.err, kErrWaitFull)) { ok = false; break; }
@@ -630,7 +636,7 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
       down_tile(tile / ks, m_tiles, n_tiles, m, n);
       if (n * kTileN >= ncols) continue;
       const int split = tile % ks;
-      const bool kempty = (int)((int64_t)(split + 1) * nkb_all / ks) <= (int)((int64_t)split * nkb_all / ks);
+      const bool kempty = split >= nkb_all;  // interleaved k-blocks: split s has none when s >= nkb_all
       const int acc = local & 1;
       const uint32_t aph = (local >> 1) & 1;
       if (!warp_wait(&bars->accf[acc], aph, a.err, kErrWaitAccFull)) break;
@@ -989,7 +995,7 @@ gateup2_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
           if (!mbar_wait(&bars->empty[s], ph ^ 1u, a.err, kErrWaitEmpty)) { ok = false; break; }
           uint8_t* As = smem + s * kGu2StageBytes;
           if (leader) mbar_arrive_expect_tx(&bars->full[s], 2 * kGu2StageBytes);
-          tma_load_2d_pair(As, &tm_w, &bars->full[s], 0, (b * nkb + kb) * kTileM);
+          tma_load_2d_pair(As, &tm_w, &bars->full[s], 0, (kb * (a.Np / kBlock) + b) * kTileM);
           tma_load_2d_pair(As + kGu2ABytes, &tm_x, &bars->full[s], kb * kTileK, m * 2 * kTileM + (int)rank * kTileM);
         }
       }
@@ -1150,7 +1156,7 @@ static int set_smem(const void* fn) {
 template <class Cfg>
 static int launch_gateup_cfg(const GateUpArgs& a, cudaStream_t st) {
   CUtensorMap tx, tw;
-  // w_gu in tile-contiguous form: rows of 64 elements, tile (b, kb) = rows [(b * nkb + kb) * 128, +128)
+  // w_gu in tile-contiguous form: rows of 64 elements, tile (b, kb) = rows [(kb * NB + b) * 128, +128)
   if (!encode_map_2d(&tx, a.x, a.D, a.M, (uint64_t)a.D * 2, kTileK, a.tiles ? 1 : Cfg::kN) ||
       !encode_map_2d(&tw, a.w_gu, kTileK, (uint64_t)a.Np * 2 * (a.D / kTileK), kTileK * 2, kTileK, kTileM))
     return FP_ERR_CUDA;

@@ -103,6 +103,12 @@ struct RouteArgs {
   unsigned int* ticket; // CTA completion counter
   int* err;
   int num_sms;
+  // Given routes (block-sharded forward with the routing split over ranks): remote ids [M, given_cap]
+  // and counts [M] computed elsewhere; the kernel then only builds the block lists, the tile list and the
+  // H clears (no projection, scores or selection)
+  const int32_t* given_idx = nullptr;
+  const int32_t* given_cnt = nullptr;
+  int given_cap = 0;
 };
 int launch_route(const RouteArgs& a, int dtype, cudaStream_t st);
 

@@ -870,8 +870,9 @@ route_kernel(const RouteArgs a) {
   const int64_t ngroups = (a.M + kRouteTokens - 1) / kRouteTokens;
   const uint64_t hrow = (uint64_t)a.hrow_vec * 16;
 
+  const bool given = a.given_idx != nullptr;
   // ---- once per CTA: keys, the zero source of the H clears, the key counters
-  stage_keys<T>(static_cast<const T*>(a.k16), NB, nbp, skT);
+  if (!given) stage_keys<T>(static_cast<const T*>(a.k16), NB, nbp, skT);
   if (a.hzero) {
     uint4* z = reinterpret_cast<uint4*>(smb + L.zbuf);
     for (int i = threadIdx.x; i < (int)(kRouteZeroBytes / 16); i += blockDim.x) z[i] = make_uint4(0u, 0u, 0u, 0u);
@@ -899,7 +900,7 @@ route_kernel(const RouteArgs a) {
     }
     {  // this warp's tokens only (other warps may already be working on theirs): lane (tt, j)
       const int r = warp * TPW + (lane >> 4);
-      if (lane < 16 * TPW && tok0 + r < a.M) qsm[r][lane & 15] = __ldcg(&a.qraw[(tok0 + r) * 16 + (lane & 15)]);
+      if (!given && lane < 16 * TPW && tok0 + r < a.M) qsm[r][lane & 15] = __ldcg(&a.qraw[(tok0 + r) * 16 + (lane & 15)]);
       if (lane < TPW) s_npair[warp * TPW + lane] = 0;
     }
     __syncwarp();
@@ -913,6 +914,34 @@ route_kernel(const RouteArgs a) {
       const int r = warp * TPW + tt;
       const int64_t tok = tok0 + r;
       if (tok >= a.M) break;
+      if (given) {
+        // the token's route, computed by another rank: its remote ids into sbuf
+        const int cmax = a.given_cap < NB - a.sel.base ? a.given_cap : NB - a.sel.base;  // fits sbuf / plist
+        int c = __ldg(&a.given_cnt[tok]);
+        c = c < 0 ? 0 : (c > cmax ? cmax : c);
+        if (csr) {
+          for (int i = lane; i < c; i += 32) sbuf[i] = __ldg(&a.given_idx[tok * a.given_cap + i]);
+          __syncwarp();
+          int32_t* pl = reinterpret_cast<int32_t*>(smb + L.plist) + r * N;
+          const int npair = a.sel.base + c;
+          for (int sl = lane; sl < npair; sl += 32) {
+            const int b = sl < a.sel.base ? sl : sbuf[sl - a.sel.base];
+            int e = -1;
+            if (b < 0 || b >= NB) {
+              record_error(a.err, kErrBadTile);  // a given id outside the blocks: reported, skipped
+            } else if (b % a.stride == a.offset) {
+              const int kl = b / a.stride;
+              const int pos = atomicAdd(&s_cnt[kl], 1);
+              if (pos < 16) e = (kl << 4) | pos;  // a block listed twice by the group's tokens could exceed
+              else record_error(a.err, kErrBadTile);  // the 16 positions of an entry: reported, skipped
+            }
+            pl[sl] = e;
+          }
+          if (lane == 0) s_npair[r] = npair;
+        }
+        __syncwarp();  // sbuf is rewritten by the next token of this warp
+        continue;
+      }
       float qn[16];
       float ss = 0.f;
 #pragma unroll
@@ -1174,7 +1203,9 @@ template <typename T, int E>
 int route_go(const RouteArgs& a, bool mma, cudaStream_t st) {
   const int64_t pblocks = (a.M + kProjTokens - 1) / kProjTokens;
   const int64_t groups = (a.M + kRouteTokens - 1) / kRouteTokens;
-  if (mma)
+  if (a.given_idx) {
+    // routes given: no projection; the routing kernel builds the block lists only
+  } else if (mma)
     route_proj_kernel<__nv_bfloat16, true><<<(unsigned)pblocks, kRouteWarps * 32, 0, st>>>(
         static_cast<const __nv_bfloat16*>(a.x), static_cast<const __nv_bfloat16*>(a.wq), a.M, a.D, a.qraw);
   else

@@ -226,6 +226,60 @@ def token_forward(x2d, k_gate, k_up, v, packed, q_proj, block_keys, out_proj, *,
     return y, ridx, cnt, S
 
 
+def route_tokens(x2d, q_proj, block_keys, *, base_blocks: int, top_p: float, min_remote: int, max_remote: int,
+                 temperature: float = 1.0, want_ctx: bool = True):
+    """Routing only (``fp_route_tokens``): (remote_indices [M, max(K_max, 1)] int32, remote_counts [M] int32,
+    ctx16 [M, 16] fp32 or None) of the token-routed forward."""
+    dev = require_cuda(x2d, q_proj, block_keys)
+    dtt = x2d.dtype
+    x2d = contig(x2d)
+    M, D = x2d.shape
+    NB = block_keys.shape[0]
+    q_proj, block_keys = contig(q_proj.detach().to(dtt)), contig(block_keys.detach().to(dtt))
+    cap = max(int(max_remote), 1)
+    ridx = torch.empty(M, cap, dtype=torch.int32, device=dev)
+    cnt = torch.empty(M, dtype=torch.int32, device=dev)
+    ctx = torch.empty(M, 16, dtype=torch.float32, device=dev) if want_ctx else None
+    lib = _lib.load()
+    ws = _lib.workspace(dev, lib.fp_route_workspace_size(M))
+    rc = lib.fp_route_tokens(ptr(x2d), M, D, NB, dtype_code(dtt), ptr(q_proj), ptr(block_keys), int(base_blocks),
+                             float(top_p), int(min_remote), int(max_remote), float(temperature), ptr(ridx), ptr(cnt),
+                             ptr(ctx), None, ptr(ws), ws.numel(), stream_handle(dev))
+    check(rc, "fp_route_tokens")
+    return ridx, cnt, ctx
+
+
+def routed_forward(x2d, k_gate, k_up, v, packed, out_proj, remote_indices, remote_counts, ctx16, *,
+                   base_blocks: int, block_stride: int = 1, block_offset: int = 0, out_f32: bool = False,
+                   y: Optional[torch.Tensor] = None):
+    """Contraction of the blocks ``b % block_stride == block_offset`` from given routes
+    (``fp_pattention_routed_fwd``): y [M, D] (fp32 when ``out_f32``) plus ctx16 . W_out^T where ctx16 is
+    given (rows of zeros add nothing)."""
+    dev = require_cuda(x2d, k_gate, k_up, v, remote_indices, remote_counts)
+    dtt = x2d.dtype
+    dt = dtype_code(dtt)
+    x2d = contig(x2d)
+    M, D = x2d.shape
+    NB = k_gate.shape[0] // 64
+    k_gate, k_up, v = contig(k_gate.detach()), contig(k_up.detach()), contig(v.detach())
+    out_proj = contig(out_proj.detach().to(dtt)) if out_proj is not None else None
+    ridx = contig(remote_indices.to(torch.int32))
+    cnt = contig(remote_counts.to(torch.int32))
+    ctx16 = contig(ctx16.float()) if ctx16 is not None else None
+    cap = ridx.shape[1]
+    if y is None:
+        y = torch.empty(M, D, dtype=torch.float32 if out_f32 else dtt, device=dev)
+    w_gu, v_t = packed if packed is not None else (None, None)
+    lib = _lib.load()
+    ws = _lib.workspace(dev, lib.fp_token_workspace_size(dt, M, D, NB, int(base_blocks), cap, int(block_stride)))
+    rc = lib.fp_pattention_routed_fwd(ptr(x2d), M, D, NB, dt, ptr(k_gate), ptr(k_up), ptr(v), ptr(w_gu), ptr(v_t),
+                                      ptr(out_proj), int(base_blocks), cap, ptr(ridx), ptr(cnt), ptr(ctx16),
+                                      int(block_stride), int(block_offset), ptr(y), 1 if out_f32 else 0, ptr(ws),
+                                      ws.numel(), stream_handle(dev))
+    check(rc, "fp_pattention_routed_fwd")
+    return y
+
+
 def pooled_forward(x2d, k_gate, k_up, v, packed, active, *, ctx16=None, out_proj=None, out_f32: bool = False):
     """Forward over one shared active set (``fp_pattention_pooled_fwd``); y [M, D].  ``packed`` as in
     :func:`token_forward`."""

@@ -1,16 +1,21 @@
 """Multi-GPU execution of the token-routed forward (one process per GPU, ``torch.distributed``).
 
-Two layouts, chosen by the caller:
+Layouts, chosen by the caller:
 
-* **Parameter-block sharding** (large shapes, e.g. the 70B MLP): every rank holds x and all router
-  parameters, runs the same deterministic router for all tokens, and computes the contraction only
-  over the blocks it owns (block b belongs to rank ``b % world``, so the always-on base blocks are
-  spread over ranks).  The fp32 partial outputs are summed with a collective (all-reduce, or
-  reduce-scatter over token rows).  The additive stream is added once, by rank 0.  This is the only
-  exchange step of the path.  With ``chunks > 1`` the tokens are processed in chunks and the collective
-  of chunk i runs (NCCL, on its own stream) while chunk i+1 is computed.
-* **Token splitting** (small shapes / throughput runs): each rank processes its own tokens with
-  replicated weights.  Tokens are independent, so there is no collective at all.
+* **Parameter-block sharding** (the 8B / 70B MLP shapes): every rank computes the contraction only over
+  the blocks it owns (block b belongs to rank ``b % world``, so the always-on base blocks are spread over
+  ranks) for all tokens, and the partial outputs are summed by one collective (reduce-scatter over token
+  rows, or all-reduce).  Partials are bf16 for a bf16 model (half the NVLink bytes of fp32).
+  The routing is split over the ranks as well: each rank routes only its share of the tokens
+  (``fp_route_tokens``), one all-gather of the routes (block ids and counts, 4·(K_max + 1) bytes per
+  token) gives every rank all of them, and each rank's contraction runs from the given routes
+  (``fp_pattention_routed_fwd``).  The additive stream of a token is added by the rank that routed it.
+  With ``chunks > 1`` the tokens are processed in chunks and the reduce-scatter of chunk i (NCCL, on its
+  own stream) runs while chunk i+1 is computed.  Routes are deterministic per token, so the result
+  equals the single-GPU forward's (the bf16 partial sums round differently).
+* **Token-partitioned input** (``sharded_forward_slices`` / ``sharded_forward_host``): each rank starts
+  from its own slice of the batch; an all-gather brings every slice's rows of a chunk to every rank.
+* **Token splitting**: each rank processes its own tokens with replicated weights; no collective.
 """
 
 from __future__ import annotations
@@ -24,12 +29,15 @@ import torch.distributed as dist
 from . import kernels
 
 
-def shard_parameter_blocks(module, group=None, partial_dtype: Optional[torch.dtype] = None) -> None:
+def shard_parameter_blocks(module, group=None, partial_dtype: Optional[torch.dtype] = None,
+                           shard_routing: bool = True) -> None:
     """Makes ``module`` (routing="token") compute only the parameter blocks of this rank.
 
     ``partial_dtype``: dtype of the partial outputs that the collective sums (default: the module's
     dtype, so a bf16 model moves bf16 partials, half the bytes of fp32; the reduction of N bf16 partials
-    stays well inside the 2e-2 relative bar of bf16 outputs).  ``torch.float32`` keeps fp32 partials."""
+    stays well inside the 2e-2 relative bar of bf16 outputs).  ``torch.float32`` keeps fp32 partials.
+    ``shard_routing``: route only this rank's share of the tokens and all-gather the routes (when the
+    token count divides by the world size); False routes every token on every rank."""
     if module.routing != "token":
         raise ValueError("parameter-block sharding applies to routing='token'")
     rank = dist.get_rank(group)
@@ -39,6 +47,7 @@ def shard_parameter_blocks(module, group=None, partial_dtype: Optional[torch.dty
     if pd not in (torch.float32, torch.bfloat16):
         raise ValueError("partial_dtype must be torch.float32 or torch.bfloat16")
     module._shard_partial_dtype = pd
+    module._shard_routing = bool(shard_routing)
 
 
 def owned_blocks(num_blocks: int, rank: int, world: int):
@@ -51,12 +60,50 @@ def _partial_dtype(module) -> torch.dtype:
 
 
 def _cuda_partial(module, x2d, world: int, rank: int, additive: bool, want_routes: bool, out=None):
+    """Replicated routing: this rank's blocks for all tokens, routing every token here."""
     kg, ku, v, packed, wq, k16, wout = module._weights()
     return kernels.token_forward(
         x2d, kg, ku, v, packed, wq, k16, wout, base_blocks=module.base_blocks, top_p=module.top_p,
         min_remote=module.min_remote_blocks, max_remote=module.max_remote_blocks,
         temperature=module.temperature, additive=additive, block_stride=world, block_offset=rank,
         out_f32=_partial_dtype(module) == torch.float32, want_routes=want_routes, y=out)
+
+
+def _cuda_route(module, x_mine):
+    """Routes of this rank's rows: (remote_indices [s, cap] int32, remote_counts [s] int32, ctx16 [s, 16])."""
+    _, _, _, _, wq, k16, _ = module._weights()
+    return kernels.route_tokens(x_mine, wq, k16, base_blocks=module.base_blocks, top_p=module.top_p,
+                                min_remote=module.min_remote_blocks, max_remote=module.max_remote_blocks,
+                                temperature=module.temperature)
+
+
+def _cuda_routed_partial(module, xc, world: int, rank: int, ridx, cnt, ctx16, out=None):
+    """This rank's blocks for the rows of ``xc`` from given routes, plus the additive stream of the rows
+    whose ctx16 rows are given (zeros elsewhere)."""
+    kg, ku, v, packed, _, _, wout = module._weights()
+    return kernels.routed_forward(xc, kg, ku, v, packed, wout, ridx, cnt, ctx16, base_blocks=module.base_blocks,
+                                  block_stride=world, block_offset=rank,
+                                  out_f32=_partial_dtype(module) == torch.float32, y=out)
+
+
+def _gather_routes(module, x_mine, group, world: int, rank: int, route_fn):
+    """Route this rank's rows and all-gather every rank's routes in rank order: (ridx [world*s, cap],
+    cnt [world*s], ctx16 [world*s, 16] with this rank's rows' contexts and zeros elsewhere).  One
+    collective carries ids and counts together."""
+    s = x_mine.shape[0]
+    ridx, cnt, ctx = route_fn(module, x_mine)
+    cap = ridx.shape[1]
+    mine = torch.cat([ridx.to(torch.int32), cnt.to(torch.int32)[:, None]], dim=1).contiguous()
+    allr = torch.empty(world * s, cap + 1, dtype=torch.int32, device=x_mine.device)
+    dist.all_gather_into_tensor(allr, mine, group=group)
+    ctx_full = torch.zeros(world * s, 16, dtype=torch.float32, device=x_mine.device)
+    ctx_full[rank * s:(rank + 1) * s] = ctx
+    return allr[:, :cap], allr[:, cap], ctx_full
+
+
+def _use_shard_routing(module, M: int, world: int, want_routes: bool, compute_partial) -> bool:
+    return (getattr(module, "_shard_routing", False) and not want_routes and compute_partial is None
+            and M % world == 0)
 
 
 def _comm_stream(module, device) -> torch.cuda.Stream:
@@ -68,24 +115,52 @@ def _comm_stream(module, device) -> torch.cuda.Stream:
 
 
 def sharded_token_forward(module, x2d: torch.Tensor, *, want_routes: bool = False, reduce: str = "all",
-                          compute_partial: Optional[Callable] = None, chunks: int = 1):
-    """Parameter-block-sharded forward.  Returns (y, remote_indices, remote_counts, scores); with
-    ``reduce="scatter"`` y holds only this rank's contiguous slice of token rows.
+                          compute_partial: Optional[Callable] = None, chunks: int = 1,
+                          route_fn: Optional[Callable] = None, routed_fn: Optional[Callable] = None):
+    """Parameter-block-sharded forward of a batch held by every rank.  Returns (y, remote_indices,
+    remote_counts, scores); with ``reduce="scatter"`` y holds only this rank's contiguous slice of token
+    rows.
 
     ``chunks > 1`` overlaps the collective with compute: chunk i's partial is reduced on a side stream
     while chunk i+1 is computed.  For ``reduce="scatter"`` chunk i gathers, for every rank r, the i-th
     piece of r's output slice, so that each rank's result stays one contiguous slice; this needs the
-    token count to divide by ``world * chunks``.  Routes are returned only without chunking."""
+    token count to divide by ``world * chunks``.  Routes are returned only without chunking (and then the
+    routing is replicated).  ``compute_partial`` / ``route_fn`` + ``routed_fn`` replace the CUDA kernels
+    (host-side tests)."""
     rank, world, group = module._shard
-    fn = compute_partial or _cuda_partial
     if reduce not in ("all", "scatter"):
         raise ValueError("reduce must be 'all' or 'scatter'")
     M, D = x2d.shape
     if reduce == "scatter" and M % world:
         raise ValueError("reduce='scatter' needs the token count to divide by the world size")
+    chunks = 1 if want_routes else max(1, int(chunks))
+    split_routes = route_fn is not None or (_use_shard_routing(module, M, world, want_routes, compute_partial)
+                                            and M % (world * chunks) == 0)
+    route_fn = route_fn or _cuda_route
+    routed_fn = routed_fn or _cuda_routed_partial
+    fn = compute_partial or _cuda_partial
+    pd = _partial_dtype(module)
+    rank_major = split_routes or (chunks > 1 and reduce == "scatter")
+    if rank_major and M % (world * chunks):
+        raise ValueError("sharding with split routing or a chunked reduce-scatter needs the token count to "
+                         "divide by world * chunks")
+    s = M // (world * chunks) if rank_major else 0
+
+    def partial_of(xc, xv_mine):
+        """This rank's partial for the rows of xc (rank-major pieces; xv_mine = this rank's piece)."""
+        if split_routes:
+            ridx, cnt, ctx = _gather_routes(module, xv_mine, group, world, rank, route_fn)
+            return routed_fn(module, xc, world, rank, ridx, cnt, ctx).to(pd)
+        return fn(module, xc, world, rank, rank == 0, False)[0].to(pd)
+
     if chunks <= 1 or want_routes:
-        y_part, ridx, cnt, S = fn(module, x2d, world, rank, rank == 0, want_routes)
-        y_part = y_part.to(_partial_dtype(module))
+        if split_routes:
+            xv = x2d.view(world, s, D)
+            y_part = partial_of(x2d, xv[rank])
+            ridx = cnt = S = None
+        else:
+            y_part, ridx, cnt, S = fn(module, x2d, world, rank, rank == 0, want_routes)
+            y_part = y_part.to(pd)
         if reduce == "all":
             dist.all_reduce(y_part, op=dist.ReduceOp.SUM, group=group)
             y = y_part
@@ -94,8 +169,6 @@ def sharded_token_forward(module, x2d: torch.Tensor, *, want_routes: bool = Fals
             dist.reduce_scatter_tensor(y, y_part, op=dist.ReduceOp.SUM, group=group)
         return y.to(x2d.dtype), ridx, cnt, S
 
-    if reduce == "scatter" and M % (world * chunks):
-        raise ValueError("chunked reduce='scatter' needs the token count to divide by world * chunks")
     # CUDA: each chunk's collective is issued from a side stream that waits for that chunk's compute, so
     # NCCL reduces chunk i while the compute stream runs chunk i+1 (host tensors: plain sequence)
     cuda = x2d.is_cuda
@@ -113,8 +186,8 @@ def sharded_token_forward(module, x2d: torch.Tensor, *, want_routes: bool = Fals
         return torch.cuda.stream(comm)
 
     works = []
-    pd = _partial_dtype(module)
-    if reduce == "all":
+    if not rank_major:
+        # all-reduce with the routing replicated: contiguous token chunks, each partial written in place
         y = torch.empty(M, D, dtype=pd, device=x2d.device)
         bounds = [M * i // chunks for i in range(chunks + 1)]
         for i in range(chunks):
@@ -122,8 +195,7 @@ def sharded_token_forward(module, x2d: torch.Tensor, *, want_routes: bool = Fals
             if fn is _cuda_partial:  # the kernel writes its partial straight into the output rows
                 part = fn(module, x2d[lo:hi], world, rank, rank == 0, False, out=y[lo:hi])[0]
             else:
-                part = fn(module, x2d[lo:hi], world, rank, rank == 0, False)[0]
-                y[lo:hi].copy_(part.to(pd))
+                y[lo:hi].copy_(fn(module, x2d[lo:hi], world, rank, rank == 0, False)[0].to(pd))
                 part = y[lo:hi]
             with after_compute():
                 works.append(dist.all_reduce(part, op=dist.ReduceOp.SUM, group=group, async_op=True))
@@ -131,34 +203,45 @@ def sharded_token_forward(module, x2d: torch.Tensor, *, want_routes: bool = Fals
             w.wait()
         return y.to(x2d.dtype), None, None, None
 
-    s = M // (world * chunks)  # rows of one rank's piece of one chunk
+    # chunk i holds piece i of every rank's row slice (rank-major), so that the routing of chunk i is split
+    # over the ranks and, for reduce-scatter, each rank's output stays one contiguous slice
     xv = x2d.view(world, chunks, s, D)
-    y = torch.empty(M // world, D, dtype=pd, device=x2d.device)
+    parts = []
+    y = torch.empty(M // world, D, dtype=pd, device=x2d.device) if reduce == "scatter" else None
     for i in range(chunks):
-        xc = xv[:, i].reshape(world * s, D)  # rank-major: piece i of every rank's slice
-        part, _, _, _ = fn(module, xc, world, rank, rank == 0, False)
-        part = part.to(pd)
+        part = partial_of(xv[:, i].reshape(world * s, D), xv[rank, i])
         with after_compute():
-            out = y[i * s:(i + 1) * s]
-            works.append(dist.reduce_scatter_tensor(out, part, op=dist.ReduceOp.SUM, group=group, async_op=True))
+            if reduce == "all":
+                parts.append(part)
+                works.append(dist.all_reduce(part, op=dist.ReduceOp.SUM, group=group, async_op=True))
+            else:
+                works.append(dist.reduce_scatter_tensor(y[i * s:(i + 1) * s], part, op=dist.ReduceOp.SUM,
+                                                        group=group, async_op=True))
     for w in works:
         w.wait()
+    if reduce == "all":  # back from rank-major pieces to token order
+        y = torch.stack(parts).view(chunks, world, s, D).transpose(0, 1).reshape(M, D)
     return y.to(x2d.dtype), None, None, None
 
 
 def sharded_forward_slices(module, x_slice: torch.Tensor, *, chunks: int = 1,
-                           compute_partial: Optional[Callable] = None) -> torch.Tensor:
+                           compute_partial: Optional[Callable] = None, route_fn: Optional[Callable] = None,
+                           routed_fn: Optional[Callable] = None) -> torch.Tensor:
     """Block-sharded forward of a token batch that is partitioned over the ranks.
 
     Every rank passes its own contiguous slice of the batch's token rows (the same number on every rank)
     and receives the output rows of that slice.  Per chunk: an all-gather brings piece i of every rank's
-    slice to every rank (NVLink, rank-major), each rank computes the partial output of its parameter
-    blocks over those rows, and a reduce-scatter returns to every rank the sum for its own piece.  Chunk
-    i+1's all-gather is issued before chunk i's reduce-scatter, so on GPUs the collectives of one chunk
-    run while another chunk computes.  No rank ever holds more than its slice of the input at the start:
-    the host-to-device traffic of a job is split over the ranks' links instead of every rank copying the
-    whole batch."""
+    slice to every rank (NVLink, rank-major), each rank routes its own piece and the routes are
+    all-gathered (or, with ``compute_partial``, every rank routes all rows), each rank computes the partial
+    output of its parameter blocks over those rows, and a reduce-scatter returns to every rank the sum for
+    its own piece.  Chunk i+1's all-gather is issued before chunk i's reduce-scatter, so on GPUs the
+    collectives of one chunk run while another chunk computes.  No rank ever holds more than its slice of
+    the input at the start: the host-to-device traffic of a job is split over the ranks' links instead of
+    every rank copying the whole batch."""
     rank, world, group = module._shard
+    split_routes = route_fn is not None or (getattr(module, "_shard_routing", False) and compute_partial is None)
+    route_fn = route_fn or _cuda_route
+    routed_fn = routed_fn or _cuda_routed_partial
     fn = compute_partial or _cuda_partial
     s_all, D = x_slice.shape
     chunks = max(1, min(int(chunks), s_all)) if s_all else 1
@@ -180,7 +263,11 @@ def sharded_forward_slices(module, x_slice: torch.Tensor, *, chunks: int = 1,
     rs = []
     for i in range(chunks):
         ag[i].wait()  # the current stream waits for chunk i's rows
-        part = fn(module, gathered[i], world, rank, rank == 0, False)[0].to(pd)
+        if split_routes:
+            ridx, cnt, ctx = _gather_routes(module, x_slice[i * s:(i + 1) * s], group, world, rank, route_fn)
+            part = routed_fn(module, gathered[i], world, rank, ridx, cnt, ctx).to(pd)
+        else:
+            part = fn(module, gathered[i], world, rank, rank == 0, False)[0].to(pd)
         rs.append(dist.reduce_scatter_tensor(y[i * s:(i + 1) * s], part, op=dist.ReduceOp.SUM, group=group,
                                              async_op=True))
         if i + 2 < chunks:
@@ -193,9 +280,10 @@ def sharded_forward_slices(module, x_slice: torch.Tensor, *, chunks: int = 1,
 def sharded_forward_host(module, x_host: torch.Tensor, out: Optional[torch.Tensor] = None, *,
                          chunks: int = 4) -> torch.Tensor:
     """:func:`sharded_forward_slices` for a slice held in host memory (pinned for the copies to overlap):
-    each chunk's rows are copied to the device on a copy stream, gathered, computed and reduce-scattered,
-    and its output rows copied back on another stream while later chunks run.  Returns the output slice
-    in host memory, complete once the caller's current stream has been synchronised."""
+    each chunk's rows are copied to the device on a copy stream, gathered, routed (this rank's rows, routes
+    all-gathered), computed and reduce-scattered, and its output rows copied back on another stream while
+    later chunks run.  Returns the output slice in host memory, complete once the caller's current stream
+    has been synchronised."""
     rank, world, group = module._shard
     dev = module.k_gate.device
     s_all, D = x_host.shape
@@ -207,6 +295,7 @@ def sharded_forward_host(module, x_host: torch.Tensor, out: Optional[torch.Tenso
         out = torch.empty(s_all, D, dtype=x_host.dtype, pin_memory=True)
     if s_all == 0:
         return out
+    split_routes = getattr(module, "_shard_routing", False)
     st = getattr(module, "_shard_host_streams", None)
     if st is None or st[0].device != dev:
         st = tuple(torch.cuda.Stream(device=dev) for _ in range(3))
@@ -234,7 +323,11 @@ def sharded_forward_host(module, x_host: torch.Tensor, out: Optional[torch.Tenso
     ag = [gather(0)] + ([gather(1)] if chunks > 1 else [])
     for i in range(chunks):
         ag[i].wait()
-        part = _cuda_partial(module, gathered[i], world, rank, rank == 0, False)[0]
+        if split_routes:
+            ridx, cnt, ctx = _gather_routes(module, x_dev[i * s:(i + 1) * s], group, world, rank, _cuda_route)
+            part = _cuda_routed_partial(module, gathered[i], world, rank, ridx, cnt, ctx)
+        else:
+            part = _cuda_partial(module, gathered[i], world, rank, rank == 0, False)[0]
         w = dist.reduce_scatter_tensor(y_dev[i * s:(i + 1) * s], part, op=dist.ReduceOp.SUM, group=group,
                                        async_op=True)
         with torch.cuda.stream(s_out):

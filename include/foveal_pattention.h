@@ -112,7 +112,8 @@ FP_API int fp_pooled_route(const void* x, const void* q_proj, const void* block_
  * tile:
  *   w_gu (2 * Np * D elements): per parameter block b, 128 packed rows (rows 32q..32q+15 = k_gate
  *        channels 16q..16q+15 and rows 32q+16..32q+31 = k_up channels 16q..16q+15 of the block, q = 0..3);
- *        the 128 x 64 tile of columns [kb*64, +64) is contiguous at element offset (b * D/64 + kb) * 8192
+ *        the 128 x 64 tile of columns [kb*64, +64) is contiguous at element offset (kb * Np/64 + b) * 8192
+ *        (k-block-major: a block's tiles are spread over the whole buffer)
  *   v_t  (ceil(D / 256) * 256 * Np elements): v transposed in 256 x 64 tiles; the tile of output columns
  *        [n*256, +256) and parameter tokens [b*64, +64) is contiguous (row = output column, 64 elements)
  *        at element offset (n * Np/64 + b) * 16384; columns past D are zero
@@ -150,6 +151,34 @@ FP_API int fp_pattention_token_fwd(const void* x, int64_t M, int D, int NB, int 
                             int block_stride, int block_offset, void* y, int y_f32,
                             int32_t* remote_indices, int32_t* remote_counts, float* scores,
                             void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * The token-routed forward split in two, for parameter-block sharding with the routing itself split
+ * over the ranks: each rank routes only its slice of the tokens (fp_route_tokens: the projection, scores
+ * and select_blocks of fp_pattention_token_fwd), the ranks exchange the routes (an all-gather), and each
+ * rank runs the contraction of its blocks for all tokens from the given routes (fp_pattention_routed_fwd:
+ * block lists, gate/up, down and the additive stream of the rows whose ctx16 is given).  Together they
+ * replace the same reference functions as fp_pattention_token_fwd.
+ *   fp_route_tokens: remote_indices [M, max_remote] int32, remote_counts [M] int32, ctx16 [M, 16] fp32
+ *   (softmax(S/T) . K_16, may be NULL), scores [M, NB] fp32 (may be NULL); workspace of
+ *   fp_route_workspace_size(M) bytes.
+ *   fp_pattention_routed_fwd: remote_indices [M, capacity], remote_counts [M] as written by
+ *   fp_route_tokens (ids outside [0, NB) are reported in the device error word and skipped); ctx16 [M, 16]
+ *   or NULL (rows of zeros add nothing); block_stride / block_offset and y / y_f32 as in
+ *   fp_pattention_token_fwd; workspace of fp_token_workspace_size(dtype, M, D, NB, base_blocks, capacity,
+ *   block_stride) bytes.
+ */
+FP_API size_t fp_route_workspace_size(int64_t M);
+FP_API int fp_route_tokens(const void* x, int64_t M, int D, int NB, int dtype, const void* q_proj,
+                           const void* block_keys, int base_blocks, float top_p, int min_remote, int max_remote,
+                           float temperature, int32_t* remote_indices, int32_t* remote_counts, float* ctx16,
+                           float* scores, void* workspace, size_t workspace_bytes, void* stream);
+FP_API int fp_pattention_routed_fwd(const void* x, int64_t M, int D, int NB, int dtype, const void* k_gate,
+                                    const void* k_up, const void* v, const void* w_gu, const void* v_t,
+                                    const void* out_proj, int base_blocks, int capacity,
+                                    const int32_t* remote_indices, const int32_t* remote_counts, const float* ctx16,
+                                    int block_stride, int block_offset, void* y, int y_f32, void* workspace,
+                                    size_t workspace_bytes, void* stream);
 
 /*
  * Pooled forward over one shared active set.  Replaces the active-block execution of

@@ -319,6 +319,34 @@ def test_block_shards_sum_to_full():
     assert rel_err(sum(parts).cpu(), full.cpu()) < 1e-5
 
 
+def test_split_routing_entry_points():
+    """The token-routed forward split in two (fp_route_tokens, then fp_pattention_routed_fwd from the given
+    routes): the routes equal the fused forward's, four stride-4 shards from the given routes (additive
+    stream from shard 0's context rows only) sum to the fused forward, and one unsharded call equals it."""
+    wl = configs.CONFIGS["8b"]
+    w = configs.make_weights(wl)
+    x2d = configs.make_x(wl).reshape(-1, wl.hidden_dim)[:1000].contiguous().to(DEV, torch.bfloat16)
+    m = module_for(wl, w)
+    kg, ku, v, packed, wq, k16, wout = m._weights()
+    kw = dict(base_blocks=wl.base_blocks, top_p=wl.top_p, min_remote=wl.min_remote_blocks,
+              max_remote=wl.max_remote_blocks)
+    full, ridx0, cnt0, _ = fsi.kernels.token_forward(x2d, kg, ku, v, packed, wq, k16, wout, out_f32=True,
+                                                     want_routes=True, **kw)
+    ridx, cnt, ctx = fsi.kernels.route_tokens(x2d, wq, k16, **kw)
+    assert torch.equal(cnt, cnt0)
+    bad, _ = compare_routes(ridx.cpu(), cnt.cpu(), ridx0.cpu(), cnt0.cpu())
+    assert bad == 0
+    one = fsi.kernels.routed_forward(x2d, kg, ku, v, packed, wout, ridx, cnt, ctx, base_blocks=wl.base_blocks,
+                                     out_f32=True)
+    assert rel_err(one.cpu(), full.cpu()) < 1e-6
+    zero = torch.zeros_like(ctx)
+    parts = [fsi.kernels.routed_forward(x2d, kg, ku, v, packed, wout, ridx, cnt, ctx if r == 0 else zero,
+                                        base_blocks=wl.base_blocks, block_stride=4, block_offset=r, out_f32=True)
+             for r in range(4)]
+    assert rel_err(sum(parts).cpu(), full.cpu()) < 1e-5
+    device_error_is_clear()
+
+
 def test_all_blocks_active_equals_dense():
     wl = configs.CONFIGS["8b"].with_(hidden_dim=1024, intermediate_dim=2048)
     w = configs.make_weights(wl)

@@ -68,15 +68,20 @@ def _worker(rank, world, port, out_dir):
         ysc, _, _, _ = fsi.sharding.sharded_token_forward(m, x, reduce="scatter", chunks=4)
         # bf16 partials (the bf16 model's default): half the bytes on NVLink
         mb = module()
-        fsi.sharding.shard_parameter_blocks(mb)
+        fsi.sharding.shard_parameter_blocks(mb)  # routing split over the ranks (the default)
         ysb, _, _, _ = fsi.sharding.sharded_token_forward(mb, x, reduce="scatter", chunks=4)
+        ysa, _, _, _ = fsi.sharding.sharded_token_forward(mb, x, reduce="all", chunks=2)
+        mr = module()
+        fsi.sharding.shard_parameter_blocks(mr, shard_routing=False)  # every rank routes every token
+        ysr, _, _, _ = fsi.sharding.sharded_token_forward(mr, x, reduce="scatter", chunks=4)
         # token-partitioned input: each rank passes only its slice (all-gather, compute, reduce-scatter),
         # from device memory and from pinned host memory
         ysl = fsi.sharding.sharded_forward_slices(mb, x[rows].contiguous(), chunks=4)
         yh = fsi.sharding.sharded_forward_host(mb, x[rows].cpu().pin_memory(), chunks=4)
     torch.cuda.synchronize()
     e_all = max(rel_err(y.float(), full.float()), rel_err(yc.float(), full.float()))
-    e_sc = max(rel_err(t.float().cpu(), full[rows].float().cpu()) for t in (ys, ysc, ysb, ysl, yh))
+    e_all = max(e_all, rel_err(ysa.float(), full.float()))
+    e_sc = max(rel_err(t.float().cpu(), full[rows].float().cpu()) for t in (ys, ysc, ysb, ysr, ysl, yh))
     same_routes = bool(torch.equal(info["remote_indices"], info_full["remote_indices"]))
     with open(os.path.join(out_dir, f"r{rank}.txt"), "w") as f:
         f.write(f"{e_all} {e_sc} {int(same_routes)}")

@@ -72,6 +72,80 @@ def _oracle_partial(module, x2d, world, rank, additive, want_routes):
     return y, idx, cnt, S
 
 
+def _oracle_route(module, x_mine):
+    """Routes of this rank's rows (oracle): (ids [s, cap], counts [s], ctx16 [s, 16])."""
+    import oracle
+    w = m_weights(module)
+    S = oracle.router_scores(x_mine, w.q_proj_16d, w.block_keys_16d) / module.temperature
+    r = oracle.select_blocks_noncausal(S[None], local_window_blocks=module.base_blocks, top_p=module.top_p,
+                                       min_remote_blocks=module.min_remote_blocks,
+                                       max_remote_blocks=module.max_remote_blocks,
+                                       remote_capacity=module.max_remote_blocks)
+    ctx = torch.softmax(S, dim=-1) @ w.block_keys_16d
+    return r.remote_indices[0], r.remote_counts[0], ctx
+
+
+def _oracle_routed(module, xc, world, rank, ridx, cnt, ctx16):
+    """This rank's blocks from given routes (oracle) plus ctx16 . W_out^T of the given context rows."""
+    w = m_weights(module)
+    M = xc.shape[0]
+    sel = torch.zeros(M, module.num_blocks, dtype=torch.bool)
+    sel[:, :module.base_blocks] = True
+    for t in range(M):
+        sel[t, ridx[t, :int(cnt[t])].long()] = True
+    y = torch.zeros(M, xc.shape[1])
+    for b in range(rank, module.num_blocks, world):
+        toks = sel[:, b].nonzero().flatten()
+        if toks.numel():
+            rows = slice(b * 64, (b + 1) * 64)
+            xb = xc[toks]
+            h = torch.nn.functional.silu(xb @ w.k_gate[rows].t()) * (xb @ w.k_up[rows].t())
+            y.index_add_(0, toks, h @ w.v[rows])
+    return y + ctx16 @ w.out_proj_16d.t()
+
+
+def _split_routes_worker(rank, world, port, out_dir):
+    """Routing split over the ranks: each rank routes its share, the routes are all-gathered, each rank's
+    contraction runs from the given routes (sharded_token_forward, chunked; sharded_forward_slices)."""
+    _setup(rank, world, port)
+    from conftest import fsi
+    import oracle
+
+    torch.manual_seed(0)
+    m = fsi.FovealPattentionMLP(hidden_dim=64, intermediate_dim=640, base_blocks=2, remote_blocks=3,
+                                dtype=torch.float32, routing="token", top_p=0.7, min_remote_blocks=1,
+                                max_remote_blocks=3)
+    with torch.no_grad():
+        m.out_proj_16d.weight.normal_(std=0.05)
+    M = 8 * world
+    x2d = torch.randn(M, 64)
+    fsi.sharding.shard_parameter_blocks(m)
+    hooks = dict(route_fn=_oracle_route, routed_fn=_oracle_routed)
+    ya, _, _, _ = fsi.sharding.sharded_token_forward(m, x2d, reduce="all", **hooks)
+    yac, _, _, _ = fsi.sharding.sharded_token_forward(m, x2d, reduce="all", chunks=2, **hooks)
+    ys, _, _, _ = fsi.sharding.sharded_token_forward(m, x2d, reduce="scatter", chunks=4, **hooks)
+    s = M // world
+    yl = fsi.sharding.sharded_forward_slices(m, x2d[rank * s:(rank + 1) * s].contiguous(), chunks=2, **hooks)
+    ref = oracle.token_forward(x2d, m_weights(m), base_blocks=2, top_p=0.7, min_remote_blocks=1,
+                               max_remote_blocks=3)["y"]
+    mine = ref[rank * s:(rank + 1) * s]
+    errs = [float((ya - ref).norm() / ref.norm()), float((yac - ref).norm() / ref.norm()),
+            float((ys - mine).norm() / mine.norm()), float((yl - mine).norm() / mine.norm())]
+    with open(os.path.join(out_dir, f"r{rank}.txt"), "w") as f:
+        f.write(" ".join(str(e) for e in errs))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_split_routing_matches_full(world):
+    port = _free_port()
+    with tempfile.TemporaryDirectory() as d:
+        mp.spawn(_split_routes_worker, args=(world, port, d), nprocs=world, join=True)
+        for r in range(world):
+            errs = list(map(float, open(os.path.join(d, f"r{r}.txt")).read().split()))
+            assert len(errs) == 4 and max(errs) < 1e-5, (r, errs)
+
+
 def _shard_worker(rank, world, port, out_dir):
     _setup(rank, world, port)
     from conftest import fsi
