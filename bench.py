@@ -48,6 +48,9 @@ configs = fsi.configs
 METRIC = "Pattention-MLP fwd tokens/s & % bf16 tensor peak (8B shape), 1/2/4/8 B200 vs host CPU"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 KERNELS_PER_STEP = 4  # route_proj, route (selection + block lists), gateup, down
+# block-sharded step with split routing, per token chunk: route_proj + route of this rank's tokens, the
+# routing kernel's block-list pass over the given routes, gateup, down
+KERNELS_PER_SHARDED_CHUNK = 5
 
 
 def parse():
@@ -642,7 +645,7 @@ def run_ours_sharded(args, rank, world, local, dev):
         "token_split": {"value": world * M * K / (t_split / 1e3), "unit": "tokens/s", "scaling": "weak",
                         "ms_per_step": t_split / K, "tokens_per_rank": M,
                         "parallelism": f"token split x{world} (no collective)"},
-        "gpu_launches": KERNELS_PER_STEP * ch * K,
+        "gpu_launches": KERNELS_PER_SHARDED_CHUNK * ch * K,
         "clocks": clk,
         "device_error": err,
     }
