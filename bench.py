@@ -49,8 +49,10 @@ METRIC = "Pattention-MLP fwd tokens/s & % bf16 tensor peak (8B shape), 1/2/4/8 B
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 KERNELS_PER_STEP = 4  # route_proj, route (selection + block lists), gateup, down
 # block-sharded step with split routing, per token chunk: route_proj + route of this rank's tokens, the
-# routing kernel's block-list pass over the given routes, gateup, down
+# routing kernel's block-list pass over the given routes, gateup, down (+ the flag and combine kernels of
+# the peer-memory reduce-scatter)
 KERNELS_PER_SHARDED_CHUNK = 5
+KERNELS_PEER_REDUCE = 2
 
 
 def parse():
@@ -69,7 +71,14 @@ def parse():
                     help="tokens of the CPU-baseline sample (about 10-30 s of host work over 3 timed calls)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the decode / sweep / 70B / pooled keys")
-    ap.add_argument("--shard-chunks", type=int, default=4, help="N > 1: token chunks of the block-sharded step")
+    ap.add_argument("--shard-chunks", type=int, default=1,
+                    help="N > 1: token chunks of the device-resident block-sharded step (1: the routes are "
+                         "split over the ranks and the whole batch runs as one piece; measured fastest)")
+    ap.add_argument("--reduce", choices=["nccl", "peer"], default="nccl",
+                    help="N > 1: sum of the block shards' partials by the NCCL reduce-scatter, or through peer "
+                         "memory (the down projection stores each row's partial on the rank that owns it)")
+    ap.add_argument("--e2e-chunks", type=int, default=4,
+                    help="N > 1: token chunks of the host-buffer block-sharded step (copies overlap compute)")
     ap.add_argument("--partial-dtype", choices=["bf16", "fp32"], default="bf16",
                     help="N > 1: dtype of the partial outputs the reduce-scatter sums")
     return ap.parse_args()
@@ -588,7 +597,8 @@ def run_ours_sharded(args, rank, world, local, dev):
         t_split, _ = timed_steps(lambda: m(x_own), K, dev, world)
         del x_own
         # block sharding
-        fsi.sharding.shard_parameter_blocks(m, partial_dtype=pd)
+        peer = args.reduce == "peer"
+        fsi.sharding.shard_parameter_blocks(m, partial_dtype=pd, peer_reduce=peer)
 
         def step():
             fsi.sharding.sharded_token_forward(m, x, reduce="scatter", chunks=ch)
@@ -612,6 +622,12 @@ def run_ours_sharded(args, rank, world, local, dev):
         ys = torch.empty(M // world, D, dtype=pd, device=dev)
         t_rs, _ = timed_steps(lambda: dist.reduce_scatter_tensor(ys, part), 10, dev, world)
         err = fsi._lib.device_error(fsi._lib.workspace(dev, 0))
+        peer_state = getattr(m, "_peer_state", None)
+        peer_used = peer_state is not None and peer_state.epoch > 0
+        if peer_state is not None:
+            err = err or fsi._lib.device_error(peer_state.err)
+        fsi.sharding.release_peer_buffers(m)
+        m._peer_reduce = False  # the host-buffer path below reduces with NCCL
         e2e = measure_e2e_sharded(args, m, x_cpu, rank, world, dev)
         del m, x, part, ys
         fsi._lib.release_workspaces()
@@ -630,9 +646,14 @@ def run_ours_sharded(args, rank, world, local, dev):
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) x, N(0,0.02) weights)",
         "config": config_block(wl, world, f"parameter blocks sharded b % {world}, routing split over the "
-                                          f"ranks (routes all-gathered) + NCCL reduce-scatter of "
-                                          f"{args.partial_dtype} partials, {ch} token chunks overlapped",
+                                          f"ranks (routes all-gathered) + "
+                                          + ("peer-memory reduce-scatter (down projection stores each row's "
+                                             "partial on its owner over NVLink, then a combine kernel)"
+                                             if peer_used else "NCCL reduce-scatter")
+                                          + f" of {args.partial_dtype} partials, "
+                                          + (f"{ch} token chunks overlapped" if ch > 1 else "one piece"),
                                global_tokens=M),
+        "reduce": "peer" if peer_used else "nccl",
         "tensor_peak_frac": total_flops / (ms_step / 1e3) / 1e12 / (peak * world),
         "active_blocks_per_token": a_mean,
         "stages_ms_rank0_unchunked": stage,
@@ -645,7 +666,7 @@ def run_ours_sharded(args, rank, world, local, dev):
         "token_split": {"value": world * M * K / (t_split / 1e3), "unit": "tokens/s", "scaling": "weak",
                         "ms_per_step": t_split / K, "tokens_per_rank": M,
                         "parallelism": f"token split x{world} (no collective)"},
-        "gpu_launches": KERNELS_PER_SHARDED_CHUNK * ch * K,
+        "gpu_launches": (KERNELS_PER_SHARDED_CHUNK + (KERNELS_PEER_REDUCE if peer_used else 0)) * ch * K,
         "clocks": clk,
         "device_error": err,
     }
@@ -663,14 +684,15 @@ def measure_e2e_sharded(args, m, x_cpu, rank, world, dev):
     x_host = x_cpu[rank * s:(rank + 1) * s].to(torch.bfloat16).pin_memory()
     y_host = torch.empty(s, D, dtype=torch.bfloat16).pin_memory()
     E = args.e2e_steps or max(10, args.steps // 10)
-    step = lambda: fsi.sharding.sharded_forward_host(m, x_host, out=y_host, chunks=args.shard_chunks)  # noqa: E731
+    step = lambda: fsi.sharding.sharded_forward_host(m, x_host, out=y_host, chunks=args.e2e_chunks)  # noqa: E731
     for _ in range(3):
         step()
     t, _ = timed_steps(step, E, dev, world)
     return {"value": M * E / (t / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": M * D * 2,
             "d2h_bytes_per_step": M * D * 2, "steps": E, "bytes_note": "summed over ranks (each copies its slice)",
             "path": "sharding.sharded_forward_host: each rank's slice from pinned host memory, NVLink all-gather, "
-                    "shard compute, reduce-scatter, pinned host output slice"}
+                    "shard compute, reduce-scatter, pinned host output slice",
+            "chunks": args.e2e_chunks}
 
 
 def blockshard_70b(args, rank, world, dev, pd):
@@ -686,7 +708,7 @@ def blockshard_70b(args, rank, world, dev, pd):
     for _ in range(3):
         m(x)
     t1, _ = timed_steps(lambda: m(x), K, dev, world)
-    fsi.sharding.shard_parameter_blocks(m, partial_dtype=pd)
+    fsi.sharding.shard_parameter_blocks(m, partial_dtype=pd, peer_reduce=args.reduce == "peer")
     step = lambda: fsi.sharding.sharded_token_forward(m, x, reduce="scatter", chunks=args.shard_chunks)  # noqa: E731
     for _ in range(3):
         step()
@@ -694,7 +716,8 @@ def blockshard_70b(args, rank, world, dev, pd):
     M = x.shape[0]
     out = {"tokens": M, "value": M * K / (tn / 1e3), "unit": "tokens/s", "ms_per_step": tn / K,
            "one_gpu_ms_per_step": t1 / K, "efficiency": (t1 / K) / (world * tn / K),
-           "speedup": t1 / tn}
+           "speedup": t1 / tn, "reduce": "peer" if getattr(m, "_peer_state", None) is not None else "nccl"}
+    fsi.sharding.release_peer_buffers(m)
     del m, x
     fsi._lib.release_workspaces()
     torch.cuda.empty_cache()

@@ -19,6 +19,7 @@ LIB_PATH = os.path.join(HERE, "libfovealpatt.so")
 
 FP_DTYPE_F32 = 0
 FP_DTYPE_BF16 = 1
+FP_ERR_UNSUPPORTED = 2
 
 _c_int, _c_i64, _c_f, _c_p, _c_sz = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p, ctypes.c_size_t
 
@@ -54,6 +55,18 @@ SIGNATURES = {
     "fp_block_sparse_linear_workspace_size": (_c_sz, [_c_int, _c_i64, _c_int, _c_int, _c_int]),
     "fp_block_sparse_linear_fwd": (_c_int, [_c_p, _c_i64, _c_int, _c_p, _c_p, _c_int, _c_int, _c_p, _c_p, _c_int,
                                             _c_p, _c_p, _c_p, _c_p, _c_sz, _c_p]),
+    "fp_pack_blocked_weight": (_c_int, [_c_p, _c_int, _c_int, _c_p, _c_p]),
+    "fp_block_sparse_linear_blocked_fwd": (_c_int, [_c_p, _c_i64, _c_int, _c_p, _c_p, _c_p, _c_int, _c_int, _c_p,
+                                                    _c_p, _c_int, _c_p, _c_p, _c_p, _c_p, _c_sz, _c_p]),
+    "fp_peer_alloc": (_c_int, [_c_sz, ctypes.POINTER(_c_p), _c_p]),
+    "fp_peer_open": (_c_int, [_c_p, ctypes.POINTER(_c_p)]),
+    "fp_peer_close": (_c_int, [_c_p]),
+    "fp_peer_free": (_c_int, [_c_p]),
+    "fp_pattention_routed_peer_fwd": (_c_int, [_c_p, _c_i64, _c_int, _c_int, _c_int, _c_p, _c_p, _c_p, _c_p, _c_p,
+                                               _c_p, _c_int, _c_int, _c_p, _c_p, _c_p, _c_int, _c_int, _c_p, _c_p,
+                                               _c_int, _c_i64, ctypes.c_uint32, _c_int, _c_p, _c_sz, _c_p]),
+    "fp_peer_combine": (_c_int, [_c_p, _c_p, _c_int, _c_i64, _c_int, _c_int, ctypes.c_uint32, _c_p, _c_int, _c_p,
+                                 _c_sz, _c_p]),
     "fp_tokenformer_workspace_size": (_c_sz, [_c_int, _c_i64, _c_int]),
     "fp_tokenformer_fwd": (_c_int, [_c_p, _c_i64, _c_int, _c_p, _c_p, _c_p, _c_int, _c_int, _c_int, _c_int, _c_p,
                                     _c_p, _c_p, _c_p, _c_p, _c_p, _c_sz, _c_p]),

@@ -34,8 +34,8 @@ bool tensor_path(int dtype, int D) { return dtype == FP_DTYPE_BF16 && D % 64 == 
 int layout_sms();
 
 struct TokenLayout {
-  size_t err, zero_bytes, key_cnt, meta, qraw, ridx, rcnt, ctx, pair_tok, tiles, h, yacc, total;
-  int ksplit;
+  size_t err, zero_bytes, key_cnt, meta, qraw, ridx, rcnt, ctx, pair_tok, tiles, h, yacc, gu_part, total;
+  int ksplit, gu_ks;
   int nbl, chunk, nkey, max_tiles;
   int64_t key_cap;
 };
@@ -51,6 +51,11 @@ TokenLayout token_layout(int dtype, int64_t M, int D, int NB, int base, int kmax
   L.nkey = (int)(nchunks * std::max(L.nbl, 1));
   L.key_cap = std::min<int64_t>(L.chunk, std::max<int64_t>(M, 1));
   const bool tc = tensor_path(dtype, D);
+  const int64_t pairs = M * (int64_t)(base + kmax);
+  L.max_tiles = (int)(pairs / kGuN + L.nkey + 1);
+  // batches of at most 64 tokens split each gate/up tile's contraction over D (work balance of the
+  // decode step)
+  L.gu_ks = tc && M <= 64 ? gateup_decode_ksplit(D) : 1;
   // error word, completion ticket and the block-CSR key counters: cleared by one memset per call.  The
   // error word stays at offset 0 (fp_noalloc_device_error reads it there in the library's scratch array).
   L.zero_bytes = 256 + (tc ? (size_t)L.nkey * 4 : 0);
@@ -61,14 +66,13 @@ TokenLayout token_layout(int dtype, int64_t M, int D, int NB, int base, int kmax
   L.ridx = c.take((size_t)M * std::max(kmax, 1) * 4);
   L.rcnt = c.take((size_t)M * 4);
   L.ctx = c.take((size_t)M * 16 * 4);
-  const int64_t pairs = M * (int64_t)(base + kmax);
-  L.max_tiles = (int)(pairs / kGuN + L.nkey + 1);
   if (tc) {
     L.pair_tok = c.take((size_t)L.nkey * L.key_cap * 4);
     L.tiles = c.take((size_t)L.max_tiles * 8);
     L.h = c.take((size_t)M * L.nbl * kBlock * 2);
     L.ksplit = down_ksplit(M, D, std::max(L.nbl, 1), layout_sms());
     if (L.ksplit > 1) L.yacc = c.take((size_t)L.ksplit * M * D * 4);
+    if (L.gu_ks > 1) L.gu_part = c.take((size_t)L.max_tiles * L.gu_ks * kTileM * 64 * 4);
   }
   L.total = c.off;
   return L;
@@ -322,6 +326,9 @@ int fp_pattention_token_fwd(const void* x, int64_t M, int D, int NB, int dtype, 
   g.tiles = tiles; g.meta = meta; g.key_cnt = key_cnt; g.pair_tok = pair_tok; g.key_cap = L.key_cap;
   g.nbl = nbl; g.stride = block_stride; g.offset = block_offset; g.active = nullptr; g.n_keys = 0;
   g.h = h; g.ldh = (int64_t)nbl * kBlock; g.err = err; g.num_sms = sms;
+  if (L.gu_ks > 1) {
+    g.gu_ks = L.gu_ks; g.gu_part = at<float>(workspace, L.gu_part); g.max_tiles = L.max_tiles;
+  }
   FP_TRY(launch_gateup(g, st));
   stage_mark(3, st);
   DownArgs d{};
@@ -329,6 +336,10 @@ int fp_pattention_token_fwd(const void* x, int64_t M, int D, int NB, int dtype, 
   d.stride = block_stride; d.offset = block_offset; d.ctx16 = ctx; d.out_proj = out_proj;
   d.out_proj_f32 = dtype == FP_DTYPE_F32; d.y = y; d.y_f32 = y_f32; d.err = err; d.num_sms = sms;
   d.ksplit = L.ksplit; d.y_acc = L.ksplit > 1 ? at<float>(workspace, L.yacc) : nullptr;
+  if (M <= 64) {
+    // one gate/up tile per touched block, in block order: contract over the touched blocks only
+    d.ktiles = tiles; d.knbl = nbl; d.kcnt = meta;
+  }
   FP_TRY(launch_down(d, st));
   stage_mark(4, st);
   return FP_OK;
@@ -365,14 +376,31 @@ int fp_route_tokens(const void* x, int64_t M, int D, int NB, int dtype, const vo
   return launch_route(r, dtype, st);
 }
 
-int fp_pattention_routed_fwd(const void* x, int64_t M, int D, int NB, int dtype, const void* k_gate,
-                             const void* k_up, const void* v, const void* w_gu, const void* v_t, const void* out_proj,
-                             int base_blocks, int capacity, const int32_t* remote_indices,
-                             const int32_t* remote_counts, const float* ctx16, int block_stride, int block_offset,
-                             void* y, int y_f32, void* workspace, size_t workspace_bytes, void* stream) {
+namespace {
+// Peer output of the routed forward: partial rows to the ranks that own them, then the writer's flag.
+struct PeerSpec {
+  void* const* out;        // [world] this rank's receive slot on each rank
+  uint32_t* const* flags;  // [world] this rank's flag word on each rank
+  int world;
+  int64_t rows;            // token rows per rank
+  uint32_t epoch;
+};
+
+int routed_fwd_impl(const void* x, int64_t M, int D, int NB, int dtype, const void* k_gate, const void* k_up,
+                    const void* v, const void* w_gu, const void* v_t, const void* out_proj, int base_blocks,
+                    int capacity, const int32_t* remote_indices, const int32_t* remote_counts, const float* ctx16,
+                    int block_stride, int block_offset, void* y, int y_f32, void* workspace, size_t workspace_bytes,
+                    void* stream, const PeerSpec* peer) {
   FP_TRY(check_common(dtype, M, D, NB));
   if (M == 0) return FP_OK;
-  if (!x || !k_gate || !k_up || !v || !y || !workspace || !remote_counts) return FP_ERR_INVALID_ARG;
+  if (!x || !k_gate || !k_up || !v || (!y && !peer) || !workspace || !remote_counts) return FP_ERR_INVALID_ARG;
+  if (peer) {
+    if (peer->world < 1 || peer->world > kMaxPeers || !peer->out || !peer->flags || peer->rows <= 0 ||
+        M != (int64_t)peer->world * peer->rows)
+      return FP_ERR_INVALID_ARG;
+    for (int w = 0; w < peer->world; ++w)
+      if (!peer->out[w] || !peer->flags[w] || !aligned16(peer->out[w])) return FP_ERR_INVALID_ARG;
+  }
   if (capacity < 0 || (capacity > 0 && !remote_indices)) return FP_ERR_INVALID_ARG;
   if (ctx16 && !out_proj) return FP_ERR_INVALID_ARG;
   if (base_blocks < 0 || base_blocks > NB) return FP_ERR_INVALID_ARG;
@@ -384,6 +412,9 @@ int fp_pattention_routed_fwd(const void* x, int64_t M, int D, int NB, int dtype,
   const int cap = std::max(capacity, 1);
   const TokenLayout L = token_layout(dtype, M, D, NB, base_blocks, capacity, block_stride, block_offset);
   if (workspace_bytes < L.total) return FP_ERR_WORKSPACE;
+  // peer output: the tensor-core path whose contraction stores whole rows (no split-K), checked before any
+  // launch so that every rank of a job (same M) falls back together
+  if (peer && (!tc || L.nbl == 0 || L.ksplit > 1)) return FP_ERR_UNSUPPORTED;
   int sms;
   FP_TRY(device_info(sms));
   cudaStream_t st = (cudaStream_t)stream;
@@ -424,6 +455,9 @@ int fp_pattention_routed_fwd(const void* x, int64_t M, int D, int NB, int dtype,
   g.tiles = tiles; g.meta = meta; g.key_cnt = key_cnt; g.pair_tok = pair_tok; g.key_cap = L.key_cap;
   g.nbl = nbl; g.stride = block_stride; g.offset = block_offset; g.active = nullptr; g.n_keys = 0;
   g.h = h; g.ldh = (int64_t)nbl * kBlock; g.err = err; g.num_sms = sms;
+  if (L.gu_ks > 1) {
+    g.gu_ks = L.gu_ks; g.gu_part = at<float>(workspace, L.gu_part); g.max_tiles = L.max_tiles;
+  }
   FP_TRY(launch_gateup(g, st));
   stage_mark(3, st);
   DownArgs d{};
@@ -431,9 +465,46 @@ int fp_pattention_routed_fwd(const void* x, int64_t M, int D, int NB, int dtype,
   d.stride = block_stride; d.offset = block_offset; d.ctx16 = ctx16; d.out_proj = out_proj;
   d.out_proj_f32 = dtype == FP_DTYPE_F32; d.y = y; d.y_f32 = y_f32; d.err = err; d.num_sms = sms;
   d.ksplit = L.ksplit; d.y_acc = L.ksplit > 1 ? at<float>(workspace, L.yacc) : nullptr;
+  if (M <= 64) {
+    d.ktiles = tiles; d.knbl = nbl; d.kcnt = meta;
+  }
+  if (peer) {
+    for (int w = 0; w < peer->world; ++w) d.peer_y[w] = peer->out[w];
+    d.peer_rows = peer->rows;
+  }
   FP_TRY(launch_down(d, st));
+  if (peer) {
+    PeerFlags f{};
+    for (int w = 0; w < peer->world; ++w) f.flag[w] = peer->flags[w];
+    f.world = peer->world;
+    FP_TRY(launch_peer_signal(f, peer->epoch, st));
+  }
   stage_mark(4, st);
   return FP_OK;
+}
+}  // namespace
+
+int fp_pattention_routed_fwd(const void* x, int64_t M, int D, int NB, int dtype, const void* k_gate,
+                             const void* k_up, const void* v, const void* w_gu, const void* v_t, const void* out_proj,
+                             int base_blocks, int capacity, const int32_t* remote_indices,
+                             const int32_t* remote_counts, const float* ctx16, int block_stride, int block_offset,
+                             void* y, int y_f32, void* workspace, size_t workspace_bytes, void* stream) {
+  return routed_fwd_impl(x, M, D, NB, dtype, k_gate, k_up, v, w_gu, v_t, out_proj, base_blocks, capacity,
+                         remote_indices, remote_counts, ctx16, block_stride, block_offset, y, y_f32, workspace,
+                         workspace_bytes, stream, nullptr);
+}
+
+int fp_pattention_routed_peer_fwd(const void* x, int64_t M, int D, int NB, int dtype, const void* k_gate,
+                                  const void* k_up, const void* v, const void* w_gu, const void* v_t,
+                                  const void* out_proj, int base_blocks, int capacity, const int32_t* remote_indices,
+                                  const int32_t* remote_counts, const float* ctx16, int block_stride,
+                                  int block_offset, void* const* peer_out, uint32_t* const* peer_flags, int world,
+                                  int64_t rows_per_rank, uint32_t epoch, int y_f32, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  const PeerSpec peer{peer_out, peer_flags, world, rows_per_rank, epoch};
+  return routed_fwd_impl(x, M, D, NB, dtype, k_gate, k_up, v, w_gu, v_t, out_proj, base_blocks, capacity,
+                         remote_indices, remote_counts, ctx16, block_stride, block_offset, nullptr, y_f32, workspace,
+                         workspace_bytes, stream, &peer);
 }
 
 int fp_pattention_pooled_fwd(const void* x, int64_t M, int D, int NB, int dtype, const void* k_gate,
@@ -698,10 +769,17 @@ size_t fp_block_sparse_linear_workspace_size(int dtype, int64_t M, int D_in, int
   return bsl_workspace(bsl_ksplit(dtype, M, D_in, out_features, max_active, layout_sms()), M, out_features);
 }
 
-int fp_block_sparse_linear_fwd(const void* x, int64_t M, int D_in, const void* weight, const void* bias,
-                               int out_features, int dtype, const int32_t* blocks, const int32_t* n_active,
-                               int max_active, const float* ctx16, const void* out_proj, void* out, void* workspace,
-                               size_t workspace_bytes, void* stream) {
+int fp_pack_blocked_weight(const void* weight, int rows, int cols, void* out, void* stream) {
+  if (!weight || !out || rows <= 0 || cols <= 0 || rows % 64 || cols % 64) return FP_ERR_INVALID_ARG;
+  if (!aligned16(weight) || !aligned16(out)) return FP_ERR_INVALID_ARG;
+  return launch_pack_blocked(weight, rows, cols, out, (cudaStream_t)stream);
+}
+
+namespace {
+int bsl_fwd(const void* x, int64_t M, int D_in, const void* weight, const void* weight_blocked, const void* bias,
+            int out_features, int dtype, const int32_t* blocks, const int32_t* n_active, int max_active,
+            const float* ctx16, const void* out_proj, void* out, void* workspace, size_t workspace_bytes,
+            void* stream) {
   if (dtype != FP_DTYPE_F32 && dtype != FP_DTYPE_BF16) return FP_ERR_UNSUPPORTED;
   if (M < 0 || D_in <= 0 || out_features <= 0 || out_features % 64 != 0) return FP_ERR_INVALID_ARG;
   if (!x || !weight || !blocks || !n_active || !out || (ctx16 && !out_proj)) return FP_ERR_INVALID_ARG;
@@ -727,6 +805,10 @@ int fp_block_sparse_linear_fwd(const void* x, int64_t M, int D_in, const void* w
     d.y_acc = ks > 1 ? reinterpret_cast<float*>(static_cast<char*>(workspace) + align_up(FP_VARIANT_WORKSPACE_MIN))
                      : nullptr;
     d.nmap = blocks; d.omap = blocks; d.ncnt = n_active; d.bias = bias; d.bias_f32 = 0; d.ldy = out_features;
+    if (weight_blocked && aligned16(weight_blocked)) {
+      d.v_t = weight_blocked;
+      d.vt_blocked = 1;
+    }
     FP_TRY(launch_down(d, st));
   } else {
     MappedGemm g{};
@@ -740,6 +822,25 @@ int fp_block_sparse_linear_fwd(const void* x, int64_t M, int D_in, const void* w
     FP_TRY(launch_mapped_gemm_simt(g, st));
   }
   return launch_fill_inactive(blocks, n_active, NB, M, ctx16, out_proj, dtype, out, out_features, sms, st);
+}
+}  // namespace
+
+int fp_block_sparse_linear_fwd(const void* x, int64_t M, int D_in, const void* weight, const void* bias,
+                               int out_features, int dtype, const int32_t* blocks, const int32_t* n_active,
+                               int max_active, const float* ctx16, const void* out_proj, void* out, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  return bsl_fwd(x, M, D_in, weight, nullptr, bias, out_features, dtype, blocks, n_active, max_active, ctx16,
+                 out_proj, out, workspace, workspace_bytes, stream);
+}
+
+int fp_block_sparse_linear_blocked_fwd(const void* x, int64_t M, int D_in, const void* weight,
+                                       const void* weight_blocked, const void* bias, int out_features, int dtype,
+                                       const int32_t* blocks, const int32_t* n_active, int max_active,
+                                       const float* ctx16, const void* out_proj, void* out, void* workspace,
+                                       size_t workspace_bytes, void* stream) {
+  if (weight_blocked && (dtype != FP_DTYPE_BF16 || D_in % 64)) return FP_ERR_INVALID_ARG;
+  return bsl_fwd(x, M, D_in, weight, weight_blocked, bias, out_features, dtype, blocks, n_active, max_active, ctx16,
+                 out_proj, out, workspace, workspace_bytes, stream);
 }
 
 namespace {

@@ -241,6 +241,12 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
   const int ntiles = gathered ? a.meta[0] : a.n_keys * (int)((a.M + kN - 1) / kN);
   const int nkb = a.D / kTileK;
   const int nbt = a.Np / kBlock;  // blocks of the packed weight (tile kb * nbt + b)
+  // work units: tile u / ks over k-blocks [kr0(u), kr1(u)) (ks = 1: whole tiles; the split exists only
+  // in the configuration for batches of at most 64 tokens)
+  const int ks = (kN == 64 && a.gu_ks > 1) ? a.gu_ks : 1;
+  const int nunits = ntiles * ks;
+  auto kr0 = [&](int u) { return (u % ks) * nkb / ks; };
+  auto kr1 = [&](int u) { return (u % ks + 1) * nkb / ks; };
   uint32_t issued = 0;
 
   if (warp == 0) {
@@ -249,16 +255,22 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-        const GuTile t = gu_decode<kN>(a, tile);
+      // batches of at most 64 tokens read every weight tile once: keep it from evicting the partials,
+      // H and x from L2
+      const uint64_t pol = l2_policy_evict_first();
+      for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
+        const GuTile t = gu_decode<kN>(a, u / ks);
         if (t.n <= 0) continue;
-        for (int kb = 0; kb < nkb; ++kb, ++it) {
+        for (int kb = kr0(u); kb < kr1(u); ++kb, ++it) {
           const int s = it % kS;
           const uint32_t ph = (it / kS) & 1u;
           if (!mbar_wait(&bars->empty[s], ph ^ 1u, a.err, kErrWaitEmpty)) { ok = false; break; }
           uint8_t* As = smem + s * kStage;
           mbar_arrive_expect_tx(&bars->full[s], kABytes + (gathered ? 0u : Cfg::kBBytes));
-          tma_load_2d(As, &tm_w, &bars->full[s], 0, (kb * nbt + t.b) * kTileM);
+          if (kN == 64)
+            tma_load_2d_hint(As, &tm_w, &bars->full[s], 0, (kb * nbt + t.b) * kTileM, pol);
+          else
+            tma_load_2d(As, &tm_w, &bars->full[s], 0, (kb * nbt + t.b) * kTileM);
           if (!gathered) tma_load_2d(As + kABytes, &tm_x, &bars->full[s], kb * kTileK, (int)t.r0);
         }
       }
@@ -275,8 +287,8 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
     const char* xbytes = reinterpret_cast<const char*>(a.x);
     uint32_t it = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-      const GuTile t = gu_decode<kN>(a, tile);
+    for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
+      const GuTile t = gu_decode<kN>(a, u / ks);
       if (t.n <= 0) continue;
       const int npad = (t.n + 15) & ~15;
       int64_t src[kRowsPerGatherThread];
@@ -287,7 +299,7 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
         const int tok = tl < 0 ? 0 : tl;
         src[j] = (int64_t)tok * a.D * 2 + chunk * 16;
       }
-      for (int kb = 0; kb < nkb; ++kb, ++it) {
+      for (int kb = kr0(u); kb < kr1(u); ++kb, ++it) {
         const int s = it % kS;
         const uint32_t ph = (it / kS) & 1u;
         if (!warp_wait(&bars->empty[s], ph ^ 1u, a.err, kErrWaitEmpty)) { ok = false; break; }
@@ -310,8 +322,8 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
       uint32_t it = 0;
       int local = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-        const GuTile t = gu_decode<kN>(a, tile);
+      for (int u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
+        const GuTile t = gu_decode<kN>(a, u / ks);
         if (t.n <= 0) continue;
         const int npad = (t.n + 15) & ~15;
         const int acc = local & 1;
@@ -320,7 +332,8 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kTileN;
         const uint32_t idesc = umma_idesc_bf16(kTileM, npad);
-        for (int kb = 0; kb < nkb; ++kb) {
+        const int k0 = kr0(u);
+        for (int kb = k0; kb < kr1(u); ++kb) {
           const int s = it % kS;
           const uint32_t ph = (it / kS) & 1u;
           if (!mbar_wait(&bars->full[s], ph, a.err, kErrWaitFull)) { ok = false; break; }
@@ -330,7 +343,7 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
           const uint64_t bd = umma_desc_sw128(smem_u32(smem + s * kStage + kABytes));
 #pragma unroll
           for (int k = 0; k < kTileK / 16; ++k)
-            umma_bf16(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+            umma_bf16(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (kb != k0) || k != 0);
           umma_commit(&bars->empty[s]);
           ++it;
         }
@@ -345,7 +358,8 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
     // ---------------- epilogue: warps 2..5; warp w reads TMEM lanes [32*(w%4), +32)
     const int q = warp & 3;
     int local = 0;
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
+      const int tile = u / ks;
       const GuTile t = gu_decode<kN>(a, tile);
       if (t.n <= 0) continue;
       const int npad = (t.n + 15) & ~15;
@@ -353,21 +367,88 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
       const uint32_t aph = (local >> 1) & 1;
       if (!warp_wait(&bars->accf[acc], aph, a.err, kErrWaitAccFull)) break;
       tc_fence_after();
-      for (int c = 0; c * 32 < npad; ++c) {
-        uint32_t v[32];
+      if (kN != 64 || ks == 1) {
+        for (int c = 0; c * 32 < npad; ++c) {
+          uint32_t v[32];
+          __syncwarp();
+          tmem_ld32(tmem_base + acc * kTileN + c * 32 + ((uint32_t)(32 * q) << 16), v);
+          tmem_ld_wait();
+          const int ni = c * 32 + lane;
+          gu_store_chunk(a, v, ni < t.n ? gu_token(t, ni, a) : -1, t.slot, q, lane);
+        }
+        tc_fence_before();
         __syncwarp();
-        tmem_ld32(tmem_base + acc * kTileN + c * 32 + ((uint32_t)(32 * q) << 16), v);
-        tmem_ld_wait();
-        const int ni = c * 32 + lane;
-        gu_store_chunk(a, v, ni < t.n ? gu_token(t, ni, a) : -1, t.slot, q, lane);
+        if (lane == 0) mbar_arrive(&bars->acce[acc]);
+      } else {
+        // split unit: this quarter's fp32 rows (row 32q + lane, npad token columns) to the unit's slot;
+        // gateup_split_combine_kernel sums a tile's slots and runs the activation
+        const int64_t row = 32 * q + lane;
+        float* mine = a.gu_part + (((int64_t)tile * ks + u % ks) * kTileM + row) * kN;
+        for (int c = 0; c * 32 < npad; ++c) {
+          uint32_t v[32];
+          __syncwarp();
+          tmem_ld32(tmem_base + acc * kTileN + c * 32 + ((uint32_t)(32 * q) << 16), v);
+          tmem_ld_wait();
+          float4* dst = reinterpret_cast<float4*>(mine + c * 32);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            dst[i] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                 __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->acce[acc]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->acce[acc]);
       ++local;
     }
   }
   pipe_teardown(bars, issued, a.err);
+}
+
+// Second half of the split gate/up (batches of at most 64 tokens): per tile, the fp32 partials of its
+// gu_ks work units are summed in split order into shared memory (coalesced loads, all splits in flight),
+// then each thread computes h for one (token, channel) and the CTA stores whole 128-byte rows of H.
+// Packed row of gate channel c: 32 (c / 16) + c % 16; of up channel c: that + 16.
+constexpr int kGuCombineThreads = 256;
+__global__ void __launch_bounds__(kGuCombineThreads) gateup_split_combine_kernel(const GateUpArgs a) {
+  constexpr int kN = 64;
+  __shared__ float s_acc[kTileM][kN + 1];
+  __shared__ int s_tok[kN];
+  griddep_wait();  // every unit's partial is stored
+  griddep_launch_dependents();
+  const int ks = a.gu_ks;
+  const int ntiles = a.meta[0];
+  const bool swiglu = a.act == FP_ACT_SWIGLU;
+  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    const GuTile t = gu_decode<kN>(a, tile);
+    if (t.n <= 0) continue;  // uniform over the CTA
+    const int npad = (t.n + 15) & ~15;
+    const int nq = npad / 4;  // float4 per row
+    if (threadIdx.x < t.n) s_tok[threadIdx.x] = gu_token(t, threadIdx.x, a);
+    const float4* part = reinterpret_cast<const float4*>(a.gu_part + (int64_t)tile * ks * kTileM * kN);
+    for (int i = threadIdx.x; i < kTileM * nq; i += kGuCombineThreads) {
+      const int row = i / nq, c4 = i - row * nq;
+      const int64_t off = (int64_t)row * (kN / 4) + c4;
+      float4 v = __ldcg(part + off);
+      for (int sp = 1; sp < ks; ++sp) {
+        const float4 p = __ldcg(part + (int64_t)sp * kTileM * (kN / 4) + off);
+        v.x += p.x; v.y += p.y; v.z += p.z; v.w += p.w;
+      }
+      s_acc[row][4 * c4] = v.x; s_acc[row][4 * c4 + 1] = v.y;
+      s_acc[row][4 * c4 + 2] = v.z; s_acc[row][4 * c4 + 3] = v.w;
+    }
+    __syncthreads();
+    __nv_bfloat16* hbase = reinterpret_cast<__nv_bfloat16*>(a.h) + (int64_t)t.slot * kBlock;
+    for (int i = threadIdx.x; i < t.n * kBlock; i += kGuCombineThreads) {
+      const int tc = i / kBlock, ch = i - tc * kBlock;
+      const int grow = 32 * (ch >> 4) + (ch & 15);
+      const float gv = s_acc[grow][tc], u = s_acc[grow + 16][tc];
+      const float h = swiglu ? __fdividef(gv, 1.0f + __expf(-gv)) * u : pattention_act<false>(a.act, gv, u);
+      const int tok = s_tok[tc];
+      if (tok >= 0) hbase[(int64_t)tok * a.ldh + ch] = __float2bfloat16_rn(h);
+    }
+    __syncthreads();  // s_acc and s_tok are rewritten by the CTA's next tile
+  }
 }
 
 // Packed gate/up layout of one parameter block b (128 rows): rows 32q .. 32q+15 are gate channels
@@ -420,6 +501,23 @@ __global__ void __launch_bounds__(256) pack_vt_kernel(const __nv_bfloat16* __res
     }
     out[e] = make_uint4(w[0], w[1], w[2], w[3]);
   }
+}
+
+// 64 x 64 blocked copy of a row-major weight [rows, cols] (BlockSparseLinear: rows = output features,
+// cols = input features): tile (kb, j) holds rows [j*64, +64) x columns [kb*64, +64) as one contiguous
+// 8 KB run at tile index kb * (rows / 64) + j, so the four column blocks of an output tile at one k-block
+// are one 32 KB run when their blocks are consecutive, and one block is an 8 KB run otherwise (a
+// row-major weight gives 64 pieces of 128 bytes, one per row, 8 KB apart at D_in = 4096).
+__global__ void pack_blocked_kernel(const uint4* __restrict__ w, int64_t rows, int vec_per_row,
+                                    uint4* __restrict__ out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // over rows * vec_per_row 16-byte words
+  if (i >= rows * vec_per_row) return;
+  const int64_t nbo = rows / 64;
+  const int c = (int)(i & 7);
+  const int r = (int)((i >> 3) & 63);
+  const int64_t t = i >> 9;  // tile = kb * nbo + j
+  const int64_t kb = t / nbo, j = t - kb * nbo;
+  out[i] = w[(j * 64 + r) * vec_per_row + kb * 8 + c];
 }
 
 // ============================================================================================
@@ -492,16 +590,28 @@ __device__ __forceinline__ void down_store_chunk(const DownArgs& a, float (&o)[3
   }
   if (!row_ok) return;
   const int64_t ldy = a.ldy > 0 ? a.ldy : (int64_t)a.D;
+  // output row: this rank's Y, or (peer output) the receive slot of the rank that owns the row
+  void* ybase = a.y;
+  int64_t yrow = row;
+  if (a.peer_rows > 0 && ks == 1) {
+    const int64_t owner = row / a.peer_rows;
+    ybase = owner < kMaxPeers ? a.peer_y[owner] : nullptr;
+    yrow = row - owner * a.peer_rows;
+    if (!ybase) {
+      record_error(a.err, kErrBadTile);  // a row past the ranks' slices: reported, not stored
+      return;
+    }
+  }
   if (ks > 1) {  // partial of this split; summed in split order by a split-K reduce kernel
     float4* yp = reinterpret_cast<float4*>(a.y_acc + ((int64_t)split * a.M + row) * a.D + col0);
 #pragma unroll
     for (int i = 0; i < 8; ++i) yp[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
   } else if (a.y_f32) {
-    float4* yp = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.y) + row * ldy + ocol0);
+    float4* yp = reinterpret_cast<float4*>(reinterpret_cast<float*>(ybase) + yrow * ldy + ocol0);
 #pragma unroll
     for (int i = 0; i < 8; ++i) yp[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
   } else {
-    uint4* yp = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.y) + row * ldy + ocol0);
+    uint4* yp = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(ybase) + yrow * ldy + ocol0);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       uint32_t pk[4];
@@ -521,7 +631,7 @@ __device__ __forceinline__ void down_store_chunk(const DownArgs& a, float (&o)[3
 // the tile's accumulator is taken as zero).
 __global__ void __launch_bounds__(kGemmThreads, 1)
 down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CUtensorMap tm_vt,
-            const DownArgs a) {
+            const __grid_constant__ CUtensorMap tm_vt_wide, const DownArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = aligned_smem(smem_raw);
   PipeBars* bars = reinterpret_cast<PipeBars*>(smem + kStages * kStageBytes);
@@ -561,12 +671,20 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
         int nb[kTileN / kBlock];  // V_t row block of each valid column block, read once per tile
 #pragma unroll
         for (int i = 0; i < kTileN / kBlock; ++i) nb[i] = i < nv ? a.nmap[n * (kTileN / kBlock) + i] : 0;
-        // parameter block of the next k-block, loaded one iteration ahead so that the load's latency
-        // overlaps the wait for a free stage
-        int gb_next = kb0 < kb1 ? (a.bmap ? a.bmap[kb0] : kb0 * a.stride + a.offset) : 0;
+        // blocked weight with the tile's four column blocks consecutive: one 256-row (32 KB) box
+        const bool wide4 = a.vt_blocked && nv == 4 && nb[1] == nb[0] + 1 && nb[2] == nb[0] + 2 && nb[3] == nb[0] + 3;
+        const int nbo = a.D / kBlock;
+        // H column block and parameter block of k-block j (touched-block list, pooled block map, or
+        // strided identity), looked up one iteration ahead so that the load's latency overlaps the wait
+        // for a free stage
+        auto kmap = [&](int j) -> int2 {
+          const int kh = a.ktiles ? a.ktiles[j].x % a.knbl : j;
+          return make_int2(kh, a.bmap ? a.bmap[kh] : kh * a.stride + a.offset);
+        };
+        int2 kg_next = kb0 < kb1 ? kmap(kb0) : make_int2(0, 0);
         for (int kb = kb0; kb < kb1; kb += ks, ++it) {
-          const int gb = gb_next;
-          if (kb + ks < kb1) gb_next = a.bmap ? a.bmap[kb + ks] : (kb + ks) * a.stride + a.offset;
+          const int kh = kg_next.x, gb = kg_next.y;
+          if (kb + ks < kb1) kg_next = kmap(kb + ks);
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1u;
           if (!mbar_wait(&bars->empty[s], ph ^ 1u, a.err, kErrWaitEmpty)) { ok = false; break; }
@@ -574,13 +692,22 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
           uint8_t* Bs = As + kABytes;
           if (a.nmap) {
             mbar_arrive_expect_tx(&bars->full[s], kABytes + (uint32_t)nv * (kBlock * kTileK * 2));
-            tma_load_2d(As, &tm_h, &bars->full[s], kb * kTileK, m * kTileM);
+            tma_load_2d(As, &tm_h, &bars->full[s], kh * kTileK, m * kTileM);
+            if (wide4) {
+              tma_load_2d(Bs, &tm_vt_wide, &bars->full[s], 0, (gb * nbo + nb[0]) * kBlock);
+            } else {
 #pragma unroll
-            for (int i = 0; i < kTileN / kBlock; ++i)
-              if (i < nv) tma_load_2d(Bs + i * (kBlock * kTileK * 2), &tm_vt, &bars->full[s], gb * kBlock, nb[i] * kBlock);
+              for (int i = 0; i < kTileN / kBlock; ++i)
+                if (i < nv) {
+                  if (a.vt_blocked)
+                    tma_load_2d(Bs + i * (kBlock * kTileK * 2), &tm_vt, &bars->full[s], 0, (gb * nbo + nb[i]) * kBlock);
+                  else
+                    tma_load_2d(Bs + i * (kBlock * kTileK * 2), &tm_vt, &bars->full[s], gb * kBlock, nb[i] * kBlock);
+                }
+            }
           } else {
             mbar_arrive_expect_tx(&bars->full[s], kStageBytes);
-            tma_load_2d(As, &tm_h, &bars->full[s], kb * kTileK, m * kTileM);
+            tma_load_2d(As, &tm_h, &bars->full[s], kh * kTileK, m * kTileM);
             if (a.vt_tiled)  // tile (n, gb) of the tile-contiguous V^T
               tma_load_2d(Bs, &tm_vt, &bars->full[s], 0, (n * (a.Np / kBlock) + gb) * kTileN);
             else
@@ -678,6 +805,7 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
       ++local;
     }
   }
+  if (a.peer_rows > 0) __threadfence_system();  // rows stored on other GPUs are visible there
   pipe_teardown(bars, issued, a.err);
 }
 
@@ -760,6 +888,7 @@ down2_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ C
         const int b0 = mine > 0 ? a.nmap[j0] : 0;
         const int b1 = mine > 1 ? a.nmap[j0 + 1] : 0;
         const bool wide = mine == 2 && b1 == b0 + 1;  // consecutive blocks (the common case): one 128-row box
+        const int nbo = a.D / kBlock;
         int gb_next = nkb > 0 ? (a.bmap ? a.bmap[0] : a.offset) : 0;  // one k-block ahead (see down_kernel)
         for (int kb = 0; kb < nkb; ++kb, ++it) {
           const int gb = gb_next;
@@ -772,11 +901,15 @@ down2_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ C
           if (a.nmap) {
             if (leader) mbar_arrive_expect_tx(&bars->full[s], 2 * kPairABytes + (uint32_t)nv * kBoxBytes);
             tma_load_2d_pair(As, &tm_h, &bars->full[s], kb * kTileK, m * 2 * kTileM + (int)rank * kTileM);
+            // row-major weight: box at (k column, weight row); blocked weight: tile rows (gb * nbo + block) * 64
+            const int c0 = a.vt_blocked ? 0 : gb * kBlock;
+            const int r0 = a.vt_blocked ? (gb * nbo + b0) * kBlock : b0 * kBlock;
+            const int r1 = a.vt_blocked ? (gb * nbo + b1) * kBlock : b1 * kBlock;
             if (wide) {
-              tma_load_2d_pair(Bs, &tm_vt_wide, &bars->full[s], gb * kBlock, b0 * kBlock);
+              tma_load_2d_pair(Bs, &tm_vt_wide, &bars->full[s], c0, r0);
             } else {
-              if (mine > 0) tma_load_2d_pair(Bs, &tm_vt, &bars->full[s], gb * kBlock, b0 * kBlock);
-              if (mine > 1) tma_load_2d_pair(Bs + kBoxBytes, &tm_vt, &bars->full[s], gb * kBlock, b1 * kBlock);
+              if (mine > 0) tma_load_2d_pair(Bs, &tm_vt, &bars->full[s], c0, r0);
+              if (mine > 1) tma_load_2d_pair(Bs + kBoxBytes, &tm_vt, &bars->full[s], c0, r1);
             }
           } else {
             if (leader) mbar_arrive_expect_tx(&bars->full[s], 2 * kPairStageBytes);
@@ -881,6 +1014,7 @@ down2_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ C
 
   // ---------------- teardown: every MMA has completed (leader: done barrier; peer: its last accf), no
   // load of this CTA is in flight unless it aborted; then both CTAs free the pair's TMEM
+  if (a.peer_rows > 0) __threadfence_system();  // rows stored on other GPUs are visible there
   tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0 && leader && aborted(a.err)) {
@@ -1167,8 +1301,15 @@ static int launch_gateup_cfg(const GateUpArgs& a, cudaStream_t st) {
                                 (int)Cfg::kSmem) == cudaSuccess ? FP_OK : FP_ERR_CUDA;
   });
   if (attr != FP_OK) return attr;
-  return launch_pdl(gateup_kernel<Cfg>, dim3(a.num_sms), dim3(kGuThreads), Cfg::kSmem, st, tx, tw, a) == cudaSuccess
-             ? FP_OK : FP_ERR_CUDA;
+  if (launch_pdl(gateup_kernel<Cfg>, dim3(a.num_sms), dim3(kGuThreads), Cfg::kSmem, st, tx, tw, a) != cudaSuccess)
+    return FP_ERR_CUDA;
+  if (Cfg::kN == 64 && a.gu_ks > 1) {
+    // the tile count is on the device: one CTA per possible tile, idle past it
+    const int grid = std::max(1, std::min(a.max_tiles, a.num_sms * 4));
+    if (launch_pdl(gateup_split_combine_kernel, dim3(grid), dim3(kGuCombineThreads), 0, st, a) != cudaSuccess)
+      return FP_ERR_CUDA;
+  }
+  return FP_OK;
 }
 
 // Pair gate/up for a shared active list (see gateup2_kernel).
@@ -1211,6 +1352,10 @@ static int launch_gateup2(const GateUpArgs& a, cudaStream_t st) {
 }
 
 int launch_gateup(const GateUpArgs& a, cudaStream_t st) {
+  // the split of a tile's contraction: batches of at most 64 tokens with token lists, 16-aligned D split
+  if (a.gu_ks > 1 && (!a.tiles || a.energy || a.M > GuSmall::kN || !a.gu_part || a.max_tiles < 1 ||
+                      a.gu_ks > (a.D / kTileK)))
+    return FP_ERR_INVALID_ARG;
   // a shared active list over more than 128 tokens: block pairs on CTA pairs
   if (!a.tiles && !a.energy && a.M > kTileM && a.num_sms >= 2) return launch_gateup2(a, st);
   // every tile of a batch of at most 64 tokens holds at most 64 tokens (a key's tokens are distinct)
@@ -1253,6 +1398,14 @@ int launch_pack_gate_up(const void* kg, const void* ku, int Np, int D, void* wgu
   return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
 }
 
+int launch_pack_blocked(const void* w, int rows, int cols, void* out, cudaStream_t st) {
+  const int vec = cols / 8;
+  const int64_t n = (int64_t)rows * vec;
+  if (n <= 0) return FP_OK;
+  pack_blocked_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>((const uint4*)w, rows, vec, (uint4*)out);
+  return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+}
+
 int launch_pack_vt(const void* v, int Np, int D, void* vt, cudaStream_t st) {
   const int NB = Np / kBlock, ntiles = (D + kTileN - 1) / kTileN;
   if (ntiles > 65535) return FP_ERR_UNSUPPORTED;
@@ -1264,15 +1417,24 @@ int launch_pack_vt(const void* v, int Np, int D, void* vt, cudaStream_t st) {
 int launch_down(const DownArgs& a, cudaStream_t st) {
   const bool mapped = a.nmap || a.omap || a.ncnt || a.kcnt || a.bias || a.ldy > 0;
   const int ks = a.ksplit > 1 ? a.ksplit : 1;
+  // peer output: whole rows of the unmapped form, stored by the contraction itself (no split-K)
+  if (a.peer_rows > 0 && (ks > 1 || a.omap || a.nmap || (a.ldy > 0 && a.ldy != a.D))) return FP_ERR_UNSUPPORTED;
   if (mapped && a.D % kBlock != 0) return FP_ERR_INVALID_ARG;
   if (a.vt_tiled && a.nmap) return FP_ERR_INVALID_ARG;
+  if (a.vt_blocked && (!a.nmap || a.vt_tiled || a.Np % kBlock)) return FP_ERR_INVALID_ARG;
+  if (a.ktiles && (!a.kcnt || a.knbl < 1 || a.bmap || a.M > kTileM)) return FP_ERR_INVALID_ARG;
   // tile-contiguous V^T: rows of 64 elements, ceil(D / 256) * (Np / 64) tiles of 256 rows
   const uint64_t vt_rows = (uint64_t)((a.D + kTileN - 1) / kTileN) * (a.Np / kBlock) * kTileN;
-  CUtensorMap th, tv;
+  // blocked weight: rows of 64 elements, (Np / 64) * (D / 64) tiles of 64 rows
+  const uint64_t blk_rows = (uint64_t)(a.Np / kBlock) * (a.D / kBlock) * kBlock;
+  CUtensorMap th, tv, tv4;
   if (!encode_map_2d(&th, a.h, a.K, a.M, (uint64_t)a.K * 2, kTileK, kTileM) ||
       !(a.vt_tiled ? encode_map_2d(&tv, a.v_t, kTileK, vt_rows, kTileK * 2, kTileK, kTileN)
-                   : encode_map_2d(&tv, a.v_t, a.Np, a.D, (uint64_t)a.Np * 2, kTileK, a.nmap ? kBlock : kTileN)))
+        : a.vt_blocked ? encode_map_2d(&tv, a.v_t, kTileK, blk_rows, kTileK * 2, kTileK, kBlock)
+                       : encode_map_2d(&tv, a.v_t, a.Np, a.D, (uint64_t)a.Np * 2, kTileK, a.nmap ? kBlock : kTileN)))
     return FP_ERR_CUDA;
+  tv4 = tv;
+  if (a.vt_blocked && !encode_map_2d(&tv4, a.v_t, kTileK, blk_rows, kTileK * 2, kTileK, kTileN)) return FP_ERR_CUDA;
   static std::once_flag once;
   static int attr = FP_OK;
   std::call_once(once, [] { attr = set_smem((const void*)down_kernel); });
@@ -1284,6 +1446,10 @@ int launch_down(const DownArgs& a, cudaStream_t st) {
     if (a.vt_tiled) {
       if (!encode_map_2d(&tv2, a.v_t, kTileK, vt_rows, kTileK * 2, kTileK, kTileN / 2)) return FP_ERR_CUDA;
       tvw = tv2;
+    } else if (a.vt_blocked) {
+      if (!encode_map_2d(&tv2, a.v_t, kTileK, blk_rows, kTileK * 2, kTileK, kBlock) ||
+          !encode_map_2d(&tvw, a.v_t, kTileK, blk_rows, kTileK * 2, kTileK, 2 * kBlock))
+        return FP_ERR_CUDA;
     } else if (!encode_map_2d(&tv2, a.v_t, a.Np, a.D, (uint64_t)a.Np * 2, kTileK, a.nmap ? kBlock : kTileN / 2) ||
                !encode_map_2d(&tvw, a.v_t, a.Np, a.D, (uint64_t)a.Np * 2, kTileK, kTileN / 2)) {
       return FP_ERR_CUDA;
@@ -1324,7 +1490,7 @@ int launch_down(const DownArgs& a, cudaStream_t st) {
   const int grid = (int)std::min<int64_t>(tiles, a.num_sms);
   if (grid <= 0) return FP_OK;
   if (ks > 1 && !a.y_acc) return FP_ERR_INVALID_ARG;
-  if (launch_pdl(down_kernel, dim3(grid), dim3(kGemmThreads), kGemmSmem, st, th, tv, a) != cudaSuccess)
+  if (launch_pdl(down_kernel, dim3(grid), dim3(kGemmThreads), kGemmSmem, st, th, tv, tv4, a) != cudaSuccess)
     return FP_ERR_CUDA;
   if (ks > 1 && mapped) {
     const int64_t n = a.M * (int64_t)a.D;

@@ -135,14 +135,29 @@ struct GateUpArgs {
   int* err;
   int num_sms;
   int act = FP_ACT_SWIGLU;  // activation of the epilogue (non-gated forms ignore the up rows)
+  // Split of each tile's contraction over D (batches of at most 64 tokens, explicit mode, no energy): work
+  // unit u = (tile u / gu_ks, k-range u % gu_ks); each unit stores its fp32 accumulator to gu_part
+  // [max_tiles][gu_ks][128][64], and a second kernel sums each tile's partials in split order and runs the
+  // epilogue (activation, store into H).
+  int gu_ks = 1;
+  float* gu_part = nullptr;
+  int max_tiles = 0;  // bound of the device tile count (sizes the second kernel's grid)
 };
 int launch_gateup(const GateUpArgs& a, cudaStream_t st);
+// Work units of the decode split: k-blocks per unit at least 8, at most 4 units per tile.
+__host__ __device__ __forceinline__ int gateup_decode_ksplit(int D) {
+  const int nkb = D / 64;
+  return nkb >= 32 ? 4 : (nkb >= 16 ? 2 : 1);
+}
 // E[t, b] = (sum_q part[q][t][b]) / 64 * vnorm[b], quarters summed in order
 int launch_energy_combine(const float* part, int64_t M, int NB, const float* vnorm, float* E, cudaStream_t st);
 int launch_iota(int32_t* out, int n, cudaStream_t st);
 int launch_pack_gate_up(const void* kg, const void* ku, int Np, int D, void* wgu, cudaStream_t st);
 // V^T tile-contiguous: ceil(D / 256) * (Np / 64) tiles of 256 x 64 (bf16), tile (n, b) at index n * NB + b.
 int launch_pack_vt(const void* v, int Np, int D, void* vt, cudaStream_t st);
+// 64 x 64 blocked copy of a row-major [rows, cols] bf16 matrix: tile (kb, j) = rows [j*64, +64) x columns
+// [kb*64, +64), contiguous 8 KB at tile index kb * (rows / 64) + j.
+int launch_pack_blocked(const void* w, int rows, int cols, void* out, cudaStream_t st);
 
 // Rows per gate/up tile of a block-CSR key with `cnt` tokens: ceil(cnt / kGuN) tiles of equal size,
 // rounded up to the UMMA N granularity (16).
@@ -151,6 +166,14 @@ __host__ __device__ __forceinline__ int balanced_rows(int cnt) {
   const int per = nt > 0 ? (cnt + nt - 1) / nt : 0;
   return (per + 15) & ~15;
 }
+
+// Peer-memory reduce-scatter (fp_peer.cu): ranks of one job, at most kMaxPeers.
+constexpr int kMaxPeers = 8;
+struct PeerFlags {
+  uint32_t* flag[kMaxPeers];  // this rank's flag word on rank w (peer pointer; own rank: local)
+  int world;
+};
+int launch_peer_signal(const PeerFlags& f, uint32_t epoch, cudaStream_t st);
 
 struct DownArgs {
   const void* h;        // [M, K] bf16
@@ -178,6 +201,17 @@ struct DownArgs {
   int bias_f32 = 0;
   int64_t ldy = 0;                // Y row stride in elements (0: D)
   int vt_tiled = 0;               // v_t in the tile-contiguous form of launch_pack_vt (the MLP's packed V)
+  // k-block j of the contraction = H column block (and parameter block slot) ktiles[j].x % knbl, for j below
+  // the device count kcnt: the routing kernel's gate/up tile list of a batch of at most 64 tokens (one tile
+  // per touched block, in block order), so that only touched blocks are contracted
+  const int2* ktiles = nullptr;
+  int knbl = 1;
+  int vt_blocked = 0;             // block-mapped form: v_t in the 64 x 64 blocked form of launch_pack_blocked
+                                  // (tile of k-block kb and row block j at rows (kb * D/64 + j) * 64)
+  // Peer output (parameter-block sharding): row r of Y goes to rank o = r / peer_rows, row r - o * peer_rows
+  // of peer_y[o] (row stride D, dtype per y_f32; peer pointers through CUDA IPC) instead of to y.
+  void* peer_y[kMaxPeers] = {};
+  int64_t peer_rows = 0;
 };
 int launch_down(const DownArgs& a, cudaStream_t st);
 // Split-K factor used by the down projection for M tokens (1 = none).  Small batches (decode) have too

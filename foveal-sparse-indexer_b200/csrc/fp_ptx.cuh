@@ -24,6 +24,7 @@ enum DeviceError : int {
   kErrWaitAccEmpty = 4,  // MMA issuer timed out waiting for the epilogue
   kErrBadTile = 5,       // a work descriptor pointed outside its bounds
   kErrDrain = 6,         // draining in-flight copies after an abort timed out
+  kErrPeerWait = 7,      // a peer rank's partial did not arrive within the wait limit
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -140,6 +141,20 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* map, uint64_t
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4}], [%2];"
       ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+// L2 policy for data read exactly once per call (streamed weights): evicted before other lines.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ void tma_load_2d_hint(void* dst, const void* map, uint64_t* bar, int c0, int c1,
+                                                 uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;"
+      ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "l"(policy)
       : "memory");
 }
 // Tile load into this CTA's shared memory whose completion (bytes) is counted on the leader CTA's

@@ -7,6 +7,7 @@ These are the operator layer the module classes are built on.  Each function val
 
 from __future__ import annotations
 
+import ctypes
 from typing import Optional, Tuple
 
 import torch
@@ -280,6 +281,86 @@ def routed_forward(x2d, k_gate, k_up, v, packed, out_proj, remote_indices, remot
     return y
 
 
+# ---------------------------------------------------------------- peer-memory reduce-scatter
+PEER_HANDLE_BYTES = 64
+PEER_FLAG_BYTES = 256
+
+
+def peer_alloc(nbytes: int) -> Tuple[int, bytes]:
+    """A zeroed device buffer shared through CUDA IPC (``fp_peer_alloc``): (device address, handle)."""
+    p = ctypes.c_void_p()
+    h = ctypes.create_string_buffer(PEER_HANDLE_BYTES)
+    check(_lib.load().fp_peer_alloc(int(nbytes), ctypes.byref(p), h), "fp_peer_alloc")
+    return int(p.value), h.raw
+
+
+def peer_open(handle: bytes) -> int:
+    """Maps another process's :func:`peer_alloc` buffer (``fp_peer_open``): its address in this process."""
+    p = ctypes.c_void_p()
+    check(_lib.load().fp_peer_open(ctypes.create_string_buffer(bytes(handle), PEER_HANDLE_BYTES), ctypes.byref(p)),
+          "fp_peer_open")
+    return int(p.value)
+
+
+def peer_close(addr: int) -> None:
+    check(_lib.load().fp_peer_close(ctypes.c_void_p(addr)), "fp_peer_close")
+
+
+def peer_free(addr: int) -> None:
+    check(_lib.load().fp_peer_free(ctypes.c_void_p(addr)), "fp_peer_free")
+
+
+def routed_peer_forward(x2d, k_gate, k_up, v, packed, out_proj, remote_indices, remote_counts, ctx16, *,
+                        base_blocks: int, block_stride: int, block_offset: int, peer_out, peer_flags,
+                        rows_per_rank: int, epoch: int, out_f32: bool = False) -> bool:
+    """:func:`routed_forward` whose output rows go straight to the ranks that own them
+    (``fp_pattention_routed_peer_fwd``): ``peer_out[o]`` / ``peer_flags[o]`` are device addresses (this
+    rank's receive slot and flag word on rank o).  Returns False, having launched nothing, for shapes
+    whose contraction is split (small batches): the caller uses the collective instead."""
+    dev = require_cuda(x2d, k_gate, k_up, v, remote_indices, remote_counts)
+    dtt = x2d.dtype
+    dt = dtype_code(dtt)
+    x2d = contig(x2d)
+    M, D = x2d.shape
+    NB = k_gate.shape[0] // 64
+    world = len(peer_out)
+    k_gate, k_up, v = contig(k_gate.detach()), contig(k_up.detach()), contig(v.detach())
+    out_proj = contig(out_proj.detach().to(dtt)) if out_proj is not None else None
+    ridx = contig(remote_indices.to(torch.int32))
+    cnt = contig(remote_counts.to(torch.int32))
+    ctx16 = contig(ctx16.float()) if ctx16 is not None else None
+    cap = ridx.shape[1]
+    w_gu, v_t = packed if packed is not None else (None, None)
+    outs = (ctypes.c_void_p * world)(*peer_out)
+    flags = (ctypes.c_void_p * world)(*peer_flags)
+    lib = _lib.load()
+    ws = _lib.workspace(dev, lib.fp_token_workspace_size(dt, M, D, NB, int(base_blocks), cap, int(block_stride)))
+    rc = lib.fp_pattention_routed_peer_fwd(ptr(x2d), M, D, NB, dt, ptr(k_gate), ptr(k_up), ptr(v), ptr(w_gu),
+                                           ptr(v_t), ptr(out_proj), int(base_blocks), cap, ptr(ridx), ptr(cnt),
+                                           ptr(ctx16), int(block_stride), int(block_offset), outs, flags, world,
+                                           int(rows_per_rank), int(epoch) & 0xFFFFFFFF, 1 if out_f32 else 0, ptr(ws),
+                                           ws.numel(), stream_handle(dev))
+    if rc == _lib.FP_ERR_UNSUPPORTED:
+        return False
+    check(rc, "fp_pattention_routed_peer_fwd")
+    return True
+
+
+def peer_combine(recv_addr: int, flags_addr: int, world: int, rows: int, D: int, *, in_f32: bool, epoch: int,
+                 out_dtype: torch.dtype, err_ws: torch.Tensor) -> torch.Tensor:
+    """This rank's rows summed over the world slots of its receive buffer once every rank's flag reached
+    ``epoch`` (``fp_peer_combine``): y [rows, D].  ``err_ws``: a device buffer of at least 256 bytes of its
+    own (the combine's error word; ``_lib.device_error(err_ws)`` reads it)."""
+    dev = err_ws.device
+    y = torch.empty(rows, D, dtype=out_dtype, device=dev)
+    ws = err_ws
+    rc = _lib.load().fp_peer_combine(ctypes.c_void_p(recv_addr), ctypes.c_void_p(flags_addr), int(world), int(rows),
+                                     int(D), 1 if in_f32 else 0, int(epoch) & 0xFFFFFFFF, ptr(y),
+                                     1 if out_dtype == torch.float32 else 0, ptr(ws), ws.numel(), stream_handle(dev))
+    check(rc, "fp_peer_combine")
+    return y
+
+
 def pooled_forward(x2d, k_gate, k_up, v, packed, active, *, ctx16=None, out_proj=None, out_f32: bool = False):
     """Forward over one shared active set (``fp_pattention_pooled_fwd``); y [M, D].  ``packed`` as in
     :func:`token_forward`."""
@@ -373,12 +454,28 @@ def union_blocks(remote_indices: torch.Tensor, remote_counts: torch.Tensor, num_
     return blocks, n_active
 
 
+def pack_blocked_weight(weight: torch.Tensor) -> torch.Tensor:
+    """64 x 64 blocked copy of a bf16 weight [rows, cols] (``fp_pack_blocked_weight``): a flat bf16 tensor
+    whose tile (kb, j) (rows j*64.., columns kb*64..) is one contiguous 8 KB run at tile kb * rows/64 + j."""
+    dev = require_cuda(weight)
+    if weight.dtype != torch.bfloat16 or weight.dim() != 2:
+        raise ValueError("pack_blocked_weight: a 2-D bf16 weight")
+    w = contig(weight.detach())
+    out = torch.empty(w.numel(), dtype=torch.bfloat16, device=dev)
+    rc = _lib.load().fp_pack_blocked_weight(ptr(w), w.shape[0], w.shape[1], ptr(out), stream_handle(dev))
+    check(rc, "fp_pack_blocked_weight")
+    return out
+
+
 def block_sparse_linear(x2d: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], blocks: torch.Tensor,
                         n_active: torch.Tensor, ctx16: Optional[torch.Tensor] = None,
-                        out_proj: Optional[torch.Tensor] = None, max_active: int = 0) -> torch.Tensor:
+                        out_proj: Optional[torch.Tensor] = None, max_active: int = 0,
+                        weight_blocked: Optional[torch.Tensor] = None) -> torch.Tensor:
     """BlockSparseLinear contraction over the union (``fp_block_sparse_linear_fwd``;
     block_matmul.py:233-254): out [M, out_features] in x's dtype.  ``max_active``: a host-side upper
-    bound of the union size (0 = all blocks), which lets small batches split the contraction."""
+    bound of the union size (0 = all blocks), which lets small batches split the contraction.
+    ``weight_blocked``: the weight's :func:`pack_blocked_weight` copy, read by the tensor cores instead of
+    the row-major weight (``fp_block_sparse_linear_blocked_fwd``; bf16 only)."""
     dev = require_cuda(x2d, weight, blocks, n_active)
     dtt = x2d.dtype
     x2d, weight = contig(x2d), contig(weight.detach().to(dtt))
@@ -391,6 +488,15 @@ def block_sparse_linear(x2d: torch.Tensor, weight: torch.Tensor, bias: Optional[
     lib = _lib.load()
     ws = _lib.workspace(dev, lib.fp_block_sparse_linear_workspace_size(dtype_code(dtt), M, D_in, out_features,
                                                                       int(max_active)))
+    if weight_blocked is not None and dtt == torch.bfloat16:
+        if weight_blocked.numel() != weight.numel() or weight_blocked.dtype != torch.bfloat16:
+            raise ValueError("weight_blocked: the bf16 pack_blocked_weight copy of this weight")
+        rc = lib.fp_block_sparse_linear_blocked_fwd(ptr(x2d), M, D_in, ptr(weight), ptr(weight_blocked), ptr(bias),
+                                                    out_features, dtype_code(dtt), ptr(blocks), ptr(n_active),
+                                                    int(max_active), ptr(ctx16), ptr(out_proj), ptr(out), ptr(ws),
+                                                    ws.numel(), stream_handle(dev))
+        check(rc, "fp_block_sparse_linear_blocked_fwd")
+        return out
     rc = lib.fp_block_sparse_linear_fwd(ptr(x2d), M, D_in, ptr(weight), ptr(bias), out_features, dtype_code(dtt),
                                         ptr(blocks), ptr(n_active), int(max_active), ptr(ctx16), ptr(out_proj),
                                         ptr(out), ptr(ws), ws.numel(), stream_handle(dev))

@@ -30,14 +30,18 @@ from . import kernels
 
 
 def shard_parameter_blocks(module, group=None, partial_dtype: Optional[torch.dtype] = None,
-                           shard_routing: bool = True) -> None:
+                           shard_routing: bool = True, peer_reduce: bool = False) -> None:
     """Makes ``module`` (routing="token") compute only the parameter blocks of this rank.
 
     ``partial_dtype``: dtype of the partial outputs that the collective sums (default: the module's
     dtype, so a bf16 model moves bf16 partials, half the bytes of fp32; the reduction of N bf16 partials
     stays well inside the 2e-2 relative bar of bf16 outputs).  ``torch.float32`` keeps fp32 partials.
     ``shard_routing``: route only this rank's share of the tokens and all-gather the routes (when the
-    token count divides by the world size); False routes every token on every rank."""
+    token count divides by the world size); False routes every token on every rank.
+    ``peer_reduce``: replace the reduce-scatter of the unchunked, split-routing forward by the peer-memory
+    one (the contraction stores each row's partial straight into the owning rank's receive buffer over
+    NVLink; see :class:`PeerReduce`).  The buffers are set up by the first such forward, on every rank of
+    the group at once; :func:`release_peer_buffers` frees them."""
     if module.routing != "token":
         raise ValueError("parameter-block sharding applies to routing='token'")
     rank = dist.get_rank(group)
@@ -48,6 +52,98 @@ def shard_parameter_blocks(module, group=None, partial_dtype: Optional[torch.dty
         raise ValueError("partial_dtype must be torch.float32 or torch.bfloat16")
     module._shard_partial_dtype = pd
     module._shard_routing = bool(shard_routing)
+    module._peer_reduce = bool(peer_reduce)
+    if not peer_reduce:
+        release_peer_buffers(module)
+
+
+class PeerReduce:
+    """Receive buffers of the peer-memory reduce-scatter, one per rank, mapped into every rank of the group
+    through CUDA IPC.  Buffer of rank w: 256 bytes of flags (flag v = the last epoch whose partial rank v
+    finished storing here), then 2 parities x world slots x ``rows`` x D partials.  Call e stores parity
+    e % 2; each call's epoch is one more than the last, on every rank."""
+
+    def __init__(self, group, rank: int, world: int, rows: int, D: int, dtype: torch.dtype, device):
+        self.group, self.rank, self.world, self.rows, self.D, self.dtype = group, rank, world, rows, D, dtype
+        esize = torch.empty((), dtype=dtype).element_size()
+        self.slot = rows * D * esize
+        nbytes = kernels.PEER_FLAG_BYTES + 2 * world * self.slot
+        self.base, handle = kernels.peer_alloc(nbytes)
+        handles = [None] * world
+        dist.all_gather_object(handles, handle, group=group)
+        self.addr = [self.base if w == rank else kernels.peer_open(handles[w]) for w in range(world)]
+        self.epoch = 0
+        self.err = torch.zeros(256, dtype=torch.uint8, device=device)
+
+    def fits(self, rows: int, D: int, dtype: torch.dtype) -> bool:
+        return rows <= self.rows and D == self.D and dtype == self.dtype
+
+    def slots(self, parity: int):
+        """This rank's receive slot on every rank (device addresses)."""
+        return [a + kernels.PEER_FLAG_BYTES + (parity * self.world + self.rank) * self.slot for a in self.addr]
+
+    def flags(self):
+        """This rank's flag word on every rank."""
+        return [a + 4 * self.rank for a in self.addr]
+
+    def recv(self, parity: int) -> int:
+        """This rank's own slots of one parity."""
+        return self.base + kernels.PEER_FLAG_BYTES + parity * self.world * self.slot
+
+    def close(self) -> None:
+        """Collective: every rank unmaps the others' buffers, then frees its own."""
+        if self.addr is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for w, a in enumerate(self.addr):
+            if w != self.rank:
+                kernels.peer_close(a)
+        dist.barrier(group=self.group)
+        kernels.peer_free(self.base)
+        self.addr = None
+
+
+def release_peer_buffers(module) -> None:
+    """Frees the module's peer-memory receive buffers (collective over the shard group)."""
+    pr = getattr(module, "_peer_state", None)
+    if pr is not None:
+        pr.close()
+        module._peer_state = None
+
+
+def _peer_state(module, rows: int, D: int, dtype: torch.dtype, device) -> PeerReduce:
+    rank, world, group = module._shard
+    pr = getattr(module, "_peer_state", None)
+    if pr is None or not pr.fits(rows, D, dtype):
+        release_peer_buffers(module)
+        pr = PeerReduce(group, rank, world, rows, D, dtype, device)
+        module._peer_state = pr
+    return pr
+
+
+def _peer_routed_scatter(module, x2d, xv_mine, world: int, rank: int, group, route_fn, pd):
+    """Unchunked split-routing forward whose reduce-scatter runs through peer memory: routes of this rank's
+    rows, all-gather of the routes, contraction storing every row's partial into the owning rank's
+    receive slot, then the sum of this rank's slots.  Returns None (nothing launched after the routes'
+    all-gather) when the shape takes a split contraction; the caller then reduces with the collective and
+    gets the routes back for that."""
+    M, D = x2d.shape
+    s = M // world
+    ridx, cnt, ctx = _gather_routes(module, xv_mine, group, world, rank, route_fn)
+    pr = _peer_state(module, s, D, pd, x2d.device)
+    epoch = pr.epoch + 1
+    kg, ku, v, packed, _, _, wout = module._weights()
+    ok = kernels.routed_peer_forward(x2d, kg, ku, v, packed, wout, ridx, cnt, ctx, base_blocks=module.base_blocks,
+                                     block_stride=world, block_offset=rank, peer_out=pr.slots(epoch & 1),
+                                     peer_flags=pr.flags(), rows_per_rank=s, epoch=epoch,
+                                     out_f32=pd == torch.float32)
+    if not ok:
+        return None, (ridx, cnt, ctx)
+    pr.epoch = epoch
+    y = kernels.peer_combine(pr.recv(epoch & 1), pr.base, world, s, D, in_f32=pd == torch.float32, epoch=epoch,
+                             out_dtype=pd, err_ws=pr.err)
+    return y, None
 
 
 def owned_blocks(num_blocks: int, rank: int, world: int):
@@ -156,7 +252,16 @@ def sharded_token_forward(module, x2d: torch.Tensor, *, want_routes: bool = Fals
     if chunks <= 1 or want_routes:
         if split_routes:
             xv = x2d.view(world, s, D)
-            y_part = partial_of(x2d, xv[rank])
+            routes = None
+            if (reduce == "scatter" and getattr(module, "_peer_reduce", False) and x2d.is_cuda
+                    and route_fn is _cuda_route and routed_fn is _cuda_routed_partial):
+                y, routes = _peer_routed_scatter(module, x2d, xv[rank], world, rank, group, route_fn, pd)
+                if y is not None:
+                    return y.to(x2d.dtype), None, None, None
+            if routes is not None:  # the peer path declined this shape: reduce with the collective
+                y_part = routed_fn(module, x2d, world, rank, *routes).to(pd)
+            else:
+                y_part = partial_of(x2d, xv[rank])
             ridx = cnt = S = None
         else:
             y_part, ridx, cnt, S = fn(module, x2d, world, rank, rank == 0, want_routes)

@@ -181,6 +181,47 @@ FP_API int fp_pattention_routed_fwd(const void* x, int64_t M, int D, int NB, int
                                     size_t workspace_bytes, void* stream);
 
 /*
+ * Peer-memory reduce-scatter of the parameter-block-sharded forward (one process per GPU; GPUs with
+ * peer access over NVLink / NVSwitch).  Replaces the NCCL reduce-scatter after the contraction: each rank's
+ * down projection stores the partial rows of token slice o directly into rank o's receive buffer while
+ * it computes, then raises its flag there; each rank's fp_peer_combine waits for every rank's flag and
+ * sums its slots in rank order.
+ *   fp_peer_alloc: a zeroed device buffer of `bytes` and its IPC handle (FP_PEER_HANDLE_BYTES written to
+ *   handle); fp_peer_open maps another process's buffer from its handle (fp_peer_close unmaps it);
+ *   fp_peer_free releases a buffer of fp_peer_alloc.
+ *   Receive buffer layout (bytes): [0, FP_PEER_FLAG_BYTES) flags uint32[world] (flag w = the last epoch
+ *   whose partial rank w finished storing here), then two parities x world slots x rows x D partials
+ *   (bf16, or fp32 with y_f32).  Call e writes parity e % 2; epochs increase by one per call.
+ *   fp_pattention_routed_peer_fwd: fp_pattention_routed_fwd (same inputs, M = world * rows_per_rank)
+ *   whose output rows go to peer_out[o] (this rank's slot of parity e % 2 on rank o; row r of the batch
+ *   to row r - o * rows_per_rank of rank o = r / rows_per_rank), followed by peer_flags[o] = epoch
+ *   (this rank's flag word on rank o, release at system scope).  Returns FP_ERR_UNSUPPORTED before any
+ *   launch when the shape takes the CUDA-core path or a split contraction (small batches): callers fall
+ *   back to the collective.
+ *   fp_peer_combine: y [rows, D] (bf16, or fp32 with y_f32) = sum over w in rank order of recv's slot w
+ *   (recv = this rank's buffer at the parity of `epoch`), after every flags[w] >= epoch; a wait longer
+ *   than the kernels' wait limit (2 s) is reported as FP_ERR_TIMEOUT by fp_device_error(workspace) and leaves y
+ *   unwritten.  workspace: at least 256 bytes (error word).
+ */
+#define FP_PEER_HANDLE_BYTES 64
+#define FP_PEER_FLAG_BYTES 256u
+FP_API int fp_peer_alloc(size_t bytes, void** ptr, void* handle);
+FP_API int fp_peer_open(const void* handle, void** ptr);
+FP_API int fp_peer_close(void* ptr);
+FP_API int fp_peer_free(void* ptr);
+FP_API int fp_pattention_routed_peer_fwd(const void* x, int64_t M, int D, int NB, int dtype, const void* k_gate,
+                                         const void* k_up, const void* v, const void* w_gu, const void* v_t,
+                                         const void* out_proj, int base_blocks, int capacity,
+                                         const int32_t* remote_indices, const int32_t* remote_counts,
+                                         const float* ctx16, int block_stride, int block_offset,
+                                         void* const* peer_out, uint32_t* const* peer_flags, int world,
+                                         int64_t rows_per_rank, uint32_t epoch, int y_f32, void* workspace,
+                                         size_t workspace_bytes, void* stream);
+FP_API int fp_peer_combine(const void* recv, const uint32_t* flags, int world, int64_t rows, int D, int in_f32,
+                           uint32_t epoch, void* y, int y_f32, void* workspace, size_t workspace_bytes,
+                           void* stream);
+
+/*
  * Pooled forward over one shared active set.  Replaces the active-block execution of
  * FovealPattentionMLP.forward (foveal_pattention.py:115-122 gather, :329-335 SwiGLU) and the
  * training-mode additive stream (:338-342) when ctx16 is given.
@@ -344,6 +385,27 @@ FP_API int fp_block_sparse_linear_fwd(const void* x, int64_t M, int D_in, const 
                                       int out_features, int dtype, const int32_t* blocks, const int32_t* n_active,
                                       int max_active, const float* ctx16, const void* out_proj, void* out,
                                       void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * 64 x 64 blocked copy of a row-major bf16 weight [rows, cols] (rows, cols multiples of 64): tile
+ * (kb, j) = weight rows [j*64, +64) x columns [kb*64, +64), stored as one contiguous 8 KB run of 64-element
+ * rows at tile index kb * (rows / 64) + j.  out: rows * cols bf16, 16-byte aligned.  The tensor-core
+ * contraction of fp_block_sparse_linear_blocked_fwd then reads one selected block at one k-block as one
+ * 8 KB run, and four consecutive blocks as one 32 KB run, instead of 64 row pieces of 128 bytes.
+ */
+FP_API int fp_pack_blocked_weight(const void* weight, int rows, int cols, void* out, void* stream);
+
+/*
+ * fp_block_sparse_linear_fwd with the weight's blocked copy (fp_pack_blocked_weight of weight
+ * [out_features, D_in]; bf16, D_in % 64 == 0) as the tensor cores' operand.  weight stays required (the
+ * CUDA-core path for shapes the tensor path does not tile reads it); weight_blocked == NULL is
+ * fp_block_sparse_linear_fwd.  Same workspace.
+ */
+FP_API int fp_block_sparse_linear_blocked_fwd(const void* x, int64_t M, int D_in, const void* weight,
+                                              const void* weight_blocked, const void* bias, int out_features,
+                                              int dtype, const int32_t* blocks, const int32_t* n_active,
+                                              int max_active, const float* ctx16, const void* out_proj, void* out,
+                                              void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * FovealTokenformerLinear contraction over the active parameter tokens (tokenformer.py:183-203):

@@ -319,6 +319,35 @@ def test_block_shards_sum_to_full():
     assert rel_err(sum(parts).cpu(), full.cpu()) < 1e-5
 
 
+@pytest.mark.parametrize("M", [1, 5, 40, 64])
+def test_decode_sizes_split_and_shards(M):
+    """Batches of at most 64 tokens at the 8B shape: each gate/up tile's contraction is split over D in
+    four work units summed in split order by the last to arrive, and the down projection contracts over
+    the touched blocks only.  Outputs match the oracle, repeated calls are bitwise identical (the split
+    sum does not depend on arrival order), and stride-4 block shards sum to the unsharded forward."""
+    wl = configs.CONFIGS["8b"]
+    w = configs.make_weights(wl)
+    x2d = configs.make_x(wl).reshape(-1, wl.hidden_dim)[:M].contiguous()
+    m = module_for(wl, w)
+    y, info = run_token(m, x2d)
+    y2, _ = run_token(m, x2d)
+    assert torch.equal(y, y2)
+    idx, cnt = info["remote_indices"].cpu(), info["remote_counts"].cpu()
+    S = oracle.router_scores(x2d, w.q_proj_16d, w.block_keys_16d) / wl.temperature
+    ref = oracle.token_pattention(x2d, w.k_gate, w.k_up, w.v, wl.base_blocks, idx, cnt)
+    ref = ref + oracle.additive_stream(S, w.block_keys_16d, w.out_proj_16d)
+    check_y(y.cpu(), ref, wl.dtype)
+    kg, ku, v, packed, wq, k16, wout = m._weights()
+    kw = dict(base_blocks=wl.base_blocks, top_p=wl.top_p, min_remote=wl.min_remote_blocks,
+              max_remote=wl.max_remote_blocks)
+    xd = x2d.to(DEV, torch.bfloat16)
+    full, _, _, _ = fsi.kernels.token_forward(xd, kg, ku, v, packed, wq, k16, wout, out_f32=True, **kw)
+    parts = [fsi.kernels.token_forward(xd, kg, ku, v, packed, wq, k16, wout, out_f32=True, block_stride=4,
+                                       block_offset=r, additive=(r == 0), **kw)[0] for r in range(4)]
+    assert rel_err(sum(parts).cpu(), full.cpu()) < 1e-5
+    device_error_is_clear()
+
+
 def test_split_routing_entry_points():
     """The token-routed forward split in two (fp_route_tokens, then fp_pattention_routed_fwd from the given
     routes): the routes equal the fused forward's, four stride-4 shards from the given routes (additive

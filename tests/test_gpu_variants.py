@@ -174,6 +174,43 @@ def test_block_sparse_linear_tensor_path(M, D_in, out_features, kmax, top_p, bia
         assert rel_err(y.float().cpu()[:, cols], ref[:, cols]) < 2e-2
 
 
+@pytest.mark.parametrize("M,D_in,out_features,nact", [
+    (600, 1024, 4096, 40),   # two token tiles: CTA-pair kernel, runs of consecutive blocks and gaps
+    (64, 1024, 14336, 200),  # decode-sized: one-SM kernel split over D_in, four-block runs as one box
+    (1, 4096, 14336, 12),    # one token, a sparse union
+    (300, 512, 1536, 24),    # every block, output width not a multiple of 256
+])
+def test_blocked_weight_matches_row_major(M, D_in, out_features, nact):
+    """The blocked weight copy (fp_pack_blocked_weight) gives the row-major weight's results bit for bit
+    (same k-block order and MMA shapes); the layout itself is checked tile by tile."""
+    g = torch.Generator().manual_seed(M + nact)
+    NB = out_features // 64
+    W = (torch.randn(out_features, D_in, generator=g) * D_in ** -0.5).to(DEV, torch.bfloat16)
+    x = torch.randn(M, D_in, generator=g).to(DEV, torch.bfloat16)
+    b = (torch.randn(out_features, generator=g) * 0.05).to(DEV, torch.bfloat16)
+    ctx = torch.randn(M, 16, generator=g).to(DEV)
+    wo = (torch.randn(out_features, 16, generator=g) * 0.05).to(DEV, torch.bfloat16)
+    act = torch.randperm(NB, generator=g)[:nact].sort().values
+    rest = torch.tensor(sorted(set(range(NB)) - set(act.tolist())), dtype=torch.int64)
+    blocks = torch.cat([act, rest]).int().to(DEV)
+    n_active = torch.tensor([nact], dtype=torch.int32, device=DEV)
+    Wb = kernels.pack_blocked_weight(W)
+    tiles = Wb.view(D_in // 64, NB, 64, 64)
+    for kb, j in ((0, 0), (D_in // 64 - 1, NB - 1), (1, NB // 2)):
+        assert torch.equal(tiles[kb, j], W[j * 64:(j + 1) * 64, kb * 64:(kb + 1) * 64])
+    ma = nact  # the host-side bound of the union: exact here
+    y0 = kernels.block_sparse_linear(x, W, b, blocks, n_active, ctx, wo, max_active=ma)
+    y1 = kernels.block_sparse_linear(x, W, b, blocks, n_active, ctx, wo, max_active=ma, weight_blocked=Wb)
+    ref = x.float() @ W.float().t() + b.float() + ctx @ wo.float().t()
+    inactive = torch.ones(NB, dtype=torch.bool)
+    inactive[act] = False
+    cols = (inactive.nonzero().view(-1, 1) * 64 + torch.arange(64)).flatten().to(DEV)
+    ref[:, cols] = ctx @ wo.float()[cols].t()
+    torch.cuda.synchronize()
+    assert torch.equal(y0, y1)
+    assert rel_err(y1.float(), ref) < 2e-2
+
+
 @pytest.mark.parametrize("M,D_in,D_out,Np,kmax,activation", [
     (300, 512, 768, 4096, 8, "softmax"),
     (129, 256, 256, 2048, 16, "gelu_l2"),

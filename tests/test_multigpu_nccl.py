@@ -78,13 +78,26 @@ def _worker(rank, world, port, out_dir):
         # from device memory and from pinned host memory
         ysl = fsi.sharding.sharded_forward_slices(mb, x[rows].contiguous(), chunks=4)
         yh = fsi.sharding.sharded_forward_host(mb, x[rows].cpu().pin_memory(), chunks=4)
+        # peer-memory reduce-scatter: the contraction stores the peer's rows over NVLink; three calls cover
+        # both receive parities and a reused buffer; bf16 and fp32 partials
+        mp_ = module()
+        fsi.sharding.shard_parameter_blocks(mp_, peer_reduce=True)
+        yp = [fsi.sharding.sharded_token_forward(mp_, x, reduce="scatter")[0] for _ in range(3)]
+        peer_err = fsi._lib.device_error(mp_._peer_state.err)
+        peer_epoch = mp_._peer_state.epoch
+        fsi.sharding.release_peer_buffers(mp_)
+        mf = module()
+        fsi.sharding.shard_parameter_blocks(mf, partial_dtype=torch.float32, peer_reduce=True)
+        ypf = fsi.sharding.sharded_token_forward(mf, x, reduce="scatter")[0]
+        fsi.sharding.release_peer_buffers(mf)
     torch.cuda.synchronize()
     e_all = max(rel_err(y.float(), full.float()), rel_err(yc.float(), full.float()))
     e_all = max(e_all, rel_err(ysa.float(), full.float()))
-    e_sc = max(rel_err(t.float().cpu(), full[rows].float().cpu()) for t in (ys, ysc, ysb, ysr, ysl, yh))
+    e_sc = max(rel_err(t.float().cpu(), full[rows].float().cpu()) for t in (ys, ysc, ysb, ysr, ysl, yh, *yp, ypf))
     same_routes = bool(torch.equal(info["remote_indices"], info_full["remote_indices"]))
+    peer_ok = int(peer_err == 0 and peer_epoch == 3 and torch.equal(yp[0], yp[1]) and torch.equal(yp[1], yp[2]))
     with open(os.path.join(out_dir, f"r{rank}.txt"), "w") as f:
-        f.write(f"{e_all} {e_sc} {int(same_routes)}")
+        f.write(f"{e_all} {e_sc} {int(same_routes)} {peer_ok}")
     dist.barrier()
     dist.destroy_process_group()
 
@@ -102,5 +115,6 @@ def test_block_sharded_forward_over_nccl_matches_single_gpu():
                         p.kill()
                 pytest.fail("sharded forward did not finish")
         for r in range(2):
-            e_all, e_sc, same = open(os.path.join(d, f"r{r}.txt")).read().split()
+            e_all, e_sc, same, peer_ok = open(os.path.join(d, f"r{r}.txt")).read().split()
             assert float(e_all) < 2e-2 and float(e_sc) < 2e-2 and same == "1", (r, e_all, e_sc, same)
+            assert peer_ok == "1", r  # peer path: no wait ran out, three epochs, repeated calls bit-equal
