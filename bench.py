@@ -621,9 +621,11 @@ def run_ours_sharded(args, rank, world, local, dev):
         part = torch.empty(M, D, dtype=pd, device=dev)
         ys = torch.empty(M // world, D, dtype=pd, device=dev)
         t_rs, _ = timed_steps(lambda: dist.reduce_scatter_tensor(ys, part), 10, dev, world)
-        err = fsi._lib.device_error(fsi._lib.workspace(dev, 0))
         peer_state = getattr(m, "_peer_state", None)
         peer_used = peer_state is not None and peer_state.epoch > 0
+        if peer_used:
+            stage["peer"] = peer_stage_times(m, x, world, rank)
+        err = fsi._lib.device_error(fsi._lib.workspace(dev, 0))
         if peer_state is not None:
             err = err or fsi._lib.device_error(peer_state.err)
         fsi.sharding.release_peer_buffers(m)
@@ -673,6 +675,37 @@ def run_ours_sharded(args, rank, world, local, dev):
     if bs70 is not None:
         line["blockshard_70b"] = bs70
     return line
+
+
+def peer_stage_times(m, x, world, rank, K=10):
+    """Where the peer-memory step's time goes on this rank (CUDA events, mean of K calls): routing of this
+    rank's rows + the route all-gather; the contraction whose epilogue stores each row on its owner
+    (+ the flag kernel); the combine (including its wait for the other ranks' flags)."""
+    sh = fsi.sharding
+    M, D = x.shape
+    s = M // world
+    xv = x.view(world, s, D)
+    pd = sh._partial_dtype(m)
+    kg, ku, v, packed, _, _, wout = m._weights()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
+    for k in range(K):
+        ev[k][0].record()
+        ridx, cnt, ctx = sh._gather_routes(m, xv[rank], None, world, rank, sh._cuda_route)
+        ev[k][1].record()
+        pr = sh._peer_state(m, s, D, pd, x.device)
+        e = pr.epoch + 1
+        fsi.kernels.routed_peer_forward(x, kg, ku, v, packed, wout, ridx, cnt, ctx, base_blocks=m.base_blocks,
+                                        block_stride=world, block_offset=rank, peer_out=pr.slots(e & 1),
+                                        peer_flags=pr.flags(), rows_per_rank=s, epoch=e,
+                                        out_f32=pd == torch.float32)
+        pr.epoch = e
+        ev[k][2].record()
+        fsi.kernels.peer_combine(pr.recv(e & 1), pr.base, world, s, D, in_f32=pd == torch.float32, epoch=e,
+                                 out_dtype=pd, err_ws=pr.err)
+        ev[k][3].record()
+    torch.cuda.synchronize()
+    mean = lambda i: statistics.mean(ev[k][i].elapsed_time(ev[k][i + 1]) for k in range(K))  # noqa: E731
+    return {"route_and_allgather": mean(0), "contraction_with_peer_stores": mean(1), "combine_incl_wait": mean(2)}
 
 
 def measure_e2e_sharded(args, m, x_cpu, rank, world, dev):

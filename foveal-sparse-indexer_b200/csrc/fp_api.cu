@@ -329,6 +329,21 @@ int fp_pattention_token_fwd(const void* x, int64_t M, int D, int NB, int dtype, 
   if (L.gu_ks > 1) {
     g.gu_ks = L.gu_ks; g.gu_part = at<float>(workspace, L.gu_part); g.max_tiles = L.max_tiles;
   }
+  if (M <= 64 && block_stride == 1) {
+    // HBM is idle while the routing kernels run, and the gate/up CTAs start (programmatic launch) on the
+    // SMs the routing leaves free: each pulls a share of the packed gate/up tiles of the lowest block ids
+    // (the first work units take the touched blocks in ascending order) into L2, about half of L2 at most
+    const int64_t tile_bytes = (int64_t)kTileM * kTileK * 2;  // 16 KB: one block at one k-block
+    const int nkb = D / kTileK;
+    const int64_t budget = 64ll << 20;
+    const int nblk = (int)std::min<int64_t>(NB, budget / ((int64_t)nkb * tile_bytes));
+    if (nblk > 0) {
+      g.pf.base = static_cast<const char*>(w_gu);
+      g.pf.stride = (int64_t)NB * tile_bytes;  // tile (kb, b) at (kb * NB + b) * 16 KB
+      g.pf.bytes = (int64_t)nblk * tile_bytes;
+      g.pf.n = nkb;
+    }
+  }
   FP_TRY(launch_gateup(g, st));
   stage_mark(3, st);
   DownArgs d{};

@@ -51,18 +51,21 @@ constexpr size_t kGemmSmem = 1024 + kStages * kStageBytes + sizeof(PipeBars) + 6
 // 16 KB (weights) + NMAX x 128 B (token rows).  <256, 4> in general; <64, 8> for batches of at most 64
 // tokens (decode), whose tiles are small and whose time is the streaming of the blocks' weights: twice
 // the stages keep twice the bytes in flight per SM.
-template <int NMAX, int STAGES>
+template <int NMAX, int STAGES, int GATHER_WARPS>
 struct GuCfg {
   static constexpr int kN = NMAX;
   static constexpr int kS = STAGES;
+  // token-row gather warps (cp.async), warps 6..; fewer for small tiles leaves each thread more registers
+  static constexpr int kGatherThreads = 32 * GATHER_WARPS;
+  static constexpr int kThreads = 192 + kGatherThreads;
   using Bars = PipeBarsT<STAGES>;
   static constexpr uint32_t kBBytes = NMAX * kTileK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr size_t kSmem = 1024 + STAGES * kStageBytes + sizeof(Bars) + 64;
   static_assert(kSmem <= 227 * 1024, "gate/up shared memory");
 };
-using GuBig = GuCfg<kGuN, kGuStages>;
-using GuSmall = GuCfg<64, 8>;
+using GuBig = GuCfg<kGuN, kGuStages, 16>;
+using GuSmall = GuCfg<64, 8, 8>;
 
 __device__ __forceinline__ uint8_t* aligned_smem(uint8_t* raw) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
@@ -210,18 +213,16 @@ __device__ __forceinline__ void gu_store_chunk(const GateUpArgs& a, const uint32
   }
 }
 
-constexpr int kGatherWarps = 16;                         // token-row gather warps (cp.async)
-constexpr int kGatherThreads = 32 * kGatherWarps;
-constexpr int kGuThreads = 192 + kGatherThreads;         // warps 6.. gather
 
 template <class Cfg>
-__global__ void __launch_bounds__(kGuThreads, 1)
+__global__ void __launch_bounds__(Cfg::kThreads, 1)
 gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
               const GateUpArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = aligned_smem(smem_raw);
   constexpr int kN = Cfg::kN, kS = Cfg::kS;
   constexpr uint32_t kStage = Cfg::kStageBytes;
+  constexpr int kGatherThreads = Cfg::kGatherThreads;
   constexpr int kRowsPerGatherThread = kN * 8 / kGatherThreads;  // 16-byte chunks per thread per stage
   static_assert(kRowsPerGatherThread * kGatherThreads == kN * 8, "gather split");
   using Bars = typename Cfg::Bars;
@@ -235,6 +236,18 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
   }
   // full barrier: one expect_tx arrival (TMA) + one arrival per gather thread
   pipe_init(bars, 4, 1 + kGatherThreads);
+  if (kN == 64 && a.pf.n > 0) {
+    // while the routing kernel runs: this CTA's share of the L2 prefetch, 64 KB pieces dealt round-robin
+    // over the CTAs (each SM's copy engine generates only its share of the requests)
+    constexpr int64_t kPiece = 64 * 1024;
+    const int64_t per_run = (a.pf.bytes + kPiece - 1) / kPiece;
+    const int64_t total = per_run * a.pf.n;
+    for (int64_t i = blockIdx.x + (int64_t)threadIdx.x * gridDim.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t run = i / per_run, off = (i - run * per_run) * kPiece;
+      const int64_t len = a.pf.bytes - off < kPiece ? a.pf.bytes - off : kPiece;
+      bulk_prefetch_l2(a.pf.base + run * a.pf.stride + off, (uint32_t)len);
+    }
+  }
   griddep_wait();  // the routing kernel's work list, token lists and cleared H are complete
   griddep_launch_dependents();
   const uint32_t tmem_base = bars->tmem;
@@ -795,9 +808,10 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
         float o[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) o[i] = kempty ? 0.f : __uint_as_float(v[i]);
-        // the additive stream and the bias are added by one split only
         const int col0 = n * kTileN + c * 32;
-        down_store_chunk(a, o, ctx, row, row_ok, col0, ((c >> 1) == 0 ? ocb0 : (c >> 1) == 1 ? ocb1 : (c >> 1) == 2 ? ocb2 : ocb3) + (col0 & 63), split == 0, split, ks, ncols);
+        // the additive stream and the bias of chunk c are added by split c % ks only: spread over the
+        // splits (one split doing all of them made it the last to finish)
+        down_store_chunk(a, o, ctx, row, row_ok, col0, ((c >> 1) == 0 ? ocb0 : (c >> 1) == 1 ? ocb1 : (c >> 1) == 2 ? ocb2 : ocb3) + (col0 & 63), c % ks == split, split, ks, ncols);
       }
       tc_fence_before();
       __syncwarp();
@@ -1301,7 +1315,7 @@ static int launch_gateup_cfg(const GateUpArgs& a, cudaStream_t st) {
                                 (int)Cfg::kSmem) == cudaSuccess ? FP_OK : FP_ERR_CUDA;
   });
   if (attr != FP_OK) return attr;
-  if (launch_pdl(gateup_kernel<Cfg>, dim3(a.num_sms), dim3(kGuThreads), Cfg::kSmem, st, tx, tw, a) != cudaSuccess)
+  if (launch_pdl(gateup_kernel<Cfg>, dim3(a.num_sms), dim3(Cfg::kThreads), Cfg::kSmem, st, tx, tw, a) != cudaSuccess)
     return FP_ERR_CUDA;
   if (Cfg::kN == 64 && a.gu_ks > 1) {
     // the tile count is on the device: one CTA per possible tile, idle past it

@@ -80,6 +80,14 @@ struct SelectOut {
 // Fused token routing (scores + selection + block CSR) of the token-routed forward.
 // Block CSR: key = chunk(t) * nbl + slot(b) for the local blocks (b % stride == offset, slot = b / stride);
 // each key owns a bucket of key_cap entries of pair_tok.  key_cnt and *ticket must be zero on entry.
+// Runs of memory pulled into L2 while the routing kernels leave HBM idle (batches of at most 64 tokens):
+// n runs of `bytes` starting at base + i * stride.
+struct L2Prefetch {
+  const char* base = nullptr;
+  int64_t stride = 0, bytes = 0;
+  int n = 0;
+};
+
 struct RouteArgs {
   const void* x;        // [M, D]
   const void* wq;       // [16, D]
@@ -142,6 +150,8 @@ struct GateUpArgs {
   int gu_ks = 1;
   float* gu_part = nullptr;
   int max_tiles = 0;  // bound of the device tile count (sizes the second kernel's grid)
+  // issued by every CTA before it waits for the routing kernel (batches of at most 64 tokens)
+  L2Prefetch pf;
 };
 int launch_gateup(const GateUpArgs& a, cudaStream_t st);
 // Work units of the decode split: k-blocks per unit at least 8, at most 4 units per tile.

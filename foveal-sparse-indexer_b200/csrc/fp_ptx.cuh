@@ -143,6 +143,10 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* map, uint64_t
       ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
       : "memory");
 }
+// Asynchronous prefetch of [p, p + bytes) into L2 (p 16-byte aligned, bytes a multiple of 16).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 // L2 policy for data read exactly once per call (streamed weights): evicted before other lines.
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t p;
