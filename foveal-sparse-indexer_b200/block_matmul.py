@@ -87,6 +87,31 @@ class BlockSparseLinear(nn.Module):
         nn.init.normal_(self.indexer.out_proj.weight, std=1e-3)
         self._cached_kp: Optional[Tensor] = None
         self._cached_vp: Optional[Tensor] = None
+        self._blocked_on = False
+        self._blocked: Optional[Tensor] = None
+        self._blocked_key = None
+
+    def use_blocked_weight(self, enable: bool = True) -> "BlockSparseLinear":
+        """Keep a 64 x 64 blocked copy of the bf16 weight for the eval-mode tensor-core contraction
+        (``fp_pack_blocked_weight``): each selected block at one k-block is one contiguous 8 KB run instead of
+        64 row pieces of 128 bytes (measured ~8 % faster at 64 tokens on the 4096 -> 14336 shape, unchanged
+        at 1 and 16384 tokens), at the cost of a second copy of the weight in device memory.  Results are
+        bit-identical.  Rebuilt when the weight changes."""
+        self._blocked_on = bool(enable)
+        if not enable:
+            self._blocked, self._blocked_key = None, None
+        return self
+
+    def _blocked_weight(self) -> Optional[Tensor]:
+        w = self.weight
+        if (not self._blocked_on or self.training or w.dtype != torch.bfloat16 or not w.is_cuda
+                or self.in_features % 64):
+            return None
+        key = (w.data_ptr(), w._version, tuple(w.shape))
+        if self._blocked_key != key:
+            self._blocked = kernels.pack_blocked_weight(w.detach())
+            self._blocked_key = key
+        return self._blocked
 
     def reset_parameters(self) -> None:
         """block_matmul.py:101-106."""
@@ -144,7 +169,8 @@ class BlockSparseLinear(nn.Module):
         ctx16 = additive_context(scores, vb) if self.use_additive_stream else None
         max_active = min(NB, base + M * idx.shape[-1])  # host-side bound of the union
         out2d = kernels.block_sparse_linear(x2d, self.weight, self.bias, blocks, n_active, ctx16,
-                                            self.indexer.out_proj.weight, max_active=max_active)
+                                            self.indexer.out_proj.weight, max_active=max_active,
+                                            weight_blocked=self._blocked_weight())
         return {"out": out2d, "scores": scores, "route": route, "stats": stats, "blocks": blocks,
                 "n_active": n_active, "ctx16": ctx16}
 

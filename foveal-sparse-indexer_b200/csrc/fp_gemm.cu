@@ -24,6 +24,7 @@
 #include "fp_internal.cuh"
 
 #include <cudaTypedefs.h>
+#include <cstring>
 #include <mutex>
 
 namespace fp {
@@ -69,6 +70,41 @@ using GuSmall = GuCfg<64, 8, 8>;
 
 __device__ __forceinline__ uint8_t* aligned_smem(uint8_t* raw) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+}
+
+// Sum over splits of 4 consecutive fp32 partials at element offset `off` (stride `n` between splits), in
+// split order; the loads of up to 8 splits are issued before the first add (decode-size reductions are
+// bound by load latency, not bandwidth).
+__device__ __forceinline__ float4 splitk_sum4(const float* __restrict__ part, int ks, int64_t n, int64_t off) {
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int k0 = 0; k0 < ks; k0 += 8) {
+    float4 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (k0 + j < ks) v[j] = __ldcg(reinterpret_cast<const float4*>(part + (int64_t)(k0 + j) * n + off));
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (k0 + j < ks) {
+        if (k0 + j == 0) {
+          acc = v[j];
+        } else {
+          acc.x += v[j].x; acc.y += v[j].y; acc.z += v[j].z; acc.w += v[j].w;
+        }
+      }
+  }
+  return acc;
+}
+
+__device__ __forceinline__ void store4(void* out, int64_t idx, float4 s, int out_f32) {
+  if (out_f32) {
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + idx) = s;
+  } else {
+    const __nv_bfloat162 a = __floats2bfloat162_rn(s.x, s.y), b = __floats2bfloat162_rn(s.z, s.w);
+    uint2 u;
+    u.x = *reinterpret_cast<const uint32_t*>(&a);
+    u.y = *reinterpret_cast<const uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(out) + idx) = u;
+  }
 }
 
 // Lane 0 waits, the warp follows its verdict (keeps warp-collective instructions uniform).
@@ -427,26 +463,32 @@ __global__ void __launch_bounds__(kGuCombineThreads) gateup_split_combine_kernel
   constexpr int kN = 64;
   __shared__ float s_acc[kTileM][kN + 1];
   __shared__ int s_tok[kN];
-  griddep_wait();  // every unit's partial is stored
-  griddep_launch_dependents();
+  // The work list and token lists were written by the routing kernel, which completed before the gate/up
+  // kernel passed its own wait, i.e. before this grid was launched: they are read before the wait for the
+  // gate/up partials, off the critical path.  (A CTA with a second tile reads it after the wait.)
   const int ks = a.gu_ks;
   const int ntiles = a.meta[0];
   const bool swiglu = a.act == FP_ACT_SWIGLU;
+  GuTile t0{};
+  int tok0 = -1;
+  if (blockIdx.x < ntiles) {
+    t0 = gu_decode<kN>(a, blockIdx.x);
+    if (threadIdx.x < t0.n) tok0 = gu_token(t0, threadIdx.x, a);
+  }
+  griddep_wait();  // every unit's partial is stored
+  griddep_launch_dependents();
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-    const GuTile t = gu_decode<kN>(a, tile);
+    const bool first = tile == (int)blockIdx.x;
+    const GuTile t = first ? t0 : gu_decode<kN>(a, tile);
     if (t.n <= 0) continue;  // uniform over the CTA
     const int npad = (t.n + 15) & ~15;
     const int nq = npad / 4;  // float4 per row
-    if (threadIdx.x < t.n) s_tok[threadIdx.x] = gu_token(t, threadIdx.x, a);
+    if (threadIdx.x < t.n) s_tok[threadIdx.x] = first ? tok0 : gu_token(t, threadIdx.x, a);
     const float4* part = reinterpret_cast<const float4*>(a.gu_part + (int64_t)tile * ks * kTileM * kN);
     for (int i = threadIdx.x; i < kTileM * nq; i += kGuCombineThreads) {
       const int row = i / nq, c4 = i - row * nq;
       const int64_t off = (int64_t)row * (kN / 4) + c4;
-      float4 v = __ldcg(part + off);
-      for (int sp = 1; sp < ks; ++sp) {
-        const float4 p = __ldcg(part + (int64_t)sp * kTileM * (kN / 4) + off);
-        v.x += p.x; v.y += p.y; v.z += p.z; v.w += p.w;
-      }
+      const float4 v = splitk_sum4(reinterpret_cast<const float*>(part), ks, (int64_t)kTileM * kN, 4 * off);
       s_acc[row][4 * c4] = v.x; s_acc[row][4 * c4 + 1] = v.y;
       s_acc[row][4 * c4 + 2] = v.z; s_acc[row][4 * c4 + 3] = v.w;
     }
@@ -553,15 +595,10 @@ __device__ __forceinline__ void down_tile(int tile, int m_tiles, int n_tiles, in
 // contributor of a tile).  With split-K (ks > 1) the fp32 partial of split `split` is stored instead of
 // the output.  Computed column c lands in Y column omap[c / 64] * 64 + c % 64 (block-mapped form) or c;
 // columns at or beyond `ncols` are not stored.
-__device__ __forceinline__ void down_store_chunk(const DownArgs& a, float (&o)[32], const float (&ctx)[16],
-                                                 int64_t row, bool row_ok, int col0, int ocol0, bool add, int split,
-                                                 int ks, int ncols) {
+// The additive stream and the bias of one 32-column chunk (see down_store_chunk), in place.
+__device__ __forceinline__ void down_add_chunk(const DownArgs& a, float (&o)[32], const float (&ctx)[16], int ocol0,
+                                               bool add) {
   const int lane = threadIdx.x & 31;
-  if (col0 >= ncols) return;  // uniform over the warp
-  if (a.omap && (ocol0 < 0 || ocol0 + 32 > (a.ldy > 0 ? (int64_t)a.ldy : (int64_t)a.D))) {
-    record_error(a.err, kErrBadTile);  // a block map entry outside Y: reported, nothing stored
-    return;
-  }
   if (a.ctx16 && add) {
     // o[i] += sum_k ctx[k] * W_out[ocol0 + i][k]; lane L loads row ocol0 + L of W_out and the warp
     // broadcasts it (all lanes of a chunk share the same 32 columns)
@@ -601,6 +638,17 @@ __device__ __forceinline__ void down_store_chunk(const DownArgs& a, float (&o)[3
       o[i] += a.bias_f32 ? __ldg(reinterpret_cast<const float*>(a.bias) + ocol0 + i)
                          : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.bias)[ocol0 + i]);
   }
+}
+
+__device__ __forceinline__ void down_store_chunk(const DownArgs& a, float (&o)[32], const float (&ctx)[16],
+                                                 int64_t row, bool row_ok, int col0, int ocol0, bool add, int split,
+                                                 int ks, int ncols) {
+  if (col0 >= ncols) return;  // uniform over the warp
+  if (a.omap && (ocol0 < 0 || ocol0 + 32 > (a.ldy > 0 ? (int64_t)a.ldy : (int64_t)a.D))) {
+    record_error(a.err, kErrBadTile);  // a block map entry outside Y: reported, nothing stored
+    return;
+  }
+  down_add_chunk(a, o, ctx, ocol0, add);
   if (!row_ok) return;
   const int64_t ldy = a.ldy > 0 ? a.ldy : (int64_t)a.D;
   // output row: this rank's Y, or (peer output) the receive slot of the rank that owns the row
@@ -834,12 +882,19 @@ constexpr uint32_t kPairABytes = kTileM * kTileK * 2;          // 16 KB: 128 row
 constexpr uint32_t kPairBBytes = (kTileN / 2) * kTileK * 2;    // 16 KB: 128 rows of V_t
 constexpr uint32_t kPairStageBytes = kPairABytes + kPairBBytes;
 using PairBars = PipeBarsT<kPairStages>;
-constexpr size_t kPairSmem = 1024 + kPairStages * kPairStageBytes + sizeof(PairBars) + 64;
+// Peer output by TMA: per epilogue warp two 4 KB tiles (32 rows x 64 bf16 columns, 128-byte swizzle) in
+// shared memory, stored to the owning rank while the warp fills the other one.
+constexpr uint32_t kPeerTileBytes = 32 * 64 * 2;
+constexpr uint32_t kPeerStageOffset = ((kPairStages * kPairStageBytes + sizeof(PairBars) + 1023) / 1024) * 1024;
+constexpr size_t kPairSmem = 1024 + kPeerStageOffset + 4 * 2 * kPeerTileBytes;
 static_assert(kPairSmem <= 227 * 1024, "pair down shared memory");
+struct PeerMaps {
+  CUtensorMap m[kMaxPeers];  // this rank's receive slot on rank o: [peer_rows, D] bf16, box 32 x 64
+};
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
 down2_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CUtensorMap tm_vt,
-             const __grid_constant__ CUtensorMap tm_vt_wide, const DownArgs a) {
+             const __grid_constant__ CUtensorMap tm_vt_wide, const DownArgs a, const __grid_constant__ PeerMaps pm) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = aligned_smem(smem_raw);
   PairBars* bars = reinterpret_cast<PairBars*>(smem + kPairStages * kPairStageBytes);
@@ -981,6 +1036,8 @@ down2_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ C
     // ---------------- epilogue (both CTAs): warp w drains TMEM lanes [32*(w%4), +32) of its CTA
     const int q = warp & 3;
     int local = 0;
+    uint8_t* peer_stage = smem + kPeerStageOffset;
+    uint32_t peer_buf = 0;
     for (int tile = pair; tile < tiles; tile += npairs) {
       int m, n;
       down_tile(tile, m_pairs, n_tiles, m, n);
@@ -1008,22 +1065,70 @@ down2_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ C
           ctx[4 * i] = f.x; ctx[4 * i + 1] = f.y; ctx[4 * i + 2] = f.z; ctx[4 * i + 3] = f.w;
         }
       }
-      for (int c = 0; c < kTileN / 32; ++c) {
-        uint32_t v[32];
-        __syncwarp();
-        tmem_ld32(tmem_base + acc * kTileN + c * 32 + ((uint32_t)(32 * q) << 16), v);
-        tmem_ld_wait();
-        float o[32];
+      const int64_t row0 = row - lane;  // the warp's first row
+      if (a.peer_tma) {
+        // peer output: 64-column pieces of the warp's 32 rows go to the owning rank by TMA from shared
+        // memory (the stores run asynchronously; the warp only waits before refilling a tile buffer)
+        const int owner = (int)(row0 / a.peer_rows);
+        const bool store = row0 < a.M && owner < kMaxPeers;
+        const int yrow0 = (int)(row0 - (int64_t)owner * a.peer_rows);
+        for (int c2 = 0; c2 < kTileN / 64; ++c2) {
+          uint8_t* tilebuf = peer_stage + (2 * q + (peer_buf & 1)) * kPeerTileBytes;
+          if (lane == 0) bulk_wait_read<1>();  // this buffer's previous store has read it
+          __syncwarp();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = nkb > 0 ? __uint_as_float(v[i]) : 0.f;  // no k-block: zero
-        const int col0 = n * kTileN + c * 32;
-        down_store_chunk(a, o, ctx, row, row_ok, col0, ((c >> 1) == 0 ? ocb0 : (c >> 1) == 1 ? ocb1 : (c >> 1) == 2 ? ocb2 : ocb3) + (col0 & 63), true, 0, 1, ncols);
+          for (int h = 0; h < 2; ++h) {
+            const int c = 2 * c2 + h;
+            uint32_t v[32];
+            __syncwarp();
+            tmem_ld32(tmem_base + acc * kTileN + c * 32 + ((uint32_t)(32 * q) << 16), v);
+            tmem_ld_wait();
+            float o[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = nkb > 0 ? __uint_as_float(v[i]) : 0.f;
+            const int col0 = n * kTileN + c * 32;
+            down_add_chunk(a, o, ctx, col0, true);
+            // row `lane` of the 128-byte swizzled tile: 16-byte piece j of the row at (j ^ lane % 8) * 16
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint32_t pk[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const __nv_bfloat162 b2 = __floats2bfloat162_rn(o[8 * j + 2 * e], o[8 * j + 2 * e + 1]);
+                pk[e] = *reinterpret_cast<const uint32_t*>(&b2);
+              }
+              const int piece = 4 * h + j;
+              *reinterpret_cast<uint4*>(tilebuf + lane * 128 + ((piece ^ (lane & 7)) << 4)) =
+                  make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && store) {
+            tma_store_2d(&pm.m[owner], smem_u32(tilebuf), n * kTileN + c2 * 64, yrow0);
+            bulk_commit();
+          }
+          ++peer_buf;
+        }
+      } else {
+        for (int c = 0; c < kTileN / 32; ++c) {
+          uint32_t v[32];
+          __syncwarp();
+          tmem_ld32(tmem_base + acc * kTileN + c * 32 + ((uint32_t)(32 * q) << 16), v);
+          tmem_ld_wait();
+          float o[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = nkb > 0 ? __uint_as_float(v[i]) : 0.f;  // no k-block: zero
+          const int col0 = n * kTileN + c * 32;
+          down_store_chunk(a, o, ctx, row, row_ok, col0, ((c >> 1) == 0 ? ocb0 : (c >> 1) == 1 ? ocb1 : (c >> 1) == 2 ? ocb2 : ocb3) + (col0 & 63), true, 0, 1, ncols);
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_leader(&bars->acce[acc]);
       ++local;
     }
+    if (a.peer_tma && lane == 0) bulk_wait_all();  // every peer store of this warp has completed
   }
 
   // ---------------- teardown: every MMA has completed (leader: done barrier; peer: its last accf), no
@@ -1235,15 +1340,13 @@ gateup2_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
   }
 }
 
-// Sums the split-K partials [ks][n] in split order (deterministic) and writes the output dtype.
+// Sums the split-K partials [ks][n] in split order (deterministic) and writes the output dtype; 4 elements
+// per thread (n % 4 == 0: D % 64 == 0 on the tensor-core path).
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int ks, int64_t n, void* out, int out_f32) {
   griddep_wait();  // every split's partial is stored
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t i = 4 * ((int64_t)blockIdx.x * blockDim.x + threadIdx.x);
   if (i >= n) return;
-  float s = part[i];
-  for (int k = 1; k < ks; ++k) s += part[(int64_t)k * n + i];
-  if (out_f32) reinterpret_cast<float*>(out)[i] = s;
-  else reinterpret_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(s);
+  store4(out, i, splitk_sum4(part, ks, n, i), out_f32);
 }
 
 // Block-mapped form: sums the split partials [ks][M][D] (computed columns) of the first 64 * ncnt
@@ -1253,16 +1356,14 @@ __global__ void splitk_reduce_mapped_kernel(const float* __restrict__ part, int 
                                             void* out, int64_t ldy, int out_f32) {
   griddep_wait();  // every split's partial is stored
   const int ncols = ncnt ? max(0, min(D / kBlock, *ncnt)) * kBlock : D;
-  const int64_t n = M * ncols;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t m = i / ncols;
-    const int c = (int)(i - m * ncols);
-    float s = part[m * D + c];
-    for (int k = 1; k < ks; ++k) s += part[((int64_t)k * M + m) * D + c];
+  const int64_t n4 = M * ncols / 4;  // 4 consecutive columns per thread (ncols % 64 == 0)
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = 4 * i / ncols;
+    const int c = (int)(4 * i - m * ncols);
+    const float4 s = splitk_sum4(part, ks, M * (int64_t)D, m * D + c);
     const int64_t col = omap ? (int64_t)omap[c / kBlock] * kBlock + c % kBlock : c;
-    if (col < 0 || col >= ldy) continue;  // a block map entry outside Y (reported by the contraction)
-    if (out_f32) reinterpret_cast<float*>(out)[m * ldy + col] = s;
-    else reinterpret_cast<__nv_bfloat16*>(out)[m * ldy + col] = __float2bfloat16_rn(s);
+    if (col < 0 || col + 4 > ldy) continue;  // a block map entry outside Y (reported by the contraction)
+    store4(out, m * ldy + col, s, out_f32);
   }
 }
 
@@ -1497,7 +1598,19 @@ int launch_down(const DownArgs& a, cudaStream_t st) {
     if (max_pairs <= 0) return FP_ERR_CUDA;
     const int64_t ptiles = ((a.M + 2 * kTileM - 1) / (2 * kTileM)) * ((a.D + kTileN - 1) / kTileN);
     const int grid2 = 2 * (int)std::min<int64_t>(ptiles, std::min(max_pairs, a.num_sms / 2));
-    return launch_pdl(down2_kernel, dim3(grid2), dim3(kGemmThreads), kPairSmem, st, th, tv2, tvw, a) == cudaSuccess
+    // peer output of bf16 rows: the epilogue stores 32 x 64 tiles by TMA through one map per owning rank
+    PeerMaps pm;
+    std::memset(&pm, 0, sizeof(pm));
+    DownArgs b = a;
+    if (a.peer_rows > 0 && !a.y_f32 && a.peer_rows % 32 == 0 && a.peer_rows <= INT32_MAX) {
+      bool ok = true;
+      for (int o = 0; o < kMaxPeers && ok; ++o)
+        if (a.peer_y[o])
+          ok = encode_map_2d(&pm.m[o], a.peer_y[o], a.D, (uint64_t)a.peer_rows, (uint64_t)a.D * 2, 64, 32);
+      if (!ok) return FP_ERR_CUDA;
+      b.peer_tma = 1;
+    }
+    return launch_pdl(down2_kernel, dim3(grid2), dim3(kGemmThreads), kPairSmem, st, th, tv2, tvw, b, pm) == cudaSuccess
                ? FP_OK : FP_ERR_CUDA;
   }
   const int64_t tiles = ((a.M + kTileM - 1) / kTileM) * ((a.D + kTileN - 1) / kTileN) * ks;
@@ -1508,13 +1621,13 @@ int launch_down(const DownArgs& a, cudaStream_t st) {
     return FP_ERR_CUDA;
   if (ks > 1 && mapped) {
     const int64_t n = a.M * (int64_t)a.D;
-    const int rgrid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (int64_t)a.num_sms * 8));
+    const int rgrid = (int)std::max<int64_t>(1, std::min<int64_t>((n / 4 + 255) / 256, (int64_t)a.num_sms * 8));
     if (launch_pdl(splitk_reduce_mapped_kernel, dim3(rgrid), dim3(256), 0, st, (const float*)a.y_acc, ks, a.M, a.D,
                    a.ncnt, a.omap, a.y, a.ldy > 0 ? a.ldy : (int64_t)a.D, a.y_f32) != cudaSuccess)
       return FP_ERR_CUDA;
   } else if (ks > 1) {
     const int64_t n = a.M * (int64_t)a.D;
-    if (launch_pdl(splitk_reduce_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, (const float*)a.y_acc,
+    if (launch_pdl(splitk_reduce_kernel, dim3((unsigned)((n / 4 + 255) / 256)), dim3(256), 0, st, (const float*)a.y_acc,
                    ks, n, a.y, a.y_f32) != cudaSuccess)
       return FP_ERR_CUDA;
   }

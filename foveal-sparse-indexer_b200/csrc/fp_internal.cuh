@@ -222,6 +222,7 @@ struct DownArgs {
   // of peer_y[o] (row stride D, dtype per y_f32; peer pointers through CUDA IPC) instead of to y.
   void* peer_y[kMaxPeers] = {};
   int64_t peer_rows = 0;
+  int peer_tma = 0;  // set by launch_down: the pair kernel stores peer rows by TMA from shared memory
 };
 int launch_down(const DownArgs& a, cudaStream_t st);
 // Split-K factor used by the down projection for M tokens (1 = none).  Small batches (decode) have too

@@ -198,6 +198,12 @@ __device__ __forceinline__ void bulk_store(void* gdst, uint32_t smem_src, uint32
   asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_src), "r"(bytes)
                : "memory");
 }
+// Tiled tensor store shared -> global (the map's box, from a 1024-byte aligned, map-swizzled smem tile),
+// completion tracked with bulk groups like bulk_store.
+__device__ __forceinline__ void tma_store_2d(const void* map, uint32_t smem_src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(map), "r"(smem_src), "r"(c0), "r"(c1) : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 // Wait until at most N bulk groups of this thread still read their shared-memory source.

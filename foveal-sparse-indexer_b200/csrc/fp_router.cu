@@ -852,7 +852,6 @@ template <typename T, int E>
 __global__ void __launch_bounds__(kRouteWarps * 32, E <= 8 ? 3 : 1)
 route_kernel(const RouteArgs a) {
   constexpr int TPW = kRouteTPW, N = 32 * E;
-  griddep_wait();  // the projection kernel's queries are complete and visible
   griddep_launch_dependents();
   extern __shared__ float4 route_smem4[];
   char* smb = reinterpret_cast<char*>(route_smem4);
@@ -880,6 +879,10 @@ route_kernel(const RouteArgs a) {
   }
   if (csr)
     for (int i = threadIdx.x; i < a.nbl; i += blockDim.x) s_cnt[i] = 0;
+  // everything above reads only the block keys and this CTA's shared memory, so it overlaps the
+  // projection kernel; the queries, the cleared counters and the previous call's readers of H are ordered
+  // by this wait
+  griddep_wait();  // the projection kernel's queries are complete and visible
   __syncthreads();
 
   for (int64_t grp = blockIdx.x; grp < ngroups; grp += gridDim.x) {

@@ -348,6 +348,50 @@ def test_decode_sizes_split_and_shards(M):
     device_error_is_clear()
 
 
+@pytest.mark.parametrize("M", [2048, 1000])
+def test_peer_output_single_rank(M):
+    """The peer-memory reduce-scatter's kernels on one GPU (a job of one rank): the contraction stores its
+    rows into the rank's own receive slot (2048 rows: TMA tile stores from the pair kernel's epilogue; 1000
+    rows, not a multiple of 32: plain stores), the flag kernel raises the rank's flag and the combine
+    waits for it and copies the slot out.  Equal bit for bit to the routed forward writing y directly, over
+    two calls (both receive parities).  Decode-size batches decline (split contraction)."""
+    wl = configs.CONFIGS["8b"]
+    w = configs.make_weights(wl)
+    x2d = configs.make_x(wl).reshape(-1, wl.hidden_dim)[:M].contiguous().to(DEV, torch.bfloat16)
+    m = module_for(wl, w)
+    kg, ku, v, packed, wq, k16, wout = m._weights()
+    kw = dict(base_blocks=wl.base_blocks, top_p=wl.top_p, min_remote=wl.min_remote_blocks,
+              max_remote=wl.max_remote_blocks)
+    ridx, cnt, ctx = fsi.kernels.route_tokens(x2d, wq, k16, **kw)
+    ref = fsi.kernels.routed_forward(x2d, kg, ku, v, packed, wout, ridx, cnt, ctx, base_blocks=wl.base_blocks)
+    D = wl.hidden_dim
+    slot = M * D * 2
+    base, _ = fsi.kernels.peer_alloc(fsi.kernels.PEER_FLAG_BYTES + 2 * slot)
+    err_ws = torch.zeros(256, dtype=torch.uint8, device=DEV)
+    try:
+        for epoch in (1, 2):
+            recv = base + fsi.kernels.PEER_FLAG_BYTES + (epoch & 1) * slot
+            ok = fsi.kernels.routed_peer_forward(x2d, kg, ku, v, packed, wout, ridx, cnt, ctx,
+                                                 base_blocks=wl.base_blocks, block_stride=1, block_offset=0,
+                                                 peer_out=[recv], peer_flags=[base], rows_per_rank=M, epoch=epoch)
+            assert ok
+            y = fsi.kernels.peer_combine(recv, base, 1, M, D, in_f32=False, epoch=epoch, out_dtype=torch.bfloat16,
+                                         err_ws=err_ws)
+            torch.cuda.synchronize()
+            assert torch.equal(y, ref), epoch
+            assert fsi._lib.device_error(err_ws) == 0
+        xs = x2d[:64].contiguous()
+        r2, c2, x2 = fsi.kernels.route_tokens(xs, wq, k16, **kw)
+        assert not fsi.kernels.routed_peer_forward(xs, kg, ku, v, packed, wout, r2, c2, x2,
+                                                   base_blocks=wl.base_blocks, block_stride=1, block_offset=0,
+                                                   peer_out=[base + fsi.kernels.PEER_FLAG_BYTES], peer_flags=[base],
+                                                   rows_per_rank=64, epoch=3)
+    finally:
+        torch.cuda.synchronize()
+        fsi.kernels.peer_free(base)
+    device_error_is_clear()
+
+
 def test_split_routing_entry_points():
     """The token-routed forward split in two (fp_route_tokens, then fp_pattention_routed_fwd from the given
     routes): the routes equal the fused forward's, four stride-4 shards from the given routes (additive

@@ -211,6 +211,32 @@ def test_blocked_weight_matches_row_major(M, D_in, out_features, nact):
     assert rel_err(y1.float(), ref) < 2e-2
 
 
+def test_module_blocked_weight_copy():
+    """BlockSparseLinear.use_blocked_weight: eval-mode outputs equal the row-major weight's bit for bit, and
+    the copy follows an in-place weight update."""
+    x, W, b, wq, wk, wv, wo = _bsl_case(64, 1024, 4096, 2, 8, 0.8, True, "bf16", 64)
+    m = fsi.BlockSparseLinear(1024, 4096, base_blocks=2, top_p=0.8, max_remote_blocks=8, remote_capacity=8, bias=True)
+    sd = {"weight": W, "bias": b, "indexer.q_proj.weight": wq, "indexer.k_proj.weight": torch.zeros(16, 1024),
+          "indexer.v_proj.weight": torch.zeros(16, 1024), "indexer.out_proj.weight": wo,
+          "weight_to_k.weight": wk, "weight_to_v.weight": wv}
+    m.load_state_dict(sd)
+    m = m.to(DEV, torch.bfloat16).eval()
+    xd = x.to(DEV, torch.bfloat16)
+    with torch.no_grad():
+        y0, _ = m(xd)
+        m.use_blocked_weight(True)
+        y1, _ = m(xd)
+        assert m._blocked is not None
+        assert torch.equal(y0, y1)
+        m.weight.mul_(0.5)  # in-place update (version counter): the copy is rebuilt on the next call
+        m.refresh_block_cache()
+        y3, _ = m(xd)
+        m.use_blocked_weight(False)
+        y2, _ = m(xd)
+    torch.cuda.synchronize()
+    assert torch.equal(y2, y3) and not torch.equal(y1, y3)
+
+
 @pytest.mark.parametrize("M,D_in,D_out,Np,kmax,activation", [
     (300, 512, 768, 4096, 8, "softmax"),
     (129, 256, 256, 2048, 16, "gelu_l2"),
