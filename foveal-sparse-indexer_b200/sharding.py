@@ -68,10 +68,30 @@ class PeerReduce:
         esize = torch.empty((), dtype=dtype).element_size()
         self.slot = rows * D * esize
         nbytes = kernels.PEER_FLAG_BYTES + 2 * world * self.slot
+        self.addr = None
         self.base, handle = kernels.peer_alloc(nbytes)
         handles = [None] * world
         dist.all_gather_object(handles, handle, group=group)
-        self.addr = [self.base if w == rank else kernels.peer_open(handles[w]) for w in range(world)]
+        addr, ok = [], True
+        for w in range(world):
+            if w == rank:
+                addr.append(self.base)
+                continue
+            try:
+                addr.append(kernels.peer_open(handles[w]))
+            except RuntimeError:
+                ok = False
+                break
+        # every rank learns whether every mapping succeeded, so that all of them use the peer path or none
+        flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+        if int(flag.item()) == 0:
+            for w, a in enumerate(addr):
+                if w != rank:
+                    kernels.peer_close(a)
+            kernels.peer_free(self.base)
+            raise RuntimeError("peer-memory reduce-scatter: a rank could not map another rank's buffer")
+        self.addr = addr
         self.epoch = 0
         self.err = torch.zeros(256, dtype=torch.uint8, device=device)
 
@@ -112,12 +132,18 @@ def release_peer_buffers(module) -> None:
         module._peer_state = None
 
 
-def _peer_state(module, rows: int, D: int, dtype: torch.dtype, device) -> PeerReduce:
+def _peer_state(module, rows: int, D: int, dtype: torch.dtype, device) -> Optional[PeerReduce]:
+    """The module's receive buffers for ``rows`` rows per rank (collective when they are (re)built); None,
+    with peer_reduce switched off on every rank, when the buffers cannot be mapped."""
     rank, world, group = module._shard
     pr = getattr(module, "_peer_state", None)
     if pr is None or not pr.fits(rows, D, dtype):
         release_peer_buffers(module)
-        pr = PeerReduce(group, rank, world, rows, D, dtype, device)
+        try:
+            pr = PeerReduce(group, rank, world, rows, D, dtype, device)
+        except RuntimeError:
+            module._peer_reduce = False
+            return None
         module._peer_state = pr
     return pr
 
@@ -132,6 +158,8 @@ def _peer_routed_scatter(module, x2d, xv_mine, world: int, rank: int, group, rou
     s = M // world
     ridx, cnt, ctx = _gather_routes(module, xv_mine, group, world, rank, route_fn)
     pr = _peer_state(module, s, D, pd, x2d.device)
+    if pr is None:
+        return None, (ridx, cnt, ctx)
     epoch = pr.epoch + 1
     kg, ku, v, packed, _, _, wout = module._weights()
     ok = kernels.routed_peer_forward(x2d, kg, ku, v, packed, wout, ridx, cnt, ctx, base_blocks=module.base_blocks,
@@ -410,9 +438,18 @@ def sharded_forward_host(module, x_host: torch.Tensor, out: Optional[torch.Tenso
     for st_ in st:
         st_.wait_stream(cur)
     pd = _partial_dtype(module)
-    x_dev = torch.empty(s_all, D, dtype=x_host.dtype, device=dev)
-    y_dev = torch.empty(s_all, D, dtype=pd, device=dev)
-    gathered = [torch.empty(world * s, D, dtype=x_host.dtype, device=dev) for _ in range(chunks)]
+    # device buffers are kept across calls (per shape): every stream above waited for the caller's stream,
+    # which waited for the previous call's last copy-out, so the previous call is done with them; fresh
+    # allocations per call left the caching allocator with blocks held by the side streams (record_stream)
+    # and measured calls that stalled in new device allocations
+    key = (s_all, D, chunks, x_host.dtype, pd, world)
+    bufs = getattr(module, "_shard_host_bufs", None)
+    if bufs is None or bufs[0] != key or bufs[1].device != dev:
+        bufs = (key, torch.empty(s_all, D, dtype=x_host.dtype, device=dev),
+                torch.empty(s_all, D, dtype=pd, device=dev),
+                [torch.empty(world * s, D, dtype=x_host.dtype, device=dev) for _ in range(chunks)])
+        module._shard_host_bufs = bufs
+    _, x_dev, y_dev, gathered = bufs
     copied = []
     with torch.cuda.stream(s_in):  # every chunk's copy-in is queued at once; each signals its own event
         for i in range(chunks):
@@ -442,9 +479,6 @@ def sharded_forward_host(module, x_host: torch.Tensor, out: Optional[torch.Tenso
         if i + 2 < chunks:
             ag.append(gather(i + 2))
     cur.wait_stream(s_out)
-    for t in (x_dev, y_dev, *gathered):
-        for st_ in st:
-            t.record_stream(st_)
     return out
 
 
