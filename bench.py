@@ -74,9 +74,10 @@ def parse():
     ap.add_argument("--shard-chunks", type=int, default=1,
                     help="N > 1: token chunks of the device-resident block-sharded step (1: the routes are "
                          "split over the ranks and the whole batch runs as one piece; measured fastest)")
-    ap.add_argument("--reduce", choices=["nccl", "peer"], default="nccl",
-                    help="N > 1: sum of the block shards' partials by the NCCL reduce-scatter, or through peer "
-                         "memory (the down projection stores each row's partial on the rank that owns it)")
+    ap.add_argument("--reduce", choices=["nccl", "peer"], default="peer",
+                    help="N > 1: sum of the block shards' partials through peer memory (the down projection "
+                         "stores each row's partial on the rank that owns it; measured faster at 2 and 8 GPUs), "
+                         "or by the NCCL reduce-scatter")
     ap.add_argument("--e2e-chunks", type=int, default=4,
                     help="N > 1: token chunks of the host-buffer block-sharded step (copies overlap compute)")
     ap.add_argument("--partial-dtype", choices=["bf16", "fp32"], default="bf16",
@@ -627,7 +628,7 @@ def run_ours_sharded(args, rank, world, local, dev):
             stage["peer"] = peer_stage_times(m, x, world, rank)
         err = fsi._lib.device_error(fsi._lib.workspace(dev, 0))
         if peer_state is not None:
-            err = err or fsi._lib.device_error(peer_state.err)
+            err = err or fsi._lib.device_error(peer_state.err) or fsi._lib.device_error(peer_state.err_wait)
         fsi.sharding.release_peer_buffers(m)
         m._peer_reduce = False  # the host-buffer path below reduces with NCCL
         e2e = measure_e2e_sharded(args, m, x_cpu, rank, world, dev)
@@ -679,33 +680,41 @@ def run_ours_sharded(args, rank, world, local, dev):
 
 def peer_stage_times(m, x, world, rank, K=10):
     """Where the peer-memory step's time goes on this rank (CUDA events, mean of K calls): routing of this
-    rank's rows + the route all-gather; the contraction whose epilogue stores each row on its owner
-    (+ the flag kernel); the combine (including its wait for the other ranks' flags)."""
+    rank's rows and their exchange through the peer route tables (put, flag, wait for every rank); the
+    contraction whose epilogue stores each row on its owner (+ the flag kernel); the combine (including its
+    wait for the other ranks' flags)."""
     sh = fsi.sharding
     M, D = x.shape
     s = M // world
     xv = x.view(world, s, D)
     pd = sh._partial_dtype(m)
     kg, ku, v, packed, _, _, wout = m._weights()
+    cap = max(int(m.max_remote_blocks), 1)
+    pr = sh._peer_state(m, s, D, pd, cap, x.device)
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
     for k in range(K):
         ev[k][0].record()
-        ridx, cnt, ctx = sh._gather_routes(m, xv[rank], None, world, rank, sh._cuda_route)
-        ev[k][1].record()
-        pr = sh._peer_state(m, s, D, pd, x.device)
+        ridx, cnt, ctx = sh._cuda_route(m, xv[rank])
         e = pr.epoch + 1
-        fsi.kernels.routed_peer_forward(x, kg, ku, v, packed, wout, ridx, cnt, ctx, base_blocks=m.base_blocks,
-                                        block_stride=world, block_offset=rank, peer_out=pr.slots(e & 1),
-                                        peer_flags=pr.flags(), rows_per_rank=s, epoch=e,
-                                        out_f32=pd == torch.float32)
+        par = e & 1
+        fsi.kernels.peer_put(ridx.to(torch.int32), [pr.route_ids(par, a) + rank * s * cap * 4 for a in pr.addr])
+        fsi.kernels.peer_put(cnt.to(torch.int32), [pr.route_counts(par, a) + rank * s * 4 for a in pr.addr])
+        fsi.kernels.peer_signal(pr.route_flags(), e, x.device)
+        pr.ctx_full[rank * s:(rank + 1) * s].copy_(ctx)
+        fsi.kernels.peer_wait(pr.base + sh.PeerReduce.ROUTE_FLAGS, world, e, pr.err_wait)
+        ev[k][1].record()
+        fsi.kernels.routed_peer_forward(x, kg, ku, v, packed, wout, pr.route_ids(par), pr.route_counts(par),
+                                        pr.ctx_full, base_blocks=m.base_blocks, block_stride=world,
+                                        block_offset=rank, peer_out=pr.slots(par), peer_flags=pr.flags(),
+                                        rows_per_rank=s, epoch=e, out_f32=pd == torch.float32, capacity=cap)
         pr.epoch = e
         ev[k][2].record()
-        fsi.kernels.peer_combine(pr.recv(e & 1), pr.base, world, s, D, in_f32=pd == torch.float32, epoch=e,
+        fsi.kernels.peer_combine(pr.recv(par), pr.base, world, s, D, in_f32=pd == torch.float32, epoch=e,
                                  out_dtype=pd, err_ws=pr.err)
         ev[k][3].record()
     torch.cuda.synchronize()
     mean = lambda i: statistics.mean(ev[k][i].elapsed_time(ev[k][i + 1]) for k in range(K))  # noqa: E731
-    return {"route_and_allgather": mean(0), "contraction_with_peer_stores": mean(1), "combine_incl_wait": mean(2)}
+    return {"route_and_exchange": mean(0), "contraction_with_peer_stores": mean(1), "combine_incl_wait": mean(2)}
 
 
 def measure_e2e_sharded(args, m, x_cpu, rank, world, dev):

@@ -67,6 +67,10 @@ SIGNATURES = {
                                                _c_int, _c_i64, ctypes.c_uint32, _c_int, _c_p, _c_sz, _c_p]),
     "fp_peer_combine": (_c_int, [_c_p, _c_p, _c_int, _c_i64, _c_int, _c_int, ctypes.c_uint32, _c_p, _c_int, _c_p,
                                  _c_sz, _c_p]),
+    "fp_peer_reduce_supported": (_c_int, [_c_int, _c_i64, _c_int, _c_int, _c_int, _c_int]),
+    "fp_peer_put": (_c_int, [_c_p, _c_sz, _c_p, _c_int, _c_p]),
+    "fp_peer_signal": (_c_int, [_c_p, _c_int, ctypes.c_uint32, _c_p]),
+    "fp_peer_wait": (_c_int, [_c_p, _c_int, ctypes.c_uint32, _c_p, _c_sz, _c_p]),
     "fp_tokenformer_workspace_size": (_c_sz, [_c_int, _c_i64, _c_int]),
     "fp_tokenformer_fwd": (_c_int, [_c_p, _c_i64, _c_int, _c_p, _c_p, _c_p, _c_int, _c_int, _c_int, _c_int, _c_p,
                                     _c_p, _c_p, _c_p, _c_p, _c_p, _c_sz, _c_p]),

@@ -332,7 +332,8 @@ int fp_pattention_token_fwd(const void* x, int64_t M, int D, int NB, int dtype, 
   if (M <= 64 && block_stride == 1) {
     // HBM is idle while the routing kernels run, and the gate/up CTAs start (programmatic launch) on the
     // SMs the routing leaves free: each pulls a share of the packed gate/up tiles of the lowest block ids
-    // (the first work units take the touched blocks in ascending order) into L2, about half of L2 at most
+    // (the first work units take the touched blocks in ascending order) into L2, about half of L2 (96 MB
+    // measured slower)
     const int64_t tile_bytes = (int64_t)kTileM * kTileK * 2;  // 16 KB: one block at one k-block
     const int nkb = D / kTileK;
     const int64_t budget = 64ll << 20;
@@ -507,6 +508,12 @@ int fp_pattention_routed_fwd(const void* x, int64_t M, int D, int NB, int dtype,
   return routed_fwd_impl(x, M, D, NB, dtype, k_gate, k_up, v, w_gu, v_t, out_proj, base_blocks, capacity,
                          remote_indices, remote_counts, ctx16, block_stride, block_offset, y, y_f32, workspace,
                          workspace_bytes, stream, nullptr);
+}
+
+int fp_peer_reduce_supported(int dtype, int64_t M, int D, int NB, int capacity, int block_stride) {
+  if (check_common(dtype, M, D, NB) != FP_OK || M <= 0 || block_stride < 1) return 0;
+  const TokenLayout L = token_layout(dtype, M, D, NB, 0, std::max(capacity, 0), block_stride, 0);
+  return tensor_path(dtype, D) && L.nbl > 0 && L.ksplit <= 1 ? 1 : 0;
 }
 
 int fp_pattention_routed_peer_fwd(const void* x, int64_t M, int D, int NB, int dtype, const void* k_gate,

@@ -458,7 +458,7 @@ gateup_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ 
 // gu_ks work units are summed in split order into shared memory (coalesced loads, all splits in flight),
 // then each thread computes h for one (token, channel) and the CTA stores whole 128-byte rows of H.
 // Packed row of gate channel c: 32 (c / 16) + c % 16; of up channel c: that + 16.
-constexpr int kGuCombineThreads = 256;
+constexpr int kGuCombineThreads = 1024;  // a base block's tile (64 tokens) is 2048 float4 of partials per split
 __global__ void __launch_bounds__(kGuCombineThreads) gateup_split_combine_kernel(const GateUpArgs a) {
   constexpr int kN = 64;
   __shared__ float s_acc[kTileM][kN + 1];
@@ -599,7 +599,10 @@ __device__ __forceinline__ void down_tile(int tile, int m_tiles, int n_tiles, in
 __device__ __forceinline__ void down_add_chunk(const DownArgs& a, float (&o)[32], const float (&ctx)[16], int ocol0,
                                                bool add) {
   const int lane = threadIdx.x & 31;
-  if (a.ctx16 && add) {
+  bool ctx_nz = false;  // rows without a context (another rank's tokens in a block shard) add nothing
+#pragma unroll
+  for (int k = 0; k < 16; ++k) ctx_nz |= ctx[k] != 0.f;
+  if (a.ctx16 && add && __any_sync(0xffffffffu, ctx_nz)) {
     // o[i] += sum_k ctx[k] * W_out[ocol0 + i][k]; lane L loads row ocol0 + L of W_out and the warp
     // broadcasts it (all lanes of a chunk share the same 32 columns)
     float wv[16];
@@ -690,12 +693,21 @@ __device__ __forceinline__ void down_store_chunk(const DownArgs& a, float (&o)[3
 // four 64-row boxes from rows nmap[j]*64 (one box per column block j), tiles past the device count of
 // column blocks are skipped by every role, and the k-loop runs over the device count of k-blocks (none:
 // the tile's accumulator is taken as zero).
+constexpr int kSmallDownStages = 0;  // 5: the small-batch variant below; 0: off
+
+// S stages of AB bytes of H + 32 KB of V_t.  AB = 8 KB (batches of at most 64 tokens): the H box holds
+// only the 64 rows that exist; the MMA still reads 128 rows, the upper 64 from the start of the stage's V_t
+// tile, and the accumulator rows they produce (tokens >= M) are never stored.  The 8 KB saved per stage
+// buy a fifth stage of V_t in flight.
+template <int S, uint32_t AB>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CUtensorMap tm_vt,
             const __grid_constant__ CUtensorMap tm_vt_wide, const DownArgs a) {
+  constexpr uint32_t kSB = AB + kBBytes;  // stage bytes
+  using Bars = PipeBarsT<S>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = aligned_smem(smem_raw);
-  PipeBars* bars = reinterpret_cast<PipeBars*>(smem + kStages * kStageBytes);
+  Bars* bars = reinterpret_cast<Bars*>(smem + S * kSB);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tm_h);
@@ -746,13 +758,13 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
         for (int kb = kb0; kb < kb1; kb += ks, ++it) {
           const int kh = kg_next.x, gb = kg_next.y;
           if (kb + ks < kb1) kg_next = kmap(kb + ks);
-          const int s = it % kStages;
-          const uint32_t ph = (it / kStages) & 1u;
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1u;
           if (!mbar_wait(&bars->empty[s], ph ^ 1u, a.err, kErrWaitEmpty)) { ok = false; break; }
-          uint8_t* As = smem + s * kStageBytes;
-          uint8_t* Bs = As + kABytes;
+          uint8_t* As = smem + s * kSB;
+          uint8_t* Bs = As + AB;
           if (a.nmap) {
-            mbar_arrive_expect_tx(&bars->full[s], kABytes + (uint32_t)nv * (kBlock * kTileK * 2));
+            mbar_arrive_expect_tx(&bars->full[s], AB + (uint32_t)nv * (kBlock * kTileK * 2));
             tma_load_2d(As, &tm_h, &bars->full[s], kh * kTileK, m * kTileM);
             if (wide4) {
               tma_load_2d(Bs, &tm_vt_wide, &bars->full[s], 0, (gb * nbo + nb[0]) * kBlock);
@@ -767,7 +779,7 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
                 }
             }
           } else {
-            mbar_arrive_expect_tx(&bars->full[s], kStageBytes);
+            mbar_arrive_expect_tx(&bars->full[s], kSB);
             tma_load_2d(As, &tm_h, &bars->full[s], kh * kTileK, m * kTileM);
             if (a.vt_tiled)  // tile (n, gb) of the tile-contiguous V^T
               tma_load_2d(Bs, &tm_vt, &bars->full[s], 0, (n * (a.Np / kBlock) + gb) * kTileN);
@@ -797,12 +809,12 @@ down_kernel(const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CU
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kTileN;
         for (int kb = kb0; kb < kb1; kb += ks) {
-          const int s = it % kStages;
-          const uint32_t ph = (it / kStages) & 1u;
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1u;
           if (!mbar_wait(&bars->full[s], ph, a.err, kErrWaitFull)) { ok = false; break; }
           tc_fence_after();
-          const uint64_t ad = umma_desc_sw128(smem_u32(smem + s * kStageBytes));
-          const uint64_t bd = umma_desc_sw128(smem_u32(smem + s * kStageBytes + kABytes));
+          const uint64_t ad = umma_desc_sw128(smem_u32(smem + s * kSB));
+          const uint64_t bd = umma_desc_sw128(smem_u32(smem + s * kSB + AB));
 #pragma unroll
           for (int k = 0; k < kTileK / 16; ++k)
             umma_bf16(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
@@ -1550,10 +1562,6 @@ int launch_down(const DownArgs& a, cudaStream_t st) {
     return FP_ERR_CUDA;
   tv4 = tv;
   if (a.vt_blocked && !encode_map_2d(&tv4, a.v_t, kTileK, blk_rows, kTileK * 2, kTileK, kTileN)) return FP_ERR_CUDA;
-  static std::once_flag once;
-  static int attr = FP_OK;
-  std::call_once(once, [] { attr = set_smem((const void*)down_kernel); });
-  if (attr != FP_OK) return attr;
   if (ks == 1 && a.M >= 2 * kTileM && a.num_sms >= 2) {
     // CTA pairs: 256 x 256 tiles, each CTA loading 128 rows of H and half of the V_t tile (two 64-row
     // boxes in the block-mapped form)
@@ -1617,8 +1625,33 @@ int launch_down(const DownArgs& a, cudaStream_t st) {
   const int grid = (int)std::min<int64_t>(tiles, a.num_sms);
   if (grid <= 0) return FP_OK;
   if (ks > 1 && !a.y_acc) return FP_ERR_INVALID_ARG;
-  if (launch_pdl(down_kernel, dim3(grid), dim3(kGemmThreads), kGemmSmem, st, th, tv, tv4, a) != cudaSuccess)
-    return FP_ERR_CUDA;
+  if (kSmallDownStages > 0 && a.M <= kTileM / 2) {
+    // at most 64 rows of H: 8 KB H boxes and five stages (measured 2 us slower than four 16 KB + 32 KB
+    // stages at the decode shape, so not taken)
+    constexpr int kS = 5;
+    constexpr uint32_t kAB = kTileK * (kTileM / 2) * 2;
+    constexpr size_t kSmem = 1024 + kS * (kAB + kBBytes) + sizeof(PipeBarsT<kS>) + 64;
+    static_assert(kSmem <= 227 * 1024, "small down shared memory");
+    static std::once_flag once_s;
+    static int attr_s = FP_OK;
+    std::call_once(once_s, [] {
+      attr_s = cudaFuncSetAttribute((const void*)down_kernel<kS, kAB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)kSmem) == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+    });
+    if (attr_s != FP_OK) return attr_s;
+    CUtensorMap th64;
+    if (!encode_map_2d(&th64, a.h, a.K, a.M, (uint64_t)a.K * 2, kTileK, kTileM / 2)) return FP_ERR_CUDA;
+    if (launch_pdl(down_kernel<kS, kAB>, dim3(grid), dim3(kGemmThreads), kSmem, st, th64, tv, tv4, a) != cudaSuccess)
+      return FP_ERR_CUDA;
+  } else {
+    static std::once_flag once;
+    static int attr = FP_OK;
+    std::call_once(once, [] { attr = set_smem((const void*)down_kernel<kStages, kABytes>); });
+    if (attr != FP_OK) return attr;
+    if (launch_pdl(down_kernel<kStages, kABytes>, dim3(grid), dim3(kGemmThreads), kGemmSmem, st, th, tv, tv4, a) !=
+        cudaSuccess)
+      return FP_ERR_CUDA;
+  }
   if (ks > 1 && mapped) {
     const int64_t n = a.M * (int64_t)a.D;
     const int rgrid = (int)std::max<int64_t>(1, std::min<int64_t>((n / 4 + 255) / 256, (int64_t)a.num_sms * 8));

@@ -103,6 +103,34 @@ __global__ void __launch_bounds__(256) peer_combine_kernel(const void* __restric
   }
 }
 
+// The same `bytes` (a multiple of 16) from src to every destination (one 16-byte word per thread and
+// destination per step): a rank's rows of a table every rank holds, written straight into the others'
+// copies over NVLink.
+__global__ void __launch_bounds__(256) peer_put_kernel(const uint4* __restrict__ src, int64_t words, PeerFlags dst) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < words; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 v = __ldg(src + i);
+    for (int w = 0; w < dst.world; ++w) reinterpret_cast<uint4*>(dst.flag[w])[i] = v;
+  }
+}
+
+// One thread waits (bounded) until every flag reached `epoch`; later work of the stream is ordered after it.
+__global__ void peer_wait_kernel(const uint32_t* __restrict__ flags, int world, uint32_t epoch, int* err) {
+  if (threadIdx.x != 0) return;
+  for (int w = 0; w < world; ++w) {
+    if ((int32_t)(ld_acquire_sys(flags + w) - epoch) >= 0) continue;
+    const uint64_t t0 = global_timer_ns();
+    for (;;) {
+      if ((int32_t)(ld_acquire_sys(flags + w) - epoch) >= 0) break;
+      if (global_timer_ns() - t0 > FP_WAIT_LIMIT_NS) {
+        record_error(err, kErrPeerWait);
+        return;
+      }
+      __nanosleep(128);
+    }
+  }
+  __threadfence();
+}
+
 int launch_peer_signal(const PeerFlags& f, uint32_t epoch, cudaStream_t st) {
   if (f.world < 1 || f.world > kMaxPeers) return FP_ERR_INVALID_ARG;
   peer_signal_kernel<<<1, 32, 0, st>>>(f, epoch);
@@ -147,6 +175,43 @@ int fp_peer_close(void* ptr) {
 int fp_peer_free(void* ptr) {
   if (!ptr) return FP_ERR_INVALID_ARG;
   return cudaFree(ptr) == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+}
+
+int fp_peer_put(const void* src, size_t bytes, void* const* dst, int world, void* stream) {
+  if (!src || !dst || world < 1 || world > kMaxPeers || bytes % 16) return FP_ERR_INVALID_ARG;
+  PeerFlags d{};  // destinations (the flag slots hold the row pointers here)
+  for (int w = 0; w < world; ++w) {
+    if (!dst[w] || (reinterpret_cast<uintptr_t>(dst[w]) & 15u)) return FP_ERR_INVALID_ARG;
+    d.flag[w] = static_cast<uint32_t*>(dst[w]);
+  }
+  d.world = world;
+  if ((reinterpret_cast<uintptr_t>(src) & 15u)) return FP_ERR_INVALID_ARG;
+  const int64_t words = (int64_t)(bytes / 16);
+  if (words == 0) return FP_OK;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((words + 255) / 256, 148 * 2));
+  peer_put_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(static_cast<const uint4*>(src), words, d);
+  return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
+}
+
+int fp_peer_signal(uint32_t* const* flags, int world, uint32_t epoch, void* stream) {
+  if (!flags || world < 1 || world > kMaxPeers) return FP_ERR_INVALID_ARG;
+  PeerFlags f{};
+  for (int w = 0; w < world; ++w) {
+    if (!flags[w]) return FP_ERR_INVALID_ARG;
+    f.flag[w] = flags[w];
+  }
+  f.world = world;
+  return launch_peer_signal(f, epoch, (cudaStream_t)stream);
+}
+
+int fp_peer_wait(const uint32_t* flags, int world, uint32_t epoch, void* workspace, size_t workspace_bytes,
+                 void* stream) {
+  if (!flags || !workspace || world < 1 || world > kMaxPeers) return FP_ERR_INVALID_ARG;
+  if (workspace_bytes < 256) return FP_ERR_WORKSPACE;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (cudaMemsetAsync(workspace, 0, 256, st) != cudaSuccess) return FP_ERR_CUDA;
+  peer_wait_kernel<<<1, 32, 0, st>>>(flags, world, epoch, static_cast<int*>(workspace));
+  return cudaGetLastError() == cudaSuccess ? FP_OK : FP_ERR_CUDA;
 }
 
 int fp_peer_combine(const void* recv, const uint32_t* flags, int world, int64_t rows, int D, int in_f32,

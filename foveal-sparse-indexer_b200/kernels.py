@@ -312,12 +312,14 @@ def peer_free(addr: int) -> None:
 
 def routed_peer_forward(x2d, k_gate, k_up, v, packed, out_proj, remote_indices, remote_counts, ctx16, *,
                         base_blocks: int, block_stride: int, block_offset: int, peer_out, peer_flags,
-                        rows_per_rank: int, epoch: int, out_f32: bool = False) -> bool:
+                        rows_per_rank: int, epoch: int, out_f32: bool = False, capacity: int = 0) -> bool:
     """:func:`routed_forward` whose output rows go straight to the ranks that own them
     (``fp_pattention_routed_peer_fwd``): ``peer_out[o]`` / ``peer_flags[o]`` are device addresses (this
-    rank's receive slot and flag word on rank o).  Returns False, having launched nothing, for shapes
-    whose contraction is split (small batches): the caller uses the collective instead."""
-    dev = require_cuda(x2d, k_gate, k_up, v, remote_indices, remote_counts)
+    rank's receive slot and flag word on rank o).  ``remote_indices`` / ``remote_counts``: int32 tensors, or
+    device addresses of [M, capacity] / [M] int32 tables (the peer route exchange's buffers).  Returns
+    False, having launched nothing, for shapes whose contraction is split (small batches): the caller uses
+    the collective instead."""
+    dev = require_cuda(x2d, k_gate, k_up, v)
     dtt = x2d.dtype
     dt = dtype_code(dtt)
     x2d = contig(x2d)
@@ -326,17 +328,20 @@ def routed_peer_forward(x2d, k_gate, k_up, v, packed, out_proj, remote_indices, 
     world = len(peer_out)
     k_gate, k_up, v = contig(k_gate.detach()), contig(k_up.detach()), contig(v.detach())
     out_proj = contig(out_proj.detach().to(dtt)) if out_proj is not None else None
-    ridx = contig(remote_indices.to(torch.int32))
-    cnt = contig(remote_counts.to(torch.int32))
+    if isinstance(remote_indices, int):
+        ridx, cnt, cap = ctypes.c_void_p(remote_indices), ctypes.c_void_p(remote_counts), int(capacity)
+    else:
+        ridx_t = contig(remote_indices.to(torch.int32))
+        cnt_t = contig(remote_counts.to(torch.int32))
+        ridx, cnt, cap = ptr(ridx_t), ptr(cnt_t), ridx_t.shape[1]
     ctx16 = contig(ctx16.float()) if ctx16 is not None else None
-    cap = ridx.shape[1]
     w_gu, v_t = packed if packed is not None else (None, None)
     outs = (ctypes.c_void_p * world)(*peer_out)
     flags = (ctypes.c_void_p * world)(*peer_flags)
     lib = _lib.load()
     ws = _lib.workspace(dev, lib.fp_token_workspace_size(dt, M, D, NB, int(base_blocks), cap, int(block_stride)))
     rc = lib.fp_pattention_routed_peer_fwd(ptr(x2d), M, D, NB, dt, ptr(k_gate), ptr(k_up), ptr(v), ptr(w_gu),
-                                           ptr(v_t), ptr(out_proj), int(base_blocks), cap, ptr(ridx), ptr(cnt),
+                                           ptr(v_t), ptr(out_proj), int(base_blocks), cap, ridx, cnt,
                                            ptr(ctx16), int(block_stride), int(block_offset), outs, flags, world,
                                            int(rows_per_rank), int(epoch) & 0xFFFFFFFF, 1 if out_f32 else 0, ptr(ws),
                                            ws.numel(), stream_handle(dev))
@@ -344,6 +349,36 @@ def routed_peer_forward(x2d, k_gate, k_up, v, packed, out_proj, remote_indices, 
         return False
     check(rc, "fp_pattention_routed_peer_fwd")
     return True
+
+
+def peer_reduce_supported(dtype: torch.dtype, M: int, D: int, NB: int, capacity: int, block_stride: int) -> bool:
+    """Whether :func:`routed_peer_forward` takes this shape (``fp_peer_reduce_supported``)."""
+    return bool(_lib.load().fp_peer_reduce_supported(dtype_code(dtype), int(M), int(D), int(NB), int(capacity),
+                                                      int(block_stride)))
+
+
+def peer_put(src: torch.Tensor, dst) -> None:
+    """The bytes of ``src`` (contiguous, 16-byte multiple) to every device address of ``dst``
+    (``fp_peer_put``)."""
+    dev = require_cuda(src)
+    src = contig(src)
+    n = src.numel() * src.element_size()
+    arr = (ctypes.c_void_p * len(dst))(*dst)
+    check(_lib.load().fp_peer_put(ptr(src), n, arr, len(dst), stream_handle(dev)), "fp_peer_put")
+
+
+def peer_signal(flags, epoch: int, device) -> None:
+    """This rank's flag word on every rank (device addresses) := epoch (``fp_peer_signal``)."""
+    arr = (ctypes.c_void_p * len(flags))(*flags)
+    check(_lib.load().fp_peer_signal(arr, len(flags), int(epoch) & 0xFFFFFFFF, stream_handle(torch.device(device))),
+          "fp_peer_signal")
+
+
+def peer_wait(flags_addr: int, world: int, epoch: int, err_ws: torch.Tensor) -> None:
+    """Orders the stream's later work after every flag of the array at ``flags_addr`` reached ``epoch``
+    (``fp_peer_wait``; bounded, its error word in ``err_ws``)."""
+    check(_lib.load().fp_peer_wait(ctypes.c_void_p(flags_addr), int(world), int(epoch) & 0xFFFFFFFF, ptr(err_ws),
+                                   err_ws.numel(), stream_handle(err_ws.device)), "fp_peer_wait")
 
 
 def peer_combine(recv_addr: int, flags_addr: int, world: int, rows: int, D: int, *, in_f32: bool, epoch: int,

@@ -58,16 +58,25 @@ def shard_parameter_blocks(module, group=None, partial_dtype: Optional[torch.dty
 
 
 class PeerReduce:
-    """Receive buffers of the peer-memory reduce-scatter, one per rank, mapped into every rank of the group
-    through CUDA IPC.  Buffer of rank w: 256 bytes of flags (flag v = the last epoch whose partial rank v
-    finished storing here), then 2 parities x world slots x ``rows`` x D partials.  Call e stores parity
+    """Receive buffers of the peer-memory reduce-scatter and route exchange, one per rank, mapped into every
+    rank of the group through CUDA IPC.  Buffer of rank w: 256 bytes of flags (word v: the last epoch whose
+    partial rank v finished storing here; word 32 + v: the last epoch whose routes rank v stored here),
+    then 2 parities x world slots x ``rows`` x D partials, then 2 parities of the route table of all
+    world x ``rows`` tokens (ids [world*rows, cap] int32, counts [world*rows] int32).  Call e uses parity
     e % 2; each call's epoch is one more than the last, on every rank."""
 
-    def __init__(self, group, rank: int, world: int, rows: int, D: int, dtype: torch.dtype, device):
-        self.group, self.rank, self.world, self.rows, self.D, self.dtype = group, rank, world, rows, D, dtype
+    ROUTE_FLAGS = 128  # byte offset of the route flags
+
+    def __init__(self, group, rank: int, world: int, rows: int, D: int, dtype: torch.dtype, cap: int, device):
+        self.group, self.rank, self.world, self.rows, self.D, self.dtype, self.cap = (group, rank, world, rows, D,
+                                                                                     dtype, cap)
         esize = torch.empty((), dtype=dtype).element_size()
         self.slot = rows * D * esize
-        nbytes = kernels.PEER_FLAG_BYTES + 2 * world * self.slot
+        al = lambda n: (n + 255) // 256 * 256  # noqa: E731
+        self.ids_bytes = al(world * rows * cap * 4)
+        self.route_par = self.ids_bytes + al(world * rows * 4)
+        self.route_base = kernels.PEER_FLAG_BYTES + 2 * world * self.slot
+        nbytes = self.route_base + 2 * self.route_par
         self.addr = None
         self.base, handle = kernels.peer_alloc(nbytes)
         handles = [None] * world
@@ -94,21 +103,33 @@ class PeerReduce:
         self.addr = addr
         self.epoch = 0
         self.err = torch.zeros(256, dtype=torch.uint8, device=device)
+        self.err_wait = torch.zeros(256, dtype=torch.uint8, device=device)
+        # additive-stream contexts of all rows: this rank's rows written per call, the others stay zero
+        self.ctx_full = torch.zeros(world * rows, 16, dtype=torch.float32, device=device)
 
-    def fits(self, rows: int, D: int, dtype: torch.dtype) -> bool:
-        return rows <= self.rows and D == self.D and dtype == self.dtype
+    def fits(self, rows: int, D: int, dtype: torch.dtype, cap: int) -> bool:
+        return rows == self.rows and D == self.D and dtype == self.dtype and cap == self.cap
 
     def slots(self, parity: int):
         """This rank's receive slot on every rank (device addresses)."""
         return [a + kernels.PEER_FLAG_BYTES + (parity * self.world + self.rank) * self.slot for a in self.addr]
 
     def flags(self):
-        """This rank's flag word on every rank."""
+        """This rank's output flag word on every rank."""
         return [a + 4 * self.rank for a in self.addr]
+
+    def route_flags(self):
+        return [a + self.ROUTE_FLAGS + 4 * self.rank for a in self.addr]
 
     def recv(self, parity: int) -> int:
         """This rank's own slots of one parity."""
         return self.base + kernels.PEER_FLAG_BYTES + parity * self.world * self.slot
+
+    def route_ids(self, parity: int, addr: Optional[int] = None) -> int:
+        return (self.base if addr is None else addr) + self.route_base + parity * self.route_par
+
+    def route_counts(self, parity: int, addr: Optional[int] = None) -> int:
+        return self.route_ids(parity, addr) + self.ids_bytes
 
     def close(self) -> None:
         """Collective: every rank unmaps the others' buffers, then frees its own."""
@@ -132,15 +153,15 @@ def release_peer_buffers(module) -> None:
         module._peer_state = None
 
 
-def _peer_state(module, rows: int, D: int, dtype: torch.dtype, device) -> Optional[PeerReduce]:
+def _peer_state(module, rows: int, D: int, dtype: torch.dtype, cap: int, device) -> Optional[PeerReduce]:
     """The module's receive buffers for ``rows`` rows per rank (collective when they are (re)built); None,
     with peer_reduce switched off on every rank, when the buffers cannot be mapped."""
     rank, world, group = module._shard
     pr = getattr(module, "_peer_state", None)
-    if pr is None or not pr.fits(rows, D, dtype):
+    if pr is None or not pr.fits(rows, D, dtype, cap):
         release_peer_buffers(module)
         try:
-            pr = PeerReduce(group, rank, world, rows, D, dtype, device)
+            pr = PeerReduce(group, rank, world, rows, D, dtype, cap, device)
         except RuntimeError:
             module._peer_reduce = False
             return None
@@ -149,27 +170,34 @@ def _peer_state(module, rows: int, D: int, dtype: torch.dtype, device) -> Option
 
 
 def _peer_routed_scatter(module, x2d, xv_mine, world: int, rank: int, group, route_fn, pd):
-    """Unchunked split-routing forward whose reduce-scatter runs through peer memory: routes of this rank's
-    rows, all-gather of the routes, contraction storing every row's partial into the owning rank's
-    receive slot, then the sum of this rank's slots.  Returns None (nothing launched after the routes'
-    all-gather) when the shape takes a split contraction; the caller then reduces with the collective and
-    gets the routes back for that."""
+    """Unchunked split-routing forward through peer memory: routes of this rank's rows, stored into every
+    rank's route table (in place of an all-gather); the contraction of this rank's blocks from the full
+    table, storing every row's partial into the owning rank's receive slot; the sum of this rank's slots.
+    Returns (y, None), or (None, (ridx, cnt, ctx)) with the routes all-gathered by NCCL when the shape takes
+    a split contraction (decode-size batches) or the buffers cannot be mapped: the caller then reduces with
+    the collective (every rank takes the same branch: same shapes)."""
     M, D = x2d.shape
     s = M // world
-    ridx, cnt, ctx = _gather_routes(module, xv_mine, group, world, rank, route_fn)
-    pr = _peer_state(module, s, D, pd, x2d.device)
-    if pr is None:
-        return None, (ridx, cnt, ctx)
-    epoch = pr.epoch + 1
     kg, ku, v, packed, _, _, wout = module._weights()
-    ok = kernels.routed_peer_forward(x2d, kg, ku, v, packed, wout, ridx, cnt, ctx, base_blocks=module.base_blocks,
-                                     block_stride=world, block_offset=rank, peer_out=pr.slots(epoch & 1),
-                                     peer_flags=pr.flags(), rows_per_rank=s, epoch=epoch,
-                                     out_f32=pd == torch.float32)
-    if not ok:
-        return None, (ridx, cnt, ctx)
+    cap = max(int(module.max_remote_blocks), 1)
+    ok = (kernels.peer_reduce_supported(x2d.dtype, M, D, kg.shape[0] // 64, cap, world) and s % 4 == 0)
+    pr = _peer_state(module, s, D, pd, cap, x2d.device) if ok else None
+    if pr is None:
+        return None, _gather_routes(module, xv_mine, group, world, rank, route_fn)
+    ridx, cnt, ctx = route_fn(module, xv_mine)
+    epoch = pr.epoch + 1
+    par = epoch & 1
+    kernels.peer_put(ridx.to(torch.int32), [pr.route_ids(par, a) + rank * s * cap * 4 for a in pr.addr])
+    kernels.peer_put(cnt.to(torch.int32), [pr.route_counts(par, a) + rank * s * 4 for a in pr.addr])
+    kernels.peer_signal(pr.route_flags(), epoch, x2d.device)
+    pr.ctx_full[rank * s:(rank + 1) * s].copy_(ctx)
+    kernels.peer_wait(pr.base + PeerReduce.ROUTE_FLAGS, world, epoch, pr.err_wait)
+    kernels.routed_peer_forward(x2d, kg, ku, v, packed, wout, pr.route_ids(par), pr.route_counts(par), pr.ctx_full,
+                                base_blocks=module.base_blocks, block_stride=world, block_offset=rank,
+                                peer_out=pr.slots(par), peer_flags=pr.flags(), rows_per_rank=s, epoch=epoch,
+                                out_f32=pd == torch.float32, capacity=cap)
     pr.epoch = epoch
-    y = kernels.peer_combine(pr.recv(epoch & 1), pr.base, world, s, D, in_f32=pd == torch.float32, epoch=epoch,
+    y = kernels.peer_combine(pr.recv(par), pr.base, world, s, D, in_f32=pd == torch.float32, epoch=epoch,
                              out_dtype=pd, err_ws=pr.err)
     return y, None
 

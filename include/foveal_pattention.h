@@ -209,6 +209,9 @@ FP_API int fp_peer_alloc(size_t bytes, void** ptr, void* handle);
 FP_API int fp_peer_open(const void* handle, void** ptr);
 FP_API int fp_peer_close(void* ptr);
 FP_API int fp_peer_free(void* ptr);
+/* 1 when fp_pattention_routed_peer_fwd takes this shape (the tensor-core path with an unsplit
+ * contraction), else 0: callers pick the peer path or the collective before exchanging anything. */
+FP_API int fp_peer_reduce_supported(int dtype, int64_t M, int D, int NB, int capacity, int block_stride);
 FP_API int fp_pattention_routed_peer_fwd(const void* x, int64_t M, int D, int NB, int dtype, const void* k_gate,
                                          const void* k_up, const void* v, const void* w_gu, const void* v_t,
                                          const void* out_proj, int base_blocks, int capacity,
@@ -220,6 +223,18 @@ FP_API int fp_pattention_routed_peer_fwd(const void* x, int64_t M, int D, int NB
 FP_API int fp_peer_combine(const void* recv, const uint32_t* flags, int world, int64_t rows, int D, int in_f32,
                            uint32_t epoch, void* y, int y_f32, void* workspace, size_t workspace_bytes,
                            void* stream);
+/*
+ * Small tables every rank holds (the routes of the split routing): fp_peer_put writes the same `bytes`
+ * (a multiple of 16, 16-byte aligned) from src to dst[w] on every rank w; fp_peer_signal then raises this
+ * rank's flag on every rank (flags[w] = this rank's flag word on rank w, release at system scope, after
+ * every store of the stream so far); fp_peer_wait (bounded, like fp_peer_combine's wait; its error word in
+ * `workspace`) orders the stream's later work after every flags[w] >= epoch.  The route exchange of the
+ * block-sharded forward uses them in place of an all-gather.
+ */
+FP_API int fp_peer_put(const void* src, size_t bytes, void* const* dst, int world, void* stream);
+FP_API int fp_peer_signal(uint32_t* const* flags, int world, uint32_t epoch, void* stream);
+FP_API int fp_peer_wait(const uint32_t* flags, int world, uint32_t epoch, void* workspace, size_t workspace_bytes,
+                        void* stream);
 
 /*
  * Pooled forward over one shared active set.  Replaces the active-block execution of

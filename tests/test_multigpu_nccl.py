@@ -83,7 +83,7 @@ def _worker(rank, world, port, out_dir):
         mp_ = module()
         fsi.sharding.shard_parameter_blocks(mp_, peer_reduce=True)
         yp = [fsi.sharding.sharded_token_forward(mp_, x, reduce="scatter")[0] for _ in range(3)]
-        peer_err = fsi._lib.device_error(mp_._peer_state.err)
+        peer_err = fsi._lib.device_error(mp_._peer_state.err) or fsi._lib.device_error(mp_._peer_state.err_wait)
         peer_epoch = mp_._peer_state.epoch
         fsi.sharding.release_peer_buffers(mp_)
         mf = module()
@@ -118,3 +118,55 @@ def test_block_sharded_forward_over_nccl_matches_single_gpu():
             e_all, e_sc, same, peer_ok = open(os.path.join(d, f"r{r}.txt")).read().split()
             assert float(e_all) < 2e-2 and float(e_sc) < 2e-2 and same == "1", (r, e_all, e_sc, same)
             assert peer_ok == "1", r  # peer path: no wait ran out, three epochs, repeated calls bit-equal
+
+
+def _single_rank_worker(index, port, out_dir):
+    sys.path.insert(0, REPO)
+    sys.path.insert(0, HERE)
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    dist.init_process_group("nccl", rank=0, world_size=1, init_method=f"tcp://127.0.0.1:{port}",
+                            timeout=datetime.timedelta(seconds=120), device_id=dev)
+    from conftest import configs, fsi, rel_err
+    wl = configs.CONFIGS["8b"]
+    w = configs.make_weights(wl)
+    x = configs.make_x(wl).reshape(-1, wl.hidden_dim)[:1024].contiguous().to(dev, torch.bfloat16)
+    m = fsi.FovealPattentionMLP(hidden_dim=wl.hidden_dim, intermediate_dim=wl.intermediate_dim,
+                                base_blocks=wl.base_blocks, remote_blocks=wl.max_remote_blocks,
+                                dtype=torch.bfloat16, routing="token", top_p=wl.top_p,
+                                min_remote_blocks=wl.min_remote_blocks, max_remote_blocks=wl.max_remote_blocks)
+    m.load_state_dict({k: t.to(torch.bfloat16) for k, t in w.state_dict().items()}, strict=False)
+    m = m.to(dev).eval()
+    with torch.no_grad():
+        full = m(x)
+        fsi.sharding.shard_parameter_blocks(m, peer_reduce=True)
+        ys = [fsi.sharding.sharded_token_forward(m, x, reduce="scatter")[0] for _ in range(3)]
+        st = m._peer_state
+        ok = (st is not None and st.epoch == 3 and fsi._lib.device_error(st.err) == 0
+              and fsi._lib.device_error(st.err_wait) == 0)
+        fsi.sharding.release_peer_buffers(m)
+    torch.cuda.synchronize()
+    e = max(rel_err(y.float(), full.float()) for y in ys)
+    same = all(torch.equal(ys[0], y) for y in ys)
+    with open(os.path.join(out_dir, "r0.txt"), "w") as f:
+        f.write(f"{e} {int(same)} {int(ok)}")
+    dist.destroy_process_group()
+
+
+def test_peer_route_exchange_single_rank():
+    """The peer-memory path of the sharded forward as a job of one rank (one GPU): the routes go through the
+    peer route table (put, flag, wait), the contraction stores into the rank's own slot, the combine waits
+    for its own flag.  Three calls (both parities) equal the unsharded forward within the bf16 bar and
+    each other bit for bit; no bounded wait ran out."""
+    port = _free_port()
+    with tempfile.TemporaryDirectory() as d:
+        ctx = mp.spawn(_single_rank_worker, args=(port, d), nprocs=1, join=False)
+        deadline = time.time() + 300
+        while not ctx.join(timeout=5):
+            if time.time() > deadline:
+                for p in ctx.processes:
+                    if p.is_alive():
+                        p.kill()
+                pytest.fail("single-rank peer forward did not finish")
+        e, same, ok = open(os.path.join(d, "r0.txt")).read().split()
+        assert float(e) < 2e-2 and same == "1" and ok == "1", (e, same, ok)
