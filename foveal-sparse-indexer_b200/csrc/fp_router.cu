@@ -800,10 +800,12 @@ __device__ __forceinline__ void stage_keys(const T* __restrict__ k16, int NB, in
 // bf16 with D % 64 == 0: mma.sync over 64-element chunks of the hidden dimension, interleaved over the
 // warps, partials summed in warp order.  Otherwise fp32 FFMA, two tokens per warp: lanes split the
 // hidden dimension in 8-element vectors, then a butterfly sum.
-template <typename T, bool kMma>
-__global__ void __launch_bounds__(kRouteWarps * 32, 2)
+// kW warps per CTA (mma form): 8, or 32 for batches of at most 64 tokens, whose projection is a chain of
+// dependent loads per warp (D / 64 / kW chunks each) rather than a stream of x.
+template <typename T, bool kMma, int kW = kRouteWarps>
+__global__ void __launch_bounds__(kW * 32, kW == kRouteWarps ? 2 : 1)
 route_proj_kernel(const T* __restrict__ x, const T* __restrict__ wq, int64_t M, int D, float* __restrict__ qraw) {
-  constexpr int W = kRouteWarps, TPW = kProjTPW;
+  constexpr int W = kMma ? kW : kRouteWarps, TPW = kProjTPW;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   griddep_launch_dependents();  // the routing kernel may launch; it waits for this grid before reading qraw
   const int64_t tok0 = (int64_t)blockIdx.x * kProjTokens;
@@ -845,11 +847,13 @@ route_proj_kernel(const T* __restrict__ x, const T* __restrict__ wq, int64_t M, 
     q[(g + 8) * 17 + 8 + 2 * t] = c1[2];
     q[(g + 8) * 17 + 9 + 2 * t] = c1[3];
     __syncthreads();
-    const int r = warp * TPW + (lane >> 4), j = lane & 15;  // lane (tt, j) of token warp*TPW + tt
-    float v = part[r * 17 + j];
+    if (threadIdx.x < 256) {  // thread (r, j): projection j of token r, partials summed in warp order
+      const int r = threadIdx.x >> 4, j = threadIdx.x & 15;
+      float v = part[r * 17 + j];
 #pragma unroll
-    for (int w = 1; w < W; ++w) v += part[w * 16 * 17 + r * 17 + j];
-    if (tok0 + r < M) qraw[(tok0 + r) * 16 + j] = v;
+      for (int w = 1; w < W; ++w) v += part[w * 16 * 17 + r * 17 + j];
+      if (tok0 + r < M) qraw[(tok0 + r) * 16 + j] = v;
+    }
   } else {
     float acc[TPW][16];
 #pragma unroll
@@ -1251,9 +1255,14 @@ int route_go(const RouteArgs& a, bool mma, cudaStream_t st) {
   const int64_t groups = (a.M + kRouteTokens - 1) / kRouteTokens;
   if (a.given_idx) {
     // routes given: no projection; the routing kernel builds the block lists only
-  } else if (mma)
-    route_proj_kernel<__nv_bfloat16, true><<<(unsigned)pblocks, kRouteWarps * 32, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(a.x), static_cast<const __nv_bfloat16*>(a.wq), a.M, a.D, a.qraw);
+  } else if (mma) {
+    if (a.M <= 64)
+      route_proj_kernel<__nv_bfloat16, true, 32><<<(unsigned)pblocks, 32 * 32, 0, st>>>(
+          static_cast<const __nv_bfloat16*>(a.x), static_cast<const __nv_bfloat16*>(a.wq), a.M, a.D, a.qraw);
+    else
+      route_proj_kernel<__nv_bfloat16, true><<<(unsigned)pblocks, kRouteWarps * 32, 0, st>>>(
+          static_cast<const __nv_bfloat16*>(a.x), static_cast<const __nv_bfloat16*>(a.wq), a.M, a.D, a.qraw);
+  }
   else
     route_proj_kernel<T, false><<<(unsigned)pblocks, kRouteWarps * 32, 0, st>>>(
         static_cast<const T*>(a.x), static_cast<const T*>(a.wq), a.M, a.D, a.qraw);

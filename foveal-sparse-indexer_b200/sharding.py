@@ -184,18 +184,21 @@ def _peer_routed_scatter(module, x2d, xv_mine, world: int, rank: int, group, rou
     pr = _peer_state(module, s, D, pd, cap, x2d.device) if ok else None
     if pr is None:
         return None, _gather_routes(module, xv_mine, group, world, rank, route_fn)
-    ridx, cnt, ctx = route_fn(module, xv_mine)
     epoch = pr.epoch + 1
     par = epoch & 1
-    kernels.peer_put(ridx.to(torch.int32), [pr.route_ids(par, a) + rank * s * cap * 4 for a in pr.addr])
-    kernels.peer_put(cnt.to(torch.int32), [pr.route_counts(par, a) + rank * s * 4 for a in pr.addr])
-    kernels.peer_signal(pr.route_flags(), epoch, x2d.device)
-    pr.ctx_full[rank * s:(rank + 1) * s].copy_(ctx)
-    kernels.peer_wait(pr.base + PeerReduce.ROUTE_FLAGS, world, epoch, pr.err_wait)
-    kernels.routed_peer_forward(x2d, kg, ku, v, packed, wout, pr.route_ids(par), pr.route_counts(par), pr.ctx_full,
-                                base_blocks=module.base_blocks, block_stride=world, block_offset=rank,
-                                peer_out=pr.slots(par), peer_flags=pr.flags(), rows_per_rank=s, epoch=epoch,
-                                out_f32=pd == torch.float32, capacity=cap)
+    if getattr(module, "_peer_routes", True):
+        ridx, cnt, ctx = route_fn(module, xv_mine)
+        kernels.peer_put(ridx.to(torch.int32), [pr.route_ids(par, a) + rank * s * cap * 4 for a in pr.addr])
+        kernels.peer_put(cnt.to(torch.int32), [pr.route_counts(par, a) + rank * s * 4 for a in pr.addr])
+        kernels.peer_signal(pr.route_flags(), epoch, x2d.device)
+        pr.ctx_full[rank * s:(rank + 1) * s].copy_(ctx)
+        kernels.peer_wait(pr.base + PeerReduce.ROUTE_FLAGS, world, epoch, pr.err_wait)
+        routes = (pr.route_ids(par), pr.route_counts(par), pr.ctx_full)
+    else:  # routes all-gathered by NCCL (module._peer_routes = False)
+        routes = _gather_routes(module, xv_mine, group, world, rank, route_fn)
+    kernels.routed_peer_forward(x2d, kg, ku, v, packed, wout, *routes, base_blocks=module.base_blocks,
+                                block_stride=world, block_offset=rank, peer_out=pr.slots(par), peer_flags=pr.flags(),
+                                rows_per_rank=s, epoch=epoch, out_f32=pd == torch.float32, capacity=cap)
     pr.epoch = epoch
     y = kernels.peer_combine(pr.recv(par), pr.base, world, s, D, in_f32=pd == torch.float32, epoch=epoch,
                              out_dtype=pd, err_ws=pr.err)
