@@ -42,7 +42,10 @@ struct TokenLayout {
 
 constexpr size_t kTicketOffset = 128;  // CTA completion counter of the routing kernel, in the error area
 
-TokenLayout token_layout(int dtype, int64_t M, int D, int NB, int base, int kmax, int stride, int offset) {
+// split: allow the decode split of the gate/up contraction (its fp32 partials need
+// max_tiles * 4 * 32 KB); a workspace sized without it runs the unsplit kernel.
+TokenLayout token_layout(int dtype, int64_t M, int D, int NB, int base, int kmax, int stride, int offset,
+                         bool split = true) {
   TokenLayout L{};
   Carve c;
   L.nbl = local_blocks(NB, stride, offset);
@@ -55,7 +58,7 @@ TokenLayout token_layout(int dtype, int64_t M, int D, int NB, int base, int kmax
   L.max_tiles = (int)(pairs / kGuN + L.nkey + 1);
   // batches of at most 64 tokens split each gate/up tile's contraction over D (work balance of the
   // decode step)
-  L.gu_ks = tc && M <= 64 ? gateup_decode_ksplit(D) : 1;
+  L.gu_ks = split && tc && M <= 64 ? gateup_decode_ksplit(D) : 1;
   // error word, completion ticket and the block-CSR key counters: cleared by one memset per call.  The
   // error word stays at offset 0 (fp_noalloc_device_error reads it there in the library's scratch array).
   L.zero_bytes = 256 + (tc ? (size_t)L.nkey * 4 : 0);
@@ -160,6 +163,12 @@ inline void stage_mark(int i, cudaStream_t st) {
   } while (0)
 
 }  // namespace
+
+// The smallest workspace the token forward accepts (without the decode split's partials).
+size_t token_workspace_size_min(int dtype, int64_t M, int D, int NB, int base_blocks, int max_remote,
+                                int block_stride) {
+  return token_layout(dtype, M, D, NB, base_blocks, max_remote, std::max(block_stride, 1), 0, false).total;
+}
 }  // namespace fp
 
 using namespace fp;
@@ -217,6 +226,7 @@ size_t fp_token_workspace_size(int dtype, int64_t M, int D, int NB, int base_blo
   return token_layout(dtype, M, D, NB, base_blocks, max_remote, std::max(block_stride, 1), 0).total;
 }
 
+
 int fp_pooled_route(const void* x, const void* q_proj, const void* block_keys, int dtype, int64_t M, int D,
                     int NB, int base_blocks, int remote_blocks, int mode, const float* token_scores,
                     int32_t* active, float* mean_scores, void* workspace, size_t workspace_bytes,
@@ -273,7 +283,9 @@ int fp_pattention_token_fwd(const void* x, int64_t M, int D, int NB, int dtype, 
   if (tc && (!v_t || !w_gu || !aligned16(v_t) || !aligned16(w_gu))) return FP_ERR_INVALID_ARG;
   if (!tc && D > 32 * 256) return FP_ERR_UNSUPPORTED;
   const int cap = std::max(max_remote, 1);
-  const TokenLayout L = token_layout(dtype, M, D, NB, base_blocks, max_remote, block_stride, block_offset);
+  TokenLayout L = token_layout(dtype, M, D, NB, base_blocks, max_remote, block_stride, block_offset);
+  if (workspace_bytes < L.total)  // a smaller workspace (the no-alloc scratch): no decode split
+    L = token_layout(dtype, M, D, NB, base_blocks, max_remote, block_stride, block_offset, false);
   if (workspace_bytes < L.total) return FP_ERR_WORKSPACE;
   int sms;
   FP_TRY(device_info(sms));
@@ -426,7 +438,9 @@ int routed_fwd_impl(const void* x, int64_t M, int D, int NB, int dtype, const vo
   if (tc && (!v_t || !w_gu || !aligned16(v_t) || !aligned16(w_gu))) return FP_ERR_INVALID_ARG;
   if (!tc && D > 32 * 256) return FP_ERR_UNSUPPORTED;
   const int cap = std::max(capacity, 1);
-  const TokenLayout L = token_layout(dtype, M, D, NB, base_blocks, capacity, block_stride, block_offset);
+  TokenLayout L = token_layout(dtype, M, D, NB, base_blocks, capacity, block_stride, block_offset);
+  if (workspace_bytes < L.total)  // a smaller workspace: no decode split
+    L = token_layout(dtype, M, D, NB, base_blocks, capacity, block_stride, block_offset, false);
   if (workspace_bytes < L.total) return FP_ERR_WORKSPACE;
   // peer output: the tensor-core path whose contraction stores whole rows (no split-K), checked before any
   // launch so that every rank of a job (same M) falls back together

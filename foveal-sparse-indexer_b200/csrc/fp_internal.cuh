@@ -184,6 +184,11 @@ struct PeerFlags {
   int world;
 };
 int launch_peer_signal(const PeerFlags& f, uint32_t epoch, cudaStream_t st);
+// ---- api.cu
+// Smallest workspace of the token forward (without the decode split's partials); the allocation-free entry
+// point runs in it.
+size_t token_workspace_size_min(int dtype, int64_t M, int D, int NB, int base_blocks, int max_remote,
+                                int block_stride);
 
 struct DownArgs {
   const void* h;        // [M, K] bf16

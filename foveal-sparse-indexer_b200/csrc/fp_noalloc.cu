@@ -64,7 +64,7 @@ int fp_pattention_token_fwd_noalloc(const void* x, int64_t M, int D, int NB, int
                                     int y_f32, int32_t* remote_indices, int32_t* remote_counts, float* scores,
                                     void* stream) {
   if (block_stride < 1) return FP_ERR_INVALID_ARG;
-  const size_t need = fp_token_workspace_size(dtype, M, D, NB, base_blocks, max_remote, block_stride);
+  const size_t need = fp::token_workspace_size_min(dtype, M, D, NB, base_blocks, max_remote, block_stride);
   if (need > fp::kNoAllocScratchBytes) return FP_ERR_WORKSPACE;
   void* scratch = nullptr;
   const int rc = fp::scratch_on_current_device(&scratch);
