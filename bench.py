@@ -49,10 +49,11 @@ METRIC = "Pattention-MLP fwd tokens/s & % bf16 tensor peak (8B shape), 1/2/4/8 B
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 KERNELS_PER_STEP = 4  # route_proj, route (selection + block lists), gateup, down
 # block-sharded step with split routing, per token chunk: route_proj + route of this rank's tokens, the
-# routing kernel's block-list pass over the given routes, gateup, down (+ the flag and combine kernels of
-# the peer-memory reduce-scatter)
+# routing kernel's block-list pass over the given routes, gateup, down
 KERNELS_PER_SHARDED_CHUNK = 5
-KERNELS_PEER_REDUCE = 2
+# the same through peer memory (one piece): those five, the route exchange (two puts, flag, wait), the
+# output flag and the combine
+KERNELS_PEER_STEP = 11
 
 
 def parse():
@@ -669,7 +670,7 @@ def run_ours_sharded(args, rank, world, local, dev):
         "token_split": {"value": world * M * K / (t_split / 1e3), "unit": "tokens/s", "scaling": "weak",
                         "ms_per_step": t_split / K, "tokens_per_rank": M,
                         "parallelism": f"token split x{world} (no collective)"},
-        "gpu_launches": (KERNELS_PER_SHARDED_CHUNK + (KERNELS_PEER_REDUCE if peer_used else 0)) * ch * K,
+        "gpu_launches": (KERNELS_PEER_STEP if peer_used else KERNELS_PER_SHARDED_CHUNK * ch) * K,
         "clocks": clk,
         "device_error": err,
     }
