@@ -57,6 +57,21 @@ def shard_parameter_blocks(module, group=None, partial_dtype: Optional[torch.dty
         release_peer_buffers(module)
 
 
+def peer_layout(world: int, rows: int, D: int, esize: int, cap: int) -> dict:
+    """Byte layout of one rank's peer buffer (see :class:`PeerReduce`): ``slot`` bytes per (parity, writer)
+    partial slot starting at ``slots`` (slots back to back: the combine kernel reads slot w at w * rows * D
+    elements), the route tables at ``routes`` (per parity ``route_par`` bytes: ids then counts at
+    ``ids_bytes``, each rounded up to 256 bytes), ``total`` bytes in all."""
+    al = lambda n: (n + 255) // 256 * 256  # noqa: E731
+    slot = rows * D * esize
+    ids_bytes = al(world * rows * cap * 4)
+    route_par = ids_bytes + al(world * rows * 4)
+    slots = kernels.PEER_FLAG_BYTES
+    routes = slots + 2 * world * slot
+    return {"slot": slot, "slots": slots, "ids_bytes": ids_bytes, "route_par": route_par, "routes": routes,
+            "total": routes + 2 * route_par}
+
+
 class PeerReduce:
     """Receive buffers of the peer-memory reduce-scatter and route exchange, one per rank, mapped into every
     rank of the group through CUDA IPC.  Buffer of rank w: 256 bytes of flags (word v: the last epoch whose
@@ -70,13 +85,10 @@ class PeerReduce:
     def __init__(self, group, rank: int, world: int, rows: int, D: int, dtype: torch.dtype, cap: int, device):
         self.group, self.rank, self.world, self.rows, self.D, self.dtype, self.cap = (group, rank, world, rows, D,
                                                                                      dtype, cap)
-        esize = torch.empty((), dtype=dtype).element_size()
-        self.slot = rows * D * esize
-        al = lambda n: (n + 255) // 256 * 256  # noqa: E731
-        self.ids_bytes = al(world * rows * cap * 4)
-        self.route_par = self.ids_bytes + al(world * rows * 4)
-        self.route_base = kernels.PEER_FLAG_BYTES + 2 * world * self.slot
-        nbytes = self.route_base + 2 * self.route_par
+        lay = peer_layout(world, rows, D, torch.empty((), dtype=dtype).element_size(), cap)
+        self.slot, self.ids_bytes, self.route_par, self.route_base = (lay["slot"], lay["ids_bytes"],
+                                                                      lay["route_par"], lay["routes"])
+        nbytes = lay["total"]
         self.addr = None
         self.base, handle = kernels.peer_alloc(nbytes)
         handles = [None] * world
